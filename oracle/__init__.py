@@ -1,0 +1,362 @@
+"""ctypes binding of the CPU restatement in oracle/oracle.cpp.
+
+TEST INFRASTRUCTURE ONLY: the parity checker for lightgbm_rs_b200. Only
+tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg import this
+module. The product path (lightgbm_rs_b200) never imports or calls it.
+"""
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+class GainConfig(ctypes.Structure):
+    _fields_ = [
+        ("min_data_in_leaf", ctypes.c_int32),
+        ("_pad", ctypes.c_int32),
+        ("min_sum_hessian_in_leaf", ctypes.c_double),
+        ("max_delta_step", ctypes.c_double),
+        ("lambda_l1", ctypes.c_double),
+        ("lambda_l2", ctypes.c_double),
+        ("min_gain_to_split", ctypes.c_double),
+        ("path_smooth", ctypes.c_double),
+        ("parent_output", ctypes.c_double),
+    ]
+
+
+class SplitInfo(ctypes.Structure):
+    _fields_ = [
+        ("threshold", ctypes.c_uint32),
+        ("default_left", ctypes.c_int32),
+        ("left_count", ctypes.c_int32),
+        ("right_count", ctypes.c_int32),
+        ("gain", ctypes.c_double),
+        ("left_sum_gradient", ctypes.c_double),
+        ("left_sum_hessian", ctypes.c_double),
+        ("right_sum_gradient", ctypes.c_double),
+        ("right_sum_hessian", ctypes.c_double),
+        ("left_output", ctypes.c_double),
+        ("right_output", ctypes.c_double),
+    ]
+
+
+class FeatureMeta(ctypes.Structure):
+    _fields_ = [
+        ("num_bin", ctypes.c_int32),
+        ("offset", ctypes.c_int32),
+        ("default_bin", ctypes.c_int32),
+        ("most_freq_bin", ctypes.c_int32),
+        ("missing_type", ctypes.c_int32),
+        ("_pad", ctypes.c_int32),
+    ]
+
+
+class LearnerConfig(ctypes.Structure):
+    _fields_ = [
+        ("num_leaves", ctypes.c_int32),
+        ("max_depth", ctypes.c_int32),
+        ("gain", GainConfig),
+    ]
+
+
+_P = ctypes.c_void_p
+
+
+class Tree(ctypes.Structure):
+    _fields_ = [
+        ("num_leaves", ctypes.c_int32),
+        ("_pad", ctypes.c_int32),
+        ("left_child", _P),
+        ("right_child", _P),
+        ("split_feature", _P),
+        ("threshold_bin", _P),
+        ("split_gain", _P),
+        ("decision_type", _P),
+        ("leaf_value", _P),
+        ("leaf_weight", _P),
+        ("leaf_count", _P),
+        ("internal_value", _P),
+        ("internal_count", _P),
+        ("leaf_depth", _P),
+        ("leaf_parent", _P),
+    ]
+
+
+TREE_ARRAYS = [
+    ("left_child", np.int32, -1),
+    ("right_child", np.int32, -1),
+    ("split_feature", np.int32, -1),
+    ("threshold_bin", np.uint32, -1),
+    ("split_gain", np.float32, -1),
+    ("decision_type", np.int8, -1),
+    ("leaf_value", np.float64, 0),
+    ("leaf_weight", np.float64, 0),
+    ("leaf_count", np.int32, 0),
+    ("internal_value", np.float64, -1),
+    ("internal_count", np.int32, -1),
+    ("leaf_depth", np.int32, 0),
+    ("leaf_parent", np.int32, 0),
+]
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        L.oracle_construct_histogram.argtypes = [_P, _P, _P, ctypes.c_int64, ctypes.c_uint32, _P]
+        L.oracle_construct_leaf_histogram.argtypes = [
+            _P, _P, ctypes.c_int64, _P, _P, ctypes.c_uint32, _P]
+        L.oracle_find_best_split.argtypes = [
+            _P, ctypes.POINTER(GainConfig), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+            ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_double, ctypes.c_double,
+            ctypes.c_int32, ctypes.POINTER(SplitInfo)]
+        L.oracle_find_best_split.restype = ctypes.c_int
+        L.oracle_subtract.argtypes = [_P, _P, ctypes.c_int64, _P]
+        L.oracle_fix_histogram.argtypes = [_P, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
+                                           ctypes.c_double]
+        L.oracle_compact_histogram.argtypes = [_P, ctypes.c_int32, ctypes.c_int32]
+        L.oracle_partition.argtypes = [_P, _P, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint32,
+                                       ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                       ctypes.c_int32, ctypes.c_int32]
+        L.oracle_partition.restype = ctypes.c_int64
+        L.oracle_grow_tree.argtypes = [
+            _P, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _P, _P, _P,
+            ctypes.POINTER(LearnerConfig), ctypes.c_int32, ctypes.POINTER(Tree), _P, _P, _P, _P]
+        L.oracle_grow_tree.restype = ctypes.c_int32
+        L.oracle_binary_gradients.argtypes = [_P, _P, ctypes.c_int64, ctypes.c_double, _P, _P,
+                                              ctypes.c_int32]
+        L.oracle_l2_gradients.argtypes = [_P, _P, ctypes.c_int64, _P, _P, ctypes.c_int32]
+        L.oracle_binary_boost_from_score.argtypes = [_P, ctypes.c_int64, ctypes.c_double]
+        L.oracle_binary_boost_from_score.restype = ctypes.c_double
+        L.oracle_l2_boost_from_score.argtypes = [_P, ctypes.c_int64]
+        L.oracle_l2_boost_from_score.restype = ctypes.c_double
+        L.oracle_quantize.argtypes = [_P, _P, ctypes.c_int64, ctypes.c_int32, _P, _P]
+        L.oracle_tree_shrinkage.argtypes = [_P, ctypes.c_int32, _P, ctypes.c_double]
+        L.oracle_add_prediction_to_score.argtypes = [_P, ctypes.c_int32, _P, _P, _P, _P]
+        L.oracle_max_threads.restype = ctypes.c_int32
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
+
+
+def gain_config(min_data_in_leaf=20, min_sum_hessian_in_leaf=1e-3, max_delta_step=0.0,
+                lambda_l1=0.0, lambda_l2=0.0, min_gain_to_split=0.0, path_smooth=0.0,
+                parent_output=0.0):
+    return GainConfig(int(min_data_in_leaf), 0, float(min_sum_hessian_in_leaf),
+                      float(max_delta_step), float(lambda_l1), float(lambda_l2),
+                      float(min_gain_to_split), float(path_smooth), float(parent_output))
+
+
+def construct_histogram(bins, g, h, num_bin):
+    bins = np.ascontiguousarray(bins, dtype=np.uint32)
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    h = np.ascontiguousarray(h, dtype=np.float32)
+    out = np.empty(2 * num_bin, dtype=np.float64)
+    lib().oracle_construct_histogram(_ptr(bins), _ptr(g), _ptr(h), len(bins), num_bin, _ptr(out))
+    return out
+
+
+def construct_leaf_histogram(bins, rows, g, h, num_bin):
+    bins = np.ascontiguousarray(bins, dtype=np.uint32)
+    rows = np.ascontiguousarray(rows, dtype=np.uint32)
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    h = np.ascontiguousarray(h, dtype=np.float32)
+    out = np.empty(2 * num_bin, dtype=np.float64)
+    lib().oracle_construct_leaf_histogram(_ptr(bins), _ptr(rows), len(rows), _ptr(g), _ptr(h),
+                                          num_bin, _ptr(out))
+    return out
+
+
+def find_best_split(hist, cfg, num_bin, offset, default_bin, skip_default_bin, na_as_missing,
+                    run_forward, sum_gradient, sum_hessian, num_data):
+    hist = np.ascontiguousarray(hist, dtype=np.float64)
+    out = SplitInfo()
+    rc = lib().oracle_find_best_split(_ptr(hist), ctypes.byref(cfg), num_bin, offset, default_bin,
+                                      int(skip_default_bin), int(na_as_missing), int(run_forward),
+                                      float(sum_gradient), float(sum_hessian), int(num_data),
+                                      ctypes.byref(out))
+    if rc != 0:
+        raise ValueError("oracle_find_best_split rejected its inputs")
+    return out
+
+
+def subtract(parent, child):
+    parent = np.ascontiguousarray(parent, dtype=np.float64)
+    child = np.ascontiguousarray(child, dtype=np.float64)
+    out = np.empty_like(parent)
+    lib().oracle_subtract(_ptr(parent), _ptr(child), len(parent), _ptr(out))
+    return out
+
+
+def partition(bins_of_rows, rows, num_bin, min_bin, max_bin, threshold, most_freq_bin,
+              na_as_missing=False, default_left=False):
+    b = np.ascontiguousarray(bins_of_rows, dtype=np.uint32)
+    r = np.array(rows, dtype=np.uint32)
+    left = lib().oracle_partition(_ptr(b), _ptr(r), len(r), num_bin, min_bin, max_bin, threshold,
+                                  most_freq_bin, int(na_as_missing), int(default_left))
+    return r, int(left)
+
+
+def feature_metas(metas):
+    """metas: list of dicts with num_bin, default_bin, most_freq_bin, missing_type."""
+    arr = (FeatureMeta * len(metas))()
+    for i, m in enumerate(metas):
+        mfb = int(m["most_freq_bin"])
+        arr[i] = FeatureMeta(int(m["num_bin"]), 1 if mfb == 0 else 0, int(m["default_bin"]), mfb,
+                             int(m.get("missing_type", 0)), 0)
+    return arr
+
+
+def grow_tree(bins_cols, metas, g, h, num_leaves, max_depth=-1, nthreads=1, **gain_kw):
+    """Grow one tree. bins_cols: 2-D array [num_features, num_data] (u8/u16/u32)."""
+    bins_cols = np.ascontiguousarray(bins_cols)
+    F, N = bins_cols.shape
+    width = bins_cols.dtype.itemsize
+    col_ptrs = (ctypes.c_void_p * F)(*[bins_cols[f].ctypes.data for f in range(F)])
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    h = np.ascontiguousarray(h, dtype=np.float32)
+    m = feature_metas(metas)
+    cfg = LearnerConfig(int(num_leaves), int(max_depth), gain_config(**gain_kw))
+    arrays = {}
+    t = Tree()
+    for name, dt, delta in TREE_ARRAYS:
+        n = max(num_leaves + delta, 1)
+        arrays[name] = np.zeros(n, dtype=dt)
+        setattr(t, name, arrays[name].ctypes.data)
+    idx = np.empty(N, dtype=np.uint32)
+    lb = np.empty(num_leaves, dtype=np.int32)
+    lc = np.empty(num_leaves, dtype=np.int32)
+    trace = np.zeros(4 * max(num_leaves, 1), dtype=np.int32)
+    rc = lib().oracle_grow_tree(col_ptrs, width, N, F, ctypes.cast(m, ctypes.c_void_p), _ptr(g),
+                                _ptr(h), ctypes.byref(cfg), int(nthreads), ctypes.byref(t),
+                                _ptr(idx), _ptr(lb), _ptr(lc), _ptr(trace))
+    if rc < 0:
+        raise ValueError(f"oracle_grow_tree failed ({rc})")
+    nl = t.num_leaves
+    tree = {"num_leaves": nl}
+    for name, dt, delta in TREE_ARRAYS:
+        tree[name] = arrays[name][: max(nl + delta, 0)].copy()
+    part = {"indices": idx, "leaf_begin": lb[:nl].copy(), "leaf_count": lc[:nl].copy()}
+    return tree, part, trace[: 4 * rc].reshape(-1, 4)
+
+
+def binary_gradients(score, label, sigmoid=1.0, nthreads=1):
+    score = np.ascontiguousarray(score, dtype=np.float64)
+    label = np.ascontiguousarray(label, dtype=np.float32)
+    g = np.empty(len(score), dtype=np.float32)
+    h = np.empty(len(score), dtype=np.float32)
+    lib().oracle_binary_gradients(_ptr(score), _ptr(label), len(score), float(sigmoid), _ptr(g),
+                                  _ptr(h), int(nthreads))
+    return g, h
+
+
+def l2_gradients(score, label, nthreads=1):
+    score = np.ascontiguousarray(score, dtype=np.float64)
+    label = np.ascontiguousarray(label, dtype=np.float32)
+    g = np.empty(len(score), dtype=np.float32)
+    h = np.empty(len(score), dtype=np.float32)
+    lib().oracle_l2_gradients(_ptr(score), _ptr(label), len(score), _ptr(g), _ptr(h),
+                              int(nthreads))
+    return g, h
+
+
+def boost_from_score(objective, label, sigmoid=1.0):
+    label = np.ascontiguousarray(label, dtype=np.float32)
+    if objective == "binary":
+        return lib().oracle_binary_boost_from_score(_ptr(label), len(label), float(sigmoid))
+    return lib().oracle_l2_boost_from_score(_ptr(label), len(label))
+
+
+def quantize(g, h, num_grad_quant_bins):
+    """Returns (dequantized g, dequantized h, int8 pairs [N,2] (qg, qh), scales)."""
+    g = np.array(g, dtype=np.float32)
+    h = np.array(h, dtype=np.float32)
+    q = np.empty((len(g), 2), dtype=np.int8)
+    scales = np.empty(3, dtype=np.float64)
+    lib().oracle_quantize(_ptr(g), _ptr(h), len(g), int(num_grad_quant_bins), _ptr(q),
+                          _ptr(scales))
+    return g, h, q, scales
+
+
+def tree_shrinkage(tree, rate):
+    lv = tree["leaf_value"]
+    iv = tree["internal_value"]
+    if len(iv) == 0:
+        iv = np.zeros(1, dtype=np.float64)
+    lib().oracle_tree_shrinkage(_ptr(lv), tree["num_leaves"], _ptr(iv), float(rate))
+
+
+def add_prediction_to_score(tree, part, score):
+    lib().oracle_add_prediction_to_score(
+        _ptr(tree["leaf_value"]), tree["num_leaves"], _ptr(part["indices"]),
+        _ptr(part["leaf_begin"]), _ptr(part["leaf_count"]), _ptr(score))
+
+
+def max_threads():
+    return lib().oracle_max_threads()
+
+
+def train(bins_cols, metas, labels, objective="binary", num_iterations=10, learning_rate=0.1,
+          num_leaves=31, max_depth=-1, use_quantized_grad=False, num_grad_quant_bins=4,
+          boost_from_average=True, sigmoid=1.0, nthreads=1, record=False, **gain_kw):
+    """Gbdt::train_one_iter loop (lgbm-boosting/src/gbdt.rs:691-1300), non-bagging GBDT.
+
+    Returns dict(trees, init_score, scores, iter_scores?, iter_grad_hess?)."""
+    labels = np.ascontiguousarray(labels, dtype=np.float32)
+    N = len(labels)
+    score = np.zeros(N, dtype=np.float64)
+    init = 0.0
+    if boost_from_average:
+        init = boost_from_score(objective, labels, sigmoid)
+        if abs(init) > float(np.float32(1e-15)):
+            score += init
+    trees = []
+    iter_scores = []
+    iter_gh = []
+    for it in range(num_iterations):
+        if objective == "binary":
+            g, h = binary_gradients(score, labels, sigmoid, nthreads)
+        else:
+            g, h = l2_gradients(score, labels, nthreads)
+        if record:
+            iter_gh.append((g.copy(), h.copy()))
+        if use_quantized_grad:
+            g, h, _, _ = quantize(g, h, num_grad_quant_bins)
+        tree, part, _ = grow_tree(bins_cols, metas, g, h, num_leaves, max_depth, nthreads,
+                                  **gain_kw)
+        if tree["num_leaves"] > 1:
+            tree_shrinkage(tree, learning_rate)
+            add_prediction_to_score(tree, part, score)
+            if it == 0 and abs(init) > float(np.float32(1e-15)):
+                tree["bias"] = init
+            trees.append(tree)
+        else:
+            if it > 0:
+                break
+            tree["leaf_value"][0] = init
+            trees.append(tree)
+        if record:
+            iter_scores.append(score.copy())
+    out = {"trees": trees, "init_score": init, "scores": score}
+    if record:
+        out["iter_scores"] = iter_scores
+        out["iter_grad_hess"] = iter_gh
+    return out

@@ -1,0 +1,990 @@
+// CPU restatement of the lightgbm_rs histogram tree-learner path.
+//
+// TEST INFRASTRUCTURE ONLY. This file is the parity checker for the B200
+// library in lightgbm_rs_b200/: only tests/, __graft_entry__.smoke() and
+// bench.py's cpu_baseline leg may load it, and only to check or time the
+// reference algorithm. The product never links, loads or calls it.
+//
+// Every function restates the reference's CPU behaviour (the Rust crates of
+// BectorVoom/lightgbm_rs, themselves a bit-exact transcription of LightGBM
+// C++ 4.6.0.99 @195c26fc). Citations are path:line inside the reference
+// project. Parity of this restatement is pinned against the reference's own
+// golden vectors (crates/oracle-harness/tests/fixtures/...) by tests/.
+//
+// Numerics: compile with -ffp-contract=off. Rust never contracts a*b+c into
+// an FMA; the only fused multiply-add on the path is the explicit
+// `fused_mul_add` of the given-output gain (lgbm-compute/src/gain.rs:62-64),
+// restated below with std::fma.
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <limits>
+#include <vector>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+namespace {
+
+// lgbm-core/src/types.rs:31 — `const score_t kEpsilon = 1e-15f;`
+const double kEps = (double)1e-15f;
+// lgbm-core/src/types.rs:35 — kZeroThreshold (the Rust reference stores the
+// f64 literal 1e-35).
+const double kZeroThreshold = 1e-35;
+const double kMinScore = -std::numeric_limits<double>::infinity();
+
+struct GainCfg {
+  int32_t min_data_in_leaf;
+  double min_sum_hessian_in_leaf;
+  double max_delta_step;
+  double lambda_l1;
+  double lambda_l2;
+  double min_gain_to_split;
+  double path_smooth;
+  double parent_output;
+  bool use_l1() const { return lambda_l1 > 0.0; }          // gain.rs:1000-1003
+  bool use_smoothing() const { return path_smooth > kEps; } // gain.rs:1018-1020
+};
+
+}  // namespace
+
+extern "C" {
+
+// Flat C layout of lgbm_compute::gain::SplitInfo (gain.rs:1040-1065).
+typedef struct {
+  uint32_t threshold;
+  int32_t default_left;
+  int32_t left_count;
+  int32_t right_count;
+  double gain;
+  double left_sum_gradient;
+  double left_sum_hessian;
+  double right_sum_gradient;
+  double right_sum_hessian;
+  double left_output;
+  double right_output;
+} OSplitInfo;
+
+typedef struct {
+  int32_t min_data_in_leaf;
+  int32_t _pad;
+  double min_sum_hessian_in_leaf;
+  double max_delta_step;
+  double lambda_l1;
+  double lambda_l2;
+  double min_gain_to_split;
+  double path_smooth;
+  double parent_output;
+} OGainConfig;
+
+// Per-feature metadata the learner reads (lgbm-treelearner/src/learner.rs:87-140).
+typedef struct {
+  int32_t num_bin;
+  int32_t offset;          // 1 iff most_freq_bin == 0 (lgbm-treelearner/src/lib.rs:89-95)
+  int32_t default_bin;
+  int32_t most_freq_bin;
+  int32_t missing_type;    // 0 None, 1 Zero, 2 NaN
+  int32_t _pad;
+} OFeatureMeta;
+
+typedef struct {
+  int32_t num_leaves;
+  int32_t max_depth;
+  OGainConfig gain;
+} OLearnerConfig;
+
+// Tree node arrays (lgbm-model/src/tree.rs:94-160). Arrays are caller-owned and
+// sized for cfg.num_leaves leaves (num_leaves - 1 internal nodes).
+typedef struct {
+  int32_t num_leaves;
+  int32_t _pad;
+  int32_t* left_child;
+  int32_t* right_child;
+  int32_t* split_feature;
+  uint32_t* threshold_bin;
+  float* split_gain;
+  int8_t* decision_type;
+  double* leaf_value;
+  double* leaf_weight;
+  int32_t* leaf_count;
+  double* internal_value;
+  int32_t* internal_count;
+  int32_t* leaf_depth;
+  int32_t* leaf_parent;
+} OTree;
+
+}  // extern "C"
+
+namespace {
+
+// ---------------- gain primitives: lgbm-compute/src/gain.rs ----------------
+
+// gain.rs:108-117 threshold_l1
+inline double threshold_l1(double s, double l1) {
+  double reg = std::max(0.0, std::fabs(s) - l1);
+  double pos = s > 0.0 ? 1.0 : 0.0;
+  double neg = s < 0.0 ? 1.0 : 0.0;
+  return (pos - neg) * reg;
+}
+
+// gain.rs:133-140 get_leaf_gain (closed form)
+inline double leaf_gain(bool use_l1, double g, double h, double l1, double l2) {
+  if (use_l1) {
+    double t = threshold_l1(g, l1);
+    return (t * t) / (h + l2);
+  }
+  return (g * g) / (h + l2);
+}
+
+// gain.rs:233-244 calculate_splitted_leaf_output
+inline double leaf_output(bool use_l1, double g, double h, double l1, double l2) {
+  if (use_l1) return -threshold_l1(g, l1) / (h + l2);
+  return -g / (h + l2);
+}
+
+// gain.rs:201-218 get_leaf_gain_given_output (first multiply fused)
+inline double leaf_gain_given_output(bool use_l1, double g, double h, double l1, double l2,
+                                     double o) {
+  double sg = use_l1 ? threshold_l1(g, l1) : g;
+  return -std::fma(2.0 * sg, o, (h + l2) * o * o);
+}
+
+// gain.rs:494-539 calculate_splitted_leaf_output_full
+inline double leaf_output_full(bool use_l1, double g, double h, double l1, double l2,
+                               double mds, bool use_smoothing, double path_smooth,
+                               int32_t num_data, double parent_output) {
+  double base = leaf_output(use_l1, g, h, l1, l2);
+  bool clamp = mds > 0.0 && std::fabs(base) > mds;
+  double pos = base > 0.0 ? 1.0 : 0.0;
+  double neg = base < 0.0 ? 1.0 : 0.0;
+  double clamped = clamp ? (pos - neg) * mds : base;
+  if (use_smoothing) {
+    double n = (double)num_data / path_smooth;
+    return clamped * n / (n + 1.0) + parent_output / (n + 1.0);
+  }
+  return clamped;
+}
+
+// gain.rs:557-596 get_leaf_gain_full
+inline double leaf_gain_full(bool use_l1, double g, double h, double l1, double l2, double mds,
+                             bool use_smoothing, double path_smooth, int32_t num_data,
+                             double parent_output) {
+  if (mds > 0.0 || use_smoothing) {
+    double o = leaf_output_full(use_l1, g, h, l1, l2, mds, use_smoothing, path_smooth, num_data,
+                                parent_output);
+    return leaf_gain_given_output(use_l1, g, h, l1, l2, o);
+  }
+  return leaf_gain(use_l1, g, h, l1, l2);
+}
+
+GainCfg to_cfg(const OGainConfig& c) {
+  GainCfg g;
+  g.min_data_in_leaf = c.min_data_in_leaf;
+  g.min_sum_hessian_in_leaf = c.min_sum_hessian_in_leaf;
+  g.max_delta_step = c.max_delta_step;
+  g.lambda_l1 = c.lambda_l1;
+  g.lambda_l2 = c.lambda_l2;
+  g.min_gain_to_split = c.min_gain_to_split;
+  g.path_smooth = c.path_smooth;
+  g.parent_output = c.parent_output;
+  return g;
+}
+
+OSplitInfo split_none() {
+  OSplitInfo s;
+  std::memset(&s, 0, sizeof(s));
+  s.gain = kMinScore;
+  s.default_left = 1;  // gain.rs:1079-1093 SplitInfo::none
+  return s;
+}
+
+// Common::RoundInt: (int)(x + 0.5f) (kernels/split.rs:9056-9058)
+inline int32_t round_int(double x) { return (int32_t)(x + (double)0.5f); }
+
+// ------------- find_best_split_cpu_native: kernels/split.rs:8970-9329 -------------
+OSplitInfo find_best_split(const double* hist, const GainCfg& cfg, int32_t num_bin, int32_t offset,
+                           int32_t default_bin, bool skip_default_bin, bool na_as_missing,
+                           bool run_forward, double sum_gradient, double sum_hessian,
+                           int32_t num_data) {
+  const double sum_hessian_bumped = sum_hessian + 2.0 * kEps;  // :9020-9021
+  const bool use_l1 = cfg.use_l1();
+  const bool use_smoothing = cfg.use_smoothing();
+  const double mds = cfg.max_delta_step;
+  const double po = cfg.parent_output;
+  const bool use_full = use_smoothing || mds > 0.0;  // :9037
+  const double l1 = cfg.lambda_l1, l2 = cfg.lambda_l2, ps = cfg.path_smooth;
+  const double gain_shift =
+      leaf_gain_full(use_l1, sum_gradient, sum_hessian_bumped, l1, l2, mds, use_smoothing, ps,
+                     num_data, po);  // :9043-9054
+  const double min_gain_shift = gain_shift + cfg.min_gain_to_split;
+
+  const int32_t rev_count = std::max(num_bin - 1 - (na_as_missing ? 1 : 0), 0);
+  const bool na_preamble = na_as_missing && offset == 1;
+  int32_t fwd_count = 0;
+  if (run_forward) {
+    int32_t base = std::max(num_bin - 1 - offset, 0);
+    fwd_count = na_preamble ? base + 1 : base;
+  }
+  const double cnt_factor = (double)num_data / sum_hessian_bumped;
+  const double min_hess = cfg.min_sum_hessian_in_leaf;
+  const int32_t min_data = cfg.min_data_in_leaf;
+
+  auto split_gain = [&](double slg, double slh, double srg, double srh, int32_t lc,
+                        int32_t rc) -> double {
+    if (use_full)
+      return leaf_gain_full(use_l1, slg, slh, l1, l2, mds, use_smoothing, ps, lc, po) +
+             leaf_gain_full(use_l1, srg, srh, l1, l2, mds, use_smoothing, ps, rc, po);
+    return leaf_gain(use_l1, slg, slh, l1, l2) + leaf_gain(use_l1, srg, srh, l1, l2);
+  };
+
+  double best_slg = 0.0, best_slh = 0.0, best_gain = kMinScore;
+  int32_t best_lc = 0, best_thr = 0;
+  bool splittable = false, best_default_left = true;
+
+  // REVERSE (:9078-9165)
+  {
+    double srg = 0.0, srh = kEps;
+    int32_t rc = 0;
+    const int32_t t_start = num_bin - 1 - offset - (na_as_missing ? 1 : 0);
+    bool done = false;
+    for (int32_t k = 0; k < rev_count; ++k) {
+      if (done) break;
+      const int32_t t = t_start - k;
+      const bool in_range = t >= (1 - offset);
+      const bool skip = skip_default_bin && (t + offset) == default_bin;
+      const bool active = in_range && !skip;
+      if (active) {
+        double hg = hist[2 * t], hh = hist[2 * t + 1];
+        srg += hg;
+        srh += hh;
+        rc += round_int(hh * cnt_factor);
+      }
+      const int32_t lc = num_data - rc;
+      const double slh = sum_hessian_bumped - srh;
+      const double slg = sum_gradient - srg;
+      const bool cont = rc < min_data || srh < min_hess;
+      const bool brk = lc < min_data || slh < min_hess;
+      done = done || (active && !cont && brk);
+      if (active && !cont && !done) {
+        double g = split_gain(slg, slh, srg, srh, lc, rc);
+        if (g > min_gain_shift) {
+          splittable = true;
+          if (g > best_gain) {
+            best_lc = lc;
+            best_slg = slg;
+            best_slh = slh;
+            best_thr = t - 1 + offset;
+            best_gain = g;
+            best_default_left = true;
+          }
+        }
+      }
+    }
+  }
+  // FORWARD (:9167-9265)
+  {
+    double slg = 0.0, slh = kEps;
+    int32_t lc = 0;
+    int32_t fwd_start = 0;
+    if (na_preamble) {
+      slg = sum_gradient;
+      slh = sum_hessian_bumped - kEps;
+      lc = num_data;
+      for (int32_t i = 0; i < num_bin - offset; ++i) {
+        slg -= hist[2 * i];
+        slh -= hist[2 * i + 1];
+        lc -= round_int(hist[2 * i + 1] * cnt_factor);
+      }
+      fwd_start = -1;
+    }
+    bool done = false;
+    for (int32_t k = 0; k < fwd_count; ++k) {
+      if (done) break;
+      const int32_t t = fwd_start + k;
+      const bool skip = skip_default_bin && (t + offset) == default_bin;
+      const bool active = !skip;
+      if (active && t >= 0) {
+        double hg = hist[2 * t], hh = hist[2 * t + 1];
+        slg += hg;
+        slh += hh;
+        lc += round_int(hh * cnt_factor);
+      }
+      const int32_t rc = num_data - lc;
+      const double srh = sum_hessian_bumped - slh;
+      const double srg = sum_gradient - slg;
+      const bool cont = lc < min_data || slh < min_hess;
+      const bool brk = rc < min_data || srh < min_hess;
+      done = done || (active && !cont && brk);
+      if (active && !cont && !done) {
+        double g = split_gain(slg, slh, srg, srh, lc, rc);
+        if (g > min_gain_shift) {
+          splittable = true;
+          if (g > best_gain) {
+            best_lc = lc;
+            best_slg = slg;
+            best_slh = slh;
+            best_thr = t + offset;
+            best_gain = g;
+            best_default_left = false;
+          }
+        }
+      }
+    }
+  }
+  // finalization (:9267-9326)
+  const int32_t best_rc = num_data - best_lc;
+  const double lo = leaf_output_full(use_l1, best_slg, best_slh, l1, l2, mds, use_smoothing, ps,
+                                     best_lc, po);
+  const double rsg = sum_gradient - best_slg;
+  const double rsh = sum_hessian_bumped - best_slh;
+  const double ro =
+      leaf_output_full(use_l1, rsg, rsh, l1, l2, mds, use_smoothing, ps, best_rc, po);
+  if (splittable && best_gain > kMinScore) {
+    OSplitInfo s;
+    s.threshold = (uint32_t)best_thr;
+    s.gain = best_gain - min_gain_shift;
+    s.left_count = best_lc;
+    s.right_count = num_data - best_lc;
+    s.left_sum_gradient = best_slg;
+    s.left_sum_hessian = best_slh - kEps;
+    s.right_sum_gradient = rsg;
+    s.right_sum_hessian = rsh - kEps;
+    s.left_output = lo;
+    s.right_output = ro;
+    s.default_left = best_default_left ? 1 : 0;
+    return s;
+  }
+  return split_none();
+}
+
+// ---------------- FixHistogram: lgbm-treelearner/src/fix_histogram.rs:50-81 ----------------
+void fix_histogram(double* hist, int32_t num_bin, int32_t mfb, double sum_g, double sum_h) {
+  if (mfb == 0 || mfb >= num_bin) return;
+  double g = sum_g, h = sum_h;
+  for (int32_t i = 0; i < num_bin; ++i) {
+    if (i != mfb) {
+      g -= hist[2 * i];
+      h -= hist[2 * i + 1];
+    }
+  }
+  hist[2 * mfb] = g;
+  hist[2 * mfb + 1] = h;
+}
+
+// ---------------- compact_histogram: learner.rs:4460-4486 ----------------
+void compact_histogram(double* hist, int32_t num_bin, int32_t offset) {
+  if (offset <= 0) return;
+  if (offset >= num_bin) {
+    std::fill(hist, hist + 2 * num_bin, 0.0);
+    return;
+  }
+  for (int32_t c = 0; c < num_bin - offset; ++c) {
+    hist[2 * c] = hist[2 * (c + offset)];
+    hist[2 * c + 1] = hist[2 * (c + offset) + 1];
+  }
+  std::fill(hist + 2 * (num_bin - offset), hist + 2 * num_bin, 0.0);
+}
+
+// split_info.rs:28-36 split_gt
+inline bool split_gt(const OSplitInfo& a, int32_t af, const OSplitInfo& b, int32_t bf) {
+  if (a.gain != b.gain) return a.gain > b.gain;
+  int32_t x = af == -1 ? INT32_MAX : af;
+  int32_t y = bf == -1 ? INT32_MAX : bf;
+  return x < y;
+}
+
+// Bin-column accessor: columns are feature-major, `bytes` wide.
+struct Bins {
+  const void* const* cols;
+  int bytes;
+  inline uint32_t get(int32_t f, int64_t row) const {
+    switch (bytes) {
+      case 1: return ((const uint8_t*)cols[f])[row];
+      case 2: return ((const uint16_t*)cols[f])[row];
+      default: return ((const uint32_t*)cols[f])[row];
+    }
+  }
+};
+
+// LeafSplits (lgbm-treelearner/src/leaf_splits.rs:43-178)
+struct LeafSplits {
+  int32_t num_data = 0;
+  double sum_g = 0.0, sum_h = 0.0, weight = 0.0;
+};
+
+// leaf_splits.rs:128-145 self_output (root: max_delta_step clamps, no smoothing)
+double self_output(double sg, double sh, const GainCfg& c) {
+  return leaf_output_full(c.use_l1(), sg, sh, c.lambda_l1, c.lambda_l2, c.max_delta_step, false,
+                          c.path_smooth, 0, 0.0);
+}
+
+inline bool is_zero(double v) { return v >= -kZeroThreshold && v <= kZeroThreshold; }
+
+// Serial tree learner state for one tree (learner.rs:980-1562).
+struct Learner {
+  const Bins bins;
+  int64_t num_data;
+  int32_t F;
+  const OFeatureMeta* meta;
+  const float* g;
+  const float* h;
+  GainCfg cfg;
+  int32_t num_leaves;
+  int32_t max_depth;
+  int nthreads;
+
+  std::vector<size_t> slot_off;
+  size_t slot_len = 0;
+  // DataPartition (data_partition.rs:16-70)
+  std::vector<uint32_t> indices, part_left, part_right;
+  std::vector<int32_t> leaf_begin, leaf_count;
+  // HistogramPool with one slot per leaf (histogram_pool.rs: cache_size == num_leaves
+  // never evicts, so Get/Move reduce to a per-leaf slot map).
+  std::vector<std::vector<double>> pool;
+  std::vector<int32_t> slot_of_leaf;  // -1 = no histogram
+  int32_t next_slot = 0;
+
+  std::vector<OSplitInfo> best_split;
+  std::vector<int32_t> best_feature;
+  std::vector<std::vector<uint8_t>> feature_splittable;
+
+  Learner(Bins b, int64_t n, int32_t f, const OFeatureMeta* m, const float* gg, const float* hh,
+          const OLearnerConfig& lc, int nt)
+      : bins(b), num_data(n), F(f), meta(m), g(gg), h(hh), cfg(to_cfg(lc.gain)),
+        num_leaves(lc.num_leaves), max_depth(lc.max_depth), nthreads(nt) {}
+
+  bool skip_default_bin(int32_t f) const {  // learner.rs:167-169
+    return meta[f].num_bin > 2 && meta[f].missing_type == 1;
+  }
+  bool na_as_missing(int32_t f) const {  // learner.rs:173-175
+    return meta[f].num_bin > 2 && meta[f].missing_type == 2;
+  }
+  bool run_forward(int32_t f) const {  // learner.rs:191-193
+    return meta[f].num_bin > 2 && meta[f].missing_type != 0;
+  }
+
+  // build_leaf_histogram_into (learner.rs:2464-2566) with the ordered per-feature
+  // fold of build_histograms_into / fold_one_feature (lgbm-compute/src/lib.rs:223-390).
+  void build_leaf(int32_t leaf, const LeafSplits& ls, double* buf, const uint8_t* used) {
+    const bool buildable = ls.sum_h > 0.0 && ls.num_data > 0;
+    std::fill(buf, buf + slot_len, 0.0);
+    if (!buildable) return;
+    const uint32_t* rows = indices.data() + leaf_begin[leaf];
+    const int32_t cnt = leaf_count[leaf];
+    std::vector<float> og(cnt), oh(cnt);
+    for (int32_t k = 0; k < cnt; ++k) {
+      og[k] = g[rows[k]];
+      oh[k] = h[rows[k]];
+    }
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nthreads) if (cnt >= 2048 && nthreads > 1)
+    for (int32_t f = 0; f < F; ++f) {
+      if (used && !used[f]) continue;
+      double* hf = buf + slot_off[f];
+      for (int32_t k = 0; k < cnt; ++k) {
+        uint32_t b = bins.get(f, rows[k]);
+        hf[2 * b] += (double)og[k];
+        hf[2 * b + 1] += (double)oh[k];
+      }
+      fix_histogram(hf, meta[f].num_bin, meta[f].most_freq_bin, ls.sum_g, ls.sum_h);
+      compact_histogram(hf, meta[f].num_bin, meta[f].offset);
+    }
+  }
+
+  // scan_leaf_histogram (learner.rs:2708-3354), spine path.
+  void scan_leaf(int32_t leaf, const LeafSplits& ls, const double* buf,
+                 const std::vector<uint8_t>* parent_splittable) {
+    std::vector<uint8_t> this_splittable(F, 0);
+    if (!(ls.sum_h > 0.0) || ls.num_data <= 0) {
+      best_split[leaf] = split_none();
+      best_feature[leaf] = -1;
+      // feature_splittable is left untouched on this early return (:2740-2745).
+      return;
+    }
+    GainCfg lc = cfg;
+    lc.parent_output = ls.weight;
+    std::vector<OSplitInfo> per(F);
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nthreads) if (nthreads > 1 && F >= 8)
+    for (int32_t f = 0; f < F; ++f) {
+      if (parent_splittable && !(*parent_splittable)[f]) continue;
+      per[f] = find_best_split(buf + slot_off[f], lc, meta[f].num_bin, meta[f].offset,
+                               meta[f].default_bin, skip_default_bin(f), na_as_missing(f),
+                               run_forward(f), ls.sum_g, ls.sum_h, ls.num_data);
+    }
+    OSplitInfo leaf_best = split_none();
+    int32_t leaf_best_feature = -1;
+    for (int32_t f = 0; f < F; ++f) {
+      if (parent_splittable && !(*parent_splittable)[f]) continue;
+      const OSplitInfo& s = per[f];
+      this_splittable[f] = s.gain > kMinScore ? 1 : 0;
+      if (s.gain > kMinScore && split_gt(s, f, leaf_best, leaf_best_feature)) {
+        leaf_best = s;
+        leaf_best_feature = f;
+      }
+    }
+    best_split[leaf] = leaf_best;
+    best_feature[leaf] = leaf_best_feature;
+    feature_splittable[leaf] = this_splittable;
+  }
+
+  int32_t get_slot(int32_t leaf, bool* existed) {
+    if (slot_of_leaf[leaf] >= 0) {
+      *existed = true;
+      return slot_of_leaf[leaf];
+    }
+    *existed = false;
+    slot_of_leaf[leaf] = next_slot++;
+    return slot_of_leaf[leaf];
+  }
+
+  // DataPartition::split -> split_fused_host_impl (data_partition.rs:192-487)
+  void partition(int32_t leaf, int32_t right_leaf, int32_t f, uint32_t threshold,
+                 bool default_left) {
+    const int32_t begin = leaf_begin[leaf], count = leaf_count[leaf];
+    const int32_t num_bin = meta[f].num_bin;
+    const int32_t min_b = 0 + std::max(meta[f].offset, 0);  // learner.rs:3957
+    const int32_t max_b = num_bin - 1;
+    const int32_t mfb = meta[f].most_freq_bin;
+    int32_t th = (int32_t)threshold + min_b;
+    if (mfb == 0) th -= 1;
+    const bool default_to_right = mfb > (int32_t)threshold;
+    const bool na = na_as_missing(f);
+    const int32_t na_bin = num_bin - 1;
+    int32_t lc = 0, rc = 0;
+    for (int32_t i = 0; i < count; ++i) {
+      const uint32_t row = indices[begin + i];
+      const int32_t b = (int32_t)bins.get(f, row);
+      bool gr;
+      if (na && b == na_bin)
+        gr = !default_left;
+      else if (b < min_b || b > max_b)
+        gr = default_to_right;
+      else
+        gr = b > th;
+      if (gr)
+        part_right[rc++] = row;
+      else
+        part_left[lc++] = row;
+    }
+    std::copy(part_left.begin(), part_left.begin() + lc, indices.begin() + begin);
+    std::copy(part_right.begin(), part_right.begin() + rc, indices.begin() + begin + lc);
+    leaf_count[leaf] = lc;
+    leaf_begin[right_leaf] = begin + lc;
+    leaf_count[right_leaf] = rc;
+  }
+
+  int grow(OTree* tree, uint32_t* idx_out, int32_t* lb_out, int32_t* lc_out, int32_t* trace) {
+    // feature_slot_layout (learner.rs:4438-4447)
+    slot_off.resize(F);
+    slot_len = 0;
+    for (int32_t f = 0; f < F; ++f) {
+      slot_off[f] = slot_len;
+      slot_len += 2 * (size_t)meta[f].num_bin;
+    }
+    indices.resize(num_data);
+    for (int64_t i = 0; i < num_data; ++i) indices[i] = (uint32_t)i;
+    part_left.resize(num_data);
+    part_right.resize(num_data);
+    leaf_begin.assign(num_leaves, 0);
+    leaf_count.assign(num_leaves, 0);
+    leaf_count[0] = (int32_t)num_data;
+    pool.assign(num_leaves, std::vector<double>(slot_len, 0.0));
+    slot_of_leaf.assign(num_leaves, -1);
+    next_slot = 0;
+    best_split.assign(num_leaves, split_none());
+    best_feature.assign(num_leaves, -1);
+    feature_splittable.assign(num_leaves, std::vector<uint8_t>(F, 1));
+
+    // root LeafSplits::init: ordered f64 fold over all rows (leaf_splits.rs:75-92)
+    LeafSplits smaller, larger;
+    {
+      double sg = 0.0, sh = 0.0;
+      for (int64_t i = 0; i < num_data; ++i) {
+        sg += (double)g[i];
+        sh += (double)h[i];
+      }
+      smaller.num_data = (int32_t)num_data;
+      smaller.sum_g = sg;
+      smaller.sum_h = sh;
+      smaller.weight = self_output(sg, sh, cfg);
+    }
+    if (!(smaller.sum_h > 0.0)) return -1;  // InvalidLeafHessian (learner.rs:1330-1336)
+
+    // root tree (learner.rs:5398-5424)
+    int32_t nl = 1;
+    tree->leaf_value[0] = smaller.weight;
+    tree->leaf_weight[0] = 0.0;
+    tree->leaf_count[0] = (int32_t)num_data;
+    tree->leaf_depth[0] = 0;
+    tree->leaf_parent[0] = -1;
+
+    int32_t left_leaf = 0, right_leaf = -1;
+    int32_t nsplit_trace = 0;
+    for (int32_t s = 0; s < num_leaves - 1; ++s) {
+      // before_find_best_split (learner.rs:1808-1839)
+      bool did = true;
+      {
+        const int32_t num_left = leaf_count[left_leaf];
+        const int32_t min2 = cfg.min_data_in_leaf * 2;
+        if (max_depth > 0 && tree->leaf_depth[left_leaf] >= max_depth) {
+          best_split[left_leaf].gain = kMinScore;
+          if (right_leaf >= 0) best_split[right_leaf].gain = kMinScore;
+          did = false;
+        } else if (right_leaf >= 0) {
+          const int32_t num_right = leaf_count[right_leaf];
+          if (num_right < min2 && num_left < min2) {
+            best_split[left_leaf].gain = kMinScore;
+            best_split[right_leaf].gain = kMinScore;
+            did = false;
+          }
+        } else if (num_left < min2) {
+          best_split[left_leaf].gain = kMinScore;
+          did = false;
+        }
+      }
+      if (did) {
+        // find_best_splits (learner.rs:1851-2453): pool slot dance.
+        int32_t smaller_leaf, larger_leaf;
+        if (right_leaf < 0) {
+          smaller_leaf = left_leaf;
+          larger_leaf = -1;
+        } else if (leaf_count[left_leaf] < leaf_count[right_leaf]) {
+          smaller_leaf = left_leaf;
+          larger_leaf = right_leaf;
+        } else {
+          smaller_leaf = right_leaf;
+          larger_leaf = left_leaf;
+        }
+        int32_t smaller_slot, larger_slot = -1;
+        bool use_subtract = false;
+        if (right_leaf < 0) {
+          bool e;
+          smaller_slot = get_slot(left_leaf, &e);
+        } else if (smaller_leaf == left_leaf) {
+          bool existed;
+          int32_t parent = get_slot(left_leaf, &existed);
+          use_subtract = existed;
+          slot_of_leaf[right_leaf] = parent;  // Move(left -> right)
+          slot_of_leaf[left_leaf] = -1;
+          bool e;
+          smaller_slot = get_slot(left_leaf, &e);
+          larger_slot = parent;
+        } else {
+          bool existed;
+          int32_t parent = get_slot(left_leaf, &existed);
+          use_subtract = existed;
+          bool e;
+          smaller_slot = get_slot(right_leaf, &e);
+          larger_slot = parent;
+        }
+        std::vector<uint8_t> parent_splittable;
+        const std::vector<uint8_t>* ps = nullptr;
+        if (use_subtract) {
+          parent_splittable = feature_splittable[left_leaf];
+          ps = &parent_splittable;
+        }
+        const LeafSplits& sls = smaller;
+        const LeafSplits& lls = right_leaf < 0 ? smaller : larger;
+        build_leaf(smaller_leaf, sls, pool[smaller_slot].data(), ps ? ps->data() : nullptr);
+        if (larger_leaf >= 0) {
+          double* lb = pool[larger_slot].data();
+          if (use_subtract) {
+            // HistogramPool::subtract_into (histogram_pool.rs:249-283)
+            const double* sb = pool[smaller_slot].data();
+            for (size_t i = 0; i < slot_len; ++i) lb[i] = lb[i] - sb[i];
+          } else {
+            build_leaf(larger_leaf, lls, lb, ps ? ps->data() : nullptr);
+          }
+        }
+        scan_leaf(smaller_leaf, sls, pool[smaller_slot].data(), ps);
+        if (larger_leaf >= 0) scan_leaf(larger_leaf, lls, pool[larger_slot].data(), ps);
+      }
+      // arg_max (learner.rs:4537-4551)
+      int32_t best_leaf = 0;
+      for (int32_t i = 1; i < num_leaves; ++i)
+        if (split_gt(best_split[i], best_feature[i], best_split[best_leaf], best_feature[best_leaf]))
+          best_leaf = i;
+      const OSplitInfo best = best_split[best_leaf];
+      if (best.gain <= 0.0) break;
+      const int32_t f = best_feature[best_leaf];
+      const int32_t new_left = best_leaf, new_right = nl;
+      partition(best_leaf, new_right, f, best.threshold, best.default_left != 0);
+      // Tree::split (lgbm-model/src/tree.rs:614-690)
+      {
+        const int32_t node = nl - 1;
+        const int32_t parent = tree->leaf_parent[best_leaf];
+        if (parent >= 0) {
+          if (tree->right_child[parent] == ~best_leaf)
+            tree->right_child[parent] = node;
+          else
+            tree->left_child[parent] = node;
+        }
+        tree->split_feature[node] = f;
+        tree->split_gain[node] = (float)(best.gain + cfg.min_gain_to_split);
+        tree->threshold_bin[node] = best.threshold;
+        tree->internal_value[node] = tree->leaf_value[best_leaf];
+        tree->internal_count[node] = leaf_count[new_left] + leaf_count[new_right];
+        tree->left_child[node] = ~best_leaf;
+        tree->right_child[node] = ~new_right;
+        int8_t dt = 0;
+        if (best.default_left) dt |= 2;
+        dt |= (int8_t)((meta[f].missing_type & 3) << 2);
+        tree->decision_type[node] = dt;
+        tree->leaf_value[best_leaf] = best.left_output;
+        tree->leaf_weight[best_leaf] = best.left_sum_hessian;
+        tree->leaf_count[best_leaf] = leaf_count[new_left];
+        tree->leaf_value[new_right] = best.right_output;
+        tree->leaf_weight[new_right] = best.right_sum_hessian;
+        tree->leaf_count[new_right] = leaf_count[new_right];
+        tree->leaf_depth[new_right] = tree->leaf_depth[best_leaf] + 1;
+        tree->leaf_depth[best_leaf] += 1;
+        tree->leaf_parent[best_leaf] = node;
+        tree->leaf_parent[new_right] = node;
+        nl += 1;
+      }
+      if (trace) {
+        trace[4 * nsplit_trace + 0] = best_leaf;
+        trace[4 * nsplit_trace + 1] = f;
+        trace[4 * nsplit_trace + 2] = (int32_t)best.threshold;
+        trace[4 * nsplit_trace + 3] = best.default_left;
+        nsplit_trace++;
+      }
+      // seed children (learner.rs:4061-4089): smaller = fewer partition rows, tie -> right
+      const int32_t pl = leaf_count[new_left], pr = leaf_count[new_right];
+      if (pl < pr) {
+        smaller = {pl, best.left_sum_gradient, best.left_sum_hessian, best.left_output};
+        larger = {pr, best.right_sum_gradient, best.right_sum_hessian, best.right_output};
+      } else {
+        smaller = {pr, best.right_sum_gradient, best.right_sum_hessian, best.right_output};
+        larger = {pl, best.left_sum_gradient, best.left_sum_hessian, best.left_output};
+      }
+      best_split[best_leaf] = split_none();
+      best_feature[best_leaf] = -1;
+      best_split[new_left] = split_none();
+      best_feature[new_left] = -1;
+      best_split[new_right] = split_none();
+      best_feature[new_right] = -1;
+      left_leaf = new_left;
+      right_leaf = new_right;
+    }
+    tree->num_leaves = nl;
+    if (idx_out) std::copy(indices.begin(), indices.end(), idx_out);
+    if (lb_out) std::copy(leaf_begin.begin(), leaf_begin.end(), lb_out);
+    if (lc_out) std::copy(leaf_count.begin(), leaf_count.end(), lc_out);
+    return nsplit_trace;
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+// Backend::construct_histograms on the CPU backend: ordered f64 fold of f32 g/h
+// over every row (lgbm-compute/src/kernels/histogram.rs:207-233).
+void oracle_construct_histogram(const uint32_t* bins, const float* g, const float* h, int64_t n,
+                                uint32_t num_bin, double* out) {
+  std::fill(out, out + 2 * (size_t)num_bin, 0.0);
+  for (int64_t i = 0; i < n; ++i) {
+    out[2 * bins[i]] += (double)g[i];
+    out[2 * bins[i] + 1] += (double)h[i];
+  }
+}
+
+// Fold over an explicit ascending row list (Backend::build_leaf_histograms_raw_into
+// for one feature, lgbm-compute/src/lib.rs:1422-1469).
+void oracle_construct_leaf_histogram(const uint32_t* bins, const uint32_t* rows, int64_t n_rows,
+                                     const float* g, const float* h, uint32_t num_bin,
+                                     double* out) {
+  std::fill(out, out + 2 * (size_t)num_bin, 0.0);
+  for (int64_t k = 0; k < n_rows; ++k) {
+    uint32_t r = rows[k];
+    out[2 * bins[r]] += (double)g[r];
+    out[2 * bins[r] + 1] += (double)h[r];
+  }
+}
+
+int oracle_find_best_split(const double* hist, const OGainConfig* cfg, int32_t num_bin,
+                           int32_t offset, int32_t default_bin, int32_t skip_default_bin,
+                           int32_t na_as_missing, int32_t run_forward, double sum_gradient,
+                           double sum_hessian, int32_t num_data, OSplitInfo* out) {
+  if (num_bin <= 0 || !(sum_hessian > 0.0)) return -1;  // split.rs:8993-9016
+  *out = find_best_split(hist, to_cfg(*cfg), num_bin, offset, default_bin, skip_default_bin != 0,
+                         na_as_missing != 0, run_forward != 0, sum_gradient, sum_hessian,
+                         num_data);
+  return 0;
+}
+
+// kernels/subtract.rs:204-227: derived[i] = parent[i] - child[i]
+void oracle_subtract(const double* parent, const double* child, int64_t len, double* out) {
+  for (int64_t i = 0; i < len; ++i) out[i] = parent[i] - child[i];
+}
+
+void oracle_fix_histogram(double* hist, int32_t num_bin, int32_t mfb, double sum_g, double sum_h) {
+  fix_histogram(hist, num_bin, mfb, sum_g, sum_h);
+}
+
+void oracle_compact_histogram(double* hist, int32_t num_bin, int32_t offset) {
+  compact_histogram(hist, num_bin, offset);
+}
+
+// DataPartition routing over one leaf (data_partition.rs:360-487). `bins` holds
+// the split feature's bin for each of the `count` rows in `rows` (in place).
+// Returns the left count; rows are reordered [left asc | right asc].
+int64_t oracle_partition(const uint32_t* bins_of_rows, uint32_t* rows, int64_t count,
+                         uint32_t num_bin, uint32_t min_bin, uint32_t max_bin, uint32_t threshold,
+                         uint32_t most_freq_bin, int32_t na_as_missing, int32_t default_left) {
+  std::vector<uint32_t> L, R;
+  const int32_t min_b = (int32_t)min_bin, max_b = (int32_t)max_bin, thr = (int32_t)threshold;
+  int32_t th = thr + min_b;
+  if (most_freq_bin == 0) th -= 1;
+  const bool default_to_right = (int32_t)most_freq_bin > thr;
+  const int32_t na_bin = (int32_t)num_bin - 1;
+  for (int64_t i = 0; i < count; ++i) {
+    const int32_t b = (int32_t)bins_of_rows[i];
+    bool gr;
+    if (na_as_missing && b == na_bin)
+      gr = !default_left;
+    else if (b < min_b || b > max_b)
+      gr = default_to_right;
+    else
+      gr = b > th;
+    (gr ? R : L).push_back(rows[i]);
+  }
+  std::copy(L.begin(), L.end(), rows);
+  std::copy(R.begin(), R.end(), rows + L.size());
+  return (int64_t)L.size();
+}
+
+// SerialTreeLearner::train (spine path). Returns the number of splits made, or
+// a negative code. `cols` are feature-major bin columns of `bin_bytes` width.
+int32_t oracle_grow_tree(const void* const* cols, int32_t bin_bytes, int64_t num_data,
+                         int32_t num_features, const OFeatureMeta* meta, const float* g,
+                         const float* h, const OLearnerConfig* cfg, int32_t nthreads,
+                         OTree* tree, uint32_t* indices_out, int32_t* leaf_begin_out,
+                         int32_t* leaf_count_out, int32_t* trace) {
+  if (num_data <= 0 || num_features <= 0 || cfg->num_leaves < 1) return -2;
+  Bins b{cols, bin_bytes};
+  Learner L(b, num_data, num_features, meta, g, h, *cfg, nthreads < 1 ? 1 : nthreads);
+  return L.grow(tree, indices_out, leaf_begin_out, leaf_count_out, trace);
+}
+
+// Binary::get_gradients (lgbm-objective/src/binary.rs:134-171), label weights 1.
+void oracle_binary_gradients(const double* score, const float* label, int64_t n, double sigmoid,
+                             float* g, float* h, int32_t nthreads) {
+#pragma omp parallel for schedule(static) num_threads(nthreads) if (nthreads > 1 && n >= 50000)
+  for (int64_t i = 0; i < n; ++i) {
+    const bool is_pos = label[i] > 0.0f;
+    const double lv = is_pos ? 1.0 : -1.0;
+    const double resp = -lv * sigmoid / (1.0 + std::exp(lv * sigmoid * score[i]));
+    const double ar = std::fabs(resp);
+    g[i] = (float)(resp * 1.0);
+    h[i] = (float)(ar * (sigmoid - ar) * 1.0);
+  }
+}
+
+// Regression (L2) get_gradients (lgbm-objective/src/regression.rs:429-433).
+void oracle_l2_gradients(const double* score, const float* label, int64_t n, float* g, float* h,
+                         int32_t nthreads) {
+#pragma omp parallel for schedule(static) num_threads(nthreads) if (nthreads > 1 && n >= 50000)
+  for (int64_t i = 0; i < n; ++i) {
+    g[i] = (float)(score[i] - (double)label[i]);
+    h[i] = 1.0f;
+  }
+}
+
+// Binary::boost_from_score (binary.rs:178-194)
+double oracle_binary_boost_from_score(const float* label, int64_t n, double sigmoid) {
+  if (n == 0) return 0.0;
+  const double sumw = (double)n;
+  double suml = 0.0;
+  for (int64_t i = 0; i < n; ++i) suml += label[i] > 0.0f ? 1.0 : 0.0;
+  double pavg = suml / sumw;
+  pavg = std::min(pavg, 1.0 - kEps);
+  pavg = std::max(pavg, kEps);
+  return std::log(pavg / (1.0 - pavg)) / sigmoid;
+}
+
+// Regression::boost_from_score (regression.rs:563-577): ordered label mean.
+double oracle_l2_boost_from_score(const float* label, int64_t n) {
+  if (n == 0) return 0.0;
+  double s = 0.0;
+  for (int64_t i = 0; i < n; ++i) s += (double)label[i];
+  return s / (double)n;
+}
+
+// quantize_grad_hess_in_place (lgbm-boosting/src/gbdt.rs:43-62) with
+// GradientDiscretizer::{compute_scales, quantize_pair}
+// (lgbm-treelearner/src/gradient_discretizer.rs:126-191), deterministic rounding.
+// Writes the int8 pair (qg, qh) per row when q_out != NULL and the dequantized f32
+// values back into g/h. scales_out = {grad_scale, hess_scale, is_constant_hessian}.
+void oracle_quantize(float* g, float* h, int64_t n, int32_t num_grad_quant_bins,
+                     int8_t* q_out, double* scales_out) {
+  if (n == 0) return;
+  bool is_const = true;
+  for (int64_t i = 0; i < n; ++i)
+    if (!(h[i] == h[0])) {
+      is_const = false;
+      break;
+    }
+  double max_g = std::fabs((double)g[0]), max_h = std::fabs((double)h[0]);
+  for (int64_t i = 0; i < n; ++i) {
+    max_g = std::max(max_g, std::fabs((double)g[i]));
+    max_h = std::max(max_h, std::fabs((double)h[i]));
+  }
+  const double half_bins = (double)(num_grad_quant_bins / 2);
+  const double gs = max_g / half_bins;
+  const double hs = is_const ? max_h : max_h / (double)num_grad_quant_bins;
+  const double igs = 1.0 / gs, ihs = 1.0 / hs;
+  for (int64_t i = 0; i < n; ++i) {
+    const double gv = (double)g[i] * igs;
+    const int8_t qg = (int8_t)(int32_t)(g[i] >= 0.0f ? gv + 0.5 : gv - 0.5);
+    const int8_t qh = is_const ? (int8_t)1 : (int8_t)(int32_t)((double)h[i] * ihs + 0.5);
+    if (q_out) {
+      q_out[2 * i] = qg;
+      q_out[2 * i + 1] = qh;
+    }
+    g[i] = (float)((double)qg * gs);
+    h[i] = (float)((double)qh * hs);
+  }
+  if (scales_out) {
+    scales_out[0] = gs;
+    scales_out[1] = hs;
+    scales_out[2] = is_const ? 1.0 : 0.0;
+  }
+}
+
+// Tree::shrinkage (lgbm-model/src/tree.rs:1074-1100) on leaf and internal values.
+void oracle_tree_shrinkage(double* leaf_value, int32_t num_leaves, double* internal_value,
+                           double rate) {
+  for (int32_t i = 0; i < num_leaves; ++i) {
+    double v = leaf_value[i] * rate;
+    leaf_value[i] = is_zero(v) ? 0.0 : v;
+  }
+  for (int32_t i = 0; i + 1 < num_leaves; ++i) {
+    double v = internal_value[i] * rate;
+    internal_value[i] = is_zero(v) ? 0.0 : v;
+  }
+}
+
+// SerialTreeLearner::add_prediction_to_score (learner.rs:4380-4395).
+void oracle_add_prediction_to_score(const double* leaf_value, int32_t num_leaves,
+                                    const uint32_t* indices, const int32_t* leaf_begin,
+                                    const int32_t* leaf_count, double* score) {
+  if (num_leaves <= 1) return;
+  for (int32_t l = 0; l < num_leaves; ++l) {
+    const double v = leaf_value[l];
+    for (int32_t k = 0; k < leaf_count[l]; ++k) score[indices[leaf_begin[l] + k]] += v;
+  }
+}
+
+int32_t oracle_max_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+}  // extern "C"

@@ -1,0 +1,61 @@
+"""Copy the reference's golden vectors for the hot path into tests/golden/.
+
+The reference (BectorVoom/lightgbm_rs) keeps its golden vectors as text files
+captured from LightGBM C++ 4.6.0.99 / lightgbm==4.6.0. The parity tests read
+them from this directory so they also run where the reference tree is absent
+(the GPU box). Large files are stored gzip-compressed; contents are unchanged.
+
+Usage: python tests/golden/make_golden.py [REFERENCE_ROOT]
+"""
+
+import gzip
+import os
+import shutil
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+# (path inside the reference project, compress?)
+FILES = [
+    ("crates/oracle-harness/tests/fixtures/kernels/histogram.txt", True),
+    ("crates/oracle-harness/tests/fixtures/kernels/split.txt", False),
+    ("crates/oracle-harness/tests/fixtures/kernels/subtract.txt", False),
+    ("crates/oracle-harness/tests/fixtures/kernels/partition.txt", False),
+    ("crates/oracle-harness/tests/fixtures/learner/spine_real.txt", False),
+    ("crates/oracle-harness/tests/fixtures/learner/mfb_pos_real.txt", False),
+    ("crates/oracle-harness/tests/fixtures/learner/real_gh.txt", False),
+    ("crates/oracle-harness/tests/fixtures/boosting/binary_gh_iter1.txt", False),
+    ("crates/oracle-harness/tests/fixtures/boosting/binary_gh_iterN.txt", False),
+    ("crates/oracle-harness/tests/fixtures/boosting/binary_scores.txt", False),
+    ("crates/oracle-harness/tests/fixtures/boosting/binary_spine_model.txt", False),
+    ("crates/oracle-harness/tests/fixtures/boosting/regression_scores.txt", False),
+    ("crates/oracle-harness/tests/fixtures/boosting/regression_gh_iter1.txt", False),
+    ("crates/oracle-harness/tests/fixtures/quantized/quant_binary.xy.csv", True),
+    ("crates/oracle-harness/tests/fixtures/quantized/quant_binary.pred", False),
+    ("crates/oracle-harness/tests/fixtures/quantized/quant_binary.pred_exact", False),
+    ("crates/oracle-harness/tests/fixtures/quantized/quant_binary.json", False),
+    ("crates/lgbm-dataset/tests/fixtures/numeric_binning.txt", True),
+    ("crates/oracle-harness/fixtures/rng_sequence.txt", True),
+]
+
+
+def main() -> None:
+    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    for rel, compress in FILES:
+        src = os.path.join(ref, rel)
+        name = os.path.basename(rel)
+        if not os.path.exists(src):
+            print(f"missing: {src}")
+            continue
+        if compress:
+            dst = os.path.join(HERE, name + ".gz")
+            with open(src, "rb") as fi, gzip.GzipFile(dst, "wb", mtime=0) as fo:
+                shutil.copyfileobj(fi, fo)
+        else:
+            dst = os.path.join(HERE, name)
+            shutil.copyfile(src, dst)
+        print(f"{rel} -> {os.path.relpath(dst, HERE)}")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,146 @@
+"""Pin the CPU restatement (oracle/) against the reference's golden vectors.
+
+Mirrors the reference's own replay tests:
+crates/oracle-harness/tests/kernel_parity.rs (histogram :162, split :512,
+partition :1162, subtract :1276) and learner_parity.rs (:1200, :1301).
+"""
+
+import numpy as np
+import pytest
+
+import _golden as G
+
+
+def test_histogram_golden_bit_exact(oracle_lib):
+    cases = G.histogram_cases()
+    assert len(cases) == 18
+    for c in cases:
+        got = oracle_lib.construct_histogram(c["bins"], c["grad"], c["hess"], c["num_bin"])
+        assert got.view(np.uint64).tolist() == c["hist"].view(np.uint64).tolist(), c["name"]
+
+
+def test_split_golden_bit_exact(oracle_lib):
+    cases = G.split_cases()
+    assert cases
+    for c in cases:
+        cfg = oracle_lib.gain_config(
+            min_data_in_leaf=c["min_data_in_leaf"],
+            min_sum_hessian_in_leaf=c["min_sum_hessian_in_leaf"],
+            lambda_l1=c["lambda_l1"], lambda_l2=c["lambda_l2"],
+            min_gain_to_split=c["min_gain_to_split"])
+        s = oracle_lib.find_best_split(c["hist"], cfg, c["num_bin"], c["offset"],
+                                       c["default_bin"], c["skip_default_bin"],
+                                       c["na_as_missing"], True, c["sum_gradient"],
+                                       c["sum_hessian"], c["num_data"])
+        w = c["win"]
+        assert (s.gain != -np.inf) == w["is_splittable"], c["name"]
+        if not w["is_splittable"]:
+            continue
+        for k in ("gain", "left_sum_gradient", "left_sum_hessian", "right_sum_gradient",
+                  "right_sum_hessian", "left_output", "right_output"):
+            assert G.bits_of_f64(getattr(s, k)) == w[k], (c["name"], k)
+        assert s.threshold == w["threshold"], c["name"]
+        assert s.left_count == w["left_count"] and s.right_count == w["right_count"], c["name"]
+        assert bool(s.default_left) == w["default_left"], c["name"]
+
+
+def test_subtract_golden_bit_exact(oracle_lib):
+    for c in G.subtract_cases():
+        got = oracle_lib.subtract(c["subparent"], c["subchild"])
+        assert got.view(np.uint64).tolist() == c["subderived"].view(np.uint64).tolist()
+
+
+def test_partition_golden_exact(oracle_lib):
+    n = 0
+    for c in G.partition_cases():
+        if c["missing_type"] != 0:
+            continue  # the reference replays missing_type == 0 only (kernel_parity.rs:1196)
+        rows = np.arange(len(c["bins"]), dtype=np.uint32)
+        order, left = oracle_lib.partition(c["bins"], rows, c["num_bin"], c["min_bin"],
+                                           c["max_bin"], c["threshold"], c["most_freq_bin"])
+        assert order.tolist() == c["order"].tolist(), c["name"]
+        assert left == c["split"], c["name"]
+        n += 1
+    assert n >= 4
+
+
+def _real_upper_bounds(num_bin, mfb_zero_sentinel=False):
+    b = [np.nextafter(np.float64(i) + 0.5, np.inf) for i in range(num_bin)]
+    if mfb_zero_sentinel:
+        b[0] = float(np.float32(1e-35))
+    return b
+
+
+def _assert_real_tree(tree, golden, upper, shrinkage):
+    nl = golden["num_leaves"]
+    assert tree["num_leaves"] == nl
+    assert tree["split_feature"].tolist() == golden["split_feature"].tolist()
+    assert tree["decision_type"].tolist() == golden["decision_type"].tolist()
+    assert tree["left_child"].tolist() == golden["left_child"].tolist()
+    assert tree["right_child"].tolist() == golden["right_child"].tolist()
+    assert tree["leaf_count"].tolist() == golden["leaf_count"].tolist()
+    assert tree["internal_count"].tolist() == golden["internal_count"].tolist()
+    thr = [G.g17(upper[b]) for b in tree["threshold_bin"]]
+    assert thr == [G.g17(x) for x in golden["threshold"]]
+    lv = tree["leaf_value"] * shrinkage
+    lv = np.where(np.abs(lv) <= float(np.float32(1e-35)), 0.0, lv)
+    assert [G.g17(x) for x in lv] == [G.g17(x) for x in golden["leaf_value"]]
+
+
+@pytest.mark.parametrize("name,bins,grad", [
+    ("spine_real.txt", [0, 0, 1, 1, 2, 2, 3, 3, 4, 4, 5, 5],
+     [-6, -6, -5, -5, -1, -1, 1, 1, 5, 5, 6, 6]),
+    ("mfb_pos_real.txt", [0, 1, 2, 2, 2, 2, 2, 2, 3, 3, 1, 0],
+     [-6, -3, -1, -1, -1, 1, 1, 1, 4, 5, -3, -6]),
+])
+def test_learner_real_lightgbm_tree(oracle_lib, name, bins, grad):
+    """learner_parity.rs:1200 / :1301 — one tree vs a real lib_lightgbm 4.6 tree."""
+    golden = G.parse_model_text(G.read_text(name))
+    assert len(golden) == 1
+    num_bin = max(bins) + 1
+    bins = np.array([bins], dtype=np.uint32)
+    meta = [{"num_bin": num_bin, "default_bin": num_bin, "most_freq_bin": 0, "missing_type": 0}]
+    g = np.array(grad, dtype=np.float32)
+    h = np.ones_like(g)
+    tree, part, _ = oracle_lib.grow_tree(bins, meta, g, h, num_leaves=4, max_depth=-1,
+                                         min_data_in_leaf=1, min_sum_hessian_in_leaf=1e-3)
+    upper = _real_upper_bounds(num_bin, mfb_zero_sentinel=(name == "mfb_pos_real.txt"))
+    _assert_real_tree(tree, golden[0], upper, 0.1)
+    # routing self-consistency: partition leaf counts equal tree leaf counts
+    assert part["leaf_count"].tolist() == tree["leaf_count"].tolist()
+
+
+def test_binary_gradients_and_scores_golden(oracle_lib):
+    """boosting_parity.rs binary cell: 12 rows, 2 features, 10 iters, num_leaves 4.
+
+    The corpus is identity-binned (bin == raw value, boosting_parity.rs:44-66), so the
+    learner sees bins f0 in 0..5 and f1 in 0..2 with most_freq_bin 0."""
+    f0 = [0, 0, 1, 1, 2, 2, 3, 3, 4, 4, 5, 5]
+    f1 = [0, 1, 2, 0, 1, 2, 0, 1, 2, 0, 1, 2]
+    labels = np.array([0, 0, 0, 0, 0, 1, 0, 1, 1, 0, 1, 1], dtype=np.float32)
+    bins = np.array([f0, f1], dtype=np.uint32)
+    metas = [{"num_bin": 6, "default_bin": 0, "most_freq_bin": 0, "missing_type": 0},
+             {"num_bin": 3, "default_bin": 0, "most_freq_bin": 0, "missing_type": 0}]
+    out = oracle_lib.train(bins, metas, labels, objective="binary", num_iterations=10,
+                           learning_rate=0.1, num_leaves=4, min_data_in_leaf=1,
+                           min_sum_hessian_in_leaf=1e-3, record=True)
+    lines = G.data_lines("binary_scores.txt")
+    assert len(lines) == len(out["iter_scores"]) == 10
+    for k, line in enumerate(lines):
+        want = G.bits_line(line)
+        got = out["iter_scores"][k]
+        assert got.view(np.uint64).tolist() == want.view(np.uint64).tolist(), f"iter {k + 1}"
+    gh = G.data_lines("binary_gh_iter1.txt")
+    g_want = G.bits_line(gh[0].split(None, 1)[1], "f32")
+    h_want = G.bits_line(gh[1].split(None, 1)[1], "f32")
+    g_got, h_got = out["iter_grad_hess"][0]
+    np.testing.assert_allclose(g_got, g_want, atol=1e-6)
+    np.testing.assert_allclose(h_got, h_want, atol=1e-6)
+    # per-tree leaf values vs the lightgbm model text (boosting_parity.rs:205-236)
+    model = G.parse_model_text(G.read_text("binary_spine_model.txt"))
+    assert len(model) == len(out["trees"])
+    for i, (t, m) in enumerate(zip(out["trees"], model)):
+        lv = t["leaf_value"].copy()
+        if "bias" in t:
+            lv = lv + t["bias"]
+        assert [G.g17(x) for x in lv] == [G.g17(x) for x in m["leaf_value"]], f"tree {i}"
