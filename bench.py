@@ -1,0 +1,335 @@
+"""Benchmark: boosting iterations/s of the B200 histogram tree learner.
+
+Workload: 10,500,000 rows x 28 dense features from the
+configs[0] generator (seeded synthetic: no public dataset is named), max_bin=255,
+num_leaves=255, min_data_in_leaf=100, objective=binary, learning_rate=0.1.
+Default gradients: use_quantized_grad with 4 quantization bins (`--grad f32` for the
+f32-gradient variant). One step = one boosting iteration (gradients, quantization,
+one 255-leaf tree, shrinkage, score update) over all rows.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line on rank 0. `--impl reference` times the reference CPU learner
+(the C++ restatement in oracle/, the reference's Rust crates cannot be built here)
+on the host cores.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_ROWS = 10_500_000
+N_FEAT = 28
+NUM_LEAVES = 255
+MIN_DATA_IN_LEAF = 100
+LEARNING_RATE = 0.1
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--grad", default="quantized", choices=["quantized", "f32"])
+    ap.add_argument("--rows", type=int, default=N_ROWS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def make_data(rows, seed=0):
+    """Seeded synthetic C1 data, binned with the reference BinMapper (host)."""
+    import concurrent.futures as cf
+
+    import lightgbm_rs_b200 as lgb
+    from lightgbm_rs_b200 import synthetic
+
+    X, y = synthetic.binary_c0(num_data=rows, num_features=N_FEAT, seed=seed)
+    mappers = [None] * N_FEAT
+    bins = np.empty((N_FEAT, rows), dtype=np.uint8)
+
+    def one(j):
+        m, b = lgb.bin_column(X[:, j], max_bin=255, min_data_in_leaf=MIN_DATA_IN_LEAF)
+        mappers[j] = m
+        bins[j] = b.astype(np.uint8)
+
+    with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4)) as ex:
+        list(ex.map(one, range(N_FEAT)))
+    del X
+    return bins, mappers, y
+
+
+def params(grad):
+    p = {"objective": "binary", "num_leaves": NUM_LEAVES, "min_data_in_leaf": MIN_DATA_IN_LEAF,
+         "learning_rate": LEARNING_RATE, "max_bin": 255}
+    if grad == "quantized":
+        p.update(use_quantized_grad=True, num_grad_quant_bins=4)
+    return p
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def hist_algorithmic_bytes(counts, rows, grad):
+    """Bytes the histogram build must move per iteration (bins of every streamed row,
+    its gradient pair, its row index for non-root leaves, and the histogram slot)."""
+    s_gh = 2 if grad == "quantized" else 8
+    slot = 2 * 256 * N_FEAT * 8
+    builds = counts["builds"]
+    rb = counts["rows_built"]
+    nonroot_rows = max(rb - rows, 0)
+    return rb * (N_FEAT * 1 + s_gh) + nonroot_rows * 4 + builds * slot, rb * N_FEAT
+
+
+def cpu_baseline(bins, mappers, y, grad, seconds_budget=25.0):
+    """The reference CPU learner (oracle/) on the host: boosting iterations on the full
+    workload until ~seconds_budget is used (at least one)."""
+    import oracle
+
+    oracle.build()
+    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
+             for m in mappers]
+    nt = os.cpu_count() or 1
+    q = grad == "quantized"
+    score = np.full(len(y), oracle.boost_from_score("binary", y), dtype=np.float64)
+    t0 = time.perf_counter()
+    iters = 0
+    while True:
+        g, h = oracle.binary_gradients(score, y, 1.0, nt)
+        if q:
+            g, h, _, _ = oracle.quantize(g, h, 4)
+        tree, part, _ = oracle.grow_tree(bins, metas, g, h, NUM_LEAVES, -1, nt,
+                                         min_data_in_leaf=MIN_DATA_IN_LEAF)
+        oracle.tree_shrinkage(tree, LEARNING_RATE)
+        oracle.add_prediction_to_score(tree, part, score)
+        iters += 1
+        el = time.perf_counter() - t0
+        if el >= seconds_budget or iters >= 50:
+            break
+    return iters / el, nt, iters, el
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    bins, mappers, y = make_data(args.rows)
+    import oracle
+
+    oracle.build()
+    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
+             for m in mappers]
+    nt = os.cpu_count() or 1
+    q = args.grad == "quantized"
+    score = np.full(len(y), oracle.boost_from_score("binary", y), dtype=np.float64)
+
+    def step():
+        g, h = oracle.binary_gradients(score, y, 1.0, nt)
+        if q:
+            g, h, _, _ = oracle.quantize(g, h, 4)
+        tree, part, _ = oracle.grow_tree(bins, metas, g, h, NUM_LEAVES, -1, nt,
+                                         min_data_in_leaf=MIN_DATA_IN_LEAF)
+        oracle.tree_shrinkage(tree, LEARNING_RATE)
+        oracle.add_prediction_to_score(tree, part, score)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    v = args.steps / el
+    out = {
+        "metric": "boosting_iters_per_sec", "value": v, "unit": "iters/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * el / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"C1 binary {args.rows}x{N_FEAT} num_leaves={NUM_LEAVES} "
+                               f"grad={args.grad}", "rows": args.rows,
+                   "num_leaves": NUM_LEAVES, "max_bin": 255},
+        "cpu_baseline": {"value": v, "unit": "iters/s", "cores": nt, "kind": "port",
+                         "sample": f"{args.steps} full boosting iterations on all {args.rows} "
+                                   f"rows, {nt} threads (C++ restatement; reference Rust "
+                                   f"crates unbuildable here)"},
+        "e2e": {"value": v, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def run_ours(args):
+    import lightgbm_rs_b200 as lgb
+    from lightgbm_rs_b200 import build as libbuild
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        raise SystemExit("multi-GPU data-parallel bench is not built yet")
+    libbuild.build()
+    assert lgb._lib.device_count() > 0, "no CUDA device"
+    bins, mappers, y = make_data(args.rows)
+    p = params(args.grad)
+    p["device"] = local
+
+    # ---- device-resident run: inputs already in HBM when the timed region starts ----
+    ds = lgb.Dataset(bins=bins, mappers=mappers, label=y, params=p)
+    booster = lgb.Booster(p, ds)
+    booster.update(args.warmup)
+    with ClockSampler(local) as clk:
+        done = booster.update(args.steps)
+        dev_ms = booster.last_train_ms()
+    assert done == args.steps, f"training stopped early ({done} of {args.steps})"
+    value = args.steps / (dev_ms / 1000.0)
+
+    # ---- per-kernel timing of one more iteration (CUDA events on the library stream) ----
+    kms, counts = booster.profile_iteration()
+    alg_bytes, bin_bytes = hist_algorithmic_bytes(counts, args.rows, args.grad)
+    build_ms = kms["build"]
+    peak, peak_kind = load_peaks()
+    achieved = alg_bytes / (build_ms / 1000.0) / 1e9 if build_ms > 0 else 0.0
+    launches_per_step = counts["launches"]
+    del booster
+
+    # ---- end to end through the public API from host buffers ----
+    t0 = time.perf_counter()
+    ds2 = lgb.Dataset(bins=bins, mappers=mappers, label=y, params=p)
+    b2 = lgb.train(p, ds2, num_boost_round=args.steps)
+    trees = b2.trees()
+    scores = b2.train_scores()
+    e2e_s = time.perf_counter() - t0
+    h2d = bins.nbytes + y.nbytes
+    d2h = scores.nbytes + sum(sum(np.asarray(v).nbytes for k, v in t.items()
+                                  if isinstance(v, np.ndarray)) for t in trees)
+    del b2, ds2
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        v, cores, iters, el = cpu_baseline(bins, mappers, y, args.grad)
+        cpu = {"value": v, "unit": "iters/s", "cores": cores, "kind": "port",
+               "sample": f"{iters} full boosting iterations on all {args.rows} rows "
+                         f"({el:.1f} s), {cores} threads"}
+
+    out = {
+        "metric": "boosting_iters_per_sec",
+        "value": value,
+        "unit": "iters/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dev_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int64+f64" if args.grad == "quantized" else "f32+f64",
+        "data": "synthetic",
+        "config": {"workload": f"C1 binary {args.rows}x{N_FEAT} num_leaves={NUM_LEAVES} "
+                               f"min_data_in_leaf={MIN_DATA_IN_LEAF} max_bin=255 "
+                               f"grad={args.grad}",
+                   "rows": args.rows, "features": N_FEAT, "num_leaves": NUM_LEAVES,
+                   "grad": args.grad, "parallelism": "single GPU",
+                   "l2": "inputs larger than L2 (bin matrix 336 MB > 126 MB)"},
+        "roofline": {"bound": "hbm", "kernel": "k_build (histogram build)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak if peak else None, "peak_kind": peak_kind,
+                     "traffic": None, "algorithmic_bytes_per_iter": alg_bytes,
+                     "bin_bytes_per_iter": bin_bytes, "build_ms_per_iter": build_ms,
+                     "builds_per_iter": counts["builds"], "rows_built_per_iter":
+                         counts["rows_built"]},
+        "kernel_ms_per_iter": kms,
+        "cpu_baseline": cpu,
+        "e2e": {"value": args.steps / e2e_s, "unit": "iters/s",
+                "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps,
+                "note": "lgb.train from host bins+labels: upload, K iterations, model+scores "
+                        "readback (binning excluded on both arms)"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

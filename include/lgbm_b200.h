@@ -1,0 +1,288 @@
+/*
+ * lgbm_b200 — C ABI of the B200 histogram tree learner.
+ *
+ * This ABI replaces the reference's compute seam, `trait Backend` of
+ * BectorVoom/lightgbm_rs (crates/lgbm-compute/src/lib.rs:1092-2782), and the
+ * whole-tree / whole-iteration device paths behind it. Each entry point names
+ * the reference interface it stands in for.
+ *
+ * Conventions
+ *  - Every function returns an int status (LGBM_B200_*). On failure,
+ *    lgbm_b200_last_error() returns a thread-local message. No C++ exception,
+ *    abort or device trap crosses this boundary.
+ *  - Host pointers are borrowed for the duration of the call only.
+ *  - Device state is owned by opaque handles with create/destroy pairs.
+ *  - Histograms are interleaved [g0, h0, g1, h1, ...] f64 cells, as in the
+ *    reference (GET_GRAD(i) = hist[2i], GET_HESS(i) = hist[2i+1]).
+ */
+#ifndef LGBM_B200_H
+#define LGBM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. 1..5 mirror lgbm_compute::error::ComputeError
+ * (crates/lgbm-compute/src/error.rs:19-80). */
+#define LGBM_B200_OK 0
+#define LGBM_B200_BIN_OUT_OF_RANGE 1
+#define LGBM_B200_LENGTH_MISMATCH 2
+#define LGBM_B200_CAPABILITY_UNAVAILABLE 3
+#define LGBM_B200_RUNTIME 4
+#define LGBM_B200_NON_FINITE 5
+#define LGBM_B200_INVALID_ARGUMENT 6
+
+/* Missing-value handling of a feature (lgbm-dataset/src/bin_mapper.rs:15-20). */
+#define LGBM_B200_MISSING_NONE 0
+#define LGBM_B200_MISSING_ZERO 1
+#define LGBM_B200_MISSING_NAN 2
+
+/* Objectives on the path (lgbm-objective/src/binary.rs, regression.rs). */
+#define LGBM_B200_OBJECTIVE_BINARY 0
+#define LGBM_B200_OBJECTIVE_L2 1
+
+/* Gradient-pair encodings accepted by lgbm_b200_learner_grow_tree. */
+#define LGBM_B200_GH_F32 0       /* float g[N], float h[N] */
+#define LGBM_B200_GH_INT8_PAIR 1 /* int8 (qg, qh) per row + grad/hess scales */
+
+/* lgbm_compute::gain::GainConfig (crates/lgbm-compute/src/gain.rs:904-960). */
+typedef struct lgbm_b200_gain_config {
+  int32_t min_data_in_leaf;
+  int32_t _reserved;
+  double min_sum_hessian_in_leaf;
+  double max_delta_step;
+  double lambda_l1;
+  double lambda_l2;
+  double min_gain_to_split;
+  double path_smooth;
+  double parent_output;
+} lgbm_b200_gain_config;
+
+/* lgbm_compute::gain::SplitInfo (crates/lgbm-compute/src/gain.rs:1040-1065).
+ * gain == -inf means "no split". */
+typedef struct lgbm_b200_split_info {
+  uint32_t threshold;
+  int32_t default_left;
+  int32_t left_count;
+  int32_t right_count;
+  double gain;
+  double left_sum_gradient;
+  double left_sum_hessian;
+  double right_sum_gradient;
+  double right_sum_hessian;
+  double left_output;
+  double right_output;
+} lgbm_b200_split_info;
+
+/* The per-feature fields of lgbm_treelearner::FeatureColumn the learner reads
+ * (crates/lgbm-treelearner/src/learner.rs:87-140). offset is derived:
+ * 1 iff most_freq_bin == 0 (crates/lgbm-treelearner/src/lib.rs:89-95). */
+typedef struct lgbm_b200_feature_meta {
+  int32_t num_bin;
+  int32_t default_bin;
+  int32_t most_freq_bin;
+  int32_t missing_type;
+} lgbm_b200_feature_meta;
+
+/* lgbm_compute::BatchedSplitFeature (crates/lgbm-compute/src/kernels/split.rs:77). */
+typedef struct lgbm_b200_batched_feature {
+  int64_t slot_off;
+  uint32_t num_bin;
+  int32_t offset;
+  uint32_t default_bin;
+  uint32_t most_freq_bin;
+  int32_t skip_default_bin;
+  int32_t na_as_missing;
+  int32_t run_forward;
+  int32_t _reserved;
+} lgbm_b200_batched_feature;
+
+/* Tree node arrays (crates/lgbm-model/src/tree.rs:94-160). Caller-owned host
+ * arrays sized for max_leaves leaves / max_leaves-1 internal nodes. */
+typedef struct lgbm_b200_tree {
+  int32_t num_leaves;
+  int32_t max_leaves;
+  int32_t* left_child;
+  int32_t* right_child;
+  int32_t* split_feature;
+  uint32_t* threshold_bin;
+  float* split_gain;
+  int8_t* decision_type;
+  double* leaf_value;
+  double* leaf_weight;
+  int32_t* leaf_count;
+  double* internal_value;
+  int32_t* internal_count;
+} lgbm_b200_tree;
+
+/* SerialTreeLearner construction parameters
+ * (crates/lgbm-treelearner/src/learner.rs:627). */
+typedef struct lgbm_b200_learner_config {
+  int32_t num_leaves;
+  int32_t max_depth;
+  lgbm_b200_gain_config gain;
+} lgbm_b200_learner_config;
+
+/* The Gbdt training knobs the path reads (crates/lgbm-boosting/src/gbdt.rs:691-1300). */
+typedef struct lgbm_b200_train_config {
+  lgbm_b200_learner_config learner;
+  int32_t objective;
+  int32_t use_quantized_grad;
+  int32_t num_grad_quant_bins;
+  int32_t boost_from_average;
+  double sigmoid;
+  double learning_rate;
+} lgbm_b200_train_config;
+
+/* BinMapper::find_bin_from_column parameters (crates/lgbm-dataset/src/bin_mapper.rs:642-675). */
+typedef struct lgbm_b200_bin_config {
+  int32_t max_bin;
+  int32_t min_data_in_bin;
+  int32_t min_data_in_leaf;
+  int32_t pre_filter;
+  int32_t use_missing;
+  int32_t zero_as_missing;
+  int32_t bin_construct_sample_cnt;
+  int32_t data_random_seed;
+} lgbm_b200_bin_config;
+
+/* BinMapper result fields (crates/lgbm-dataset/src/bin_mapper.rs:45-60). */
+typedef struct lgbm_b200_bin_mapper {
+  int32_t num_bin;
+  int32_t missing_type;
+  int32_t default_bin;
+  int32_t most_freq_bin;
+  int32_t is_trivial;
+  int32_t _reserved;
+  double min_val;
+  double max_val;
+  double sparse_rate;
+} lgbm_b200_bin_mapper;
+
+typedef struct lgbm_b200_dataset lgbm_b200_dataset;
+typedef struct lgbm_b200_learner lgbm_b200_learner;
+typedef struct lgbm_b200_booster lgbm_b200_booster;
+
+/* Thread-local message of the last failed call on this thread ("" if none). */
+const char* lgbm_b200_last_error(void);
+
+/* ABI version of this header (major * 100 + minor). */
+int32_t lgbm_b200_abi_version(void);
+
+/* Number of CUDA devices visible (0 when none; never an error). */
+int lgbm_b200_device_count(int32_t* out);
+
+/* ------------------------------------------------------------------ binning */
+
+/* BinMapper::find_bin_from_column + value_to_bin
+ * (crates/lgbm-dataset/src/bin_mapper.rs:642-675, :148-199, :201-415).
+ * upper_bounds receives num_bin values (capacity upper_cap); bins_out (may be
+ * NULL) receives value_to_bin of every row. Host-only; needs no GPU. */
+int lgbm_b200_bin_column(const double* column, int64_t n, const lgbm_b200_bin_config* cfg,
+                         lgbm_b200_bin_mapper* mapper_out, double* upper_bounds,
+                         int32_t upper_cap, uint32_t* bins_out);
+
+/* ------------------------------------------------------ per-op Backend mirror */
+
+/* Backend::construct_histograms (crates/lgbm-compute/src/lib.rs:1119-1126):
+ * histogram of one feature over all rows. out has 2*num_bin cells.
+ * f32 g/h accumulate in 64-bit fixed point (relative error ~1e-11 of the
+ * reference's f64 fold). num_bin <= 256. */
+int lgbm_b200_construct_histograms(const uint32_t* binned, const float* gradients,
+                                   const float* hessians, int64_t n, uint32_t num_bin,
+                                   double* out);
+
+/* Backend::find_best_split (crates/lgbm-compute/src/lib.rs:1174-1189), computed
+ * by the device threshold-scan kernel; bit-exact with the reference CPU scan. */
+int lgbm_b200_find_best_split(const double* hist, const lgbm_b200_gain_config* cfg,
+                              uint32_t num_bin, int32_t offset, uint32_t default_bin,
+                              uint32_t most_freq_bin, int32_t skip_default_bin,
+                              int32_t na_as_missing, int32_t run_forward, double sum_gradient,
+                              double sum_hessian, int32_t num_data, lgbm_b200_split_info* out);
+
+/* Backend::find_best_splits_batched (crates/lgbm-compute/src/lib.rs:1500-1509). */
+int lgbm_b200_find_best_splits_batched(const double* buf, int64_t buf_len,
+                                       const lgbm_b200_batched_feature* feats, int32_t n_feats,
+                                       const lgbm_b200_gain_config* cfg, double sum_gradient,
+                                       double sum_hessian, int32_t num_data,
+                                       lgbm_b200_split_info* out);
+
+/* Backend::data_partition (crates/lgbm-compute/src/lib.rs:1206-1215): stable
+ * partition of rows 0..n-1; order_out = [left ascending | right ascending]. */
+int lgbm_b200_data_partition(const uint32_t* bins, int64_t n, uint32_t num_bin, uint32_t min_bin,
+                             uint32_t max_bin, uint32_t threshold, uint32_t most_freq_bin,
+                             uint32_t* order_out, int64_t* split_point_out);
+
+/* Backend::subtract_histograms (crates/lgbm-compute/src/lib.rs:1314-1319). */
+int lgbm_b200_subtract_histograms(const double* parent, const double* child, int64_t len,
+                                  double* out);
+
+/* ---------------------------------------------------- device-resident dataset */
+
+/* Backend::upload_resident_bins (crates/lgbm-compute/src/lib.rs:1564): take
+ * feature-major bin columns (bin_width 1, 2 or 4 bytes per bin) and keep a
+ * row-major u8 bin matrix resident on `device`. Validates bin < num_bin once
+ * (the learner's bin-range gate, learner.rs:1161-1187). */
+int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t bin_width,
+                             int64_t num_data, int32_t num_features,
+                             const lgbm_b200_feature_meta* meta, lgbm_b200_dataset** out);
+int lgbm_b200_dataset_destroy(lgbm_b200_dataset* ds);
+int lgbm_b200_dataset_num_data(const lgbm_b200_dataset* ds, int64_t* out);
+
+/* ------------------------------------------------------------ tree learner */
+
+/* SerialTreeLearner::new (crates/lgbm-treelearner/src/learner.rs:627). */
+int lgbm_b200_learner_create(lgbm_b200_dataset* ds, const lgbm_b200_learner_config* cfg,
+                             lgbm_b200_learner** out);
+int lgbm_b200_learner_destroy(lgbm_b200_learner* learner);
+
+/* Backend::grow_tree_on_device_with_cfg (crates/lgbm-compute/src/lib.rs:2771-2781):
+ * grow one tree from host gradients. gh_kind LGBM_B200_GH_F32: gh = float[2][N]
+ * (g then h); LGBM_B200_GH_INT8_PAIR: gh = int8 (qg, qh) per row and
+ * quant_scales = {grad_scale, hess_scale, is_constant_hessian, num_grad_quant_bins}
+ * as produced by GradientDiscretizer (gradient_discretizer.rs:145-191), in which
+ * case the tree is bit-identical to the reference learner on the dequantized
+ * gradients. indices_out (N), leaf_begin_out / leaf_count_out (num_leaves) may
+ * be NULL; rows inside a leaf are a permutation of the reference's order. */
+int lgbm_b200_learner_grow_tree(lgbm_b200_learner* learner, int32_t gh_kind, const void* gh,
+                                const double* quant_scales, lgbm_b200_tree* tree_out,
+                                uint32_t* indices_out, int32_t* leaf_begin_out,
+                                int32_t* leaf_count_out);
+
+/* ------------------------------------------------------------------ booster */
+
+/* Gbdt (crates/lgbm-boosting/src/gbdt.rs:691-1300) with the score kept resident:
+ * gradients, quantization, tree growth, shrinkage and score update all run on
+ * the device; labels are copied once. */
+int lgbm_b200_booster_create(lgbm_b200_dataset* ds, const float* labels,
+                             const lgbm_b200_train_config* cfg, lgbm_b200_booster** out);
+int lgbm_b200_booster_destroy(lgbm_b200_booster* b);
+/* Run up to num_iterations boosting iterations; *done_out receives how many
+ * produced a tree before training stopped (a 1-leaf tree after the first). */
+int lgbm_b200_booster_train(lgbm_b200_booster* b, int32_t num_iterations, int32_t* done_out);
+int lgbm_b200_booster_num_trees(const lgbm_b200_booster* b, int32_t* out);
+/* Trees after shrinkage; the init score of boost_from_average is reported separately. */
+int lgbm_b200_booster_get_tree(lgbm_b200_booster* b, int32_t index, lgbm_b200_tree* out);
+int lgbm_b200_booster_init_score(const lgbm_b200_booster* b, double* out);
+int lgbm_b200_booster_get_scores(lgbm_b200_booster* b, double* out);
+/* The gradients of the most recent iteration (f32, before quantization). */
+int lgbm_b200_booster_get_gradients(lgbm_b200_booster* b, float* g, float* h);
+/* Device time of the last lgbm_b200_booster_train call in ms (out3[1]; the other
+ * two entries are 0). */
+int lgbm_b200_booster_phase_ms(const lgbm_b200_booster* b, double* out3);
+/* Run ONE more boosting iteration outside the CUDA graph with CUDA events around
+ * every kernel launch. ms_out[7] receives the summed device time per kernel class
+ * {prepare, histogram build, fix+scan, partition, tree init, gradients, finish};
+ * counts_out[4] = {kernel launches, histogram builds, rows streamed by the builds,
+ * splits}. The iteration counts as a normal boosting iteration. */
+int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
+                                        int64_t* counts_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LGBM_B200_H */

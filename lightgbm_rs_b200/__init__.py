@@ -1,0 +1,349 @@
+"""lightgbm_rs_b200 — B200-native histogram tree learner behind lightgbm_rs's surface.
+
+The Python surface mirrors the reference's `lightgbm_rs` package for this path
+(crates/lgbm-python/python/lightgbm_rs/engine.py:254 `train`, `Dataset`,
+`Booster.predict`). All training work runs through the C ABI in
+include/lgbm_b200.h on the GPU; there is no CPU fallback: without the built
+library or a CUDA device the calls raise.
+"""
+
+import ctypes
+
+import numpy as np
+
+from . import _lib as C
+from ._lib import LightGBMError
+
+__all__ = ["Dataset", "Booster", "train", "bin_column", "LightGBMError", "Learner"]
+
+# Reference config defaults (crates/lgbm-core/src/config/mod.rs:430-587).
+_DEFAULTS = {
+    "objective": "regression",
+    "num_leaves": 31,
+    "max_depth": -1,
+    "min_data_in_leaf": 20,
+    "min_sum_hessian_in_leaf": 1e-3,
+    "lambda_l1": 0.0,
+    "lambda_l2": 0.0,
+    "min_gain_to_split": 0.0,
+    "max_delta_step": 0.0,
+    "path_smooth": 0.0,
+    "learning_rate": 0.1,
+    "max_bin": 255,
+    "min_data_in_bin": 3,
+    "bin_construct_sample_cnt": 200000,
+    "data_random_seed": 1,
+    "use_missing": True,
+    "zero_as_missing": False,
+    "feature_pre_filter": False,
+    "use_quantized_grad": False,
+    "num_grad_quant_bins": 4,
+    "stochastic_rounding": False,
+    "boost_from_average": True,
+    "sigmoid": 1.0,
+    "device": 0,
+}
+
+_ALIASES = {
+    "min_child_samples": "min_data_in_leaf", "min_data": "min_data_in_leaf",
+    "reg_alpha": "lambda_l1", "reg_lambda": "lambda_l2", "lr": "learning_rate",
+    "eta": "learning_rate", "shrinkage_rate": "learning_rate", "num_leaf": "num_leaves",
+    "max_leaves": "num_leaves", "min_split_gain": "min_gain_to_split",
+    "min_sum_hessian": "min_sum_hessian_in_leaf", "min_child_weight": "min_sum_hessian_in_leaf",
+    "application": "objective", "app": "objective", "loss": "objective",
+    "data_seed": "data_random_seed", "subsample_for_bin": "bin_construct_sample_cnt",
+    "device_id": "device", "gpu_device_id": "device",
+}
+
+_OBJECTIVES = {"binary": C.OBJECTIVE_BINARY, "regression": C.OBJECTIVE_L2,
+               "regression_l2": C.OBJECTIVE_L2, "l2": C.OBJECTIVE_L2, "mse": C.OBJECTIVE_L2}
+
+
+def _resolve(params):
+    p = dict(_DEFAULTS)
+    for k, v in (params or {}).items():
+        k = _ALIASES.get(k, k)
+        p[k] = v
+    if p.get("stochastic_rounding"):
+        raise LightGBMError(C.CAPABILITY_UNAVAILABLE,
+                            "stochastic_rounding=true is not on the device path")
+    return p
+
+
+def bin_column(values, max_bin=255, min_data_in_bin=3, min_data_in_leaf=20, pre_filter=False,
+               use_missing=True, zero_as_missing=False, bin_construct_sample_cnt=200000,
+               data_random_seed=1, want_bins=True):
+    """BinMapper::find_bin_from_column + value_to_bin (host-side; no GPU needed)."""
+    col = np.ascontiguousarray(values, dtype=np.float64)
+    cfg = C.BinConfig(int(max_bin), int(min_data_in_bin), int(min_data_in_leaf),
+                      int(bool(pre_filter)), int(bool(use_missing)), int(bool(zero_as_missing)),
+                      int(bin_construct_sample_cnt), int(data_random_seed))
+    m = C.BinMapperC()
+    cap = max(int(max_bin) + 2, 4)
+    upper = np.zeros(cap, dtype=np.float64)
+    bins = np.empty(len(col), dtype=np.uint32) if want_bins else None
+    C.check(C.lib().lgbm_b200_bin_column(C.ptr(col), len(col), ctypes.byref(cfg),
+                                         ctypes.byref(m), C.ptr(upper), cap, C.ptr(bins)))
+    mapper = {"num_bin": m.num_bin, "missing_type": m.missing_type,
+              "default_bin": m.default_bin, "most_freq_bin": m.most_freq_bin,
+              "is_trivial": bool(m.is_trivial), "min_val": m.min_val, "max_val": m.max_val,
+              "sparse_rate": m.sparse_rate, "upper": upper[: m.num_bin].copy()}
+    return mapper, bins
+
+
+class Dataset:
+    """Binned training data resident on one GPU (lightgbm_rs.Dataset for this path).
+
+    data: 2-D array [num_data, num_features] of raw values (binned on the host with
+    the reference BinMapper), or pass `bins`/`mappers` to reuse an existing binning."""
+
+    def __init__(self, data=None, label=None, params=None, bins=None, mappers=None):
+        self.params = _resolve(params)
+        self.label = None if label is None else np.ascontiguousarray(label, dtype=np.float32)
+        if bins is None:
+            X = np.asarray(data)
+            if X.ndim != 2:
+                raise LightGBMError(C.INVALID_ARGUMENT, "data must be 2-D")
+            p = self.params
+            cols, mappers = [], []
+            for j in range(X.shape[1]):
+                m, b = bin_column(X[:, j], p["max_bin"], p["min_data_in_bin"],
+                                  p["min_data_in_leaf"], p["feature_pre_filter"],
+                                  p["use_missing"], p["zero_as_missing"],
+                                  p["bin_construct_sample_cnt"], p["data_random_seed"])
+                mappers.append(m)
+                cols.append(b.astype(np.uint8 if m["num_bin"] <= 256 else np.uint32))
+            width = 1 if all(c.dtype == np.uint8 for c in cols) else 4
+            bins = np.stack([c.astype(np.uint8 if width == 1 else np.uint32) for c in cols])
+        self.bins = np.ascontiguousarray(bins)
+        self.mappers = mappers
+        self.num_features, self.num_data = self.bins.shape
+        self._handle = None
+
+    def construct(self):
+        if self._handle is None:
+            metas = (C.FeatureMeta * self.num_features)()
+            for f, m in enumerate(self.mappers):
+                metas[f] = C.FeatureMeta(int(m["num_bin"]), int(m["default_bin"]),
+                                         int(m["most_freq_bin"]), int(m.get("missing_type", 0)))
+            cols = (ctypes.c_void_p * self.num_features)(
+                *[self.bins[f].ctypes.data for f in range(self.num_features)])
+            h = ctypes.c_void_p()
+            C.check(C.lib().lgbm_b200_dataset_create(
+                int(self.params.get("device", 0)), cols, self.bins.dtype.itemsize,
+                self.num_data, self.num_features, ctypes.cast(metas, ctypes.c_void_p),
+                ctypes.byref(h)))
+            self._handle = h
+        return self._handle
+
+    def __del__(self):
+        try:
+            if self._handle is not None:
+                C.lib().lgbm_b200_dataset_destroy(self._handle)
+                self._handle = None
+        except Exception:
+            pass
+
+
+def _learner_config(p):
+    return C.LearnerConfig(int(p["num_leaves"]), int(p["max_depth"]), C.gain_config(
+        p["min_data_in_leaf"], p["min_sum_hessian_in_leaf"], p["max_delta_step"],
+        p["lambda_l1"], p["lambda_l2"], p["min_gain_to_split"], p["path_smooth"]))
+
+
+class Learner:
+    """SerialTreeLearner on the device: grows one tree from given gradients."""
+
+    def __init__(self, dataset, params=None):
+        self.dataset = dataset
+        p = _resolve(params)
+        self.num_leaves = int(p["num_leaves"])
+        cfg = _learner_config(p)
+        h = ctypes.c_void_p()
+        C.check(C.lib().lgbm_b200_learner_create(dataset.construct(), ctypes.byref(cfg),
+                                                 ctypes.byref(h)))
+        self._handle = h
+
+    def grow(self, g=None, h=None, quantized=None, scales=None, with_partition=True):
+        """Grow one tree. f32 g/h, or quantized=int8 [N,2] pairs (qg, qh) + scales
+        (grad_scale, hess_scale, is_constant_hessian, num_grad_quant_bins)."""
+        N = self.dataset.num_data
+        t, arrays = C.tree_buffers(self.num_leaves)
+        idx = np.empty(N, dtype=np.uint32) if with_partition else None
+        lb = np.empty(self.num_leaves, dtype=np.int32) if with_partition else None
+        lc = np.empty(self.num_leaves, dtype=np.int32) if with_partition else None
+        if quantized is None:
+            gh = np.concatenate([np.asarray(g, np.float32), np.asarray(h, np.float32)])
+            kind, sc = C.GH_F32, None
+        else:
+            gh = np.ascontiguousarray(quantized, dtype=np.int8).reshape(-1)
+            kind = C.GH_INT8_PAIR
+            sc = np.asarray(scales, dtype=np.float64)
+        C.check(C.lib().lgbm_b200_learner_grow_tree(self._handle, kind, C.ptr(gh), C.ptr(sc),
+                                                    ctypes.byref(t), C.ptr(idx), C.ptr(lb),
+                                                    C.ptr(lc)))
+        tree = C.tree_dict(t, arrays)
+        part = None
+        if with_partition:
+            nl = tree["num_leaves"]
+            part = {"indices": idx, "leaf_begin": lb[:nl].copy(), "leaf_count": lc[:nl].copy()}
+        return tree, part
+
+    def __del__(self):
+        try:
+            C.lib().lgbm_b200_learner_destroy(self._handle)
+        except Exception:
+            pass
+
+
+class Booster:
+    """Trained model (lightgbm_rs.Booster subset: predict, trees, scores)."""
+
+    def __init__(self, params, train_set):
+        self.params = _resolve(params)
+        self.train_set = train_set
+        p = self.params
+        obj = str(p["objective"]).lower()
+        if obj not in _OBJECTIVES:
+            raise LightGBMError(C.CAPABILITY_UNAVAILABLE, f"objective {obj!r} not on the path")
+        self.objective = obj
+        if train_set.label is None:
+            raise LightGBMError(C.INVALID_ARGUMENT, "Dataset has no label")
+        cfg = C.TrainConfig(_learner_config(p), _OBJECTIVES[obj], int(bool(p["use_quantized_grad"])),
+                            int(p["num_grad_quant_bins"]), int(bool(p["boost_from_average"])),
+                            float(p["sigmoid"]), float(p["learning_rate"]))
+        h = ctypes.c_void_p()
+        C.check(C.lib().lgbm_b200_booster_create(train_set.construct(), C.ptr(train_set.label),
+                                                 ctypes.byref(cfg), ctypes.byref(h)))
+        self._handle = h
+        self.num_leaves = int(p["num_leaves"])
+        self._trees = None
+
+    def update(self, num_iterations=1):
+        done = C._i32(0)
+        C.check(C.lib().lgbm_b200_booster_train(self._handle, int(num_iterations),
+                                                ctypes.byref(done)))
+        self._trees = None
+        return done.value
+
+    def num_trees(self):
+        n = C._i32(0)
+        C.check(C.lib().lgbm_b200_booster_num_trees(self._handle, ctypes.byref(n)))
+        return n.value
+
+    def init_score(self):
+        v = C._f64(0.0)
+        C.check(C.lib().lgbm_b200_booster_init_score(self._handle, ctypes.byref(v)))
+        return v.value
+
+    def trees(self):
+        if self._trees is None:
+            out = []
+            for i in range(self.num_trees()):
+                t, arrays = C.tree_buffers(self.num_leaves)
+                C.check(C.lib().lgbm_b200_booster_get_tree(self._handle, i, ctypes.byref(t)))
+                out.append(C.tree_dict(t, arrays))
+            self._trees = out
+        return self._trees
+
+    def train_scores(self):
+        s = np.empty(self.train_set.num_data, dtype=np.float64)
+        C.check(C.lib().lgbm_b200_booster_get_scores(self._handle, C.ptr(s)))
+        return s
+
+    def last_gradients(self):
+        n = self.train_set.num_data
+        g = np.empty(n, dtype=np.float32)
+        h = np.empty(n, dtype=np.float32)
+        C.check(C.lib().lgbm_b200_booster_get_gradients(self._handle, C.ptr(g), C.ptr(h)))
+        return g, h
+
+    def last_train_ms(self):
+        out = np.zeros(3, dtype=np.float64)
+        C.check(C.lib().lgbm_b200_booster_phase_ms(self._handle, C.ptr(out)))
+        return float(out[1])
+
+    KERNEL_CLASSES = ("prepare", "build", "fixscan", "partition", "tree_init", "gradients",
+                      "finish")
+
+    def profile_iteration(self):
+        """One extra iteration with per-kernel-class device timing (CUDA events on the
+        library's stream). Returns (ms by class, counts dict)."""
+        ms = np.zeros(7, dtype=np.float64)
+        cnt = np.zeros(4, dtype=np.int64)
+        C.check(C.lib().lgbm_b200_booster_profile_iteration(self._handle, C.ptr(ms), C.ptr(cnt)))
+        self._trees = None
+        return (dict(zip(self.KERNEL_CLASSES, ms.tolist())),
+                {"launches": int(cnt[0]), "builds": int(cnt[1]), "rows_built": int(cnt[2]),
+                 "splits": int(cnt[3])})
+
+    def _predict_bins(self, bins_cols):
+        """Raw score from binned features (feature-major [F, N])."""
+        n = bins_cols.shape[1]
+        out = np.full(n, self.init_score(), dtype=np.float64)
+        mappers = self.train_set.mappers
+        for t in self.trees():
+            if t["num_leaves"] <= 1:
+                continue
+            node = np.zeros(n, dtype=np.int64)
+            active = np.ones(n, dtype=bool)
+            leaf = np.zeros(n, dtype=np.int64)
+            while active.any():
+                nd = node[active]
+                f = t["split_feature"][nd]
+                b = bins_cols[f, np.nonzero(active)[0]].astype(np.int64)
+                thr = t["threshold_bin"][nd].astype(np.int64)
+                dl = (t["decision_type"][nd] & 2) != 0
+                nb = np.array([mappers[ff]["num_bin"] for ff in f], dtype=np.int64)
+                mt = np.array([mappers[ff].get("missing_type", 0) for ff in f], dtype=np.int64)
+                na = (mt == 2) & (nb > 2) & (b == nb - 1)
+                right = np.where(na, ~dl, b > thr)
+                nxt = np.where(right, t["right_child"][nd], t["left_child"][nd])
+                idx = np.nonzero(active)[0]
+                done = nxt < 0
+                leaf[idx[done]] = ~nxt[done]
+                node[idx] = np.where(done, 0, nxt)
+                active[idx[done]] = False
+            out += t["leaf_value"][leaf]
+        return out
+
+    def predict(self, data, raw_score=False):
+        X = np.asarray(data, dtype=np.float64)
+        cols = []
+        for j, m in enumerate(self.train_set.mappers):
+            up = m["upper"]
+            v = X[:, j].copy()
+            nanm = np.isnan(v)
+            if m.get("missing_type", 0) == 2:
+                b = np.searchsorted(up[:-1][: m["num_bin"] - 1], v, side="left")
+                b = np.minimum(b, m["num_bin"] - 2)
+                b[nanm] = m["num_bin"] - 1
+            else:
+                v[nanm] = 0.0
+                b = np.searchsorted(up[: m["num_bin"]], v, side="left")
+                b = np.minimum(b, m["num_bin"] - 1)
+            cols.append(b)
+        raw = self._predict_bins(np.stack(cols))
+        if raw_score or self.objective != "binary":
+            return raw
+        return 1.0 / (1.0 + np.exp(-float(self.params["sigmoid"]) * raw))
+
+    def __del__(self):
+        try:
+            C.lib().lgbm_b200_booster_destroy(self._handle)
+        except Exception:
+            pass
+
+
+def train(params, train_set, num_boost_round=100):
+    """lightgbm_rs.train (engine.py:254): boosting on the device for num_boost_round."""
+    p = dict(params or {})
+    for k in ("num_iterations", "num_iteration", "n_iter", "num_tree", "num_trees",
+              "num_round", "num_rounds", "num_boost_round", "n_estimators"):
+        if k in p:
+            num_boost_round = int(p.pop(k))
+    if isinstance(train_set, Dataset) and train_set.params != _resolve(p):
+        train_set.params.update(_resolve(p))
+    b = Booster(p, train_set)
+    b.update(int(num_boost_round))
+    return b

@@ -1,0 +1,1152 @@
+// Host runtime behind the C ABI (include/lgbm_b200.h): device-resident datasets,
+// the tree learner, the boosting loop and the per-op Backend mirror.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "binning.h"
+#include "common.cuh"
+#include "kernels.cuh"
+#include "lgbm_b200.h"
+
+namespace lgbm_b200 {
+void set_build_smem_limit(size_t bytes);
+void launch_learner_gradients(const ObjDev& o, int32_t kind, cudaStream_t st);
+void launch_gather_partition(const GrowDev& d, uint32_t* out, cudaStream_t st);
+}  // namespace lgbm_b200
+
+using namespace lgbm_b200;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Error {
+  int code;
+  std::string msg;
+};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CUDA_TRY(expr)                                                                     \
+  do {                                                                                     \
+    cudaError_t _e = (expr);                                                               \
+    if (_e != cudaSuccess)                                                                 \
+      return fail(LGBM_B200_RUNTIME, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), \
+                  __FILE__, __LINE__);                                                     \
+  } while (0)
+
+// RAII device buffer.
+template <typename T>
+struct DevBuf {
+  T* p = nullptr;
+  size_t n = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+  cudaError_t alloc(size_t count) {
+    release();
+    n = count;
+    if (count == 0) return cudaSuccess;
+    return cudaMalloc((void**)&p, count * sizeof(T));
+  }
+};
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+DevGainConfig to_dev_gain(const lgbm_b200_gain_config& g) {
+  DevGainConfig c;
+  c.min_data_in_leaf = g.min_data_in_leaf;
+  c.use_l1 = g.lambda_l1 > 0.0 ? 1 : 0;                  // gain.rs:1000-1003
+  c.use_smoothing = g.path_smooth > (double)1e-15f ? 1 : 0;  // gain.rs:1018-1020
+  c.use_full = (c.use_smoothing || g.max_delta_step > 0.0) ? 1 : 0;
+  c.min_sum_hessian_in_leaf = g.min_sum_hessian_in_leaf;
+  c.max_delta_step = g.max_delta_step;
+  c.lambda_l1 = g.lambda_l1;
+  c.lambda_l2 = g.lambda_l2;
+  c.min_gain_to_split = g.min_gain_to_split;
+  c.path_smooth = g.path_smooth;
+  return c;
+}
+
+DevFeature make_feature(int32_t num_bin, int32_t default_bin, int32_t mfb, int32_t missing_type) {
+  DevFeature f{};
+  f.num_bin = num_bin;
+  f.offset = mfb == 0 ? 1 : 0;
+  f.default_bin = default_bin;
+  f.most_freq_bin = mfb;
+  f.missing_type = missing_type;
+  int flags = 0;
+  if (num_bin > 2 && missing_type == LGBM_B200_MISSING_ZERO) flags |= 1;  // learner.rs:167-169
+  if (num_bin > 2 && missing_type == LGBM_B200_MISSING_NAN) flags |= 2;   // learner.rs:173-175
+  if (num_bin > 2 && missing_type != LGBM_B200_MISSING_NONE) flags |= 4;  // learner.rs:191-193
+  f.flags = flags;
+  f.route_min = f.offset;
+  f.route_max = num_bin - 1;
+  return f;
+}
+
+lgbm_b200_split_info to_abi(const DevSplitInfo& s) {
+  lgbm_b200_split_info o;
+  o.threshold = s.threshold;
+  o.default_left = s.default_left;
+  o.left_count = s.left_count;
+  o.right_count = s.right_count;
+  o.gain = s.gain;
+  o.left_sum_gradient = s.left_sum_gradient;
+  o.left_sum_hessian = s.left_sum_hessian;
+  o.right_sum_gradient = s.right_sum_gradient;
+  o.right_sum_hessian = s.right_sum_hessian;
+  o.left_output = s.left_output;
+  o.right_output = s.right_output;
+  return o;
+}
+
+int sm_count(int device) {
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+  return n > 0 ? n : 148;
+}
+
+bool have_device() {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return n > 0;
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------------------------
+// Dataset
+// ----------------------------------------------------------------------------------
+
+struct lgbm_b200_dataset {
+  int device = 0;
+  int64_t num_data = 0;
+  int32_t num_features = 0;
+  int32_t stride = 0;
+  int32_t total_bins = 0;
+  std::vector<DevFeature> feats;
+  DevBuf<uint8_t> bins;
+  DevBuf<DevFeature> d_feats;
+};
+
+// ----------------------------------------------------------------------------------
+// Learner
+// ----------------------------------------------------------------------------------
+
+struct lgbm_b200_learner {
+  lgbm_b200_dataset* ds = nullptr;
+  lgbm_b200_learner_config cfg{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int32_t L = 0;
+  int32_t slot_len = 0;
+  int32_t max_tiles = 0;
+  int gh_mode = GH_FLOAT;
+  int build_blocks = 0;
+  size_t build_smem = 0;
+  std::vector<DevFeatureGroup> groups;
+  DevBuf<DevFeatureGroup> d_groups;
+  DevBuf<GrowCtrl> ctrl;
+  DevBuf<int32_t> leaf_i32;  // leaf_begin, leaf_count, leaf_buf, slot_of_leaf, best_feature
+  DevBuf<DevLeafSplits> ls;
+  DevBuf<DevSplitInfo> best;
+  DevBuf<uint8_t> splittable;
+  DevBuf<int32_t> tree_i32;  // left, right, split_feature, leaf_count, internal_count, depth, parent
+  DevBuf<uint32_t> tree_thr;
+  DevBuf<float> tree_gain;
+  DevBuf<int8_t> tree_dec;
+  DevBuf<double> tree_f64;  // leaf_value, leaf_weight, internal_value
+  DevBuf<uint32_t> idx;     // 2 * N
+  DevBuf<unsigned long long> part_status;
+  DevBuf<double> pool;
+  DevBuf<long long> raw;
+  DevBuf<DevSplitInfo> scan_out;
+  DevBuf<uint8_t> scan_ok;
+  // gradients owned by a standalone learner (the booster owns its own)
+  DevBuf<uint8_t> gh;
+  DevBuf<DevGhParams> ghp;
+  GrowDev d{};
+
+  int configure_groups(int mode);
+  int init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_config& c);
+  void bind(const void* gh_ptr, const DevGhParams* ghp_ptr, const int32_t* stopped);
+};
+
+int lgbm_b200_learner::configure_groups(int mode) {
+  // Feature groups: runs of 16-feature blocks whose bins fit the shared-memory
+  // budget of one build CTA.
+  const int bpb = build_smem_bytes_per_bin(mode);
+  const size_t budget = 112 * 1024;
+  groups.clear();
+  const int F = ds->num_features;
+  DevFeatureGroup cur{0, 0, 0, 0};
+  for (int b0 = 0; b0 < F; b0 += 16) {
+    const int b1 = std::min(F, b0 + 16);
+    int nb = 0;
+    for (int f = b0; f < b1; ++f) nb += ds->feats[f].num_bin;
+    const bool fits = (size_t)(cur.num_bins + nb) * bpb <= budget && (b1 - cur.f_begin) <= 128;
+    if (cur.f_end > cur.f_begin && !fits) {
+      groups.push_back(cur);
+      cur = DevFeatureGroup{b0, b0, ds->feats[b0].bin_off, 0};
+    }
+    if (cur.f_end == cur.f_begin) {
+      cur.f_begin = b0;
+      cur.bin_base = ds->feats[b0].bin_off;
+    }
+    cur.f_end = b1;
+    cur.num_bins += nb;
+  }
+  if (cur.f_end > cur.f_begin) groups.push_back(cur);
+  size_t max_bins = 0;
+  for (auto& g : groups) max_bins = std::max(max_bins, (size_t)g.num_bins);
+  build_smem = max_bins * bpb;
+  gh_mode = mode;
+  CUDA_TRY(d_groups.alloc(groups.size()));
+  CUDA_TRY(cudaMemcpy(d_groups.p, groups.data(), groups.size() * sizeof(DevFeatureGroup),
+                      cudaMemcpyHostToDevice));
+  set_build_smem_limit(build_smem);
+  CUDA_TRY(cudaGetLastError());
+  // grid: resident CTAs of the build kernel, and enough CTAs to keep <= 2^18 rows each
+  int per_sm = std::max(1, (int)((228 * 1024) / (build_smem + 4096)));
+  per_sm = std::min(per_sm, 4);
+  const int sms = sm_count(device);
+  build_blocks = sms * per_sm;
+  const int64_t need = (ds->num_data + (1 << 18) - 1) >> 18;
+  if (build_blocks < need) build_blocks = (int)need;
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_config& c) {
+  ds = dataset;
+  cfg = c;
+  device = ds->device;
+  L = c.num_leaves;
+  if (L < 2) L = 2;
+  if (L > 256)
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE,
+                "num_leaves %d: the device learner supports at most 256 leaves", L);
+  slot_len = 2 * ds->total_bins;
+  const int64_t N = ds->num_data;
+  max_tiles = (int32_t)((N + 2047) / 2048) + 1;
+  CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  CUDA_TRY(ctrl.alloc(1));
+  CUDA_TRY(cudaMemset(ctrl.p, 0, sizeof(GrowCtrl)));
+  CUDA_TRY(leaf_i32.alloc((size_t)5 * L));
+  CUDA_TRY(ls.alloc(L));
+  CUDA_TRY(best.alloc(L));
+  CUDA_TRY(splittable.alloc((size_t)L * ds->num_features));
+  CUDA_TRY(tree_i32.alloc((size_t)7 * L));
+  CUDA_TRY(tree_thr.alloc(L));
+  CUDA_TRY(tree_gain.alloc(L));
+  CUDA_TRY(tree_dec.alloc(L));
+  CUDA_TRY(tree_f64.alloc((size_t)3 * L));
+  CUDA_TRY(idx.alloc((size_t)2 * N));
+  CUDA_TRY(part_status.alloc(max_tiles));
+  CUDA_TRY(pool.alloc((size_t)L * slot_len));
+  CUDA_TRY(raw.alloc((size_t)slot_len));
+  CUDA_TRY(cudaMemset(raw.p, 0, (size_t)slot_len * sizeof(long long)));
+  CUDA_TRY(scan_out.alloc((size_t)2 * ds->num_features));
+  CUDA_TRY(scan_ok.alloc(2));
+  d = GrowDev{};
+  d.ctrl = ctrl.p;
+  d.feat = ds->d_feats.p;
+  d.F = ds->num_features;
+  d.bins = ds->bins.p;
+  d.stride = ds->stride;
+  d.L = L;
+  d.N = N;
+  d.max_depth = c.max_depth;
+  d.slot_len = slot_len;
+  d.gain = to_dev_gain(c.gain);
+  d.leaf_begin = leaf_i32.p;
+  d.leaf_count = leaf_i32.p + L;
+  d.leaf_buf = leaf_i32.p + 2 * L;
+  d.slot_of_leaf = leaf_i32.p + 3 * L;
+  d.best_feature = leaf_i32.p + 4 * L;
+  d.ls = ls.p;
+  d.best = best.p;
+  d.splittable = splittable.p;
+  d.t_left = tree_i32.p;
+  d.t_right = tree_i32.p + L;
+  d.t_split_feature = tree_i32.p + 2 * L;
+  d.t_leaf_count = tree_i32.p + 3 * L;
+  d.t_internal_count = tree_i32.p + 4 * L;
+  d.t_leaf_depth = tree_i32.p + 5 * L;
+  d.t_leaf_parent = tree_i32.p + 6 * L;
+  d.t_threshold = tree_thr.p;
+  d.t_split_gain = tree_gain.p;
+  d.t_decision = tree_dec.p;
+  d.t_leaf_value = tree_f64.p;
+  d.t_leaf_weight = tree_f64.p + L;
+  d.t_internal_value = tree_f64.p + 2 * L;
+  d.idx0 = idx.p;
+  d.idx1 = idx.p + N;
+  d.part_status = part_status.p;
+  d.max_tiles = max_tiles;
+  d.pool = pool.p;
+  d.raw = raw.p;
+  d.scan_out = scan_out.p;
+  d.scan_ok = scan_ok.p;
+  return LGBM_B200_OK;
+}
+
+void lgbm_b200_learner::bind(const void* gh_ptr, const DevGhParams* ghp_ptr,
+                             const int32_t* stopped) {
+  d.gh = gh_ptr;
+  d.ghp = ghp_ptr;
+  d.stopped = stopped;
+  d.gh_mode = gh_mode;
+  d.groups = d_groups.p;
+  d.num_groups = (int32_t)groups.size();
+}
+
+namespace {
+
+int read_tree(lgbm_b200_learner* l, lgbm_b200_tree* out) {
+  const int L = l->L;
+  GrowCtrl c;
+  CUDA_TRY(cudaMemcpy(&c, l->ctrl.p, sizeof(GrowCtrl), cudaMemcpyDeviceToHost));
+  if (c.error)
+    return fail(LGBM_B200_RUNTIME, "tree grower reported device error bits 0x%x", c.error);
+  std::vector<int32_t> ti((size_t)7 * L);
+  std::vector<uint32_t> thr(L);
+  std::vector<float> gain(L);
+  std::vector<int8_t> dec(L);
+  std::vector<double> tf((size_t)3 * L);
+  CUDA_TRY(cudaMemcpy(ti.data(), l->tree_i32.p, ti.size() * 4, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemcpy(thr.data(), l->tree_thr.p, thr.size() * 4, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemcpy(gain.data(), l->tree_gain.p, gain.size() * 4, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemcpy(dec.data(), l->tree_dec.p, dec.size(), cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemcpy(tf.data(), l->tree_f64.p, tf.size() * 8, cudaMemcpyDeviceToHost));
+  const int nl = c.num_leaves;
+  if (out->max_leaves < nl)
+    return fail(LGBM_B200_LENGTH_MISMATCH, "tree_out holds %d leaves, tree has %d",
+                out->max_leaves, nl);
+  out->num_leaves = nl;
+  for (int i = 0; i + 1 < nl; ++i) {
+    if (out->left_child) out->left_child[i] = ti[i];
+    if (out->right_child) out->right_child[i] = ti[L + i];
+    if (out->split_feature) out->split_feature[i] = ti[2 * L + i];
+    if (out->internal_count) out->internal_count[i] = ti[4 * L + i];
+    if (out->threshold_bin) out->threshold_bin[i] = thr[i];
+    if (out->split_gain) out->split_gain[i] = gain[i];
+    if (out->decision_type) out->decision_type[i] = dec[i];
+    if (out->internal_value) out->internal_value[i] = tf[2 * L + i];
+  }
+  for (int i = 0; i < nl; ++i) {
+    if (out->leaf_value) out->leaf_value[i] = tf[i];
+    if (out->leaf_weight) out->leaf_weight[i] = tf[L + i];
+    if (out->leaf_count) out->leaf_count[i] = ti[3 * L + i];
+  }
+  return LGBM_B200_OK;
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------------------------
+// Booster
+// ----------------------------------------------------------------------------------
+
+struct lgbm_b200_booster {
+  lgbm_b200_dataset* ds = nullptr;
+  lgbm_b200_train_config cfg{};
+  std::unique_ptr<lgbm_b200_learner> learner;
+  DevBuf<float> label;
+  DevBuf<double> score;
+  DevBuf<uint8_t> gh;  // float2[N] followed by uint16[N]
+  DevBuf<DevGhParams> ghp;
+  DevBuf<int32_t> state;  // [0] stopped, [1] iter counter
+  int32_t capacity = 0;
+  DevBuf<int32_t> rec_i32;  // num_leaves[cap], left, right, split_feature, leaf_count, internal_count
+  DevBuf<uint32_t> rec_thr;
+  DevBuf<float> rec_gain;
+  DevBuf<int8_t> rec_dec;
+  DevBuf<double> rec_f64;  // leaf_value, leaf_weight, internal_value
+  double init_score = 0.0;
+  ObjDev obj{};
+  FinishDev fin{};
+  cudaGraphExec_t graph_exec = nullptr;
+  cudaGraph_t graph = nullptr;
+  float last_ms = 0.f;
+
+  int ensure_capacity(int32_t need);
+  void destroy_graph() {
+    if (graph_exec) cudaGraphExecDestroy(graph_exec);
+    if (graph) cudaGraphDestroy(graph);
+    graph_exec = nullptr;
+    graph = nullptr;
+  }
+  ~lgbm_b200_booster() { destroy_graph(); }
+};
+
+int lgbm_b200_booster::ensure_capacity(int32_t need) {
+  if (need <= capacity) return LGBM_B200_OK;
+  int32_t cap = std::max(need, capacity * 2);
+  const int L = learner->L;
+  // grow while keeping already recorded trees
+  DevBuf<int32_t> i32;
+  DevBuf<uint32_t> thr;
+  DevBuf<float> gain;
+  DevBuf<int8_t> dec;
+  DevBuf<double> f64;
+  CUDA_TRY(i32.alloc((size_t)cap + (size_t)5 * cap * L));
+  CUDA_TRY(thr.alloc((size_t)cap * L));
+  CUDA_TRY(gain.alloc((size_t)cap * L));
+  CUDA_TRY(dec.alloc((size_t)cap * L));
+  CUDA_TRY(f64.alloc((size_t)3 * cap * L));
+  if (capacity > 0) {
+    const size_t oc = capacity, nc = cap, L_ = L;
+    CUDA_TRY(cudaMemcpy(i32.p, rec_i32.p, oc * 4, cudaMemcpyDeviceToDevice));
+    for (int a = 0; a < 5; ++a)
+      CUDA_TRY(cudaMemcpy(i32.p + nc + a * nc * L_, rec_i32.p + oc + a * oc * L_, oc * L_ * 4,
+                          cudaMemcpyDeviceToDevice));
+    CUDA_TRY(cudaMemcpy(thr.p, rec_thr.p, oc * L_ * 4, cudaMemcpyDeviceToDevice));
+    CUDA_TRY(cudaMemcpy(gain.p, rec_gain.p, oc * L_ * 4, cudaMemcpyDeviceToDevice));
+    CUDA_TRY(cudaMemcpy(dec.p, rec_dec.p, oc * L_, cudaMemcpyDeviceToDevice));
+    for (int a = 0; a < 3; ++a)
+      CUDA_TRY(cudaMemcpy(f64.p + a * nc * L_, rec_f64.p + a * oc * L_, oc * L_ * 8,
+                          cudaMemcpyDeviceToDevice));
+  }
+  std::swap(rec_i32.p, i32.p);
+  std::swap(rec_i32.n, i32.n);
+  std::swap(rec_thr.p, thr.p);
+  std::swap(rec_thr.n, thr.n);
+  std::swap(rec_gain.p, gain.p);
+  std::swap(rec_gain.n, gain.n);
+  std::swap(rec_dec.p, dec.p);
+  std::swap(rec_dec.n, dec.n);
+  std::swap(rec_f64.p, f64.p);
+  std::swap(rec_f64.n, f64.n);
+  capacity = cap;
+  const size_t nc = cap, L_ = L;
+  fin.max_iters = cap;
+  fin.rec_num_leaves = rec_i32.p;
+  fin.rec_left = rec_i32.p + nc;
+  fin.rec_right = rec_i32.p + nc + nc * L_;
+  fin.rec_split_feature = rec_i32.p + nc + 2 * nc * L_;
+  fin.rec_leaf_count = rec_i32.p + nc + 3 * nc * L_;
+  fin.rec_internal_count = rec_i32.p + nc + 4 * nc * L_;
+  fin.rec_threshold = rec_thr.p;
+  fin.rec_split_gain = rec_gain.p;
+  fin.rec_decision = rec_dec.p;
+  fin.rec_leaf_value = rec_f64.p;
+  fin.rec_leaf_weight = rec_f64.p + nc * L_;
+  fin.rec_internal_value = rec_f64.p + 2 * nc * L_;
+  destroy_graph();  // pointers changed
+  return LGBM_B200_OK;
+}
+
+// ----------------------------------------------------------------------------------
+// C ABI
+// ----------------------------------------------------------------------------------
+
+extern "C" {
+
+const char* lgbm_b200_last_error(void) { return g_last_error.c_str(); }
+
+int32_t lgbm_b200_abi_version(void) { return 100; }
+
+int lgbm_b200_device_count(int32_t* out) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (out) *out = n;
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_bin_column(const double* column, int64_t n, const lgbm_b200_bin_config* cfg,
+                         lgbm_b200_bin_mapper* mapper_out, double* upper_bounds,
+                         int32_t upper_cap, uint32_t* bins_out) {
+  if (!column || !cfg || !mapper_out || n < 0)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "bin_column: null argument");
+  BinMapperHost m = find_bin_from_column(column, n, cfg->max_bin, cfg->min_data_in_bin,
+                                         cfg->min_data_in_leaf, cfg->pre_filter != 0,
+                                         cfg->use_missing != 0, cfg->zero_as_missing != 0,
+                                         cfg->bin_construct_sample_cnt, cfg->data_random_seed);
+  mapper_out->num_bin = m.num_bin;
+  mapper_out->missing_type = m.missing_type;
+  mapper_out->default_bin = m.default_bin;
+  mapper_out->most_freq_bin = m.most_freq_bin;
+  mapper_out->is_trivial = m.is_trivial ? 1 : 0;
+  mapper_out->min_val = m.min_val;
+  mapper_out->max_val = m.max_val;
+  mapper_out->sparse_rate = m.sparse_rate;
+  if (upper_bounds) {
+    if (upper_cap < m.num_bin)
+      return fail(LGBM_B200_LENGTH_MISMATCH, "upper_bounds holds %d, need %d", upper_cap,
+                  m.num_bin);
+    std::copy(m.upper.begin(), m.upper.end(), upper_bounds);
+  }
+  if (bins_out)
+    for (int64_t i = 0; i < n; ++i) bins_out[i] = m.value_to_bin(column[i]);
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_construct_histograms(const uint32_t* binned, const float* gradients,
+                                   const float* hessians, int64_t n, uint32_t num_bin,
+                                   double* out) {
+  if (num_bin == 0) return fail(LGBM_B200_RUNTIME, "construct_histograms: num_bin must be > 0");
+  if (num_bin > (uint32_t)kMaxBins)
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE,
+                "construct_histograms: num_bin %u exceeds the u8 bin matrix (256)", num_bin);
+  if (n < 0 || (n > 0 && (!binned || !gradients || !hessians)) || !out)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "construct_histograms: null argument");
+  for (int64_t i = 0; i < n; ++i)
+    if (binned[i] >= num_bin)
+      return fail(LGBM_B200_BIN_OUT_OF_RANGE, "row %lld bin %u >= num_bin %u", (long long)i,
+                  binned[i], num_bin);
+  if (!have_device()) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "no CUDA device");
+  std::fill(out, out + 2 * (size_t)num_bin, 0.0);
+  if (n == 0) return LGBM_B200_OK;
+  // host-side scale choice, as the objective kernel does per iteration
+  double mg = 0.0, mh = 0.0;
+  for (int64_t i = 0; i < n; ++i) {
+    mg = std::max(mg, std::fabs((double)gradients[i]));
+    mh = std::max(mh, std::fabs((double)hessians[i]));
+  }
+  int lg = 0;
+  while (lg < 62 && ((int64_t)1 << lg) < n) ++lg;
+  auto kscale = [&](double m) -> int {
+    if (!(m > 0.0) || !std::isfinite(m)) return 0;
+    int e;
+    std::frexp(m, &e);
+    return std::max(-1000, std::min(1000, 62 - e - lg));
+  };
+  const int kg = kscale(mg), kh = kscale(mh);
+  std::vector<uint8_t> rm((size_t)n * 16, 0);
+  std::vector<float2> gh(n);
+  for (int64_t i = 0; i < n; ++i) {
+    rm[(size_t)i * 16] = (uint8_t)binned[i];
+    gh[i] = make_float2(gradients[i], hessians[i]);
+  }
+  DevBuf<uint8_t> d_rm;
+  DevBuf<float2> d_gh;
+  DevBuf<long long> d_raw;
+  CUDA_TRY(d_rm.alloc(rm.size()));
+  CUDA_TRY(d_gh.alloc(n));
+  CUDA_TRY(d_raw.alloc(2 * (size_t)num_bin));
+  CUDA_TRY(cudaMemcpy(d_rm.p, rm.data(), rm.size(), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(d_gh.p, gh.data(), n * sizeof(float2), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemset(d_raw.p, 0, 2 * (size_t)num_bin * 8));
+  launch_construct_histogram_f32(d_rm.p, 16, n, d_gh.p, (int32_t)num_bin, std::ldexp(1.0, kg),
+                                 std::ldexp(1.0, kh), d_raw.p, 0);
+  CUDA_TRY(cudaGetLastError());
+  std::vector<long long> raw(2 * (size_t)num_bin);
+  CUDA_TRY(cudaMemcpy(raw.data(), d_raw.p, raw.size() * 8, cudaMemcpyDeviceToHost));
+  for (uint32_t b = 0; b < num_bin; ++b) {
+    out[2 * b] = (double)raw[2 * b] * std::ldexp(1.0, -kg);
+    out[2 * b + 1] = (double)raw[2 * b + 1] * std::ldexp(1.0, -kh);
+  }
+  return LGBM_B200_OK;
+}
+
+static int scan_batch(const double* buf, int64_t buf_len, std::vector<DevFeature>& feats,
+                      const lgbm_b200_gain_config* cfg, double sum_g, double sum_h,
+                      int32_t num_data, lgbm_b200_split_info* out) {
+  if (!have_device()) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "no CUDA device");
+  DevBuf<double> d_hist;
+  DevBuf<DevFeature> d_f;
+  DevBuf<DevSplitInfo> d_out;
+  CUDA_TRY(d_hist.alloc(buf_len));
+  CUDA_TRY(d_f.alloc(feats.size()));
+  CUDA_TRY(d_out.alloc(feats.size()));
+  CUDA_TRY(cudaMemcpy(d_hist.p, buf, buf_len * 8, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(d_f.p, feats.data(), feats.size() * sizeof(DevFeature),
+                      cudaMemcpyHostToDevice));
+  DevLeafSplits ls{num_data, 0, sum_g, sum_h, cfg->parent_output};
+  launch_scan_features(d_hist.p, d_f.p, (int32_t)feats.size(), to_dev_gain(*cfg), ls, d_out.p, 0);
+  CUDA_TRY(cudaGetLastError());
+  std::vector<DevSplitInfo> res(feats.size());
+  CUDA_TRY(cudaMemcpy(res.data(), d_out.p, res.size() * sizeof(DevSplitInfo),
+                      cudaMemcpyDeviceToHost));
+  for (size_t i = 0; i < res.size(); ++i) out[i] = to_abi(res[i]);
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_find_best_split(const double* hist, const lgbm_b200_gain_config* cfg,
+                              uint32_t num_bin, int32_t offset, uint32_t default_bin,
+                              uint32_t most_freq_bin, int32_t skip_default_bin,
+                              int32_t na_as_missing, int32_t run_forward, double sum_gradient,
+                              double sum_hessian, int32_t num_data, lgbm_b200_split_info* out) {
+  if (!hist || !cfg || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "find_best_split: null");
+  if (num_bin == 0) return fail(LGBM_B200_RUNTIME, "find_best_split: num_bin must be > 0");
+  if (num_bin > (uint32_t)kMaxBins)
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "find_best_split: num_bin %u > 256", num_bin);
+  if (!(sum_hessian > 0.0))
+    return fail(LGBM_B200_RUNTIME,
+                "find_best_split: sum_hessian must be > 0 (cnt_factor divides by it)");
+  std::vector<DevFeature> f(1);
+  f[0] = make_feature((int32_t)num_bin, (int32_t)default_bin, (int32_t)most_freq_bin, 0);
+  f[0].offset = offset;
+  f[0].flags = (skip_default_bin ? 1 : 0) | (na_as_missing ? 2 : 0) | (run_forward ? 4 : 0);
+  f[0].slot_off = 0;
+  return scan_batch(hist, 2 * (int64_t)num_bin, f, cfg, sum_gradient, sum_hessian, num_data,
+                    out);
+}
+
+int lgbm_b200_find_best_splits_batched(const double* buf, int64_t buf_len,
+                                       const lgbm_b200_batched_feature* feats, int32_t n_feats,
+                                       const lgbm_b200_gain_config* cfg, double sum_gradient,
+                                       double sum_hessian, int32_t num_data,
+                                       lgbm_b200_split_info* out) {
+  if (!buf || !feats || !cfg || !out || n_feats < 0)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "find_best_splits_batched: null");
+  if (!(sum_hessian > 0.0))
+    return fail(LGBM_B200_RUNTIME, "find_best_splits_batched: sum_hessian must be > 0");
+  std::vector<DevFeature> f(n_feats);
+  for (int i = 0; i < n_feats; ++i) {
+    const auto& b = feats[i];
+    if (b.num_bin == 0 || b.num_bin > (uint32_t)kMaxBins)
+      return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "feature %d: num_bin %u", i, b.num_bin);
+    if (b.slot_off < 0 || b.slot_off + 2 * (int64_t)b.num_bin > buf_len)
+      return fail(LGBM_B200_LENGTH_MISMATCH, "feature %d slot outside the buffer", i);
+    f[i] = make_feature((int32_t)b.num_bin, (int32_t)b.default_bin, (int32_t)b.most_freq_bin, 0);
+    f[i].offset = b.offset;
+    f[i].flags = (b.skip_default_bin ? 1 : 0) | (b.na_as_missing ? 2 : 0) | (b.run_forward ? 4 : 0);
+    f[i].slot_off = (int32_t)b.slot_off;
+  }
+  if (n_feats == 0) return LGBM_B200_OK;
+  return scan_batch(buf, buf_len, f, cfg, sum_gradient, sum_hessian, num_data, out);
+}
+
+int lgbm_b200_data_partition(const uint32_t* bins, int64_t n, uint32_t num_bin, uint32_t min_bin,
+                             uint32_t max_bin, uint32_t threshold, uint32_t most_freq_bin,
+                             uint32_t* order_out, int64_t* split_point_out) {
+  if (!order_out || !split_point_out || (n > 0 && !bins) || n < 0)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "data_partition: null argument");
+  if (num_bin == 0) return fail(LGBM_B200_RUNTIME, "data_partition: num_bin must be > 0");
+  if (threshold >= num_bin)
+    return fail(LGBM_B200_RUNTIME, "data_partition: threshold %u >= num_bin %u", threshold,
+                num_bin);
+  if (num_bin > (uint32_t)kMaxBins)
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "data_partition: num_bin %u > 256", num_bin);
+  for (int64_t i = 0; i < n; ++i)
+    if (bins[i] >= num_bin)
+      return fail(LGBM_B200_BIN_OUT_OF_RANGE, "row %lld bin %u >= num_bin %u", (long long)i,
+                  bins[i], num_bin);
+  if (n > (int64_t)INT32_MAX) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "n > 2^31");
+  if (!have_device()) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "no CUDA device");
+  *split_point_out = 0;
+  if (n == 0) return LGBM_B200_OK;
+  std::vector<uint8_t> rm((size_t)n * 16, 0);
+  for (int64_t i = 0; i < n; ++i) rm[(size_t)i * 16] = (uint8_t)bins[i];
+  DevFeature f = make_feature((int32_t)num_bin, 0, (int32_t)most_freq_bin, 0);
+  f.route_min = (int32_t)min_bin;
+  f.route_max = (int32_t)max_bin;
+  const int64_t tiles = (n + 2047) / 2048;
+  DevBuf<uint8_t> d_rm;
+  DevBuf<uint32_t> d_dst;
+  DevBuf<unsigned long long> d_status;
+  DevBuf<int32_t> d_cnt;  // [0] left total, [1] ticket
+  DevBuf<DevFeature> d_f;
+  CUDA_TRY(d_rm.alloc(rm.size()));
+  CUDA_TRY(d_dst.alloc(n));
+  CUDA_TRY(d_status.alloc(tiles));
+  CUDA_TRY(d_cnt.alloc(2));
+  CUDA_TRY(d_f.alloc(1));
+  CUDA_TRY(cudaMemcpy(d_rm.p, rm.data(), rm.size(), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(d_f.p, &f, sizeof(f), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemset(d_status.p, 0, tiles * 8));
+  CUDA_TRY(cudaMemset(d_cnt.p, 0, 8));
+  launch_partition_rows(d_rm.p, 16, 0, d_f.p, threshold, 0, n, d_dst.p, d_status.p, d_cnt.p,
+                        reinterpret_cast<uint32_t*>(d_cnt.p + 1), 0);
+  CUDA_TRY(cudaGetLastError());
+  int32_t cnt[2];
+  CUDA_TRY(cudaMemcpy(cnt, d_cnt.p, 8, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemcpy(order_out, d_dst.p, n * 4, cudaMemcpyDeviceToHost));
+  // the device writes the right rows from the back; the reference returns them ascending
+  std::reverse(order_out + cnt[0], order_out + n);
+  *split_point_out = cnt[0];
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_subtract_histograms(const double* parent, const double* child, int64_t len,
+                                  double* out) {
+  if (len < 0 || (len > 0 && (!parent || !child || !out)))
+    return fail(LGBM_B200_INVALID_ARGUMENT, "subtract_histograms: null argument");
+  if (!have_device()) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "no CUDA device");
+  if (len == 0) return LGBM_B200_OK;
+  DevBuf<double> a, b, o;
+  CUDA_TRY(a.alloc(len));
+  CUDA_TRY(b.alloc(len));
+  CUDA_TRY(o.alloc(len));
+  CUDA_TRY(cudaMemcpy(a.p, parent, len * 8, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(b.p, child, len * 8, cudaMemcpyHostToDevice));
+  launch_subtract(a.p, b.p, o.p, len, 0);
+  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(cudaMemcpy(out, o.p, len * 8, cudaMemcpyDeviceToHost));
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t bin_width,
+                             int64_t num_data, int32_t num_features,
+                             const lgbm_b200_feature_meta* meta, lgbm_b200_dataset** out) {
+  if (!out || !meta || (num_features > 0 && !columns))
+    return fail(LGBM_B200_INVALID_ARGUMENT, "dataset_create: null argument");
+  *out = nullptr;
+  if (num_data <= 0) return fail(LGBM_B200_RUNTIME, "dataset_create: empty dataset (no rows)");
+  if (num_features <= 0) return fail(LGBM_B200_RUNTIME, "dataset_create: no features");
+  if (num_data > (int64_t)INT32_MAX - 1)
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "num_data %lld exceeds 2^31-1",
+                (long long)num_data);
+  if (bin_width != 1 && bin_width != 2 && bin_width != 4)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "bin_width must be 1, 2 or 4");
+  for (int f = 0; f < num_features; ++f) {
+    if (meta[f].num_bin <= 0 || meta[f].num_bin > kMaxBins)
+      return fail(LGBM_B200_CAPABILITY_UNAVAILABLE,
+                  "feature %d: num_bin %d outside 1..256 (u8 bin matrix)", f, meta[f].num_bin);
+    if (meta[f].most_freq_bin < 0 || meta[f].most_freq_bin >= meta[f].num_bin)
+      return fail(LGBM_B200_INVALID_ARGUMENT, "feature %d: most_freq_bin out of range", f);
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    cudaGetLastError();
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "no CUDA device");
+  }
+  if (device < 0 || device >= ndev)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "device %d not present", device);
+  DeviceGuard guard(device);
+  auto ds = std::make_unique<lgbm_b200_dataset>();
+  ds->device = device;
+  ds->num_data = num_data;
+  ds->num_features = num_features;
+  ds->stride = ((num_features + 15) / 16) * 16;
+  int32_t bin_off = 0;
+  for (int f = 0; f < num_features; ++f) {
+    DevFeature d = make_feature(meta[f].num_bin, meta[f].default_bin, meta[f].most_freq_bin,
+                                meta[f].missing_type);
+    d.bin_off = bin_off;
+    d.slot_off = 2 * bin_off;
+    bin_off += meta[f].num_bin;
+    ds->feats.push_back(d);
+  }
+  ds->total_bins = bin_off;
+  // bin-range gate + transpose to row-major u8, in row chunks
+  const int64_t chunk = 1 << 20;
+  std::vector<uint8_t> host((size_t)std::min(chunk, num_data) * ds->stride);
+  CUDA_TRY(ds->bins.alloc((size_t)num_data * ds->stride));
+  for (int64_t r0 = 0; r0 < num_data; r0 += chunk) {
+    const int64_t r1 = std::min(num_data, r0 + chunk);
+    std::fill(host.begin(), host.end(), 0);
+    for (int f = 0; f < num_features; ++f) {
+      const uint32_t nb = (uint32_t)meta[f].num_bin;
+      for (int64_t r = r0; r < r1; ++r) {
+        uint32_t b;
+        if (bin_width == 1)
+          b = ((const uint8_t*)columns[f])[r];
+        else if (bin_width == 2)
+          b = ((const uint16_t*)columns[f])[r];
+        else
+          b = ((const uint32_t*)columns[f])[r];
+        if (b >= nb)
+          return fail(LGBM_B200_BIN_OUT_OF_RANGE,
+                      "feature %d row %lld: bin %u >= num_bin %u", f, (long long)r, b, nb);
+        host[(size_t)(r - r0) * ds->stride + f] = (uint8_t)b;
+      }
+    }
+    CUDA_TRY(cudaMemcpy(ds->bins.p + (size_t)r0 * ds->stride, host.data(),
+                        (size_t)(r1 - r0) * ds->stride, cudaMemcpyHostToDevice));
+  }
+  CUDA_TRY(ds->d_feats.alloc(num_features));
+  CUDA_TRY(cudaMemcpy(ds->d_feats.p, ds->feats.data(), num_features * sizeof(DevFeature),
+                      cudaMemcpyHostToDevice));
+  *out = ds.release();
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_dataset_destroy(lgbm_b200_dataset* ds) {
+  if (ds) {
+    DeviceGuard g(ds->device);
+    delete ds;
+  }
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_dataset_num_data(const lgbm_b200_dataset* ds, int64_t* out) {
+  if (!ds || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
+  *out = ds->num_data;
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_learner_create(lgbm_b200_dataset* ds, const lgbm_b200_learner_config* cfg,
+                             lgbm_b200_learner** out) {
+  if (!ds || !cfg || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "learner_create: null");
+  *out = nullptr;
+  if (cfg->num_leaves < 1)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "InvalidNumLeaves: %d", cfg->num_leaves);
+  DeviceGuard g(ds->device);
+  auto l = std::make_unique<lgbm_b200_learner>();
+  int rc = l->init(ds, *cfg);
+  if (rc) return rc;
+  CUDA_TRY(l->gh.alloc((size_t)ds->num_data * 10));
+  CUDA_TRY(l->ghp.alloc(1));
+  CUDA_TRY(cudaMemset(l->ghp.p, 0, sizeof(DevGhParams)));
+  *out = l.release();
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_learner_destroy(lgbm_b200_learner* l) {
+  if (l) {
+    DeviceGuard g(l->device);
+    if (l->stream) cudaStreamDestroy(l->stream);
+    delete l;
+  }
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_learner_grow_tree(lgbm_b200_learner* l, int32_t gh_kind, const void* gh,
+                                const double* quant_scales, lgbm_b200_tree* tree_out,
+                                uint32_t* indices_out, int32_t* leaf_begin_out,
+                                int32_t* leaf_count_out) {
+  if (!l || !gh || !tree_out) return fail(LGBM_B200_INVALID_ARGUMENT, "grow_tree: null argument");
+  DeviceGuard g(l->device);
+  const int64_t N = l->ds->num_data;
+  int mode;
+  DevGhParams hp{};
+  if (gh_kind == LGBM_B200_GH_F32) {
+    mode = GH_FLOAT;
+    std::vector<float2> v(N);
+    const float* gp = (const float*)gh;
+    for (int64_t i = 0; i < N; ++i) v[i] = make_float2(gp[i], gp[N + i]);
+    CUDA_TRY(cudaMemcpyAsync(l->gh.p, v.data(), N * sizeof(float2), cudaMemcpyHostToDevice,
+                             l->stream));
+    CUDA_TRY(cudaStreamSynchronize(l->stream));
+  } else if (gh_kind == LGBM_B200_GH_INT8_PAIR) {
+    if (!quant_scales) return fail(LGBM_B200_INVALID_ARGUMENT, "grow_tree: quant_scales");
+    const int bins = (int)quant_scales[3];
+    mode = bins <= 4 ? GH_QPACK : GH_QLUT;
+    const int8_t* q = (const int8_t*)gh;
+    std::vector<uint16_t> v(N);
+    for (int64_t i = 0; i < N; ++i)
+      v[i] = (uint16_t)((uint8_t)q[2 * i] | ((uint16_t)(uint8_t)q[2 * i + 1] << 8));
+    CUDA_TRY(cudaMemcpyAsync(l->gh.p + 8 * N, v.data(), N * 2, cudaMemcpyHostToDevice,
+                             l->stream));
+    CUDA_TRY(cudaStreamSynchronize(l->stream));
+    hp.grad_scale = quant_scales[0];
+    hp.hess_scale = quant_scales[1];
+    hp.is_const_hess = quant_scales[2] != 0.0 ? 1 : 0;
+    hp.num_quant_bins = bins;
+  } else {
+    return fail(LGBM_B200_INVALID_ARGUMENT, "grow_tree: unknown gh_kind %d", gh_kind);
+  }
+  if (l->gh_mode != mode || l->groups.empty()) {
+    int rc = l->configure_groups(mode);
+    if (rc) return rc;
+  }
+  hp.mode = mode;
+  CUDA_TRY(cudaMemcpyAsync(l->ghp.p, &hp, sizeof(hp), cudaMemcpyHostToDevice, l->stream));
+  l->bind(mode == GH_FLOAT ? (const void*)l->gh.p : (const void*)(l->gh.p + 8 * N), l->ghp.p,
+          nullptr);
+  ObjDev o{};
+  o.N = N;
+  o.gh_mode = mode;
+  o.gh = l->gh.p;
+  o.ghp = l->ghp.p;
+  o.num_quant_bins = hp.num_quant_bins;
+  launch_learner_gradients(o, gh_kind, l->stream);
+  launch_tree(l->d, l->build_blocks, l->build_smem, l->stream);
+  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(cudaStreamSynchronize(l->stream));
+  int rc = read_tree(l, tree_out);
+  if (rc) return rc;
+  const int nl = tree_out->num_leaves;
+  if (leaf_begin_out)
+    CUDA_TRY(cudaMemcpy(leaf_begin_out, l->d.leaf_begin, nl * 4, cudaMemcpyDeviceToHost));
+  if (leaf_count_out)
+    CUDA_TRY(cudaMemcpy(leaf_count_out, l->d.leaf_count, nl * 4, cudaMemcpyDeviceToHost));
+  if (indices_out) {
+    DevBuf<uint32_t> out;
+    CUDA_TRY(out.alloc(N));
+    launch_gather_partition(l->d, out.p, l->stream);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaStreamSynchronize(l->stream));
+    CUDA_TRY(cudaMemcpy(indices_out, out.p, N * 4, cudaMemcpyDeviceToHost));
+  }
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_create(lgbm_b200_dataset* ds, const float* labels,
+                             const lgbm_b200_train_config* cfg, lgbm_b200_booster** out) {
+  if (!ds || !labels || !cfg || !out)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "booster_create: null argument");
+  *out = nullptr;
+  if (cfg->objective != LGBM_B200_OBJECTIVE_BINARY && cfg->objective != LGBM_B200_OBJECTIVE_L2)
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "objective %d not on the device path",
+                cfg->objective);
+  if (cfg->use_quantized_grad && (cfg->num_grad_quant_bins < 1 || cfg->num_grad_quant_bins > 127))
+    return fail(LGBM_B200_INVALID_ARGUMENT, "num_grad_quant_bins %d", cfg->num_grad_quant_bins);
+  if (cfg->objective == LGBM_B200_OBJECTIVE_BINARY && !(cfg->sigmoid > 0.0))
+    return fail(LGBM_B200_INVALID_ARGUMENT, "binary sigmoid %g must be > 0", cfg->sigmoid);
+  DeviceGuard g(ds->device);
+  auto b = std::make_unique<lgbm_b200_booster>();
+  b->ds = ds;
+  b->cfg = *cfg;
+  b->learner = std::make_unique<lgbm_b200_learner>();
+  int rc = b->learner->init(ds, cfg->learner);
+  if (rc) return rc;
+  const int64_t N = ds->num_data;
+  const int mode = !cfg->use_quantized_grad ? GH_FLOAT
+                   : cfg->num_grad_quant_bins <= 4 ? GH_QPACK
+                                                   : GH_QLUT;
+  rc = b->learner->configure_groups(mode);
+  if (rc) return rc;
+  CUDA_TRY(b->label.alloc(N));
+  CUDA_TRY(b->score.alloc(N));
+  CUDA_TRY(b->gh.alloc((size_t)N * 10));
+  CUDA_TRY(b->ghp.alloc(1));
+  CUDA_TRY(b->state.alloc(2));
+  CUDA_TRY(cudaMemset(b->ghp.p, 0, sizeof(DevGhParams)));
+  CUDA_TRY(cudaMemset(b->state.p, 0, 8));
+  CUDA_TRY(cudaMemcpy(b->label.p, labels, N * 4, cudaMemcpyHostToDevice));
+  // boost_from_average (gbdt.rs:619-639): init score on the host from the labels.
+  double init = 0.0;
+  if (cfg->boost_from_average) {
+    const double eps = (double)1e-15f;
+    if (cfg->objective == LGBM_B200_OBJECTIVE_BINARY) {
+      double suml = 0.0;
+      for (int64_t i = 0; i < N; ++i) suml += labels[i] > 0.0f ? 1.0 : 0.0;
+      double pavg = suml / (double)N;  // binary.rs:178-194
+      pavg = std::min(pavg, 1.0 - eps);
+      pavg = std::max(pavg, eps);
+      init = std::log(pavg / (1.0 - pavg)) / cfg->sigmoid;
+    } else {
+      double s = 0.0;  // regression.rs:563-577
+      for (int64_t i = 0; i < N; ++i) s += (double)labels[i];
+      init = s / (double)N;
+    }
+  }
+  b->init_score = init;
+  {
+    std::vector<double> sc(N, std::fabs(init) > (double)1e-15f ? init : 0.0);
+    CUDA_TRY(cudaMemcpy(b->score.p, sc.data(), N * 8, cudaMemcpyHostToDevice));
+  }
+  b->learner->bind(mode == GH_FLOAT ? (const void*)b->gh.p : (const void*)(b->gh.p + 8 * N),
+                   b->ghp.p, b->state.p);
+  ObjDev& o = b->obj;
+  o.N = N;
+  o.objective = cfg->objective;
+  o.gh_mode = mode;
+  o.sigmoid = cfg->sigmoid;
+  o.label = b->label.p;
+  o.score = b->score.p;
+  o.gh = b->gh.p;
+  o.ghp = b->ghp.p;
+  o.num_quant_bins = cfg->num_grad_quant_bins;
+  o.stopped = b->state.p;
+  FinishDev& f = b->fin;
+  f.stopped = b->state.p;
+  f.iter_counter = b->state.p + 1;
+  f.learning_rate = cfg->learning_rate;
+  f.score = b->score.p;
+  *out = b.release();
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_destroy(lgbm_b200_booster* b) {
+  if (b) {
+    DeviceGuard g(b->ds->device);
+    b->destroy_graph();
+    if (b->learner && b->learner->stream) cudaStreamDestroy(b->learner->stream);
+    delete b;
+  }
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_train(lgbm_b200_booster* b, int32_t num_iterations, int32_t* done_out) {
+  if (!b || num_iterations < 0) return fail(LGBM_B200_INVALID_ARGUMENT, "booster_train: args");
+  DeviceGuard g(b->ds->device);
+  int32_t state[2];
+  CUDA_TRY(cudaMemcpy(state, b->state.p, 8, cudaMemcpyDeviceToHost));
+  int rc = b->ensure_capacity(state[1] + num_iterations);
+  if (rc) return rc;
+  cudaStream_t st = b->learner->stream;
+  if (!b->graph_exec) {
+    CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    launch_gradients(b->obj, st);
+    launch_tree(b->learner->d, b->learner->build_blocks, b->learner->build_smem, st);
+    launch_finish_iteration(b->learner->d, b->fin, st);
+    cudaError_t e = cudaStreamEndCapture(st, &b->graph);
+    if (e != cudaSuccess)
+      return fail(LGBM_B200_RUNTIME, "graph capture failed: %s", cudaGetErrorString(e));
+    CUDA_TRY(cudaGraphInstantiate(&b->graph_exec, b->graph, 0));
+  }
+  cudaEvent_t e0, e1;
+  CUDA_TRY(cudaEventCreate(&e0));
+  CUDA_TRY(cudaEventCreate(&e1));
+  CUDA_TRY(cudaEventRecord(e0, st));
+  for (int i = 0; i < num_iterations; ++i) CUDA_TRY(cudaGraphLaunch(b->graph_exec, st));
+  CUDA_TRY(cudaEventRecord(e1, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  cudaEventElapsedTime(&b->last_ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  int32_t after[2];
+  CUDA_TRY(cudaMemcpy(after, b->state.p, 8, cudaMemcpyDeviceToHost));
+  GrowCtrl c;
+  CUDA_TRY(cudaMemcpy(&c, b->learner->ctrl.p, sizeof(GrowCtrl), cudaMemcpyDeviceToHost));
+  if (c.error)
+    return fail(LGBM_B200_RUNTIME, "tree grower reported device error bits 0x%x", c.error);
+  if (done_out) *done_out = after[1] - state[1];
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_num_trees(const lgbm_b200_booster* b, int32_t* out) {
+  if (!b || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
+  int32_t state[2];
+  CUDA_TRY(cudaMemcpy(state, b->state.p, 8, cudaMemcpyDeviceToHost));
+  *out = state[1];
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_get_tree(lgbm_b200_booster* b, int32_t index, lgbm_b200_tree* out) {
+  if (!b || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
+  int32_t n = 0;
+  int rc = lgbm_b200_booster_num_trees(b, &n);
+  if (rc) return rc;
+  if (index < 0 || index >= n) return fail(LGBM_B200_INVALID_ARGUMENT, "tree %d of %d", index, n);
+  const size_t L = b->learner->L, cap = b->capacity, it = index;
+  int32_t nl;
+  CUDA_TRY(cudaMemcpy(&nl, b->fin.rec_num_leaves + it, 4, cudaMemcpyDeviceToHost));
+  if (out->max_leaves < nl) return fail(LGBM_B200_LENGTH_MISMATCH, "tree_out too small");
+  out->num_leaves = nl;
+  auto cp = [&](void* dst, const void* src, size_t bytes) -> cudaError_t {
+    if (!dst || bytes == 0) return cudaSuccess;
+    return cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost);
+  };
+  const size_t ni = nl > 1 ? nl - 1 : 0;
+  CUDA_TRY(cp(out->left_child, b->fin.rec_left + it * L, ni * 4));
+  CUDA_TRY(cp(out->right_child, b->fin.rec_right + it * L, ni * 4));
+  CUDA_TRY(cp(out->split_feature, b->fin.rec_split_feature + it * L, ni * 4));
+  CUDA_TRY(cp(out->internal_count, b->fin.rec_internal_count + it * L, ni * 4));
+  CUDA_TRY(cp(out->threshold_bin, b->fin.rec_threshold + it * L, ni * 4));
+  CUDA_TRY(cp(out->split_gain, b->fin.rec_split_gain + it * L, ni * 4));
+  CUDA_TRY(cp(out->decision_type, b->fin.rec_decision + it * L, ni));
+  CUDA_TRY(cp(out->internal_value, b->fin.rec_internal_value + it * L, ni * 8));
+  CUDA_TRY(cp(out->leaf_value, b->fin.rec_leaf_value + it * L, nl * 8));
+  CUDA_TRY(cp(out->leaf_weight, b->fin.rec_leaf_weight + it * L, nl * 8));
+  CUDA_TRY(cp(out->leaf_count, b->fin.rec_leaf_count + it * L, nl * 4));
+  (void)cap;
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_init_score(const lgbm_b200_booster* b, double* out) {
+  if (!b || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
+  *out = b->init_score;
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_get_scores(lgbm_b200_booster* b, double* out) {
+  if (!b || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
+  CUDA_TRY(cudaMemcpy(out, b->score.p, b->ds->num_data * 8, cudaMemcpyDeviceToHost));
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_get_gradients(lgbm_b200_booster* b, float* g, float* h) {
+  if (!b || !g || !h) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
+  const int64_t N = b->ds->num_data;
+  std::vector<float2> v(N);
+  CUDA_TRY(cudaMemcpy(v.data(), b->gh.p, N * 8, cudaMemcpyDeviceToHost));
+  for (int64_t i = 0; i < N; ++i) {
+    g[i] = v[i].x;
+    h[i] = v[i].y;
+  }
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_phase_ms(const lgbm_b200_booster* b, double* out3) {
+  if (!b || !out3) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
+  out3[0] = 0.0;
+  out3[1] = b->last_ms;
+  out3[2] = 0.0;
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
+                                        int64_t* counts_out) {
+  if (!b || !ms_out || !counts_out) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
+  DeviceGuard g(b->ds->device);
+  int32_t state[2];
+  CUDA_TRY(cudaMemcpy(state, b->state.p, 8, cudaMemcpyDeviceToHost));
+  int rc = b->ensure_capacity(state[1] + 1);
+  if (rc) return rc;
+  cudaStream_t st = b->learner->stream;
+  const int cap = 4 * b->learner->L + 64;
+  std::vector<cudaEvent_t> evs(2 * (size_t)cap);
+  for (auto& e : evs) CUDA_TRY(cudaEventCreate(&e));
+  std::vector<int> cls(cap);
+  LaunchProfiler prof;
+  prof.ev = reinterpret_cast<cudaEvent_t(*)[2]>(evs.data());
+  prof.cls = cls.data();
+  prof.cap = cap;
+  prof.n = 0;
+  launch_gradients(b->obj, st, &prof);
+  launch_tree(b->learner->d, b->learner->build_blocks, b->learner->build_smem, st, &prof);
+  launch_finish_iteration(b->learner->d, b->fin, st, &prof);
+  cudaError_t le = cudaGetLastError();
+  cudaError_t se = cudaStreamSynchronize(st);
+  if (le != cudaSuccess || se != cudaSuccess) {
+    for (auto& e : evs) cudaEventDestroy(e);
+    return fail(LGBM_B200_RUNTIME, "profiled iteration failed: %s",
+                cudaGetErrorString(le != cudaSuccess ? le : se));
+  }
+  for (int k = 0; k < KC_COUNT; ++k) ms_out[k] = 0.0;
+  int64_t launches = 0;
+  for (int i = 0; i < prof.n; ++i) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, prof.ev[i][0], prof.ev[i][1]);
+    ms_out[cls[i]] += ms;
+    launches += (cls[i] == KC_GRAD) ? 4 : (cls[i] == KC_FINISH ? 2 : 1);
+  }
+  for (auto& e : evs) cudaEventDestroy(e);
+  GrowCtrl c;
+  CUDA_TRY(cudaMemcpy(&c, b->learner->ctrl.p, sizeof(GrowCtrl), cudaMemcpyDeviceToHost));
+  if (c.error)
+    return fail(LGBM_B200_RUNTIME, "tree grower reported device error bits 0x%x", c.error);
+  counts_out[0] = launches;
+  counts_out[1] = c.num_builds;
+  counts_out[2] = c.rows_built;
+  counts_out[3] = c.num_splits;
+  return LGBM_B200_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,1202 @@
+// Hand-written sm_100a kernels of the leaf-wise histogram tree learner.
+//
+// Per split s the host enqueues (no host synchronisation anywhere in a tree):
+//   k_prepare(s)   1 CTA  apply split s-1 (Tree::split + child LeafSplits seeding),
+//                         BeforeFindBestSplit gates, smaller/larger choice, pool slots
+//   k_build        grid   shared-memory-privatised histogram of the smaller child
+//   k_fixscan      F CTAs decode + FixHistogram + compaction + parent-smaller
+//                         subtraction + REVERSE/FORWARD threshold scans; the last CTA
+//                         does the per-leaf and cross-leaf argmax
+//   k_partition    grid   stable single-pass partition of the chosen leaf's rows
+// All decisions live in GrowCtrl on the device; kernels after a finished tree
+// return at once.
+#include <cstdio>
+
+#include "kernels.cuh"
+
+namespace lgbm_b200 {
+
+namespace {
+
+constexpr int kBuildThreads = 512;
+constexpr int kMinRowsPerBlock = 2048;
+constexpr int kScanThreads = 128;
+constexpr int kPartThreads = 256;
+constexpr int kPartItems = 8;
+constexpr int kPartTile = kPartThreads * kPartItems;
+constexpr long long kSpinLimit = 1ll << 22;
+
+__device__ __forceinline__ bool leaf_buildable(const DevLeafSplits& l) {
+  return l.sum_h > 0.0 && l.num_data > 0;  // learner.rs:2477-2481
+}
+
+// Decoding of the raw integer accumulators into f64 histogram cells. For the
+// quantized modes the result equals the reference's f64 fold exactly: every
+// dequantized level is an integer multiple of the ulp of the smallest nonzero
+// level, so all partial sums of the reference's sequential fold are exact.
+__device__ __forceinline__ double decode_g(const DevGhParams& p, long long v) {
+  return (double)v * p.unit_g;
+}
+__device__ __forceinline__ double decode_h(const DevGhParams& p, long long v) {
+  if (p.mode == GH_QPACK) {
+    const long long hl = v & 0xffffffffll;
+    const long long c3 = v >> 32;
+    return (double)hl * p.unit_h + (double)c3 * p.v3h;
+  }
+  return (double)v * p.unit_h;
+}
+
+// ------------------------------------------------------------------------------------
+// Histogram build: one CTA accumulates a row range of one feature group in shared
+// memory with 64-bit integer atomics, then merges into the global raw accumulator.
+// ------------------------------------------------------------------------------------
+
+template <int MODE>
+struct GhValue;
+
+template <>
+struct GhValue<GH_FLOAT> {
+  long long a, b;
+  __device__ __forceinline__ void load(const void* gh, uint32_t row, const DevGhParams& p,
+                                       const long long*, const long long*) {
+    const float2 v = reinterpret_cast<const float2*>(gh)[row];
+    a = __double2ll_rn((double)v.x * p.scale_g);
+    b = __double2ll_rn((double)v.y * p.scale_h);
+  }
+};
+
+template <>
+struct GhValue<GH_QLUT> {
+  long long a, b;
+  __device__ __forceinline__ void load(const void* gh, uint32_t row, const DevGhParams&,
+                                       const long long* lut_g, const long long* lut_h) {
+    const uint16_t q = reinterpret_cast<const uint16_t*>(gh)[row];
+    a = lut_g[(int)(int8_t)(q & 0xff) + 128];
+    b = lut_h[(int)(int8_t)(q >> 8) + 128];
+  }
+};
+
+// Packed form for num_grad_quant_bins <= 4: qg in [-2,2] (linear levels), qh in [0,4]
+// where only level 3 is not a multiple of level 1. One int64 per row:
+//   bits 0..20 signed sum of qg | bits 21..41 sum of qh over levels {1,2,4} | bits 42.. count of qh==3
+template <>
+struct GhValue<GH_QPACK> {
+  long long a, b;
+  __device__ __forceinline__ void load(const void* gh, uint32_t row, const DevGhParams&,
+                                       const long long*, const long long*) {
+    const uint16_t q = reinterpret_cast<const uint16_t*>(gh)[row];
+    const long long qg = (long long)(int8_t)(q & 0xff);
+    const int qh = (int)(int8_t)(q >> 8);
+    const long long hl = qh == 3 ? 0 : qh;
+    const long long c3 = qh == 3 ? 1 : 0;
+    a = qg + (hl << 21) + (c3 << 42);
+    b = 0;
+  }
+};
+
+__device__ __forceinline__ void unpack_qpack(unsigned long long v, long long* g, long long* hlc3) {
+  const long long sv = (long long)v;
+  const long long gg = (sv << 43) >> 43;  // sign-extend bits 0..20
+  const unsigned long long rest = (unsigned long long)(sv - gg) >> 21;
+  const long long hl = (long long)(rest & ((1ull << 21) - 1));
+  const long long c3 = (long long)(rest >> 21);
+  *g = gg;
+  *hlc3 = hl | (c3 << 32);
+}
+
+template <int MODE>
+__device__ __forceinline__ void build_block(const uint8_t* __restrict__ bins, int32_t stride,
+                                            const uint32_t* __restrict__ idx, int32_t begin,
+                                            int32_t r0, int32_t r1, bool identity,
+                                            const void* __restrict__ gh, const DevGhParams& p,
+                                            const DevFeatureGroup& grp,
+                                            const int32_t* s_binoff, const uint8_t* s_used,
+                                            const long long* s_lut_g, const long long* s_lut_h,
+                                            unsigned long long* acc) {
+  constexpr int kWords = MODE == GH_QPACK ? 1 : 2;
+  const int nf = grp.f_end - grp.f_begin;
+  const int nchunks = (nf + 15) >> 4;
+  for (int32_t k = r0 + (int32_t)threadIdx.x; k < r1; k += (int32_t)blockDim.x) {
+    const uint32_t row = identity ? (uint32_t)(begin + k) : idx[begin + k];
+    GhValue<MODE> v;
+    v.load(gh, row, p, s_lut_g, s_lut_h);
+    const uint8_t* rp = bins + (size_t)row * stride + grp.f_begin;
+    for (int c = 0; c < nchunks; ++c) {
+      const uint4 w = *reinterpret_cast<const uint4*>(rp + 16 * c);
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int fl = 16 * c + j;
+        if (fl >= nf) break;
+        if (!s_used[fl]) continue;
+        const uint32_t bin = (words[j >> 2] >> (8 * (j & 3))) & 0xffu;
+        unsigned long long* cell = acc + (size_t)kWords * (s_binoff[fl] + bin);
+        atomicAdd(cell, (unsigned long long)v.a);
+        if (kWords == 2) atomicAdd(cell + 1, (unsigned long long)v.b);
+      }
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d) {
+  extern __shared__ unsigned long long acc[];
+  __shared__ int32_t s_binoff[128];
+  __shared__ uint8_t s_used[128];
+  __shared__ long long s_lut[MODE == GH_QLUT ? 512 : 1];
+  GrowCtrl* c = d.ctrl;
+  if (c->done || !c->do_find) return;
+  const int32_t leaf = c->smaller_leaf;
+  const DevLeafSplits ls = d.ls[leaf];
+  if (!leaf_buildable(ls)) return;
+  const int32_t begin = d.leaf_begin[leaf];
+  const int32_t count = d.leaf_count[leaf];
+  const int32_t buf = d.leaf_buf[leaf];
+  const DevFeatureGroup grp = d.groups[blockIdx.y];
+  const int nf = grp.f_end - grp.f_begin;
+  int nb_active = (count + kMinRowsPerBlock - 1) / kMinRowsPerBlock;
+  if (nb_active > (int)gridDim.x) nb_active = gridDim.x;
+  if (nb_active < 1) nb_active = 1;
+  // QPACK field widths hold at most 2^18 rows per CTA.
+  if (MODE == GH_QPACK) {
+    const int need = (count + (1 << 18) - 1) >> 18;
+    if (nb_active < need) nb_active = need;
+  }
+  if ((int)blockIdx.x >= nb_active) return;
+  const int32_t per = (count + nb_active - 1) / nb_active;
+  const int32_t r0 = per * (int32_t)blockIdx.x;
+  const int32_t r1 = min(count, r0 + per);
+  if (r0 >= r1) return;
+
+  constexpr int kWords = MODE == GH_QPACK ? 1 : 2;
+  const int nwords = kWords * grp.num_bins;
+  for (int i = threadIdx.x; i < nwords; i += blockDim.x) acc[i] = 0ull;
+  // Features the parent could not split are neither built nor scanned
+  // (learner.rs:2003-2020 build mask).
+  {
+    const uint8_t* ps = d.splittable + (size_t)c->left_leaf * d.F;
+    const bool sub = c->use_subtract != 0;
+    for (int fl = threadIdx.x; fl < nf; fl += blockDim.x)
+      s_used[fl] = sub ? ps[grp.f_begin + fl] : (uint8_t)1;
+  }
+  for (int fl = threadIdx.x; fl < nf; fl += blockDim.x)
+    s_binoff[fl] = d.feat[grp.f_begin + fl].bin_off - grp.bin_base;
+  if (MODE == GH_QLUT)
+    for (int i = threadIdx.x; i < 512; i += blockDim.x)
+      s_lut[i] = i < 256 ? d.ghp->lut_g[i] : d.ghp->lut_h[i - 256];
+  __syncthreads();
+  const DevGhParams& p = *d.ghp;
+  const uint32_t* idx = buf == 1 ? d.idx1 : d.idx0;
+  build_block<MODE>(d.bins, d.stride, idx, begin, r0, r1, buf == 2, d.gh, p, grp, s_binoff,
+                    s_used, s_lut, s_lut + 256, acc);
+  __syncthreads();
+  long long* raw = d.raw + 2 * (size_t)grp.bin_base;
+  for (int w = threadIdx.x; w < grp.num_bins; w += blockDim.x) {
+    if (MODE == GH_QPACK) {
+      const unsigned long long v = acc[w];
+      if (v) {
+        long long g, h;
+        unpack_qpack(v, &g, &h);
+        if (g) atomicAdd((unsigned long long*)&raw[2 * w], (unsigned long long)g);
+        if (h) atomicAdd((unsigned long long*)&raw[2 * w + 1], (unsigned long long)h);
+      }
+    } else {
+      const unsigned long long a = acc[2 * w], b = acc[2 * w + 1];
+      if (a) atomicAdd((unsigned long long*)&raw[2 * w], a);
+      if (b) atomicAdd((unsigned long long*)&raw[2 * w + 1], b);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// Threshold scan of one direction of one feature by one warp
+// (find_best_split_cpu_native, lgbm-compute/src/kernels/split.rs:8970-9329).
+// The dependent f64 chains (running gradient / hessian sums, seeded with kEpsilon)
+// run sequentially in one lane each, in the reference's order; the integer count
+// prefix and the per-candidate gains run across the warp.
+// ------------------------------------------------------------------------------------
+
+struct ScanCand {
+  int32_t has;         // a candidate cleared min_gain_shift (is_splittable)
+  int32_t best_k;      // -1 if none
+  double gain;
+  double slg, slh;
+  int32_t lc;
+  int32_t thr;
+};
+
+struct ScanLeaf {
+  double sum_g, sum_h, parent_output;
+  int32_t num_data;
+};
+
+__device__ __forceinline__ void warp_best(double& gain, int32_t& k) {
+  // max gain, ties to the smallest k (first in scan order)
+  for (int o = 16; o > 0; o >>= 1) {
+    const double og = __shfl_xor_sync(0xffffffffu, gain, o);
+    const int32_t ok = __shfl_xor_sync(0xffffffffu, k, o);
+    if (og > gain || (og == gain && ok >= 0 && (k < 0 || ok < k))) {
+      gain = og;
+      k = ok;
+    }
+  }
+}
+
+__device__ void scan_direction(const double* hist, const DevFeature& f, const DevGainConfig& cfg,
+                               const ScanLeaf& leaf, bool forward, double* pg, double* ph,
+                               int32_t* pc, ScanCand* out) {
+  const int lane = threadIdx.x & 31;
+  const double eps = k_eps();
+  const int nb = f.num_bin;
+  const int offset = f.offset;
+  const int na = (f.flags & 2) ? 1 : 0;
+  const bool skip_def = (f.flags & 1) != 0;
+  const double bumped = leaf.sum_h + 2.0 * eps;
+  const double cnt_factor = (double)leaf.num_data / bumped;
+  const double gain_shift = d_leaf_gain_full(cfg, leaf.sum_g, bumped, leaf.num_data,
+                                             leaf.parent_output);
+  const double min_gain_shift = gain_shift + cfg.min_gain_to_split;
+  const int32_t min_data = cfg.min_data_in_leaf;
+  const double min_hess = cfg.min_sum_hessian_in_leaf;
+
+  int count, t0;  // t = forward ? t0 + k : t0 - k
+  double g_init = 0.0, h_init = eps;
+  int32_t c_init = 0;
+  if (!forward) {
+    count = max(nb - 1 - na, 0);
+    t0 = nb - 1 - offset - na;
+  } else {
+    const bool run_forward = (f.flags & 4) != 0;
+    const bool na_pre = na && offset == 1;
+    if (!run_forward) {
+      count = 0;
+    } else {
+      count = max(nb - 1 - offset, 0) + (na_pre ? 1 : 0);
+    }
+    t0 = na_pre ? -1 : 0;
+    if (na_pre && count > 0) {
+      // NA preamble (split.rs:9183-9199): seed with the leaf totals and subtract every
+      // explicit bin in ascending order.
+      double gg = leaf.sum_g, hh = bumped - eps;
+      int32_t cc = leaf.num_data;
+      for (int i = 0; i < nb - offset; ++i) {
+        gg -= hist[2 * i];
+        hh -= hist[2 * i + 1];
+        cc -= d_round_int(hist[2 * i + 1] * cnt_factor);
+      }
+      g_init = gg;
+      h_init = hh;
+      c_init = cc;
+    }
+  }
+  auto active_at = [&](int k, int* t_out) -> bool {
+    const int t = forward ? t0 + k : t0 - k;
+    *t_out = t;
+    const bool skip = skip_def && (t + offset) == f.default_bin;
+    if (!forward) return (t >= (1 - offset)) && !skip;
+    return !skip;
+  };
+  // Sequential f64 chains: lane 0 gradient, lane 1 hessian.
+  if (lane < 2 && count > 0) {
+    double acc = lane == 0 ? g_init : h_init;
+    for (int k = 0; k < count; ++k) {
+      int t;
+      const bool act = active_at(k, &t);
+      if (act && t >= 0) acc += hist[2 * t + lane];
+      if (lane == 0)
+        pg[k] = acc;
+      else
+        ph[k] = acc;
+    }
+  }
+  // Integer count prefix across the warp.
+  int32_t carry = c_init;
+  for (int k0 = 0; k0 < count; k0 += 32) {
+    const int k = k0 + lane;
+    int32_t v = 0;
+    if (k < count) {
+      int t;
+      if (active_at(k, &t) && t >= 0) v = d_round_int(hist[2 * t + 1] * cnt_factor);
+    }
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += n;
+    }
+    if (k < count) pc[k] = carry + v;
+    carry += __shfl_sync(0xffffffffu, v, 31);
+  }
+  __syncwarp();
+  // First step that breaks the scan (sticky `done`).
+  int32_t kstar = 0x7fffffff;
+  for (int k = lane; k < count; k += 32) {
+    int t;
+    const bool act = active_at(k, &t);
+    const int32_t c_own = pc[k];
+    const int32_t c_oth = leaf.num_data - c_own;
+    const double h_own = ph[k];
+    const double h_oth = bumped - h_own;
+    const bool cont = c_own < min_data || h_own < min_hess;
+    const bool brk = c_oth < min_data || h_oth < min_hess;
+    if (act && !cont && brk) {
+      kstar = k;
+      break;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) kstar = min(kstar, __shfl_xor_sync(0xffffffffu, kstar, o));
+  // Candidate gains.
+  double best_gain = kNegInf;
+  int32_t best_k = -1;
+  int32_t has = 0;
+  const int kend = min(count, kstar);
+  for (int k = lane; k < kend; k += 32) {
+    int t;
+    const bool act = active_at(k, &t);
+    if (!act) continue;
+    const int32_t c_own = pc[k];
+    const int32_t c_oth = leaf.num_data - c_own;
+    const double h_own = ph[k];
+    if (c_own < min_data || h_own < min_hess) continue;
+    const double g_own = pg[k];
+    const double h_oth = bumped - h_own;
+    const double g_oth = leaf.sum_g - g_own;
+    double gain;
+    if (!forward)  // own side is the right child
+      gain = d_split_gain(cfg, g_oth, h_oth, g_own, h_own, c_oth, c_own, leaf.parent_output);
+    else
+      gain = d_split_gain(cfg, g_own, h_own, g_oth, h_oth, c_own, c_oth, leaf.parent_output);
+    if (gain > min_gain_shift) {
+      has = 1;
+      if (gain > best_gain) {
+        best_gain = gain;
+        best_k = k;
+      }
+    }
+  }
+  has = __any_sync(0xffffffffu, has) ? 1 : 0;
+  warp_best(best_gain, best_k);
+  if (lane == 0) {
+    out->has = has;
+    out->best_k = best_k;
+    out->gain = best_gain;
+    if (best_k >= 0) {
+      int t;
+      active_at(best_k, &t);
+      if (!forward) {
+        out->slg = leaf.sum_g - pg[best_k];
+        out->slh = bumped - ph[best_k];
+        out->lc = leaf.num_data - pc[best_k];
+        out->thr = t - 1 + offset;
+      } else {
+        out->slg = pg[best_k];
+        out->slh = ph[best_k];
+        out->lc = pc[best_k];
+        out->thr = t + offset;
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// Finalization of the winning candidate (split.rs:9267-9326).
+__device__ DevSplitInfo finalize_split(const DevGainConfig& cfg, const ScanLeaf& leaf,
+                                       const ScanCand& rev, const ScanCand& fwd) {
+  const double eps = k_eps();
+  const double bumped = leaf.sum_h + 2.0 * eps;
+  const double min_gain_shift =
+      d_leaf_gain_full(cfg, leaf.sum_g, bumped, leaf.num_data, leaf.parent_output) +
+      cfg.min_gain_to_split;
+  bool splittable = rev.has || fwd.has;
+  double best_gain = kNegInf;
+  double slg = 0.0, slh = 0.0;
+  int32_t lc = 0, thr = 0, dl = 1;
+  if (rev.best_k >= 0) {
+    best_gain = rev.gain;
+    slg = rev.slg;
+    slh = rev.slh;
+    lc = rev.lc;
+    thr = rev.thr;
+    dl = 1;
+  }
+  if (fwd.best_k >= 0 && fwd.gain > best_gain) {
+    best_gain = fwd.gain;
+    slg = fwd.slg;
+    slh = fwd.slh;
+    lc = fwd.lc;
+    thr = fwd.thr;
+    dl = 0;
+  }
+  if (!(splittable && best_gain > kNegInf)) return d_split_none();
+  DevSplitInfo s;
+  const int32_t rc = leaf.num_data - lc;
+  s.threshold = (uint32_t)thr;
+  s.default_left = dl;
+  s.left_count = lc;
+  s.right_count = rc;
+  s.gain = best_gain - min_gain_shift;
+  s.left_sum_gradient = slg;
+  s.left_sum_hessian = slh - eps;
+  const double rsg = leaf.sum_g - slg;
+  const double rsh = bumped - slh;
+  s.right_sum_gradient = rsg;
+  s.right_sum_hessian = rsh - eps;
+  s.left_output = d_leaf_output_full(cfg, cfg.use_smoothing, slg, slh, lc, leaf.parent_output);
+  s.right_output = d_leaf_output_full(cfg, cfg.use_smoothing, rsg, rsh, rc, leaf.parent_output);
+  return s;
+}
+
+// ------------------------------------------------------------------------------------
+// Per-split control kernel.
+// ------------------------------------------------------------------------------------
+
+__global__ void k_tree_init(GrowDev d) {
+  GrowCtrl* c = d.ctrl;
+  const bool stopped = d.stopped && *d.stopped;
+  const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int gsz = gridDim.x * blockDim.x;
+  for (int l = gtid; l < d.L; l += gsz) {
+    d.leaf_begin[l] = 0;
+    d.leaf_count[l] = 0;
+    d.leaf_buf[l] = 0;
+    d.slot_of_leaf[l] = -1;
+    d.best[l] = d_split_none();
+    d.best_feature[l] = -1;
+    d.t_left[l] = 0;
+    d.t_right[l] = 0;
+    d.t_split_feature[l] = 0;
+    d.t_threshold[l] = 0;
+    d.t_split_gain[l] = 0.f;
+    d.t_decision[l] = 0;
+    d.t_leaf_value[l] = 0.0;
+    d.t_leaf_weight[l] = 0.0;
+    d.t_leaf_count[l] = 0;
+    d.t_internal_value[l] = 0.0;
+    d.t_internal_count[l] = 0;
+    d.t_leaf_depth[l] = 0;
+    d.t_leaf_parent[l] = 0;
+  }
+  const size_t nsp = (size_t)d.L * d.F;
+  for (size_t i = gtid; i < nsp; i += gsz) d.splittable[i] = 1;
+  for (int i = gtid; i < d.max_tiles; i += gsz) d.part_status[i] = 0ull;
+  if (gtid == 0) {
+    const uint32_t epoch = c->epoch;
+    const uint32_t err = c->error;
+    GrowCtrl z = {};
+    *c = z;
+    c->epoch = epoch;
+    c->error = err;
+    c->num_leaves = 1;
+    c->left_leaf = 0;
+    c->right_leaf = -1;
+    c->next_slot = 0;
+    d.leaf_count[0] = (int32_t)d.N;
+    d.leaf_buf[0] = 2;
+    const DevGhParams& p = *d.ghp;
+    // LeafSplits::init over all rows (leaf_splits.rs:75-92): integer root sums
+    // decoded exactly like histogram cells.
+    DevLeafSplits r;
+    r.num_data = (int32_t)d.N;
+    r._pad = 0;
+    r.sum_g = decode_g(p, p.root_g);
+    r.sum_h = decode_h(p, p.root_h);
+    // self_output: max_delta_step clamps, no smoothing (leaf_splits.rs:128-145)
+    r.weight = d_leaf_output_full(d.gain, false, r.sum_g, r.sum_h, 0, 0.0);
+    d.ls[0] = r;
+    d.t_leaf_value[0] = r.weight;
+    d.t_leaf_count[0] = (int32_t)d.N;
+    d.t_leaf_parent[0] = -1;
+    if (stopped) c->done = 1;
+    if (!(r.sum_h > 0.0)) {
+      c->error |= kErrRootHessian;
+      c->done = 1;
+    }
+  }
+}
+
+__global__ void k_prepare(GrowDev d, int s) {
+  GrowCtrl* c = d.ctrl;
+  if (threadIdx.x != 0) return;
+  if (c->pending) {
+    // ---- apply the split chosen at step s-1 (learner.rs:3895-4092) ----
+    const int32_t leaf = c->split_leaf;
+    const int32_t nr = c->num_leaves;
+    const int32_t f = c->split_feature;
+    const DevSplitInfo b = c->split;
+    const int32_t lc = c->part_left_total;
+    const int32_t rc = d.leaf_count[leaf] - lc;
+    const int32_t src = d.leaf_buf[leaf];
+    const int32_t dst = src == 1 ? 0 : 1;
+    d.leaf_begin[nr] = d.leaf_begin[leaf] + lc;
+    d.leaf_count[leaf] = lc;
+    d.leaf_count[nr] = rc;
+    d.leaf_buf[leaf] = dst;
+    d.leaf_buf[nr] = dst;
+    // Tree::split (lgbm-model/src/tree.rs:614-690)
+    const int32_t node = nr - 1;
+    const int32_t parent = d.t_leaf_parent[leaf];
+    if (parent >= 0) {
+      if (d.t_right[parent] == ~leaf)
+        d.t_right[parent] = node;
+      else
+        d.t_left[parent] = node;
+    }
+    d.t_split_feature[node] = f;
+    d.t_split_gain[node] = (float)(b.gain + d.gain.min_gain_to_split);
+    d.t_threshold[node] = b.threshold;
+    d.t_internal_value[node] = d.t_leaf_value[leaf];
+    d.t_internal_count[node] = lc + rc;
+    d.t_left[node] = ~leaf;
+    d.t_right[node] = ~nr;
+    int8_t dt = 0;
+    if (b.default_left) dt |= 2;
+    dt |= (int8_t)((d.feat[f].missing_type & 3) << 2);
+    d.t_decision[node] = dt;
+    d.t_leaf_value[leaf] = b.left_output;
+    d.t_leaf_weight[leaf] = b.left_sum_hessian;
+    d.t_leaf_count[leaf] = lc;
+    d.t_leaf_value[nr] = b.right_output;
+    d.t_leaf_weight[nr] = b.right_sum_hessian;
+    d.t_leaf_count[nr] = rc;
+    d.t_leaf_depth[nr] = d.t_leaf_depth[leaf] + 1;
+    d.t_leaf_depth[leaf] += 1;
+    d.t_leaf_parent[leaf] = node;
+    d.t_leaf_parent[nr] = node;
+    // child LeafSplits seeded from the SplitInfo (learner.rs:4061-4089)
+    DevLeafSplits L, R;
+    L.num_data = lc;
+    L._pad = 0;
+    L.sum_g = b.left_sum_gradient;
+    L.sum_h = b.left_sum_hessian;
+    L.weight = b.left_output;
+    R.num_data = rc;
+    R._pad = 0;
+    R.sum_g = b.right_sum_gradient;
+    R.sum_h = b.right_sum_hessian;
+    R.weight = b.right_output;
+    d.ls[leaf] = L;
+    d.ls[nr] = R;
+    d.best[leaf] = d_split_none();
+    d.best_feature[leaf] = -1;
+    d.best[nr] = d_split_none();
+    d.best_feature[nr] = -1;
+    c->left_leaf = leaf;
+    c->right_leaf = nr;
+    c->num_leaves = nr + 1;
+    c->num_splits += 1;
+    c->pending = 0;
+  }
+  if (c->done || s >= d.L - 1) {
+    c->do_find = 0;
+    return;
+  }
+  c->epoch += 1;
+  c->part_ticket = 0;
+  c->part_left_total = 0;
+  c->scan_counter = 0;
+  // ---- BeforeFindBestSplit (learner.rs:1808-1839) ----
+  const int32_t left = c->left_leaf, right = c->right_leaf;
+  const int32_t num_left = d.leaf_count[left];
+  const int32_t min2 = d.gain.min_data_in_leaf * 2;
+  int32_t did = 1;
+  if (d.max_depth > 0 && d.t_leaf_depth[left] >= d.max_depth) {
+    d.best[left].gain = kNegInf;
+    if (right >= 0) d.best[right].gain = kNegInf;
+    did = 0;
+  } else if (right >= 0) {
+    if (d.leaf_count[right] < min2 && num_left < min2) {
+      d.best[left].gain = kNegInf;
+      d.best[right].gain = kNegInf;
+      did = 0;
+    }
+  } else if (num_left < min2) {
+    d.best[left].gain = kNegInf;
+    did = 0;
+  }
+  c->do_find = did;
+  if (!did) return;
+  // ---- smaller child + pool slots (learner.rs:1882-1916) ----
+  int32_t smaller, larger;
+  if (right < 0) {
+    smaller = left;
+    larger = -1;
+  } else if (d.leaf_count[left] < d.leaf_count[right]) {
+    smaller = left;
+    larger = right;
+  } else {
+    smaller = right;
+    larger = left;
+  }
+  int32_t ss, lsl = -1, use_sub = 0;
+  if (right < 0) {
+    if (d.slot_of_leaf[left] < 0) d.slot_of_leaf[left] = c->next_slot++;
+    ss = d.slot_of_leaf[left];
+  } else {
+    const int32_t parent_slot = d.slot_of_leaf[left];
+    use_sub = parent_slot >= 0 ? 1 : 0;
+    if (smaller == left) {
+      d.slot_of_leaf[right] = parent_slot;
+      d.slot_of_leaf[left] = c->next_slot++;
+      ss = d.slot_of_leaf[left];
+    } else {
+      d.slot_of_leaf[right] = c->next_slot++;
+      ss = d.slot_of_leaf[right];
+    }
+    lsl = parent_slot;
+    if (!use_sub) {
+      // Cannot happen with a one-slot-per-leaf pool: a leaf is split only after its
+      // histogram was built or derived.
+      c->error |= kErrNoParentHistogram;
+      c->done = 1;
+      c->do_find = 0;
+      return;
+    }
+  }
+  if (leaf_buildable(d.ls[smaller])) {
+    c->num_builds += 1;
+    c->rows_built += d.leaf_count[smaller];
+  }
+  c->smaller_leaf = smaller;
+  c->larger_leaf = larger;
+  c->smaller_slot = ss;
+  c->larger_slot = lsl;
+  c->use_subtract = use_sub;
+}
+
+// ------------------------------------------------------------------------------------
+// Decode + FixHistogram + compaction + subtraction + scans, one CTA per feature.
+// The last CTA to finish does the argmax (scan_leaf_histogram's cross-feature
+// argmax, learner.rs:3314-3340, then arg_max over leaves, learner.rs:4537-4551).
+// ------------------------------------------------------------------------------------
+
+__device__ void pick_split(const GrowDev& d) {
+  GrowCtrl* c = d.ctrl;
+  __shared__ double s_gain[kScanThreads];
+  __shared__ int32_t s_key[kScanThreads];
+  const int tid = threadIdx.x;
+  if (c->do_find) {
+    for (int sel = 0; sel < 2; ++sel) {
+      const int32_t leaf = sel == 0 ? c->smaller_leaf : c->larger_leaf;
+      if (leaf < 0) continue;
+      if (!__ldcg(&d.scan_ok[sel])) {
+        if (tid == 0) {
+          d.best[leaf] = d_split_none();
+          d.best_feature[leaf] = -1;
+        }
+        continue;
+      }
+      double bg = kNegInf;
+      int32_t bf = -1;
+      for (int f = tid; f < d.F; f += blockDim.x) {
+        const double g = __ldcg(&d.scan_out[sel * d.F + f].gain);
+        d.splittable[(size_t)leaf * d.F + f] = g > kNegInf ? 1 : 0;
+        if (g > kNegInf && d_split_gt(g, f, bg, bf)) {
+          bg = g;
+          bf = f;
+        }
+      }
+      s_gain[tid] = bg;
+      s_key[tid] = bf;
+      __syncthreads();
+      if (tid == 0) {
+        for (int i = 1; i < (int)blockDim.x; ++i)
+          if (s_key[i] >= 0 && d_split_gt(s_gain[i], s_key[i], bg, bf)) {
+            bg = s_gain[i];
+            bf = s_key[i];
+          }
+        d.best[leaf] = bf >= 0 ? d.scan_out[sel * d.F + bf] : d_split_none();
+        d.best_feature[leaf] = bf;
+      }
+      __syncthreads();
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int32_t bl = 0;
+    for (int i = 1; i < d.L; ++i)
+      if (d_split_gt(d.best[i].gain, d.best_feature[i], d.best[bl].gain, d.best_feature[bl]))
+        bl = i;
+    const DevSplitInfo b = d.best[bl];
+    if (b.gain <= 0.0) {
+      c->done = 1;
+    } else {
+      c->pending = 1;
+      c->split_leaf = bl;
+      c->split_feature = d.best_feature[bl];
+      c->split = b;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
+  __shared__ double s_hist[2][2 * kMaxBins];
+  __shared__ double s_pg[4][kMaxBins];
+  __shared__ double s_ph[4][kMaxBins];
+  __shared__ int32_t s_pc[4][kMaxBins];
+  __shared__ ScanCand s_cand[4];
+  __shared__ bool s_last;
+  GrowCtrl* c = d.ctrl;
+  const int f = blockIdx.x;
+  const int tid = threadIdx.x;
+  const bool live = !c->done && c->do_find;
+  if (live) {
+    const int32_t S = c->smaller_leaf, Lg = c->larger_leaf;
+    const DevLeafSplits lss = d.ls[S];
+    const bool used =
+        !c->use_subtract || d.splittable[(size_t)c->left_leaf * d.F + f] != 0;
+    const DevFeature ft = d.feat[f];
+    const int nb = ft.num_bin;
+    if (used) {
+      const DevGhParams& p = *d.ghp;
+      const bool buildable = leaf_buildable(lss);
+      long long* raw = d.raw + 2 * (size_t)ft.bin_off;
+      for (int i = tid; i < nb; i += blockDim.x) {
+        double g = 0.0, h = 0.0;
+        if (buildable) {
+          g = decode_g(p, raw[2 * i]);
+          h = decode_h(p, raw[2 * i + 1]);
+          raw[2 * i] = 0;
+          raw[2 * i + 1] = 0;
+        }
+        s_hist[0][2 * i] = g;
+        s_hist[0][2 * i + 1] = h;
+      }
+      __syncthreads();
+      // FixHistogram (fix_histogram.rs:50-81): sequential ascending subtraction.
+      const int mfb = ft.most_freq_bin;
+      if (buildable && mfb > 0 && mfb < nb && (tid == 0 || tid == 32)) {
+        const int w = tid == 0 ? 0 : 1;
+        double acc = w == 0 ? lss.sum_g : lss.sum_h;
+        for (int i = 0; i < nb; ++i)
+          if (i != mfb) acc -= s_hist[0][2 * i + w];
+        s_hist[0][2 * mfb + w] = acc;
+      }
+      __syncthreads();
+      // compact_histogram (learner.rs:4460-4486)
+      if (ft.offset > 0) {
+        const int off = ft.offset;
+        double tmp[2 * ((2 * kMaxBins + kScanThreads - 1) / kScanThreads)];
+        int n = 0;
+        for (int i = tid; i < 2 * nb; i += blockDim.x) {
+          const int src = i + 2 * off;
+          tmp[n++] = src < 2 * nb ? s_hist[0][src] : 0.0;
+        }
+        __syncthreads();
+        n = 0;
+        for (int i = tid; i < 2 * nb; i += blockDim.x) s_hist[0][i] = tmp[n++];
+        __syncthreads();
+      }
+      // store the smaller child's slot; larger = parent - smaller in the parent's slot
+      double* ps = d.pool + (size_t)c->smaller_slot * d.slot_len + ft.slot_off;
+      for (int i = tid; i < 2 * nb; i += blockDim.x) ps[i] = s_hist[0][i];
+      if (Lg >= 0) {
+        double* pl = d.pool + (size_t)c->larger_slot * d.slot_len + ft.slot_off;
+        for (int i = tid; i < 2 * nb; i += blockDim.x) {
+          const double v = pl[i] - s_hist[0][i];
+          pl[i] = v;
+          s_hist[1][i] = v;
+        }
+      }
+      __syncthreads();
+      const int warp = tid >> 5;
+      const int sel = warp >> 1;
+      const bool fwd = (warp & 1) != 0;
+      const int32_t leaf = sel == 0 ? S : Lg;
+      if (leaf >= 0) {
+        const DevLeafSplits ls = d.ls[leaf];
+        if (leaf_buildable(ls)) {
+          ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
+          scan_direction(s_hist[sel], ft, d.gain, sl, fwd, s_pg[warp], s_ph[warp], s_pc[warp],
+                         &s_cand[warp]);
+        }
+      }
+      __syncthreads();
+      if (tid == 0 || tid == 32) {
+        const int sl_i = tid == 0 ? 0 : 1;
+        const int32_t leaf2 = sl_i == 0 ? S : Lg;
+        if (leaf2 >= 0) {
+          const DevLeafSplits ls = d.ls[leaf2];
+          const bool scannable = leaf_buildable(ls);
+          if (f == 0) d.scan_ok[sl_i] = scannable ? 1 : 0;
+          DevSplitInfo si = d_split_none();
+          if (scannable) {
+            ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
+            si = finalize_split(d.gain, sl, s_cand[2 * sl_i], s_cand[2 * sl_i + 1]);
+          }
+          d.scan_out[sl_i * d.F + f] = si;
+        }
+      }
+    } else {
+      long long* raw = d.raw + 2 * (size_t)ft.bin_off;
+      for (int i = tid; i < 2 * nb; i += blockDim.x) raw[i] = 0;
+      if (tid == 0) {
+        d.scan_out[f] = d_split_none();
+        d.scan_out[d.F + f] = d_split_none();
+        if (f == 0) {
+          d.scan_ok[0] = leaf_buildable(lss) ? 1 : 0;
+          d.scan_ok[1] = Lg >= 0 && leaf_buildable(d.ls[Lg]) ? 1 : 0;
+        }
+      }
+    }
+  }
+  // last-CTA argmax
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const uint32_t t = atomicAdd(&c->scan_counter, 1u);
+    s_last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (c->done) return;
+  pick_split(d);
+}
+
+// ------------------------------------------------------------------------------------
+// Stable partition of one leaf's rows, single pass with decoupled look-back.
+// Left rows keep ascending position order from the front of the leaf's range;
+// right rows are written from the back (a stable reversal), so no second pass
+// over the data is needed to learn the left total.
+// ------------------------------------------------------------------------------------
+
+__device__ __forceinline__ unsigned long long pack_status(uint32_t epoch, uint32_t flag,
+                                                          uint32_t v) {
+  return ((unsigned long long)(epoch & 0xffffffu) << 40) | ((unsigned long long)flag << 32) | v;
+}
+
+struct PartitionTile {
+  // returns false on look-back timeout
+  __device__ static bool run(const uint8_t* __restrict__ bins, int32_t stride,
+                             const DevFeature& ft, int32_t feature, uint32_t threshold,
+                             bool default_left, const uint32_t* __restrict__ src,
+                             bool identity, uint32_t* __restrict__ dst, int32_t begin,
+                             int32_t count, int32_t tile, uint32_t epoch,
+                             unsigned long long* status, int32_t* left_total) {
+    __shared__ int32_t s_warp[kPartThreads / 32];
+    __shared__ int32_t s_prefix;
+    __shared__ int32_t s_ok;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int32_t base = tile * kPartTile;
+    uint32_t rows[kPartItems];
+    uint32_t leftmask = 0, validmask = 0;
+#pragma unroll
+    for (int j = 0; j < kPartItems; ++j) {
+      const int32_t p = base + tid * kPartItems + j;
+      if (p < count) {
+        const uint32_t row = identity ? (uint32_t)(begin + p) : src[begin + p];
+        rows[j] = row;
+        const int32_t bin = bins[(size_t)row * stride + feature];
+        validmask |= 1u << j;
+        if (!d_go_right(ft, threshold, default_left, bin)) leftmask |= 1u << j;
+      }
+    }
+    const int32_t my_left = __popc(leftmask);
+    int32_t incl = my_left;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    int32_t warp_off = 0, tile_left = 0;
+    for (int w = 0; w < kPartThreads / 32; ++w) {
+      const int32_t v = s_warp[w];
+      if (w < warp) warp_off += v;
+      tile_left += v;
+    }
+    const int32_t excl = warp_off + incl - my_left;
+    if (tid == 0) {
+      int32_t prefix = 0;
+      int32_t ok = 1;
+      if (tile == 0) {
+        __threadfence();
+        atomicExch(&status[0], pack_status(epoch, 2u, (uint32_t)tile_left));
+      } else {
+        __threadfence();
+        atomicExch(&status[tile], pack_status(epoch, 1u, (uint32_t)tile_left));
+        int32_t j = tile - 1;
+        long long spins = 0;
+        while (j >= 0) {
+          const unsigned long long w = atomicAdd(&status[j], 0ull);
+          const uint32_t we = (uint32_t)(w >> 40);
+          const uint32_t fl = (uint32_t)(w >> 32) & 0xffu;
+          if (we != (epoch & 0xffffffu) || fl == 0u) {
+            if (++spins > kSpinLimit) {
+              ok = 0;
+              break;
+            }
+            __nanosleep(32);
+            continue;
+          }
+          prefix += (int32_t)(uint32_t)(w & 0xffffffffull);
+          if (fl == 2u) break;
+          --j;
+        }
+        __threadfence();
+        atomicExch(&status[tile], pack_status(epoch, 2u, (uint32_t)(prefix + tile_left)));
+      }
+      atomicAdd(left_total, tile_left);
+      s_prefix = prefix;
+      s_ok = ok;
+    }
+    __syncthreads();
+    const int32_t prefix_left = s_prefix;
+    const bool ok = s_ok != 0;
+    if (ok) {
+      const int32_t prefix_right = base - prefix_left;
+      int32_t lrank = excl;
+      const int32_t my_base = tid * kPartItems;
+#pragma unroll
+      for (int j = 0; j < kPartItems; ++j) {
+        if (!((validmask >> j) & 1u)) continue;
+        if ((leftmask >> j) & 1u) {
+          dst[begin + prefix_left + lrank] = rows[j];
+          ++lrank;
+        } else {
+          const int32_t rrank = (my_base + j) - lrank;  // rights before this item in tile
+          dst[begin + count - 1 - (prefix_right + rrank)] = rows[j];
+        }
+      }
+    }
+    __syncthreads();
+    return ok;
+  }
+};
+
+__global__ void __launch_bounds__(kPartThreads) k_partition(GrowDev d) {
+  __shared__ int32_t s_tile;
+  GrowCtrl* c = d.ctrl;
+  if (c->done || !c->pending) return;
+  const int32_t leaf = c->split_leaf;
+  const int32_t f = c->split_feature;
+  const DevFeature ft = d.feat[f];
+  const int32_t begin = d.leaf_begin[leaf];
+  const int32_t count = d.leaf_count[leaf];
+  const int32_t src = d.leaf_buf[leaf];
+  const uint32_t* sp = src == 1 ? d.idx1 : d.idx0;
+  uint32_t* dp = src == 1 ? d.idx0 : d.idx1;
+  const int32_t ntiles = (count + kPartTile - 1) / kPartTile;
+  const uint32_t epoch = c->epoch;
+  const uint32_t thr = c->split.threshold;
+  const bool dl = c->split.default_left != 0;
+  while (true) {
+    if (threadIdx.x == 0) s_tile = (int32_t)atomicAdd(&c->part_ticket, 1u);
+    __syncthreads();
+    const int32_t tile = s_tile;
+    __syncthreads();
+    if (tile >= ntiles) break;
+    const bool ok = PartitionTile::run(d.bins, d.stride, ft, f, thr, dl, sp, src == 2, dp, begin,
+                                       count, tile, epoch, d.part_status, &c->part_left_total);
+    if (!ok) {
+      if (threadIdx.x == 0) {
+        atomicOr(&c->error, kErrSpinTimeout);
+        c->done = 1;
+      }
+      break;
+    }
+  }
+}
+
+// ---------------------------- standalone per-op kernels ----------------------------
+
+__global__ void k_hist_standalone(const uint8_t* bins, int32_t stride, int64_t n,
+                                  const float2* gh, int32_t num_bin, double sg, double sh,
+                                  long long* raw) {
+  __shared__ unsigned long long acc[2 * kMaxBins];
+  for (int i = threadIdx.x; i < 2 * num_bin; i += blockDim.x) acc[i] = 0ull;
+  __syncthreads();
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < n;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    const float2 v = gh[r];
+    const uint32_t bin = bins[(size_t)r * stride];
+    atomicAdd(&acc[2 * bin], (unsigned long long)__double2ll_rn((double)v.x * sg));
+    atomicAdd(&acc[2 * bin + 1], (unsigned long long)__double2ll_rn((double)v.y * sh));
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 * num_bin; i += blockDim.x)
+    if (acc[i]) atomicAdd((unsigned long long*)&raw[i], acc[i]);
+}
+
+__global__ void __launch_bounds__(64) k_scan_standalone(const double* hist,
+                                                        const DevFeature* feats,
+                                                        DevGainConfig cfg, DevLeafSplits ls,
+                                                        DevSplitInfo* out) {
+  __shared__ double s_hist[2 * kMaxBins];
+  __shared__ double s_pg[2][kMaxBins];
+  __shared__ double s_ph[2][kMaxBins];
+  __shared__ int32_t s_pc[2][kMaxBins];
+  __shared__ ScanCand s_cand[2];
+  const DevFeature ft = feats[blockIdx.x];
+  for (int i = threadIdx.x; i < 2 * ft.num_bin; i += blockDim.x)
+    s_hist[i] = hist[ft.slot_off + i];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5;
+  ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
+  scan_direction(s_hist, ft, cfg, sl, warp == 1, s_pg[warp], s_ph[warp], s_pc[warp],
+                 &s_cand[warp]);
+  __syncthreads();
+  if (threadIdx.x == 0) out[blockIdx.x] = finalize_split(cfg, sl, s_cand[0], s_cand[1]);
+}
+
+__global__ void __launch_bounds__(kPartThreads) k_partition_standalone(
+    const uint8_t* bins, int32_t stride, int32_t feature, const DevFeature* feat,
+    uint32_t threshold, int32_t default_left, int32_t count, uint32_t* dst,
+    unsigned long long* status, int32_t* left_total, uint32_t* ticket) {
+  __shared__ int32_t s_tile;
+  const DevFeature ft = *feat;
+  const int32_t ntiles = (count + kPartTile - 1) / kPartTile;
+  while (true) {
+    if (threadIdx.x == 0) s_tile = (int32_t)atomicAdd(ticket, 1u);
+    __syncthreads();
+    const int32_t tile = s_tile;
+    __syncthreads();
+    if (tile >= ntiles) break;
+    if (!PartitionTile::run(bins, stride, ft, feature, threshold, default_left != 0, nullptr,
+                            true, dst, 0, count, tile, 1u, status, left_total))
+      break;
+  }
+}
+
+__global__ void k_gather_partition(GrowDev d, uint32_t* out) {
+  const int leaf = blockIdx.y;
+  if (leaf >= d.ctrl->num_leaves) return;
+  const int32_t begin = d.leaf_begin[leaf];
+  const int32_t count = d.leaf_count[leaf];
+  const int32_t buf = d.leaf_buf[leaf];
+  const uint32_t* src = buf == 1 ? d.idx1 : d.idx0;
+  for (int32_t p = blockIdx.x * blockDim.x + threadIdx.x; p < count; p += gridDim.x * blockDim.x)
+    out[begin + p] = buf == 2 ? (uint32_t)(begin + p) : src[begin + p];
+}
+
+__global__ void k_subtract(const double* a, const double* b, double* o, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    o[i] = a[i] - b[i];
+}
+
+}  // namespace
+
+int build_smem_bytes_per_bin(int gh_mode) { return gh_mode == GH_QPACK ? 8 : 16; }
+
+static int g_num_sms = 0;
+
+static int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+int LaunchProfiler::begin(cudaStream_t st, int c) {
+  if (n >= cap) return -1;
+  cls[n] = c;
+  cudaEventRecord(ev[n][0], st);
+  return n++;
+}
+
+void LaunchProfiler::end(cudaStream_t st, int slot) {
+  if (slot >= 0) cudaEventRecord(ev[slot][1], st);
+}
+
+#define PROF_BEGIN(c) const int _slot = prof ? prof->begin(st, (c)) : -1
+#define PROF_END() \
+  do {             \
+    if (prof) prof->end(st, _slot); \
+  } while (0)
+
+void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStream_t st,
+                 LaunchProfiler* prof) {
+  const int sms = num_sms();
+  {
+    PROF_BEGIN(KC_INIT);
+    k_tree_init<<<32, 256, 0, st>>>(d);
+    PROF_END();
+  }
+  const dim3 bgrid(build_blocks, d.num_groups);
+  const int part_blocks = sms * 4;
+  for (int s = 0; s < d.L - 1; ++s) {
+    {
+      PROF_BEGIN(KC_PREPARE);
+      k_prepare<<<1, 32, 0, st>>>(d, s);
+      PROF_END();
+    }
+    {
+      PROF_BEGIN(KC_BUILD);
+      if (d.gh_mode == GH_QPACK)
+        k_build<GH_QPACK><<<bgrid, kBuildThreads, build_smem, st>>>(d);
+      else if (d.gh_mode == GH_QLUT)
+        k_build<GH_QLUT><<<bgrid, kBuildThreads, build_smem, st>>>(d);
+      else
+        k_build<GH_FLOAT><<<bgrid, kBuildThreads, build_smem, st>>>(d);
+      PROF_END();
+    }
+    {
+      PROF_BEGIN(KC_FIXSCAN);
+      k_fixscan<<<d.F, kScanThreads, 0, st>>>(d);
+      PROF_END();
+    }
+    {
+      PROF_BEGIN(KC_PARTITION);
+      k_partition<<<part_blocks, kPartThreads, 0, st>>>(d);
+      PROF_END();
+    }
+  }
+  {
+    PROF_BEGIN(KC_PREPARE);
+    k_prepare<<<1, 32, 0, st>>>(d, d.L - 1);
+    PROF_END();
+  }
+}
+
+void set_build_smem_limit(size_t bytes) {
+  cudaFuncSetAttribute(k_build<GH_QPACK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)bytes);
+  cudaFuncSetAttribute(k_build<GH_QLUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)bytes);
+  cudaFuncSetAttribute(k_build<GH_FLOAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)bytes);
+}
+
+void launch_construct_histogram_f32(const uint8_t* bins_rm, int32_t stride, int64_t n,
+                                    const float2* gh, int32_t num_bin, double scale_g,
+                                    double scale_h, long long* raw, cudaStream_t st) {
+  int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 4);
+  if (blocks < 1) blocks = 1;
+  k_hist_standalone<<<blocks, 256, 0, st>>>(bins_rm, stride, n, gh, num_bin, scale_g, scale_h,
+                                            raw);
+}
+
+void launch_scan_features(const double* hist, const DevFeature* feats, int32_t n_feats,
+                          DevGainConfig cfg, DevLeafSplits ls, DevSplitInfo* out,
+                          cudaStream_t st) {
+  if (n_feats <= 0) return;
+  k_scan_standalone<<<n_feats, 64, 0, st>>>(hist, feats, cfg, ls, out);
+}
+
+void launch_partition_rows(const uint8_t* bins_rm, int32_t stride, int32_t feature,
+                           const DevFeature* feat, uint32_t threshold, int32_t default_left,
+                           int64_t count, uint32_t* dst, unsigned long long* status,
+                           int32_t* left_total, uint32_t* ticket, cudaStream_t st) {
+  const int32_t ntiles = (int32_t)((count + kPartTile - 1) / kPartTile);
+  int blocks = std::min(ntiles, num_sms() * 4);
+  if (blocks < 1) blocks = 1;
+  k_partition_standalone<<<blocks, kPartThreads, 0, st>>>(
+      bins_rm, stride, feature, feat, threshold, default_left, (int32_t)count, dst, status,
+      left_total, ticket);
+}
+
+void launch_gather_partition(const GrowDev& d, uint32_t* out, cudaStream_t st) {
+  k_gather_partition<<<dim3(64, d.L), 256, 0, st>>>(d, out);
+}
+
+void launch_subtract(const double* parent, const double* child, double* out, int64_t len,
+                     cudaStream_t st) {
+  int blocks = (int)std::min<int64_t>((len + 255) / 256, 1024);
+  if (blocks < 1) blocks = 1;
+  k_subtract<<<blocks, 256, 0, st>>>(parent, child, out, len);
+}
+
+}  // namespace lgbm_b200

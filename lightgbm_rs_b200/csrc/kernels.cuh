@@ -1,0 +1,145 @@
+// Kernel entry points and the device-state bundle shared by the host runtime.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace lgbm_b200 {
+
+// A contiguous run of features whose bins share one shared-memory accumulator
+// in the histogram build. f_begin is a multiple of 16 so every block reads the
+// row with aligned 16-byte vector loads.
+struct DevFeatureGroup {
+  int32_t f_begin;
+  int32_t f_end;
+  int32_t bin_base;  // first global bin of the group
+  int32_t num_bins;  // bins in the group
+};
+
+// Everything the per-split kernels touch, passed by value.
+struct GrowDev {
+  GrowCtrl* ctrl;
+  const int32_t* stopped;  // booster-level stop flag (may be null)
+  const DevFeature* feat;
+  const DevFeatureGroup* groups;
+  int32_t F;
+  int32_t num_groups;
+  const uint8_t* bins;  // row-major [N][stride]
+  int32_t stride;
+  int32_t L;
+  int64_t N;
+  int32_t max_depth;
+  int32_t slot_len;  // cells per histogram slot
+  DevGainConfig gain;
+  // per-leaf state [L]
+  int32_t* leaf_begin;
+  int32_t* leaf_count;
+  int32_t* leaf_buf;  // 0/1 = index buffer, 2 = identity (root)
+  int32_t* slot_of_leaf;
+  DevLeafSplits* ls;
+  DevSplitInfo* best;
+  int32_t* best_feature;
+  uint8_t* splittable;  // [L][F]
+  // tree arrays [L]
+  int32_t* t_left;
+  int32_t* t_right;
+  int32_t* t_split_feature;
+  uint32_t* t_threshold;
+  float* t_split_gain;
+  int8_t* t_decision;
+  double* t_leaf_value;
+  double* t_leaf_weight;
+  int32_t* t_leaf_count;
+  double* t_internal_value;
+  int32_t* t_internal_count;
+  int32_t* t_leaf_depth;
+  int32_t* t_leaf_parent;
+  // work buffers
+  uint32_t* idx0;
+  uint32_t* idx1;
+  unsigned long long* part_status;
+  int32_t max_tiles;
+  double* pool;            // [L][slot_len]
+  long long* raw;          // [2 * total_bins]
+  DevSplitInfo* scan_out;  // [2][F]
+  uint8_t* scan_ok;        // [2] leaf scanned flags
+  // gradients
+  int32_t gh_mode;
+  const void* gh;  // float2[N] (GH_FLOAT) or uint16 int8 pairs (quantized)
+  const DevGhParams* ghp;
+};
+
+// Optional per-kernel timing of a launch sequence: events recorded around each kernel.
+enum KernelClass { KC_PREPARE = 0, KC_BUILD = 1, KC_FIXSCAN = 2, KC_PARTITION = 3, KC_INIT = 4,
+                   KC_GRAD = 5, KC_FINISH = 6, KC_COUNT = 7 };
+struct LaunchProfiler {
+  cudaEvent_t (*ev)[2];
+  int* cls;
+  int cap;
+  int n;
+  int begin(cudaStream_t st, int c);
+  void end(cudaStream_t st, int slot);
+};
+
+// Host-side launch helpers (kernels.cu).
+void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStream_t st,
+                 LaunchProfiler* prof = nullptr);
+int build_smem_bytes_per_bin(int gh_mode);
+
+// Objective / score kernels (objective.cu).
+struct ObjDev {
+  int64_t N;
+  int32_t objective;  // 0 binary, 1 l2
+  int32_t gh_mode;
+  double sigmoid;
+  const float* label;
+  double* score;
+  void* gh;  // float2 (FLOAT) or uint16 (quantized)
+  DevGhParams* ghp;
+  int32_t num_quant_bins;
+  const int32_t* stopped;
+};
+void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof = nullptr);
+
+// Per-iteration tree finish: shrinkage + score update + tree record.
+struct FinishDev {
+  const GrowDev* gd_host;  // unused on device
+  int32_t* stopped;
+  int32_t* iter_counter;
+  int32_t max_iters;
+  double learning_rate;
+  double* score;
+  // tree record storage [max_iters][L] per array, + num_leaves per iter
+  int32_t* rec_num_leaves;
+  int32_t* rec_left;
+  int32_t* rec_right;
+  int32_t* rec_split_feature;
+  uint32_t* rec_threshold;
+  float* rec_split_gain;
+  int8_t* rec_decision;
+  double* rec_leaf_value;
+  double* rec_leaf_weight;
+  int32_t* rec_leaf_count;
+  double* rec_internal_value;
+  int32_t* rec_internal_count;
+};
+void launch_finish_iteration(const GrowDev& d, const FinishDev& f, cudaStream_t st,
+                             LaunchProfiler* prof = nullptr);
+
+// Standalone per-op launches (the Backend-trait entry points).
+void launch_construct_histogram_f32(const uint8_t* bins_rm, int32_t stride, int64_t n,
+                                    const float2* gh, int32_t num_bin, double scale_g,
+                                    double scale_h, long long* raw, cudaStream_t st);
+void launch_scan_features(const double* hist, const DevFeature* feats, int32_t n_feats,
+                          DevGainConfig cfg, DevLeafSplits ls, DevSplitInfo* out,
+                          cudaStream_t st);
+void launch_partition_rows(const uint8_t* bins_rm, int32_t stride, int32_t feature,
+                           const DevFeature* feat, uint32_t threshold, int32_t default_left,
+                           int64_t count, uint32_t* dst, unsigned long long* status,
+                           int32_t* left_total, uint32_t* ticket, cudaStream_t st);
+void launch_subtract(const double* parent, const double* child, double* out, int64_t len,
+                     cudaStream_t st);
+
+}  // namespace lgbm_b200

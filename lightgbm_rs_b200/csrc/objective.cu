@@ -1,0 +1,401 @@
+// Gradient/hessian, quantization, root sums, shrinkage and score update kernels.
+#include <cfloat>
+#include <cmath>
+
+#include "kernels.cuh"
+
+namespace lgbm_b200 {
+
+namespace {
+
+constexpr int kObjThreads = 256;
+
+__device__ __forceinline__ uint32_t f32_key(float x) {
+  x = x + 0.0f;  // -0.0 -> +0.0: the reference compares hessians with ==
+  const uint32_t b = __float_as_uint(x);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Binary::get_gradients (lgbm-objective/src/binary.rs:134-171), label weights 1.
+// Regression L2 (lgbm-objective/src/regression.rs:429-433).
+__device__ __forceinline__ float2 grad_hess(int objective, double sigmoid, double s, float l) {
+  if (objective == LGBM_B200_OBJECTIVE_BINARY) {
+    const bool is_pos = l > 0.0f;
+    const double lv = is_pos ? 1.0 : -1.0;
+    const double resp = -lv * sigmoid / (1.0 + exp(lv * sigmoid * s));
+    const double ar = fabs(resp);
+    return make_float2((float)(resp * 1.0), (float)(ar * (sigmoid - ar) * 1.0));
+  }
+  return make_float2((float)(s - (double)l), 1.0f);
+}
+
+// Rust `f64 as i8`: truncation toward zero, saturating, NaN -> 0.
+__device__ __forceinline__ int as_i8(double x) {
+  if (x != x) return 0;
+  if (x >= 127.0) return 127;
+  if (x <= -128.0) return -128;
+  return (int)x;
+}
+
+__global__ void k_gh_reset(DevGhParams* p, const int32_t* stopped) {
+  if (stopped && *stopped) return;
+  p->max_abs_g_bits = 0u;
+  p->max_abs_h_bits = 0u;
+  p->min_h_key = 0xffffffffu;
+  p->max_h_key = 0u;
+  p->root_g = 0;
+  p->root_h = 0;
+}
+
+__global__ void __launch_bounds__(kObjThreads) k_grad_pass1(ObjDev o) {
+  if (o.stopped && *o.stopped) return;
+  uint32_t mg = 0, mh = 0, kmin = 0xffffffffu, kmax = 0u;
+  float2* gh = reinterpret_cast<float2*>(o.gh);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < o.N;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float2 v = grad_hess(o.objective, o.sigmoid, o.score[i], o.label[i]);
+    gh[i] = v;
+    mg = max(mg, __float_as_uint(fabsf(v.x)));
+    mh = max(mh, __float_as_uint(fabsf(v.y)));
+    const uint32_t k = f32_key(v.y);
+    kmin = min(kmin, k);
+    kmax = max(kmax, k);
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    mg = max(mg, __shfl_xor_sync(0xffffffffu, mg, off));
+    mh = max(mh, __shfl_xor_sync(0xffffffffu, mh, off));
+    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, off));
+    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, off));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(&o.ghp->max_abs_g_bits, mg);
+    atomicMax(&o.ghp->max_abs_h_bits, mh);
+    atomicMin(&o.ghp->min_h_key, kmin);
+    atomicMax(&o.ghp->max_h_key, kmax);
+  }
+}
+
+// Quantized decode units for given grad/hess scales (see GhMode).
+__device__ void set_quant_units(DevGhParams* p, int mode, double gs, double hs) {
+  if (mode == GH_QPACK) {
+    p->unit_g = (double)(float)(1.0 * gs);
+    p->unit_h = (double)(float)(1.0 * hs);
+    p->v3h = (double)(float)(3.0 * hs);
+    return;
+  }
+  // QLUT: every dequantized level (f32)(q * scale) is an integer multiple of the
+  // f32 ulp of the level-1 value; accumulate those integers.
+  auto unit_of = [](double v1) -> double {
+    if (!(v1 > 0.0)) return 1.0;
+    int e;
+    frexp(v1, &e);
+    return ldexp(1.0, e - 24);
+  };
+  const double ug = unit_of((double)(float)gs);
+  const double uh = unit_of((double)(float)hs);
+  p->unit_g = ug;
+  p->unit_h = uh;
+  for (int q = -128; q < 128; ++q) {
+    p->lut_g[q + 128] = (long long)((double)(float)((double)q * gs) / ug);
+    p->lut_h[q + 128] = (long long)((double)(float)((double)q * hs) / uh);
+  }
+}
+
+// Per-iteration encoding parameters. Quantized: GradientDiscretizer::compute_scales
+// (lgbm-treelearner/src/gradient_discretizer.rs:145-165).
+__global__ void k_gh_scales(ObjDev o) {
+  if (o.stopped && *o.stopped) return;
+  DevGhParams* p = o.ghp;
+  const double max_g = (double)__uint_as_float(p->max_abs_g_bits);
+  const double max_h = (double)__uint_as_float(p->max_abs_h_bits);
+  p->mode = o.gh_mode;
+  p->num_quant_bins = o.num_quant_bins;
+  p->root_g = 0;
+  p->root_h = 0;
+  if (o.gh_mode == GH_FLOAT) {
+    int lg = 0;
+    while (lg < 62 && ((int64_t)1 << lg) < o.N) ++lg;
+    auto kscale = [&](double m) -> int {
+      if (!(m > 0.0) || !isfinite(m)) return 0;
+      int e;
+      frexp(m, &e);  // m < 2^e
+      int k = 62 - e - lg;
+      if (k > 1000) k = 1000;
+      if (k < -1000) k = -1000;
+      return k;
+    };
+    const int kg = kscale(max_g), kh = kscale(max_h);
+    p->scale_g = ldexp(1.0, kg);
+    p->unit_g = ldexp(1.0, -kg);
+    p->scale_h = ldexp(1.0, kh);
+    p->unit_h = ldexp(1.0, -kh);
+    p->is_const_hess = 0;
+    return;
+  }
+  const int bins = o.num_quant_bins;
+  const bool is_const = p->min_h_key == p->max_h_key;
+  const double half_bins = (double)(bins / 2);
+  const double gs = max_g / half_bins;
+  const double hs = is_const ? max_h : max_h / (double)bins;
+  p->is_const_hess = is_const ? 1 : 0;
+  p->grad_scale = gs;
+  p->hess_scale = hs;
+  p->inv_grad_scale = 1.0 / gs;
+  p->inv_hess_scale = 1.0 / hs;
+  set_quant_units(p, o.gh_mode, gs, hs);
+}
+
+// Scales handed in by the caller (learner entry point with int8 pairs).
+__global__ void k_gh_given_scales(ObjDev o) {
+  DevGhParams* p = o.ghp;
+  p->root_g = 0;
+  p->root_h = 0;
+  p->inv_grad_scale = 1.0 / p->grad_scale;
+  p->inv_hess_scale = 1.0 / p->hess_scale;
+  set_quant_units(p, p->mode, p->grad_scale, p->hess_scale);
+}
+
+__global__ void k_maxabs(ObjDev o) {
+  uint32_t mg = 0, mh = 0;
+  const float2* gh = reinterpret_cast<const float2*>(o.gh);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < o.N;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float2 v = gh[i];
+    mg = max(mg, __float_as_uint(fabsf(v.x)));
+    mh = max(mh, __float_as_uint(fabsf(v.y)));
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    mg = max(mg, __shfl_xor_sync(0xffffffffu, mg, off));
+    mh = max(mh, __shfl_xor_sync(0xffffffffu, mh, off));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(&o.ghp->max_abs_g_bits, mg);
+    atomicMax(&o.ghp->max_abs_h_bits, mh);
+  }
+}
+
+// Root sums of caller-provided int8 pairs.
+__global__ void __launch_bounds__(kObjThreads) k_root_sums_q(ObjDev o) {
+  const DevGhParams& p = *o.ghp;
+  const uint16_t* q = reinterpret_cast<const uint16_t*>(reinterpret_cast<const float2*>(o.gh) + o.N);
+  long long sa = 0, sb = 0;
+  const bool pack = p.mode == GH_QPACK;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < o.N;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint16_t v = q[i];
+    const int qg = (int)(int8_t)(v & 0xff);
+    const int qh = (int)(int8_t)(v >> 8);
+    if (pack) {
+      sa += qg;
+      sb += qh == 3 ? (1ll << 32) : (long long)qh;
+    } else {
+      sa += p.lut_g[qg + 128];
+      sb += p.lut_h[qh + 128];
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    sa += __shfl_xor_sync(0xffffffffu, sa, off);
+    sb += __shfl_xor_sync(0xffffffffu, sb, off);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd((unsigned long long*)&o.ghp->root_g, (unsigned long long)sa);
+    atomicAdd((unsigned long long*)&o.ghp->root_h, (unsigned long long)sb);
+  }
+}
+
+// GradientDiscretizer::quantize_pair, deterministic rounding
+// (gradient_discretizer.rs:167-191), plus the exact integer root sums.
+__global__ void __launch_bounds__(kObjThreads) k_quantize(ObjDev o) {
+  if (o.stopped && *o.stopped) return;
+  const DevGhParams& p = *o.ghp;
+  const float2* gh = reinterpret_cast<const float2*>(o.gh);
+  // int8 pairs live right after the f32 pairs
+  uint16_t* q = reinterpret_cast<uint16_t*>(reinterpret_cast<float2*>(o.gh) + o.N);
+  long long sa = 0, sb = 0;
+  const bool pack = p.mode == GH_QPACK;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < o.N;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float2 v = gh[i];
+    const double gv = (double)v.x * p.inv_grad_scale;
+    const int qg = as_i8(v.x >= 0.0f ? gv + 0.5 : gv - 0.5);
+    const int qh = p.is_const_hess ? 1 : as_i8((double)v.y * p.inv_hess_scale + 0.5);
+    q[i] = (uint16_t)((qg & 0xff) | ((qh & 0xff) << 8));
+    if (pack) {
+      sa += qg;
+      sb += qh == 3 ? (1ll << 32) : (long long)qh;
+    } else {
+      sa += p.lut_g[qg + 128];
+      sb += p.lut_h[qh + 128];
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    sa += __shfl_xor_sync(0xffffffffu, sa, off);
+    sb += __shfl_xor_sync(0xffffffffu, sb, off);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd((unsigned long long*)&o.ghp->root_g, (unsigned long long)sa);
+    atomicAdd((unsigned long long*)&o.ghp->root_h, (unsigned long long)sb);
+  }
+}
+
+__global__ void __launch_bounds__(kObjThreads) k_root_sums_float(ObjDev o) {
+  if (o.stopped && *o.stopped) return;
+  const DevGhParams& p = *o.ghp;
+  const float2* gh = reinterpret_cast<const float2*>(o.gh);
+  long long sa = 0, sb = 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < o.N;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float2 v = gh[i];
+    sa += __double2ll_rn((double)v.x * p.scale_g);
+    sb += __double2ll_rn((double)v.y * p.scale_h);
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    sa += __shfl_xor_sync(0xffffffffu, sa, off);
+    sb += __shfl_xor_sync(0xffffffffu, sb, off);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd((unsigned long long*)&o.ghp->root_g, (unsigned long long)sa);
+    atomicAdd((unsigned long long*)&o.ghp->root_h, (unsigned long long)sb);
+  }
+}
+
+__device__ __forceinline__ bool is_zero(double v) { return v >= -1e-35 && v <= 1e-35; }
+
+// Tree::shrinkage (lgbm-model/src/tree.rs:1074-1100) and the record of the tree.
+__global__ void k_finish_tree(GrowDev d, FinishDev f) {
+  if (*f.stopped) return;
+  const int nl = d.ctrl->num_leaves;
+  const int it = *f.iter_counter;
+  __shared__ int s_skip;
+  if (threadIdx.x == 0) {
+    s_skip = 0;
+    if (nl <= 1 && it > 0) {
+      // no split after the first iteration: training stops (gbdt.rs:1272-1283)
+      *f.stopped = 1;
+      s_skip = 1;
+    } else if (it >= f.max_iters) {
+      s_skip = 1;
+    }
+  }
+  __syncthreads();
+  if (s_skip) return;
+  const int L = d.L;
+  for (int i = threadIdx.x; i < L; i += blockDim.x) {
+    double lv = d.t_leaf_value[i];
+    if (nl > 1 && i < nl) {
+      lv = lv * f.learning_rate;
+      lv = is_zero(lv) ? 0.0 : lv;
+      d.t_leaf_value[i] = lv;
+    }
+    double iv = d.t_internal_value[i];
+    if (nl > 1 && i + 1 < nl) {
+      iv = iv * f.learning_rate;
+      iv = is_zero(iv) ? 0.0 : iv;
+      d.t_internal_value[i] = iv;
+    }
+    const size_t o = (size_t)it * L + i;
+    f.rec_left[o] = d.t_left[i];
+    f.rec_right[o] = d.t_right[i];
+    f.rec_split_feature[o] = d.t_split_feature[i];
+    f.rec_threshold[o] = d.t_threshold[i];
+    f.rec_split_gain[o] = d.t_split_gain[i];
+    f.rec_decision[o] = d.t_decision[i];
+    f.rec_leaf_value[o] = nl > 1 ? lv : 0.0;
+    f.rec_leaf_weight[o] = d.t_leaf_weight[i];
+    f.rec_leaf_count[o] = d.t_leaf_count[i];
+    f.rec_internal_value[o] = iv;
+    f.rec_internal_count[o] = d.t_internal_count[i];
+  }
+  if (threadIdx.x == 0) {
+    f.rec_num_leaves[it] = nl;
+    *f.iter_counter = it + 1;
+  }
+}
+
+// score[row] += leaf_value[leaf(row)] (learner.rs:4380-4395), walking the tree on the
+// row's bins in row order so the score array streams instead of scattering.
+__global__ void __launch_bounds__(256) k_score_update(GrowDev d, double* score,
+                                                      const int32_t* stopped,
+                                                      const int32_t* iter_counter,
+                                                      const int32_t* rec_num_leaves) {
+  if (*stopped) return;
+  const int it = *iter_counter - 1;
+  if (it < 0 || rec_num_leaves[it] <= 1) return;
+  __shared__ int32_t s_left[256], s_right[256], s_feat[256];
+  __shared__ uint32_t s_thr[256];
+  __shared__ int8_t s_dl[256];
+  __shared__ double s_val[256];
+  const int nl = d.ctrl->num_leaves;
+  for (int i = threadIdx.x; i < nl; i += blockDim.x) {
+    s_val[i] = d.t_leaf_value[i];
+    if (i + 1 < nl) {
+      s_left[i] = d.t_left[i];
+      s_right[i] = d.t_right[i];
+      s_feat[i] = d.t_split_feature[i];
+      s_thr[i] = d.t_threshold[i];
+      s_dl[i] = (d.t_decision[i] & 2) ? 1 : 0;
+    }
+  }
+  __syncthreads();
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < d.N;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    const uint8_t* rp = d.bins + (size_t)r * d.stride;
+    int node = 0;
+    while (node >= 0) {
+      const int f = s_feat[node];
+      const bool right = d_go_right(d.feat[f], s_thr[node], s_dl[node] != 0, rp[f]);
+      node = right ? s_right[node] : s_left[node];
+    }
+    score[r] += s_val[~node];
+  }
+}
+
+int num_sms_obj() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+}  // namespace
+
+void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof) {
+  const int grid = num_sms_obj() * 8;
+  const int slot = prof ? prof->begin(st, KC_GRAD) : -1;
+  k_gh_reset<<<1, 1, 0, st>>>(o.ghp, o.stopped);
+  k_grad_pass1<<<grid, kObjThreads, 0, st>>>(o);
+  k_gh_scales<<<1, 1, 0, st>>>(o);
+  if (o.gh_mode == GH_FLOAT)
+    k_root_sums_float<<<grid, kObjThreads, 0, st>>>(o);
+  else
+    k_quantize<<<grid, kObjThreads, 0, st>>>(o);
+  if (prof) prof->end(st, slot);
+}
+
+void launch_learner_gradients(const ObjDev& o, int32_t kind, cudaStream_t st) {
+  const int grid = num_sms_obj() * 8;
+  if (kind == LGBM_B200_GH_F32) {
+    k_gh_reset<<<1, 1, 0, st>>>(o.ghp, nullptr);
+    k_maxabs<<<grid, kObjThreads, 0, st>>>(o);
+    k_gh_scales<<<1, 1, 0, st>>>(o);
+    k_root_sums_float<<<grid, kObjThreads, 0, st>>>(o);
+  } else {
+    k_gh_given_scales<<<1, 1, 0, st>>>(o);
+    k_root_sums_q<<<grid, kObjThreads, 0, st>>>(o);
+  }
+}
+
+void launch_finish_iteration(const GrowDev& d, const FinishDev& f, cudaStream_t st,
+                             LaunchProfiler* prof) {
+  const int slot = prof ? prof->begin(st, KC_FINISH) : -1;
+  k_finish_tree<<<1, 256, 0, st>>>(d, f);
+  k_score_update<<<num_sms_obj() * 8, 256, 0, st>>>(d, f.score, f.stopped, f.iter_counter,
+                                                    f.rec_num_leaves);
+  if (prof) prof->end(st, slot);
+}
+
+}  // namespace lgbm_b200

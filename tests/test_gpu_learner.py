@@ -1,0 +1,155 @@
+"""Whole-tree and whole-training parity of the device learner against the oracle.
+
+Quantized gradients (the reference's use_quantized_grad path, gbdt.rs:931-959):
+trees, leaf values, split gains and leaf row sets must be bit-identical.
+f32 gradients: histograms accumulate in 64-bit fixed point, so the tree structure
+must match and leaf values agree to 1e-9 relative (near-tie splits are reported).
+"""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TREE_EXACT = ["split_feature", "threshold_bin", "decision_type", "left_child", "right_child",
+              "leaf_count", "internal_count"]
+TREE_BITS = ["leaf_value", "leaf_weight", "internal_value", "split_gain"]
+
+
+@pytest.fixture(scope="module")
+def data():
+    import lightgbm_rs_b200 as lgb
+    from lightgbm_rs_b200 import synthetic
+
+    X, y = synthetic.binary_c0(num_data=60_000, seed=1)
+    params = {"max_bin": 255, "min_data_in_leaf": 20}
+    ds = lgb.Dataset(X, y, params)
+    metas = [{"num_bin": m["num_bin"], "default_bin": m["default_bin"],
+              "most_freq_bin": m["most_freq_bin"], "missing_type": m["missing_type"]}
+             for m in ds.mappers]
+    return X, y, ds, metas
+
+
+def _assert_trees_bit_equal(got, want, tag):
+    assert got["num_leaves"] == want["num_leaves"], tag
+    for k in TREE_EXACT:
+        assert got[k].tolist() == want[k].tolist(), (tag, k)
+    for k in TREE_BITS:
+        a = np.asarray(got[k])
+        b = np.asarray(want[k]).astype(a.dtype)
+        assert a.tobytes() == b.tobytes(), (tag, k)
+
+
+def _leaf_sets(part, nl):
+    out = []
+    for l in range(nl):
+        b, c = part["leaf_begin"][l], part["leaf_count"][l]
+        out.append(np.sort(part["indices"][b:b + c]))
+    return out
+
+
+@pytest.mark.parametrize("num_quant_bins,num_leaves", [(4, 31), (4, 255), (16, 63)])
+def test_quantized_tree_bit_exact(data, num_quant_bins, num_leaves):
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, y, ds, metas = data
+    init = oracle.boost_from_score("binary", y)
+    rng = np.random.default_rng(num_leaves)
+    score = init + rng.normal(0, 0.3, len(y))  # a mid-training score
+    g, h = oracle.binary_gradients(score, y)
+    gq, hq, q, scales = oracle.quantize(g, h, num_quant_bins)
+    want, wpart, _ = oracle.grow_tree(ds.bins, metas, gq, hq, num_leaves=num_leaves,
+                                      min_data_in_leaf=20, min_sum_hessian_in_leaf=1e-3)
+    learner = lgb.Learner(ds, {"num_leaves": num_leaves, "min_data_in_leaf": 20})
+    sc = [scales[0], scales[1], scales[2], num_quant_bins]
+    got, gpart = learner.grow(quantized=q, scales=sc)
+    _assert_trees_bit_equal(got, want, f"q{num_quant_bins}/L{num_leaves}")
+    assert gpart["leaf_count"].tolist() == wpart["leaf_count"].tolist()
+    for a, b in zip(_leaf_sets(gpart, got["num_leaves"]), _leaf_sets(wpart, want["num_leaves"])):
+        assert np.array_equal(a, b)
+
+
+def test_quantized_tree_with_regularisation(data):
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, y, ds, metas = data
+    g, h = oracle.binary_gradients(np.zeros(len(y)), y)
+    gq, hq, q, scales = oracle.quantize(g, h, 4)
+    kw = dict(min_data_in_leaf=50, min_sum_hessian_in_leaf=1.0, lambda_l1=0.5, lambda_l2=2.0,
+              min_gain_to_split=0.1, max_delta_step=0.7, path_smooth=3.0)
+    want, _, _ = oracle.grow_tree(ds.bins, metas, gq, hq, num_leaves=63, max_depth=7, **kw)
+    learner = lgb.Learner(ds, {"num_leaves": 63, "max_depth": 7, **kw})
+    got, _ = learner.grow(quantized=q, scales=[scales[0], scales[1], scales[2], 4])
+    _assert_trees_bit_equal(got, want, "regularised")
+
+
+def test_float_tree_matches_within_tolerance(data):
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, y, ds, metas = data
+    g, h = oracle.binary_gradients(np.zeros(len(y)), y)
+    want, _, _ = oracle.grow_tree(ds.bins, metas, g, h, num_leaves=31, min_data_in_leaf=20)
+    learner = lgb.Learner(ds, {"num_leaves": 31, "min_data_in_leaf": 20})
+    got, _ = learner.grow(g=g, h=h)
+    assert got["num_leaves"] == want["num_leaves"]
+    for k in TREE_EXACT:
+        assert got[k].tolist() == want[k].tolist(), k
+    np.testing.assert_allclose(got["leaf_value"], want["leaf_value"], rtol=1e-9, atol=1e-12)
+
+
+def test_booster_quantized_bit_exact_vs_oracle(data):
+    """Gbdt loop on device (gradients, quantization, trees, shrinkage, score update)
+    vs the oracle loop, 10 iterations, use_quantized_grad with 4 bins."""
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, y, ds, metas = data
+    params = {"objective": "binary", "num_leaves": 31, "min_data_in_leaf": 20,
+              "learning_rate": 0.1, "use_quantized_grad": True, "num_grad_quant_bins": 4}
+    booster = lgb.train(params, ds, num_boost_round=10)
+    ref = oracle.train(ds.bins, metas, y, objective="binary", num_iterations=10,
+                       learning_rate=0.1, num_leaves=31, use_quantized_grad=True,
+                       num_grad_quant_bins=4, min_data_in_leaf=20)
+    trees = booster.trees()
+    assert len(trees) == len(ref["trees"])
+    for i, (a, b) in enumerate(zip(trees, ref["trees"])):
+        _assert_trees_bit_equal(a, b, f"tree {i}")
+    s = booster.train_scores()
+    assert s.view(np.uint64).tolist() == ref["scores"].view(np.uint64).tolist()
+
+
+def test_booster_float_predictions_close(data):
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, y, ds, metas = data
+    params = {"objective": "binary", "num_leaves": 31, "min_data_in_leaf": 20,
+              "learning_rate": 0.1}
+    booster = lgb.train(params, ds, num_boost_round=10)
+    ref = oracle.train(ds.bins, metas, y, objective="binary", num_iterations=10,
+                       learning_rate=0.1, num_leaves=31, min_data_in_leaf=20)
+    s = booster.train_scores()
+    np.testing.assert_allclose(s, ref["scores"], rtol=0, atol=1e-5)
+    p = booster.predict(X[:1000], raw_score=True)
+    np.testing.assert_allclose(p, s[:1000], rtol=0, atol=1e-9)
+
+
+def test_booster_l2_quantized_constant_hessian(data):
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, y, ds, metas = data
+    yr = (X[:, 2] * 2.0 + X[:, 9]).astype(np.float32)
+    ds2 = lgb.Dataset(bins=ds.bins, mappers=ds.mappers, label=yr,
+                      params={"min_data_in_leaf": 20})
+    params = {"objective": "regression", "num_leaves": 15, "min_data_in_leaf": 20,
+              "use_quantized_grad": True, "num_grad_quant_bins": 4}
+    booster = lgb.train(params, ds2, num_boost_round=5)
+    ref = oracle.train(ds.bins, metas, yr, objective="l2", num_iterations=5, learning_rate=0.1,
+                       num_leaves=15, use_quantized_grad=True, num_grad_quant_bins=4,
+                       min_data_in_leaf=20)
+    for i, (a, b) in enumerate(zip(booster.trees(), ref["trees"])):
+        _assert_trees_bit_equal(a, b, f"l2 tree {i}")
