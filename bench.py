@@ -57,12 +57,21 @@ def load_peaks():
 
 
 def make_data(rows, seed=0):
-    """Seeded synthetic C1 data, binned with the reference BinMapper (host)."""
+    """Seeded synthetic C1 data, binned with the reference BinMapper (host).
+
+    The binned result is cached under the system temp directory so repeated runs on
+    one machine skip generation (the cache is keyed by rows and seed)."""
     import concurrent.futures as cf
+    import pickle
+    import tempfile
 
     import lightgbm_rs_b200 as lgb
     from lightgbm_rs_b200 import synthetic
 
+    cache = os.path.join(tempfile.gettempdir(), f"lgbm_b200_c1_{rows}_{seed}.pkl")
+    if os.path.exists(cache):
+        with open(cache, "rb") as f:
+            return pickle.load(f)
     X, y = synthetic.binary_c0(num_data=rows, num_features=N_FEAT, seed=seed)
     mappers = [None] * N_FEAT
     bins = np.empty((N_FEAT, rows), dtype=np.uint8)
@@ -75,6 +84,12 @@ def make_data(rows, seed=0):
     with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4)) as ex:
         list(ex.map(one, range(N_FEAT)))
     del X
+    try:
+        with open(cache + ".tmp", "wb") as f:
+            pickle.dump((bins, mappers, y), f, protocol=4)
+        os.replace(cache + ".tmp", cache)
+    except OSError:
+        pass
     return bins, mappers, y
 
 

@@ -217,7 +217,51 @@ int lgbm_b200_learner::configure_groups(int mode) {
   const size_t budget = 112 * 1024;
   groups.clear();
   const int F = ds->num_features;
-  DevFeatureGroup cur{0, 0, 0, 0};
+  if (mode == GH_QPACK) {
+    // fixed power-of-two bin stride per group: cell = (feature << shift) + bin
+    auto ceil_log2 = [](int v) {
+      int s = 0;
+      while ((1 << s) < v) ++s;
+      return s;
+    };
+    DevFeatureGroup cur{0, 0, 0, 0, 0, 0};
+    for (int b0 = 0; b0 < F; b0 += 16) {
+      const int b1 = std::min(F, b0 + 16);
+      int sh = 0;
+      for (int f = b0; f < b1; ++f) sh = std::max(sh, ceil_log2(ds->feats[f].num_bin));
+      const int nsh = std::max(cur.shift, sh);
+      const bool fits = ((b1 - cur.f_begin) << nsh) <= kQ4MaxCells && (b1 - cur.f_begin) <= 128;
+      if (cur.f_end > cur.f_begin && !fits) {
+        groups.push_back(cur);
+        cur = DevFeatureGroup{b0, b0, ds->feats[b0].bin_off, 0, 0, 0};
+      }
+      if (cur.f_end == cur.f_begin) {
+        cur.f_begin = b0;
+        cur.bin_base = ds->feats[b0].bin_off;
+      }
+      cur.f_end = b1;
+      cur.shift = std::max(cur.shift, sh);
+      cur.num_bins = (cur.f_end - cur.f_begin) << cur.shift;
+    }
+    if (cur.f_end > cur.f_begin) groups.push_back(cur);
+    size_t cap = 0;
+    for (auto& g : groups) cap = std::max(cap, (size_t)g.num_bins);
+    // hot packed cells (4 B) + hot level-3 counts (2 B) + cold g and q sums (8 B)
+    build_smem = (cap + (cap + 1) / 2 + 2 * cap) * 4;
+    gh_mode = mode;
+    CUDA_TRY(d_groups.alloc(groups.size()));
+    CUDA_TRY(cudaMemcpy(d_groups.p, groups.data(), groups.size() * sizeof(DevFeatureGroup),
+                        cudaMemcpyHostToDevice));
+    set_build_smem_limit(build_smem);
+    CUDA_TRY(cudaGetLastError());
+    const int sms = sm_count(device);
+    build_blocks = sms * 2;
+    // per-CTA row ranges stay below 65536 rows (16-bit level-3 counters)
+    const int64_t need = (ds->num_data + 65535 - 1) / 65535;
+    if (build_blocks < need) build_blocks = (int)need;
+    return LGBM_B200_OK;
+  }
+  DevFeatureGroup cur{0, 0, 0, 0, 0, 0};
   for (int b0 = 0; b0 < F; b0 += 16) {
     const int b1 = std::min(F, b0 + 16);
     int nb = 0;
@@ -225,7 +269,7 @@ int lgbm_b200_learner::configure_groups(int mode) {
     const bool fits = (size_t)(cur.num_bins + nb) * bpb <= budget && (b1 - cur.f_begin) <= 128;
     if (cur.f_end > cur.f_begin && !fits) {
       groups.push_back(cur);
-      cur = DevFeatureGroup{b0, b0, ds->feats[b0].bin_off, 0};
+      cur = DevFeatureGroup{b0, b0, ds->feats[b0].bin_off, 0, 0, 0};
     }
     if (cur.f_end == cur.f_begin) {
       cur.f_begin = b0;

@@ -209,6 +209,130 @@ __global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d) {
 }
 
 // ------------------------------------------------------------------------------------
+// Histogram build for quantized gradients with num_grad_quant_bins <= 4 (levels
+// qg in [-2,2], qh in [0,4]). One native 32-bit shared atomic per (row, feature)
+// adds the signed packed word qg + (qh << 16); rows with qh == 3 (the one level
+// that is not a multiple of level 1 after dequantization) also bump a 16-bit
+// counter. The packed words are folded into 32-bit cold sums every kQ4Chunk rows,
+// before a field can overflow. Shared-memory cell = (feature << shift) + bin.
+// ------------------------------------------------------------------------------------
+
+constexpr int kQ4Threads = 512;
+constexpr int kQ4Chunk = 8191;  // |sum qg| <= 2*8191 and sum qh <= 4*8191 fit 16-bit fields
+
+__global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
+  extern __shared__ uint32_t sm[];
+  __shared__ int32_t s_nb[128];
+  __shared__ int32_t s_boff[128];
+  __shared__ uint32_t s_mask[4];
+  GrowCtrl* c = d.ctrl;
+  if (c->done || !c->do_find) return;
+  const int32_t leaf = c->smaller_leaf;
+  const DevLeafSplits ls = d.ls[leaf];
+  if (!leaf_buildable(ls)) return;
+  const int32_t begin = d.leaf_begin[leaf];
+  const int32_t count = d.leaf_count[leaf];
+  const int32_t buf = d.leaf_buf[leaf];
+  const DevFeatureGroup grp = d.groups[blockIdx.y];
+  const int nf = grp.f_end - grp.f_begin;
+  const int shift = grp.shift;
+  const int cap = grp.num_bins;
+  int nb_active = (count + kMinRowsPerBlock - 1) / kMinRowsPerBlock;
+  if (nb_active > (int)gridDim.x) nb_active = gridDim.x;
+  if (nb_active < 1) nb_active = 1;
+  if ((int)blockIdx.x >= nb_active) return;
+  const int32_t per = (count + nb_active - 1) / nb_active;  // <= 65535 (host grid sizing)
+  const int32_t r0 = per * (int32_t)blockIdx.x;
+  const int32_t r1 = min(count, r0 + per);
+  if (r0 >= r1) return;
+
+  uint32_t* hot = sm;                                            // [cap]
+  const int c3n = (cap + 1) >> 1;
+  uint32_t* c3w = sm + cap;                                      // [c3n] 16-bit pairs
+  int32_t* cold_g = reinterpret_cast<int32_t*>(c3w + c3n);       // [cap]
+  int32_t* cold_q = cold_g + cap;                                // [cap]
+  const int nwords = cap + c3n + 2 * cap;
+  for (int i = threadIdx.x; i < nwords; i += blockDim.x) sm[i] = 0u;
+  const bool sub = c->use_subtract != 0;
+  const uint8_t* ps = d.splittable + (size_t)c->left_leaf * d.F + grp.f_begin;
+  for (int fl = threadIdx.x; fl < nf; fl += blockDim.x) {
+    const DevFeature ft = d.feat[grp.f_begin + fl];
+    s_nb[fl] = ft.num_bin;
+    s_boff[fl] = ft.bin_off;
+  }
+  if (threadIdx.x < 4) {
+    uint32_t m = 0;
+    for (int b = 0; b < 32; ++b) {
+      const int fl = threadIdx.x * 32 + b;
+      if (fl < nf && (!sub || ps[fl])) m |= 1u << b;
+    }
+    s_mask[threadIdx.x] = m;
+  }
+  __syncthreads();
+  const uint32_t m0 = s_mask[0], m1 = s_mask[1], m2 = s_mask[2], m3 = s_mask[3];
+  const uint32_t* idx = buf == 1 ? d.idx1 : d.idx0;
+  const uint16_t* gq = reinterpret_cast<const uint16_t*>(d.gh);
+  const bool identity = buf == 2;
+  const int nchunks = (nf + 15) >> 4;
+  for (int32_t cs = r0; cs < r1; cs += kQ4Chunk) {
+    const int32_t ce = min(r1, cs + kQ4Chunk);
+    for (int32_t k = cs + (int32_t)threadIdx.x; k < ce; k += kQ4Threads) {
+      const uint32_t row = identity ? (uint32_t)(begin + k) : idx[begin + k];
+      const uint16_t q = gq[row];
+      const int qg = (int)(int8_t)(q & 0xff);
+      const int qh = (int)(int8_t)(q >> 8);
+      const int32_t pv = qg + (qh << 16);
+      const bool is3 = qh == 3;
+      const uint4* rp = reinterpret_cast<const uint4*>(d.bins + (size_t)row * d.stride +
+                                                       grp.f_begin);
+      for (int ch = 0; ch < nchunks; ++ch) {
+        const uint4 w = rp[ch];
+        const int wi = ch >> 1;  // 16-feature chunk ch lives in 32-bit mask word ch / 2
+        const uint32_t mw = wi < 2 ? (wi == 0 ? m0 : m1) : (wi == 2 ? m2 : m3);
+        const uint32_t m16 = (ch & 1) ? (mw >> 16) : (mw & 0xffffu);
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (!((m16 >> j) & 1u)) continue;
+          const uint32_t bin = (words[j >> 2] >> (8 * (j & 3))) & 0xffu;
+          const uint32_t cell = ((uint32_t)(16 * ch + j) << shift) + bin;
+          atomicAdd(reinterpret_cast<int*>(hot) + cell, pv);
+          if (is3) atomicAdd(c3w + (cell >> 1), 1u << ((cell & 1u) << 4));
+        }
+      }
+    }
+    if (ce < r1) {
+      __syncthreads();
+      for (int s = threadIdx.x; s < cap; s += kQ4Threads) {
+        const int32_t v = (int32_t)hot[s];
+        const int32_t lo = (int32_t)(int16_t)(v & 0xffff);
+        cold_g[s] += lo;
+        cold_q[s] += (v - lo) >> 16;
+        hot[s] = 0u;
+      }
+      __syncthreads();
+    }
+  }
+  __syncthreads();
+  long long* raw = d.raw;
+  for (int s = threadIdx.x; s < cap; s += kQ4Threads) {
+    const int fl = s >> shift;
+    const int bin = s & ((1 << shift) - 1);
+    if (fl >= nf || bin >= s_nb[fl]) continue;
+    const int32_t v = (int32_t)hot[s];
+    const int32_t lo = (int32_t)(int16_t)(v & 0xffff);
+    const long long g = (long long)cold_g[s] + lo;
+    const long long qsum = (long long)cold_q[s] + ((v - lo) >> 16);
+    const long long c3 = (c3w[s >> 1] >> ((s & 1) << 4)) & 0xffffu;
+    const long long h = (qsum - 3 * c3) | (c3 << 32);
+    const size_t gb = (size_t)(s_boff[fl] + bin);
+    if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb]), (unsigned long long)g);
+    if (h)
+      atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb + 1]), (unsigned long long)h);
+  }
+}
+
+// ------------------------------------------------------------------------------------
 // Threshold scan of one direction of one feature by one warp
 // (find_best_split_cpu_native, lgbm-compute/src/kernels/split.rs:8970-9329).
 // The dependent f64 chains (running gradient / hessian sums, seeded with kEpsilon)
@@ -296,17 +420,24 @@ __device__ void scan_direction(const double* hist, const DevFeature& f, const De
     if (!forward) return (t >= (1 - offset)) && !skip;
     return !skip;
   };
-  // Sequential f64 chains: lane 0 gradient, lane 1 hessian.
+  // Addend of every step across the warp (0 when the step is inactive; the running
+  // sums are never -0.0, so `+ 0.0` leaves them unchanged, split.rs:8950-8960), then
+  // the dependent f64 chains, sequential in the reference's order: lane 0 gradient,
+  // lane 1 hessian, in SIMT lockstep.
+  for (int k = lane; k < count; k += 32) {
+    int t;
+    const bool act = active_at(k, &t) && t >= 0;
+    pg[k] = act ? hist[2 * t] : 0.0;
+    ph[k] = act ? hist[2 * t + 1] : 0.0;
+  }
+  __syncwarp();
   if (lane < 2 && count > 0) {
+    double* p = lane == 0 ? pg : ph;
     double acc = lane == 0 ? g_init : h_init;
+#pragma unroll 8
     for (int k = 0; k < count; ++k) {
-      int t;
-      const bool act = active_at(k, &t);
-      if (act && t >= 0) acc += hist[2 * t + lane];
-      if (lane == 0)
-        pg[k] = acc;
-      else
-        ph[k] = acc;
+      acc += p[k];
+      p[k] = acc;
     }
   }
   // Integer count prefix across the warp.
@@ -512,29 +643,43 @@ __global__ void k_tree_init(GrowDev d) {
   }
 }
 
+// One thread; all per-leaf loads are issued up front so their latencies overlap
+// (this kernel sits on the critical path of every split).
 __global__ void k_prepare(GrowDev d, int s) {
-  GrowCtrl* c = d.ctrl;
   if (threadIdx.x != 0) return;
-  if (c->pending) {
+  GrowCtrl* cp = d.ctrl;
+  GrowCtrl c = *cp;
+  int32_t left = c.left_leaf, right = c.right_leaf;
+  int32_t cnt_left = 0, cnt_right = 0, depth_left = 0, slot_left = -1;
+  bool known = false;
+  DevLeafSplits lsL{}, lsR{};
+  if (c.pending) {
     // ---- apply the split chosen at step s-1 (learner.rs:3895-4092) ----
-    const int32_t leaf = c->split_leaf;
-    const int32_t nr = c->num_leaves;
-    const int32_t f = c->split_feature;
-    const DevSplitInfo b = c->split;
-    const int32_t lc = c->part_left_total;
-    const int32_t rc = d.leaf_count[leaf] - lc;
+    const int32_t leaf = c.split_leaf;
+    const int32_t nr = c.num_leaves;
+    const int32_t f = c.split_feature;
+    const DevSplitInfo b = c.split;
+    const int32_t cnt = d.leaf_count[leaf];
+    const int32_t beg = d.leaf_begin[leaf];
     const int32_t src = d.leaf_buf[leaf];
+    const int32_t parent = d.t_leaf_parent[leaf];
+    const double old_value = d.t_leaf_value[leaf];
+    const int32_t depth = d.t_leaf_depth[leaf];
+    const int32_t mt = d.feat[f].missing_type;
+    slot_left = d.slot_of_leaf[leaf];
+    const int32_t parent_right = parent >= 0 ? d.t_right[parent] : 0;
+    const int32_t lc = c.part_left_total;
+    const int32_t rc = cnt - lc;
     const int32_t dst = src == 1 ? 0 : 1;
-    d.leaf_begin[nr] = d.leaf_begin[leaf] + lc;
+    d.leaf_begin[nr] = beg + lc;
     d.leaf_count[leaf] = lc;
     d.leaf_count[nr] = rc;
     d.leaf_buf[leaf] = dst;
     d.leaf_buf[nr] = dst;
     // Tree::split (lgbm-model/src/tree.rs:614-690)
     const int32_t node = nr - 1;
-    const int32_t parent = d.t_leaf_parent[leaf];
     if (parent >= 0) {
-      if (d.t_right[parent] == ~leaf)
+      if (parent_right == ~leaf)
         d.t_right[parent] = node;
       else
         d.t_left[parent] = node;
@@ -542,13 +687,13 @@ __global__ void k_prepare(GrowDev d, int s) {
     d.t_split_feature[node] = f;
     d.t_split_gain[node] = (float)(b.gain + d.gain.min_gain_to_split);
     d.t_threshold[node] = b.threshold;
-    d.t_internal_value[node] = d.t_leaf_value[leaf];
+    d.t_internal_value[node] = old_value;
     d.t_internal_count[node] = lc + rc;
     d.t_left[node] = ~leaf;
     d.t_right[node] = ~nr;
     int8_t dt = 0;
     if (b.default_left) dt |= 2;
-    dt |= (int8_t)((d.feat[f].missing_type & 3) << 2);
+    dt |= (int8_t)((mt & 3) << 2);
     d.t_decision[node] = dt;
     d.t_leaf_value[leaf] = b.left_output;
     d.t_leaf_weight[leaf] = b.left_sum_hessian;
@@ -556,109 +701,133 @@ __global__ void k_prepare(GrowDev d, int s) {
     d.t_leaf_value[nr] = b.right_output;
     d.t_leaf_weight[nr] = b.right_sum_hessian;
     d.t_leaf_count[nr] = rc;
-    d.t_leaf_depth[nr] = d.t_leaf_depth[leaf] + 1;
-    d.t_leaf_depth[leaf] += 1;
+    d.t_leaf_depth[nr] = depth + 1;
+    d.t_leaf_depth[leaf] = depth + 1;
     d.t_leaf_parent[leaf] = node;
     d.t_leaf_parent[nr] = node;
     // child LeafSplits seeded from the SplitInfo (learner.rs:4061-4089)
-    DevLeafSplits L, R;
-    L.num_data = lc;
-    L._pad = 0;
-    L.sum_g = b.left_sum_gradient;
-    L.sum_h = b.left_sum_hessian;
-    L.weight = b.left_output;
-    R.num_data = rc;
-    R._pad = 0;
-    R.sum_g = b.right_sum_gradient;
-    R.sum_h = b.right_sum_hessian;
-    R.weight = b.right_output;
-    d.ls[leaf] = L;
-    d.ls[nr] = R;
+    lsL.num_data = lc;
+    lsL.sum_g = b.left_sum_gradient;
+    lsL.sum_h = b.left_sum_hessian;
+    lsL.weight = b.left_output;
+    lsR.num_data = rc;
+    lsR.sum_g = b.right_sum_gradient;
+    lsR.sum_h = b.right_sum_hessian;
+    lsR.weight = b.right_output;
+    d.ls[leaf] = lsL;
+    d.ls[nr] = lsR;
     d.best[leaf] = d_split_none();
     d.best_feature[leaf] = -1;
     d.best[nr] = d_split_none();
     d.best_feature[nr] = -1;
-    c->left_leaf = leaf;
-    c->right_leaf = nr;
-    c->num_leaves = nr + 1;
-    c->num_splits += 1;
-    c->pending = 0;
+    left = leaf;
+    right = nr;
+    cnt_left = lc;
+    cnt_right = rc;
+    depth_left = depth + 1;
+    known = true;
+    c.left_leaf = leaf;
+    c.right_leaf = nr;
+    c.num_leaves = nr + 1;
+    c.num_splits += 1;
+    c.pending = 0;
   }
-  if (c->done || s >= d.L - 1) {
-    c->do_find = 0;
+  if (c.done || s >= d.L - 1) {
+    c.do_find = 0;
+    *cp = c;
     return;
   }
-  c->epoch += 1;
-  c->part_ticket = 0;
-  c->part_left_total = 0;
-  c->scan_counter = 0;
+  if (!known) {
+    cnt_left = d.leaf_count[left];
+    cnt_right = right >= 0 ? d.leaf_count[right] : 0;
+    depth_left = d.t_leaf_depth[left];
+    slot_left = d.slot_of_leaf[left];
+    lsL = d.ls[left];
+    if (right >= 0) lsR = d.ls[right];
+  }
+  c.epoch += 1;
+  c.part_ticket = 0;
+  c.part_left_total = 0;
+  c.scan_counter = 0;
   // ---- BeforeFindBestSplit (learner.rs:1808-1839) ----
-  const int32_t left = c->left_leaf, right = c->right_leaf;
-  const int32_t num_left = d.leaf_count[left];
   const int32_t min2 = d.gain.min_data_in_leaf * 2;
   int32_t did = 1;
-  if (d.max_depth > 0 && d.t_leaf_depth[left] >= d.max_depth) {
+  if (d.max_depth > 0 && depth_left >= d.max_depth) {
     d.best[left].gain = kNegInf;
     if (right >= 0) d.best[right].gain = kNegInf;
     did = 0;
   } else if (right >= 0) {
-    if (d.leaf_count[right] < min2 && num_left < min2) {
+    if (cnt_right < min2 && cnt_left < min2) {
       d.best[left].gain = kNegInf;
       d.best[right].gain = kNegInf;
       did = 0;
     }
-  } else if (num_left < min2) {
+  } else if (cnt_left < min2) {
     d.best[left].gain = kNegInf;
     did = 0;
   }
-  c->do_find = did;
-  if (!did) return;
+  c.do_find = did;
+  if (!did) {
+    *cp = c;
+    return;
+  }
   // ---- smaller child + pool slots (learner.rs:1882-1916) ----
-  int32_t smaller, larger;
+  int32_t smaller, larger, cnt_smaller;
+  DevLeafSplits ls_smaller;
   if (right < 0) {
     smaller = left;
     larger = -1;
-  } else if (d.leaf_count[left] < d.leaf_count[right]) {
+    cnt_smaller = cnt_left;
+    ls_smaller = lsL;
+  } else if (cnt_left < cnt_right) {
     smaller = left;
     larger = right;
+    cnt_smaller = cnt_left;
+    ls_smaller = lsL;
   } else {
     smaller = right;
     larger = left;
+    cnt_smaller = cnt_right;
+    ls_smaller = lsR;
   }
   int32_t ss, lsl = -1, use_sub = 0;
   if (right < 0) {
-    if (d.slot_of_leaf[left] < 0) d.slot_of_leaf[left] = c->next_slot++;
-    ss = d.slot_of_leaf[left];
+    if (slot_left < 0) {
+      slot_left = c.next_slot++;
+      d.slot_of_leaf[left] = slot_left;
+    }
+    ss = slot_left;
   } else {
-    const int32_t parent_slot = d.slot_of_leaf[left];
+    const int32_t parent_slot = slot_left;
     use_sub = parent_slot >= 0 ? 1 : 0;
+    ss = c.next_slot++;
     if (smaller == left) {
       d.slot_of_leaf[right] = parent_slot;
-      d.slot_of_leaf[left] = c->next_slot++;
-      ss = d.slot_of_leaf[left];
+      d.slot_of_leaf[left] = ss;
     } else {
-      d.slot_of_leaf[right] = c->next_slot++;
-      ss = d.slot_of_leaf[right];
+      d.slot_of_leaf[right] = ss;
     }
     lsl = parent_slot;
     if (!use_sub) {
       // Cannot happen with a one-slot-per-leaf pool: a leaf is split only after its
       // histogram was built or derived.
-      c->error |= kErrNoParentHistogram;
-      c->done = 1;
-      c->do_find = 0;
+      c.error |= kErrNoParentHistogram;
+      c.done = 1;
+      c.do_find = 0;
+      *cp = c;
       return;
     }
   }
-  if (leaf_buildable(d.ls[smaller])) {
-    c->num_builds += 1;
-    c->rows_built += d.leaf_count[smaller];
+  if (leaf_buildable(ls_smaller)) {
+    c.num_builds += 1;
+    c.rows_built += cnt_smaller;
   }
-  c->smaller_leaf = smaller;
-  c->larger_leaf = larger;
-  c->smaller_slot = ss;
-  c->larger_slot = lsl;
-  c->use_subtract = use_sub;
+  c.smaller_leaf = smaller;
+  c.larger_leaf = larger;
+  c.smaller_slot = ss;
+  c.larger_slot = lsl;
+  c.use_subtract = use_sub;
+  *cp = c;
 }
 
 // ------------------------------------------------------------------------------------
@@ -667,10 +836,55 @@ __global__ void k_prepare(GrowDev d, int s) {
 // argmax, learner.rs:3314-3340, then arg_max over leaves, learner.rs:4537-4551).
 // ------------------------------------------------------------------------------------
 
+// Lexicographic order behind the reference's sequential first-max scans: gain
+// descending, then feature ascending with -1 last (split_gt, split_info.rs:28-36),
+// then position ascending (the scan keeps the first of equal candidates).
+__device__ __forceinline__ bool cand_better(double ga, int32_t fa, int32_t ia, double gb,
+                                            int32_t fb, int32_t ib) {
+  if (ga != gb) return ga > gb;
+  const int32_t x = fa == -1 ? 0x7fffffff : fa;
+  const int32_t y = fb == -1 ? 0x7fffffff : fb;
+  if (x != y) return x < y;
+  return ia < ib;
+}
+
+// Block-wide argmax of (g, f, i) under cand_better; result valid in every thread.
+__device__ void block_argmax(double& g, int32_t& f, int32_t& i) {
+  __shared__ double s_g[32];
+  __shared__ int32_t s_f[32], s_i[32];
+  for (int o = 16; o > 0; o >>= 1) {
+    const double og = __shfl_xor_sync(0xffffffffu, g, o);
+    const int32_t of = __shfl_xor_sync(0xffffffffu, f, o);
+    const int32_t oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (cand_better(og, of, oi, g, f, i)) {
+      g = og;
+      f = of;
+      i = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (lane == 0) {
+    s_g[warp] = g;
+    s_f[warp] = f;
+    s_i[warp] = i;
+  }
+  __syncthreads();
+  g = s_g[0];
+  f = s_f[0];
+  i = s_i[0];
+  for (int w = 1; w < nw; ++w)
+    if (cand_better(s_g[w], s_f[w], s_i[w], g, f, i)) {
+      g = s_g[w];
+      f = s_f[w];
+      i = s_i[w];
+    }
+  __syncthreads();
+}
+
 __device__ void pick_split(const GrowDev& d) {
   GrowCtrl* c = d.ctrl;
-  __shared__ double s_gain[kScanThreads];
-  __shared__ int32_t s_key[kScanThreads];
   const int tid = threadIdx.x;
   if (c->do_find) {
     for (int sel = 0; sel < 2; ++sel) {
@@ -683,45 +897,49 @@ __device__ void pick_split(const GrowDev& d) {
         }
         continue;
       }
+      // cross-feature argmax of this leaf (learner.rs:3314-3321)
       double bg = kNegInf;
       int32_t bf = -1;
       for (int f = tid; f < d.F; f += blockDim.x) {
         const double g = __ldcg(&d.scan_out[sel * d.F + f].gain);
         d.splittable[(size_t)leaf * d.F + f] = g > kNegInf ? 1 : 0;
-        if (g > kNegInf && d_split_gt(g, f, bg, bf)) {
+        if (g > kNegInf && cand_better(g, f, f, bg, bf, bf)) {
           bg = g;
           bf = f;
         }
       }
-      s_gain[tid] = bg;
-      s_key[tid] = bf;
-      __syncthreads();
+      int32_t bi = bf;
+      block_argmax(bg, bf, bi);
       if (tid == 0) {
-        for (int i = 1; i < (int)blockDim.x; ++i)
-          if (s_key[i] >= 0 && d_split_gt(s_gain[i], s_key[i], bg, bf)) {
-            bg = s_gain[i];
-            bf = s_key[i];
-          }
         d.best[leaf] = bf >= 0 ? d.scan_out[sel * d.F + bf] : d_split_none();
         d.best_feature[leaf] = bf;
       }
       __syncthreads();
     }
   }
+  __threadfence_block();
   __syncthreads();
+  // arg_max over leaves (learner.rs:4537-4551)
+  double bg = kNegInf;
+  int32_t bf = -1, bl = 0x7fffffff;
+  for (int i = tid; i < d.L; i += blockDim.x) {
+    const double g = __ldcg(&d.best[i].gain);
+    const int32_t f = __ldcg(&d.best_feature[i]);
+    if (bl == 0x7fffffff || cand_better(g, f, i, bg, bf, bl)) {
+      bg = g;
+      bf = f;
+      bl = i;
+    }
+  }
+  block_argmax(bg, bf, bl);
   if (tid == 0) {
-    int32_t bl = 0;
-    for (int i = 1; i < d.L; ++i)
-      if (d_split_gt(d.best[i].gain, d.best_feature[i], d.best[bl].gain, d.best_feature[bl]))
-        bl = i;
-    const DevSplitInfo b = d.best[bl];
-    if (b.gain <= 0.0) {
+    if (bg <= 0.0) {  // learner.rs:1503-1505
       c->done = 1;
     } else {
       c->pending = 1;
       c->split_leaf = bl;
-      c->split_feature = d.best_feature[bl];
-      c->split = b;
+      c->split_feature = bf;
+      c->split = d.best[bl];
     }
   }
 }
@@ -765,8 +983,11 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
       if (buildable && mfb > 0 && mfb < nb && (tid == 0 || tid == 32)) {
         const int w = tid == 0 ? 0 : 1;
         double acc = w == 0 ? lss.sum_g : lss.sum_h;
-        for (int i = 0; i < nb; ++i)
-          if (i != mfb) acc -= s_hist[0][2 * i + w];
+        const double* hv = &s_hist[0][w];
+#pragma unroll 8
+        for (int i = 0; i < mfb; ++i) acc -= hv[2 * i];
+#pragma unroll 8
+        for (int i = mfb + 1; i < nb; ++i) acc -= hv[2 * i];
         s_hist[0][2 * mfb + w] = acc;
       }
       __syncthreads();
@@ -1126,7 +1347,7 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
     {
       PROF_BEGIN(KC_BUILD);
       if (d.gh_mode == GH_QPACK)
-        k_build<GH_QPACK><<<bgrid, kBuildThreads, build_smem, st>>>(d);
+        k_build_q4<<<bgrid, kQ4Threads, build_smem, st>>>(d);
       else if (d.gh_mode == GH_QLUT)
         k_build<GH_QLUT><<<bgrid, kBuildThreads, build_smem, st>>>(d);
       else
@@ -1152,8 +1373,7 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
 }
 
 void set_build_smem_limit(size_t bytes) {
-  cudaFuncSetAttribute(k_build<GH_QPACK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       (int)bytes);
+  cudaFuncSetAttribute(k_build_q4, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
   cudaFuncSetAttribute(k_build<GH_QLUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)bytes);
   cudaFuncSetAttribute(k_build<GH_FLOAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -15,8 +15,14 @@ struct DevFeatureGroup {
   int32_t f_begin;
   int32_t f_end;
   int32_t bin_base;  // first global bin of the group
-  int32_t num_bins;  // bins in the group
+  int32_t num_bins;  // bins in the group (packed layout) or (f_end-f_begin) << shift
+  int32_t shift;     // quantized kernel: log2 of the per-feature bin stride in shared memory
+  int32_t _pad;
 };
+
+// The 4-bin quantized build kernel keeps per-CTA accumulators for at most this many
+// shared-memory cells (features x power-of-two bin stride).
+constexpr int kQ4MaxCells = 8192;
 
 // Everything the per-split kernels touch, passed by value.
 struct GrowDev {
