@@ -19,6 +19,8 @@
 
 namespace lgbm_b200 {
 void set_build_smem_limit(size_t bytes);
+int q4_max_cells();
+bool q4_supported(int shift, int nch);
 void launch_learner_gradients(const ObjDev& o, int32_t kind, cudaStream_t st);
 void launch_gather_partition(const GrowDev& d, uint32_t* out, cudaStream_t st);
 }  // namespace lgbm_b200
@@ -180,6 +182,8 @@ struct lgbm_b200_learner {
   int32_t slot_len = 0;
   int32_t max_tiles = 0;
   int gh_mode = GH_FLOAT;
+  int q4_shift = 0;
+  int q4_nch = 0;
   int build_blocks = 0;
   size_t build_smem = 0;
   std::vector<DevFeatureGroup> groups;
@@ -218,36 +222,26 @@ int lgbm_b200_learner::configure_groups(int mode) {
   groups.clear();
   const int F = ds->num_features;
   if (mode == GH_QPACK) {
-    // fixed power-of-two bin stride per group: cell = (feature << shift) + bin
-    auto ceil_log2 = [](int v) {
-      int s = 0;
-      while ((1 << s) < v) ++s;
-      return s;
-    };
-    DevFeatureGroup cur{0, 0, 0, 0, 0, 0};
-    for (int b0 = 0; b0 < F; b0 += 16) {
-      const int b1 = std::min(F, b0 + 16);
-      int sh = 0;
-      for (int f = b0; f < b1; ++f) sh = std::max(sh, ceil_log2(ds->feats[f].num_bin));
-      const int nsh = std::max(cur.shift, sh);
-      const bool fits = ((b1 - cur.f_begin) << nsh) <= kQ4MaxCells && (b1 - cur.f_begin) <= 128;
-      if (cur.f_end > cur.f_begin && !fits) {
-        groups.push_back(cur);
-        cur = DevFeatureGroup{b0, b0, ds->feats[b0].bin_off, 0, 0, 0};
-      }
-      if (cur.f_end == cur.f_begin) {
-        cur.f_begin = b0;
-        cur.bin_base = ds->feats[b0].bin_off;
-      }
-      cur.f_end = b1;
-      cur.shift = std::max(cur.shift, sh);
-      cur.num_bins = (cur.f_end - cur.f_begin) << cur.shift;
+    // One power-of-two bin stride for every group: cell = (feature << shift) + bin.
+    // Groups hold whole 16-feature blocks (aligned 16-byte row loads) except the last.
+    int shift = 4;
+    for (int f = 0; f < F; ++f)
+      while ((1 << shift) < ds->feats[f].num_bin) ++shift;
+    const int max_nf = std::min(128, kQ4MaxCells >> shift);
+    const int per_group = F <= max_nf ? F : (max_nf / 16) * 16;
+    for (int f0 = 0; f0 < F; f0 += per_group) {
+      const int f1 = std::min(F, f0 + per_group);
+      groups.push_back(DevFeatureGroup{f0, f1, ds->feats[f0].bin_off, (f1 - f0) << shift, shift,
+                                       0});
     }
-    if (cur.f_end > cur.f_begin) groups.push_back(cur);
-    size_t cap = 0;
-    for (auto& g : groups) cap = std::max(cap, (size_t)g.num_bins);
-    // hot packed cells (4 B) + hot level-3 counts (2 B) + cold g and q sums (8 B)
-    build_smem = (cap + (cap + 1) / 2 + 2 * cap) * 4;
+    const int nch = (per_group + 15) / 16;
+    if (!q4_supported(shift, nch))
+      return fail(LGBM_B200_CAPABILITY_UNAVAILABLE,
+                  "quantized build: no kernel for bin stride 2^%d with %d feature chunks", shift,
+                  nch);
+    q4_shift = shift;
+    q4_nch = nch;
+    build_smem = (size_t)4 * sizeof(uint32_t) * q4_max_cells();
     gh_mode = mode;
     CUDA_TRY(d_groups.alloc(groups.size()));
     CUDA_TRY(cudaMemcpy(d_groups.p, groups.data(), groups.size() * sizeof(DevFeatureGroup),
@@ -256,7 +250,7 @@ int lgbm_b200_learner::configure_groups(int mode) {
     CUDA_TRY(cudaGetLastError());
     const int sms = sm_count(device);
     build_blocks = sms * 2;
-    // per-CTA row ranges stay below 65536 rows (16-bit level-3 counters)
+    // per-CTA row ranges stay below 65536 rows (level-3 counters and cold sums)
     const int64_t need = (ds->num_data + 65535 - 1) / 65535;
     if (build_blocks < need) build_blocks = (int)need;
     return LGBM_B200_OK;
@@ -378,6 +372,8 @@ void lgbm_b200_learner::bind(const void* gh_ptr, const DevGhParams* ghp_ptr,
   d.ghp = ghp_ptr;
   d.stopped = stopped;
   d.gh_mode = gh_mode;
+  d.q4_shift = q4_shift;
+  d.q4_nch = q4_nch;
   d.groups = d_groups.p;
   d.num_groups = (int32_t)groups.size();
 }

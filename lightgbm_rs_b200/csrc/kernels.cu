@@ -20,7 +20,7 @@ namespace {
 
 constexpr int kBuildThreads = 512;
 constexpr int kMinRowsPerBlock = 2048;
-constexpr int kScanThreads = 128;
+constexpr int kScanThreads = 1024;
 constexpr int kPartThreads = 256;
 constexpr int kPartItems = 8;
 constexpr int kPartTile = kPartThreads * kPartItems;
@@ -212,14 +212,42 @@ __global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d) {
 // Histogram build for quantized gradients with num_grad_quant_bins <= 4 (levels
 // qg in [-2,2], qh in [0,4]). One native 32-bit shared atomic per (row, feature)
 // adds the signed packed word qg + (qh << 16); rows with qh == 3 (the one level
-// that is not a multiple of level 1 after dequantization) also bump a 16-bit
-// counter. The packed words are folded into 32-bit cold sums every kQ4Chunk rows,
-// before a field can overflow. Shared-memory cell = (feature << shift) + bin.
+// that is not a multiple of level 1 after dequantization) also bump a counter that
+// sits at a fixed offset from the packed cell. Packed words are folded into 32-bit
+// cold sums every kQ4Chunk rows, before a field can overflow.
+// Shared-memory cell = (local feature << SHIFT) + bin; SHIFT and the number of
+// 16-feature chunks NCH are compile-time so cell offsets fold into immediates.
+// Layout (u32 words): hot[kQ4MaxCells] | c3[kQ4MaxCells] | cold_g | cold_q.
 // ------------------------------------------------------------------------------------
 
 constexpr int kQ4Threads = 512;
 constexpr int kQ4Chunk = 8191;  // |sum qg| <= 2*8191 and sum qh <= 4*8191 fit 16-bit fields
 
+// MASKED: per-feature build mask on every chunk. Otherwise every feature of the group
+// is used and only the last chunk (features nf-16(NCH-1) .. 15 absent) is masked.
+template <int SHIFT, int NCH, bool MASKED>
+__device__ __forceinline__ void q4_row(const uint4* __restrict__ rp, int32_t pv, bool is3,
+                                       uint32_t* hot, const uint32_t* mask, uint32_t tail) {
+  uint4 w[NCH];
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch) w[ch] = rp[ch];
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch) {
+    const uint32_t words[4] = {w[ch].x, w[ch].y, w[ch].z, w[ch].w};
+    const uint32_t m16 = MASKED ? ((mask[ch >> 1] >> ((ch & 1) * 16)) & 0xffffu) : tail;
+    const bool test = MASKED || ch == NCH - 1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (test && !((m16 >> j) & 1u)) continue;
+      const uint32_t bin = (words[j >> 2] >> (8 * (j & 3))) & 0xffu;
+      uint32_t* cell = hot + ((16 * ch + j) << SHIFT) + bin;
+      atomicAdd(reinterpret_cast<int*>(cell), pv);
+      if (is3) atomicAdd(cell + kQ4MaxCells, 1u);
+    }
+  }
+}
+
+template <int SHIFT, int NCH>
 __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
   extern __shared__ uint32_t sm[];
   __shared__ int32_t s_nb[128];
@@ -235,8 +263,7 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
   const int32_t buf = d.leaf_buf[leaf];
   const DevFeatureGroup grp = d.groups[blockIdx.y];
   const int nf = grp.f_end - grp.f_begin;
-  const int shift = grp.shift;
-  const int cap = grp.num_bins;
+  const int cap = nf << SHIFT;  // <= kQ4MaxCells (host group planning)
   int nb_active = (count + kMinRowsPerBlock - 1) / kMinRowsPerBlock;
   if (nb_active > (int)gridDim.x) nb_active = gridDim.x;
   if (nb_active < 1) nb_active = 1;
@@ -246,13 +273,18 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
   const int32_t r1 = min(count, r0 + per);
   if (r0 >= r1) return;
 
-  uint32_t* hot = sm;                                            // [cap]
-  const int c3n = (cap + 1) >> 1;
-  uint32_t* c3w = sm + cap;                                      // [c3n] 16-bit pairs
-  int32_t* cold_g = reinterpret_cast<int32_t*>(c3w + c3n);       // [cap]
-  int32_t* cold_q = cold_g + cap;                                // [cap]
-  const int nwords = cap + c3n + 2 * cap;
-  for (int i = threadIdx.x; i < nwords; i += blockDim.x) sm[i] = 0u;
+  uint32_t* hot = sm;
+  uint32_t* c3 = sm + kQ4MaxCells;
+  int32_t* cold_g = reinterpret_cast<int32_t*>(sm + 2 * kQ4MaxCells);
+  int32_t* cold_q = reinterpret_cast<int32_t*>(sm + 3 * kQ4MaxCells);
+  for (int i = threadIdx.x; i < cap; i += kQ4Threads) {
+    hot[i] = 0u;
+    c3[i] = 0u;
+    cold_g[i] = 0;
+    cold_q[i] = 0;
+  }
+  // Features the parent could not split are neither built nor scanned
+  // (learner.rs:2003-2020 build mask).
   const bool sub = c->use_subtract != 0;
   const uint8_t* ps = d.splittable + (size_t)c->left_leaf * d.F + grp.f_begin;
   for (int fl = threadIdx.x; fl < nf; fl += blockDim.x) {
@@ -269,36 +301,42 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
     s_mask[threadIdx.x] = m;
   }
   __syncthreads();
-  const uint32_t m0 = s_mask[0], m1 = s_mask[1], m2 = s_mask[2], m3 = s_mask[3];
+  uint32_t mask[4] = {s_mask[0], s_mask[1], s_mask[2], s_mask[3]};
+  const int ntail = nf - 16 * (NCH - 1);  // features in the last chunk, 1..16
+  // a short last group (ntail <= 0) never takes the unmasked path: its earlier chunks
+  // are incomplete, so `full` below is false
+  const uint32_t tail = ntail >= 16 ? 0xffffu : (ntail <= 0 ? 0u : ((1u << ntail) - 1u));
+  bool full = true;
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch) {
+    const uint32_t want = ch == NCH - 1 ? tail : 0xffffu;
+    const uint32_t m16 = (mask[ch >> 1] >> ((ch & 1) * 16)) & 0xffffu;
+    if (m16 != want) full = false;
+  }
   const uint32_t* idx = buf == 1 ? d.idx1 : d.idx0;
   const uint16_t* gq = reinterpret_cast<const uint16_t*>(d.gh);
   const bool identity = buf == 2;
-  const int nchunks = (nf + 15) >> 4;
+  const uint8_t* bins = d.bins + grp.f_begin;
+  const size_t stride = (size_t)d.stride;
   for (int32_t cs = r0; cs < r1; cs += kQ4Chunk) {
     const int32_t ce = min(r1, cs + kQ4Chunk);
-    for (int32_t k = cs + (int32_t)threadIdx.x; k < ce; k += kQ4Threads) {
-      const uint32_t row = identity ? (uint32_t)(begin + k) : idx[begin + k];
-      const uint16_t q = gq[row];
-      const int qg = (int)(int8_t)(q & 0xff);
-      const int qh = (int)(int8_t)(q >> 8);
-      const int32_t pv = qg + (qh << 16);
-      const bool is3 = qh == 3;
-      const uint4* rp = reinterpret_cast<const uint4*>(d.bins + (size_t)row * d.stride +
-                                                       grp.f_begin);
-      for (int ch = 0; ch < nchunks; ++ch) {
-        const uint4 w = rp[ch];
-        const int wi = ch >> 1;  // 16-feature chunk ch lives in 32-bit mask word ch / 2
-        const uint32_t mw = wi < 2 ? (wi == 0 ? m0 : m1) : (wi == 2 ? m2 : m3);
-        const uint32_t m16 = (ch & 1) ? (mw >> 16) : (mw & 0xffffu);
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (!((m16 >> j) & 1u)) continue;
-          const uint32_t bin = (words[j >> 2] >> (8 * (j & 3))) & 0xffu;
-          const uint32_t cell = ((uint32_t)(16 * ch + j) << shift) + bin;
-          atomicAdd(reinterpret_cast<int*>(hot) + cell, pv);
-          if (is3) atomicAdd(c3w + (cell >> 1), 1u << ((cell & 1u) << 4));
-        }
+    for (int32_t k = cs + (int32_t)threadIdx.x; k < ce; k += 2 * kQ4Threads) {
+      const int32_t k2 = k + kQ4Threads;
+      const bool two = k2 < ce;
+      const uint32_t row0 = identity ? (uint32_t)(begin + k) : idx[begin + k];
+      const uint32_t row1 = two ? (identity ? (uint32_t)(begin + k2) : idx[begin + k2]) : row0;
+      const uint16_t q0 = gq[row0];
+      const uint16_t q1 = gq[row1];
+      const uint4* rp0 = reinterpret_cast<const uint4*>(bins + (size_t)row0 * stride);
+      const uint4* rp1 = reinterpret_cast<const uint4*>(bins + (size_t)row1 * stride);
+      const int qg0 = (int)(int8_t)(q0 & 0xff), qh0 = (int)(int8_t)(q0 >> 8);
+      const int qg1 = (int)(int8_t)(q1 & 0xff), qh1 = (int)(int8_t)(q1 >> 8);
+      if (full) {
+        q4_row<SHIFT, NCH, false>(rp0, qg0 + (qh0 << 16), qh0 == 3, hot, mask, tail);
+        if (two) q4_row<SHIFT, NCH, false>(rp1, qg1 + (qh1 << 16), qh1 == 3, hot, mask, tail);
+      } else {
+        q4_row<SHIFT, NCH, true>(rp0, qg0 + (qh0 << 16), qh0 == 3, hot, mask, tail);
+        if (two) q4_row<SHIFT, NCH, true>(rp1, qg1 + (qh1 << 16), qh1 == 3, hot, mask, tail);
       }
     }
     if (ce < r1) {
@@ -316,20 +354,37 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
   __syncthreads();
   long long* raw = d.raw;
   for (int s = threadIdx.x; s < cap; s += kQ4Threads) {
-    const int fl = s >> shift;
-    const int bin = s & ((1 << shift) - 1);
+    const int fl = s >> SHIFT;
+    const int bin = s & ((1 << SHIFT) - 1);
     if (fl >= nf || bin >= s_nb[fl]) continue;
     const int32_t v = (int32_t)hot[s];
     const int32_t lo = (int32_t)(int16_t)(v & 0xffff);
     const long long g = (long long)cold_g[s] + lo;
     const long long qsum = (long long)cold_q[s] + ((v - lo) >> 16);
-    const long long c3 = (c3w[s >> 1] >> ((s & 1) << 4)) & 0xffffu;
-    const long long h = (qsum - 3 * c3) | (c3 << 32);
+    const long long n3 = (long long)c3[s];
+    const long long h = (qsum - 3 * n3) | (n3 << 32);
     const size_t gb = (size_t)(s_boff[fl] + bin);
     if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb]), (unsigned long long)g);
     if (h)
       atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb + 1]), (unsigned long long)h);
   }
+}
+
+// (SHIFT, NCH) instantiations with (16 * (NCH - 1) + 1) << SHIFT <= kQ4MaxCells.
+using Q4Kernel = void (*)(GrowDev);
+__host__ Q4Kernel q4_kernel(int shift, int nch) {
+#define Q4_CASE(S, N) \
+  if (shift == S && nch == N) return k_build_q4<S, N>;
+  Q4_CASE(4, 1) Q4_CASE(4, 2) Q4_CASE(4, 3) Q4_CASE(4, 4)
+  Q4_CASE(4, 5) Q4_CASE(4, 6) Q4_CASE(4, 7) Q4_CASE(4, 8)
+  Q4_CASE(5, 1) Q4_CASE(5, 2) Q4_CASE(5, 3) Q4_CASE(5, 4)
+  Q4_CASE(5, 5) Q4_CASE(5, 6) Q4_CASE(5, 7) Q4_CASE(5, 8)
+  Q4_CASE(6, 1) Q4_CASE(6, 2) Q4_CASE(6, 3) Q4_CASE(6, 4)
+  Q4_CASE(6, 5) Q4_CASE(6, 6) Q4_CASE(6, 7)
+  Q4_CASE(7, 1) Q4_CASE(7, 2) Q4_CASE(7, 3) Q4_CASE(7, 4)
+  Q4_CASE(8, 1) Q4_CASE(8, 2)
+#undef Q4_CASE
+  return nullptr;
 }
 
 // ------------------------------------------------------------------------------------
@@ -354,6 +409,51 @@ struct ScanLeaf {
   int32_t num_data;
 };
 
+// Named barrier over one 256-thread group (ids 1..15; id 0 is __syncthreads).
+__device__ __forceinline__ void group_sync(int id) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(256) : "memory");
+}
+
+// p[k] <- init + p[0] + ... + p[k] in place, strictly left to right: the reference's
+// sequential f64 accumulation. Blocks of 16 addends are loaded into registers first,
+// so each step costs one dependent add.
+__device__ __forceinline__ double seq_prefix_inplace(double* p, int count, double init) {
+  double acc = init;
+  int k = 0;
+  for (; k + 16 <= count; k += 16) {
+    double v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = p[k + j];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      acc += v[j];
+      v[j] = acc;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) p[k + j] = v[j];
+  }
+  for (; k < count; ++k) {
+    acc += p[k];
+    p[k] = acc;
+  }
+  return acc;
+}
+
+// init - v[0] - v[stride] - ... - v[(n-1)*stride], strictly left to right.
+__device__ __forceinline__ double seq_sub(const double* v, int stride, int n, double init) {
+  double acc = init;
+  int k = 0;
+  for (; k + 16 <= n; k += 16) {
+    double x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = v[(k + j) * stride];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc -= x[j];
+  }
+  for (; k < n; ++k) acc -= v[k * stride];
+  return acc;
+}
+
 __device__ __forceinline__ void warp_best(double& gain, int32_t& k) {
   // max gain, ties to the smallest k (first in scan order)
   for (int o = 16; o > 0; o >>= 1) {
@@ -366,10 +466,30 @@ __device__ __forceinline__ void warp_best(double& gain, int32_t& k) {
   }
 }
 
+constexpr int kScanGroup = 256;  // threads per (leaf, direction) scan: one candidate each
+
+struct ScanScratch {
+  double pg[kMaxBins];   // addends, then running gradient sums
+  double ph[kMaxBins];   // addends, then running hessian sums
+  int32_t pc[kMaxBins];  // running counts
+  int32_t wsum[8];
+  int32_t wpre[8];
+  int32_t wmin[8];
+  int32_t wk[8];
+  int32_t whas[8];
+  double wgain[8];
+};
+
+// One direction of find_best_split_cpu_native (lgbm-compute/src/kernels/split.rs:8970-9329)
+// for one feature, by one 256-thread group (thread k owns candidate step k). The two
+// dependent f64 chains (running gradient and hessian sums, the hessian seeded with
+// kEpsilon) run sequentially in the reference's order on threads 0 and 32; counts,
+// the sticky stop, gains and the first-max selection run across the group.
 __device__ void scan_direction(const double* hist, const DevFeature& f, const DevGainConfig& cfg,
-                               const ScanLeaf& leaf, bool forward, double* pg, double* ph,
-                               int32_t* pc, ScanCand* out) {
-  const int lane = threadIdx.x & 31;
+                               const ScanLeaf& leaf, bool forward, ScanScratch& s, int bar_id,
+                               ScanCand* out) {
+  const int gt = threadIdx.x & (kScanGroup - 1);
+  const int lane = gt & 31, wg = gt >> 5;
   const double eps = k_eps();
   const int nb = f.num_bin;
   const int offset = f.offset;
@@ -377,118 +497,90 @@ __device__ void scan_direction(const double* hist, const DevFeature& f, const De
   const bool skip_def = (f.flags & 1) != 0;
   const double bumped = leaf.sum_h + 2.0 * eps;
   const double cnt_factor = (double)leaf.num_data / bumped;
-  const double gain_shift = d_leaf_gain_full(cfg, leaf.sum_g, bumped, leaf.num_data,
-                                             leaf.parent_output);
-  const double min_gain_shift = gain_shift + cfg.min_gain_to_split;
   const int32_t min_data = cfg.min_data_in_leaf;
   const double min_hess = cfg.min_sum_hessian_in_leaf;
-
   int count, t0;  // t = forward ? t0 + k : t0 - k
-  double g_init = 0.0, h_init = eps;
-  int32_t c_init = 0;
+  bool na_pre = false;
   if (!forward) {
     count = max(nb - 1 - na, 0);
     t0 = nb - 1 - offset - na;
   } else {
-    const bool run_forward = (f.flags & 4) != 0;
-    const bool na_pre = na && offset == 1;
-    if (!run_forward) {
-      count = 0;
-    } else {
-      count = max(nb - 1 - offset, 0) + (na_pre ? 1 : 0);
-    }
+    na_pre = na && offset == 1;
+    count = (f.flags & 4) ? max(nb - 1 - offset, 0) + (na_pre ? 1 : 0) : 0;
     t0 = na_pre ? -1 : 0;
-    if (na_pre && count > 0) {
-      // NA preamble (split.rs:9183-9199): seed with the leaf totals and subtract every
-      // explicit bin in ascending order.
-      double gg = leaf.sum_g, hh = bumped - eps;
-      int32_t cc = leaf.num_data;
-      for (int i = 0; i < nb - offset; ++i) {
-        gg -= hist[2 * i];
-        hh -= hist[2 * i + 1];
-        cc -= d_round_int(hist[2 * i + 1] * cnt_factor);
-      }
-      g_init = gg;
-      h_init = hh;
-      c_init = cc;
-    }
+    if (count == 0) na_pre = false;
   }
-  auto active_at = [&](int k, int* t_out) -> bool {
-    const int t = forward ? t0 + k : t0 - k;
-    *t_out = t;
-    const bool skip = skip_def && (t + offset) == f.default_bin;
-    if (!forward) return (t >= (1 - offset)) && !skip;
-    return !skip;
-  };
-  // Addend of every step across the warp (0 when the step is inactive; the running
-  // sums are never -0.0, so `+ 0.0` leaves them unchanged, split.rs:8950-8960), then
-  // the dependent f64 chains, sequential in the reference's order: lane 0 gradient,
-  // lane 1 hessian, in SIMT lockstep.
-  for (int k = lane; k < count; k += 32) {
-    int t;
-    const bool act = active_at(k, &t) && t >= 0;
-    pg[k] = act ? hist[2 * t] : 0.0;
-    ph[k] = act ? hist[2 * t + 1] : 0.0;
+  // 1. addend of step k (0 when the step is inactive; the running sums are never -0.0,
+  //    so `+ 0.0` leaves them unchanged, split.rs:8950-8960)
+  const int k = gt;
+  const int t = forward ? t0 + k : t0 - k;
+  const bool skip = skip_def && (t + offset) == f.default_bin;
+  const bool act = k < count && (forward ? !skip : (t >= (1 - offset) && !skip));
+  const bool act_t = act && t >= 0;
+  const double ah = act_t ? hist[2 * t + 1] : 0.0;
+  if (k < count) {
+    s.pg[k] = act_t ? hist[2 * t] : 0.0;
+    s.ph[k] = ah;
   }
-  __syncwarp();
-  if (lane < 2 && count > 0) {
-    double* p = lane == 0 ? pg : ph;
-    double acc = lane == 0 ? g_init : h_init;
-#pragma unroll 8
-    for (int k = 0; k < count; ++k) {
-      acc += p[k];
-      p[k] = acc;
-    }
+  int32_t cv = act_t ? d_round_int(ah * cnt_factor) : 0;
+  int32_t pre = (na_pre && gt < nb - offset) ? d_round_int(hist[2 * gt + 1] * cnt_factor) : 0;
+  group_sync(bar_id);
+  // 2. sequential chains
+  if ((gt == 0 || gt == 32) && count > 0) {
+    const bool isg = gt == 0;
+    double init = isg ? 0.0 : eps;
+    if (na_pre)  // NA preamble (split.rs:9183-9199): leaf totals minus every explicit bin
+      init = isg ? seq_sub(hist, 2, nb - offset, leaf.sum_g)
+                 : seq_sub(hist + 1, 2, nb - offset, bumped - eps);
+    seq_prefix_inplace(isg ? s.pg : s.ph, count, init);
   }
-  // Integer count prefix across the warp.
-  int32_t carry = c_init;
-  for (int k0 = 0; k0 < count; k0 += 32) {
-    const int k = k0 + lane;
-    int32_t v = 0;
-    if (k < count) {
-      int t;
-      if (active_at(k, &t) && t >= 0) v = d_round_int(hist[2 * t + 1] * cnt_factor);
-    }
-    for (int o = 1; o < 32; o <<= 1) {
-      const int32_t n = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += n;
-    }
-    if (k < count) pc[k] = carry + v;
-    carry += __shfl_sync(0xffffffffu, v, 31);
+  // 3. integer count prefix across the group
+  int32_t incl = cv;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
   }
-  __syncwarp();
-  // First step that breaks the scan (sticky `done`).
+  for (int o = 16; o > 0; o >>= 1) pre += __shfl_xor_sync(0xffffffffu, pre, o);
+  if (lane == 31) s.wsum[wg] = incl;
+  if (lane == 0) s.wpre[wg] = pre;
+  group_sync(bar_id);
+  int32_t c_init = 0, woff = 0;
+  if (na_pre) {
+    int32_t tot = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot += s.wpre[w];
+    c_init = leaf.num_data - tot;
+  }
+#pragma unroll
+  for (int w = 0; w < 8; ++w)
+    if (w < wg) woff += s.wsum[w];
+  const int32_t c_own = c_init + woff + incl;
+  const int32_t c_oth = leaf.num_data - c_own;
+  double g_own = 0.0, h_own = 0.0;
+  if (k < count) {
+    g_own = s.pg[k];
+    h_own = s.ph[k];
+    s.pc[k] = c_own;
+  }
+  const double h_oth = bumped - h_own;
+  const bool cont = c_own < min_data || h_own < min_hess;
+  const bool brk = c_oth < min_data || h_oth < min_hess;
+  // 4. first step that breaks the scan (sticky `done`)
+  int32_t kst = (act && !cont && brk) ? k : 0x7fffffff;
+  for (int o = 16; o > 0; o >>= 1) kst = min(kst, __shfl_xor_sync(0xffffffffu, kst, o));
+  if (lane == 0) s.wmin[wg] = kst;
+  group_sync(bar_id);
   int32_t kstar = 0x7fffffff;
-  for (int k = lane; k < count; k += 32) {
-    int t;
-    const bool act = active_at(k, &t);
-    const int32_t c_own = pc[k];
-    const int32_t c_oth = leaf.num_data - c_own;
-    const double h_own = ph[k];
-    const double h_oth = bumped - h_own;
-    const bool cont = c_own < min_data || h_own < min_hess;
-    const bool brk = c_oth < min_data || h_oth < min_hess;
-    if (act && !cont && brk) {
-      kstar = k;
-      break;
-    }
-  }
-  for (int o = 16; o > 0; o >>= 1) kstar = min(kstar, __shfl_xor_sync(0xffffffffu, kstar, o));
-  // Candidate gains.
+#pragma unroll
+  for (int w = 0; w < 8; ++w) kstar = min(kstar, s.wmin[w]);
+  // 5. candidate gain of step k
   double best_gain = kNegInf;
   int32_t best_k = -1;
   int32_t has = 0;
-  const int kend = min(count, kstar);
-  for (int k = lane; k < kend; k += 32) {
-    int t;
-    const bool act = active_at(k, &t);
-    if (!act) continue;
-    const int32_t c_own = pc[k];
-    const int32_t c_oth = leaf.num_data - c_own;
-    const double h_own = ph[k];
-    if (c_own < min_data || h_own < min_hess) continue;
-    const double g_own = pg[k];
-    const double h_oth = bumped - h_own;
+  if (act && !cont && k < kstar) {
+    const double gain_shift = d_leaf_gain_full(cfg, leaf.sum_g, bumped, leaf.num_data,
+                                               leaf.parent_output);
+    const double min_gain_shift = gain_shift + cfg.min_gain_to_split;
     const double g_oth = leaf.sum_g - g_own;
     double gain;
     if (!forward)  // own side is the right child
@@ -497,35 +589,49 @@ __device__ void scan_direction(const double* hist, const DevFeature& f, const De
       gain = d_split_gain(cfg, g_own, h_own, g_oth, h_oth, c_own, c_oth, leaf.parent_output);
     if (gain > min_gain_shift) {
       has = 1;
-      if (gain > best_gain) {
-        best_gain = gain;
-        best_k = k;
-      }
+      best_gain = gain;
+      best_k = k;
     }
   }
   has = __any_sync(0xffffffffu, has) ? 1 : 0;
   warp_best(best_gain, best_k);
   if (lane == 0) {
-    out->has = has;
-    out->best_k = best_k;
-    out->gain = best_gain;
-    if (best_k >= 0) {
-      int t;
-      active_at(best_k, &t);
+    s.wgain[wg] = best_gain;
+    s.wk[wg] = best_k;
+    s.whas[wg] = has;
+  }
+  group_sync(bar_id);
+  if (gt == 0) {
+    double bg = kNegInf;
+    int32_t bk = -1, hs = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      hs |= s.whas[w];
+      const double g = s.wgain[w];
+      const int32_t kk = s.wk[w];
+      if (g > bg || (g == bg && kk >= 0 && (bk < 0 || kk < bk))) {
+        bg = g;
+        bk = kk;
+      }
+    }
+    out->has = hs;
+    out->best_k = bk;
+    out->gain = bg;
+    if (bk >= 0) {
+      const int tb = forward ? t0 + bk : t0 - bk;
       if (!forward) {
-        out->slg = leaf.sum_g - pg[best_k];
-        out->slh = bumped - ph[best_k];
-        out->lc = leaf.num_data - pc[best_k];
-        out->thr = t - 1 + offset;
+        out->slg = leaf.sum_g - s.pg[bk];
+        out->slh = bumped - s.ph[bk];
+        out->lc = leaf.num_data - s.pc[bk];
+        out->thr = tb - 1 + offset;
       } else {
-        out->slg = pg[best_k];
-        out->slh = ph[best_k];
-        out->lc = pc[best_k];
-        out->thr = t + offset;
+        out->slg = s.pg[bk];
+        out->slh = s.ph[bk];
+        out->lc = s.pc[bk];
+        out->thr = tb + offset;
       }
     }
   }
-  __syncwarp();
 }
 
 // Finalization of the winning candidate (split.rs:9267-9326).
@@ -848,107 +954,115 @@ __device__ __forceinline__ bool cand_better(double ga, int32_t fa, int32_t ia, d
   return ia < ib;
 }
 
-// Block-wide argmax of (g, f, i) under cand_better; result valid in every thread.
-__device__ void block_argmax(double& g, int32_t& f, int32_t& i) {
-  __shared__ double s_g[32];
-  __shared__ int32_t s_f[32], s_i[32];
+struct Cand {
+  double g;
+  int32_t f, i;
+};
+
+__device__ __forceinline__ void warp_argmax(Cand& c) {
   for (int o = 16; o > 0; o >>= 1) {
-    const double og = __shfl_xor_sync(0xffffffffu, g, o);
-    const int32_t of = __shfl_xor_sync(0xffffffffu, f, o);
-    const int32_t oi = __shfl_xor_sync(0xffffffffu, i, o);
-    if (cand_better(og, of, oi, g, f, i)) {
-      g = og;
-      f = of;
-      i = oi;
-    }
+    Cand x;
+    x.g = __shfl_xor_sync(0xffffffffu, c.g, o);
+    x.f = __shfl_xor_sync(0xffffffffu, c.f, o);
+    x.i = __shfl_xor_sync(0xffffffffu, c.i, o);
+    if (cand_better(x.g, x.f, x.i, c.g, c.f, c.i)) c = x;
   }
+}
+
+// Block-wide argmax of NC candidates per thread under cand_better (two shuffle levels);
+// the results are valid in every thread.
+template <int NC>
+__device__ void block_argmax(Cand (&c)[NC]) {
+  __shared__ Cand s_c[NC][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int j = 0; j < NC; ++j) warp_argmax(c[j]);
   __syncthreads();
-  if (lane == 0) {
-    s_g[warp] = g;
-    s_f[warp] = f;
-    s_i[warp] = i;
+  if (lane == 0)
+#pragma unroll
+    for (int j = 0; j < NC; ++j) s_c[j][warp] = c[j];
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+      Cand x = lane < nw ? s_c[j][lane] : Cand{kNegInf, -1, 0x7fffffff};
+      warp_argmax(x);
+      if (lane == 0) s_c[j][0] = x;
+    }
   }
   __syncthreads();
-  g = s_g[0];
-  f = s_f[0];
-  i = s_i[0];
-  for (int w = 1; w < nw; ++w)
-    if (cand_better(s_g[w], s_f[w], s_i[w], g, f, i)) {
-      g = s_g[w];
-      f = s_f[w];
-      i = s_i[w];
-    }
-  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < NC; ++j) c[j] = s_c[j][0];
 }
 
 __device__ void pick_split(const GrowDev& d) {
   GrowCtrl* c = d.ctrl;
   const int tid = threadIdx.x;
-  if (c->do_find) {
-    for (int sel = 0; sel < 2; ++sel) {
-      const int32_t leaf = sel == 0 ? c->smaller_leaf : c->larger_leaf;
-      if (leaf < 0) continue;
-      if (!__ldcg(&d.scan_ok[sel])) {
-        if (tid == 0) {
-          d.best[leaf] = d_split_none();
-          d.best_feature[leaf] = -1;
-        }
-        continue;
-      }
-      // cross-feature argmax of this leaf (learner.rs:3314-3321)
-      double bg = kNegInf;
-      int32_t bf = -1;
-      for (int f = tid; f < d.F; f += blockDim.x) {
-        const double g = __ldcg(&d.scan_out[sel * d.F + f].gain);
-        d.splittable[(size_t)leaf * d.F + f] = g > kNegInf ? 1 : 0;
-        if (g > kNegInf && cand_better(g, f, f, bg, bf, bf)) {
-          bg = g;
-          bf = f;
-        }
-      }
-      int32_t bi = bf;
-      block_argmax(bg, bf, bi);
-      if (tid == 0) {
-        d.best[leaf] = bf >= 0 ? d.scan_out[sel * d.F + bf] : d_split_none();
-        d.best_feature[leaf] = bf;
-      }
-      __syncthreads();
-    }
-  }
-  __threadfence_block();
-  __syncthreads();
-  // arg_max over leaves (learner.rs:4537-4551)
-  double bg = kNegInf;
-  int32_t bf = -1, bl = 0x7fffffff;
+  __shared__ DevSplitInfo s_win[2];
+  const int32_t S = c->smaller_leaf, Lg = c->larger_leaf;
+  const bool find = c->do_find != 0;
+  // the other leaves' current best (learner.rs:4537-4551 arg_max inputs), prefetched;
+  // the two leaves scanned now join below with their new values
+  Cand lc{kNegInf, -1, 0x7fffffff};
   for (int i = tid; i < d.L; i += blockDim.x) {
-    const double g = __ldcg(&d.best[i].gain);
-    const int32_t f = __ldcg(&d.best_feature[i]);
-    if (bl == 0x7fffffff || cand_better(g, f, i, bg, bf, bl)) {
-      bg = g;
-      bf = f;
-      bl = i;
+    if (find && (i == S || i == Lg)) continue;
+    const Cand x{__ldcg(&d.best[i].gain), __ldcg(&d.best_feature[i]), i};
+    if (lc.i == 0x7fffffff || cand_better(x.g, x.f, x.i, lc.g, lc.f, lc.i)) lc = x;
+  }
+  if (find) {
+    // cross-feature argmax of both scanned leaves at once (learner.rs:3314-3321)
+    const bool ok0 = __ldcg(&d.scan_ok[0]) != 0;
+    const bool ok1 = Lg >= 0 && __ldcg(&d.scan_ok[1]) != 0;
+    Cand fc[2] = {{kNegInf, -1, -1}, {kNegInf, -1, -1}};
+    for (int f = tid; f < d.F; f += blockDim.x) {
+      const double g0 = __ldcg(&d.scan_out[f].gain);
+      const double g1 = Lg >= 0 ? __ldcg(&d.scan_out[d.F + f].gain) : kNegInf;
+      if (ok0) d.splittable[(size_t)S * d.F + f] = g0 > kNegInf ? 1 : 0;
+      if (ok1) d.splittable[(size_t)Lg * d.F + f] = g1 > kNegInf ? 1 : 0;
+      if (g0 > kNegInf && cand_better(g0, f, f, fc[0].g, fc[0].f, fc[0].i)) fc[0] = {g0, f, f};
+      if (g1 > kNegInf && cand_better(g1, f, f, fc[1].g, fc[1].f, fc[1].i)) fc[1] = {g1, f, f};
+    }
+    block_argmax<2>(fc);
+    if (tid == 0 || tid == 32) {
+      const int sel = tid == 0 ? 0 : 1;
+      const int32_t leaf = sel == 0 ? S : Lg;
+      const bool ok = sel == 0 ? ok0 : ok1;
+      if (leaf >= 0) {
+        const int32_t bf = ok ? fc[sel].f : -1;
+        const DevSplitInfo si = bf >= 0 ? d.scan_out[sel * d.F + bf] : d_split_none();
+        d.best[leaf] = si;
+        d.best_feature[leaf] = bf;
+        s_win[sel] = si;
+      }
+    }
+    if (tid == 0) {
+      const Cand a{ok0 ? fc[0].g : kNegInf, ok0 ? fc[0].f : -1, S};
+      if (lc.i == 0x7fffffff || cand_better(a.g, a.f, a.i, lc.g, lc.f, lc.i)) lc = a;
+      if (Lg >= 0) {
+        const Cand b{ok1 ? fc[1].g : kNegInf, ok1 ? fc[1].f : -1, Lg};
+        if (cand_better(b.g, b.f, b.i, lc.g, lc.f, lc.i)) lc = b;
+      }
     }
   }
-  block_argmax(bg, bf, bl);
+  Cand w[1] = {lc};
+  block_argmax<1>(w);
   if (tid == 0) {
-    if (bg <= 0.0) {  // learner.rs:1503-1505
+    const int32_t bl = w[0].i;
+    if (w[0].g <= 0.0 || bl == 0x7fffffff) {  // learner.rs:1503-1505
       c->done = 1;
     } else {
       c->pending = 1;
       c->split_leaf = bl;
-      c->split_feature = bf;
-      c->split = d.best[bl];
+      c->split_feature = w[0].f;
+      c->split = (find && bl == S) ? s_win[0] : (find && bl == Lg) ? s_win[1] : d.best[bl];
     }
   }
 }
 
 __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
   __shared__ double s_hist[2][2 * kMaxBins];
-  __shared__ double s_pg[4][kMaxBins];
-  __shared__ double s_ph[4][kMaxBins];
-  __shared__ int32_t s_pc[4][kMaxBins];
+  __shared__ ScanScratch s_scan[4];
   __shared__ ScanCand s_cand[4];
   __shared__ bool s_last;
   GrowCtrl* c = d.ctrl;
@@ -962,21 +1076,23 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
         !c->use_subtract || d.splittable[(size_t)c->left_leaf * d.F + f] != 0;
     const DevFeature ft = d.feat[f];
     const int nb = ft.num_bin;
+    long long* raw = d.raw + 2 * (size_t)ft.bin_off;
     if (used) {
       const DevGhParams& p = *d.ghp;
       const bool buildable = leaf_buildable(lss);
-      long long* raw = d.raw + 2 * (size_t)ft.bin_off;
-      for (int i = tid; i < nb; i += blockDim.x) {
-        double g = 0.0, h = 0.0;
-        if (buildable) {
-          g = decode_g(p, raw[2 * i]);
-          h = decode_h(p, raw[2 * i + 1]);
-          raw[2 * i] = 0;
-          raw[2 * i + 1] = 0;
-        }
-        s_hist[0][2 * i] = g;
-        s_hist[0][2 * i + 1] = h;
+      // one histogram cell per thread (2*num_bin <= 512 cells); the parent's cell is
+      // loaded up front together with the raw accumulator
+      const bool mine = tid < 2 * nb;
+      double* pl = d.pool + (size_t)c->larger_slot * d.slot_len + ft.slot_off;
+      double parent = 0.0;
+      if (mine && Lg >= 0) parent = pl[tid];
+      double v = 0.0;
+      if (mine && buildable) {
+        const long long rv = raw[tid];
+        v = (tid & 1) ? decode_h(p, rv) : decode_g(p, rv);
+        raw[tid] = 0;
       }
+      if (mine) s_hist[0][tid] = v;
       __syncthreads();
       // FixHistogram (fix_histogram.rs:50-81): sequential ascending subtraction.
       const int mfb = ft.most_freq_bin;
@@ -984,49 +1100,38 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
         const int w = tid == 0 ? 0 : 1;
         double acc = w == 0 ? lss.sum_g : lss.sum_h;
         const double* hv = &s_hist[0][w];
-#pragma unroll 8
-        for (int i = 0; i < mfb; ++i) acc -= hv[2 * i];
-#pragma unroll 8
-        for (int i = mfb + 1; i < nb; ++i) acc -= hv[2 * i];
+        acc = seq_sub(hv, 2, mfb, acc);
+        acc = seq_sub(hv + 2 * (mfb + 1), 2, nb - mfb - 1, acc);
         s_hist[0][2 * mfb + w] = acc;
       }
       __syncthreads();
       // compact_histogram (learner.rs:4460-4486)
+      double sv = mine ? s_hist[0][tid] : 0.0;
       if (ft.offset > 0) {
-        const int off = ft.offset;
-        double tmp[2 * ((2 * kMaxBins + kScanThreads - 1) / kScanThreads)];
-        int n = 0;
-        for (int i = tid; i < 2 * nb; i += blockDim.x) {
-          const int src = i + 2 * off;
-          tmp[n++] = src < 2 * nb ? s_hist[0][src] : 0.0;
-        }
+        const int src = tid + 2 * ft.offset;
+        sv = (mine && src < 2 * nb) ? s_hist[0][src] : 0.0;
         __syncthreads();
-        n = 0;
-        for (int i = tid; i < 2 * nb; i += blockDim.x) s_hist[0][i] = tmp[n++];
-        __syncthreads();
+        if (mine) s_hist[0][tid] = sv;
       }
       // store the smaller child's slot; larger = parent - smaller in the parent's slot
-      double* ps = d.pool + (size_t)c->smaller_slot * d.slot_len + ft.slot_off;
-      for (int i = tid; i < 2 * nb; i += blockDim.x) ps[i] = s_hist[0][i];
-      if (Lg >= 0) {
-        double* pl = d.pool + (size_t)c->larger_slot * d.slot_len + ft.slot_off;
-        for (int i = tid; i < 2 * nb; i += blockDim.x) {
-          const double v = pl[i] - s_hist[0][i];
-          pl[i] = v;
-          s_hist[1][i] = v;
+      if (mine) {
+        d.pool[(size_t)c->smaller_slot * d.slot_len + ft.slot_off + tid] = sv;
+        if (Lg >= 0) {
+          const double lv = parent - sv;
+          pl[tid] = lv;
+          s_hist[1][tid] = lv;
         }
       }
       __syncthreads();
-      const int warp = tid >> 5;
-      const int sel = warp >> 1;
-      const bool fwd = (warp & 1) != 0;
+      const int grp = tid >> 8;  // (leaf, direction) group
+      const int sel = grp >> 1;
+      const bool fwd = (grp & 1) != 0;
       const int32_t leaf = sel == 0 ? S : Lg;
       if (leaf >= 0) {
         const DevLeafSplits ls = d.ls[leaf];
         if (leaf_buildable(ls)) {
           ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
-          scan_direction(s_hist[sel], ft, d.gain, sl, fwd, s_pg[warp], s_ph[warp], s_pc[warp],
-                         &s_cand[warp]);
+          scan_direction(s_hist[sel], ft, d.gain, sl, fwd, s_scan[grp], 1 + grp, &s_cand[grp]);
         }
       }
       __syncthreads();
@@ -1046,7 +1151,6 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
         }
       }
     } else {
-      long long* raw = d.raw + 2 * (size_t)ft.bin_off;
       for (int i = tid; i < 2 * nb; i += blockDim.x) raw[i] = 0;
       if (tid == 0) {
         d.scan_out[f] = d_split_none();
@@ -1126,39 +1230,57 @@ struct PartitionTile {
       tile_left += v;
     }
     const int32_t excl = warp_off + incl - my_left;
-    if (tid == 0) {
+    if (warp == 0) {
+      // Decoupled look-back, one warp reading a window of 32 predecessor words per step.
+      // Flag 1 = tile aggregate, 2 = inclusive prefix; a word of another epoch is "not
+      // ready". Positions before tile 0 read as an inclusive prefix of 0.
       int32_t prefix = 0;
       int32_t ok = 1;
-      if (tile == 0) {
+      if (lane == 0) {
         __threadfence();
-        atomicExch(&status[0], pack_status(epoch, 2u, (uint32_t)tile_left));
-      } else {
-        __threadfence();
-        atomicExch(&status[tile], pack_status(epoch, 1u, (uint32_t)tile_left));
-        int32_t j = tile - 1;
+        atomicExch(&status[tile], pack_status(epoch, tile == 0 ? 2u : 1u, (uint32_t)tile_left));
+      }
+      if (tile > 0) {
+        const uint32_t ep = epoch & 0xffffffu;
+        int32_t j_end = tile;
         long long spins = 0;
-        while (j >= 0) {
-          const unsigned long long w = atomicAdd(&status[j], 0ull);
-          const uint32_t we = (uint32_t)(w >> 40);
-          const uint32_t fl = (uint32_t)(w >> 32) & 0xffu;
-          if (we != (epoch & 0xffffffu) || fl == 0u) {
+        while (true) {
+          const int32_t j = j_end - 32 + lane;
+          uint32_t fl = 2u, val = 0u;
+          if (j >= 0) {
+            const unsigned long long w =
+                *reinterpret_cast<volatile unsigned long long*>(&status[j]);
+            fl = ((uint32_t)(w >> 40) == ep) ? ((uint32_t)(w >> 32) & 0xffu) : 0u;
+            val = (uint32_t)(w & 0xffffffffull);
+          }
+          const uint32_t pref = __ballot_sync(0xffffffffu, fl == 2u);
+          const uint32_t notready = __ballot_sync(0xffffffffu, fl == 0u);
+          const int hp = pref ? 31 - __clz(pref) : -1;  // nearest inclusive prefix
+          const uint32_t need = hp >= 0 ? (0xffffffffu << hp) : 0xffffffffu;
+          if (notready & need) {
             if (++spins > kSpinLimit) {
               ok = 0;
               break;
             }
-            __nanosleep(32);
+            __nanosleep(20);
             continue;
           }
-          prefix += (int32_t)(uint32_t)(w & 0xffffffffull);
-          if (fl == 2u) break;
-          --j;
+          int32_t v = (lane >= hp) ? (int32_t)val : 0;
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          prefix += v;
+          if (hp >= 0) break;
+          j_end -= 32;
         }
-        __threadfence();
-        atomicExch(&status[tile], pack_status(epoch, 2u, (uint32_t)(prefix + tile_left)));
+        if (lane == 0 && ok) {
+          __threadfence();
+          atomicExch(&status[tile], pack_status(epoch, 2u, (uint32_t)(prefix + tile_left)));
+        }
       }
-      atomicAdd(left_total, tile_left);
-      s_prefix = prefix;
-      s_ok = ok;
+      if (lane == 0) {
+        atomicAdd(left_total, tile_left);
+        s_prefix = prefix;
+        s_ok = ok;
+      }
     }
     __syncthreads();
     const int32_t prefix_left = s_prefix;
@@ -1238,23 +1360,20 @@ __global__ void k_hist_standalone(const uint8_t* bins, int32_t stride, int64_t n
     if (acc[i]) atomicAdd((unsigned long long*)&raw[i], acc[i]);
 }
 
-__global__ void __launch_bounds__(64) k_scan_standalone(const double* hist,
-                                                        const DevFeature* feats,
-                                                        DevGainConfig cfg, DevLeafSplits ls,
-                                                        DevSplitInfo* out) {
+__global__ void __launch_bounds__(512) k_scan_standalone(const double* hist,
+                                                         const DevFeature* feats,
+                                                         DevGainConfig cfg, DevLeafSplits ls,
+                                                         DevSplitInfo* out) {
   __shared__ double s_hist[2 * kMaxBins];
-  __shared__ double s_pg[2][kMaxBins];
-  __shared__ double s_ph[2][kMaxBins];
-  __shared__ int32_t s_pc[2][kMaxBins];
+  __shared__ ScanScratch s_scan[2];
   __shared__ ScanCand s_cand[2];
   const DevFeature ft = feats[blockIdx.x];
   for (int i = threadIdx.x; i < 2 * ft.num_bin; i += blockDim.x)
     s_hist[i] = hist[ft.slot_off + i];
   __syncthreads();
-  const int warp = threadIdx.x >> 5;
+  const int grp = threadIdx.x >> 8;
   ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
-  scan_direction(s_hist, ft, cfg, sl, warp == 1, s_pg[warp], s_ph[warp], s_pc[warp],
-                 &s_cand[warp]);
+  scan_direction(s_hist, ft, cfg, sl, grp == 1, s_scan[grp], 1 + grp, &s_cand[grp]);
   __syncthreads();
   if (threadIdx.x == 0) out[blockIdx.x] = finalize_split(cfg, sl, s_cand[0], s_cand[1]);
 }
@@ -1347,7 +1466,7 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
     {
       PROF_BEGIN(KC_BUILD);
       if (d.gh_mode == GH_QPACK)
-        k_build_q4<<<bgrid, kQ4Threads, build_smem, st>>>(d);
+        q4_kernel(d.q4_shift, d.q4_nch)<<<bgrid, kQ4Threads, build_smem, st>>>(d);
       else if (d.gh_mode == GH_QLUT)
         k_build<GH_QLUT><<<bgrid, kBuildThreads, build_smem, st>>>(d);
       else
@@ -1372,8 +1491,19 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
   }
 }
 
+int q4_max_cells() { return kQ4MaxCells; }
+
+bool q4_supported(int shift, int nch) { return q4_kernel(shift, nch) != nullptr; }
+
 void set_build_smem_limit(size_t bytes) {
-  cudaFuncSetAttribute(k_build_q4, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  for (int sh = 4; sh <= 8; ++sh)
+    for (int n = 1; n <= 8; ++n)
+      if (q4_kernel(sh, n)) {
+        cudaFuncSetAttribute(q4_kernel(sh, n), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(4 * sizeof(uint32_t) * kQ4MaxCells));
+        cudaFuncSetAttribute(q4_kernel(sh, n), cudaFuncAttributePreferredSharedMemoryCarveout,
+                             100);
+      }
   cudaFuncSetAttribute(k_build<GH_QLUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)bytes);
   cudaFuncSetAttribute(k_build<GH_FLOAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1393,7 +1523,7 @@ void launch_scan_features(const double* hist, const DevFeature* feats, int32_t n
                           DevGainConfig cfg, DevLeafSplits ls, DevSplitInfo* out,
                           cudaStream_t st) {
   if (n_feats <= 0) return;
-  k_scan_standalone<<<n_feats, 64, 0, st>>>(hist, feats, cfg, ls, out);
+  k_scan_standalone<<<n_feats, 512, 0, st>>>(hist, feats, cfg, ls, out);
 }
 
 void launch_partition_rows(const uint8_t* bins_rm, int32_t stride, int32_t feature,

@@ -21,8 +21,9 @@ struct DevFeatureGroup {
 };
 
 // The 4-bin quantized build kernel keeps per-CTA accumulators for at most this many
-// shared-memory cells (features x power-of-two bin stride).
-constexpr int kQ4MaxCells = 8192;
+// shared-memory cells (features x power-of-two bin stride): 4 x 4 B x 7168 = 112 KB,
+// two CTAs per SM.
+constexpr int kQ4MaxCells = 7168;
 
 // Everything the per-split kernels touch, passed by value.
 struct GrowDev {
@@ -73,6 +74,8 @@ struct GrowDev {
   uint8_t* scan_ok;        // [2] leaf scanned flags
   // gradients
   int32_t gh_mode;
+  int32_t q4_shift;  // quantized build: log2 bin stride
+  int32_t q4_nch;    // quantized build: 16-feature chunks per group
   const void* gh;  // float2[N] (GH_FLOAT) or uint16 int8 pairs (quantized)
   const DevGhParams* ghp;
 };
