@@ -19,7 +19,7 @@ namespace lgbm_b200 {
 namespace {
 
 constexpr int kBuildThreads = 512;
-constexpr int kMinRowsPerBlock = 2048;
+constexpr int kMinRowsPerBlock = 1024;
 constexpr int kScanThreads = 1024;
 constexpr int kPartThreads = 256;
 constexpr int kPartItems = 8;
@@ -28,6 +28,15 @@ constexpr long long kSpinLimit = 1ll << 22;
 
 __device__ __forceinline__ bool leaf_buildable(const DevLeafSplits& l) {
   return l.sum_h > 0.0 && l.num_data > 0;  // learner.rs:2477-2481
+}
+
+// Small children (rows x features under a budget) are built feature-parallel inside
+// k_fixscan, one CTA per feature, instead of by the row-parallel build kernel.
+constexpr int64_t kInBlockBudget = 1 << 16;
+constexpr int32_t kInBlockMaxRows = 65536;
+__device__ __forceinline__ bool build_in_fixscan(const GrowDev& d, int32_t count) {
+  return d.gh_mode == GH_QPACK && count <= kInBlockMaxRows &&
+         (int64_t)count * d.F <= kInBlockBudget;
 }
 
 // Decoding of the raw integer accumulators into f64 histogram cells. For the
@@ -261,6 +270,7 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
   const int32_t begin = d.leaf_begin[leaf];
   const int32_t count = d.leaf_count[leaf];
   const int32_t buf = d.leaf_buf[leaf];
+  if (build_in_fixscan(d, count)) return;
   const DevFeatureGroup grp = d.groups[blockIdx.y];
   const int nf = grp.f_end - grp.f_begin;
   const int cap = nf << SHIFT;  // <= kQ4MaxCells (host group planning)
@@ -277,11 +287,24 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
   uint32_t* c3 = sm + kQ4MaxCells;
   int32_t* cold_g = reinterpret_cast<int32_t*>(sm + 2 * kQ4MaxCells);
   int32_t* cold_q = reinterpret_cast<int32_t*>(sm + 3 * kQ4MaxCells);
-  for (int i = threadIdx.x; i < cap; i += kQ4Threads) {
-    hot[i] = 0u;
-    c3[i] = 0u;
-    cold_g[i] = 0;
-    cold_q[i] = 0;
+  // cold sums exist only when this CTA's range needs more than one chunk
+  const bool folds = (r1 - r0) > kQ4Chunk;
+  {
+    uint4* h4 = reinterpret_cast<uint4*>(hot);
+    uint4* c4 = reinterpret_cast<uint4*>(c3);
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = threadIdx.x; i < (cap + 3) / 4; i += kQ4Threads) {
+      h4[i] = z;
+      c4[i] = z;
+    }
+    if (folds) {
+      uint4* g4 = reinterpret_cast<uint4*>(cold_g);
+      uint4* q4 = reinterpret_cast<uint4*>(cold_q);
+      for (int i = threadIdx.x; i < (cap + 3) / 4; i += kQ4Threads) {
+        g4[i] = z;
+        q4[i] = z;
+      }
+    }
   }
   // Features the parent could not split are neither built nor scanned
   // (learner.rs:2003-2020 build mask).
@@ -359,8 +382,8 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
     if (fl >= nf || bin >= s_nb[fl]) continue;
     const int32_t v = (int32_t)hot[s];
     const int32_t lo = (int32_t)(int16_t)(v & 0xffff);
-    const long long g = (long long)cold_g[s] + lo;
-    const long long qsum = (long long)cold_q[s] + ((v - lo) >> 16);
+    const long long g = (folds ? (long long)cold_g[s] : 0ll) + lo;
+    const long long qsum = (folds ? (long long)cold_q[s] : 0ll) + ((v - lo) >> 16);
     const long long n3 = (long long)c3[s];
     const long long h = (qsum - 3 * n3) | (n3 << 32);
     const size_t gb = (size_t)(s_boff[fl] + bin);
@@ -1064,6 +1087,7 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
   __shared__ double s_hist[2][2 * kMaxBins];
   __shared__ ScanScratch s_scan[4];
   __shared__ ScanCand s_cand[4];
+  __shared__ int32_t s_acc[8][2][kMaxBins];  // in-block build: 8 sub-histograms of (G, Q)
   __shared__ bool s_last;
   GrowCtrl* c = d.ctrl;
   const int f = blockIdx.x;
@@ -1087,7 +1111,70 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
       double parent = 0.0;
       if (mine && Lg >= 0) parent = pl[tid];
       double v = 0.0;
-      if (mine && buildable) {
+      const int32_t cnt_s = d.leaf_count[S];
+      if (buildable && build_in_fixscan(d, cnt_s)) {
+        // Feature-parallel build of this feature for the smaller child: every warp takes
+        // a contiguous run of the child's rows; warp w adds into sub-histogram w % 8, so
+        // a sub-histogram sees at most 65536 / 8 rows and its 16-bit fields cannot wrap.
+        // G = sum qg; Q = sum qh | (rows with qh == 3) << 16.
+        int32_t* acc = &s_acc[0][0][0];
+        for (int i = tid; i < 8 * 2 * kMaxBins; i += blockDim.x) acc[i] = 0;
+        __syncthreads();
+        const int w = tid >> 5, lane = tid & 31;
+        int32_t* sg = s_acc[w & 7][0];
+        int32_t* sq = s_acc[w & 7][1];
+        const int32_t beg = d.leaf_begin[S];
+        const int32_t lbuf = d.leaf_buf[S];
+        const uint32_t* lidx = lbuf == 1 ? d.idx1 : d.idx0;
+        const uint16_t* gq = reinterpret_cast<const uint16_t*>(d.gh);
+        const uint8_t* fb = d.bins + f;
+        const int32_t per = (cnt_s + 31) / 32;
+        const int32_t r0 = w * per, r1 = min(cnt_s, r0 + per);
+        for (int32_t k0 = r0; k0 < r1; k0 += 128) {
+          uint32_t rows[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int32_t k = k0 + u * 32 + lane;
+            rows[u] = k < r1 ? (lbuf == 2 ? (uint32_t)(beg + k) : lidx[beg + k]) : 0xffffffffu;
+          }
+          uint32_t bin[4];
+          uint16_t q[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (rows[u] != 0xffffffffu) {
+              bin[u] = fb[(size_t)rows[u] * d.stride];
+              q[u] = gq[rows[u]];
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (rows[u] == 0xffffffffu) continue;
+            const int qg = (int)(int8_t)(q[u] & 0xff);
+            const int qh = (int)(int8_t)(q[u] >> 8);
+            atomicAdd(&sg[bin[u]], qg);
+            atomicAdd(&sq[bin[u]], qh + (qh == 3 ? (1 << 16) : 0));
+          }
+        }
+        __syncthreads();
+        if (mine) {
+          const int b = tid >> 1;
+          if ((tid & 1) == 0) {
+            long long gs = 0;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) gs += s_acc[u][0][b];
+            v = decode_g(p, gs);
+          } else {
+            long long qs = 0, c3 = 0;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int32_t x = s_acc[u][1][b];
+              qs += x & 0xffff;
+              c3 += x >> 16;
+            }
+            v = decode_h(p, (qs - 3 * c3) | (c3 << 32));
+          }
+        }
+      } else if (mine && buildable) {
         const long long rv = raw[tid];
         v = (tid & 1) ? decode_h(p, rv) : decode_g(p, rv);
         raw[tid] = 0;
