@@ -216,6 +216,38 @@ int lgbm_b200_data_partition(const uint32_t* bins, int64_t n, uint32_t num_bin, 
                              uint32_t max_bin, uint32_t threshold, uint32_t most_freq_bin,
                              uint32_t* order_out, int64_t* split_point_out);
 
+/* Allocation-free variant of lgbm_b200_data_partition. No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc when they
+ * partition rows. Examples are a host engine whose device memory belongs to its
+ * own pool allocator, which has reserved the HBM up front so that a cudaMalloc
+ * can fail or fragment its reservation, and a latency-bound loop that cannot
+ * pay for cudaMalloc/cudaFree, which synchronise the whole device.
+ *
+ * Same argument meaning and result as lgbm_b200_data_partition, except that
+ * `bins` (n bytes, one bin per row), `order_out` (n words) and
+ * `split_point_out` (one int64) are DEVICE pointers on the current device, and
+ * the work is enqueued on `stream` (a cudaStream_t; NULL is the legacy default
+ * stream) without waiting for it: the outputs are ready once the stream
+ * reaches that point. Bins are not range-checked on this path; a bin outside
+ * [min_bin, max_bin] goes where the most frequent bin goes.
+ *
+ * Scratch: the partition's look-back status words (one per 2048-row tile), two
+ * counters and the routing descriptor live in a fixed array compiled into the
+ * library, one per device, 256 B + 8 B per tile = 262,400 B at the limit. The
+ * function allocates nothing. n above LGBM_B200_NOALLOC_MAX_ROWS fails with
+ * LGBM_B200_CAPABILITY_UNAVAILABLE and enqueues no work. Each call first
+ * clears, on `stream`, the status words and counters it uses; they must start
+ * at zero. Every call on a device shares the one array, so calls that overlap
+ * on the GPU (different streams, or different host threads) race and return
+ * wrong results: serialise them. The first call on each device looks the
+ * array up with cudaGetSymbolAddress (with that device current); make that
+ * first call before any stream capture. */
+#define LGBM_B200_NOALLOC_MAX_ROWS 67108864 /* 2^26 rows */
+int lgbm_b200_data_partition_noalloc(const uint8_t* bins, int64_t n, uint32_t num_bin,
+                                     uint32_t min_bin, uint32_t max_bin, uint32_t threshold,
+                                     uint32_t most_freq_bin, uint32_t* order_out,
+                                     int64_t* split_point_out, void* stream);
+
 /* Backend::subtract_histograms (crates/lgbm-compute/src/lib.rs:1314-1319). */
 int lgbm_b200_subtract_histograms(const double* parent, const double* child, int64_t len,
                                   double* out);

@@ -104,6 +104,8 @@ _SIGS = {
     "lgbm_b200_find_best_splits_batched": ([_P, _i64, _P, _i32, _P, _f64, _f64, _i32, _P],
                                            ctypes.c_int),
     "lgbm_b200_data_partition": ([_P, _i64, _u32, _u32, _u32, _u32, _u32, _P, _P], ctypes.c_int),
+    "lgbm_b200_data_partition_noalloc": ([_P, _i64, _u32, _u32, _u32, _u32, _u32, _P, _P, _P],
+                                         ctypes.c_int),
     "lgbm_b200_subtract_histograms": ([_P, _P, _i64, _P], ctypes.c_int),
     "lgbm_b200_dataset_create": ([_i32, _P, _i32, _i64, _i32, _P, _P], ctypes.c_int),
     "lgbm_b200_dataset_destroy": ([_P], ctypes.c_int),

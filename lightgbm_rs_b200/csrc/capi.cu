@@ -7,6 +7,7 @@
 #include <cstring>
 #include <limits>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -515,6 +516,77 @@ int lgbm_b200_booster::ensure_capacity(int32_t need) {
 }
 
 // ----------------------------------------------------------------------------------
+// Allocation-free row partition (lgbm_b200_data_partition_noalloc)
+//
+// Some callers cannot call cudaMalloc when they partition rows: a host engine whose
+// device memory belongs to its own pool allocator (the pool has reserved the HBM up
+// front, so a cudaMalloc can fail or fragment it), or a latency-bound loop that cannot
+// pay for cudaMalloc/cudaFree, which synchronise the whole device. For them the
+// partition's only scratch -- one look-back status word per 2048-row tile, the two
+// counters (left total, tile ticket) and the routing descriptor -- lives in the fixed
+// array below instead of a cudaMalloc'd buffer. Layout, in 8-byte words:
+//   word 0        int32 left total | uint32 tile ticket
+//   words 8..     DevFeature routing descriptor
+//   words 32..    status words, one per tile, at most LGBM_B200_NOALLOC_MAX_ROWS / 2048
+// Every call on a device shares this one array: calls that overlap on the GPU race.
+// ----------------------------------------------------------------------------------
+
+namespace {
+
+constexpr int64_t kNoAllocMaxRows = LGBM_B200_NOALLOC_MAX_ROWS;
+constexpr int64_t kNoAllocMaxTiles = kNoAllocMaxRows / kPartitionTileRows;
+constexpr int kNoAllocHeaderWords = 32;
+constexpr int kNoAllocFeatureWord = 8;
+static_assert(kNoAllocMaxRows % kPartitionTileRows == 0, "limit is whole tiles");
+static_assert(kNoAllocMaxRows <= (int64_t)INT32_MAX, "partition counts are int32");
+static_assert(sizeof(DevFeature) <= 8 * (kNoAllocHeaderWords - kNoAllocFeatureWord),
+              "descriptor fits the header");
+
+static __device__ __align__(256) unsigned long long
+    g_noalloc_partition_scratch[kNoAllocHeaderWords + kNoAllocMaxTiles];
+
+// Per-device result of the one-time symbol lookup.
+struct NoAllocDevice {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  unsigned long long* scratch = nullptr;
+  int sms = 0;
+};
+constexpr int kNoAllocMaxDevices = 64;
+NoAllocDevice g_noalloc_devices[kNoAllocMaxDevices];
+
+// Clears what the partition kernel needs at zero (status words of the tiles this call
+// uses, both counters) and stores the routing descriptor.
+__global__ void k_noalloc_partition_setup(unsigned long long* scratch, int64_t tiles,
+                                          DevFeature f) {
+  unsigned long long* status = scratch + kNoAllocHeaderWords;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < tiles;
+       i += (int64_t)gridDim.x * blockDim.x)
+    status[i] = 0ull;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    scratch[0] = 0ull;
+    *reinterpret_cast<DevFeature*>(scratch + kNoAllocFeatureWord) = f;
+  }
+}
+
+// The partition kernel writes right-going rows from the back of the range; this puts
+// them in ascending order, as the host entry point does, and publishes the split point.
+__global__ void k_noalloc_partition_finish(const unsigned long long* scratch, uint32_t* order,
+                                           int64_t n, int64_t* split_point) {
+  const int64_t left = (int64_t)*reinterpret_cast<const int32_t*>(scratch);
+  const int64_t half = (n - left) / 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < half;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t a = order[left + i];
+    order[left + i] = order[n - 1 - i];
+    order[n - 1 - i] = a;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *split_point = left;
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------------------------
 // C ABI
 // ----------------------------------------------------------------------------------
 
@@ -737,6 +809,67 @@ int lgbm_b200_data_partition(const uint32_t* bins, int64_t n, uint32_t num_bin, 
   // the device writes the right rows from the back; the reference returns them ascending
   std::reverse(order_out + cnt[0], order_out + n);
   *split_point_out = cnt[0];
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_data_partition_noalloc(const uint8_t* bins, int64_t n, uint32_t num_bin,
+                                     uint32_t min_bin, uint32_t max_bin, uint32_t threshold,
+                                     uint32_t most_freq_bin, uint32_t* order_out,
+                                     int64_t* split_point_out, void* stream) {
+  if (!split_point_out || n < 0 || (n > 0 && (!bins || !order_out)))
+    return fail(LGBM_B200_INVALID_ARGUMENT, "data_partition_noalloc: null argument");
+  if (num_bin == 0) return fail(LGBM_B200_RUNTIME, "data_partition_noalloc: num_bin must be > 0");
+  if (threshold >= num_bin)
+    return fail(LGBM_B200_RUNTIME, "data_partition_noalloc: threshold %u >= num_bin %u",
+                threshold, num_bin);
+  if (num_bin > (uint32_t)kMaxBins)
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "data_partition_noalloc: num_bin %u > 256",
+                num_bin);
+  if (n > kNoAllocMaxRows)
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE,
+                "data_partition_noalloc: n = %lld rows exceeds the fixed scratch limit "
+                "LGBM_B200_NOALLOC_MAX_ROWS = %lld; use lgbm_b200_data_partition",
+                (long long)n, (long long)kNoAllocMaxRows);
+  if (!have_device()) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "no CUDA device");
+  int dev = -1;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "data_partition_noalloc: device %d >= %d",
+                dev, kNoAllocMaxDevices);
+  NoAllocDevice& nd = g_noalloc_devices[dev];
+  std::call_once(nd.once, [&nd, dev] {
+    nd.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&nd.scratch),
+                                  g_noalloc_partition_scratch);
+    if (nd.err == cudaSuccess)
+      nd.err = cudaDeviceGetAttribute(&nd.sms, cudaDevAttrMultiProcessorCount, dev);
+  });
+  if (nd.err != cudaSuccess || !nd.scratch)
+    return fail(LGBM_B200_RUNTIME,
+                "data_partition_noalloc: scratch set-up on device %d failed: %s", dev,
+                cudaGetErrorString(nd.err));
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned long long* scratch = nd.scratch;
+  const int sms = std::max(1, nd.sms);
+  DevFeature f = make_feature((int32_t)num_bin, 0, (int32_t)most_freq_bin, 0);
+  f.route_min = (int32_t)min_bin;
+  f.route_max = (int32_t)max_bin;
+  const int64_t tiles = (n + kPartitionTileRows - 1) / kPartitionTileRows;
+  const int setup_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((tiles + 255) / 256, sms));
+  k_noalloc_partition_setup<<<setup_blocks, 256, 0, st>>>(scratch, tiles, f);
+  CUDA_TRY(cudaGetLastError());
+  if (n > 0) {
+    int32_t* counters = reinterpret_cast<int32_t*>(scratch);
+    launch_partition_rows(bins, 1, 0,
+                          reinterpret_cast<const DevFeature*>(scratch + kNoAllocFeatureWord),
+                          threshold, 0, n, order_out, scratch + kNoAllocHeaderWords, counters,
+                          reinterpret_cast<uint32_t*>(counters + 1), st);
+    CUDA_TRY(cudaGetLastError());
+  }
+  const int finish_blocks =
+      (int)std::max<int64_t>(1, std::min<int64_t>((n / 2 + 255) / 256, 2 * (int64_t)sms));
+  k_noalloc_partition_finish<<<finish_blocks, 256, 0, st>>>(scratch, order_out, n,
+                                                            split_point_out);
+  CUDA_TRY(cudaGetLastError());
   return LGBM_B200_OK;
 }
 

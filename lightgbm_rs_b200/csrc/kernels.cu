@@ -24,6 +24,7 @@ constexpr int kScanThreads = 1024;
 constexpr int kPartThreads = 256;
 constexpr int kPartItems = 8;
 constexpr int kPartTile = kPartThreads * kPartItems;
+static_assert(kPartTile == kPartitionTileRows, "partition tile size is part of the host contract");
 constexpr long long kSpinLimit = 1ll << 22;
 
 __device__ __forceinline__ bool leaf_buildable(const DevLeafSplits& l) {

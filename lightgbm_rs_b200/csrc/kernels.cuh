@@ -25,6 +25,9 @@ struct DevFeatureGroup {
 // two CTAs per SM.
 constexpr int kQ4MaxCells = 7168;
 
+// Rows per tile of the row-partition kernel (one look-back status word per tile).
+constexpr int kPartitionTileRows = 2048;
+
 // Everything the per-split kernels touch, passed by value.
 struct GrowDev {
   GrowCtrl* ctrl;
