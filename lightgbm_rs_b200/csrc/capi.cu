@@ -190,7 +190,8 @@ struct lgbm_b200_learner {
   std::vector<DevFeatureGroup> groups;
   DevBuf<DevFeatureGroup> d_groups;
   DevBuf<GrowCtrl> ctrl;
-  DevBuf<int32_t> leaf_i32;  // leaf_begin, leaf_count, leaf_buf, slot_of_leaf, best_feature
+  DevBuf<int32_t> leaf_i32;  // leaf_begin, leaf_count, leaf_buf, slot_of_leaf, best_feature,
+                             // leaf_count_g
   DevBuf<DevLeafSplits> ls;
   DevBuf<DevSplitInfo> best;
   DevBuf<uint8_t> splittable;
@@ -203,6 +204,7 @@ struct lgbm_b200_learner {
   DevBuf<unsigned long long> part_status;
   DevBuf<double> pool;
   DevBuf<long long> raw;
+  DevBuf<long long> rawpool;
   DevBuf<DevSplitInfo> scan_out;
   DevBuf<uint8_t> scan_ok;
   // gradients owned by a standalone learner (the booster owns its own)
@@ -308,7 +310,7 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   CUDA_TRY(ctrl.alloc(1));
   CUDA_TRY(cudaMemset(ctrl.p, 0, sizeof(GrowCtrl)));
-  CUDA_TRY(leaf_i32.alloc((size_t)5 * L));
+  CUDA_TRY(leaf_i32.alloc((size_t)6 * L));
   CUDA_TRY(ls.alloc(L));
   CUDA_TRY(best.alloc(L));
   CUDA_TRY(splittable.alloc((size_t)L * ds->num_features));
@@ -320,8 +322,9 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   CUDA_TRY(idx.alloc((size_t)2 * N));
   CUDA_TRY(part_status.alloc(max_tiles));
   CUDA_TRY(pool.alloc((size_t)L * slot_len));
-  CUDA_TRY(raw.alloc((size_t)slot_len));
-  CUDA_TRY(cudaMemset(raw.p, 0, (size_t)slot_len * sizeof(long long)));
+  CUDA_TRY(raw.alloc((size_t)slot_len + 2));
+  CUDA_TRY(cudaMemset(raw.p, 0, ((size_t)slot_len + 2) * sizeof(long long)));
+  CUDA_TRY(rawpool.alloc((size_t)L * slot_len));
   CUDA_TRY(scan_out.alloc((size_t)2 * ds->num_features));
   CUDA_TRY(scan_ok.alloc(2));
   d = GrowDev{};
@@ -340,6 +343,7 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.leaf_buf = leaf_i32.p + 2 * L;
   d.slot_of_leaf = leaf_i32.p + 3 * L;
   d.best_feature = leaf_i32.p + 4 * L;
+  d.leaf_count_g = leaf_i32.p + 5 * L;
   d.ls = ls.p;
   d.best = best.p;
   d.splittable = splittable.p;
@@ -362,6 +366,9 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.max_tiles = max_tiles;
   d.pool = pool.p;
   d.raw = raw.p;
+  d.rawpool = rawpool.p;
+  d.raw_len = slot_len;
+  d.n_global = N;
   d.scan_out = scan_out.p;
   d.scan_ok = scan_ok.p;
   return LGBM_B200_OK;
@@ -374,6 +381,7 @@ void lgbm_b200_learner::bind(const void* gh_ptr, const DevGhParams* ghp_ptr,
   d.stopped = stopped;
   d.gh_mode = gh_mode;
   d.q4_shift = q4_shift;
+  d.fused = fused_partition_supported(gh_mode, (int)groups.size(), q4_shift, q4_nch) ? 1 : 0;
   d.q4_nch = q4_nch;
   d.groups = d_groups.p;
   d.num_groups = (int32_t)groups.size();

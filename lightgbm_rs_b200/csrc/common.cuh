@@ -126,8 +126,9 @@ struct GrowCtrl {
   uint32_t error;
   int32_t num_splits;
   int32_t num_builds;      // histogram builds in this tree
-  int32_t _pad2;
+  int32_t build_left;      // the pending split's left rows are accumulated (else right)
   long long rows_built;    // rows streamed by those builds
+  long long rows_parted;   // parent rows streamed by the partitions
   DevSplitInfo split;
 };
 

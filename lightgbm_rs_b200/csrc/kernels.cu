@@ -31,13 +31,55 @@ __device__ __forceinline__ bool leaf_buildable(const DevLeafSplits& l) {
   return l.sum_h > 0.0 && l.num_data > 0;  // learner.rs:2477-2481
 }
 
-// Small children (rows x features under a budget) are built feature-parallel inside
-// k_fixscan, one CTA per feature, instead of by the row-parallel build kernel.
-constexpr int64_t kInBlockBudget = 1 << 16;
-constexpr int32_t kInBlockMaxRows = 65536;
-__device__ __forceinline__ bool build_in_fixscan(const GrowDev& d, int32_t count) {
-  return d.gh_mode == GH_QPACK && count <= kInBlockMaxRows &&
-         (int64_t)count * d.F <= kInBlockBudget;
+// What a histogram build accumulates into d.raw. Phase 0: the root (all rows of this
+// device, identity order, every feature). Phase 1: one child of the split just
+// partitioned -- its left rows [begin, begin + left) or right rows [begin + left,
+// begin + count) in the partition's destination buffer, features the parent could
+// split only. Phase 2: nothing (last split of the tree); the partition's left count
+// is still published.
+struct BuildTarget {
+  int32_t begin, count, buf, mask_leaf;
+  bool ok;
+};
+
+__device__ __forceinline__ BuildTarget build_target(const GrowDev& d, int phase) {
+  const GrowCtrl* c = d.ctrl;
+  BuildTarget t{0, 0, 2, -1, false};
+  if (c->done) return t;
+  if (phase == 0) {
+    t.count = (int32_t)d.N;
+    t.ok = t.count > 0;
+    return t;
+  }
+  if (phase != 1 || !c->pending) return t;
+  const int32_t leaf = c->split_leaf;
+  const int32_t beg = d.leaf_begin[leaf];
+  const int32_t cnt = d.leaf_count[leaf];
+  const int32_t lc = c->part_left_total;
+  t.buf = d.leaf_buf[leaf] == 1 ? 0 : 1;
+  if (c->build_left) {
+    t.begin = beg;
+    t.count = lc;
+  } else {
+    t.begin = beg + lc;
+    t.count = cnt - lc;
+  }
+  t.mask_leaf = leaf;
+  t.ok = t.count > 0;
+  return t;
+}
+
+// Build bookkeeping, once per build launch (block (0,0), thread 0): the non-fused
+// partition publishes its left count here for the next split's control step.
+__device__ __forceinline__ void build_account(const GrowDev& d, int phase, const BuildTarget& t) {
+  if (blockIdx.x != 0 || blockIdx.y != 0 || threadIdx.x != 0) return;
+  GrowCtrl* c = d.ctrl;
+  if (phase != 0 && !d.fused && !c->done && c->pending)
+    d.raw[d.raw_len] = (long long)c->part_left_total;
+  if (t.ok) {
+    c->num_builds += 1;
+    c->rows_built += t.count;
+  }
 }
 
 // Decoding of the raw integer accumulators into f64 histogram cells. For the
@@ -149,19 +191,17 @@ __device__ __forceinline__ void build_block(const uint8_t* __restrict__ bins, in
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d) {
+__global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d, int phase) {
   extern __shared__ unsigned long long acc[];
   __shared__ int32_t s_binoff[128];
   __shared__ uint8_t s_used[128];
   __shared__ long long s_lut[MODE == GH_QLUT ? 512 : 1];
-  GrowCtrl* c = d.ctrl;
-  if (c->done || !c->do_find) return;
-  const int32_t leaf = c->smaller_leaf;
-  const DevLeafSplits ls = d.ls[leaf];
-  if (!leaf_buildable(ls)) return;
-  const int32_t begin = d.leaf_begin[leaf];
-  const int32_t count = d.leaf_count[leaf];
-  const int32_t buf = d.leaf_buf[leaf];
+  const BuildTarget t = build_target(d, phase);
+  build_account(d, phase, t);
+  if (!t.ok) return;
+  const int32_t begin = t.begin;
+  const int32_t count = t.count;
+  const int32_t buf = t.buf;
   const DevFeatureGroup grp = d.groups[blockIdx.y];
   const int nf = grp.f_end - grp.f_begin;
   int nb_active = (count + kMinRowsPerBlock - 1) / kMinRowsPerBlock;
@@ -184,8 +224,8 @@ __global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d) {
   // Features the parent could not split are neither built nor scanned
   // (learner.rs:2003-2020 build mask).
   {
-    const uint8_t* ps = d.splittable + (size_t)c->left_leaf * d.F;
-    const bool sub = c->use_subtract != 0;
+    const bool sub = t.mask_leaf >= 0;
+    const uint8_t* ps = d.splittable + (size_t)(sub ? t.mask_leaf : 0) * d.F;
     for (int fl = threadIdx.x; fl < nf; fl += blockDim.x)
       s_used[fl] = sub ? ps[grp.f_begin + fl] : (uint8_t)1;
   }
@@ -236,11 +276,8 @@ constexpr int kQ4Chunk = 8191;  // |sum qg| <= 2*8191 and sum qh <= 4*8191 fit 1
 // MASKED: per-feature build mask on every chunk. Otherwise every feature of the group
 // is used and only the last chunk (features nf-16(NCH-1) .. 15 absent) is masked.
 template <int SHIFT, int NCH, bool MASKED>
-__device__ __forceinline__ void q4_row(const uint4* __restrict__ rp, int32_t pv, bool is3,
-                                       uint32_t* hot, const uint32_t* mask, uint32_t tail) {
-  uint4 w[NCH];
-#pragma unroll
-  for (int ch = 0; ch < NCH; ++ch) w[ch] = rp[ch];
+__device__ __forceinline__ void q4_row_regs(const uint4 (&w)[NCH], int32_t pv, bool is3,
+                                            uint32_t* hot, const uint32_t* mask, uint32_t tail) {
 #pragma unroll
   for (int ch = 0; ch < NCH; ++ch) {
     const uint32_t words[4] = {w[ch].x, w[ch].y, w[ch].z, w[ch].w};
@@ -257,21 +294,54 @@ __device__ __forceinline__ void q4_row(const uint4* __restrict__ rp, int32_t pv,
   }
 }
 
+template <int SHIFT, int NCH, bool MASKED>
+__device__ __forceinline__ void q4_row(const uint4* __restrict__ rp, int32_t pv, bool is3,
+                                       uint32_t* hot, const uint32_t* mask, uint32_t tail) {
+  uint4 w[NCH];
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch) w[ch] = rp[ch];
+  q4_row_regs<SHIFT, NCH, MASKED>(w, pv, is3, hot, mask, tail);
+}
+
+// Build mask of one 128-feature group as four 32-bit words, and whether every feature of
+// the group is used (then only the last 16-feature chunk needs a mask: `tail`).
+struct Q4Mask {
+  uint32_t w[4];
+  uint32_t tail;
+  bool full;
+};
+
+template <int NCH>
+__device__ __forceinline__ Q4Mask q4_mask(const uint32_t* s_mask, int nf) {
+  Q4Mask m;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m.w[i] = s_mask[i];
+  const int ntail = nf - 16 * (NCH - 1);  // features in the last chunk, 1..16
+  // a short last group (ntail <= 0) never takes the unmasked path: its earlier chunks
+  // are incomplete, so `full` below is false
+  m.tail = ntail >= 16 ? 0xffffu : (ntail <= 0 ? 0u : ((1u << ntail) - 1u));
+  m.full = true;
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch) {
+    const uint32_t want = ch == NCH - 1 ? m.tail : 0xffffu;
+    const uint32_t m16 = (m.w[ch >> 1] >> ((ch & 1) * 16)) & 0xffffu;
+    if (m16 != want) m.full = false;
+  }
+  return m;
+}
+
 template <int SHIFT, int NCH>
-__global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
+__global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase) {
   extern __shared__ uint32_t sm[];
   __shared__ int32_t s_nb[128];
   __shared__ int32_t s_boff[128];
   __shared__ uint32_t s_mask[4];
-  GrowCtrl* c = d.ctrl;
-  if (c->done || !c->do_find) return;
-  const int32_t leaf = c->smaller_leaf;
-  const DevLeafSplits ls = d.ls[leaf];
-  if (!leaf_buildable(ls)) return;
-  const int32_t begin = d.leaf_begin[leaf];
-  const int32_t count = d.leaf_count[leaf];
-  const int32_t buf = d.leaf_buf[leaf];
-  if (build_in_fixscan(d, count)) return;
+  const BuildTarget t = build_target(d, phase);
+  build_account(d, phase, t);
+  if (!t.ok) return;
+  const int32_t begin = t.begin;
+  const int32_t count = t.count;
+  const int32_t buf = t.buf;
   const DevFeatureGroup grp = d.groups[blockIdx.y];
   const int nf = grp.f_end - grp.f_begin;
   const int cap = nf << SHIFT;  // <= kQ4MaxCells (host group planning)
@@ -309,8 +379,8 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
   }
   // Features the parent could not split are neither built nor scanned
   // (learner.rs:2003-2020 build mask).
-  const bool sub = c->use_subtract != 0;
-  const uint8_t* ps = d.splittable + (size_t)c->left_leaf * d.F + grp.f_begin;
+  const bool sub = t.mask_leaf >= 0;
+  const uint8_t* ps = d.splittable + (size_t)(sub ? t.mask_leaf : 0) * d.F + grp.f_begin;
   for (int fl = threadIdx.x; fl < nf; fl += blockDim.x) {
     const DevFeature ft = d.feat[grp.f_begin + fl];
     s_nb[fl] = ft.num_bin;
@@ -325,18 +395,10 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
     s_mask[threadIdx.x] = m;
   }
   __syncthreads();
-  uint32_t mask[4] = {s_mask[0], s_mask[1], s_mask[2], s_mask[3]};
-  const int ntail = nf - 16 * (NCH - 1);  // features in the last chunk, 1..16
-  // a short last group (ntail <= 0) never takes the unmasked path: its earlier chunks
-  // are incomplete, so `full` below is false
-  const uint32_t tail = ntail >= 16 ? 0xffffu : (ntail <= 0 ? 0u : ((1u << ntail) - 1u));
-  bool full = true;
-#pragma unroll
-  for (int ch = 0; ch < NCH; ++ch) {
-    const uint32_t want = ch == NCH - 1 ? tail : 0xffffu;
-    const uint32_t m16 = (mask[ch >> 1] >> ((ch & 1) * 16)) & 0xffffu;
-    if (m16 != want) full = false;
-  }
+  const Q4Mask qm = q4_mask<NCH>(s_mask, nf);
+  const uint32_t* mask = qm.w;
+  const uint32_t tail = qm.tail;
+  const bool full = qm.full;
   const uint32_t* idx = buf == 1 ? d.idx1 : d.idx0;
   const uint16_t* gq = reinterpret_cast<const uint16_t*>(d.gh);
   const bool identity = buf == 2;
@@ -395,7 +457,7 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d) {
 }
 
 // (SHIFT, NCH) instantiations with (16 * (NCH - 1) + 1) << SHIFT <= kQ4MaxCells.
-using Q4Kernel = void (*)(GrowDev);
+using Q4Kernel = void (*)(GrowDev, int);
 __host__ Q4Kernel q4_kernel(int shift, int nch) {
 #define Q4_CASE(S, N) \
   if (shift == S && nch == N) return k_build_q4<S, N>;
@@ -717,6 +779,7 @@ __global__ void k_tree_init(GrowDev d) {
   for (int l = gtid; l < d.L; l += gsz) {
     d.leaf_begin[l] = 0;
     d.leaf_count[l] = 0;
+    d.leaf_count_g[l] = 0;
     d.leaf_buf[l] = 0;
     d.slot_of_leaf[l] = -1;
     d.best[l] = d_split_none();
@@ -750,12 +813,13 @@ __global__ void k_tree_init(GrowDev d) {
     c->right_leaf = -1;
     c->next_slot = 0;
     d.leaf_count[0] = (int32_t)d.N;
+    d.leaf_count_g[0] = (int32_t)d.n_global;
     d.leaf_buf[0] = 2;
     const DevGhParams& p = *d.ghp;
     // LeafSplits::init over all rows (leaf_splits.rs:75-92): integer root sums
     // decoded exactly like histogram cells.
     DevLeafSplits r;
-    r.num_data = (int32_t)d.N;
+    r.num_data = (int32_t)d.n_global;
     r._pad = 0;
     r.sum_g = decode_g(p, p.root_g);
     r.sum_h = decode_h(p, p.root_h);
@@ -763,7 +827,7 @@ __global__ void k_tree_init(GrowDev d) {
     r.weight = d_leaf_output_full(d.gain, false, r.sum_g, r.sum_h, 0, 0.0);
     d.ls[0] = r;
     d.t_leaf_value[0] = r.weight;
-    d.t_leaf_count[0] = (int32_t)d.N;
+    d.t_leaf_count[0] = (int32_t)d.n_global;
     d.t_leaf_parent[0] = -1;
     if (stopped) c->done = 1;
     if (!(r.sum_h > 0.0)) {
@@ -773,87 +837,104 @@ __global__ void k_tree_init(GrowDev d) {
   }
 }
 
-// One thread; all per-leaf loads are issued up front so their latencies overlap
-// (this kernel sits on the critical path of every split).
-__global__ void k_prepare(GrowDev d, int s) {
-  if (threadIdx.x != 0) return;
-  GrowCtrl* cp = d.ctrl;
-  GrowCtrl c = *cp;
+// ------------------------------------------------------------------------------------
+// Per-split control step: apply the split chosen at step s-1 (learner.rs:3895-4092),
+// BeforeFindBestSplit gates (learner.rs:1808-1839), smaller child and pool slots
+// (learner.rs:1882-1916). It runs in thread 0 of every k_fixscan CTA from the same
+// inputs (prep_compute only reads), and the kernel's last CTA writes the result
+// (prep_commit), after every CTA has read what it needs. Leaf counts come in two kinds:
+// rows on this device (ranges of the index buffers) and rows on all devices (tree
+// counts, gates, smaller child, LeafSplits); with one device they are equal.
+// ------------------------------------------------------------------------------------
+
+struct Prep {
+  GrowCtrl c;  // control block after this step
+  int32_t applied;
+  int32_t leaf, nr, node, parent, parent_is_right;
+  int32_t lc, rc, lcg, rcg, dst, beg, depth;
+  int32_t feature;
+  int8_t dt;
+  float split_gain;
+  double old_value;
+  DevLeafSplits lsL, lsR;  // children (applied)
+  int32_t live;            // the two leaves below are scanned
+  int32_t kill0, kill1;    // leaves whose best split is cleared by the gates (-1: none)
+  int32_t slot_leaf0, slot_val0, slot_leaf1, slot_val1;  // slot_of_leaf writes (-1: none)
+  int32_t S, Lg, sslot, lslot, use_sub, mask_leaf, smaller_is_left;
+  DevLeafSplits lsS, lsLg;
+};
+
+__device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
+  GrowCtrl c = *d.ctrl;
+  P.applied = 0;
+  P.live = 0;
+  P.kill0 = P.kill1 = -1;
+  P.slot_leaf0 = P.slot_leaf1 = -1;
+  P.slot_val0 = P.slot_val1 = -1;
+  P.S = P.Lg = -1;
+  P.sslot = P.lslot = -1;
+  P.use_sub = 0;
+  P.mask_leaf = -1;
+  P.smaller_is_left = 1;
   int32_t left = c.left_leaf, right = c.right_leaf;
   int32_t cnt_left = 0, cnt_right = 0, depth_left = 0, slot_left = -1;
   bool known = false;
   DevLeafSplits lsL{}, lsR{};
   if (c.pending) {
-    // ---- apply the split chosen at step s-1 (learner.rs:3895-4092) ----
     const int32_t leaf = c.split_leaf;
     const int32_t nr = c.num_leaves;
     const int32_t f = c.split_feature;
     const DevSplitInfo b = c.split;
     const int32_t cnt = d.leaf_count[leaf];
+    const int32_t cntg = d.leaf_count_g[leaf];
     const int32_t beg = d.leaf_begin[leaf];
     const int32_t src = d.leaf_buf[leaf];
     const int32_t parent = d.t_leaf_parent[leaf];
     const double old_value = d.t_leaf_value[leaf];
     const int32_t depth = d.t_leaf_depth[leaf];
     const int32_t mt = d.feat[f].missing_type;
+    const long long lcg_raw = d.raw[d.raw_len];
     slot_left = d.slot_of_leaf[leaf];
     const int32_t parent_right = parent >= 0 ? d.t_right[parent] : 0;
     const int32_t lc = c.part_left_total;
-    const int32_t rc = cnt - lc;
-    const int32_t dst = src == 1 ? 0 : 1;
-    d.leaf_begin[nr] = beg + lc;
-    d.leaf_count[leaf] = lc;
-    d.leaf_count[nr] = rc;
-    d.leaf_buf[leaf] = dst;
-    d.leaf_buf[nr] = dst;
-    // Tree::split (lgbm-model/src/tree.rs:614-690)
-    const int32_t node = nr - 1;
-    if (parent >= 0) {
-      if (parent_right == ~leaf)
-        d.t_right[parent] = node;
-      else
-        d.t_left[parent] = node;
-    }
-    d.t_split_feature[node] = f;
-    d.t_split_gain[node] = (float)(b.gain + d.gain.min_gain_to_split);
-    d.t_threshold[node] = b.threshold;
-    d.t_internal_value[node] = old_value;
-    d.t_internal_count[node] = lc + rc;
-    d.t_left[node] = ~leaf;
-    d.t_right[node] = ~nr;
+    const int32_t lcg = (int32_t)lcg_raw;
+    P.applied = 1;
+    P.leaf = leaf;
+    P.nr = nr;
+    P.node = nr - 1;
+    P.parent = parent;
+    P.parent_is_right = parent >= 0 && parent_right == ~leaf;
+    P.lc = lc;
+    P.rc = cnt - lc;
+    P.lcg = lcg;
+    P.rcg = cntg - lcg;
+    P.dst = src == 1 ? 0 : 1;
+    P.beg = beg;
+    P.depth = depth;
+    P.feature = f;
     int8_t dt = 0;
     if (b.default_left) dt |= 2;
     dt |= (int8_t)((mt & 3) << 2);
-    d.t_decision[node] = dt;
-    d.t_leaf_value[leaf] = b.left_output;
-    d.t_leaf_weight[leaf] = b.left_sum_hessian;
-    d.t_leaf_count[leaf] = lc;
-    d.t_leaf_value[nr] = b.right_output;
-    d.t_leaf_weight[nr] = b.right_sum_hessian;
-    d.t_leaf_count[nr] = rc;
-    d.t_leaf_depth[nr] = depth + 1;
-    d.t_leaf_depth[leaf] = depth + 1;
-    d.t_leaf_parent[leaf] = node;
-    d.t_leaf_parent[nr] = node;
+    P.dt = dt;
+    P.split_gain = (float)(b.gain + d.gain.min_gain_to_split);
+    P.old_value = old_value;
     // child LeafSplits seeded from the SplitInfo (learner.rs:4061-4089)
-    lsL.num_data = lc;
+    lsL.num_data = lcg;
+    lsL._pad = 0;
     lsL.sum_g = b.left_sum_gradient;
     lsL.sum_h = b.left_sum_hessian;
     lsL.weight = b.left_output;
-    lsR.num_data = rc;
+    lsR.num_data = P.rcg;
+    lsR._pad = 0;
     lsR.sum_g = b.right_sum_gradient;
     lsR.sum_h = b.right_sum_hessian;
     lsR.weight = b.right_output;
-    d.ls[leaf] = lsL;
-    d.ls[nr] = lsR;
-    d.best[leaf] = d_split_none();
-    d.best_feature[leaf] = -1;
-    d.best[nr] = d_split_none();
-    d.best_feature[nr] = -1;
+    P.lsL = lsL;
+    P.lsR = lsR;
     left = leaf;
     right = nr;
-    cnt_left = lc;
-    cnt_right = rc;
+    cnt_left = lcg;
+    cnt_right = P.rcg;
     depth_left = depth + 1;
     known = true;
     c.left_leaf = leaf;
@@ -864,12 +945,12 @@ __global__ void k_prepare(GrowDev d, int s) {
   }
   if (c.done || s >= d.L - 1) {
     c.do_find = 0;
-    *cp = c;
+    P.c = c;
     return;
   }
   if (!known) {
-    cnt_left = d.leaf_count[left];
-    cnt_right = right >= 0 ? d.leaf_count[right] : 0;
+    cnt_left = d.leaf_count_g[left];
+    cnt_right = right >= 0 ? d.leaf_count_g[right] : 0;
     depth_left = d.t_leaf_depth[left];
     slot_left = d.slot_of_leaf[left];
     lsL = d.ls[left];
@@ -883,48 +964,48 @@ __global__ void k_prepare(GrowDev d, int s) {
   const int32_t min2 = d.gain.min_data_in_leaf * 2;
   int32_t did = 1;
   if (d.max_depth > 0 && depth_left >= d.max_depth) {
-    d.best[left].gain = kNegInf;
-    if (right >= 0) d.best[right].gain = kNegInf;
+    P.kill0 = left;
+    P.kill1 = right;
     did = 0;
   } else if (right >= 0) {
     if (cnt_right < min2 && cnt_left < min2) {
-      d.best[left].gain = kNegInf;
-      d.best[right].gain = kNegInf;
+      P.kill0 = left;
+      P.kill1 = right;
       did = 0;
     }
   } else if (cnt_left < min2) {
-    d.best[left].gain = kNegInf;
+    P.kill0 = left;
     did = 0;
   }
   c.do_find = did;
   if (!did) {
-    *cp = c;
+    P.c = c;
     return;
   }
   // ---- smaller child + pool slots (learner.rs:1882-1916) ----
-  int32_t smaller, larger, cnt_smaller;
-  DevLeafSplits ls_smaller;
+  int32_t smaller, larger;
+  DevLeafSplits ls_smaller, ls_larger{};
   if (right < 0) {
     smaller = left;
     larger = -1;
-    cnt_smaller = cnt_left;
     ls_smaller = lsL;
   } else if (cnt_left < cnt_right) {
     smaller = left;
     larger = right;
-    cnt_smaller = cnt_left;
     ls_smaller = lsL;
+    ls_larger = lsR;
   } else {
     smaller = right;
     larger = left;
-    cnt_smaller = cnt_right;
     ls_smaller = lsR;
+    ls_larger = lsL;
   }
   int32_t ss, lsl = -1, use_sub = 0;
   if (right < 0) {
     if (slot_left < 0) {
       slot_left = c.next_slot++;
-      d.slot_of_leaf[left] = slot_left;
+      P.slot_leaf0 = left;
+      P.slot_val0 = slot_left;
     }
     ss = slot_left;
   } else {
@@ -932,10 +1013,13 @@ __global__ void k_prepare(GrowDev d, int s) {
     use_sub = parent_slot >= 0 ? 1 : 0;
     ss = c.next_slot++;
     if (smaller == left) {
-      d.slot_of_leaf[right] = parent_slot;
-      d.slot_of_leaf[left] = ss;
+      P.slot_leaf0 = right;
+      P.slot_val0 = parent_slot;
+      P.slot_leaf1 = left;
+      P.slot_val1 = ss;
     } else {
-      d.slot_of_leaf[right] = ss;
+      P.slot_leaf0 = right;
+      P.slot_val0 = ss;
     }
     lsl = parent_slot;
     if (!use_sub) {
@@ -944,20 +1028,85 @@ __global__ void k_prepare(GrowDev d, int s) {
       c.error |= kErrNoParentHistogram;
       c.done = 1;
       c.do_find = 0;
-      *cp = c;
+      P.c = c;
       return;
     }
-  }
-  if (leaf_buildable(ls_smaller)) {
-    c.num_builds += 1;
-    c.rows_built += cnt_smaller;
   }
   c.smaller_leaf = smaller;
   c.larger_leaf = larger;
   c.smaller_slot = ss;
   c.larger_slot = lsl;
   c.use_subtract = use_sub;
-  *cp = c;
+  P.c = c;
+  P.live = 1;
+  P.S = smaller;
+  P.Lg = larger;
+  P.sslot = ss;
+  P.lslot = lsl;
+  P.use_sub = use_sub;
+  P.mask_leaf = left;  // the leaf that was split keeps the left child's id
+  P.smaller_is_left = smaller == left;
+  P.lsS = ls_smaller;
+  P.lsLg = ls_larger;
+}
+
+__device__ void prep_commit(const GrowDev& d, const Prep& P) {
+  if (P.applied) {
+    const int32_t leaf = P.leaf, nr = P.nr, node = P.node;
+    const DevSplitInfo& b = P.c.split;
+    d.leaf_begin[nr] = P.beg + P.lc;
+    d.leaf_count[leaf] = P.lc;
+    d.leaf_count[nr] = P.rc;
+    d.leaf_count_g[leaf] = P.lcg;
+    d.leaf_count_g[nr] = P.rcg;
+    d.leaf_buf[leaf] = P.dst;
+    d.leaf_buf[nr] = P.dst;
+    // Tree::split (lgbm-model/src/tree.rs:614-690)
+    if (P.parent >= 0) {
+      if (P.parent_is_right)
+        d.t_right[P.parent] = node;
+      else
+        d.t_left[P.parent] = node;
+    }
+    d.t_split_feature[node] = P.feature;
+    d.t_split_gain[node] = P.split_gain;
+    d.t_threshold[node] = b.threshold;
+    d.t_internal_value[node] = P.old_value;
+    d.t_internal_count[node] = P.lcg + P.rcg;
+    d.t_left[node] = ~leaf;
+    d.t_right[node] = ~nr;
+    d.t_decision[node] = P.dt;
+    d.t_leaf_value[leaf] = b.left_output;
+    d.t_leaf_weight[leaf] = b.left_sum_hessian;
+    d.t_leaf_count[leaf] = P.lcg;
+    d.t_leaf_value[nr] = b.right_output;
+    d.t_leaf_weight[nr] = b.right_sum_hessian;
+    d.t_leaf_count[nr] = P.rcg;
+    d.t_leaf_depth[nr] = P.depth + 1;
+    d.t_leaf_depth[leaf] = P.depth + 1;
+    d.t_leaf_parent[leaf] = node;
+    d.t_leaf_parent[nr] = node;
+    d.ls[leaf] = P.lsL;
+    d.ls[nr] = P.lsR;
+    d.best[leaf] = d_split_none();
+    d.best_feature[leaf] = -1;
+    d.best[nr] = d_split_none();
+    d.best_feature[nr] = -1;
+    d.raw[d.raw_len] = 0;
+  }
+  if (P.kill0 >= 0) d.best[P.kill0].gain = kNegInf;
+  if (P.kill1 >= 0) d.best[P.kill1].gain = kNegInf;
+  if (P.slot_leaf0 >= 0) d.slot_of_leaf[P.slot_leaf0] = P.slot_val0;
+  if (P.slot_leaf1 >= 0) d.slot_of_leaf[P.slot_leaf1] = P.slot_val1;
+  *d.ctrl = P.c;
+}
+
+// The control step alone: applies the tree's last split.
+__global__ void k_prepare(GrowDev d, int s) {
+  if (threadIdx.x != 0) return;
+  Prep P;
+  prep_compute(d, s, P);
+  prep_commit(d, P);
 }
 
 // ------------------------------------------------------------------------------------
@@ -1079,108 +1228,66 @@ __device__ void pick_split(const GrowDev& d) {
       c->pending = 1;
       c->split_leaf = bl;
       c->split_feature = w[0].f;
-      c->split = (find && bl == S) ? s_win[0] : (find && bl == Lg) ? s_win[1] : d.best[bl];
+      const DevSplitInfo si =
+          (find && bl == S) ? s_win[0] : (find && bl == Lg) ? s_win[1] : d.best[bl];
+      c->split = si;
+      // accumulate the side the scan expects to be smaller (any side is exact)
+      c->build_left = si.left_count <= si.right_count ? 1 : 0;
     }
   }
 }
 
-__global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
+__global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
   __shared__ double s_hist[2][2 * kMaxBins];
   __shared__ ScanScratch s_scan[4];
   __shared__ ScanCand s_cand[4];
-  __shared__ int32_t s_acc[8][2][kMaxBins];  // in-block build: 8 sub-histograms of (G, Q)
+  __shared__ Prep s_prep;
   __shared__ bool s_last;
-  GrowCtrl* c = d.ctrl;
   const int f = blockIdx.x;
   const int tid = threadIdx.x;
-  const bool live = !c->done && c->do_find;
-  if (live) {
-    const int32_t S = c->smaller_leaf, Lg = c->larger_leaf;
-    const DevLeafSplits lss = d.ls[S];
-    const bool used =
-        !c->use_subtract || d.splittable[(size_t)c->left_leaf * d.F + f] != 0;
-    const DevFeature ft = d.feat[f];
-    const int nb = ft.num_bin;
-    long long* raw = d.raw + 2 * (size_t)ft.bin_off;
+  const DevFeature ft = d.feat[f];
+  const int nb = ft.num_bin;
+  // one histogram cell per thread (2*num_bin <= 512 cells)
+  const bool mine = tid < 2 * nb;
+  const size_t cell = 2 * (size_t)ft.bin_off + tid;
+  // the accumulated child (its left or right rows, all devices summed); read it and
+  // clear it for the next partition
+  long long bv = 0;
+  if (mine) bv = d.raw[cell];
+  if (tid == 0) prep_compute(d, s, s_prep);
+  __syncthreads();
+  if (mine) d.raw[cell] = 0;
+  const Prep& P = s_prep;
+  if (P.live) {
+    const int32_t S = P.S, Lg = P.Lg;
+    const bool used = !P.use_sub || d.splittable[(size_t)P.mask_leaf * d.F + f] != 0;
     if (used) {
       const DevGhParams& p = *d.ghp;
+      const DevLeafSplits lss = P.lsS;
       const bool buildable = leaf_buildable(lss);
-      // one histogram cell per thread (2*num_bin <= 512 cells); the parent's cell is
-      // loaded up front together with the raw accumulator
-      const bool mine = tid < 2 * nb;
-      double* pl = d.pool + (size_t)c->larger_slot * d.slot_len + ft.slot_off;
+      double* pl = d.pool + (size_t)P.lslot * d.slot_len + ft.slot_off;
       double parent = 0.0;
       if (mine && Lg >= 0) parent = pl[tid];
       double v = 0.0;
-      const int32_t cnt_s = d.leaf_count[S];
-      if (buildable && build_in_fixscan(d, cnt_s)) {
-        // Feature-parallel build of this feature for the smaller child: every warp takes
-        // a contiguous run of the child's rows; warp w adds into sub-histogram w % 8, so
-        // a sub-histogram sees at most 65536 / 8 rows and its 16-bit fields cannot wrap.
-        // G = sum qg; Q = sum qh | (rows with qh == 3) << 16.
-        int32_t* acc = &s_acc[0][0][0];
-        for (int i = tid; i < 8 * 2 * kMaxBins; i += blockDim.x) acc[i] = 0;
-        __syncthreads();
-        const int w = tid >> 5, lane = tid & 31;
-        int32_t* sg = s_acc[w & 7][0];
-        int32_t* sq = s_acc[w & 7][1];
-        const int32_t beg = d.leaf_begin[S];
-        const int32_t lbuf = d.leaf_buf[S];
-        const uint32_t* lidx = lbuf == 1 ? d.idx1 : d.idx0;
-        const uint16_t* gq = reinterpret_cast<const uint16_t*>(d.gh);
-        const uint8_t* fb = d.bins + f;
-        const int32_t per = (cnt_s + 31) / 32;
-        const int32_t r0 = w * per, r1 = min(cnt_s, r0 + per);
-        for (int32_t k0 = r0; k0 < r1; k0 += 128) {
-          uint32_t rows[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int32_t k = k0 + u * 32 + lane;
-            rows[u] = k < r1 ? (lbuf == 2 ? (uint32_t)(beg + k) : lidx[beg + k]) : 0xffffffffu;
-          }
-          uint32_t bin[4];
-          uint16_t q[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (rows[u] != 0xffffffffu) {
-              bin[u] = fb[(size_t)rows[u] * d.stride];
-              q[u] = gq[rows[u]];
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (rows[u] == 0xffffffffu) continue;
-            const int qg = (int)(int8_t)(q[u] & 0xff);
-            const int qh = (int)(int8_t)(q[u] >> 8);
-            atomicAdd(&sg[bin[u]], qg);
-            atomicAdd(&sq[bin[u]], qh + (qh == 3 ? (1 << 16) : 0));
-          }
+      if (mine) {
+        // Integer histograms of both children: the accumulated side as is, the other as
+        // parent - accumulated. Exact, so the smaller child's cells equal a direct build.
+        long long sv = bv;
+        if (P.applied) {
+          long long* pr = d.rawpool + (size_t)P.leaf * d.raw_len + cell;
+          const long long ov = *pr - bv;
+          const bool bl = P.c.build_left != 0;
+          const long long lv = bl ? bv : ov;
+          const long long rv = bl ? ov : bv;
+          *pr = lv;
+          d.rawpool[(size_t)P.nr * d.raw_len + cell] = rv;
+          sv = P.smaller_is_left ? lv : rv;
+        } else {
+          d.rawpool[cell] = bv;  // root
         }
-        __syncthreads();
-        if (mine) {
-          const int b = tid >> 1;
-          if ((tid & 1) == 0) {
-            long long gs = 0;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) gs += s_acc[u][0][b];
-            v = decode_g(p, gs);
-          } else {
-            long long qs = 0, c3 = 0;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int32_t x = s_acc[u][1][b];
-              qs += x & 0xffff;
-              c3 += x >> 16;
-            }
-            v = decode_h(p, (qs - 3 * c3) | (c3 << 32));
-          }
-        }
-      } else if (mine && buildable) {
-        const long long rv = raw[tid];
-        v = (tid & 1) ? decode_h(p, rv) : decode_g(p, rv);
-        raw[tid] = 0;
+        if (buildable) v = (tid & 1) ? decode_h(p, sv) : decode_g(p, sv);
+        s_hist[0][tid] = v;
       }
-      if (mine) s_hist[0][tid] = v;
       __syncthreads();
       // FixHistogram (fix_histogram.rs:50-81): sequential ascending subtraction.
       const int mfb = ft.most_freq_bin;
@@ -1203,7 +1310,7 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
       }
       // store the smaller child's slot; larger = parent - smaller in the parent's slot
       if (mine) {
-        d.pool[(size_t)c->smaller_slot * d.slot_len + ft.slot_off + tid] = sv;
+        d.pool[(size_t)P.sslot * d.slot_len + ft.slot_off + tid] = sv;
         if (Lg >= 0) {
           const double lv = parent - sv;
           pl[tid] = lv;
@@ -1216,7 +1323,7 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
       const bool fwd = (grp & 1) != 0;
       const int32_t leaf = sel == 0 ? S : Lg;
       if (leaf >= 0) {
-        const DevLeafSplits ls = d.ls[leaf];
+        const DevLeafSplits ls = sel == 0 ? P.lsS : P.lsLg;
         if (leaf_buildable(ls)) {
           ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
           scan_direction(s_hist[sel], ft, d.gain, sl, fwd, s_scan[grp], 1 + grp, &s_cand[grp]);
@@ -1227,7 +1334,7 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
         const int sl_i = tid == 0 ? 0 : 1;
         const int32_t leaf2 = sl_i == 0 ? S : Lg;
         if (leaf2 >= 0) {
-          const DevLeafSplits ls = d.ls[leaf2];
+          const DevLeafSplits ls = sl_i == 0 ? P.lsS : P.lsLg;
           const bool scannable = leaf_buildable(ls);
           if (f == 0) d.scan_ok[sl_i] = scannable ? 1 : 0;
           DevSplitInfo si = d_split_none();
@@ -1238,29 +1345,32 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d) {
           d.scan_out[sl_i * d.F + f] = si;
         }
       }
-    } else {
-      for (int i = tid; i < 2 * nb; i += blockDim.x) raw[i] = 0;
-      if (tid == 0) {
-        d.scan_out[f] = d_split_none();
-        d.scan_out[d.F + f] = d_split_none();
-        if (f == 0) {
-          d.scan_ok[0] = leaf_buildable(lss) ? 1 : 0;
-          d.scan_ok[1] = Lg >= 0 && leaf_buildable(d.ls[Lg]) ? 1 : 0;
-        }
+    } else if (tid == 0) {
+      d.scan_out[f] = d_split_none();
+      d.scan_out[d.F + f] = d_split_none();
+      if (f == 0) {
+        d.scan_ok[0] = leaf_buildable(P.lsS) ? 1 : 0;
+        d.scan_ok[1] = Lg >= 0 && leaf_buildable(P.lsLg) ? 1 : 0;
       }
     }
   }
-  // last-CTA argmax
+  // last CTA: write the control step, then the argmax
   __threadfence();
   __syncthreads();
   if (tid == 0) {
-    const uint32_t t = atomicAdd(&c->scan_counter, 1u);
+    const uint32_t t = atomicAdd(&d.ctrl->scan_counter, 1u);
     s_last = (t == gridDim.x - 1);
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  if (c->done) return;
+  if (tid == 0) {
+    prep_commit(d, s_prep);
+    d.ctrl->scan_counter = 0;
+    __threadfence();
+  }
+  __syncthreads();
+  if (s_prep.c.done) return;
   pick_split(d);
 }
 
@@ -1407,6 +1517,7 @@ __global__ void __launch_bounds__(kPartThreads) k_partition(GrowDev d) {
   const uint32_t* sp = src == 1 ? d.idx1 : d.idx0;
   uint32_t* dp = src == 1 ? d.idx0 : d.idx1;
   const int32_t ntiles = (count + kPartTile - 1) / kPartTile;
+  if (blockIdx.x == 0 && threadIdx.x == 0) c->rows_parted += count;
   const uint32_t epoch = c->epoch;
   const uint32_t thr = c->split.threshold;
   const bool dl = c->split.default_left != 0;
@@ -1426,6 +1537,312 @@ __global__ void __launch_bounds__(kPartThreads) k_partition(GrowDev d) {
       break;
     }
   }
+}
+
+// ------------------------------------------------------------------------------------
+// Partition fused with the histogram build of one child (quantized, <= 4 quant bins,
+// every feature in one shared-memory group). The partition already fetches each row's
+// 32-byte bin sector to route it; the rows that go to the accumulated side
+// (GrowCtrl::build_left) are added to the CTA's shared histogram straight from those
+// registers, while warp 0 waits on the look-back. The other child's histogram is
+// derived exactly in k_fixscan as parent - accumulated. One CTA of 1024 threads per
+// SM; tiles are the standalone partition's 2048-row tiles (same status words).
+// ------------------------------------------------------------------------------------
+
+constexpr int kFpThreads = 1024;
+constexpr int kFpItems = 2;
+static_assert(kFpThreads * kFpItems == kPartTile, "fused tiles are partition tiles");
+constexpr int kFpMaxChunks = 2;  // 16-feature row chunks held in registers per item
+
+// Decoupled look-back of one tile by warp 0 (status words as in PartitionTile).
+// Returns the exclusive prefix of left rows; *ok = 0 after kSpinLimit polls.
+__device__ __forceinline__ int32_t tile_lookback(unsigned long long* status, int32_t tile,
+                                                 uint32_t epoch, int32_t tile_left,
+                                                 int32_t* ok) {
+  const int lane = threadIdx.x & 31;
+  int32_t prefix = 0;
+  *ok = 1;
+  if (lane == 0) {
+    __threadfence();
+    atomicExch(&status[tile], pack_status(epoch, tile == 0 ? 2u : 1u, (uint32_t)tile_left));
+  }
+  if (tile == 0) return 0;
+  const uint32_t ep = epoch & 0xffffffu;
+  int32_t j_end = tile;
+  long long spins = 0;
+  while (true) {
+    const int32_t j = j_end - 32 + lane;
+    uint32_t fl = 2u, val = 0u;
+    if (j >= 0) {
+      const unsigned long long w = *reinterpret_cast<volatile unsigned long long*>(&status[j]);
+      fl = ((uint32_t)(w >> 40) == ep) ? ((uint32_t)(w >> 32) & 0xffu) : 0u;
+      val = (uint32_t)(w & 0xffffffffull);
+    }
+    const uint32_t pref = __ballot_sync(0xffffffffu, fl == 2u);
+    const uint32_t notready = __ballot_sync(0xffffffffu, fl == 0u);
+    const int hp = pref ? 31 - __clz(pref) : -1;
+    const uint32_t need = hp >= 0 ? (0xffffffffu << hp) : 0xffffffffu;
+    if (notready & need) {
+      if (++spins > kSpinLimit) {
+        *ok = 0;
+        return 0;
+      }
+      __nanosleep(20);
+      continue;
+    }
+    int32_t v = (lane >= hp) ? (int32_t)val : 0;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    prefix += v;
+    if (hp >= 0) break;
+    j_end -= 32;
+  }
+  if (lane == 0) {
+    __threadfence();
+    atomicExch(&status[tile], pack_status(epoch, 2u, (uint32_t)(prefix + tile_left)));
+  }
+  return prefix;
+}
+
+template <int SHIFT, int NCH>
+__global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int build) {
+  static_assert(NCH <= kFpMaxChunks, "row chunks held in registers");
+  extern __shared__ uint32_t sm[];  // hot | c3 | cold_g | cold_q, kQ4MaxCells words each
+  __shared__ int32_t s_warp[kFpThreads / 32];
+  __shared__ int32_t s_tile, s_prefix, s_ok;
+  __shared__ int32_t s_nb[128];
+  __shared__ int32_t s_boff[128];
+  __shared__ uint32_t s_mask[4];
+  GrowCtrl* c = d.ctrl;
+  if (c->done || !c->pending) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int32_t leaf = c->split_leaf;
+  const int32_t f = c->split_feature;
+  const DevFeature ft = d.feat[f];
+  const int32_t begin = d.leaf_begin[leaf];
+  const int32_t count = d.leaf_count[leaf];
+  const int32_t src = d.leaf_buf[leaf];
+  const uint32_t* sp = src == 1 ? d.idx1 : d.idx0;
+  uint32_t* dp = src == 1 ? d.idx0 : d.idx1;
+  const bool identity = src == 2;
+  const int32_t ntiles = (count + kPartTile - 1) / kPartTile;
+  const uint32_t epoch = c->epoch;
+  const uint32_t thr = c->split.threshold;
+  const bool dl = c->split.default_left != 0;
+  const bool build_left = c->build_left != 0;
+  const int nf = d.F;
+  const int cap = nf << SHIFT;
+  if (blockIdx.x == 0 && tid == 0) {
+    c->rows_parted += count;
+    if (build) c->num_builds += 1;
+  }
+  if (tid == 0) s_tile = (int32_t)atomicAdd(&c->part_ticket, 1u);
+  __syncthreads();
+  int32_t tile = s_tile;
+  if (tile >= ntiles) return;
+  uint32_t* hot = sm;
+  uint32_t* c3 = sm + kQ4MaxCells;
+  int32_t* cold_g = reinterpret_cast<int32_t*>(sm + 2 * kQ4MaxCells);
+  int32_t* cold_q = reinterpret_cast<int32_t*>(sm + 3 * kQ4MaxCells);
+  if (build) {
+    uint4* h4 = reinterpret_cast<uint4*>(hot);
+    uint4* c4 = reinterpret_cast<uint4*>(c3);
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < (cap + 3) / 4; i += kFpThreads) {
+      h4[i] = z;
+      c4[i] = z;
+    }
+    // the children keep the features their parent could split (learner.rs:2003-2020)
+    const uint8_t* ps = d.splittable + (size_t)leaf * d.F;
+    for (int fl = tid; fl < nf; fl += kFpThreads) {
+      const DevFeature g = d.feat[fl];
+      s_nb[fl] = g.num_bin;
+      s_boff[fl] = g.bin_off;
+    }
+    if (tid < 4) {
+      uint32_t m = 0;
+      for (int b = 0; b < 32; ++b) {
+        const int fl = tid * 32 + b;
+        if (fl < nf && ps[fl]) m |= 1u << b;
+      }
+      s_mask[tid] = m;
+    }
+  }
+  __syncthreads();
+  Q4Mask qm = q4_mask<NCH>(s_mask, nf);
+  const uint16_t* gq = reinterpret_cast<const uint16_t*>(d.gh);
+  const int fch = f >> 4, fw = (f >> 2) & 3, fsh = (f & 3) * 8;
+  const size_t stride = (size_t)d.stride;
+  bool folded = false;
+  int32_t acc_rows = 0;
+  int32_t cta_left = 0;
+  long long cta_built = 0;
+  bool failed = false;
+  while (true) {
+    const int32_t base = tile * kPartTile;
+    uint32_t rows[kFpItems];
+    uint4 w[kFpItems][NCH];
+    uint16_t q[kFpItems];
+    uint32_t leftmask = 0, validmask = 0;
+#pragma unroll
+    for (int j = 0; j < kFpItems; ++j) {
+      const int32_t p = base + tid * kFpItems + j;
+      rows[j] = 0;
+      if (p < count) {
+        rows[j] = identity ? (uint32_t)(begin + p) : sp[begin + p];
+        validmask |= 1u << j;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kFpItems; ++j) {
+      if ((validmask >> j) & 1u) {
+        const uint4* rp = reinterpret_cast<const uint4*>(d.bins + (size_t)rows[j] * stride);
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch) w[j][ch] = rp[ch];
+        q[j] = build ? gq[rows[j]] : (uint16_t)0;
+      } else {
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch) w[j][ch] = make_uint4(0u, 0u, 0u, 0u);
+        q[j] = 0;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kFpItems; ++j) {
+      if (!((validmask >> j) & 1u)) continue;
+      uint4 v = w[j][0];
+#pragma unroll
+      for (int ch = 1; ch < NCH; ++ch)
+        if (ch == fch) v = w[j][ch];
+      const uint32_t word = fw == 0 ? v.x : fw == 1 ? v.y : fw == 2 ? v.z : v.w;
+      const int32_t bin = (int32_t)((word >> fsh) & 0xffu);
+      if (!d_go_right(ft, thr, dl, bin)) leftmask |= 1u << j;
+    }
+    const int32_t my_left = __popc(leftmask);
+    int32_t incl = my_left;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    int32_t warp_off = 0, tile_left = 0;
+#pragma unroll 8
+    for (int wi = 0; wi < kFpThreads / 32; ++wi) {
+      const int32_t v = s_warp[wi];
+      if (wi < warp) warp_off += v;
+      tile_left += v;
+    }
+    const int32_t excl = warp_off + incl - my_left;
+    if (warp == 0) {
+      int32_t ok = 1;
+      const int32_t prefix = tile_lookback(d.part_status, tile, epoch, tile_left, &ok);
+      if (lane == 0) {
+        s_prefix = prefix;
+        s_ok = ok;
+      }
+    }
+    // accumulate the chosen side while warp 0 looks back
+    if (build) {
+#pragma unroll
+      for (int j = 0; j < kFpItems; ++j) {
+        if (!((validmask >> j) & 1u)) continue;
+        const bool is_left = (leftmask >> j) & 1u;
+        if (is_left != build_left) continue;
+        const int qg = (int)(int8_t)(q[j] & 0xff), qh = (int)(int8_t)(q[j] >> 8);
+        if (qm.full)
+          q4_row_regs<SHIFT, NCH, false>(w[j], qg + (qh << 16), qh == 3, hot, qm.w, qm.tail);
+        else
+          q4_row_regs<SHIFT, NCH, true>(w[j], qg + (qh << 16), qh == 3, hot, qm.w, qm.tail);
+      }
+    }
+    __syncthreads();
+    const int32_t prefix_left = s_prefix;
+    if (s_ok == 0) {
+      failed = true;
+      break;
+    }
+    {
+      const int32_t prefix_right = base - prefix_left;
+      int32_t lrank = excl;
+      const int32_t my_base = tid * kFpItems;
+#pragma unroll
+      for (int j = 0; j < kFpItems; ++j) {
+        if (!((validmask >> j) & 1u)) continue;
+        if ((leftmask >> j) & 1u) {
+          dp[begin + prefix_left + lrank] = rows[j];
+          ++lrank;
+        } else {
+          const int32_t rrank = (my_base + j) - lrank;
+          dp[begin + count - 1 - (prefix_right + rrank)] = rows[j];
+        }
+      }
+    }
+    const int32_t valid = min(kPartTile, count - base);
+    const int32_t built = build_left ? tile_left : valid - tile_left;
+    cta_left += tile_left;
+    cta_built += built;
+    acc_rows += built;
+    if (tid == 0) s_tile = (int32_t)atomicAdd(&c->part_ticket, 1u);
+    __syncthreads();
+    tile = s_tile;
+    if (tile >= ntiles) break;
+    // fold the 16-bit packed fields before the next tile could overflow them
+    if (build && acc_rows + kPartTile > kQ4Chunk) {
+      for (int s2 = tid; s2 < cap; s2 += kFpThreads) {
+        const int32_t v = (int32_t)hot[s2];
+        const int32_t lo = (int32_t)(int16_t)(v & 0xffff);
+        const int32_t hi = (v - lo) >> 16;
+        cold_g[s2] = folded ? cold_g[s2] + lo : lo;
+        cold_q[s2] = folded ? cold_q[s2] + hi : hi;
+        hot[s2] = 0u;
+      }
+      folded = true;
+      acc_rows = 0;
+      __syncthreads();
+    }
+  }
+  if (failed) {
+    if (tid == 0) {
+      atomicOr(&c->error, kErrSpinTimeout);
+      c->done = 1;
+    }
+    return;
+  }
+  if (build) {
+    __syncthreads();
+    long long* raw = d.raw;
+    for (int s2 = tid; s2 < cap; s2 += kFpThreads) {
+      const int fl = s2 >> SHIFT;
+      const int bin = s2 & ((1 << SHIFT) - 1);
+      if (fl >= nf || bin >= s_nb[fl]) continue;
+      const int32_t v = (int32_t)hot[s2];
+      const int32_t lo = (int32_t)(int16_t)(v & 0xffff);
+      const long long g = (folded ? (long long)cold_g[s2] : 0ll) + lo;
+      const long long qsum = (folded ? (long long)cold_q[s2] : 0ll) + ((v - lo) >> 16);
+      const long long n3 = (long long)c3[s2];
+      const long long h = (qsum - 3 * n3) | (n3 << 32);
+      const size_t gb = (size_t)(s_boff[fl] + bin);
+      if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb]), (unsigned long long)g);
+      if (h)
+        atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb + 1]), (unsigned long long)h);
+    }
+  }
+  if (tid == 0) {
+    atomicAdd(&c->part_left_total, cta_left);
+    atomicAdd(reinterpret_cast<unsigned long long*>(&d.raw[d.raw_len]),
+              (unsigned long long)(long long)cta_left);
+    if (build) atomicAdd(reinterpret_cast<unsigned long long*>(&c->rows_built),
+                         (unsigned long long)cta_built);
+  }
+}
+
+using PartQ4Kernel = void (*)(GrowDev, int);
+__host__ PartQ4Kernel part_q4_kernel(int shift, int nch) {
+#define PQ4_CASE(S, N) \
+  if (shift == S && nch == N) return k_partition_q4<S, N>;
+  PQ4_CASE(4, 1) PQ4_CASE(4, 2) PQ4_CASE(5, 1) PQ4_CASE(5, 2) PQ4_CASE(6, 1) PQ4_CASE(6, 2)
+  PQ4_CASE(7, 1) PQ4_CASE(7, 2) PQ4_CASE(8, 1) PQ4_CASE(8, 2)
+#undef PQ4_CASE
+  return nullptr;
 }
 
 // ---------------------------- standalone per-op kernels ----------------------------
@@ -1535,8 +1952,19 @@ void LaunchProfiler::end(cudaStream_t st, int slot) {
     if (prof) prof->end(st, _slot); \
   } while (0)
 
+bool fused_partition_supported(int gh_mode, int num_groups, int shift, int nch) {
+  return gh_mode == GH_QPACK && num_groups == 1 && nch <= kFpMaxChunks &&
+         part_q4_kernel(shift, nch) != nullptr;
+}
+
+size_t fused_partition_smem() { return (size_t)4 * sizeof(uint32_t) * kQ4MaxCells; }
+
+// One tree: root build, then per split the control step + scans (k_fixscan) and the
+// partition, which in the fused mode also accumulates one child's histogram (else a
+// build kernel follows). `exchange`, when set, sums the accumulated child (d.raw,
+// raw_len cells + the left count) over all devices after every build.
 void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStream_t st,
-                 LaunchProfiler* prof) {
+                 LaunchProfiler* prof, const TreeExchange* exchange) {
   const int sms = num_sms();
   {
     PROF_BEGIN(KC_INIT);
@@ -1545,32 +1973,42 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
   }
   const dim3 bgrid(build_blocks, d.num_groups);
   const int part_blocks = sms * 4;
+  auto build = [&](int phase) {
+    PROF_BEGIN(KC_BUILD);
+    if (d.gh_mode == GH_QPACK)
+      q4_kernel(d.q4_shift, d.q4_nch)<<<bgrid, kQ4Threads, build_smem, st>>>(d, phase);
+    else if (d.gh_mode == GH_QLUT)
+      k_build<GH_QLUT><<<bgrid, kBuildThreads, build_smem, st>>>(d, phase);
+    else
+      k_build<GH_FLOAT><<<bgrid, kBuildThreads, build_smem, st>>>(d, phase);
+    PROF_END();
+  };
+  auto exchange_raw = [&]() {
+    if (exchange && exchange->fn) exchange->fn(exchange->ctx, d.raw, d.raw_len + 1, st);
+  };
+  build(0);
+  exchange_raw();
   for (int s = 0; s < d.L - 1; ++s) {
     {
-      PROF_BEGIN(KC_PREPARE);
-      k_prepare<<<1, 32, 0, st>>>(d, s);
-      PROF_END();
-    }
-    {
-      PROF_BEGIN(KC_BUILD);
-      if (d.gh_mode == GH_QPACK)
-        q4_kernel(d.q4_shift, d.q4_nch)<<<bgrid, kQ4Threads, build_smem, st>>>(d);
-      else if (d.gh_mode == GH_QLUT)
-        k_build<GH_QLUT><<<bgrid, kBuildThreads, build_smem, st>>>(d);
-      else
-        k_build<GH_FLOAT><<<bgrid, kBuildThreads, build_smem, st>>>(d);
-      PROF_END();
-    }
-    {
       PROF_BEGIN(KC_FIXSCAN);
-      k_fixscan<<<d.F, kScanThreads, 0, st>>>(d);
+      k_fixscan<<<d.F, kScanThreads, 0, st>>>(d, s);
       PROF_END();
     }
-    {
+    const int phase = s < d.L - 2 ? 1 : 2;
+    if (d.fused) {
       PROF_BEGIN(KC_PARTITION);
-      k_partition<<<part_blocks, kPartThreads, 0, st>>>(d);
+      part_q4_kernel(d.q4_shift, d.q4_nch)<<<sms, kFpThreads, fused_partition_smem(), st>>>(
+          d, phase == 1 ? 1 : 0);
       PROF_END();
+    } else {
+      {
+        PROF_BEGIN(KC_PARTITION);
+        k_partition<<<part_blocks, kPartThreads, 0, st>>>(d);
+        PROF_END();
+      }
+      build(phase);
     }
+    exchange_raw();
   }
   {
     PROF_BEGIN(KC_PREPARE);
@@ -1592,6 +2030,11 @@ void set_build_smem_limit(size_t bytes) {
         cudaFuncSetAttribute(q4_kernel(sh, n), cudaFuncAttributePreferredSharedMemoryCarveout,
                              100);
       }
+  for (int sh = 4; sh <= 8; ++sh)
+    for (int n = 1; n <= kFpMaxChunks; ++n)
+      if (part_q4_kernel(sh, n))
+        cudaFuncSetAttribute(part_q4_kernel(sh, n), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)fused_partition_smem());
   cudaFuncSetAttribute(k_build<GH_QLUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)bytes);
   cudaFuncSetAttribute(k_build<GH_FLOAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,

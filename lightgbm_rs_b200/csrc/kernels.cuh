@@ -45,7 +45,8 @@ struct GrowDev {
   DevGainConfig gain;
   // per-leaf state [L]
   int32_t* leaf_begin;
-  int32_t* leaf_count;
+  int32_t* leaf_count;    // rows of the leaf on this device
+  int32_t* leaf_count_g;  // rows of the leaf on all devices
   int32_t* leaf_buf;  // 0/1 = index buffer, 2 = identity (root)
   int32_t* slot_of_leaf;
   DevLeafSplits* ls;
@@ -72,7 +73,11 @@ struct GrowDev {
   unsigned long long* part_status;
   int32_t max_tiles;
   double* pool;            // [L][slot_len]
-  long long* raw;          // [2 * total_bins]
+  long long* raw;          // [raw_len + 2]: the accumulated child, then its left-row count
+  long long* rawpool;      // [L][raw_len]: integer histogram of every leaf
+  int32_t raw_len;         // 2 * total_bins
+  int32_t fused;           // the partition kernel accumulates the child histogram
+  int64_t n_global;        // rows on all devices
   DevSplitInfo* scan_out;  // [2][F]
   uint8_t* scan_ok;        // [2] leaf scanned flags
   // gradients
@@ -95,9 +100,18 @@ struct LaunchProfiler {
   void end(cudaStream_t st, int slot);
 };
 
+// Sum of the accumulated child histogram over devices, enqueued on the tree's stream
+// after every build (data-parallel training); fn(ctx, buf, count, stream) sums `count`
+// int64 cells in place.
+struct TreeExchange {
+  void (*fn)(void* ctx, long long* buf, int64_t count, cudaStream_t st);
+  void* ctx;
+};
+
 // Host-side launch helpers (kernels.cu).
 void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStream_t st,
-                 LaunchProfiler* prof = nullptr);
+                 LaunchProfiler* prof = nullptr, const TreeExchange* exchange = nullptr);
+bool fused_partition_supported(int gh_mode, int num_groups, int shift, int nch);
 int build_smem_bytes_per_bin(int gh_mode);
 
 // Objective / score kernels (objective.cu).

@@ -153,3 +153,43 @@ def test_booster_l2_quantized_constant_hessian(data):
                        min_data_in_leaf=20)
     for i, (a, b) in enumerate(zip(booster.trees(), ref["trees"])):
         _assert_trees_bit_equal(a, b, f"l2 tree {i}")
+
+
+@pytest.mark.parametrize("num_features,num_quant_bins", [(72, 4), (72, 16), (40, 4)])
+def test_wide_quantized_tree_bit_exact(num_features, num_quant_bins):
+    """More features than one shared-memory group: the partition and the build run as
+    separate kernels (and the build spans several feature groups)."""
+    import lightgbm_rs_b200 as lgb
+    import oracle
+    from lightgbm_rs_b200 import synthetic
+
+    X, y = synthetic.binary_c0(num_data=30_000, num_features=num_features, seed=3)
+    ds = lgb.Dataset(X, y, {"max_bin": 255, "min_data_in_leaf": 20})
+    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
+             for m in ds.mappers]
+    g, h = oracle.binary_gradients(np.zeros(len(y)), y)
+    gq, hq, q, scales = oracle.quantize(g, h, num_quant_bins)
+    want, wpart, _ = oracle.grow_tree(ds.bins, metas, gq, hq, num_leaves=63, min_data_in_leaf=20)
+    learner = lgb.Learner(ds, {"num_leaves": 63, "min_data_in_leaf": 20})
+    got, gpart = learner.grow(quantized=q, scales=[scales[0], scales[1], scales[2],
+                                                   num_quant_bins])
+    _assert_trees_bit_equal(got, want, f"wide F{num_features} q{num_quant_bins}")
+    for a, b in zip(_leaf_sets(gpart, got["num_leaves"]), _leaf_sets(wpart, want["num_leaves"])):
+        assert np.array_equal(a, b)
+
+
+def test_tree_that_stops_early(data):
+    """A large min_data_in_leaf ends the tree before num_leaves: the remaining split
+    steps run with nothing to do and must leave the next tree a clean state."""
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, y, ds, metas = data
+    g, h = oracle.binary_gradients(np.zeros(len(y)), y)
+    gq, hq, q, scales = oracle.quantize(g, h, 4)
+    learner = lgb.Learner(ds, {"num_leaves": 255, "min_data_in_leaf": 4000})
+    want, _, _ = oracle.grow_tree(ds.bins, metas, gq, hq, num_leaves=255, min_data_in_leaf=4000)
+    assert want["num_leaves"] < 255
+    for _ in range(2):
+        got, _ = learner.grow(quantized=q, scales=[scales[0], scales[1], scales[2], 4])
+        _assert_trees_bit_equal(got, want, "early stop")
