@@ -158,15 +158,25 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def hist_algorithmic_bytes(counts, rows, grad):
-    """Bytes the histogram build must move per iteration (bins of every streamed row,
-    its gradient pair, its row index for non-root leaves, and the histogram slot)."""
+def kernel_bytes(counts, rows, grad):
+    """Algorithmic bytes per iteration of the tree kernels, from the device counters.
+
+    Partition: per parent row 1 B (split-feature bin) + 4 B (index write) + 4 B (index read,
+    none for the root's identity order). Build: per built row F B of bins + its gradient
+    pair (2 B quantized, 8 B f32) + 4 B index (none at the root). In the fused mode the
+    partition kernel builds the child itself, so those built rows are charged to it, minus
+    the split-feature byte and the index it has already read."""
     s_gh = 2 if grad == "quantized" else 8
-    slot = 2 * 256 * N_FEAT * 8
-    builds = counts["builds"]
-    rb = counts["rows_built"]
-    nonroot_rows = max(rb - rows, 0)
-    return rb * (N_FEAT * 1 + s_gh) + nonroot_rows * 4 + builds * slot, rb * N_FEAT
+    rp, rb = counts["rows_parted"], counts["rows_built"]
+    part = rp * 5 + max(rp - rows, 0) * 4
+    root_build = rows * (N_FEAT + s_gh)
+    child_rows = max(rb - rows, 0)
+    if counts["fused"]:
+        part += child_rows * (N_FEAT - 1 + s_gh)
+        build = root_build
+    else:
+        build = root_build + child_rows * (N_FEAT + s_gh + 4)
+    return {"partition": part, "build": build, "bin_bytes": rb * N_FEAT + rp}
 
 
 def cpu_baseline(bins, mappers, y, grad, seconds_budget=25.0):
@@ -230,7 +240,7 @@ def run_reference(args):
     out = {
         "metric": "boosting_iters_per_sec", "value": v, "unit": "iters/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * el / args.steps, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1000.0 * el / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": {"workload": f"C1 binary {args.rows}x{N_FEAT} num_leaves={NUM_LEAVES} "
                                f"grad={args.grad}", "rows": args.rows,
@@ -247,82 +257,129 @@ def run_reference(args):
 def run_ours(args):
     import lightgbm_rs_b200 as lgb
     from lightgbm_rs_b200 import build as libbuild
+    from lightgbm_rs_b200 import distributed as D
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
     if world > 1:
-        raise SystemExit("multi-GPU data-parallel bench is not built yet")
-    libbuild.build()
+        import datetime
+
+        import torch.distributed as dist
+
+        # host plumbing only (barriers, the NCCL id, max over ranks); the data path's
+        # all-reduces run inside the library on its own NCCL communicator
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+    if rank == 0:
+        libbuild.build()
+        make_data(args.rows)  # generates and caches for the other ranks
+    if dist:
+        dist.barrier()
     assert lgb._lib.device_count() > 0, "no CUDA device"
     bins, mappers, y = make_data(args.rows)
     p = params(args.grad)
     p["device"] = local
+    b0, b1 = D.shard_range(args.rows, world, rank)
+    local_rows = b1 - b0
+    shard_bins = bins[:, b0:b1] if world > 1 else bins
+    shard_y = y[b0:b1]
+    comm = D.from_torch(local) if dist else None
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        import torch
+
+        t = torch.tensor([float(x)], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     # ---- device-resident run: inputs already in HBM when the timed region starts ----
-    ds = lgb.Dataset(bins=bins, mappers=mappers, label=y, params=p)
-    booster = lgb.Booster(p, ds)
+    ds = lgb.Dataset(bins=shard_bins, mappers=mappers, label=shard_y, params=p)
+    booster = lgb.Booster(p, ds, comm=comm)
     booster.update(args.warmup)
+    if dist:
+        dist.barrier()
     with ClockSampler(local) as clk:
         done = booster.update(args.steps)
         dev_ms = booster.last_train_ms()
+    if dist:
+        dist.barrier()
     assert done == args.steps, f"training stopped early ({done} of {args.steps})"
+    dev_ms = max_over_ranks(dev_ms)
     value = args.steps / (dev_ms / 1000.0)
 
     # ---- per-kernel timing of one more iteration (CUDA events on the library stream) ----
     kms, counts = booster.profile_iteration()
-    alg_bytes, bin_bytes = hist_algorithmic_bytes(counts, args.rows, args.grad)
-    build_ms = kms["build"]
+    kb = kernel_bytes(counts, local_rows, args.grad)
     peak, peak_kind = load_peaks()
-    achieved = alg_bytes / (build_ms / 1000.0) / 1e9 if build_ms > 0 else 0.0
+    per_kernel = {}
+    for cls, label in (("partition", "k_partition_q4 (partition + child histogram)"
+                        if counts["fused"] else "k_partition (row partition)"),
+                       ("build", "k_build_q4 (root histogram)" if counts["fused"]
+                        else "k_build (histogram build)")):
+        ms = kms[cls]
+        ach = kb[cls] / (ms / 1000.0) / 1e9 if ms > 0 else 0.0
+        per_kernel[cls] = {"kernel": label, "ms_per_iter": ms, "bytes_per_iter": kb[cls],
+                           "achieved": ach, "frac": ach / peak if peak else None}
+    dom = max(per_kernel, key=lambda k: per_kernel[k]["ms_per_iter"])
     launches_per_step = counts["launches"]
     del booster
 
     # ---- end to end through the public API from host buffers ----
+    if dist:
+        dist.barrier()
     t0 = time.perf_counter()
-    ds2 = lgb.Dataset(bins=bins, mappers=mappers, label=y, params=p)
-    b2 = lgb.train(p, ds2, num_boost_round=args.steps)
+    ds2 = lgb.Dataset(bins=shard_bins, mappers=mappers, label=shard_y, params=p)
+    b2 = lgb.train(p, ds2, num_boost_round=args.steps, comm=comm)
     trees = b2.trees()
     scores = b2.train_scores()
-    e2e_s = time.perf_counter() - t0
-    h2d = bins.nbytes + y.nbytes
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    h2d = np.ascontiguousarray(shard_bins).nbytes + shard_y.nbytes
     d2h = scores.nbytes + sum(sum(np.asarray(v).nbytes for k, v in t.items()
                                   if isinstance(v, np.ndarray)) for t in trees)
     del b2, ds2
 
     cpu = None
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         v, cores, iters, el = cpu_baseline(bins, mappers, y, args.grad)
         cpu = {"value": v, "unit": "iters/s", "cores": cores, "kind": "port",
                "sample": f"{iters} full boosting iterations on all {args.rows} rows "
                          f"({el:.1f} s), {cores} threads"}
 
+    par = "single GPU" if world == 1 else (
+        f"data-parallel, {world} GPUs: rows sharded, one NCCL all-reduce of the integer "
+        f"child histogram per split")
     out = {
         "metric": "boosting_iters_per_sec",
         "value": value,
         "unit": "iters/s",
-        "n_gpus": 1,
+        "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": dev_ms / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int64+f64" if args.grad == "quantized" else "f32+f64",
         "data": "synthetic",
         "config": {"workload": f"C1 binary {args.rows}x{N_FEAT} num_leaves={NUM_LEAVES} "
                                f"min_data_in_leaf={MIN_DATA_IN_LEAF} max_bin=255 "
                                f"grad={args.grad}",
-                   "rows": args.rows, "features": N_FEAT, "num_leaves": NUM_LEAVES,
-                   "grad": args.grad, "parallelism": "single GPU",
-                   "l2": "inputs larger than L2 (bin matrix 336 MB > 126 MB)"},
-        "roofline": {"bound": "hbm", "kernel": "k_build (histogram build)",
-                     "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak if peak else None, "peak_kind": peak_kind,
-                     "traffic": None, "algorithmic_bytes_per_iter": alg_bytes,
-                     "bin_bytes_per_iter": bin_bytes, "build_ms_per_iter": build_ms,
-                     "builds_per_iter": counts["builds"], "rows_built_per_iter":
-                         counts["rows_built"]},
+                   "rows": args.rows, "rows_per_gpu": local_rows, "features": N_FEAT,
+                   "num_leaves": NUM_LEAVES, "grad": args.grad, "parallelism": par,
+                   "l2": f"inputs larger than L2 (bin matrix {args.rows * 32 / 1e6:.0f} MB "
+                         f"> 126 MB)"},
+        "roofline": {"bound": "hbm", "kernel": per_kernel[dom]["kernel"],
+                     "achieved": per_kernel[dom]["achieved"], "peak": peak, "unit": "GB/s",
+                     "frac": per_kernel[dom]["frac"], "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_iter": per_kernel[dom]["bytes_per_iter"],
+                     "ms_per_iter": per_kernel[dom]["ms_per_iter"],
+                     "other_kernels": {k: v for k, v in per_kernel.items() if k != dom},
+                     "rows_parted_per_iter": counts["rows_parted"],
+                     "rows_built_per_iter": counts["rows_built"],
+                     "builds_per_iter": counts["builds"], "splits_per_iter": counts["splits"]},
         "kernel_ms_per_iter": kms,
         "cpu_baseline": cpu,
         "e2e": {"value": args.steps / e2e_s, "unit": "iters/s",
@@ -332,6 +389,11 @@ def run_ours(args):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
+    if comm is not None:
+        comm.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(out), flush=True)
 

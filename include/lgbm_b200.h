@@ -308,10 +308,41 @@ int lgbm_b200_booster_phase_ms(const lgbm_b200_booster* b, double* out3);
 /* Run ONE more boosting iteration outside the CUDA graph with CUDA events around
  * every kernel launch. ms_out[7] receives the summed device time per kernel class
  * {prepare, histogram build, fix+scan, partition, tree init, gradients, finish};
- * counts_out[4] = {kernel launches, histogram builds, rows streamed by the builds,
- * splits}. The iteration counts as a normal boosting iteration. */
+ * counts_out[6] = {kernel launches, histogram builds, rows streamed by the builds,
+ * splits, parent rows streamed by the partitions, 1 if the partition kernel also
+ * builds the child histogram}. The iteration counts as a normal boosting iteration. */
 int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
                                         int64_t* counts_out);
+
+/* ---------------------------------------------------- data-parallel training */
+
+/* Several GPUs train one model on a dataset sharded by rows, one process (or
+ * thread) per GPU: LightGBM's data-parallel tree learner. The reference has no
+ * counterpart: it maps tree_learner=data/feature/voting back to serial
+ * (crates/lgbm-core/src/config/set.rs:592-600). Every rank keeps its own rows;
+ * after each histogram build the ranks sum the integer child histogram and its
+ * left-row count over NCCL (one all-reduce per split), so all ranks take the
+ * same decisions and hold the same trees. With quantized gradients the trees
+ * are bit-identical to single-GPU training on all rows.
+ *
+ * NCCL is loaded at run time (libnccl.so.2); without it these calls return
+ * LGBM_B200_CAPABILITY_UNAVAILABLE. Rank 0 makes the id with
+ * lgbm_b200_comm_unique_id and hands the bytes to every rank out of band. */
+typedef struct lgbm_b200_comm lgbm_b200_comm;
+#define LGBM_B200_COMM_ID_BYTES 128
+int lgbm_b200_comm_unique_id(uint8_t* id_out);
+int lgbm_b200_comm_create(int32_t device, int32_t nranks, int32_t rank, const uint8_t* id,
+                          lgbm_b200_comm** out);
+int lgbm_b200_comm_destroy(lgbm_b200_comm* comm);
+
+/* Gbdt over this rank's shard. `labels` are the shard's rows in the dataset's
+ * order; the global row order is the shards in rank order (the init score is
+ * computed from all labels, gathered once). Every rank must call
+ * lgbm_b200_booster_train with the same iteration counts. Tree and score
+ * accessors work as for lgbm_b200_booster_create; scores are this shard's. */
+int lgbm_b200_booster_create_distributed(lgbm_b200_dataset* ds, const float* labels,
+                                         const lgbm_b200_train_config* cfg,
+                                         lgbm_b200_comm* comm, lgbm_b200_booster** out);
 
 #ifdef __cplusplus
 }

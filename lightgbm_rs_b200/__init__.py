@@ -13,8 +13,10 @@ import numpy as np
 
 from . import _lib as C
 from ._lib import LightGBMError
+from . import distributed  # noqa: E402
 
-__all__ = ["Dataset", "Booster", "train", "bin_column", "LightGBMError", "Learner"]
+__all__ = ["Dataset", "Booster", "train", "bin_column", "LightGBMError", "Learner",
+           "distributed"]
 
 # Reference config defaults (crates/lgbm-core/src/config/mod.rs:430-587).
 _DEFAULTS = {
@@ -199,7 +201,9 @@ class Learner:
 class Booster:
     """Trained model (lightgbm_rs.Booster subset: predict, trees, scores)."""
 
-    def __init__(self, params, train_set):
+    def __init__(self, params, train_set, comm=None):
+        """comm: a distributed.Communicator for data-parallel training; train_set then
+        holds this rank's shard of the rows (in global row order, shards in rank order)."""
         self.params = _resolve(params)
         self.train_set = train_set
         p = self.params
@@ -213,9 +217,19 @@ class Booster:
                             int(p["num_grad_quant_bins"]), int(bool(p["boost_from_average"])),
                             float(p["sigmoid"]), float(p["learning_rate"]))
         h = ctypes.c_void_p()
-        C.check(C.lib().lgbm_b200_booster_create(train_set.construct(), C.ptr(train_set.label),
-                                                 ctypes.byref(cfg), ctypes.byref(h)))
+        if comm is not None:
+            C.check(C.lib().lgbm_b200_booster_create_distributed(
+                train_set.construct(), C.ptr(train_set.label), ctypes.byref(cfg), comm._handle,
+                ctypes.byref(h)))
+        elif str(p.get("tree_learner", "serial")).lower() in ("data", "data_parallel"):
+            raise LightGBMError(C.INVALID_ARGUMENT,
+                                "tree_learner=data needs a distributed.Communicator (comm=)")
+        else:
+            C.check(C.lib().lgbm_b200_booster_create(train_set.construct(),
+                                                     C.ptr(train_set.label),
+                                                     ctypes.byref(cfg), ctypes.byref(h)))
         self._handle = h
+        self._comm = comm  # keeps the communicator alive as long as the booster
         self.num_leaves = int(p["num_leaves"])
         self._trees = None
 
@@ -270,12 +284,12 @@ class Booster:
         """One extra iteration with per-kernel-class device timing (CUDA events on the
         library's stream). Returns (ms by class, counts dict)."""
         ms = np.zeros(7, dtype=np.float64)
-        cnt = np.zeros(4, dtype=np.int64)
+        cnt = np.zeros(6, dtype=np.int64)
         C.check(C.lib().lgbm_b200_booster_profile_iteration(self._handle, C.ptr(ms), C.ptr(cnt)))
         self._trees = None
         return (dict(zip(self.KERNEL_CLASSES, ms.tolist())),
                 {"launches": int(cnt[0]), "builds": int(cnt[1]), "rows_built": int(cnt[2]),
-                 "splits": int(cnt[3])})
+                 "splits": int(cnt[3]), "rows_parted": int(cnt[4]), "fused": bool(cnt[5])})
 
     def _predict_bins(self, bins_cols):
         """Raw score from binned features (feature-major [F, N])."""
@@ -335,8 +349,9 @@ class Booster:
             pass
 
 
-def train(params, train_set, num_boost_round=100):
-    """lightgbm_rs.train (engine.py:254): boosting on the device for num_boost_round."""
+def train(params, train_set, num_boost_round=100, comm=None):
+    """lightgbm_rs.train (engine.py:254): boosting on the device for num_boost_round.
+    With comm (distributed.Communicator), data-parallel over the ranks' row shards."""
     p = dict(params or {})
     for k in ("num_iterations", "num_iteration", "n_iter", "num_tree", "num_trees",
               "num_round", "num_rounds", "num_boost_round", "n_estimators"):
@@ -344,6 +359,6 @@ def train(params, train_set, num_boost_round=100):
             num_boost_round = int(p.pop(k))
     if isinstance(train_set, Dataset) and train_set.params != _resolve(p):
         train_set.params.update(_resolve(p))
-    b = Booster(p, train_set)
+    b = Booster(p, train_set, comm=comm)
     b.update(int(num_boost_round))
     return b

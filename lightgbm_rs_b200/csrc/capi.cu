@@ -5,6 +5,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <limits>
 #include <memory>
 #include <mutex>
@@ -12,6 +13,8 @@
 #include <vector>
 
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>  // types only: the library is loaded at run time
 
 #include "binning.h"
 #include "common.cuh"
@@ -431,6 +434,86 @@ int read_tree(lgbm_b200_learner* l, lgbm_b200_tree* out) {
 }  // namespace
 
 // ----------------------------------------------------------------------------------
+// Data-parallel communicator: NCCL, loaded at run time so that single-GPU use needs no
+// NCCL library. Reductions run on the booster's stream and are captured into its graph.
+// ----------------------------------------------------------------------------------
+
+namespace {
+
+struct NcclApi {
+  bool ok = false;
+  std::string error;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+// The NCCL already in the process (e.g. the one a framework loaded) is used as is, so
+// that one process never holds two NCCL builds under one soname; else the library named
+// by LGBM_B200_NCCL_LIBRARY, else libnccl.so.2 from the loader's search path. It is
+// loaded RTLD_LOCAL, so its symbols do not bind other libraries' NCCL references.
+NcclApi load_nccl() {
+  NcclApi a;
+  void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+  if (!h) {
+    const char* path = std::getenv("LGBM_B200_NCCL_LIBRARY");
+    h = dlopen(path && *path ? path : "libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+  }
+  if (!h) {
+    a.error = std::string("cannot load libnccl.so.2: ") + dlerror();
+    return a;
+  }
+  auto sym = [&](const char* name) -> void* { return dlsym(h, name); };
+  a.GetUniqueId = reinterpret_cast<decltype(a.GetUniqueId)>(sym("ncclGetUniqueId"));
+  a.CommInitRank = reinterpret_cast<decltype(a.CommInitRank)>(sym("ncclCommInitRank"));
+  a.CommDestroy = reinterpret_cast<decltype(a.CommDestroy)>(sym("ncclCommDestroy"));
+  a.AllReduce = reinterpret_cast<decltype(a.AllReduce)>(sym("ncclAllReduce"));
+  a.AllGather = reinterpret_cast<decltype(a.AllGather)>(sym("ncclAllGather"));
+  a.GetErrorString = reinterpret_cast<decltype(a.GetErrorString)>(sym("ncclGetErrorString"));
+  a.ok = a.GetUniqueId && a.CommInitRank && a.CommDestroy && a.AllReduce && a.AllGather &&
+         a.GetErrorString;
+  if (!a.ok) a.error = "libnccl.so.2 lacks an expected symbol";
+  return a;
+}
+
+NcclApi& nccl() {
+  static NcclApi api = load_nccl();
+  return api;
+}
+
+}  // namespace
+
+struct lgbm_b200_comm {
+  int device = 0;
+  int nranks = 1;
+  int rank = 0;
+  ncclComm_t comm = nullptr;
+  ncclResult_t first_error = ncclSuccess;  // first failure of an enqueued reduction
+  DeviceComm dev{};
+
+  void note(ncclResult_t r) {
+    if (r != ncclSuccess && first_error == ncclSuccess) first_error = r;
+  }
+  static void sum_i64(void* ctx, long long* buf, int64_t n, cudaStream_t st) {
+    auto* c = static_cast<lgbm_b200_comm*>(ctx);
+    c->note(nccl().AllReduce(buf, buf, (size_t)n, ncclInt64, ncclSum, c->comm, st));
+  }
+  static void max_u32(void* ctx, uint32_t* buf, int64_t n, cudaStream_t st) {
+    auto* c = static_cast<lgbm_b200_comm*>(ctx);
+    c->note(nccl().AllReduce(buf, buf, (size_t)n, ncclUint32, ncclMax, c->comm, st));
+  }
+  static void min_u32(void* ctx, uint32_t* buf, int64_t n, cudaStream_t st) {
+    auto* c = static_cast<lgbm_b200_comm*>(ctx);
+    c->note(nccl().AllReduce(buf, buf, (size_t)n, ncclUint32, ncclMin, c->comm, st));
+  }
+};
+
+// ----------------------------------------------------------------------------------
 // Booster
 // ----------------------------------------------------------------------------------
 
@@ -455,6 +538,8 @@ struct lgbm_b200_booster {
   cudaGraphExec_t graph_exec = nullptr;
   cudaGraph_t graph = nullptr;
   float last_ms = 0.f;
+  lgbm_b200_comm* comm = nullptr;  // data-parallel job (null: one device)
+  const DeviceComm* dcomm() const { return comm ? &comm->dev : nullptr; }
 
   int ensure_capacity(int32_t need);
   void destroy_graph() {
@@ -1060,6 +1145,7 @@ int lgbm_b200_learner_grow_tree(lgbm_b200_learner* l, int32_t gh_kind, const voi
           nullptr);
   ObjDev o{};
   o.N = N;
+  o.n_global = N;
   o.gh_mode = mode;
   o.gh = l->gh.p;
   o.ghp = l->ghp.p;
@@ -1086,8 +1172,53 @@ int lgbm_b200_learner_grow_tree(lgbm_b200_learner* l, int32_t gh_kind, const voi
   return LGBM_B200_OK;
 }
 
-int lgbm_b200_booster_create(lgbm_b200_dataset* ds, const float* labels,
-                             const lgbm_b200_train_config* cfg, lgbm_b200_booster** out) {
+}  // extern "C"
+
+namespace {
+
+// All ranks' labels in global row order (shards in rank order), gathered once so that
+// the init score is computed exactly as on one device.
+int gather_labels(lgbm_b200_comm* comm, const float* labels, int64_t n_local, cudaStream_t st,
+                  std::vector<float>* all) {
+  const int R = comm->nranks;
+  DevBuf<long long> cnt;
+  CUDA_TRY(cnt.alloc((size_t)R + 1));
+  long long mine = n_local;
+  CUDA_TRY(cudaMemcpy(cnt.p + R, &mine, 8, cudaMemcpyHostToDevice));
+  ncclResult_t r = nccl().AllGather(cnt.p + R, cnt.p, 1, ncclInt64, comm->comm, st);
+  if (r != ncclSuccess)
+    return fail(LGBM_B200_RUNTIME, "NCCL all-gather failed: %s", nccl().GetErrorString(r));
+  std::vector<long long> counts(R);
+  CUDA_TRY(cudaStreamSynchronize(st));
+  CUDA_TRY(cudaMemcpy(counts.data(), cnt.p, 8 * (size_t)R, cudaMemcpyDeviceToHost));
+  long long mx = 0, total = 0;
+  for (long long c : counts) {
+    mx = std::max(mx, c);
+    total += c;
+  }
+  DevBuf<float> send, recv;
+  CUDA_TRY(send.alloc((size_t)std::max(mx, 1ll)));
+  CUDA_TRY(recv.alloc((size_t)std::max(mx, 1ll) * R));
+  CUDA_TRY(cudaMemset(send.p, 0, (size_t)std::max(mx, 1ll) * 4));
+  if (n_local > 0)
+    CUDA_TRY(cudaMemcpy(send.p, labels, (size_t)n_local * 4, cudaMemcpyHostToDevice));
+  r = nccl().AllGather(send.p, recv.p, (size_t)std::max(mx, 1ll), ncclFloat32, comm->comm, st);
+  if (r != ncclSuccess)
+    return fail(LGBM_B200_RUNTIME, "NCCL all-gather failed: %s", nccl().GetErrorString(r));
+  std::vector<float> padded((size_t)std::max(mx, 1ll) * R);
+  CUDA_TRY(cudaStreamSynchronize(st));
+  CUDA_TRY(cudaMemcpy(padded.data(), recv.p, padded.size() * 4, cudaMemcpyDeviceToHost));
+  all->clear();
+  all->reserve((size_t)total);
+  for (int k = 0; k < R; ++k)
+    all->insert(all->end(), padded.begin() + (size_t)k * std::max(mx, 1ll),
+                padded.begin() + (size_t)k * std::max(mx, 1ll) + counts[k]);
+  return LGBM_B200_OK;
+}
+
+int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
+                        const lgbm_b200_train_config* cfg, lgbm_b200_comm* comm,
+                        lgbm_b200_booster** out) {
   if (!ds || !labels || !cfg || !out)
     return fail(LGBM_B200_INVALID_ARGUMENT, "booster_create: null argument");
   *out = nullptr;
@@ -1119,21 +1250,34 @@ int lgbm_b200_booster_create(lgbm_b200_dataset* ds, const float* labels,
   CUDA_TRY(cudaMemset(b->ghp.p, 0, sizeof(DevGhParams)));
   CUDA_TRY(cudaMemset(b->state.p, 0, 8));
   CUDA_TRY(cudaMemcpy(b->label.p, labels, N * 4, cudaMemcpyHostToDevice));
+  // the labels of every row of the job: this device's, or all ranks' in row order
+  std::vector<float> gathered;
+  const float* all = labels;
+  int64_t NG = N;
+  if (comm) {
+    rc = gather_labels(comm, labels, N, b->learner->stream, &gathered);
+    if (rc) return rc;
+    all = gathered.data();
+    NG = (int64_t)gathered.size();
+    if (NG > (int64_t)INT32_MAX)
+      return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "%lld rows in the job: more than 2^31 - 1",
+                  (long long)NG);
+  }
   // boost_from_average (gbdt.rs:619-639): init score on the host from the labels.
   double init = 0.0;
   if (cfg->boost_from_average) {
     const double eps = (double)1e-15f;
     if (cfg->objective == LGBM_B200_OBJECTIVE_BINARY) {
       double suml = 0.0;
-      for (int64_t i = 0; i < N; ++i) suml += labels[i] > 0.0f ? 1.0 : 0.0;
-      double pavg = suml / (double)N;  // binary.rs:178-194
+      for (int64_t i = 0; i < NG; ++i) suml += all[i] > 0.0f ? 1.0 : 0.0;
+      double pavg = suml / (double)NG;  // binary.rs:178-194
       pavg = std::min(pavg, 1.0 - eps);
       pavg = std::max(pavg, eps);
       init = std::log(pavg / (1.0 - pavg)) / cfg->sigmoid;
     } else {
       double s = 0.0;  // regression.rs:563-577
-      for (int64_t i = 0; i < N; ++i) s += (double)labels[i];
-      init = s / (double)N;
+      for (int64_t i = 0; i < NG; ++i) s += (double)all[i];
+      init = s / (double)NG;
     }
   }
   b->init_score = init;
@@ -1143,8 +1287,11 @@ int lgbm_b200_booster_create(lgbm_b200_dataset* ds, const float* labels,
   }
   b->learner->bind(mode == GH_FLOAT ? (const void*)b->gh.p : (const void*)(b->gh.p + 8 * N),
                    b->ghp.p, b->state.p);
+  b->learner->d.n_global = NG;
+  b->comm = comm;
   ObjDev& o = b->obj;
   o.N = N;
+  o.n_global = NG;
   o.objective = cfg->objective;
   o.gh_mode = mode;
   o.sigmoid = cfg->sigmoid;
@@ -1161,6 +1308,70 @@ int lgbm_b200_booster_create(lgbm_b200_dataset* ds, const float* labels,
   f.score = b->score.p;
   *out = b.release();
   return LGBM_B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lgbm_b200_booster_create(lgbm_b200_dataset* ds, const float* labels,
+                             const lgbm_b200_train_config* cfg, lgbm_b200_booster** out) {
+  return booster_create_impl(ds, labels, cfg, nullptr, out);
+}
+
+int lgbm_b200_comm_unique_id(uint8_t* id_out) {
+  if (!id_out) return fail(LGBM_B200_INVALID_ARGUMENT, "comm_unique_id: null argument");
+  if (!nccl().ok) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "%s", nccl().error.c_str());
+  ncclUniqueId id;
+  const ncclResult_t r = nccl().GetUniqueId(&id);
+  if (r != ncclSuccess)
+    return fail(LGBM_B200_RUNTIME, "ncclGetUniqueId: %s", nccl().GetErrorString(r));
+  std::memcpy(id_out, id.internal, LGBM_B200_COMM_ID_BYTES);
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_comm_create(int32_t device, int32_t nranks, int32_t rank, const uint8_t* id,
+                          lgbm_b200_comm** out) {
+  if (!id || !out || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "comm_create: rank %d of %d", rank, nranks);
+  *out = nullptr;
+  if (!nccl().ok) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "%s", nccl().error.c_str());
+  if (!have_device()) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "no CUDA device");
+  DeviceGuard g(device);
+  auto c = std::make_unique<lgbm_b200_comm>();
+  c->device = device;
+  c->nranks = nranks;
+  c->rank = rank;
+  ncclUniqueId uid;
+  std::memcpy(uid.internal, id, LGBM_B200_COMM_ID_BYTES);
+  const ncclResult_t r = nccl().CommInitRank(&c->comm, nranks, uid, rank);
+  if (r != ncclSuccess)
+    return fail(LGBM_B200_RUNTIME, "ncclCommInitRank: %s", nccl().GetErrorString(r));
+  c->dev.ctx = c.get();
+  c->dev.sum_i64 = &lgbm_b200_comm::sum_i64;
+  c->dev.max_u32 = &lgbm_b200_comm::max_u32;
+  c->dev.min_u32 = &lgbm_b200_comm::min_u32;
+  *out = c.release();
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_comm_destroy(lgbm_b200_comm* comm) {
+  if (comm) {
+    DeviceGuard g(comm->device);
+    if (comm->comm) nccl().CommDestroy(comm->comm);
+    delete comm;
+  }
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_create_distributed(lgbm_b200_dataset* ds, const float* labels,
+                                         const lgbm_b200_train_config* cfg,
+                                         lgbm_b200_comm* comm, lgbm_b200_booster** out) {
+  if (!comm) return fail(LGBM_B200_INVALID_ARGUMENT, "booster_create_distributed: null comm");
+  if (ds && ds->device != comm->device)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "dataset on device %d, communicator on device %d",
+                ds->device, comm->device);
+  return booster_create_impl(ds, labels, cfg, comm, out);
 }
 
 int lgbm_b200_booster_destroy(lgbm_b200_booster* b) {
@@ -1183,8 +1394,9 @@ int lgbm_b200_booster_train(lgbm_b200_booster* b, int32_t num_iterations, int32_
   cudaStream_t st = b->learner->stream;
   if (!b->graph_exec) {
     CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    launch_gradients(b->obj, st);
-    launch_tree(b->learner->d, b->learner->build_blocks, b->learner->build_smem, st);
+    launch_gradients(b->obj, st, nullptr, b->dcomm());
+    launch_tree(b->learner->d, b->learner->build_blocks, b->learner->build_smem, st, nullptr,
+                b->dcomm());
     launch_finish_iteration(b->learner->d, b->fin, st);
     cudaError_t e = cudaStreamEndCapture(st, &b->graph);
     if (e != cudaSuccess)
@@ -1201,6 +1413,9 @@ int lgbm_b200_booster_train(lgbm_b200_booster* b, int32_t num_iterations, int32_
   cudaEventElapsedTime(&b->last_ms, e0, e1);
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
+  if (b->comm && b->comm->first_error != ncclSuccess)
+    return fail(LGBM_B200_RUNTIME, "NCCL reduction failed: %s",
+                nccl().GetErrorString(b->comm->first_error));
   int32_t after[2];
   CUDA_TRY(cudaMemcpy(after, b->state.p, 8, cudaMemcpyDeviceToHost));
   GrowCtrl c;
@@ -1300,8 +1515,9 @@ int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
   prof.cls = cls.data();
   prof.cap = cap;
   prof.n = 0;
-  launch_gradients(b->obj, st, &prof);
-  launch_tree(b->learner->d, b->learner->build_blocks, b->learner->build_smem, st, &prof);
+  launch_gradients(b->obj, st, &prof, b->dcomm());
+  launch_tree(b->learner->d, b->learner->build_blocks, b->learner->build_smem, st, &prof,
+              b->dcomm());
   launch_finish_iteration(b->learner->d, b->fin, st, &prof);
   cudaError_t le = cudaGetLastError();
   cudaError_t se = cudaStreamSynchronize(st);
@@ -1327,6 +1543,8 @@ int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
   counts_out[1] = c.num_builds;
   counts_out[2] = c.rows_built;
   counts_out[3] = c.num_splits;
+  counts_out[4] = c.rows_parted;
+  counts_out[5] = b->learner->d.fused;
   return LGBM_B200_OK;
 }
 

@@ -333,8 +333,6 @@ __device__ __forceinline__ Q4Mask q4_mask(const uint32_t* s_mask, int nf) {
 template <int SHIFT, int NCH>
 __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase) {
   extern __shared__ uint32_t sm[];
-  __shared__ int32_t s_nb[128];
-  __shared__ int32_t s_boff[128];
   __shared__ uint32_t s_mask[4];
   const BuildTarget t = build_target(d, phase);
   build_account(d, phase, t);
@@ -381,11 +379,6 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase
   // (learner.rs:2003-2020 build mask).
   const bool sub = t.mask_leaf >= 0;
   const uint8_t* ps = d.splittable + (size_t)(sub ? t.mask_leaf : 0) * d.F + grp.f_begin;
-  for (int fl = threadIdx.x; fl < nf; fl += blockDim.x) {
-    const DevFeature ft = d.feat[grp.f_begin + fl];
-    s_nb[fl] = ft.num_bin;
-    s_boff[fl] = ft.bin_off;
-  }
   if (threadIdx.x < 4) {
     uint32_t m = 0;
     for (int b = 0; b < 32; ++b) {
@@ -442,14 +435,18 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase
   for (int s = threadIdx.x; s < cap; s += kQ4Threads) {
     const int fl = s >> SHIFT;
     const int bin = s & ((1 << SHIFT) - 1);
-    if (fl >= nf || bin >= s_nb[fl]) continue;
+    if (fl >= nf) continue;
+    // feature tables are read from global memory here: with no static shared arrays the
+    // CTA's shared footprint lets two CTAs share an SM
+    const DevFeature* fp = d.feat + grp.f_begin + fl;
+    if (bin >= __ldg(&fp->num_bin)) continue;
     const int32_t v = (int32_t)hot[s];
     const int32_t lo = (int32_t)(int16_t)(v & 0xffff);
     const long long g = (folds ? (long long)cold_g[s] : 0ll) + lo;
     const long long qsum = (folds ? (long long)cold_q[s] : 0ll) + ((v - lo) >> 16);
     const long long n3 = (long long)c3[s];
     const long long h = (qsum - 3 * n3) | (n3 << 32);
-    const size_t gb = (size_t)(s_boff[fl] + bin);
+    const size_t gb = (size_t)(__ldg(&fp->bin_off) + bin);
     if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb]), (unsigned long long)g);
     if (h)
       atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb + 1]), (unsigned long long)h);
@@ -1242,6 +1239,7 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
   __shared__ ScanScratch s_scan[4];
   __shared__ ScanCand s_cand[4];
   __shared__ Prep s_prep;
+  __shared__ double s_fix[2 * kMaxBins / 32][3];  // per-warp exact sums for FixHistogram
   __shared__ bool s_last;
   const int f = blockIdx.x;
   const int tid = threadIdx.x;
@@ -1289,15 +1287,76 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
         s_hist[0][tid] = v;
       }
       __syncthreads();
-      // FixHistogram (fix_histogram.rs:50-81): sequential ascending subtraction.
+      // FixHistogram (fix_histogram.rs:50-81): the most-frequent-bin cell becomes the leaf
+      // sum minus the other cells, subtracted in ascending order. With quantized
+      // gradients every cell is an exact multiple of one unit u. When every partial
+      // result of that chain is representable (checked below from exact sums) each
+      // subtraction is exact, so the chain equals sum - (other cells summed in any
+      // order). Otherwise the sequential chain runs.
       const int mfb = ft.most_freq_bin;
-      if (buildable && mfb > 0 && mfb < nb && (tid == 0 || tid == 32)) {
+      if (buildable && mfb > 0 && mfb < nb) {
         const int w = tid == 0 ? 0 : 1;
-        double acc = w == 0 ? lss.sum_g : lss.sum_h;
-        const double* hv = &s_hist[0][w];
-        acc = seq_sub(hv, 2, mfb, acc);
-        acc = seq_sub(hv + 2 * (mfb + 1), 2, nb - mfb - 1, acc);
-        s_hist[0][2 * mfb + w] = acc;
+        bool fast = false;
+        double fixed = 0.0;
+        if (p.mode != GH_FLOAT) {
+          double xg = 0.0, xh = 0.0, ag = 0.0;
+          if (mine && (tid >> 1) != mfb) {
+            if (tid & 1) {
+              xh = s_hist[0][tid];
+            } else {
+              xg = s_hist[0][tid];
+              ag = fabs(xg);
+            }
+          }
+          // exact in any order: partial sums are multiples of u below 2^53 u (checked)
+          for (int o = 16; o > 0; o >>= 1) {
+            xg += __shfl_xor_sync(0xffffffffu, xg, o);
+            xh += __shfl_xor_sync(0xffffffffu, xh, o);
+            ag += __shfl_xor_sync(0xffffffffu, ag, o);
+          }
+          if ((tid & 31) == 0 && tid < 2 * kMaxBins) {
+            s_fix[tid >> 5][0] = xg;
+            s_fix[tid >> 5][1] = xh;
+            s_fix[tid >> 5][2] = ag;
+          }
+          __syncthreads();
+          if (tid == 0 || tid == 32) {
+            const int nw = (2 * nb + 31) >> 5;
+            double cs = 0.0, as = 0.0;
+            for (int k = 0; k < nw; ++k) {
+              cs += s_fix[k][w];
+              as += s_fix[k][2];
+            }
+            const double unit = w == 0 ? p.unit_g : p.unit_h;
+            double u = unit;
+            if (p.mode == GH_QPACK) {  // the f32 level's ulp divides every level
+              int e = 0;
+              frexp(unit, &e);
+              u = ldexp(1.0, e - 24);
+            }
+            const double sum = w == 0 ? lss.sum_g : lss.sum_h;
+            const double lim = ldexp(u, 52);
+            if (unit > 0.0) {
+              if (w == 0) {
+                const double m = sum / u;  // power-of-two division: exact
+                fast = m == trunc(m) && fabs(sum) + as < lim;
+              } else {
+                fast = sum >= 0.0 && cs <= 2.0 * sum && sum < lim;
+              }
+            }
+            fixed = sum - cs;
+          }
+        }
+        if ((tid == 0 || tid == 32)) {
+          if (!fast) {
+            double acc = w == 0 ? lss.sum_g : lss.sum_h;
+            const double* hv = &s_hist[0][w];
+            acc = seq_sub(hv, 2, mfb, acc);
+            acc = seq_sub(hv + 2 * (mfb + 1), 2, nb - mfb - 1, acc);
+            fixed = acc;
+          }
+          s_hist[0][2 * mfb + w] = fixed;
+        }
       }
       __syncthreads();
       // compact_histogram (learner.rs:4460-4486)
@@ -1961,10 +2020,11 @@ size_t fused_partition_smem() { return (size_t)4 * sizeof(uint32_t) * kQ4MaxCell
 
 // One tree: root build, then per split the control step + scans (k_fixscan) and the
 // partition, which in the fused mode also accumulates one child's histogram (else a
-// build kernel follows). `exchange`, when set, sums the accumulated child (d.raw,
-// raw_len cells + the left count) over all devices after every build.
+// build kernel follows). With several devices the accumulated child (d.raw: raw_len
+// integer cells + the left-row count) is summed over them after every build, so every
+// device takes the same decisions.
 void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStream_t st,
-                 LaunchProfiler* prof, const TreeExchange* exchange) {
+                 LaunchProfiler* prof, const DeviceComm* comm) {
   const int sms = num_sms();
   {
     PROF_BEGIN(KC_INIT);
@@ -1984,7 +2044,7 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
     PROF_END();
   };
   auto exchange_raw = [&]() {
-    if (exchange && exchange->fn) exchange->fn(exchange->ctx, d.raw, d.raw_len + 1, st);
+    if (comm) comm->sum_i64(comm->ctx, d.raw, (int64_t)d.raw_len + 1, st);
   };
   build(0);
   exchange_raw();

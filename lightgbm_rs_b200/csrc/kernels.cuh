@@ -100,23 +100,26 @@ struct LaunchProfiler {
   void end(cudaStream_t st, int slot);
 };
 
-// Sum of the accumulated child histogram over devices, enqueued on the tree's stream
-// after every build (data-parallel training); fn(ctx, buf, count, stream) sums `count`
-// int64 cells in place.
-struct TreeExchange {
-  void (*fn)(void* ctx, long long* buf, int64_t count, cudaStream_t st);
+// Reductions over the devices of a data-parallel job, enqueued on the caller's stream
+// (and captured into its CUDA graph). Every device issues the same calls in the same
+// order. A null DeviceComm means one device.
+struct DeviceComm {
   void* ctx;
+  void (*sum_i64)(void* ctx, long long* buf, int64_t n, cudaStream_t st);
+  void (*max_u32)(void* ctx, uint32_t* buf, int64_t n, cudaStream_t st);
+  void (*min_u32)(void* ctx, uint32_t* buf, int64_t n, cudaStream_t st);
 };
 
 // Host-side launch helpers (kernels.cu).
 void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStream_t st,
-                 LaunchProfiler* prof = nullptr, const TreeExchange* exchange = nullptr);
+                 LaunchProfiler* prof = nullptr, const DeviceComm* comm = nullptr);
 bool fused_partition_supported(int gh_mode, int num_groups, int shift, int nch);
 int build_smem_bytes_per_bin(int gh_mode);
 
 // Objective / score kernels (objective.cu).
 struct ObjDev {
-  int64_t N;
+  int64_t N;         // rows on this device
+  int64_t n_global;  // rows on all devices
   int32_t objective;  // 0 binary, 1 l2
   int32_t gh_mode;
   double sigmoid;
@@ -127,7 +130,8 @@ struct ObjDev {
   int32_t num_quant_bins;
   const int32_t* stopped;
 };
-void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof = nullptr);
+void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof = nullptr,
+                      const DeviceComm* comm = nullptr);
 
 // Per-iteration tree finish: shrinkage + score update + tree record.
 struct FinishDev {

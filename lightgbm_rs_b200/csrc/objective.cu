@@ -114,7 +114,7 @@ __global__ void k_gh_scales(ObjDev o) {
   p->root_h = 0;
   if (o.gh_mode == GH_FLOAT) {
     int lg = 0;
-    while (lg < 62 && ((int64_t)1 << lg) < o.N) ++lg;
+    while (lg < 62 && ((int64_t)1 << lg) < o.n_global) ++lg;
     auto kscale = [&](double m) -> int {
       if (!(m > 0.0) || !isfinite(m)) return 0;
       int e;
@@ -363,16 +363,25 @@ int num_sms_obj() {
 
 }  // namespace
 
-void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof) {
+// With several devices: the scales come from the maxima over all devices' rows, and the
+// root sums are summed over devices (integers, so exact in any order).
+void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof,
+                      const DeviceComm* comm) {
   const int grid = num_sms_obj() * 8;
   const int slot = prof ? prof->begin(st, KC_GRAD) : -1;
   k_gh_reset<<<1, 1, 0, st>>>(o.ghp, o.stopped);
   k_grad_pass1<<<grid, kObjThreads, 0, st>>>(o);
+  if (comm) {
+    comm->max_u32(comm->ctx, &o.ghp->max_abs_g_bits, 2, st);
+    comm->min_u32(comm->ctx, &o.ghp->min_h_key, 1, st);
+    comm->max_u32(comm->ctx, &o.ghp->max_h_key, 1, st);
+  }
   k_gh_scales<<<1, 1, 0, st>>>(o);
   if (o.gh_mode == GH_FLOAT)
     k_root_sums_float<<<grid, kObjThreads, 0, st>>>(o);
   else
     k_quantize<<<grid, kObjThreads, 0, st>>>(o);
+  if (comm) comm->sum_i64(comm->ctx, &o.ghp->root_g, 2, st);
   if (prof) prof->end(st, slot);
 }
 

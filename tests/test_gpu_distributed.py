@@ -1,0 +1,96 @@
+"""Data-parallel training on 2 GPUs (one spawned process per GPU) against one GPU.
+
+Quantized gradients: trees and scores of every rank must be bit-identical to training
+on all rows on one GPU. f32 gradients: same tree structure, scores within 1e-9.
+Needs at least 2 GPUs; never runs two ranks on one GPU.
+"""
+
+import multiprocessing as mp
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+PARAMS = {"objective": "binary", "num_leaves": 31, "min_data_in_leaf": 20,
+          "learning_rate": 0.1, "max_bin": 255}
+ROWS = 50_001
+ITERS = 5
+
+
+def _data():
+    import lightgbm_rs_b200 as lgb
+    from lightgbm_rs_b200 import synthetic
+
+    X, y = synthetic.binary_c0(num_data=ROWS, seed=7)
+    return lgb.Dataset(X, y, dict(PARAMS))  # host binning only, deterministic
+
+
+def _worker(rank, world, uid, quantized, q):
+    try:
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        import lightgbm_rs_b200 as lgb
+        from lightgbm_rs_b200 import distributed as D
+
+        full = _data()
+        b, e = D.shard_range(full.num_data, world, rank)
+        p = dict(PARAMS, device=rank, use_quantized_grad=quantized, num_grad_quant_bins=4)
+        shard = lgb.Dataset(bins=full.bins[:, b:e], mappers=full.mappers,
+                            label=full.label[b:e], params=p)
+        comm = D.Communicator(rank, world, rank, uid)
+        booster = lgb.train(p, shard, num_boost_round=ITERS, comm=comm)
+        q.put((rank, booster.trees(), booster.train_scores()))
+        del booster
+        comm.close()
+    except Exception as ex:
+        q.put((rank, "error", repr(ex)))
+
+
+@pytest.mark.parametrize("quantized", [True, False])
+def test_two_gpus_match_one(quantized):
+    import lightgbm_rs_b200 as lgb
+    from lightgbm_rs_b200 import distributed as D
+
+    if lgb._lib.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    uid = D.unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, uid, quantized, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(2):
+            r = q.get(timeout=300)
+            out[r[0]] = r
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(2):
+        assert out[r][1] != "error", out[r]
+    full = _data()
+    p = dict(PARAMS, use_quantized_grad=quantized, num_grad_quant_bins=4)
+    ref = lgb.train(p, full, num_boost_round=ITERS)
+    want_trees, want_scores = ref.trees(), ref.train_scores()
+    scores = np.concatenate([out[0][2], out[1][2]])
+    for r in range(2):
+        trees = out[r][1]
+        assert len(trees) == len(want_trees)
+        for a, b in zip(trees, want_trees):
+            for k in ("split_feature", "threshold_bin", "left_child", "right_child",
+                      "leaf_count", "internal_count"):
+                assert a[k].tolist() == b[k].tolist(), (r, k)
+            if quantized:
+                assert a["leaf_value"].tobytes() == b["leaf_value"].tobytes()
+            else:
+                np.testing.assert_allclose(a["leaf_value"], b["leaf_value"], rtol=1e-9)
+    if quantized:
+        assert scores.view(np.uint64).tolist() == want_scores.view(np.uint64).tolist()
+    else:
+        np.testing.assert_allclose(scores, want_scores, rtol=0, atol=1e-9)
