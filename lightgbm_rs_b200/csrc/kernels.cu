@@ -27,6 +27,7 @@ constexpr int kPartTile = kPartThreads * kPartItems;
 static_assert(kPartTile == kPartitionTileRows, "partition tile size is part of the host contract");
 constexpr long long kSpinLimit = 1ll << 22;
 
+
 __device__ __forceinline__ bool leaf_buildable(const DevLeafSplits& l) {
   return l.sum_h > 0.0 && l.num_data > 0;  // learner.rs:2477-2481
 }
@@ -1047,6 +1048,7 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   P.lsLg = ls_larger;
 }
 
+// Writes of the control step except the control block itself.
 __device__ void prep_commit(const GrowDev& d, const Prep& P) {
   if (P.applied) {
     const int32_t leaf = P.leaf, nr = P.nr, node = P.node;
@@ -1095,7 +1097,6 @@ __device__ void prep_commit(const GrowDev& d, const Prep& P) {
   if (P.kill1 >= 0) d.best[P.kill1].gain = kNegInf;
   if (P.slot_leaf0 >= 0) d.slot_of_leaf[P.slot_leaf0] = P.slot_val0;
   if (P.slot_leaf1 >= 0) d.slot_of_leaf[P.slot_leaf1] = P.slot_val1;
-  *d.ctrl = P.c;
 }
 
 // The control step alone: applies the tree's last split.
@@ -1104,6 +1105,7 @@ __global__ void k_prepare(GrowDev d, int s) {
   Prep P;
   prep_compute(d, s, P);
   prep_commit(d, P);
+  *d.ctrl = P.c;
 }
 
 // ------------------------------------------------------------------------------------
@@ -1139,109 +1141,106 @@ __device__ __forceinline__ void warp_argmax(Cand& c) {
   }
 }
 
-// Block-wide argmax of NC candidates per thread under cand_better (two shuffle levels);
-// the results are valid in every thread.
-template <int NC>
-__device__ void block_argmax(Cand (&c)[NC]) {
-  __shared__ Cand s_c[NC][32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nw = (blockDim.x + 31) >> 5;
-#pragma unroll
-  for (int j = 0; j < NC; ++j) warp_argmax(c[j]);
-  __syncthreads();
-  if (lane == 0)
-#pragma unroll
-    for (int j = 0; j < NC; ++j) s_c[j][warp] = c[j];
-  __syncthreads();
-  if (warp == 0) {
-#pragma unroll
-    for (int j = 0; j < NC; ++j) {
-      Cand x = lane < nw ? s_c[j][lane] : Cand{kNegInf, -1, 0x7fffffff};
-      warp_argmax(x);
-      if (lane == 0) s_c[j][0] = x;
-    }
+// Best split among the leaves a control step leaves alone: the arg_max inputs of
+// learner.rs:4537-4551 other than the leaves being scanned (the two children of the
+// applied split, or the root), by one warp. Their best splits are final before the
+// step starts, so this runs concurrently with the control step itself.
+__device__ Cand other_leaves_best(const GrowDev& d) {
+  const GrowCtrl* c = d.ctrl;
+  const int lane = threadIdx.x & 31;
+  int32_t ex0 = 0, ex1 = -1;
+  if (c->pending) {
+    ex0 = c->split_leaf;
+    ex1 = c->num_leaves;
   }
-  __syncthreads();
-#pragma unroll
-  for (int j = 0; j < NC; ++j) c[j] = s_c[j][0];
-}
-
-__device__ void pick_split(const GrowDev& d) {
-  GrowCtrl* c = d.ctrl;
-  const int tid = threadIdx.x;
-  __shared__ DevSplitInfo s_win[2];
-  const int32_t S = c->smaller_leaf, Lg = c->larger_leaf;
-  const bool find = c->do_find != 0;
-  // the other leaves' current best (learner.rs:4537-4551 arg_max inputs), prefetched;
-  // the two leaves scanned now join below with their new values
   Cand lc{kNegInf, -1, 0x7fffffff};
-  for (int i = tid; i < d.L; i += blockDim.x) {
-    if (find && (i == S || i == Lg)) continue;
+  for (int i = lane; i < d.L; i += 32) {
+    if (i == ex0 || i == ex1) continue;
     const Cand x{__ldcg(&d.best[i].gain), __ldcg(&d.best_feature[i]), i};
     if (lc.i == 0x7fffffff || cand_better(x.g, x.f, x.i, lc.g, lc.f, lc.i)) lc = x;
   }
+  warp_argmax(lc);
+  return lc;
+}
+
+// Outcome of the pick at the end of a control step.
+struct PickOut {
+  DevSplitInfo si[2];  // best split of the smaller / larger scanned leaf
+  int32_t bf[2];       // its feature (-1: none)
+  int32_t done;        // no leaf has a positive gain: the tree is finished
+  int32_t leaf, feature, build_left;
+  DevSplitInfo split;  // the split to apply next
+};
+
+// Cross-feature argmax of both scanned leaves (learner.rs:3314-3321) and the arg_max
+// over all leaves (learner.rs:4537-4551, first max under split_gt, learner.rs:1503-1505
+// stop rule), by one warp: the feature candidates are reduced with shuffles only.
+__device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand& other, PickOut& o) {
+  const int lane = threadIdx.x & 31;
+  const bool find = P.live != 0;
+  const int32_t S = P.S, Lg = P.Lg;
+  Cand best = other;
   if (find) {
-    // cross-feature argmax of both scanned leaves at once (learner.rs:3314-3321)
     const bool ok0 = __ldcg(&d.scan_ok[0]) != 0;
     const bool ok1 = Lg >= 0 && __ldcg(&d.scan_ok[1]) != 0;
-    Cand fc[2] = {{kNegInf, -1, -1}, {kNegInf, -1, -1}};
-    for (int f = tid; f < d.F; f += blockDim.x) {
+    Cand f0{kNegInf, -1, -1}, f1{kNegInf, -1, -1};
+    for (int f = lane; f < d.F; f += 32) {
       const double g0 = __ldcg(&d.scan_out[f].gain);
       const double g1 = Lg >= 0 ? __ldcg(&d.scan_out[d.F + f].gain) : kNegInf;
       if (ok0) d.splittable[(size_t)S * d.F + f] = g0 > kNegInf ? 1 : 0;
       if (ok1) d.splittable[(size_t)Lg * d.F + f] = g1 > kNegInf ? 1 : 0;
-      if (g0 > kNegInf && cand_better(g0, f, f, fc[0].g, fc[0].f, fc[0].i)) fc[0] = {g0, f, f};
-      if (g1 > kNegInf && cand_better(g1, f, f, fc[1].g, fc[1].f, fc[1].i)) fc[1] = {g1, f, f};
+      if (g0 > kNegInf && cand_better(g0, f, f, f0.g, f0.f, f0.i)) f0 = Cand{g0, f, f};
+      if (g1 > kNegInf && cand_better(g1, f, f, f1.g, f1.f, f1.i)) f1 = Cand{g1, f, f};
     }
-    block_argmax<2>(fc);
-    if (tid == 0 || tid == 32) {
-      const int sel = tid == 0 ? 0 : 1;
-      const int32_t leaf = sel == 0 ? S : Lg;
-      const bool ok = sel == 0 ? ok0 : ok1;
-      if (leaf >= 0) {
-        const int32_t bf = ok ? fc[sel].f : -1;
-        const DevSplitInfo si = bf >= 0 ? d.scan_out[sel * d.F + bf] : d_split_none();
-        d.best[leaf] = si;
-        d.best_feature[leaf] = bf;
-        s_win[sel] = si;
-      }
+    warp_argmax(f0);
+    warp_argmax(f1);
+    const int32_t bf0 = ok0 ? f0.f : -1;
+    const int32_t bf1 = ok1 ? f1.f : -1;
+    if (lane == 0) {
+      o.si[0] = bf0 >= 0 ? d.scan_out[bf0] : d_split_none();
+      o.bf[0] = bf0;
+    } else if (lane == 1) {
+      o.si[1] = (Lg >= 0 && bf1 >= 0) ? d.scan_out[d.F + bf1] : d_split_none();
+      o.bf[1] = bf1;
     }
-    if (tid == 0) {
-      const Cand a{ok0 ? fc[0].g : kNegInf, ok0 ? fc[0].f : -1, S};
-      if (lc.i == 0x7fffffff || cand_better(a.g, a.f, a.i, lc.g, lc.f, lc.i)) lc = a;
-      if (Lg >= 0) {
-        const Cand b{ok1 ? fc[1].g : kNegInf, ok1 ? fc[1].f : -1, Lg};
-        if (cand_better(b.g, b.f, b.i, lc.g, lc.f, lc.i)) lc = b;
-      }
+    const Cand a{ok0 ? f0.g : kNegInf, ok0 ? f0.f : -1, S};
+    if (best.i == 0x7fffffff || cand_better(a.g, a.f, a.i, best.g, best.f, best.i)) best = a;
+    if (Lg >= 0) {
+      const Cand b{ok1 ? f1.g : kNegInf, ok1 ? f1.f : -1, Lg};
+      if (cand_better(b.g, b.f, b.i, best.g, best.f, best.i)) best = b;
     }
   }
-  Cand w[1] = {lc};
-  block_argmax<1>(w);
-  if (tid == 0) {
-    const int32_t bl = w[0].i;
-    if (w[0].g <= 0.0 || bl == 0x7fffffff) {  // learner.rs:1503-1505
-      c->done = 1;
+  __syncwarp();
+  if (lane == 0) {
+    const int32_t bl = best.i;
+    if (best.g <= 0.0 || bl == 0x7fffffff) {
+      o.done = 1;
     } else {
-      c->pending = 1;
-      c->split_leaf = bl;
-      c->split_feature = w[0].f;
-      const DevSplitInfo si =
-          (find && bl == S) ? s_win[0] : (find && bl == Lg) ? s_win[1] : d.best[bl];
-      c->split = si;
+      o.done = 0;
+      o.leaf = bl;
+      o.feature = best.f;
+      const DevSplitInfo sp =
+          (find && bl == S) ? o.si[0] : (find && bl == Lg) ? o.si[1] : d.best[bl];
+      o.split = sp;
       // accumulate the side the scan expects to be smaller (any side is exact)
-      c->build_left = si.left_count <= si.right_count ? 1 : 0;
+      o.build_left = sp.left_count <= sp.right_count ? 1 : 0;
     }
   }
 }
 
-__global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
-  __shared__ double s_hist[2][2 * kMaxBins];
-  __shared__ ScanScratch s_scan[4];
-  __shared__ ScanCand s_cand[4];
-  __shared__ Prep s_prep;
-  __shared__ double s_fix[2 * kMaxBins / 32][3];  // per-warp exact sums for FixHistogram
-  __shared__ bool s_last;
-  const int f = blockIdx.x;
+// Shared memory of one feature's control-step work (decode, FixHistogram, scans).
+struct FixScanSmem {
+  double hist[2][2 * kMaxBins];
+  ScanScratch scan[4];
+  ScanCand cand[4];
+  double fix[2 * kMaxBins / 32][3];  // per-warp exact sums for FixHistogram
+};
+
+// Feature f of one control step (every thread of the CTA calls it): the smaller child's
+// histogram cells (accumulated by the partition, or derived from the parent), FixHistogram,
+// compaction, the larger child by subtraction, and the REVERSE/FORWARD scans of both
+// children.
+__device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanSmem& sm) {
   const int tid = threadIdx.x;
   const DevFeature ft = d.feat[f];
   const int nb = ft.num_bin;
@@ -1251,11 +1250,10 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
   // the accumulated child (its left or right rows, all devices summed); read it and
   // clear it for the next partition
   long long bv = 0;
-  if (mine) bv = d.raw[cell];
-  if (tid == 0) prep_compute(d, s, s_prep);
-  __syncthreads();
-  if (mine) d.raw[cell] = 0;
-  const Prep& P = s_prep;
+  if (mine) {
+    bv = d.raw[cell];
+    d.raw[cell] = 0;
+  }
   if (P.live) {
     const int32_t S = P.S, Lg = P.Lg;
     const bool used = !P.use_sub || d.splittable[(size_t)P.mask_leaf * d.F + f] != 0;
@@ -1284,7 +1282,7 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
           d.rawpool[cell] = bv;  // root
         }
         if (buildable) v = (tid & 1) ? decode_h(p, sv) : decode_g(p, sv);
-        s_hist[0][tid] = v;
+        sm.hist[0][tid] = v;
       }
       __syncthreads();
       // FixHistogram (fix_histogram.rs:50-81): the most-frequent-bin cell becomes the leaf
@@ -1302,9 +1300,9 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
           double xg = 0.0, xh = 0.0, ag = 0.0;
           if (mine && (tid >> 1) != mfb) {
             if (tid & 1) {
-              xh = s_hist[0][tid];
+              xh = sm.hist[0][tid];
             } else {
-              xg = s_hist[0][tid];
+              xg = sm.hist[0][tid];
               ag = fabs(xg);
             }
           }
@@ -1315,17 +1313,17 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
             ag += __shfl_xor_sync(0xffffffffu, ag, o);
           }
           if ((tid & 31) == 0 && tid < 2 * kMaxBins) {
-            s_fix[tid >> 5][0] = xg;
-            s_fix[tid >> 5][1] = xh;
-            s_fix[tid >> 5][2] = ag;
+            sm.fix[tid >> 5][0] = xg;
+            sm.fix[tid >> 5][1] = xh;
+            sm.fix[tid >> 5][2] = ag;
           }
           __syncthreads();
           if (tid == 0 || tid == 32) {
             const int nw = (2 * nb + 31) >> 5;
             double cs = 0.0, as = 0.0;
             for (int k = 0; k < nw; ++k) {
-              cs += s_fix[k][w];
-              as += s_fix[k][2];
+              cs += sm.fix[k][w];
+              as += sm.fix[k][2];
             }
             const double unit = w == 0 ? p.unit_g : p.unit_h;
             double u = unit;
@@ -1350,22 +1348,22 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
         if ((tid == 0 || tid == 32)) {
           if (!fast) {
             double acc = w == 0 ? lss.sum_g : lss.sum_h;
-            const double* hv = &s_hist[0][w];
+            const double* hv = &sm.hist[0][w];
             acc = seq_sub(hv, 2, mfb, acc);
             acc = seq_sub(hv + 2 * (mfb + 1), 2, nb - mfb - 1, acc);
             fixed = acc;
           }
-          s_hist[0][2 * mfb + w] = fixed;
+          sm.hist[0][2 * mfb + w] = fixed;
         }
       }
       __syncthreads();
       // compact_histogram (learner.rs:4460-4486)
-      double sv = mine ? s_hist[0][tid] : 0.0;
+      double sv = mine ? sm.hist[0][tid] : 0.0;
       if (ft.offset > 0) {
         const int src = tid + 2 * ft.offset;
-        sv = (mine && src < 2 * nb) ? s_hist[0][src] : 0.0;
+        sv = (mine && src < 2 * nb) ? sm.hist[0][src] : 0.0;
         __syncthreads();
-        if (mine) s_hist[0][tid] = sv;
+        if (mine) sm.hist[0][tid] = sv;
       }
       // store the smaller child's slot; larger = parent - smaller in the parent's slot
       if (mine) {
@@ -1373,7 +1371,7 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
         if (Lg >= 0) {
           const double lv = parent - sv;
           pl[tid] = lv;
-          s_hist[1][tid] = lv;
+          sm.hist[1][tid] = lv;
         }
       }
       __syncthreads();
@@ -1385,7 +1383,7 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
         const DevLeafSplits ls = sel == 0 ? P.lsS : P.lsLg;
         if (leaf_buildable(ls)) {
           ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
-          scan_direction(s_hist[sel], ft, d.gain, sl, fwd, s_scan[grp], 1 + grp, &s_cand[grp]);
+          scan_direction(sm.hist[sel], ft, d.gain, sl, fwd, sm.scan[grp], 1 + grp, &sm.cand[grp]);
         }
       }
       __syncthreads();
@@ -1399,7 +1397,7 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
           DevSplitInfo si = d_split_none();
           if (scannable) {
             ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
-            si = finalize_split(d.gain, sl, s_cand[2 * sl_i], s_cand[2 * sl_i + 1]);
+            si = finalize_split(d.gain, sl, sm.cand[2 * sl_i], sm.cand[2 * sl_i + 1]);
           }
           d.scan_out[sl_i * d.F + f] = si;
         }
@@ -1413,6 +1411,24 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
       }
     }
   }
+}
+
+__global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
+  __shared__ FixScanSmem sm;
+  __shared__ Prep s_prep;
+  __shared__ Cand s_other;
+  __shared__ PickOut s_pick;
+  __shared__ bool s_last;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  if (tid == 0) {
+    prep_compute(d, s, s_prep);
+  } else if (warp == 1) {
+    const Cand o = other_leaves_best(d);
+    if ((tid & 31) == 0) s_other = o;
+  }
+  __syncthreads();
+  fixscan_feature(d, s_prep, blockIdx.x, sm);
   // last CTA: write the control step, then the argmax
   __threadfence();
   __syncthreads();
@@ -1423,14 +1439,39 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  if (tid == 0) {
-    prep_commit(d, s_prep);
-    d.ctrl->scan_counter = 0;
-    __threadfence();
+  // the pick (warp 0) and the control step's writes (warp 1) run side by side; then one
+  // thread writes the scanned leaves' best splits and the control block
+  const Prep& P = s_prep;
+  if (warp == 0) {
+    if (!P.c.done) pick_warp(d, P, s_other, s_pick);
+  } else if (warp == 1 && (tid & 31) == 0) {
+    prep_commit(d, P);
   }
   __syncthreads();
-  if (s_prep.c.done) return;
-  pick_split(d);
+  if (tid == 0) {
+    GrowCtrl c = P.c;
+    c.scan_counter = 0;
+    if (!c.done) {
+      if (P.live) {
+        d.best[P.S] = s_pick.si[0];
+        d.best_feature[P.S] = s_pick.bf[0];
+        if (P.Lg >= 0) {
+          d.best[P.Lg] = s_pick.si[1];
+          d.best_feature[P.Lg] = s_pick.bf[1];
+        }
+      }
+      if (s_pick.done) {
+        c.done = 1;
+      } else {
+        c.pending = 1;
+        c.split_leaf = s_pick.leaf;
+        c.split_feature = s_pick.feature;
+        c.split = s_pick.split;
+        c.build_left = s_pick.build_left;
+      }
+    }
+    *d.ctrl = c;
+  }
 }
 
 // ------------------------------------------------------------------------------------
