@@ -33,6 +33,10 @@ using namespace lgbm_b200;
 
 namespace {
 
+// Splits of leaves with at most this many 2048-row tiles (this device's rows) hand the
+// accumulated child to the next control step as one partial histogram per tile.
+constexpr int kPrivateTiles = 16;
+
 thread_local std::string g_last_error;
 
 struct Error {
@@ -208,6 +212,7 @@ struct lgbm_b200_learner {
   DevBuf<double> pool;
   DevBuf<long long> raw;
   DevBuf<long long> rawpool;
+  DevBuf<long long> partials;
   DevBuf<DevSplitInfo> scan_out;
   DevBuf<uint8_t> scan_ok;
   // gradients owned by a standalone learner (the booster owns its own)
@@ -328,6 +333,7 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   CUDA_TRY(raw.alloc((size_t)slot_len + 2));
   CUDA_TRY(cudaMemset(raw.p, 0, ((size_t)slot_len + 2) * sizeof(long long)));
   CUDA_TRY(rawpool.alloc((size_t)L * slot_len));
+  CUDA_TRY(partials.alloc((size_t)kPrivateTiles * slot_len));
   CUDA_TRY(scan_out.alloc((size_t)2 * ds->num_features));
   CUDA_TRY(scan_ok.alloc(2));
   d = GrowDev{};
@@ -370,6 +376,8 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.pool = pool.p;
   d.raw = raw.p;
   d.rawpool = rawpool.p;
+  d.partials = partials.p;
+  d.private_tiles = kPrivateTiles;
   d.raw_len = slot_len;
   d.n_global = N;
   d.scan_out = scan_out.p;
@@ -1288,6 +1296,8 @@ int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
   b->learner->bind(mode == GH_FLOAT ? (const void*)b->gh.p : (const void*)(b->gh.p + 8 * N),
                    b->ghp.p, b->state.p);
   b->learner->d.n_global = NG;
+  // the accumulated child has to be summed over devices in one buffer
+  if (comm) b->learner->d.private_tiles = 0;
   b->comm = comm;
   ObjDev& o = b->obj;
   o.N = N;

@@ -380,13 +380,10 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase
   // (learner.rs:2003-2020 build mask).
   const bool sub = t.mask_leaf >= 0;
   const uint8_t* ps = d.splittable + (size_t)(sub ? t.mask_leaf : 0) * d.F + grp.f_begin;
-  if (threadIdx.x < 4) {
-    uint32_t m = 0;
-    for (int b = 0; b < 32; ++b) {
-      const int fl = threadIdx.x * 32 + b;
-      if (fl < nf && (!sub || ps[fl])) m |= 1u << b;
-    }
-    s_mask[threadIdx.x] = m;
+  if (threadIdx.x < 128) {
+    const int fl = threadIdx.x;
+    const uint32_t m = __ballot_sync(0xffffffffu, fl < nf && (!sub || ps[fl] != 0));
+    if ((fl & 31) == 0) s_mask[fl >> 5] = m;
   }
   __syncthreads();
   const Q4Mask qm = q4_mask<NCH>(s_mask, nf);
@@ -860,6 +857,7 @@ struct Prep {
   int32_t slot_leaf0, slot_val0, slot_leaf1, slot_val1;  // slot_of_leaf writes (-1: none)
   int32_t S, Lg, sslot, lslot, use_sub, mask_leaf, smaller_is_left;
   DevLeafSplits lsS, lsLg;
+  int32_t priv_tiles;  // > 0: the accumulated child is this many per-tile partials
 };
 
 __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
@@ -874,6 +872,7 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   P.use_sub = 0;
   P.mask_leaf = -1;
   P.smaller_is_left = 1;
+  P.priv_tiles = 0;
   int32_t left = c.left_leaf, right = c.right_leaf;
   int32_t cnt_left = 0, cnt_right = 0, depth_left = 0, slot_left = -1;
   bool known = false;
@@ -929,6 +928,10 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
     lsR.weight = b.right_output;
     P.lsL = lsL;
     P.lsR = lsR;
+    if (d.fused && d.private_tiles > 0) {
+      const int32_t nt = (cnt + kPartitionTileRows - 1) / kPartitionTileRows;
+      if (nt <= d.private_tiles) P.priv_tiles = nt;
+    }
     left = leaf;
     right = nr;
     cnt_left = lcg;
@@ -1251,8 +1254,12 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
   // clear it for the next partition
   long long bv = 0;
   if (mine) {
-    bv = d.raw[cell];
-    d.raw[cell] = 0;
+    if (P.priv_tiles > 0) {
+      for (int t = 0; t < P.priv_tiles; ++t) bv += __ldcg(&d.partials[(size_t)t * d.raw_len + cell]);
+    } else {
+      bv = d.raw[cell];
+      d.raw[cell] = 0;
+    }
   }
   if (P.live) {
     const int32_t S = P.S, Lg = P.Lg;
@@ -1654,6 +1661,13 @@ constexpr int kFpItems = 2;
 static_assert(kFpThreads * kFpItems == kPartTile, "fused tiles are partition tiles");
 constexpr int kFpMaxChunks = 2;  // 16-feature row chunks held in registers per item
 
+// A status word carries its flag and count together in one aligned 64-bit store, and
+// readers use nothing else that the writer stored before it: a relaxed store suffices
+// (no fence, no read-modify-write round trip on the critical path).
+__device__ __forceinline__ void publish_status(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 // Decoupled look-back of one tile by warp 0 (status words as in PartitionTile).
 // Returns the exclusive prefix of left rows; *ok = 0 after kSpinLimit polls.
 __device__ __forceinline__ int32_t tile_lookback(unsigned long long* status, int32_t tile,
@@ -1662,10 +1676,8 @@ __device__ __forceinline__ int32_t tile_lookback(unsigned long long* status, int
   const int lane = threadIdx.x & 31;
   int32_t prefix = 0;
   *ok = 1;
-  if (lane == 0) {
-    __threadfence();
-    atomicExch(&status[tile], pack_status(epoch, tile == 0 ? 2u : 1u, (uint32_t)tile_left));
-  }
+  if (lane == 0)
+    publish_status(&status[tile], pack_status(epoch, tile == 0 ? 2u : 1u, (uint32_t)tile_left));
   if (tile == 0) return 0;
   const uint32_t ep = epoch & 0xffffffu;
   int32_t j_end = tile;
@@ -1696,10 +1708,7 @@ __device__ __forceinline__ int32_t tile_lookback(unsigned long long* status, int
     if (hp >= 0) break;
     j_end -= 32;
   }
-  if (lane == 0) {
-    __threadfence();
-    atomicExch(&status[tile], pack_status(epoch, 2u, (uint32_t)(prefix + tile_left)));
-  }
+  if (lane == 0) publish_status(&status[tile], pack_status(epoch, 2u, (uint32_t)(prefix + tile_left)));
   return prefix;
 }
 
@@ -1712,9 +1721,12 @@ __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int b
   __shared__ int32_t s_nb[128];
   __shared__ int32_t s_boff[128];
   __shared__ uint32_t s_mask[4];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // the first tile ticket is taken before anything else is read: its round trip overlaps
+  // the reads below (a ticket taken when there is nothing to do is harmless)
+  if (tid == 0) s_tile = (int32_t)atomicAdd(&d.ctrl->part_ticket, 1u);
   GrowCtrl* c = d.ctrl;
   if (c->done || !c->pending) return;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int32_t leaf = c->split_leaf;
   const int32_t f = c->split_feature;
   const DevFeature ft = d.feat[f];
@@ -1731,14 +1743,17 @@ __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int b
   const bool build_left = c->build_left != 0;
   const int nf = d.F;
   const int cap = nf << SHIFT;
+  // few tiles: every CTA takes exactly one tile and stores its own partial histogram
+  // (plain stores, summed by the next control step) instead of adding it atomically
+  const bool priv = build && ntiles <= d.private_tiles;
   if (blockIdx.x == 0 && tid == 0) {
     c->rows_parted += count;
     if (build) c->num_builds += 1;
   }
-  if (tid == 0) s_tile = (int32_t)atomicAdd(&c->part_ticket, 1u);
   __syncthreads();
   int32_t tile = s_tile;
   if (tile >= ntiles) return;
+  const int32_t my_tile = tile;
   uint32_t* hot = sm;
   uint32_t* c3 = sm + kQ4MaxCells;
   int32_t* cold_g = reinterpret_cast<int32_t*>(sm + 2 * kQ4MaxCells);
@@ -1758,13 +1773,9 @@ __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int b
       s_nb[fl] = g.num_bin;
       s_boff[fl] = g.bin_off;
     }
-    if (tid < 4) {
-      uint32_t m = 0;
-      for (int b = 0; b < 32; ++b) {
-        const int fl = tid * 32 + b;
-        if (fl < nf && ps[fl]) m |= 1u << b;
-      }
-      s_mask[tid] = m;
+    if (tid < 128) {
+      const uint32_t m = __ballot_sync(0xffffffffu, tid < nf && ps[tid] != 0);
+      if ((tid & 31) == 0) s_mask[tid >> 5] = m;
     }
   }
   __syncthreads();
@@ -1881,6 +1892,7 @@ __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int b
     cta_left += tile_left;
     cta_built += built;
     acc_rows += built;
+    if (priv) break;
     if (tid == 0) s_tile = (int32_t)atomicAdd(&c->part_ticket, 1u);
     __syncthreads();
     tile = s_tile;
@@ -1910,6 +1922,7 @@ __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int b
   if (build) {
     __syncthreads();
     long long* raw = d.raw;
+    long long* part = d.partials + (size_t)my_tile * d.raw_len;
     for (int s2 = tid; s2 < cap; s2 += kFpThreads) {
       const int fl = s2 >> SHIFT;
       const int bin = s2 & ((1 << SHIFT) - 1);
@@ -1921,9 +1934,15 @@ __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int b
       const long long n3 = (long long)c3[s2];
       const long long h = (qsum - 3 * n3) | (n3 << 32);
       const size_t gb = (size_t)(s_boff[fl] + bin);
-      if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb]), (unsigned long long)g);
-      if (h)
-        atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb + 1]), (unsigned long long)h);
+      if (priv) {
+        *reinterpret_cast<longlong2*>(&part[2 * gb]) = make_longlong2(g, h);
+      } else {
+        if (g)
+          atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb]), (unsigned long long)g);
+        if (h)
+          atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb + 1]),
+                    (unsigned long long)h);
+      }
     }
   }
   if (tid == 0) {

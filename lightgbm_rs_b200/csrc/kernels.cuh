@@ -77,6 +77,8 @@ struct GrowDev {
   long long* rawpool;      // [L][raw_len]: integer histogram of every leaf
   int32_t raw_len;         // 2 * total_bins
   int32_t fused;           // the partition kernel accumulates the child histogram
+  int32_t private_tiles;   // fused: splits of up to this many tiles store per-tile partials
+  long long* partials;     // [private_tiles][raw_len]
   int64_t n_global;        // rows on all devices
   DevSplitInfo* scan_out;  // [2][F]
   uint8_t* scan_ok;        // [2] leaf scanned flags
