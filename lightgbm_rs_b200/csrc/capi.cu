@@ -334,6 +334,7 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   CUDA_TRY(cudaMemset(raw.p, 0, ((size_t)slot_len + 2) * sizeof(long long)));
   CUDA_TRY(rawpool.alloc((size_t)L * slot_len));
   CUDA_TRY(partials.alloc((size_t)kPrivateTiles * slot_len));
+
   CUDA_TRY(scan_out.alloc((size_t)2 * ds->num_features));
   CUDA_TRY(scan_ok.alloc(2));
   d = GrowDev{};
@@ -378,6 +379,7 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.rawpool = rawpool.p;
   d.partials = partials.p;
   d.private_tiles = kPrivateTiles;
+
   d.raw_len = slot_len;
   d.n_global = N;
   d.scan_out = scan_out.p;
@@ -393,6 +395,7 @@ void lgbm_b200_learner::bind(const void* gh_ptr, const DevGhParams* ghp_ptr,
   d.gh_mode = gh_mode;
   d.q4_shift = q4_shift;
   d.fused = fused_partition_supported(gh_mode, (int)groups.size(), q4_shift, q4_nch) ? 1 : 0;
+
   d.q4_nch = q4_nch;
   d.groups = d_groups.p;
   d.num_groups = (int32_t)groups.size();
@@ -1296,7 +1299,7 @@ int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
   b->learner->bind(mode == GH_FLOAT ? (const void*)b->gh.p : (const void*)(b->gh.p + 8 * N),
                    b->ghp.p, b->state.p);
   b->learner->d.n_global = NG;
-  // the accumulated child has to be summed over devices in one buffer
+  // the accumulated child has to be summed over devices in one buffer, between kernels
   if (comm) b->learner->d.private_tiles = 0;
   b->comm = comm;
   ObjDev& o = b->obj;

@@ -1420,37 +1420,46 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
   }
 }
 
-__global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
-  __shared__ FixScanSmem sm;
-  __shared__ Prep s_prep;
-  __shared__ Cand s_other;
-  __shared__ PickOut s_pick;
-  __shared__ bool s_last;
+// Shared memory of a control step besides the per-feature scratch.
+struct CtlSmem {
+  Prep prep;
+  Cand other;
+  PickOut pick;
+  bool last;
+};
+
+// One control step by the CTAs [0, min(F, gridDim.x)), each taking features
+// blockIdx.x, blockIdx.x + gridDim.x, ...: apply the pending split, scan the two leaves,
+// and -- in the CTA that finishes last -- pick the next split and write the control block.
+__device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& cs) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
+  const int nparts = min(d.F, (int)gridDim.x);
   if (tid == 0) {
-    prep_compute(d, s, s_prep);
+    prep_compute(d, s, cs.prep);
   } else if (warp == 1) {
     const Cand o = other_leaves_best(d);
-    if ((tid & 31) == 0) s_other = o;
+    if ((tid & 31) == 0) cs.other = o;
   }
   __syncthreads();
-  fixscan_feature(d, s_prep, blockIdx.x, sm);
-  // last CTA: write the control step, then the argmax
+  for (int f = blockIdx.x; f < d.F; f += gridDim.x) {
+    fixscan_feature(d, cs.prep, f, sm);
+    __syncthreads();
+  }
+  // last CTA: the pick (warp 0) and the control step's writes (warp 1) run side by side;
+  // then one thread writes the scanned leaves' best splits and the control block
   __threadfence();
   __syncthreads();
   if (tid == 0) {
     const uint32_t t = atomicAdd(&d.ctrl->scan_counter, 1u);
-    s_last = (t == gridDim.x - 1);
+    cs.last = (t == (uint32_t)nparts - 1);
   }
   __syncthreads();
-  if (!s_last) return;
+  if (!cs.last) return;
   __threadfence();
-  // the pick (warp 0) and the control step's writes (warp 1) run side by side; then one
-  // thread writes the scanned leaves' best splits and the control block
-  const Prep& P = s_prep;
+  const Prep& P = cs.prep;
   if (warp == 0) {
-    if (!P.c.done) pick_warp(d, P, s_other, s_pick);
+    if (!P.c.done) pick_warp(d, P, cs.other, cs.pick);
   } else if (warp == 1 && (tid & 31) == 0) {
     prep_commit(d, P);
   }
@@ -1460,25 +1469,31 @@ __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
     c.scan_counter = 0;
     if (!c.done) {
       if (P.live) {
-        d.best[P.S] = s_pick.si[0];
-        d.best_feature[P.S] = s_pick.bf[0];
+        d.best[P.S] = cs.pick.si[0];
+        d.best_feature[P.S] = cs.pick.bf[0];
         if (P.Lg >= 0) {
-          d.best[P.Lg] = s_pick.si[1];
-          d.best_feature[P.Lg] = s_pick.bf[1];
+          d.best[P.Lg] = cs.pick.si[1];
+          d.best_feature[P.Lg] = cs.pick.bf[1];
         }
       }
-      if (s_pick.done) {
+      if (cs.pick.done) {
         c.done = 1;
       } else {
         c.pending = 1;
-        c.split_leaf = s_pick.leaf;
-        c.split_feature = s_pick.feature;
-        c.split = s_pick.split;
-        c.build_left = s_pick.build_left;
+        c.split_leaf = cs.pick.leaf;
+        c.split_feature = cs.pick.feature;
+        c.split = cs.pick.split;
+        c.build_left = cs.pick.build_left;
       }
     }
     *d.ctrl = c;
   }
+}
+
+__global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
+  __shared__ FixScanSmem sm;
+  __shared__ CtlSmem cs;
+  control_step(d, s, sm, cs);
 }
 
 // ------------------------------------------------------------------------------------
@@ -1712,15 +1727,27 @@ __device__ __forceinline__ int32_t tile_lookback(unsigned long long* status, int
   return prefix;
 }
 
+// Shared memory of the fused partition besides its accumulators.
+struct PartSmem {
+  int32_t warp[kFpThreads / 32];
+  int32_t tile, prefix, ok;
+  int32_t nb[128];
+  int32_t boff[128];
+  uint32_t mask[4];
+};
+
+// One fused partition by the whole grid (every thread of every CTA calls it); `sm` holds
+// the accumulators: hot | c3 | cold_g | cold_q, kQ4MaxCells words each.
 template <int SHIFT, int NCH>
-__global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int build) {
+__device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, PartSmem& ps_) {
   static_assert(NCH <= kFpMaxChunks, "row chunks held in registers");
-  extern __shared__ uint32_t sm[];  // hot | c3 | cold_g | cold_q, kQ4MaxCells words each
-  __shared__ int32_t s_warp[kFpThreads / 32];
-  __shared__ int32_t s_tile, s_prefix, s_ok;
-  __shared__ int32_t s_nb[128];
-  __shared__ int32_t s_boff[128];
-  __shared__ uint32_t s_mask[4];
+  int32_t* s_warp = ps_.warp;
+  int32_t& s_tile = ps_.tile;
+  int32_t& s_prefix = ps_.prefix;
+  int32_t& s_ok = ps_.ok;
+  int32_t* s_nb = ps_.nb;
+  int32_t* s_boff = ps_.boff;
+  uint32_t* s_mask = ps_.mask;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // the first tile ticket is taken before anything else is read: its round trip overlaps
   // the reads below (a ticket taken when there is nothing to do is harmless)
@@ -1954,6 +1981,14 @@ __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int b
   }
 }
 
+
+template <int SHIFT, int NCH>
+__global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int build) {
+  extern __shared__ uint32_t sm[];
+  __shared__ PartSmem ps;
+  partition_q4_phase<SHIFT, NCH>(d, build, sm, ps);
+}
+
 using PartQ4Kernel = void (*)(GrowDev, int);
 __host__ PartQ4Kernel part_q4_kernel(int shift, int nch) {
 #define PQ4_CASE(S, N) \
@@ -2077,6 +2112,7 @@ bool fused_partition_supported(int gh_mode, int num_groups, int shift, int nch) 
 }
 
 size_t fused_partition_smem() { return (size_t)4 * sizeof(uint32_t) * kQ4MaxCells; }
+
 
 // One tree: root build, then per split the control step + scans (k_fixscan) and the
 // partition, which in the fused mode also accumulates one child's histogram (else a
