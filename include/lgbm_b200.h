@@ -185,6 +185,16 @@ int lgbm_b200_bin_column(const double* column, int64_t n, const lgbm_b200_bin_co
                          lgbm_b200_bin_mapper* mapper_out, double* upper_bounds,
                          int32_t upper_cap, uint32_t* bins_out);
 
+/* BinMapper::find_bin_categorical + value_to_bin for a categorical column
+ * (crates/lgbm-dataset/src/bin_mapper.rs:416-641, :148-199): categories by
+ * descending count, bin 0 the dummy bin of NaN / negative / unseen values.
+ * bin_to_category receives num_bin category values (bin 0: -1; capacity cap);
+ * mapper_out->_reserved is 1 (categorical). Host-only; needs no GPU. */
+int lgbm_b200_bin_column_categorical(const double* column, int64_t n,
+                                     const lgbm_b200_bin_config* cfg,
+                                     lgbm_b200_bin_mapper* mapper_out, int32_t* bin_to_category,
+                                     int32_t cap, uint32_t* bins_out);
+
 /* ------------------------------------------------------ per-op Backend mirror */
 
 /* Backend::construct_histograms (crates/lgbm-compute/src/lib.rs:1119-1126):

@@ -74,22 +74,36 @@ def _resolve(params):
 
 def bin_column(values, max_bin=255, min_data_in_bin=3, min_data_in_leaf=20, pre_filter=False,
                use_missing=True, zero_as_missing=False, bin_construct_sample_cnt=200000,
-               data_random_seed=1, want_bins=True):
-    """BinMapper::find_bin_from_column + value_to_bin (host-side; no GPU needed)."""
+               data_random_seed=1, want_bins=True, categorical=False):
+    """BinMapper::find_bin_from_column + value_to_bin (host-side; no GPU needed).
+    categorical=True bins the column as categories (find_bin_categorical); the mapper
+    then carries bin_to_category instead of upper bounds."""
     col = np.ascontiguousarray(values, dtype=np.float64)
     cfg = C.BinConfig(int(max_bin), int(min_data_in_bin), int(min_data_in_leaf),
                       int(bool(pre_filter)), int(bool(use_missing)), int(bool(zero_as_missing)),
                       int(bin_construct_sample_cnt), int(data_random_seed))
     m = C.BinMapperC()
     cap = max(int(max_bin) + 2, 4)
-    upper = np.zeros(cap, dtype=np.float64)
     bins = np.empty(len(col), dtype=np.uint32) if want_bins else None
-    C.check(C.lib().lgbm_b200_bin_column(C.ptr(col), len(col), ctypes.byref(cfg),
-                                         ctypes.byref(m), C.ptr(upper), cap, C.ptr(bins)))
+    if categorical:
+        # the 99 % cut may keep more categories than max_bin
+        cap = max(cap, min(len(col), 1 << 20) + 2)
+        b2c = np.zeros(cap, dtype=np.int32)
+        C.check(C.lib().lgbm_b200_bin_column_categorical(C.ptr(col), len(col), ctypes.byref(cfg),
+                                                         ctypes.byref(m), C.ptr(b2c), cap,
+                                                         C.ptr(bins)))
+    else:
+        upper = np.zeros(cap, dtype=np.float64)
+        C.check(C.lib().lgbm_b200_bin_column(C.ptr(col), len(col), ctypes.byref(cfg),
+                                             ctypes.byref(m), C.ptr(upper), cap, C.ptr(bins)))
     mapper = {"num_bin": m.num_bin, "missing_type": m.missing_type,
               "default_bin": m.default_bin, "most_freq_bin": m.most_freq_bin,
               "is_trivial": bool(m.is_trivial), "min_val": m.min_val, "max_val": m.max_val,
-              "sparse_rate": m.sparse_rate, "upper": upper[: m.num_bin].copy()}
+              "sparse_rate": m.sparse_rate, "bin_type": 1 if categorical else 0}
+    if categorical:
+        mapper["bin_to_category"] = b2c[: m.num_bin].copy()
+    else:
+        mapper["upper"] = upper[: m.num_bin].copy()
     return mapper, bins
 
 

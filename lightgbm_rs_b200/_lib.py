@@ -98,6 +98,7 @@ _SIGS = {
     "lgbm_b200_abi_version": ([], _i32),
     "lgbm_b200_device_count": ([_P], ctypes.c_int),
     "lgbm_b200_bin_column": ([_P, _i64, _P, _P, _P, _i32, _P], ctypes.c_int),
+    "lgbm_b200_bin_column_categorical": ([_P, _i64, _P, _P, _P, _i32, _P], ctypes.c_int),
     "lgbm_b200_construct_histograms": ([_P, _P, _P, _i64, _u32, _P], ctypes.c_int),
     "lgbm_b200_find_best_split": ([_P, _P, _u32, _i32, _u32, _u32, _i32, _i32, _i32, _f64, _f64,
                                    _i32, _P], ctypes.c_int),

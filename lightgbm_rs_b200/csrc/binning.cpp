@@ -190,8 +190,16 @@ bool need_filter(const std::vector<int32_t>& cnt_in_bin, int32_t total_cnt, int3
 
 uint32_t BinMapperHost::value_to_bin(double value) const {  // bin_mapper.rs:148-199
   if (std::isnan(value)) {
+    if (bin_type == 1) return 0;
     if (missing_type == 2) return (uint32_t)(num_bin - 1);
     value = 0.0;
+  }
+  if (bin_type == 1) {
+    // categorical: truncate to int; negatives and unseen categories -> bin 0
+    const int32_t iv = (int32_t)value;
+    if (iv < 0) return 0;
+    auto it = category_to_bin.find(iv);
+    return it == category_to_bin.end() ? 0u : it->second;
   }
   int32_t l = 0, r = num_bin - 1;
   if (missing_type == 2) r -= 1;
@@ -204,6 +212,55 @@ uint32_t BinMapperHost::value_to_bin(double value) const {  // bin_mapper.rs:148
   }
   return (uint32_t)l;
 }
+
+namespace {
+
+// Sorted distinct values with counts, plus the zero pseudo-value for the rows the
+// sample did not hold (bin_mapper.rs:339-375 numeric prefix, shared with categorical).
+void distinct_with_zero(std::vector<double>& values, int32_t zero_cnt, std::vector<double>* dv,
+                        std::vector<int32_t>* counts) {
+  const size_t ns = values.size();
+  std::sort(values.begin(), values.end());
+  if (ns == 0 || (values[0] > 0.0 && zero_cnt > 0)) {
+    dv->push_back(0.0);
+    counts->push_back(zero_cnt);
+  }
+  if (ns > 0) {
+    dv->push_back(values[0]);
+    counts->push_back(1);
+  }
+  for (size_t i = 1; i < ns; ++i) {
+    if (!check_equal_ordered(values[i - 1], values[i])) {
+      if (values[i - 1] < 0.0 && values[i] > 0.0) {
+        dv->push_back(0.0);
+        counts->push_back(zero_cnt);
+      }
+      dv->push_back(values[i]);
+      counts->push_back(1);
+    } else {
+      dv->back() = values[i];
+      counts->back() += 1;
+    }
+  }
+  if (ns > 0 && values[ns - 1] < 0.0 && zero_cnt > 0) {
+    dv->push_back(0.0);
+    counts->push_back(zero_cnt);
+  }
+}
+
+// need_filter (bin_mapper.rs:724-746), categorical case: only one- or two-bin
+// features can be filtered.
+bool need_filter_categorical(const std::vector<int32_t>& cnt_in_bin, int32_t total_cnt,
+                             int32_t filter_cnt) {
+  if (cnt_in_bin.size() > 2) return false;
+  for (size_t i = 0; i + 1 < cnt_in_bin.size(); ++i) {
+    const int32_t left = cnt_in_bin[i];
+    if (left >= filter_cnt && total_cnt - left >= filter_cnt) return false;
+  }
+  return true;
+}
+
+}  // namespace
 
 // find_bin_numeric (bin_mapper.rs:201-415)
 BinMapperHost find_bin_numeric(std::vector<double> values, int32_t max_bin,
@@ -230,32 +287,7 @@ BinMapperHost find_bin_numeric(std::vector<double> values, int32_t max_bin,
   const int32_t zero_cnt = (int32_t)(total_sample_cnt - (int64_t)ns - na_cnt);
   std::vector<double> dv;
   std::vector<int32_t> counts;
-  std::sort(values.begin(), values.end());
-  if (ns == 0 || (values[0] > 0.0 && zero_cnt > 0)) {
-    dv.push_back(0.0);
-    counts.push_back(zero_cnt);
-  }
-  if (ns > 0) {
-    dv.push_back(values[0]);
-    counts.push_back(1);
-  }
-  for (size_t i = 1; i < ns; ++i) {
-    if (!check_equal_ordered(values[i - 1], values[i])) {
-      if (values[i - 1] < 0.0 && values[i] > 0.0) {
-        dv.push_back(0.0);
-        counts.push_back(zero_cnt);
-      }
-      dv.push_back(values[i]);
-      counts.push_back(1);
-    } else {
-      dv.back() = values[i];
-      counts.back() += 1;
-    }
-  }
-  if (ns > 0 && values[ns - 1] < 0.0 && zero_cnt > 0) {
-    dv.push_back(0.0);
-    counts.push_back(zero_cnt);
-  }
+  distinct_with_zero(values, zero_cnt, &dv, &counts);
   BinMapperHost m;
   m.min_val = dv.empty() ? 0.0 : dv.front();
   m.max_val = dv.empty() ? 0.0 : dv.back();
@@ -303,11 +335,116 @@ BinMapperHost find_bin_numeric(std::vector<double> values, int32_t max_bin,
   return m;
 }
 
+// find_bin_categorical (bin_mapper.rs:416-641): categories by descending sample count
+// (stable: ties keep ascending category order), kept until 99 % of the non-missing
+// sample is covered and max_bin is reached; rare categories stop the fold at
+// min_data_in_bin. Bin 0 is the dummy bin of NaN, negative and unseen values.
+BinMapperHost find_bin_categorical(std::vector<double> values, int32_t max_bin,
+                                   int32_t min_data_in_bin, int32_t min_split_data,
+                                   bool pre_filter, bool use_missing, bool zero_as_missing,
+                                   int64_t total_sample_cnt) {
+  const int32_t num_in = (int32_t)values.size();
+  size_t non_na = 0;
+  for (size_t i = 0; i < values.size(); ++i)
+    if (!std::isnan(values[i])) values[non_na++] = values[i];
+  int32_t na_cnt = 0;
+  int32_t missing_type;
+  if (!use_missing)
+    missing_type = 0;
+  else if (zero_as_missing)
+    missing_type = 1;
+  else if ((int32_t)non_na == num_in)
+    missing_type = 0;
+  else {
+    na_cnt = num_in - (int32_t)non_na;
+    missing_type = 2;
+  }
+  values.resize(non_na);
+  const int32_t zero_cnt = (int32_t)(total_sample_cnt - (int64_t)non_na - na_cnt);
+  std::vector<double> dv;
+  std::vector<int32_t> counts;
+  distinct_with_zero(values, zero_cnt, &dv, &counts);
+  BinMapperHost m;
+  m.bin_type = 1;
+  m.min_val = dv.empty() ? 0.0 : dv.front();
+  m.max_val = dv.empty() ? 0.0 : dv.back();
+  // integer categories (negatives count as missing), equal neighbours merged
+  std::vector<int32_t> cats, cat_cnt;
+  for (size_t i = 0; i < dv.size(); ++i) {
+    const int32_t v = (int32_t)dv[i];
+    if (v < 0) {
+      na_cnt += counts[i];
+    } else if (cats.empty() || v != cats.back()) {
+      cats.push_back(v);
+      cat_cnt.push_back(counts[i]);
+    } else {
+      cat_cnt.back() += counts[i];
+    }
+  }
+  m.num_bin = 1;
+  std::vector<int32_t> cnt_in_bin;
+  int32_t used_cnt = 0;
+  const int32_t rest_cnt = (int32_t)(total_sample_cnt - na_cnt);
+  if (rest_cnt > 0) {
+    std::vector<size_t> order(cats.size());
+    for (size_t i = 0; i < order.size(); ++i) order[i] = i;
+    std::stable_sort(order.begin(), order.end(),
+                     [&](size_t a, size_t b) { return cat_cnt[a] > cat_cnt[b]; });
+    std::vector<int32_t> sc(cats.size()), sn(cats.size());
+    for (size_t i = 0; i < order.size(); ++i) {
+      sc[i] = cats[order[i]];
+      sn[i] = cat_cnt[order[i]];
+    }
+    // cut_cnt = RoundInt((total - na) * 0.99f): the multiply is in f32
+    const float scaled = (float)rest_cnt * 0.99f;
+    const int32_t cut_cnt = (int32_t)((double)scaled + (double)0.5f);
+    int32_t distinct_cnt = (int32_t)sc.size() + (na_cnt > 0 ? 1 : 0);
+    max_bin = std::min(max_bin, distinct_cnt);
+    m.bin_to_category.push_back(-1);
+    m.category_to_bin[-1] = 0;
+    cnt_in_bin.push_back(0);
+    size_t idx = 0;
+    while (idx < sc.size() && (used_cnt < cut_cnt || m.num_bin < max_bin)) {
+      if (sn[idx] < min_data_in_bin && idx > 1) break;
+      m.bin_to_category.push_back(sc[idx]);
+      m.category_to_bin[sc[idx]] = (uint32_t)m.num_bin;
+      used_cnt += sn[idx];
+      cnt_in_bin.push_back(sn[idx]);
+      m.num_bin += 1;
+      ++idx;
+    }
+    missing_type = (idx == sc.size() && na_cnt == 0) ? 0 : 2;
+    cnt_in_bin[0] = (int32_t)(total_sample_cnt - used_cnt);
+  }
+  m.missing_type = missing_type;
+  bool trivial = m.num_bin <= 1;
+  if (!trivial && pre_filter &&
+      need_filter_categorical(cnt_in_bin, (int32_t)total_sample_cnt, min_split_data))
+    trivial = true;
+  if (!trivial) {
+    const uint32_t default_bin = m.value_to_bin(0.0);
+    size_t best = 0;
+    for (size_t i = 1; i < cnt_in_bin.size(); ++i)
+      if (cnt_in_bin[i] > cnt_in_bin[best]) best = i;
+    uint32_t mfb = (uint32_t)best;
+    const double max_sparse = (double)cnt_in_bin[mfb] / (double)total_sample_cnt;
+    if (mfb != default_bin && max_sparse < 0.7) mfb = default_bin;
+    m.sparse_rate = (double)cnt_in_bin[mfb] / (double)total_sample_cnt;
+    m.default_bin = (int32_t)default_bin;
+    m.most_freq_bin = (int32_t)mfb;
+  } else {
+    m.sparse_rate = 1.0;
+  }
+  m.is_trivial = trivial;
+  return m;
+}
+
 // find_bin_from_column (bin_mapper.rs:642-675)
 BinMapperHost find_bin_from_column(const double* column, int64_t n, int32_t max_bin,
                                    int32_t min_data_in_bin, int32_t min_data_in_leaf,
                                    bool pre_filter, bool use_missing, bool zero_as_missing,
-                                   int32_t bin_construct_sample_cnt, int32_t data_random_seed) {
+                                   int32_t bin_construct_sample_cnt, int32_t data_random_seed,
+                                   bool categorical) {
   const int32_t total = (int32_t)n;
   const int32_t k = total < bin_construct_sample_cnt ? total : bin_construct_sample_cnt;
   Random rnd(data_random_seed);
@@ -319,6 +456,9 @@ BinMapperHost find_bin_from_column(const double* column, int64_t n, int32_t max_
   const int32_t filter_cnt =
       total == 0 ? min_data_in_leaf
                  : (int32_t)(((int64_t)min_data_in_leaf * total_sample_cnt) / (int64_t)total);
+  if (categorical)
+    return find_bin_categorical(std::move(sampled), max_bin, min_data_in_bin, filter_cnt,
+                                pre_filter, use_missing, zero_as_missing, total_sample_cnt);
   return find_bin_numeric(std::move(sampled), max_bin, min_data_in_bin, filter_cnt, pre_filter,
                           use_missing, zero_as_missing, total_sample_cnt);
 }

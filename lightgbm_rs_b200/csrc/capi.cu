@@ -738,6 +738,37 @@ int lgbm_b200_bin_column(const double* column, int64_t n, const lgbm_b200_bin_co
   return LGBM_B200_OK;
 }
 
+int lgbm_b200_bin_column_categorical(const double* column, int64_t n,
+                                     const lgbm_b200_bin_config* cfg,
+                                     lgbm_b200_bin_mapper* mapper_out, int32_t* bin_to_category,
+                                     int32_t cap, uint32_t* bins_out) {
+  if (!column || !cfg || !mapper_out || n < 0)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "bin_column_categorical: null argument");
+  BinMapperHost m = find_bin_from_column(column, n, cfg->max_bin, cfg->min_data_in_bin,
+                                         cfg->min_data_in_leaf, cfg->pre_filter != 0,
+                                         cfg->use_missing != 0, cfg->zero_as_missing != 0,
+                                         cfg->bin_construct_sample_cnt, cfg->data_random_seed,
+                                         true);
+  mapper_out->num_bin = m.num_bin;
+  mapper_out->missing_type = m.missing_type;
+  mapper_out->default_bin = m.default_bin;
+  mapper_out->most_freq_bin = m.most_freq_bin;
+  mapper_out->is_trivial = m.is_trivial ? 1 : 0;
+  mapper_out->_reserved = 1;  // categorical
+  mapper_out->min_val = m.min_val;
+  mapper_out->max_val = m.max_val;
+  mapper_out->sparse_rate = m.sparse_rate;
+  if (bin_to_category) {
+    if (cap < (int32_t)m.bin_to_category.size())
+      return fail(LGBM_B200_LENGTH_MISMATCH, "bin_to_category holds %d, need %d", cap,
+                  (int)m.bin_to_category.size());
+    std::copy(m.bin_to_category.begin(), m.bin_to_category.end(), bin_to_category);
+  }
+  if (bins_out)
+    for (int64_t i = 0; i < n; ++i) bins_out[i] = m.value_to_bin(column[i]);
+  return LGBM_B200_OK;
+}
+
 int lgbm_b200_construct_histograms(const uint32_t* binned, const float* gradients,
                                    const float* hessians, int64_t n, uint32_t num_bin,
                                    double* out) {

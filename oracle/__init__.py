@@ -32,6 +32,12 @@ class GainConfig(ctypes.Structure):
         ("min_gain_to_split", ctypes.c_double),
         ("path_smooth", ctypes.c_double),
         ("parent_output", ctypes.c_double),
+        ("min_data_per_group", ctypes.c_int32),
+        ("max_cat_threshold", ctypes.c_int32),
+        ("max_cat_to_onehot", ctypes.c_int32),
+        ("_pad2", ctypes.c_int32),
+        ("cat_l2", ctypes.c_double),
+        ("cat_smooth", ctypes.c_double),
     ]
 
 
@@ -58,7 +64,7 @@ class FeatureMeta(ctypes.Structure):
         ("default_bin", ctypes.c_int32),
         ("most_freq_bin", ctypes.c_int32),
         ("missing_type", ctypes.c_int32),
-        ("_pad", ctypes.c_int32),
+        ("is_categorical", ctypes.c_int32),
     ]
 
 
@@ -90,6 +96,7 @@ class Tree(ctypes.Structure):
         ("internal_count", _P),
         ("leaf_depth", _P),
         ("leaf_parent", _P),
+        ("cat_bins", _P),
     ]
 
 
@@ -159,10 +166,13 @@ def _ptr(a):
 
 def gain_config(min_data_in_leaf=20, min_sum_hessian_in_leaf=1e-3, max_delta_step=0.0,
                 lambda_l1=0.0, lambda_l2=0.0, min_gain_to_split=0.0, path_smooth=0.0,
-                parent_output=0.0):
+                parent_output=0.0, min_data_per_group=100, max_cat_threshold=32,
+                max_cat_to_onehot=4, cat_l2=10.0, cat_smooth=10.0):
     return GainConfig(int(min_data_in_leaf), 0, float(min_sum_hessian_in_leaf),
                       float(max_delta_step), float(lambda_l1), float(lambda_l2),
-                      float(min_gain_to_split), float(path_smooth), float(parent_output))
+                      float(min_gain_to_split), float(path_smooth), float(parent_output),
+                      int(min_data_per_group), int(max_cat_threshold), int(max_cat_to_onehot),
+                      0, float(cat_l2), float(cat_smooth))
 
 
 def construct_histogram(bins, g, h, num_bin):
@@ -221,7 +231,7 @@ def feature_metas(metas):
     for i, m in enumerate(metas):
         mfb = int(m["most_freq_bin"])
         arr[i] = FeatureMeta(int(m["num_bin"]), 1 if mfb == 0 else 0, int(m["default_bin"]), mfb,
-                             int(m.get("missing_type", 0)), 0)
+                             int(m.get("missing_type", 0)), int(m.get("bin_type", 0)))
     return arr
 
 
@@ -241,6 +251,8 @@ def grow_tree(bins_cols, metas, g, h, num_leaves, max_depth=-1, nthreads=1, **ga
         n = max(num_leaves + delta, 1)
         arrays[name] = np.zeros(n, dtype=dt)
         setattr(t, name, arrays[name].ctypes.data)
+    cat_bins = np.zeros((max(num_leaves - 1, 1), 8), dtype=np.uint32)
+    t.cat_bins = cat_bins.ctypes.data
     idx = np.empty(N, dtype=np.uint32)
     lb = np.empty(num_leaves, dtype=np.int32)
     lc = np.empty(num_leaves, dtype=np.int32)
@@ -254,6 +266,7 @@ def grow_tree(bins_cols, metas, g, h, num_leaves, max_depth=-1, nthreads=1, **ga
     tree = {"num_leaves": nl}
     for name, dt, delta in TREE_ARRAYS:
         tree[name] = arrays[name][: max(nl + delta, 0)].copy()
+    tree["cat_bins"] = cat_bins[: max(nl - 1, 0)].copy()
     part = {"indices": idx, "leaf_begin": lb[:nl].copy(), "leaf_count": lc[:nl].copy()}
     return tree, part, trace[: 4 * rc].reshape(-1, 4)
 
@@ -360,3 +373,24 @@ def train(bins_cols, metas, labels, objective="binary", num_iterations=10, learn
         out["iter_scores"] = iter_scores
         out["iter_grad_hess"] = iter_gh
     return out
+
+
+def categorical_bitsets(tree, bin_to_category_of):
+    """cat_boundaries / cat_threshold of a tree (Tree::split_categorical,
+    lgbm-model/src/tree.rs:710-770): per categorical node, in node order, the bitset of
+    the REAL categories of the bins sent left (Common::ConstructBitset)."""
+    bounds, words = [0], []
+    for node, dt in enumerate(tree["decision_type"]):
+        if not (int(dt) & 1):
+            continue
+        f = int(tree["split_feature"][node])
+        b2c = bin_to_category_of(f)
+        bits = tree["cat_bins"][node]
+        cats = [int(b2c[b]) for b in range(256) if (int(bits[b >> 5]) >> (b & 31)) & 1]
+        n = max(cats) // 32 + 1 if cats else 0
+        blk = [0] * n
+        for c in cats:
+            blk[c // 32] |= 1 << (c % 32)
+        words.extend(blk)
+        bounds.append(bounds[-1] + n)
+    return bounds, words

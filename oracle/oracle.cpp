@@ -17,6 +17,7 @@
 // restated below with std::fma.
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -45,6 +46,11 @@ struct GainCfg {
   double min_gain_to_split;
   double path_smooth;
   double parent_output;
+  int32_t min_data_per_group = 100;
+  int32_t max_cat_threshold = 32;
+  int32_t max_cat_to_onehot = 4;
+  double cat_l2 = 10.0;
+  double cat_smooth = 10.0;
   bool use_l1() const { return lambda_l1 > 0.0; }          // gain.rs:1000-1003
   bool use_smoothing() const { return path_smooth > kEps; } // gain.rs:1018-1020
 };
@@ -78,6 +84,13 @@ typedef struct {
   double min_gain_to_split;
   double path_smooth;
   double parent_output;
+  // categorical split parameters (gain.rs GainConfig; config defaults 100, 32, 4, 10, 10)
+  int32_t min_data_per_group;
+  int32_t max_cat_threshold;
+  int32_t max_cat_to_onehot;
+  int32_t _pad2;
+  double cat_l2;
+  double cat_smooth;
 } OGainConfig;
 
 // Per-feature metadata the learner reads (lgbm-treelearner/src/learner.rs:87-140).
@@ -87,7 +100,7 @@ typedef struct {
   int32_t default_bin;
   int32_t most_freq_bin;
   int32_t missing_type;    // 0 None, 1 Zero, 2 NaN
-  int32_t _pad;
+  int32_t is_categorical;  // BinType::Categorical (learner.rs:130-140)
 } OFeatureMeta;
 
 typedef struct {
@@ -114,6 +127,8 @@ typedef struct {
   int32_t* internal_count;
   int32_t* leaf_depth;
   int32_t* leaf_parent;
+  // categorical nodes: the bins sent left, a 256-bit set per internal node (may be NULL)
+  uint32_t* cat_bins;
 } OTree;
 
 }  // extern "C"
@@ -190,6 +205,11 @@ GainCfg to_cfg(const OGainConfig& c) {
   g.min_gain_to_split = c.min_gain_to_split;
   g.path_smooth = c.path_smooth;
   g.parent_output = c.parent_output;
+  g.min_data_per_group = c.min_data_per_group;
+  g.max_cat_threshold = c.max_cat_threshold;
+  g.max_cat_to_onehot = c.max_cat_to_onehot;
+  g.cat_l2 = c.cat_l2;
+  g.cat_smooth = c.cat_smooth;
   return g;
 }
 
@@ -397,6 +417,134 @@ inline bool split_gt(const OSplitInfo& a, int32_t af, const OSplitInfo& b, int32
 }
 
 // Bin-column accessor: columns are feature-major, `bytes` wide.
+// ------- categorical split finder: feature_histogram_categorical.rs:96-490 -------
+// (LightGBM FeatureHistogram::FindBestThresholdCategoricalInner). `sum_hessian` is the
+// leaf sum already bumped by 2 kEpsilon, as at the numeric call site. `bins_out` gets
+// the set of (uncompacted) bins sent left; the split's threshold is 0 and default_left
+// false.
+OSplitInfo find_best_categorical(const double* hist, const GainCfg& cfg, int32_t num_bin,
+                                 int32_t offset, double sum_gradient, double sum_hessian,
+                                 int32_t num_data, uint32_t bins_out[8]) {
+  for (int i = 0; i < 8; ++i) bins_out[i] = 0;
+  const bool use_l1 = cfg.use_l1();
+  const double l1 = cfg.lambda_l1, mds = cfg.max_delta_step, ps = cfg.path_smooth;
+  const bool smoothing = cfg.use_smoothing();
+  const double parent = cfg.parent_output;
+  // gain_shift with the original l2 (the deliberate asymmetry, :140-160)
+  const double gain_shift =
+      smoothing ? leaf_gain_given_output(use_l1, sum_gradient, sum_hessian, l1, cfg.lambda_l2,
+                                         parent)
+                : leaf_gain_full(use_l1, sum_gradient, sum_hessian, l1, cfg.lambda_l2, mds, false,
+                                 0.0, num_data, 0.0);
+  const double min_gain_shift = gain_shift + cfg.min_gain_to_split;
+  const int32_t bin_start = 1 - offset, bin_end = num_bin - offset;
+  const double cnt_factor = (double)num_data / sum_hessian;
+  auto gains = [&](double lg, double lh, double rg, double rh, int32_t lc, int32_t rc,
+                   double l2) {
+    return leaf_gain_full(use_l1, lg, lh, l1, l2, mds, smoothing, ps, lc, parent) +
+           leaf_gain_full(use_l1, rg, rh, l1, l2, mds, smoothing, ps, rc, parent);
+  };
+  bool splittable = false;
+  double best_gain = kMinScore, best_slg = 0.0, best_slh = 0.0;
+  int32_t best_lc = 0, best_thr = -1, best_dir = 1;
+  const bool onehot = num_bin <= cfg.max_cat_to_onehot;
+  double l2 = cfg.lambda_l2;
+  std::vector<int32_t> order;
+  int32_t used = 0;
+  if (onehot) {
+    for (int32_t t = bin_start; t < bin_end; ++t) {
+      const double gr = hist[2 * t], he = hist[2 * t + 1];
+      const int32_t cnt = round_int(he * cnt_factor);
+      if (cnt < cfg.min_data_in_leaf || he < cfg.min_sum_hessian_in_leaf) continue;
+      const int32_t other = num_data - cnt;
+      if (other < cfg.min_data_in_leaf) continue;
+      const double soh = sum_hessian - he - kEps;
+      if (soh < cfg.min_sum_hessian_in_leaf) continue;
+      const double sog = sum_gradient - gr;
+      const double g = gains(sog, soh, gr, he + kEps, other, cnt, l2);
+      if (g <= min_gain_shift) continue;
+      splittable = true;
+      if (g > best_gain) {
+        best_thr = t;
+        best_slg = gr;
+        best_slh = he + kEps;
+        best_lc = cnt;
+        best_gain = g;
+      }
+    }
+  } else {
+    // many-vs-many: categories with enough rows, in ascending order of the smoothed
+    // gradient ratio (a stable sort), scanned from both ends (:300-420)
+    for (int32_t t = bin_start; t < bin_end; ++t)
+      if ((double)round_int(hist[2 * t + 1] * cnt_factor) >= cfg.cat_smooth) order.push_back(t);
+    used = (int32_t)order.size();
+    l2 += cfg.cat_l2;
+    auto ctr = [&](int32_t t) { return hist[2 * t] / (hist[2 * t + 1] + cfg.cat_smooth); };
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int32_t a, int32_t b) { return ctr(a) < ctr(b); });
+    const int32_t max_num_cat = std::min(cfg.max_cat_threshold, (used + 1) / 2);
+    for (int dir_i = 0; dir_i < 2; ++dir_i) {
+      const int32_t dir = dir_i == 0 ? 1 : -1;
+      int32_t pos = dir_i == 0 ? 0 : used - 1;
+      int32_t cnt_group = 0, lc = 0;
+      double slg = 0.0, slh = kEps;
+      for (int32_t i = 0; i < used && i < max_num_cat; ++i) {
+        const int32_t t = order[pos];
+        pos += dir;
+        const double gr = hist[2 * t], he = hist[2 * t + 1];
+        const int32_t cnt = round_int(he * cnt_factor);
+        slg += gr;
+        slh += he;
+        lc += cnt;
+        cnt_group += cnt;
+        if (lc < cfg.min_data_in_leaf || slh < cfg.min_sum_hessian_in_leaf) continue;
+        const int32_t rc = num_data - lc;
+        if (rc < cfg.min_data_in_leaf || rc < cfg.min_data_per_group) break;
+        const double srh = sum_hessian - slh;
+        if (srh < cfg.min_sum_hessian_in_leaf) break;
+        if (cnt_group < cfg.min_data_per_group) continue;
+        cnt_group = 0;
+        const double srg = sum_gradient - slg;
+        const double g = gains(slg, slh, srg, srh, lc, rc, l2);
+        if (g <= min_gain_shift) continue;
+        splittable = true;
+        if (g > best_gain) {
+          best_lc = lc;
+          best_slg = slg;
+          best_slh = slh;
+          best_thr = i;
+          best_gain = g;
+          best_dir = dir;
+        }
+      }
+    }
+  }
+  OSplitInfo s = split_none();
+  s.default_left = 0;
+  if (!splittable) return s;
+  const int32_t rc = num_data - best_lc;
+  s.threshold = 0;
+  s.gain = best_gain - min_gain_shift;
+  s.left_count = best_lc;
+  s.right_count = rc;
+  s.left_output = leaf_output_full(use_l1, best_slg, best_slh, l1, l2, mds, smoothing, ps,
+                                   best_lc, parent);
+  s.left_sum_gradient = best_slg;
+  s.left_sum_hessian = best_slh - kEps;
+  s.right_output = leaf_output_full(use_l1, sum_gradient - best_slg, sum_hessian - best_slh, l1,
+                                    l2, mds, smoothing, ps, rc, parent);
+  s.right_sum_gradient = sum_gradient - best_slg;
+  s.right_sum_hessian = sum_hessian - best_slh - kEps;
+  auto put = [&](int32_t bin) { bins_out[bin >> 5] |= 1u << (bin & 31); };
+  if (onehot) {
+    put(best_thr + offset);
+  } else {
+    for (int32_t i = 0; i <= best_thr; ++i)
+      put((best_dir == 1 ? order[i] : order[used - 1 - i]) + offset);
+  }
+  return s;
+}
+
 struct Bins {
   const void* const* cols;
   int bytes;
@@ -450,6 +598,10 @@ struct Learner {
   std::vector<OSplitInfo> best_split;
   std::vector<int32_t> best_feature;
   std::vector<std::vector<uint8_t>> feature_splittable;
+  // bins sent left by each leaf's best split when its feature is categorical
+  // (learner.rs:1356-1357 best_cat_threshold, as a bin set)
+  std::vector<std::array<uint32_t, 8>> best_cat;
+  int32_t num_cat = 0;
 
   Learner(Bins b, int64_t n, int32_t f, const OFeatureMeta* m, const float* gg, const float* hh,
           const OLearnerConfig& lc, int nt)
@@ -506,9 +658,17 @@ struct Learner {
     GainCfg lc = cfg;
     lc.parent_output = ls.weight;
     std::vector<OSplitInfo> per(F);
+    std::vector<std::array<uint32_t, 8>> cat_bits(F);
 #pragma omp parallel for schedule(dynamic, 1) num_threads(nthreads) if (nthreads > 1 && F >= 8)
     for (int32_t f = 0; f < F; ++f) {
       if (parent_splittable && !(*parent_splittable)[f]) continue;
+      if (meta[f].is_categorical) {
+        // bin_type dispatch (learner.rs:3099-3149): the leaf hessian is bumped here
+        per[f] = find_best_categorical(buf + slot_off[f], lc, meta[f].num_bin, meta[f].offset,
+                                       ls.sum_g, ls.sum_h + 2.0 * kEps, ls.num_data,
+                                       cat_bits[f].data());
+        continue;
+      }
       per[f] = find_best_split(buf + slot_off[f], lc, meta[f].num_bin, meta[f].offset,
                                meta[f].default_bin, skip_default_bin(f), na_as_missing(f),
                                run_forward(f), ls.sum_g, ls.sum_h, ls.num_data);
@@ -526,6 +686,8 @@ struct Learner {
     }
     best_split[leaf] = leaf_best;
     best_feature[leaf] = leaf_best_feature;
+    if (leaf_best_feature >= 0 && meta[leaf_best_feature].is_categorical)
+      best_cat[leaf] = cat_bits[leaf_best_feature];
     feature_splittable[leaf] = this_splittable;
   }
 
@@ -553,11 +715,15 @@ struct Learner {
     const bool na = na_as_missing(f);
     const int32_t na_bin = num_bin - 1;
     int32_t lc = 0, rc = 0;
+    const bool cat = meta[f].is_categorical != 0;
+    const std::array<uint32_t, 8> cb = best_cat[leaf];
     for (int32_t i = 0; i < count; ++i) {
       const uint32_t row = indices[begin + i];
       const int32_t b = (int32_t)bins.get(f, row);
       bool gr;
-      if (na && b == na_bin)
+      if (cat)  // DataPartition::split_categorical (data_partition.rs:636-688)
+        gr = !((cb[b >> 5] >> (b & 31)) & 1u);
+      else if (na && b == na_bin)
         gr = !default_left;
       else if (b < min_b || b > max_b)
         gr = default_to_right;
@@ -596,6 +762,10 @@ struct Learner {
     best_split.assign(num_leaves, split_none());
     best_feature.assign(num_leaves, -1);
     feature_splittable.assign(num_leaves, std::vector<uint8_t>(F, 1));
+    best_cat.assign(num_leaves, std::array<uint32_t, 8>{});
+    num_cat = 0;
+    for (int32_t f = 0; f < F; ++f)
+      if (meta[f].is_categorical && meta[f].num_bin > 256) return -2;
 
     // root LeafSplits::init: ordered f64 fold over all rows (leaf_splits.rs:75-92)
     LeafSplits smaller, larger;
@@ -724,12 +894,22 @@ struct Learner {
         tree->split_feature[node] = f;
         tree->split_gain[node] = (float)(best.gain + cfg.min_gain_to_split);
         tree->threshold_bin[node] = best.threshold;
+        const bool cat = meta[f].is_categorical != 0;
         tree->internal_value[node] = tree->leaf_value[best_leaf];
         tree->internal_count[node] = leaf_count[new_left] + leaf_count[new_right];
         tree->left_child[node] = ~best_leaf;
         tree->right_child[node] = ~new_right;
         int8_t dt = 0;
-        if (best.default_left) dt |= 2;
+        if (cat) {
+          // Tree::split_categorical (lgbm-model/src/tree.rs:710-770): the threshold
+          // is the categorical-node index, default_left is not encoded
+          dt |= 1;
+          tree->threshold_bin[node] = (uint32_t)num_cat++;
+          if (tree->cat_bins)
+            for (int k = 0; k < 8; ++k) tree->cat_bins[8 * node + k] = best_cat[best_leaf][k];
+        } else if (best.default_left) {
+          dt |= 2;
+        }
         dt |= (int8_t)((meta[f].missing_type & 3) << 2);
         tree->decision_type[node] = dt;
         tree->leaf_value[best_leaf] = best.left_output;

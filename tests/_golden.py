@@ -264,3 +264,35 @@ def bits_line(line, kind="f64"):
 
 def data_lines(name):
     return [l for l in read_text(name).splitlines() if l.strip() and not l.lstrip().startswith("#")]
+
+
+def categorical_binning_cases():
+    """lgbm-dataset categorical_folding.txt (CCASE/VALUES/MAPPER/C2B/B2C/ASSIGN)."""
+    cases = []
+    it = _records(read_text("categorical_folding.txt"))
+    for t in it:
+        if t[0] != "CCASE":
+            continue
+        f = fields(t[1:])
+        rec = {k: int(f[k]) for k in ("max_bin", "min_data_in_bin", "use_missing",
+                                       "zero_as_missing", "pre_filter", "min_split_data",
+                                       "num_rows")}
+        rec["name"] = f["name"]
+        r = next(it)
+        assert r[0] == "VALUES"
+        rec["values"] = f64_list(r[1] if len(r) > 1 else "")
+        r = next(it)
+        assert r[0] == "MAPPER"
+        rec["mapper"] = {k: int(v) for k, v in fields(r[1:]).items()}
+        r = next(it)
+        assert r[0] == "C2B"
+        rec["c2b"] = {int(a): int(b) for a, b in (p.split(":") for p in r[1].split(";"))} \
+            if len(r) > 1 else {}
+        r = next(it)
+        assert r[0] == "B2C"
+        rec["b2c"] = [int(x) for x in r[1].split(";")] if len(r) > 1 else []
+        r = next(it)
+        assert r[0] == "ASSIGN"
+        rec["assign"] = u32_list(r[1] if len(r) > 1 else "")
+        cases.append(rec)
+    return cases

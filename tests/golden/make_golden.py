@@ -35,6 +35,11 @@ FILES = [
     ("crates/oracle-harness/tests/fixtures/quantized/quant_binary.pred_exact", False),
     ("crates/oracle-harness/tests/fixtures/quantized/quant_binary.json", False),
     ("crates/lgbm-dataset/tests/fixtures/numeric_binning.txt", True),
+    ("crates/lgbm-dataset/tests/fixtures/categorical_folding.txt", False),
+    ("crates/oracle-harness/tests/fixtures/categorical/cat_onehot.txt", False),
+    ("crates/oracle-harness/tests/fixtures/categorical/cat_onehot.bins.json", False),
+    ("crates/oracle-harness/tests/fixtures/categorical/cat_manyvsmany.txt", False),
+    ("crates/oracle-harness/tests/fixtures/categorical/cat_manyvsmany.bins.json", False),
     ("crates/oracle-harness/fixtures/rng_sequence.txt", True),
 ]
 

@@ -64,6 +64,32 @@ def test_binning_matches_reference_golden(capi):
         assert bins.tolist() == c["assign"].tolist(), c["name"]
 
 
+def test_categorical_binning_matches_reference_golden(capi):
+    """categorical_folding.txt: descending-count fold, the 0.99 cut, the min_data_in_bin
+    fold break, negative values and the NaN dummy bin 0 (bin_mapper.rs:416-641)."""
+    import lightgbm_rs_b200 as lgb
+
+    cases = G.categorical_binning_cases()
+    assert len(cases) == 6
+    for c in cases:
+        m, bins = lgb.bin_column(c["values"], max_bin=c["max_bin"],
+                                 min_data_in_bin=c["min_data_in_bin"],
+                                 min_data_in_leaf=c["min_split_data"],
+                                 pre_filter=c["pre_filter"], use_missing=c["use_missing"],
+                                 zero_as_missing=c["zero_as_missing"],
+                                 bin_construct_sample_cnt=max(len(c["values"]), 1),
+                                 categorical=True)
+        gm = c["mapper"]
+        assert m["bin_type"] == gm["bin_type"] == 1, c["name"]
+        for k in ("num_bin", "missing_type", "default_bin", "most_freq_bin"):
+            assert m[k] == gm[k], (c["name"], k)
+        assert m["is_trivial"] == bool(gm["is_trivial"]), c["name"]
+        assert m["bin_to_category"].tolist() == c["b2c"], c["name"]
+        c2b = {int(cat): b for b, cat in enumerate(m["bin_to_category"])}
+        assert c2b == c["c2b"], c["name"]
+        assert bins.tolist() == c["assign"].tolist(), c["name"]
+
+
 def test_errors_are_typed_not_crashes(capi):
     L = capi.lib()
     out = np.zeros(4, dtype=np.float64)

@@ -193,3 +193,61 @@ def test_tree_that_stops_early(data):
     for _ in range(2):
         got, _ = learner.grow(quantized=q, scales=[scales[0], scales[1], scales[2], 4])
         _assert_trees_bit_equal(got, want, "early stop")
+
+
+def _missing_data(n=40_000, seed=11):
+    """Numeric features with NaN (missing_type NaN), one zero-as-missing feature and a
+    feature with many exact zeros, in the spirit of the reference's na_missing corpus."""
+    from lightgbm_rs_b200 import synthetic
+
+    X, y = synthetic.binary_c0(num_data=n, num_features=12, seed=seed)
+    rng = np.random.default_rng(seed)
+    X = X.astype(np.float64)
+    for j in (0, 3, 5, 8):
+        X[rng.random(n) < 0.1, j] = np.nan
+    X[rng.random(n) < 0.3, 9] = 0.0
+    return X, y
+
+
+@pytest.mark.parametrize("zero_as_missing", [False, True])
+def test_missing_values_tree_bit_exact(zero_as_missing):
+    """NaN rows go to the NaN bin and are routed by default_left; zero-as-missing
+    features skip the default bin in the scan (learner.rs:167-193)."""
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, y = _missing_data()
+    params = {"max_bin": 255, "min_data_in_leaf": 20, "zero_as_missing": zero_as_missing}
+    ds = lgb.Dataset(X, y, params)
+    kinds = {m["missing_type"] for m in ds.mappers}
+    assert kinds & {1, 2}, kinds
+    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
+             for m in ds.mappers]
+    g, h = oracle.binary_gradients(np.zeros(len(y)), y)
+    gq, hq, q, scales = oracle.quantize(g, h, 4)
+    want, wpart, _ = oracle.grow_tree(ds.bins, metas, gq, hq, num_leaves=63, min_data_in_leaf=20)
+    learner = lgb.Learner(ds, {"num_leaves": 63, "min_data_in_leaf": 20})
+    got, gpart = learner.grow(quantized=q, scales=[scales[0], scales[1], scales[2], 4])
+    _assert_trees_bit_equal(got, want, f"missing zero_as_missing={zero_as_missing}")
+    for a, b in zip(_leaf_sets(gpart, got["num_leaves"]), _leaf_sets(wpart, want["num_leaves"])):
+        assert np.array_equal(a, b)
+
+
+def test_missing_values_booster_bit_exact():
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, y = _missing_data(seed=12)
+    ds = lgb.Dataset(X, y, {"max_bin": 255, "min_data_in_leaf": 20})
+    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
+             for m in ds.mappers]
+    params = {"objective": "binary", "num_leaves": 31, "min_data_in_leaf": 20,
+              "learning_rate": 0.1, "use_quantized_grad": True, "num_grad_quant_bins": 4}
+    booster = lgb.train(params, ds, num_boost_round=6)
+    ref = oracle.train(ds.bins, metas, y, objective="binary", num_iterations=6,
+                       learning_rate=0.1, num_leaves=31, use_quantized_grad=True,
+                       num_grad_quant_bins=4, min_data_in_leaf=20)
+    for i, (a, b) in enumerate(zip(booster.trees(), ref["trees"])):
+        _assert_trees_bit_equal(a, b, f"missing tree {i}")
+    s = booster.train_scores()
+    assert s.view(np.uint64).tolist() == ref["scores"].view(np.uint64).tolist()

@@ -144,3 +144,46 @@ def test_binary_gradients_and_scores_golden(oracle_lib):
         if "bias" in t:
             lv = lv + t["bias"]
         assert [G.g17(x) for x in lv] == [G.g17(x) for x in m["leaf_value"]], f"tree {i}"
+
+
+@pytest.mark.parametrize("name", ["cat_onehot", "cat_manyvsmany"])
+def test_categorical_learner_real_lightgbm_tree(oracle_lib, name):
+    """oracle-harness learner_parity.rs:1486-1535 categorical cells: one categorical feature,
+    hessian 1, grown by the oracle, against the tree lib_lightgbm 4.6 grew (one-hot and
+    sorted many-vs-many splits, the categorical decision bit, cat_boundaries, and the real
+    category bitset cat_threshold)."""
+    import json
+
+    import oracle
+
+    side = json.loads(G.read_text(f"{name}.bins.json"))
+    gold = G.parse_model_text(G.read_text(f"{name}.txt"))[0]
+    gold_raw = dict(l.split("=", 1) for l in G.read_text(f"{name}.txt").splitlines()
+                    if "=" in l and l.split("=", 1)[0] in ("cat_boundaries", "cat_threshold",
+                                                            "num_cat"))
+    bins = np.array(side["bins"], dtype=np.uint32).reshape(1, -1)
+    nb, mfb = int(side["num_bin"]), int(side["most_freq_bin"])
+    metas = [{"num_bin": nb, "default_bin": nb, "most_freq_bin": mfb, "missing_type": 0,
+              "bin_type": 1}]
+    g = np.array(side["grad"], dtype=np.float32)
+    h = np.ones_like(g)
+    tree, _, _ = oracle.grow_tree(bins, metas, g, h, num_leaves=int(side["num_leaves"]),
+                                  min_data_in_leaf=1, min_sum_hessian_in_leaf=1e-3,
+                                  cat_l2=side["cat_l2"], cat_smooth=side["cat_smooth"],
+                                  min_data_per_group=int(side["min_data_per_group"]),
+                                  max_cat_threshold=int(side["max_cat_threshold"]),
+                                  max_cat_to_onehot=int(side["max_cat_to_onehot"]))
+    assert tree["num_leaves"] == gold["num_leaves"]
+    for k in ("split_feature", "decision_type", "left_child", "right_child", "leaf_count",
+              "internal_count"):
+        assert tree[k].tolist() == gold[k].tolist(), k
+    assert [G.g17(float(t)) for t in tree["threshold_bin"]] == \
+        [G.g17(t) for t in gold["threshold"]]
+    b2c = side["bin_2_categorical"]
+    bounds, words = oracle.categorical_bitsets(tree, lambda f: b2c)
+    assert len(bounds) - 1 == int(gold_raw["num_cat"])
+    assert bounds == [int(x) for x in gold_raw["cat_boundaries"].split()]
+    assert words == [int(x) for x in gold_raw["cat_threshold"].split()]
+    shrink = float(side.get("shrinkage", 0.1))
+    lv = [0.0 if abs(v * shrink) <= 1e-35 else v * shrink for v in tree["leaf_value"]]
+    assert [G.g17(v) for v in lv] == [G.g17(v) for v in gold["leaf_value"]]
