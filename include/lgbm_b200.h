@@ -59,6 +59,14 @@ typedef struct lgbm_b200_gain_config {
   double min_gain_to_split;
   double path_smooth;
   double parent_output;
+  /* categorical splits (feature_histogram_categorical.rs; LightGBM defaults 100, 32,
+   * 4, 10, 10) */
+  int32_t min_data_per_group;
+  int32_t max_cat_threshold;
+  int32_t max_cat_to_onehot;
+  int32_t _reserved2;
+  double cat_l2;
+  double cat_smooth;
 } lgbm_b200_gain_config;
 
 /* lgbm_compute::gain::SplitInfo (crates/lgbm-compute/src/gain.rs:1040-1065).
@@ -85,6 +93,7 @@ typedef struct lgbm_b200_feature_meta {
   int32_t default_bin;
   int32_t most_freq_bin;
   int32_t missing_type;
+  int32_t bin_type; /* 0 numerical, 1 categorical (BinType, bin_mapper.rs:22-26) */
 } lgbm_b200_feature_meta;
 
 /* lgbm_compute::BatchedSplitFeature (crates/lgbm-compute/src/kernels/split.rs:77). */
@@ -116,6 +125,11 @@ typedef struct lgbm_b200_tree {
   int32_t* leaf_count;
   double* internal_value;
   int32_t* internal_count;
+  /* per internal node, 8 words: the set of bins a categorical node sends left
+   * (decision_type bit 0; threshold_bin is the categorical-node index); may be
+   * NULL. The category bitsets of the model text follow from the feature's
+   * bin_to_category (Tree::split_categorical, lgbm-model/src/tree.rs:710-770). */
+  uint32_t* cat_bins;
 } lgbm_b200_tree;
 
 /* SerialTreeLearner construction parameters

@@ -16,7 +16,7 @@ from ._lib import LightGBMError
 from . import distributed  # noqa: E402
 
 __all__ = ["Dataset", "Booster", "train", "bin_column", "LightGBMError", "Learner",
-           "distributed"]
+           "distributed", "categorical_bitsets"]
 
 # Reference config defaults (crates/lgbm-core/src/config/mod.rs:430-587).
 _DEFAULTS = {
@@ -41,6 +41,11 @@ _DEFAULTS = {
     "use_quantized_grad": False,
     "num_grad_quant_bins": 4,
     "stochastic_rounding": False,
+    "min_data_per_group": 100,
+    "max_cat_threshold": 32,
+    "max_cat_to_onehot": 4,
+    "cat_l2": 10.0,
+    "cat_smooth": 10.0,
     "boost_from_average": True,
     "sigmoid": 1.0,
     "device": 0,
@@ -113,8 +118,12 @@ class Dataset:
     data: 2-D array [num_data, num_features] of raw values (binned on the host with
     the reference BinMapper), or pass `bins`/`mappers` to reuse an existing binning."""
 
-    def __init__(self, data=None, label=None, params=None, bins=None, mappers=None):
+    def __init__(self, data=None, label=None, params=None, bins=None, mappers=None,
+                 categorical_feature=None):
+        """categorical_feature: column indices binned as categories (non-negative integer
+        codes; negatives and NaN count as missing), as lightgbm's Dataset takes them."""
         self.params = _resolve(params)
+        cats = set(int(c) for c in (categorical_feature or []))
         self.label = None if label is None else np.ascontiguousarray(label, dtype=np.float32)
         if bins is None:
             X = np.asarray(data)
@@ -126,7 +135,8 @@ class Dataset:
                 m, b = bin_column(X[:, j], p["max_bin"], p["min_data_in_bin"],
                                   p["min_data_in_leaf"], p["feature_pre_filter"],
                                   p["use_missing"], p["zero_as_missing"],
-                                  p["bin_construct_sample_cnt"], p["data_random_seed"])
+                                  p["bin_construct_sample_cnt"], p["data_random_seed"],
+                                  categorical=j in cats)
                 mappers.append(m)
                 cols.append(b.astype(np.uint8 if m["num_bin"] <= 256 else np.uint32))
             width = 1 if all(c.dtype == np.uint8 for c in cols) else 4
@@ -141,7 +151,8 @@ class Dataset:
             metas = (C.FeatureMeta * self.num_features)()
             for f, m in enumerate(self.mappers):
                 metas[f] = C.FeatureMeta(int(m["num_bin"]), int(m["default_bin"]),
-                                         int(m["most_freq_bin"]), int(m.get("missing_type", 0)))
+                                         int(m["most_freq_bin"]), int(m.get("missing_type", 0)),
+                                         int(m.get("bin_type", 0)))
             cols = (ctypes.c_void_p * self.num_features)(
                 *[self.bins[f].ctypes.data for f in range(self.num_features)])
             h = ctypes.c_void_p()
@@ -164,7 +175,9 @@ class Dataset:
 def _learner_config(p):
     return C.LearnerConfig(int(p["num_leaves"]), int(p["max_depth"]), C.gain_config(
         p["min_data_in_leaf"], p["min_sum_hessian_in_leaf"], p["max_delta_step"],
-        p["lambda_l1"], p["lambda_l2"], p["min_gain_to_split"], p["path_smooth"]))
+        p["lambda_l1"], p["lambda_l2"], p["min_gain_to_split"], p["path_smooth"], 0.0,
+        p["min_data_per_group"], p["max_cat_threshold"], p["max_cat_to_onehot"], p["cat_l2"],
+        p["cat_smooth"]))
 
 
 class Learner:
@@ -326,6 +339,11 @@ class Booster:
                 mt = np.array([mappers[ff].get("missing_type", 0) for ff in f], dtype=np.int64)
                 na = (mt == 2) & (nb > 2) & (b == nb - 1)
                 right = np.where(na, ~dl, b > thr)
+                cat = (t["decision_type"][nd] & 1) != 0
+                if cat.any():
+                    # categorical node: the bins in the node's set go left
+                    words = t["cat_bins"][nd, np.minimum(b >> 5, 7)].astype(np.int64)
+                    right = np.where(cat, ((words >> (b & 31)) & 1) == 0, right)
                 nxt = np.where(right, t["right_child"][nd], t["left_child"][nd])
                 idx = np.nonzero(active)[0]
                 done = nxt < 0
@@ -339,9 +357,16 @@ class Booster:
         X = np.asarray(data, dtype=np.float64)
         cols = []
         for j, m in enumerate(self.train_set.mappers):
-            up = m["upper"]
             v = X[:, j].copy()
             nanm = np.isnan(v)
+            if m.get("bin_type", 0) == 1:
+                # categorical value_to_bin: the category's bin; NaN, negative, unseen -> 0
+                lut = {int(c): b for b, c in enumerate(m["bin_to_category"]) if c >= 0}
+                iv = np.where(nanm, -1, np.trunc(np.where(nanm, 0, v))).astype(np.int64)
+                cols.append(np.array([lut.get(int(c), 0) if c >= 0 else 0 for c in iv],
+                                     dtype=np.int64))
+                continue
+            up = m["upper"]
             if m.get("missing_type", 0) == 2:
                 b = np.searchsorted(up[:-1][: m["num_bin"] - 1], v, side="left")
                 b = np.minimum(b, m["num_bin"] - 2)
@@ -376,3 +401,23 @@ def train(params, train_set, num_boost_round=100, comm=None):
     b = Booster(p, train_set, comm=comm)
     b.update(int(num_boost_round))
     return b
+
+
+def categorical_bitsets(tree, mappers):
+    """cat_boundaries / cat_threshold of a tree as the LightGBM model text holds them
+    (Tree::split_categorical, lgbm-model/src/tree.rs:710-770): for each categorical node
+    in node order, the bitset of the categories whose bins the node sends left."""
+    bounds, words = [0], []
+    for node, dt in enumerate(tree["decision_type"]):
+        if not (int(dt) & 1):
+            continue
+        b2c = mappers[int(tree["split_feature"][node])]["bin_to_category"]
+        bits = tree["cat_bins"][node]
+        cats = [int(b2c[b]) for b in range(min(len(b2c), 256))
+                if (int(bits[b >> 5]) >> (b & 31)) & 1]
+        blk = [0] * (max(cats) // 32 + 1 if cats else 0)
+        for c in cats:
+            blk[c // 32] |= 1 << (c % 32)
+        words.extend(blk)
+        bounds.append(bounds[-1] + len(blk))
+    return bounds, words

@@ -42,7 +42,10 @@ class GainConfig(ctypes.Structure):
     _fields_ = [("min_data_in_leaf", _i32), ("_reserved", _i32),
                 ("min_sum_hessian_in_leaf", _f64), ("max_delta_step", _f64),
                 ("lambda_l1", _f64), ("lambda_l2", _f64), ("min_gain_to_split", _f64),
-                ("path_smooth", _f64), ("parent_output", _f64)]
+                ("path_smooth", _f64), ("parent_output", _f64),
+                ("min_data_per_group", _i32), ("max_cat_threshold", _i32),
+                ("max_cat_to_onehot", _i32), ("_reserved2", _i32), ("cat_l2", _f64),
+                ("cat_smooth", _f64)]
 
 
 class SplitInfo(ctypes.Structure):
@@ -54,7 +57,7 @@ class SplitInfo(ctypes.Structure):
 
 class FeatureMeta(ctypes.Structure):
     _fields_ = [("num_bin", _i32), ("default_bin", _i32), ("most_freq_bin", _i32),
-                ("missing_type", _i32)]
+                ("missing_type", _i32), ("bin_type", _i32)]
 
 
 class BatchedFeature(ctypes.Structure):
@@ -68,7 +71,7 @@ class TreeC(ctypes.Structure):
                 ("right_child", _P), ("split_feature", _P), ("threshold_bin", _P),
                 ("split_gain", _P), ("decision_type", _P), ("leaf_value", _P),
                 ("leaf_weight", _P), ("leaf_count", _P), ("internal_value", _P),
-                ("internal_count", _P)]
+                ("internal_count", _P), ("cat_bins", _P)]
 
 
 class LearnerConfig(ctypes.Structure):
@@ -174,10 +177,13 @@ def device_count():
 
 def gain_config(min_data_in_leaf=20, min_sum_hessian_in_leaf=1e-3, max_delta_step=0.0,
                 lambda_l1=0.0, lambda_l2=0.0, min_gain_to_split=0.0, path_smooth=0.0,
-                parent_output=0.0):
+                parent_output=0.0, min_data_per_group=100, max_cat_threshold=32,
+                max_cat_to_onehot=4, cat_l2=10.0, cat_smooth=10.0):
     return GainConfig(int(min_data_in_leaf), 0, float(min_sum_hessian_in_leaf),
                       float(max_delta_step), float(lambda_l1), float(lambda_l2),
-                      float(min_gain_to_split), float(path_smooth), float(parent_output))
+                      float(min_gain_to_split), float(path_smooth), float(parent_output),
+                      int(min_data_per_group), int(max_cat_threshold), int(max_cat_to_onehot),
+                      0, float(cat_l2), float(cat_smooth))
 
 
 TREE_FIELDS = [
@@ -197,6 +203,8 @@ def tree_buffers(max_leaves):
     for name, dt, delta in TREE_FIELDS:
         arrays[name] = np.zeros(max(max_leaves + delta, 1), dtype=dt)
         setattr(t, name, arrays[name].ctypes.data)
+    arrays["cat_bins"] = np.zeros((max(max_leaves - 1, 1), 8), dtype=np.uint32)
+    t.cat_bins = arrays["cat_bins"].ctypes.data
     return t, arrays
 
 
@@ -205,4 +213,5 @@ def tree_dict(t, arrays):
     out = {"num_leaves": nl}
     for name, _, delta in TREE_FIELDS:
         out[name] = arrays[name][: max(nl + delta, 0)].copy()
+    out["cat_bins"] = arrays["cat_bins"][: max(nl - 1, 0)].copy()
     return out

@@ -109,6 +109,12 @@ DevGainConfig to_dev_gain(const lgbm_b200_gain_config& g) {
   c.lambda_l2 = g.lambda_l2;
   c.min_gain_to_split = g.min_gain_to_split;
   c.path_smooth = g.path_smooth;
+  c.min_data_per_group = g.min_data_per_group;
+  c.max_cat_threshold = g.max_cat_threshold;
+  c.max_cat_to_onehot = g.max_cat_to_onehot;
+  c._pad = 0;
+  c.cat_l2 = g.cat_l2;
+  c.cat_smooth = g.cat_smooth;
   return c;
 }
 
@@ -214,6 +220,7 @@ struct lgbm_b200_learner {
   DevBuf<long long> rawpool;
   DevBuf<long long> partials;
   DevBuf<DevSplitInfo> scan_out;
+  DevBuf<uint32_t> cat_words;  // scan_cat [2F][8] | best_cat [L][8] | t_cat [L][8] | split_cat [8]
   DevBuf<uint8_t> scan_ok;
   // gradients owned by a standalone learner (the booster owns its own)
   DevBuf<uint8_t> gh;
@@ -336,6 +343,9 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   CUDA_TRY(partials.alloc((size_t)kPrivateTiles * slot_len));
 
   CUDA_TRY(scan_out.alloc((size_t)2 * ds->num_features));
+  CUDA_TRY(cat_words.alloc((size_t)kCatWords * (2 * ds->num_features + 2 * L + 1)));
+  CUDA_TRY(cudaMemset(cat_words.p, 0,
+                      sizeof(uint32_t) * kCatWords * (2 * ds->num_features + 2 * L + 1)));
   CUDA_TRY(scan_ok.alloc(2));
   d = GrowDev{};
   d.ctrl = ctrl.p;
@@ -383,6 +393,13 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.raw_len = slot_len;
   d.n_global = N;
   d.scan_out = scan_out.p;
+  d.scan_cat = cat_words.p;
+  d.best_cat = cat_words.p + (size_t)kCatWords * 2 * ds->num_features;
+  d.t_cat = d.best_cat + (size_t)kCatWords * L;
+  d.split_cat = d.t_cat + (size_t)kCatWords * L;
+  d.has_cat = 0;
+  for (const DevFeature& f : ds->feats)
+    if (f.flags & kFeatCategorical) d.has_cat = 1;
   d.scan_ok = scan_ok.p;
   return LGBM_B200_OK;
 }
@@ -439,6 +456,9 @@ int read_tree(lgbm_b200_learner* l, lgbm_b200_tree* out) {
     if (out->leaf_weight) out->leaf_weight[i] = tf[L + i];
     if (out->leaf_count) out->leaf_count[i] = ti[3 * L + i];
   }
+  if (out->cat_bins && nl > 1)
+    CUDA_TRY(cudaMemcpy(out->cat_bins, l->d.t_cat, sizeof(uint32_t) * kCatWords * (nl - 1),
+                        cudaMemcpyDeviceToHost));
   return LGBM_B200_OK;
 }
 
@@ -543,6 +563,7 @@ struct lgbm_b200_booster {
   DevBuf<float> rec_gain;
   DevBuf<int8_t> rec_dec;
   DevBuf<double> rec_f64;  // leaf_value, leaf_weight, internal_value
+  DevBuf<uint32_t> rec_cat;  // [cap][L][kCatWords] categorical node bins
   double init_score = 0.0;
   ObjDev obj{};
   FinishDev fin{};
@@ -572,7 +593,9 @@ int lgbm_b200_booster::ensure_capacity(int32_t need) {
   DevBuf<float> gain;
   DevBuf<int8_t> dec;
   DevBuf<double> f64;
+  DevBuf<uint32_t> catw;
   CUDA_TRY(i32.alloc((size_t)cap + (size_t)5 * cap * L));
+  CUDA_TRY(catw.alloc((size_t)cap * L * kCatWords));
   CUDA_TRY(thr.alloc((size_t)cap * L));
   CUDA_TRY(gain.alloc((size_t)cap * L));
   CUDA_TRY(dec.alloc((size_t)cap * L));
@@ -589,6 +612,7 @@ int lgbm_b200_booster::ensure_capacity(int32_t need) {
     for (int a = 0; a < 3; ++a)
       CUDA_TRY(cudaMemcpy(f64.p + a * nc * L_, rec_f64.p + a * oc * L_, oc * L_ * 8,
                           cudaMemcpyDeviceToDevice));
+    CUDA_TRY(cudaMemcpy(catw.p, rec_cat.p, oc * L_ * kCatWords * 4, cudaMemcpyDeviceToDevice));
   }
   std::swap(rec_i32.p, i32.p);
   std::swap(rec_i32.n, i32.n);
@@ -600,6 +624,8 @@ int lgbm_b200_booster::ensure_capacity(int32_t need) {
   std::swap(rec_dec.n, dec.n);
   std::swap(rec_f64.p, f64.p);
   std::swap(rec_f64.n, f64.n);
+  std::swap(rec_cat.p, catw.p);
+  std::swap(rec_cat.n, catw.n);
   capacity = cap;
   const size_t nc = cap, L_ = L;
   fin.max_iters = cap;
@@ -615,6 +641,7 @@ int lgbm_b200_booster::ensure_capacity(int32_t need) {
   fin.rec_leaf_value = rec_f64.p;
   fin.rec_leaf_weight = rec_f64.p + nc * L_;
   fin.rec_internal_value = rec_f64.p + 2 * nc * L_;
+  fin.rec_cat = rec_cat.p;
   destroy_graph();  // pointers changed
   return LGBM_B200_OK;
 }
@@ -698,7 +725,7 @@ extern "C" {
 
 const char* lgbm_b200_last_error(void) { return g_last_error.c_str(); }
 
-int32_t lgbm_b200_abi_version(void) { return 100; }
+int32_t lgbm_b200_abi_version(void) { return 101; }
 
 int lgbm_b200_device_count(int32_t* out) {
   int n = 0;
@@ -1045,6 +1072,9 @@ int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t
                   "feature %d: num_bin %d outside 1..256 (u8 bin matrix)", f, meta[f].num_bin);
     if (meta[f].most_freq_bin < 0 || meta[f].most_freq_bin >= meta[f].num_bin)
       return fail(LGBM_B200_INVALID_ARGUMENT, "feature %d: most_freq_bin out of range", f);
+    if (meta[f].bin_type != 0 && meta[f].bin_type != 1)
+      return fail(LGBM_B200_INVALID_ARGUMENT, "feature %d: bin_type %d is not 0 or 1", f,
+                  meta[f].bin_type);
   }
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
@@ -1063,6 +1093,7 @@ int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t
   for (int f = 0; f < num_features; ++f) {
     DevFeature d = make_feature(meta[f].num_bin, meta[f].default_bin, meta[f].most_freq_bin,
                                 meta[f].missing_type);
+    if (meta[f].bin_type == 1) d.flags |= kFeatCategorical;
     d.bin_off = bin_off;
     d.slot_off = 2 * bin_off;
     bin_off += meta[f].num_bin;
@@ -1505,6 +1536,7 @@ int lgbm_b200_booster_get_tree(lgbm_b200_booster* b, int32_t index, lgbm_b200_tr
   CUDA_TRY(cp(out->leaf_value, b->fin.rec_leaf_value + it * L, nl * 8));
   CUDA_TRY(cp(out->leaf_weight, b->fin.rec_leaf_weight + it * L, nl * 8));
   CUDA_TRY(cp(out->leaf_count, b->fin.rec_leaf_count + it * L, nl * 4));
+  CUDA_TRY(cp(out->cat_bins, b->fin.rec_cat + it * L * kCatWords, ni * kCatWords * 4));
   (void)cap;
   return LGBM_B200_OK;
 }

@@ -28,7 +28,8 @@ struct DevFeature {
   int32_t missing_type;  // 0 None, 1 Zero, 2 NaN
   int32_t slot_off;      // first cell of this feature in a histogram slot (cells = 2*num_bin)
   int32_t bin_off;       // first bin of this feature in the raw accumulator (bins)
-  int32_t flags;         // bit0 skip_default_bin, bit1 na_as_missing, bit2 run_forward
+  int32_t flags;         // bit0 skip_default_bin, bit1 na_as_missing, bit2 run_forward,
+                         // bit3 categorical
   int32_t route_min;     // partition min_bin (learner.rs:3957: min_bin + offset)
   int32_t route_max;     // partition max_bin (num_bin - 1)
 };
@@ -44,7 +45,16 @@ struct DevGainConfig {
   double lambda_l2;
   double min_gain_to_split;
   double path_smooth;
+  int32_t min_data_per_group;
+  int32_t max_cat_threshold;
+  int32_t max_cat_to_onehot;
+  int32_t _pad;
+  double cat_l2;
+  double cat_smooth;
 };
+
+constexpr int32_t kFeatCategorical = 8;  // DevFeature::flags bit of categorical features
+constexpr int kCatWords = 8;             // bins sent left by a categorical split (<= 256)
 
 // lgbm_compute::gain::SplitInfo (gain.rs:1040-1065) in a flat layout.
 struct DevSplitInfo {
@@ -129,6 +139,8 @@ struct GrowCtrl {
   int32_t build_left;      // the pending split's left rows are accumulated (else right)
   long long rows_built;    // rows streamed by those builds
   long long rows_parted;   // parent rows streamed by the partitions
+  int32_t num_cat;         // categorical nodes in the tree so far
+  int32_t _pad3;
   DevSplitInfo split;
 };
 
@@ -225,6 +237,12 @@ __device__ __forceinline__ DevSplitInfo d_split_none() {
 }
 
 // Row-to-child routing of DataPartition::split (lgbm-treelearner/src/data_partition.rs:360-432).
+// Row routing of a categorical split: the chosen bins go left
+// (DataPartition::split_categorical, data_partition.rs:636-688).
+__device__ __forceinline__ bool d_cat_go_right(const uint32_t* cat, int32_t bin) {
+  return !((cat[bin >> 5] >> (bin & 31)) & 1u);
+}
+
 __device__ __forceinline__ bool d_go_right(const DevFeature& f, uint32_t threshold,
                                            bool default_left, int32_t bin) {
   int32_t th = (int32_t)threshold + f.route_min;

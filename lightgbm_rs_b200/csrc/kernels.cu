@@ -848,6 +848,7 @@ struct Prep {
   int32_t leaf, nr, node, parent, parent_is_right;
   int32_t lc, rc, lcg, rcg, dst, beg, depth;
   int32_t feature;
+  int32_t cat_index;  // categorical node: its index among the tree's categorical nodes
   int8_t dt;
   float split_gain;
   double old_value;
@@ -910,7 +911,16 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
     P.depth = depth;
     P.feature = f;
     int8_t dt = 0;
-    if (b.default_left) dt |= 2;
+    P.cat_index = -1;
+    if (d.feat[f].flags & kFeatCategorical) {
+      // Tree::split_categorical (lgbm-model/src/tree.rs:710-770): categorical bit, the
+      // node's threshold is its categorical-node index, default_left is not encoded
+      dt |= 1;
+      P.cat_index = c.num_cat;
+      c.num_cat += 1;
+    } else if (b.default_left) {
+      dt |= 2;
+    }
     dt |= (int8_t)((mt & 3) << 2);
     P.dt = dt;
     P.split_gain = (float)(b.gain + d.gain.min_gain_to_split);
@@ -1051,7 +1061,9 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   P.lsLg = ls_larger;
 }
 
-// Writes of the control step except the control block itself.
+// Writes of the control step except the control block itself. CAT: the dataset has
+// categorical features, whose nodes also record their bin set.
+template <bool CAT>
 __device__ void prep_commit(const GrowDev& d, const Prep& P) {
   if (P.applied) {
     const int32_t leaf = P.leaf, nr = P.nr, node = P.node;
@@ -1072,7 +1084,10 @@ __device__ void prep_commit(const GrowDev& d, const Prep& P) {
     }
     d.t_split_feature[node] = P.feature;
     d.t_split_gain[node] = P.split_gain;
-    d.t_threshold[node] = b.threshold;
+    d.t_threshold[node] = P.cat_index >= 0 ? (uint32_t)P.cat_index : b.threshold;
+    if (CAT)
+      for (int k = 0; k < kCatWords; ++k)
+        d.t_cat[(size_t)node * kCatWords + k] = P.cat_index >= 0 ? d.split_cat[k] : 0u;
     d.t_internal_value[node] = P.old_value;
     d.t_internal_count[node] = P.lcg + P.rcg;
     d.t_left[node] = ~leaf;
@@ -1107,7 +1122,10 @@ __global__ void k_prepare(GrowDev d, int s) {
   if (threadIdx.x != 0) return;
   Prep P;
   prep_compute(d, s, P);
-  prep_commit(d, P);
+  if (d.has_cat)
+    prep_commit<true>(d, P);
+  else
+    prep_commit<false>(d, P);
   *d.ctrl = P.c;
 }
 
@@ -1173,11 +1191,14 @@ struct PickOut {
   int32_t done;        // no leaf has a positive gain: the tree is finished
   int32_t leaf, feature, build_left;
   DevSplitInfo split;  // the split to apply next
+  uint32_t si_cat[2][kCatWords];  // left bins of si[] when their feature is categorical
+  uint32_t split_cat[kCatWords];  // left bins of `split`
 };
 
 // Cross-feature argmax of both scanned leaves (learner.rs:3314-3321) and the arg_max
 // over all leaves (learner.rs:4537-4551, first max under split_gt, learner.rs:1503-1505
 // stop rule), by one warp: the feature candidates are reduced with shuffles only.
+template <bool CAT>
 __device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand& other, PickOut& o) {
   const int lane = threadIdx.x & 31;
   const bool find = P.live != 0;
@@ -1202,9 +1223,16 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand& other, Pi
     if (lane == 0) {
       o.si[0] = bf0 >= 0 ? d.scan_out[bf0] : d_split_none();
       o.bf[0] = bf0;
+      if (CAT)
+        for (int k = 0; k < kCatWords; ++k)
+          o.si_cat[0][k] = bf0 >= 0 ? d.scan_cat[(size_t)bf0 * kCatWords + k] : 0u;
     } else if (lane == 1) {
       o.si[1] = (Lg >= 0 && bf1 >= 0) ? d.scan_out[d.F + bf1] : d_split_none();
       o.bf[1] = bf1;
+      if (CAT)
+        for (int k = 0; k < kCatWords; ++k)
+          o.si_cat[1][k] =
+              (Lg >= 0 && bf1 >= 0) ? d.scan_cat[((size_t)d.F + bf1) * kCatWords + k] : 0u;
     }
     const Cand a{ok0 ? f0.g : kNegInf, ok0 ? f0.f : -1, S};
     if (best.i == 0x7fffffff || cand_better(a.g, a.f, a.i, best.g, best.f, best.i)) best = a;
@@ -1222,13 +1250,221 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand& other, Pi
       o.done = 0;
       o.leaf = bl;
       o.feature = best.f;
-      const DevSplitInfo sp =
-          (find && bl == S) ? o.si[0] : (find && bl == Lg) ? o.si[1] : d.best[bl];
+      const int sel = (find && bl == S) ? 0 : (find && bl == Lg) ? 1 : -1;
+      const DevSplitInfo sp = sel == 0 ? o.si[0] : sel == 1 ? o.si[1] : d.best[bl];
       o.split = sp;
+      if (CAT)
+        for (int k = 0; k < kCatWords; ++k)
+          o.split_cat[k] = sel >= 0 ? o.si_cat[sel][k] : d.best_cat[(size_t)bl * kCatWords + k];
       // accumulate the side the scan expects to be smaller (any side is exact)
       o.build_left = sp.left_count <= sp.right_count ? 1 : 0;
     }
   }
+}
+
+// ------------------------------------------------------------------------------------
+// Categorical split finder for one leaf by one 256-thread group
+// (find_best_threshold_categorical, lgbm-treelearner/src/feature_histogram_categorical.rs
+// :96-490, LightGBM FindBestThresholdCategoricalInner). One-hot (num_bin <=
+// max_cat_to_onehot): every category is a candidate on its own, one per thread.
+// Many-vs-many: the categories with enough rows are ranked by grad / (hess +
+// cat_smooth) (a stable sort: ties keep bin order), then two lanes run the reference's
+// sequential prefix chains from both ends. `out->bits` gets the bins sent left.
+// ------------------------------------------------------------------------------------
+
+struct CatOut {
+  DevSplitInfo si;
+  uint32_t bits[kCatWords];
+};
+
+__device__ void cat_scan(const double* hist, const DevFeature& ft, const DevGainConfig& cfg,
+                         const ScanLeaf& leaf, ScanScratch& s, int bar_id, CatOut* out) {
+  const int gt = threadIdx.x & (kScanGroup - 1);
+  const int lane = gt & 31, wg = gt >> 5;
+  const double eps = k_eps();
+  const int nb = ft.num_bin, offset = ft.offset;
+  const double sum_g = leaf.sum_g;
+  const double sum_h = leaf.sum_h + 2.0 * eps;  // bumped at the call site (learner.rs:3104-3109)
+  const int32_t nd = leaf.num_data;
+  const double cf = (double)nd / sum_h;
+  const int bin_start = 1 - offset, bin_end = nb - offset;
+  const int nscan = max(bin_end - bin_start, 0);
+  const bool onehot = nb <= cfg.max_cat_to_onehot;
+  const int32_t min_data = cfg.min_data_in_leaf;
+  const double min_hess = cfg.min_sum_hessian_in_leaf;
+  const double po = leaf.parent_output;
+  // gain_shift uses the original l2 and, without smoothing, no smoothing at all
+  double gain_shift;
+  if (cfg.use_smoothing) {
+    const double sg = cfg.use_l1 ? d_threshold_l1(sum_g, cfg.lambda_l1) : sum_g;
+    gain_shift = -fma(2.0 * sg, po, (sum_h + cfg.lambda_l2) * po * po);
+  } else {
+    DevGainConfig c0 = cfg;
+    c0.use_smoothing = 0;
+    c0.use_full = cfg.max_delta_step > 0.0 ? 1 : 0;
+    gain_shift = d_leaf_gain_full(c0, sum_g, sum_h, nd, 0.0);
+  }
+  const double mgs = gain_shift + cfg.min_gain_to_split;
+  DevGainConfig c2 = cfg;  // per-category gains and outputs: many-vs-many adds cat_l2
+  if (!onehot) c2.lambda_l2 = cfg.lambda_l2 + cfg.cat_l2;
+  auto gains = [&](double lg, double lh, double rg, double rh, int32_t lc, int32_t rc) {
+    return d_leaf_gain_full(c2, lg, lh, lc, po) + d_leaf_gain_full(c2, rg, rh, rc, po);
+  };
+  double best_gain = kNegInf, best_slg = 0.0, best_slh = 0.0;
+  int32_t best_lc = 0, best_thr = -1, best_dir = 1;
+  bool splittable = false;
+  int32_t* sorted = reinterpret_cast<int32_t*>(s.ph);
+  int used = 0;
+  if (onehot) {
+    const int t = bin_start + gt;
+    double cg = kNegInf;
+    if (gt < nscan) {
+      const double gr = hist[2 * t], he = hist[2 * t + 1];
+      const int32_t cnt = d_round_int(he * cf);
+      const int32_t other = nd - cnt;
+      const double soh = sum_h - he - eps;
+      if (!(cnt < min_data || he < min_hess) && other >= min_data && soh >= min_hess) {
+        const double v = gains(sum_g - gr, soh, gr, he + eps, other, cnt);
+        if (v > mgs) cg = v;
+      }
+    }
+    // first maximum in bin order
+    int32_t bt = cg > kNegInf ? t : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1) {
+      const double og = __shfl_xor_sync(0xffffffffu, cg, o);
+      const int32_t ot = __shfl_xor_sync(0xffffffffu, bt, o);
+      if (og > cg || (og == cg && ot < bt)) {
+        cg = og;
+        bt = ot;
+      }
+    }
+    if (lane == 0) {
+      s.wgain[wg] = cg;
+      s.wk[wg] = bt;
+    }
+    group_sync(bar_id);
+    if (gt == 0) {
+      for (int w = 1; w < kScanGroup / 32; ++w)
+        if (s.wgain[w] > cg || (s.wgain[w] == cg && s.wk[w] < bt)) {
+          cg = s.wgain[w];
+          bt = s.wk[w];
+        }
+      if (cg > kNegInf) {
+        splittable = true;
+        best_gain = cg;
+        best_thr = bt;
+        best_slg = hist[2 * bt];
+        best_slh = hist[2 * bt + 1] + eps;
+        best_lc = d_round_int(hist[2 * bt + 1] * cf);
+      }
+    }
+  } else {
+    const int t = bin_start + gt;
+    bool keep = false;
+    double ctr = 0.0;
+    if (gt < nscan) {
+      keep = (double)d_round_int(hist[2 * t + 1] * cf) >= cfg.cat_smooth;
+      ctr = hist[2 * t] / (hist[2 * t + 1] + cfg.cat_smooth);
+    }
+    s.pg[gt] = ctr;
+    s.pc[gt] = keep ? 1 : 0;
+    group_sync(bar_id);
+    int rank = 0;
+    for (int u = 0; u < nscan; ++u) {
+      if (!s.pc[u]) continue;
+      ++used;
+      const double cu = s.pg[u];
+      if (cu < ctr || (cu == ctr && u < gt)) ++rank;
+    }
+    group_sync(bar_id);
+    if (keep) sorted[rank] = t;
+    group_sync(bar_id);
+    if (gt == 0 || gt == 32) {
+      const int di = gt == 0 ? 0 : 1;
+      const int dir = di == 0 ? 1 : -1;
+      int pos = di == 0 ? 0 : used - 1;
+      const int max_num_cat = min(cfg.max_cat_threshold, (used + 1) / 2);
+      int32_t cnt_group = 0, lc = 0;
+      double slg = 0.0, slh = eps;
+      double bg = kNegInf, bslg = 0.0, bslh = 0.0;
+      int32_t blc = 0, bi = -1, has = 0;
+      for (int i = 0; i < used && i < max_num_cat; ++i) {
+        const int tt = sorted[pos];
+        pos += dir;
+        const double gr = hist[2 * tt], he = hist[2 * tt + 1];
+        const int32_t cnt = d_round_int(he * cf);
+        slg += gr;
+        slh += he;
+        lc += cnt;
+        cnt_group += cnt;
+        if (lc < min_data || slh < min_hess) continue;
+        const int32_t rc = nd - lc;
+        if (rc < min_data || rc < cfg.min_data_per_group) break;
+        const double srh = sum_h - slh;
+        if (srh < min_hess) break;
+        if (cnt_group < cfg.min_data_per_group) continue;
+        cnt_group = 0;
+        const double v = gains(slg, slh, sum_g - slg, srh, lc, rc);
+        if (v <= mgs) continue;
+        has = 1;
+        if (v > bg) {
+          blc = lc;
+          bslg = slg;
+          bslh = slh;
+          bi = i;
+          bg = v;
+        }
+      }
+      s.wgain[4 * di + 0] = bg;
+      s.wgain[4 * di + 1] = bslg;
+      s.wgain[4 * di + 2] = bslh;
+      s.wk[4 * di + 0] = blc;
+      s.wk[4 * di + 1] = bi;
+      s.whas[4 * di] = has;
+    }
+    group_sync(bar_id);
+    if (gt == 0) {
+      for (int di = 0; di < 2; ++di) {
+        if (s.whas[4 * di]) splittable = true;
+        if (s.wk[4 * di + 1] >= 0 && s.wgain[4 * di] > best_gain) {
+          best_gain = s.wgain[4 * di];
+          best_slg = s.wgain[4 * di + 1];
+          best_slh = s.wgain[4 * di + 2];
+          best_lc = s.wk[4 * di];
+          best_thr = s.wk[4 * di + 1];
+          best_dir = di == 0 ? 1 : -1;
+        }
+      }
+    }
+  }
+  if (gt != 0) return;
+  for (int k = 0; k < kCatWords; ++k) out->bits[k] = 0u;
+  DevSplitInfo si = d_split_none();
+  si.default_left = 0;
+  if (splittable && best_thr >= 0) {
+    const int32_t rc = nd - best_lc;
+    si.threshold = 0;
+    si.gain = best_gain - mgs;
+    si.left_count = best_lc;
+    si.right_count = rc;
+    si.left_output = d_leaf_output_full(c2, c2.use_smoothing, best_slg, best_slh, best_lc, po);
+    si.left_sum_gradient = best_slg;
+    si.left_sum_hessian = best_slh - eps;
+    si.right_output = d_leaf_output_full(c2, c2.use_smoothing, sum_g - best_slg,
+                                         sum_h - best_slh, rc, po);
+    si.right_sum_gradient = sum_g - best_slg;
+    si.right_sum_hessian = sum_h - best_slh - eps;
+    if (onehot) {
+      const int b = best_thr + offset;
+      out->bits[b >> 5] |= 1u << (b & 31);
+    } else {
+      for (int i = 0; i <= best_thr; ++i) {
+        const int b = (best_dir == 1 ? sorted[i] : sorted[used - 1 - i]) + offset;
+        out->bits[b >> 5] |= 1u << (b & 31);
+      }
+    }
+  }
+  out->si = si;
 }
 
 // Shared memory of one feature's control-step work (decode, FixHistogram, scans).
@@ -1237,12 +1473,14 @@ struct FixScanSmem {
   ScanScratch scan[4];
   ScanCand cand[4];
   double fix[2 * kMaxBins / 32][3];  // per-warp exact sums for FixHistogram
+  CatOut cat[2];                     // categorical results of the two scanned leaves
 };
 
 // Feature f of one control step (every thread of the CTA calls it): the smaller child's
 // histogram cells (accumulated by the partition, or derived from the parent), FixHistogram,
 // compaction, the larger child by subtraction, and the REVERSE/FORWARD scans of both
 // children.
+template <bool CAT>
 __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanSmem& sm) {
   const int tid = threadIdx.x;
   const DevFeature ft = d.feat[f];
@@ -1386,11 +1624,16 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
       const int sel = grp >> 1;
       const bool fwd = (grp & 1) != 0;
       const int32_t leaf = sel == 0 ? S : Lg;
+      const bool is_cat = CAT && (ft.flags & kFeatCategorical) != 0;
       if (leaf >= 0) {
         const DevLeafSplits ls = sel == 0 ? P.lsS : P.lsLg;
         if (leaf_buildable(ls)) {
           ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
-          scan_direction(sm.hist[sel], ft, d.gain, sl, fwd, sm.scan[grp], 1 + grp, &sm.cand[grp]);
+          if (!is_cat)
+            scan_direction(sm.hist[sel], ft, d.gain, sl, fwd, sm.scan[grp], 1 + grp,
+                           &sm.cand[grp]);
+          else if (!fwd)  // bin_type dispatch (learner.rs:3099-3149)
+            cat_scan(sm.hist[sel], ft, d.gain, sl, sm.scan[grp], 1 + grp, &sm.cat[sel]);
         }
       }
       __syncthreads();
@@ -1403,8 +1646,14 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
           if (f == 0) d.scan_ok[sl_i] = scannable ? 1 : 0;
           DevSplitInfo si = d_split_none();
           if (scannable) {
-            ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
-            si = finalize_split(d.gain, sl, sm.cand[2 * sl_i], sm.cand[2 * sl_i + 1]);
+            if (is_cat) {
+              si = sm.cat[sl_i].si;
+              uint32_t* dst = d.scan_cat + ((size_t)sl_i * d.F + f) * kCatWords;
+              for (int k = 0; k < kCatWords; ++k) dst[k] = sm.cat[sl_i].bits[k];
+            } else {
+              ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
+              si = finalize_split(d.gain, sl, sm.cand[2 * sl_i], sm.cand[2 * sl_i + 1]);
+            }
           }
           d.scan_out[sl_i * d.F + f] = si;
         }
@@ -1431,6 +1680,7 @@ struct CtlSmem {
 // One control step by the CTAs [0, min(F, gridDim.x)), each taking features
 // blockIdx.x, blockIdx.x + gridDim.x, ...: apply the pending split, scan the two leaves,
 // and -- in the CTA that finishes last -- pick the next split and write the control block.
+template <bool CAT>
 __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& cs) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -1443,7 +1693,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   }
   __syncthreads();
   for (int f = blockIdx.x; f < d.F; f += gridDim.x) {
-    fixscan_feature(d, cs.prep, f, sm);
+    fixscan_feature<CAT>(d, cs.prep, f, sm);
     __syncthreads();
   }
   // last CTA: the pick (warp 0) and the control step's writes (warp 1) run side by side;
@@ -1459,9 +1709,9 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   __threadfence();
   const Prep& P = cs.prep;
   if (warp == 0) {
-    if (!P.c.done) pick_warp(d, P, cs.other, cs.pick);
+    if (!P.c.done) pick_warp<CAT>(d, P, cs.other, cs.pick);
   } else if (warp == 1 && (tid & 31) == 0) {
-    prep_commit(d, P);
+    prep_commit<CAT>(d, P);
   }
   __syncthreads();
   if (tid == 0) {
@@ -1471,9 +1721,15 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
       if (P.live) {
         d.best[P.S] = cs.pick.si[0];
         d.best_feature[P.S] = cs.pick.bf[0];
+        if (CAT)
+          for (int k = 0; k < kCatWords; ++k)
+            d.best_cat[(size_t)P.S * kCatWords + k] = cs.pick.si_cat[0][k];
         if (P.Lg >= 0) {
           d.best[P.Lg] = cs.pick.si[1];
           d.best_feature[P.Lg] = cs.pick.bf[1];
+          if (CAT)
+            for (int k = 0; k < kCatWords; ++k)
+              d.best_cat[(size_t)P.Lg * kCatWords + k] = cs.pick.si_cat[1][k];
         }
       }
       if (cs.pick.done) {
@@ -1484,16 +1740,19 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
         c.split_feature = cs.pick.feature;
         c.split = cs.pick.split;
         c.build_left = cs.pick.build_left;
+        if (CAT)
+          for (int k = 0; k < kCatWords; ++k) d.split_cat[k] = cs.pick.split_cat[k];
       }
     }
     *d.ctrl = c;
   }
 }
 
+template <bool CAT>
 __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
   __shared__ FixScanSmem sm;
   __shared__ CtlSmem cs;
-  control_step(d, s, sm, cs);
+  control_step<CAT>(d, s, sm, cs);
 }
 
 // ------------------------------------------------------------------------------------
@@ -1515,7 +1774,8 @@ struct PartitionTile {
                              bool default_left, const uint32_t* __restrict__ src,
                              bool identity, uint32_t* __restrict__ dst, int32_t begin,
                              int32_t count, int32_t tile, uint32_t epoch,
-                             unsigned long long* status, int32_t* left_total) {
+                             unsigned long long* status, int32_t* left_total,
+                             const uint32_t* cat = nullptr) {
     __shared__ int32_t s_warp[kPartThreads / 32];
     __shared__ int32_t s_prefix;
     __shared__ int32_t s_ok;
@@ -1532,7 +1792,8 @@ struct PartitionTile {
         rows[j] = row;
         const int32_t bin = bins[(size_t)row * stride + feature];
         validmask |= 1u << j;
-        if (!d_go_right(ft, threshold, default_left, bin)) leftmask |= 1u << j;
+        const bool gr = cat ? d_cat_go_right(cat, bin) : d_go_right(ft, threshold, default_left, bin);
+        if (!gr) leftmask |= 1u << j;
       }
     }
     const int32_t my_left = __popc(leftmask);
@@ -1650,7 +1911,8 @@ __global__ void __launch_bounds__(kPartThreads) k_partition(GrowDev d) {
     __syncthreads();
     if (tile >= ntiles) break;
     const bool ok = PartitionTile::run(d.bins, d.stride, ft, f, thr, dl, sp, src == 2, dp, begin,
-                                       count, tile, epoch, d.part_status, &c->part_left_total);
+                                       count, tile, epoch, d.part_status, &c->part_left_total,
+                                       (ft.flags & kFeatCategorical) ? d.split_cat : nullptr);
     if (!ok) {
       if (threadIdx.x == 0) {
         atomicOr(&c->error, kErrSpinTimeout);
@@ -1734,6 +1996,7 @@ struct PartSmem {
   int32_t nb[128];
   int32_t boff[128];
   uint32_t mask[4];
+  uint32_t cat[kCatWords];  // left bins of a categorical split
 };
 
 // One fused partition by the whole grid (every thread of every CTA calls it); `sm` holds
@@ -1768,6 +2031,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
   const uint32_t thr = c->split.threshold;
   const bool dl = c->split.default_left != 0;
   const bool build_left = c->build_left != 0;
+  const bool is_cat = (ft.flags & kFeatCategorical) != 0;
   const int nf = d.F;
   const int cap = nf << SHIFT;
   // few tiles: every CTA takes exactly one tile and stores its own partial histogram
@@ -1777,6 +2041,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
     c->rows_parted += count;
     if (build) c->num_builds += 1;
   }
+  if (is_cat && tid < kCatWords) ps_.cat[tid] = d.split_cat[tid];
   __syncthreads();
   int32_t tile = s_tile;
   if (tile >= ntiles) return;
@@ -1852,7 +2117,8 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
         if (ch == fch) v = w[j][ch];
       const uint32_t word = fw == 0 ? v.x : fw == 1 ? v.y : fw == 2 ? v.z : v.w;
       const int32_t bin = (int32_t)((word >> fsh) & 0xffu);
-      if (!d_go_right(ft, thr, dl, bin)) leftmask |= 1u << j;
+      const bool gr = is_cat ? d_cat_go_right(ps_.cat, bin) : d_go_right(ft, thr, dl, bin);
+      if (!gr) leftmask |= 1u << j;
     }
     const int32_t my_left = __popc(leftmask);
     int32_t incl = my_left;
@@ -2147,7 +2413,10 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
   for (int s = 0; s < d.L - 1; ++s) {
     {
       PROF_BEGIN(KC_FIXSCAN);
-      k_fixscan<<<d.F, kScanThreads, 0, st>>>(d, s);
+      if (d.has_cat)
+        k_fixscan<true><<<d.F, kScanThreads, 0, st>>>(d, s);
+      else
+        k_fixscan<false><<<d.F, kScanThreads, 0, st>>>(d, s);
       PROF_END();
     }
     const int phase = s < d.L - 2 ? 1 : 2;

@@ -81,6 +81,11 @@ struct GrowDev {
   long long* partials;     // [private_tiles][raw_len]
   int64_t n_global;        // rows on all devices
   DevSplitInfo* scan_out;  // [2][F]
+  uint32_t* scan_cat;      // [2][F][kCatWords] left bins of categorical scan results
+  uint32_t* best_cat;      // [L][kCatWords] left bins of each leaf's best split
+  uint32_t* t_cat;         // [L][kCatWords] left bins of each categorical tree node
+  uint32_t* split_cat;     // [kCatWords] left bins of the pending split (categorical)
+  int32_t has_cat;         // some feature is categorical: the control step's CAT variant
   uint8_t* scan_ok;        // [2] leaf scanned flags
   // gradients
   int32_t gh_mode;
@@ -156,6 +161,7 @@ struct FinishDev {
   int32_t* rec_leaf_count;
   double* rec_internal_value;
   int32_t* rec_internal_count;
+  uint32_t* rec_cat;  // [max_iters][L][kCatWords]
 };
 void launch_finish_iteration(const GrowDev& d, const FinishDev& f, cudaStream_t st,
                              LaunchProfiler* prof = nullptr);

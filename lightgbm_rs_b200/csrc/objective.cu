@@ -305,6 +305,8 @@ __global__ void k_finish_tree(GrowDev d, FinishDev f) {
     f.rec_leaf_count[o] = d.t_leaf_count[i];
     f.rec_internal_value[o] = iv;
     f.rec_internal_count[o] = d.t_internal_count[i];
+#pragma unroll
+    for (int k = 0; k < kCatWords; ++k) f.rec_cat[o * kCatWords + k] = d.t_cat[i * kCatWords + k];
   }
   if (threadIdx.x == 0) {
     f.rec_num_leaves[it] = nl;
@@ -323,8 +325,9 @@ __global__ void __launch_bounds__(256) k_score_update(GrowDev d, double* score,
   if (it < 0 || rec_num_leaves[it] <= 1) return;
   __shared__ int32_t s_left[256], s_right[256], s_feat[256];
   __shared__ uint32_t s_thr[256];
-  __shared__ int8_t s_dl[256];
+  __shared__ int8_t s_dec[256];
   __shared__ double s_val[256];
+  __shared__ uint32_t s_cat[256][kCatWords];
   const int nl = d.ctrl->num_leaves;
   for (int i = threadIdx.x; i < nl; i += blockDim.x) {
     s_val[i] = d.t_leaf_value[i];
@@ -333,7 +336,9 @@ __global__ void __launch_bounds__(256) k_score_update(GrowDev d, double* score,
       s_right[i] = d.t_right[i];
       s_feat[i] = d.t_split_feature[i];
       s_thr[i] = d.t_threshold[i];
-      s_dl[i] = (d.t_decision[i] & 2) ? 1 : 0;
+      s_dec[i] = d.t_decision[i];
+      if (d.t_decision[i] & 1)
+        for (int k = 0; k < kCatWords; ++k) s_cat[i][k] = d.t_cat[i * kCatWords + k];
     }
   }
   __syncthreads();
@@ -343,7 +348,9 @@ __global__ void __launch_bounds__(256) k_score_update(GrowDev d, double* score,
     int node = 0;
     while (node >= 0) {
       const int f = s_feat[node];
-      const bool right = d_go_right(d.feat[f], s_thr[node], s_dl[node] != 0, rp[f]);
+      const int8_t dec = s_dec[node];
+      const bool right = (dec & 1) ? d_cat_go_right(s_cat[node], rp[f])
+                                   : d_go_right(d.feat[f], s_thr[node], (dec & 2) != 0, rp[f]);
       node = right ? s_right[node] : s_left[node];
     }
     score[r] += s_val[~node];
