@@ -148,6 +148,10 @@ def lib():
         L.oracle_binary_gradients.argtypes = [_P, _P, ctypes.c_int64, ctypes.c_double, _P, _P,
                                               ctypes.c_int32]
         L.oracle_l2_gradients.argtypes = [_P, _P, ctypes.c_int64, _P, _P, ctypes.c_int32]
+        L.oracle_lambdarank_gradients.argtypes = [
+            _P, _P, ctypes.c_int64, _P, ctypes.c_int32, ctypes.c_double, ctypes.c_int32,
+            ctypes.c_int32, _P, ctypes.c_int32, _P, _P, ctypes.c_int32]
+        L.oracle_lambdarank_gradients.restype = ctypes.c_int32
         L.oracle_binary_boost_from_score.argtypes = [_P, ctypes.c_int64, ctypes.c_double]
         L.oracle_binary_boost_from_score.restype = ctypes.c_double
         L.oracle_l2_boost_from_score.argtypes = [_P, ctypes.c_int64]
@@ -291,6 +295,24 @@ def l2_gradients(score, label, nthreads=1):
     return g, h
 
 
+def lambdarank_gradients(score, label, query_boundaries, sigmoid=1.0, norm=True,
+                         truncation_level=30, label_gain=None, nthreads=1):
+    """Lambdarank::get_gradients (lgbm-objective/src/rank.rs:264-366): f32 g, h."""
+    score = np.ascontiguousarray(score, dtype=np.float64)
+    label = np.ascontiguousarray(label, dtype=np.float32)
+    qb = np.ascontiguousarray(query_boundaries, dtype=np.int32)
+    lg = None if label_gain is None else np.ascontiguousarray(label_gain, dtype=np.float64)
+    g = np.empty(len(score), dtype=np.float32)
+    h = np.empty(len(score), dtype=np.float32)
+    rc = lib().oracle_lambdarank_gradients(
+        _ptr(score), _ptr(label), len(score), _ptr(qb), len(qb) - 1, float(sigmoid),
+        int(bool(norm)), int(truncation_level), _ptr(lg), 0 if lg is None else len(lg),
+        _ptr(g), _ptr(h), int(nthreads))
+    if rc != 0:
+        raise ValueError("invalid query boundaries or ranking labels")
+    return g, h
+
+
 def boost_from_score(objective, label, sigmoid=1.0):
     label = np.ascontiguousarray(label, dtype=np.float32)
     if objective == "binary":
@@ -329,15 +351,19 @@ def max_threads():
 
 def train(bins_cols, metas, labels, objective="binary", num_iterations=10, learning_rate=0.1,
           num_leaves=31, max_depth=-1, use_quantized_grad=False, num_grad_quant_bins=4,
-          boost_from_average=True, sigmoid=1.0, nthreads=1, record=False, **gain_kw):
+          boost_from_average=True, sigmoid=1.0, nthreads=1, record=False,
+          query_boundaries=None, lambdarank_norm=True, lambdarank_truncation_level=30,
+          label_gain=None, **gain_kw):
     """Gbdt::train_one_iter loop (lgbm-boosting/src/gbdt.rs:691-1300), non-bagging GBDT.
+    objective: "binary", "regression" (L2) or "lambdarank" (with query_boundaries; a
+    ranking objective has no boost-from-average score).
 
     Returns dict(trees, init_score, scores, iter_scores?, iter_grad_hess?)."""
     labels = np.ascontiguousarray(labels, dtype=np.float32)
     N = len(labels)
     score = np.zeros(N, dtype=np.float64)
     init = 0.0
-    if boost_from_average:
+    if boost_from_average and objective != "lambdarank":
         init = boost_from_score(objective, labels, sigmoid)
         if abs(init) > float(np.float32(1e-15)):
             score += init
@@ -347,6 +373,10 @@ def train(bins_cols, metas, labels, objective="binary", num_iterations=10, learn
     for it in range(num_iterations):
         if objective == "binary":
             g, h = binary_gradients(score, labels, sigmoid, nthreads)
+        elif objective == "lambdarank":
+            g, h = lambdarank_gradients(score, labels, query_boundaries, sigmoid,
+                                        lambdarank_norm, lambdarank_truncation_level,
+                                        label_gain, nthreads)
         else:
             g, h = l2_gradients(score, labels, nthreads)
         if record:

@@ -1074,6 +1074,125 @@ void oracle_l2_gradients(const double* score, const float* label, int64_t n, flo
   }
 }
 
+// Lambdarank::new + get_gradients (lgbm-objective/src/rank.rs:152-366; LightGBM
+// rank_objective.hpp:140-294), unweighted, no position bias. Per query: a stable sort
+// by descending score, then for every pair with its upper document above the
+// truncation level and different labels, the sigmoid-table lambda and hessian scaled
+// by the pair's NDCG change, accumulated into the f32 outputs in loop order; with
+// `norm`, a final rescale by log2(1 + sum_lambdas) / sum_lambdas. The DCG tables follow
+// DcgCalculator (lgbm-metric/src/dcg_calculator.rs:48-162): gains 2^i - 1 (31 entries)
+// unless given, discount 1 / log2(2 + rank) for 10000 ranks. Returns 0, or -1 when the
+// query boundaries or labels are invalid.
+int32_t oracle_lambdarank_gradients(const double* score, const float* label, int64_t n,
+                                    const int32_t* qb, int32_t nq, double sigmoid,
+                                    int32_t norm, int32_t trunc, const double* label_gain_in,
+                                    int32_t n_gain_in, float* g, float* h, int32_t nthreads) {
+  if (nq < 1 || qb[0] != 0 || qb[nq] != n || !(sigmoid > 0.0)) return -1;
+  for (int32_t q = 0; q < nq; ++q)
+    if (qb[q + 1] < qb[q]) return -1;
+  std::vector<double> gain;
+  if (n_gain_in > 0) {
+    gain.assign(label_gain_in, label_gain_in + n_gain_in);
+  } else {
+    gain.push_back(0.0);
+    for (int i = 1; i < 31; ++i) gain.push_back((double)((1ll << i) - 1));
+  }
+  for (int64_t i = 0; i < n; ++i) {
+    const float l = label[i];
+    if (std::fabs(l - (float)(int32_t)l) > 1e-15f || l < 0.0f || (int64_t)l >= (int64_t)gain.size())
+      return -1;
+  }
+  constexpr int kMaxPosition = 10000;
+  static std::vector<double> discount;
+  if (discount.empty())
+    for (int i = 0; i < kMaxPosition; ++i) discount.push_back(1.0 / std::log2(2.0 + (double)i));
+  // ConstructSigmoidTable: 2^20 bins over [-50 / sigmoid / 2, +50 / sigmoid / 2]
+  constexpr int64_t kBins = 1024 * 1024;
+  static std::vector<double> table;
+  static double table_sigmoid = 0.0;
+  const double min_in = -50.0 / sigmoid / 2.0, max_in = -min_in;
+  const double idx_factor = (double)kBins / (max_in - min_in);
+  if (table.empty() || table_sigmoid != sigmoid) {
+    table.resize(kBins);
+    for (int64_t i = 0; i < kBins; ++i) {
+      const double s = (double)i / idx_factor + min_in;
+      table[i] = 1.0 / (1.0 + std::exp(s * sigmoid));
+    }
+    table_sigmoid = sigmoid;
+  }
+  auto sig = [&](double s) {
+    if (s <= min_in) return table[0];
+    if (s >= max_in) return table[kBins - 1];
+    return table[(size_t)((s - min_in) * idx_factor)];
+  };
+  const double kMinScore = -std::numeric_limits<double>::infinity();
+#pragma omp parallel for schedule(dynamic, 16) num_threads(nthreads) if (nthreads > 1 && nq >= 64)
+  for (int32_t q = 0; q < nq; ++q) {
+    const int64_t b = qb[q];
+    const int64_t cnt = qb[q + 1] - b;
+    const double* s = score + b;
+    const float* lab = label + b;
+    float* lam = g + b;
+    float* hes = h + b;
+    for (int64_t i = 0; i < cnt; ++i) lam[i] = hes[i] = 0.0f;
+    if (cnt == 0) continue;
+    // DcgCalculator::cal_max_dcg_at_k(trunc) -> inverse
+    std::vector<int64_t> lc(gain.size(), 0);
+    for (int64_t i = 0; i < cnt; ++i) lc[(size_t)lab[i]] += 1;
+    double maxdcg = 0.0;
+    int64_t top = (int64_t)gain.size() - 1;
+    const int64_t kk = std::min<int64_t>(trunc, cnt);
+    for (int64_t j = 0; j < kk; ++j) {
+      while (top > 0 && lc[top] <= 0) --top;
+      if (top < 0) break;
+      maxdcg += discount[j] * gain[top];
+      lc[top] -= 1;
+    }
+    const double inv_max = maxdcg > 0.0 ? 1.0 / maxdcg : maxdcg;
+    std::vector<int64_t> order(cnt);
+    for (int64_t i = 0; i < cnt; ++i) order[i] = i;
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int64_t a, int64_t c) { return s[a] > s[c]; });
+    const double best = s[order[0]];
+    int64_t wi = cnt - 1;
+    if (wi > 0 && s[order[wi]] == kMinScore) --wi;
+    const double worst = s[order[wi]];
+    double sum_lambdas = 0.0;
+    for (int64_t i = 0; i + 1 < cnt && i < trunc; ++i) {
+      if (s[order[i]] == kMinScore) continue;
+      for (int64_t j = i + 1; j < cnt; ++j) {
+        if (s[order[j]] == kMinScore) continue;
+        if (lab[order[i]] == lab[order[j]]) continue;
+        const bool i_high = lab[order[i]] > lab[order[j]];
+        const int64_t hr = i_high ? i : j, lr = i_high ? j : i;
+        const int64_t hi = order[hr], lo = order[lr];
+        const double ds = s[hi] - s[lo];
+        const double gap = gain[(size_t)lab[hi]] - gain[(size_t)lab[lo]];
+        const double pd = std::fabs(discount[hr] - discount[lr]);
+        double dndcg = gap * pd * inv_max;
+        if (norm && best != worst) dndcg /= (double)0.01f + std::fabs(ds);
+        double pl = sig(ds);
+        double ph = pl * (1.0 - pl);
+        pl *= -sigmoid * dndcg;
+        ph *= sigmoid * sigmoid * dndcg;
+        lam[lo] -= (float)pl;
+        hes[lo] += (float)ph;
+        lam[hi] += (float)pl;
+        hes[hi] += (float)ph;
+        sum_lambdas -= 2.0 * pl;
+      }
+    }
+    if (norm && sum_lambdas > 0.0) {
+      const double nf = std::log2(1.0 + sum_lambdas) / sum_lambdas;
+      for (int64_t i = 0; i < cnt; ++i) {
+        lam[i] = (float)((double)lam[i] * nf);
+        hes[i] = (float)((double)hes[i] * nf);
+      }
+    }
+  }
+  return 0;
+}
+
 // Binary::boost_from_score (binary.rs:178-194)
 double oracle_binary_boost_from_score(const float* label, int64_t n, double sigmoid) {
   if (n == 0) return 0.0;

@@ -296,3 +296,29 @@ def categorical_binning_cases():
         rec["assign"] = u32_list(r[1] if len(r) > 1 else "")
         cases.append(rec)
     return cases
+
+
+def rank_case():
+    """The lambdarank cells (oracle-harness rank/ fixtures, captured from lib_lightgbm
+    4.6 by the reference's rank_oracle_capture.py): the 30-row, 6-query corpus. Its
+    features and labels come from numpy's legacy RandomState(20240607) exactly as the
+    capture drew them (randint(0, 8, (30, 3)), then randint(0, 4, 30)); the captured
+    labels are checked against the regenerated ones. Returns X, labels (f32),
+    query_boundaries, iteration-1 (g, h) and the final raw scores."""
+    sc = {}
+    for line in read_text("lambdarank_scores.txt").splitlines():
+        if "=" in line and not line.startswith("#"):
+            k, v = line.strip().split("=", 1)
+            sc[k] = v.split(",")
+    labels = np.array([int(x) for x in sc["labels"]], dtype=np.uint32).view(np.float32)
+    qb = np.array([int(x) for x in sc["query_boundaries"]], dtype=np.int32)
+    final = np.array([int(x) for x in sc["scores"]], dtype=np.uint64).view(np.float64)
+    gh = {}
+    for line in data_lines("lambdarank_gh_iter1.txt"):
+        t = line.split()
+        gh[t[0]] = np.array([int(x) for x in t[1:]], dtype=np.uint32).view(np.float32)
+    rng = np.random.RandomState(20240607)
+    X = rng.randint(0, 8, size=(30, 3)).astype(np.float64)
+    regen = rng.randint(0, 4, size=30).astype(np.float32)
+    assert np.array_equal(regen, labels), "rank corpus regeneration drifted"
+    return X, labels, qb, gh["GRAD"], gh["HESS"], final

@@ -41,6 +41,9 @@ FILES = [
     ("crates/oracle-harness/tests/fixtures/categorical/cat_manyvsmany.txt", False),
     ("crates/oracle-harness/tests/fixtures/categorical/cat_manyvsmany.bins.json", False),
     ("crates/oracle-harness/fixtures/rng_sequence.txt", True),
+    ("crates/oracle-harness/tests/fixtures/rank/lambdarank_gh_iter1.txt", False),
+    ("crates/oracle-harness/tests/fixtures/rank/lambdarank_scores.txt", False),
+    ("crates/oracle-harness/tests/fixtures/rank/rank_lambdarank_byq0_es0_model.txt", False),
 ]
 
 

@@ -187,3 +187,47 @@ def test_categorical_learner_real_lightgbm_tree(oracle_lib, name):
     shrink = float(side.get("shrinkage", 0.1))
     lv = [0.0 if abs(v * shrink) <= 1e-35 else v * shrink for v in tree["leaf_value"]]
     assert [G.g17(v) for v in lv] == [G.g17(v) for v in gold["leaf_value"]]
+
+
+RANK_PARAMS = dict(max_bin=255, min_data_in_bin=1, min_data_in_leaf=1, pre_filter=False,
+                   bin_construct_sample_cnt=1_000_000)
+
+
+def test_lambdarank_gradients_real_lightgbm(oracle_lib):
+    """rank/lambdarank_gh_iter1.txt: lib_lightgbm 4.6's iteration-1 lambdas and hessians
+    (zero scores, sigmoid 1, lambdarank_norm, truncation level 5), bit-exact."""
+    import oracle
+
+    _, labels, qb, G1, H1, _ = G.rank_case()
+    g, h = oracle.lambdarank_gradients(np.zeros(len(labels)), labels, qb, 1.0, True, 5)
+    assert g.view(np.uint32).tolist() == G1.view(np.uint32).tolist()
+    assert h.view(np.uint32).tolist() == H1.view(np.uint32).tolist()
+
+
+def test_lambdarank_training_real_lightgbm(oracle_lib):
+    """rank_lambdarank_byq0_es0_model.txt + lambdarank_scores.txt: 10 lambdarank
+    iterations (7 leaves, f32 gradients) replayed by the oracle: every tree's structure
+    and %.17g leaf values, and the final raw scores bit-exact."""
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, labels, qb, _, _, final = G.rank_case()
+    mappers, cols = [], []
+    for j in range(X.shape[1]):
+        m, b = lgb.bin_column(X[:, j], **RANK_PARAMS)
+        mappers.append(m)
+        cols.append(b.astype(np.uint8))
+    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
+             for m in mappers]
+    out = oracle.train(np.stack(cols), metas, labels, objective="lambdarank",
+                       num_iterations=10, learning_rate=0.1, num_leaves=7,
+                       query_boundaries=qb, lambdarank_truncation_level=5,
+                       min_data_in_leaf=1, min_sum_hessian_in_leaf=1e-3)
+    model = G.parse_model_text(G.read_text("rank_lambdarank_byq0_es0_model.txt"))
+    assert len(out["trees"]) == len(model) == 10
+    for i, (t, m) in enumerate(zip(out["trees"], model)):
+        for k in ("split_feature", "left_child", "right_child", "leaf_count",
+                  "internal_count"):
+            assert t[k].tolist() == m[k].tolist(), (i, k)
+        assert [G.g17(x) for x in t["leaf_value"]] == [G.g17(x) for x in m["leaf_value"]], i
+    assert out["scores"].view(np.uint64).tolist() == final.view(np.uint64).tolist()
