@@ -40,9 +40,14 @@ extern "C" {
 #define LGBM_B200_MISSING_ZERO 1
 #define LGBM_B200_MISSING_NAN 2
 
-/* Objectives on the path (lgbm-objective/src/binary.rs, regression.rs). */
+/* Objectives on the path (lgbm-objective/src/binary.rs, regression.rs, rank.rs). */
 #define LGBM_B200_OBJECTIVE_BINARY 0
 #define LGBM_B200_OBJECTIVE_L2 1
+#define LGBM_B200_OBJECTIVE_LAMBDARANK 2
+
+/* Largest query a lambdarank objective accepts: the DCG discount table's length
+ * (K_MAX_POSITION, lgbm-metric/src/dcg_calculator.rs:32). */
+#define LGBM_B200_MAX_QUERY_ROWS 10000
 
 /* Gradient-pair encodings accepted by lgbm_b200_learner_grow_tree. */
 #define LGBM_B200_GH_F32 0       /* float g[N], float h[N] */
@@ -149,6 +154,17 @@ typedef struct lgbm_b200_train_config {
   int32_t boost_from_average;
   double sigmoid;
   double learning_rate;
+  /* Lambdarank only (Lambdarank::new, lgbm-objective/src/rank.rs:152-227): the query
+   * boundaries of this device's rows (num_queries + 1 ascending prefix sums from 0 to
+   * num_data; borrowed for the call), lambdarank_truncation_level, lambdarank_norm,
+   * and the label gains (num_label_gain = 0: the default 2^i - 1 for i < 31). A
+   * ranking objective has no boost-from-average score. */
+  const int32_t* query_boundaries;
+  int32_t num_queries;
+  int32_t lambdarank_truncation_level;
+  int32_t lambdarank_norm;
+  int32_t num_label_gain;
+  const double* label_gain;
 } lgbm_b200_train_config;
 
 /* BinMapper::find_bin_from_column parameters (crates/lgbm-dataset/src/bin_mapper.rs:642-675). */

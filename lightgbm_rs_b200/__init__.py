@@ -48,6 +48,9 @@ _DEFAULTS = {
     "cat_smooth": 10.0,
     "boost_from_average": True,
     "sigmoid": 1.0,
+    "lambdarank_truncation_level": 30,
+    "lambdarank_norm": True,
+    "label_gain": None,
     "device": 0,
 }
 
@@ -63,7 +66,8 @@ _ALIASES = {
 }
 
 _OBJECTIVES = {"binary": C.OBJECTIVE_BINARY, "regression": C.OBJECTIVE_L2,
-               "regression_l2": C.OBJECTIVE_L2, "l2": C.OBJECTIVE_L2, "mse": C.OBJECTIVE_L2}
+               "regression_l2": C.OBJECTIVE_L2, "l2": C.OBJECTIVE_L2, "mse": C.OBJECTIVE_L2,
+               "lambdarank": C.OBJECTIVE_LAMBDARANK}
 
 
 def _resolve(params):
@@ -119,10 +123,16 @@ class Dataset:
     the reference BinMapper), or pass `bins`/`mappers` to reuse an existing binning."""
 
     def __init__(self, data=None, label=None, params=None, bins=None, mappers=None,
-                 categorical_feature=None):
+                 categorical_feature=None, group=None):
         """categorical_feature: column indices binned as categories (non-negative integer
-        codes; negatives and NaN count as missing), as lightgbm's Dataset takes them."""
+        codes; negatives and NaN count as missing), as lightgbm's Dataset takes them.
+        group: query sizes in row order for ranking objectives (also accepted as
+        params["group"], a comma-separated string as the reference's sklearn layer
+        passes it)."""
         self.params = _resolve(params)
+        if group is None and self.params.get("group") is not None:
+            group = self.params["group"]
+        self.set_group(group)
         cats = set(int(c) for c in (categorical_feature or []))
         self.label = None if label is None else np.ascontiguousarray(label, dtype=np.float32)
         if bins is None:
@@ -145,6 +155,18 @@ class Dataset:
         self.mappers = mappers
         self.num_features, self.num_data = self.bins.shape
         self._handle = None
+
+    def set_group(self, group):
+        """Query sizes (or None); stored as query boundaries (prefix sums)."""
+        if group is None:
+            self.query_boundaries = None
+            return
+        if isinstance(group, str):
+            group = [int(t) for t in group.split(",") if t.strip()]
+        sizes = np.asarray(group, dtype=np.int64).reshape(-1)
+        if (sizes < 0).any():
+            raise LightGBMError(C.INVALID_ARGUMENT, "group sizes must be non-negative")
+        self.query_boundaries = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)
 
     def construct(self):
         if self._handle is None:
@@ -243,6 +265,26 @@ class Booster:
         cfg = C.TrainConfig(_learner_config(p), _OBJECTIVES[obj], int(bool(p["use_quantized_grad"])),
                             int(p["num_grad_quant_bins"]), int(bool(p["boost_from_average"])),
                             float(p["sigmoid"]), float(p["learning_rate"]))
+        self._rank_arrays = None
+        if obj == "lambdarank":
+            qb = train_set.query_boundaries
+            if qb is None:
+                raise LightGBMError(C.INVALID_ARGUMENT,
+                                    "lambdarank needs query sizes (Dataset group=)")
+            if qb[-1] != train_set.num_data:
+                raise LightGBMError(C.INVALID_ARGUMENT, f"group sizes sum to {qb[-1]}, "
+                                    f"the dataset has {train_set.num_data} rows")
+            lg = p.get("label_gain")
+            if isinstance(lg, str):
+                lg = [float(t) for t in lg.split(",") if t.strip()]
+            lg = None if lg is None or len(lg) == 0 else np.asarray(lg, dtype=np.float64)
+            self._rank_arrays = (qb, lg)  # borrowed by the create call
+            cfg.query_boundaries = C.ptr(qb)
+            cfg.num_queries = len(qb) - 1
+            cfg.lambdarank_truncation_level = int(p["lambdarank_truncation_level"])
+            cfg.lambdarank_norm = int(bool(p["lambdarank_norm"]))
+            cfg.num_label_gain = 0 if lg is None else len(lg)
+            cfg.label_gain = C.ptr(lg)
         h = ctypes.c_void_p()
         if comm is not None:
             C.check(C.lib().lgbm_b200_booster_create_distributed(

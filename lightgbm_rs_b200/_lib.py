@@ -20,7 +20,7 @@ NON_FINITE = 5
 INVALID_ARGUMENT = 6
 
 MISSING_NONE, MISSING_ZERO, MISSING_NAN = 0, 1, 2
-OBJECTIVE_BINARY, OBJECTIVE_L2 = 0, 1
+OBJECTIVE_BINARY, OBJECTIVE_L2, OBJECTIVE_LAMBDARANK = 0, 1, 2
 GH_F32, GH_INT8_PAIR = 0, 1
 
 _P = ctypes.c_void_p
@@ -81,7 +81,9 @@ class LearnerConfig(ctypes.Structure):
 class TrainConfig(ctypes.Structure):
     _fields_ = [("learner", LearnerConfig), ("objective", _i32), ("use_quantized_grad", _i32),
                 ("num_grad_quant_bins", _i32), ("boost_from_average", _i32), ("sigmoid", _f64),
-                ("learning_rate", _f64)]
+                ("learning_rate", _f64), ("query_boundaries", _P), ("num_queries", _i32),
+                ("lambdarank_truncation_level", _i32), ("lambdarank_norm", _i32),
+                ("num_label_gain", _i32), ("label_gain", _P)]
 
 
 class BinConfig(ctypes.Structure):

@@ -564,6 +564,10 @@ struct lgbm_b200_booster {
   DevBuf<int8_t> rec_dec;
   DevBuf<double> rec_f64;  // leaf_value, leaf_weight, internal_value
   DevBuf<uint32_t> rec_cat;  // [cap][L][kCatWords] categorical node bins
+  // lambdarank tables (objective 2)
+  DevBuf<int32_t> rank_qb;
+  DevBuf<double> rank_f64;  // sigmoid table | discounts | label gains | inverse max DCGs
+  DevBuf<int32_t> rank_order;
   double init_score = 0.0;
   ObjDev obj{};
   FinishDev fin{};
@@ -725,7 +729,7 @@ extern "C" {
 
 const char* lgbm_b200_last_error(void) { return g_last_error.c_str(); }
 
-int32_t lgbm_b200_abi_version(void) { return 101; }
+int32_t lgbm_b200_abi_version(void) { return 102; }
 
 int lgbm_b200_device_count(int32_t* out) {
   int n = 0;
@@ -1289,19 +1293,105 @@ int gather_labels(lgbm_b200_comm* comm, const float* labels, int64_t n_local, cu
   return LGBM_B200_OK;
 }
 
+// Lambdarank::new (lgbm-objective/src/rank.rs:152-227): validated query boundaries and
+// labels, then the tables the device objective reads. DcgCalculator
+// (lgbm-metric/src/dcg_calculator.rs:48-162): gains 2^i - 1 unless given, discount
+// 1 / log2(2 + rank), per-query 1 / max DCG at the truncation level; the 2^20-entry
+// sigmoid table of ConstructSigmoidTable. Built here with the host libm, like the
+// reference's.
+struct RankTables {
+  std::vector<double> sig, discount, gain, inv_max;
+  double sig_min = 0.0, sig_max = 0.0, sig_factor = 0.0;
+};
+
+int rank_tables(const lgbm_b200_train_config& cfg, const float* labels, int64_t n,
+                RankTables* rt) {
+  const int32_t* qb = cfg.query_boundaries;
+  const int32_t nq = cfg.num_queries;
+  if (!qb || nq < 1)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "lambdarank needs query boundaries");
+  if (qb[0] != 0 || (int64_t)qb[nq] != n)
+    return fail(LGBM_B200_INVALID_ARGUMENT,
+                "query boundaries must run from 0 to num_data %lld (got %d .. %d)",
+                (long long)n, qb[0], qb[nq]);
+  for (int32_t q = 0; q < nq; ++q) {
+    if (qb[q + 1] < qb[q])
+      return fail(LGBM_B200_INVALID_ARGUMENT, "query boundaries must be non-decreasing");
+    if (qb[q + 1] - qb[q] > LGBM_B200_MAX_QUERY_ROWS)
+      return fail(LGBM_B200_INVALID_ARGUMENT, "query %d has %d rows (more than %d)", q,
+                  qb[q + 1] - qb[q], LGBM_B200_MAX_QUERY_ROWS);
+  }
+  if (cfg.lambdarank_truncation_level < 0)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "lambdarank_truncation_level %d",
+                cfg.lambdarank_truncation_level);
+  if (cfg.num_label_gain > 0) {
+    if (!cfg.label_gain) return fail(LGBM_B200_INVALID_ARGUMENT, "label_gain: null pointer");
+    rt->gain.assign(cfg.label_gain, cfg.label_gain + cfg.num_label_gain);
+  } else {
+    rt->gain.push_back(0.0);
+    for (int i = 1; i < 31; ++i) rt->gain.push_back((double)((1ll << i) - 1));
+  }
+  // DcgCalculator::check_labels: integral, non-negative, inside the gain table
+  for (int64_t i = 0; i < n; ++i) {
+    const float l = labels[i];
+    if (!(std::fabs(l - (float)(int32_t)l) <= 1e-15f))
+      return fail(LGBM_B200_INVALID_ARGUMENT, "ranking label %g at row %lld is not an integer",
+                  (double)l, (long long)i);
+    if (l < 0.0f || (size_t)l >= rt->gain.size())
+      return fail(LGBM_B200_INVALID_ARGUMENT,
+                  "ranking label %g at row %lld outside the %zu label gains", (double)l,
+                  (long long)i, rt->gain.size());
+  }
+  rt->discount.resize(LGBM_B200_MAX_QUERY_ROWS);
+  for (int i = 0; i < LGBM_B200_MAX_QUERY_ROWS; ++i)
+    rt->discount[i] = 1.0 / std::log2(2.0 + (double)i);
+  rt->inv_max.resize(nq);
+  std::vector<int64_t> cnt(rt->gain.size());
+  for (int32_t q = 0; q < nq; ++q) {
+    std::fill(cnt.begin(), cnt.end(), 0);
+    for (int32_t i = qb[q]; i < qb[q + 1]; ++i) cnt[(size_t)labels[i]] += 1;
+    double m = 0.0;
+    int64_t top = (int64_t)rt->gain.size() - 1;
+    const int64_t k = std::min<int64_t>(cfg.lambdarank_truncation_level, qb[q + 1] - qb[q]);
+    for (int64_t j = 0; j < k; ++j) {
+      while (top > 0 && cnt[top] <= 0) --top;
+      if (top < 0) break;
+      m += rt->discount[j] * rt->gain[top];
+      cnt[top] -= 1;
+    }
+    rt->inv_max[q] = m > 0.0 ? 1.0 / m : m;
+  }
+  rt->sig_min = -50.0 / cfg.sigmoid / 2.0;
+  rt->sig_max = -rt->sig_min;
+  rt->sig_factor = (double)kRankSigmoidBins / (rt->sig_max - rt->sig_min);
+  rt->sig.resize(kRankSigmoidBins);
+  for (int64_t i = 0; i < kRankSigmoidBins; ++i) {
+    const double x = (double)i / rt->sig_factor + rt->sig_min;
+    rt->sig[i] = 1.0 / (1.0 + std::exp(x * cfg.sigmoid));
+  }
+  return LGBM_B200_OK;
+}
+
 int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
                         const lgbm_b200_train_config* cfg, lgbm_b200_comm* comm,
                         lgbm_b200_booster** out) {
   if (!ds || !labels || !cfg || !out)
     return fail(LGBM_B200_INVALID_ARGUMENT, "booster_create: null argument");
   *out = nullptr;
-  if (cfg->objective != LGBM_B200_OBJECTIVE_BINARY && cfg->objective != LGBM_B200_OBJECTIVE_L2)
+  if (cfg->objective != LGBM_B200_OBJECTIVE_BINARY && cfg->objective != LGBM_B200_OBJECTIVE_L2 &&
+      cfg->objective != LGBM_B200_OBJECTIVE_LAMBDARANK)
     return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "objective %d not on the device path",
                 cfg->objective);
+  const bool rank = cfg->objective == LGBM_B200_OBJECTIVE_LAMBDARANK;
+  if ((cfg->objective == LGBM_B200_OBJECTIVE_BINARY || rank) && !(cfg->sigmoid > 0.0))
+    return fail(LGBM_B200_INVALID_ARGUMENT, "sigmoid %g must be > 0", cfg->sigmoid);
+  RankTables rt;
+  if (rank) {
+    const int rc0 = rank_tables(*cfg, labels, ds->num_data, &rt);
+    if (rc0) return rc0;
+  }
   if (cfg->use_quantized_grad && (cfg->num_grad_quant_bins < 1 || cfg->num_grad_quant_bins > 127))
     return fail(LGBM_B200_INVALID_ARGUMENT, "num_grad_quant_bins %d", cfg->num_grad_quant_bins);
-  if (cfg->objective == LGBM_B200_OBJECTIVE_BINARY && !(cfg->sigmoid > 0.0))
-    return fail(LGBM_B200_INVALID_ARGUMENT, "binary sigmoid %g must be > 0", cfg->sigmoid);
   DeviceGuard g(ds->device);
   auto b = std::make_unique<lgbm_b200_booster>();
   b->ds = ds;
@@ -1338,7 +1428,7 @@ int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
   }
   // boost_from_average (gbdt.rs:619-639): init score on the host from the labels.
   double init = 0.0;
-  if (cfg->boost_from_average) {
+  if (cfg->boost_from_average && !rank) {
     const double eps = (double)1e-15f;
     if (cfg->objective == LGBM_B200_OBJECTIVE_BINARY) {
       double suml = 0.0;
@@ -1376,6 +1466,36 @@ int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
   o.ghp = b->ghp.p;
   o.num_quant_bins = cfg->num_grad_quant_bins;
   o.stopped = b->state.p;
+  if (rank) {
+    const size_t nq = rt.inv_max.size();
+    CUDA_TRY(b->rank_qb.alloc(nq + 1));
+    CUDA_TRY(cudaMemcpy(b->rank_qb.p, cfg->query_boundaries, (nq + 1) * 4,
+                        cudaMemcpyHostToDevice));
+    const size_t nf = rt.sig.size() + rt.discount.size() + rt.gain.size() + nq;
+    CUDA_TRY(b->rank_f64.alloc(nf));
+    double* p = b->rank_f64.p;
+    const std::vector<double>* parts[4] = {&rt.sig, &rt.discount, &rt.gain, &rt.inv_max};
+    const double* dst[4];
+    for (int k = 0; k < 4; ++k) {
+      dst[k] = p;
+      if (!parts[k]->empty())
+        CUDA_TRY(cudaMemcpy(p, parts[k]->data(), parts[k]->size() * 8, cudaMemcpyHostToDevice));
+      p += parts[k]->size();
+    }
+    CUDA_TRY(b->rank_order.alloc((size_t)std::max<int64_t>(N, 1)));
+    o.qb = b->rank_qb.p;
+    o.num_queries = (int32_t)nq;
+    o.trunc = cfg->lambdarank_truncation_level;
+    o.norm = cfg->lambdarank_norm ? 1 : 0;
+    o.sig_table = dst[0];
+    o.sig_min = rt.sig_min;
+    o.sig_max = rt.sig_max;
+    o.sig_factor = rt.sig_factor;
+    o.discount = dst[1];
+    o.label_gain = dst[2];
+    o.inv_max_dcg = dst[3];
+    o.order = b->rank_order.p;
+  }
   FinishDev& f = b->fin;
   f.stopped = b->state.p;
   f.iter_counter = b->state.p + 1;

@@ -136,7 +136,20 @@ struct ObjDev {
   DevGhParams* ghp;
   int32_t num_quant_bins;
   const int32_t* stopped;
+  // lambdarank (objective 2): per-query tables built once on the host
+  const int32_t* qb;          // [num_queries + 1] query boundaries
+  int32_t num_queries;
+  int32_t trunc;              // lambdarank_truncation_level
+  int32_t norm;               // lambdarank_norm
+  int32_t _pad;
+  const double* sig_table;    // [kRankSigmoidBins] 1 / (1 + exp(sigmoid * x))
+  double sig_min, sig_max, sig_factor;
+  const double* discount;     // [LGBM_B200_MAX_QUERY_ROWS] 1 / log2(2 + rank)
+  const double* label_gain;   // gain of each integer label
+  const double* inv_max_dcg;  // [num_queries] 1 / max DCG at the truncation level
+  int32_t* order;             // [N] each query's rows by descending score
 };
+constexpr int64_t kRankSigmoidBins = 1 << 20;  // LambdarankNDCG::_sigmoid_bins
 void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof = nullptr,
                       const DeviceComm* comm = nullptr);
 

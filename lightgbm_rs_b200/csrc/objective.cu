@@ -1,4 +1,5 @@
 // Gradient/hessian, quantization, root sums, shrinkage and score update kernels.
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 
@@ -68,6 +69,192 @@ __global__ void __launch_bounds__(kObjThreads) k_grad_pass1(ObjDev o) {
     kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, off));
   }
   if ((threadIdx.x & 31) == 0) {
+    atomicMax(&o.ghp->max_abs_g_bits, mg);
+    atomicMax(&o.ghp->max_abs_h_bits, mh);
+    atomicMin(&o.ghp->min_h_key, kmin);
+    atomicMax(&o.ghp->max_h_key, kmax);
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// LambdarankNDCG gradients (Lambdarank::get_gradients, lgbm-objective/src/rank.rs:264-366;
+// LightGBM rank_objective.hpp:180-266), one warp per query. The reference walks the
+// document pairs (i, j) of each query in the order of its score-sorted positions,
+// outer i below the truncation level, and adds every pair's f32 lambda and hessian into
+// both documents, so each document receives its terms in a fixed order: first the
+// pairs in which it is the inner j (outer i ascending), then those in which it is the
+// outer i (inner j ascending). One lane per document replays exactly that order, so
+// the f32 sums are the reference's. The f64 sum of all lambdas, which the norm needs,
+// depends on the whole pair order: the warp computes 32 pairs at a time and every lane
+// folds them sequentially.
+// ------------------------------------------------------------------------------------
+
+// LambdarankNDCG::GetSigmoid (rank.rs:230-241): the table lookup.
+__device__ __forceinline__ double rank_sigmoid(const ObjDev& o, double x) {
+  if (x <= o.sig_min) return o.sig_table[0];
+  if (x >= o.sig_max) return o.sig_table[kRankSigmoidBins - 1];
+  // (x - min) * factor can round up to the table length just below max: clamp
+  const size_t i = (size_t)((x - o.sig_min) * o.sig_factor);
+  return o.sig_table[i < (size_t)kRankSigmoidBins ? i : (size_t)kRankSigmoidBins - 1];
+}
+
+// One pair's lambda and hessian (rank.rs:326-351). hr / lr are the sorted positions of
+// the higher- and lower-labelled documents.
+__device__ __forceinline__ void rank_pair(const ObjDev& o, double hs, double ls, float hl,
+                                          float ll, int hr, int lr, double inv_max,
+                                          bool scale, double* pl, double* ph) {
+  const double ds = hs - ls;
+  const double gap = o.label_gain[(int)hl] - o.label_gain[(int)ll];
+  const double pd = fabs(o.discount[hr] - o.discount[lr]);
+  double dn = gap * pd * inv_max;
+  if (scale) dn /= (double)0.01f + fabs(ds);
+  double p = rank_sigmoid(o, ds);
+  double h = p * (1.0 - p);
+  p *= -o.sigmoid * dn;
+  h *= o.sigmoid * o.sigmoid * dn;
+  *pl = p;
+  *ph = h;
+}
+
+// Total order of scores for the stable descending sort: -0.0 and +0.0 share a key, so
+// equal scores keep row order as in the reference's sort.
+__device__ __forceinline__ unsigned long long score_key(double x) {
+  x = x + 0.0;
+  const unsigned long long b = (unsigned long long)__double_as_longlong(x);
+  return (b >> 63) ? ~b : (b | 0x8000000000000000ull);
+}
+
+__global__ void __launch_bounds__(kObjThreads) k_lambdarank(ObjDev o) {
+  if (o.stopped && *o.stopped) return;
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const double kMinScore = -INFINITY;
+  float2* gh = reinterpret_cast<float2*>(o.gh);
+  uint32_t mg = 0, mh = 0, kmin = 0xffffffffu, kmax = 0u;
+  for (int64_t q = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; q < o.num_queries;
+       q += nwarps) {
+    const int32_t b = o.qb[q];
+    const int32_t cnt = o.qb[q + 1] - b;
+    const double* s = o.score + b;
+    const float* lab = o.label + b;
+    int32_t* ord = o.order + b;
+    // stable sort by descending score: position = rows ahead of this one
+    for (int i = lane; i < cnt; i += 32) {
+      const unsigned long long ki = score_key(s[i]);
+      int r = 0;
+      for (int e = 0; e < cnt; ++e) {
+        const unsigned long long ke = score_key(s[e]);
+        r += (ke > ki || (ke == ki && e < i)) ? 1 : 0;
+      }
+      ord[r] = i;
+    }
+    __syncwarp();
+    if (cnt == 0) continue;
+    const double best = s[ord[0]];
+    int wi = cnt - 1;
+    if (wi > 0 && s[ord[wi]] == kMinScore) --wi;
+    const double worst = s[ord[wi]];
+    const bool scale = o.norm && best != worst;
+    const double inv_max = o.inv_max_dcg[q];
+    const int I = min(o.trunc, cnt - 1);  // outer positions: i + 1 < cnt && i < trunc
+    // the f64 sum of the lambdas, in the reference's pair order
+    double sum = 0.0;
+    if (o.norm) {
+      for (int i = 0; i < I; ++i) {
+        const int ei = ord[i];
+        const double si = s[ei];
+        if (si == kMinScore) continue;
+        const float li = lab[ei];
+        for (int j0 = i + 1; j0 < cnt; j0 += 32) {
+          const int j = j0 + lane;
+          double t = 0.0;
+          bool valid = false;
+          if (j < cnt) {
+            const int ej = ord[j];
+            const double sj = s[ej];
+            const float lj = lab[ej];
+            if (sj != kMinScore && lj != li) {
+              double pl, ph;
+              if (li > lj)
+                rank_pair(o, si, sj, li, lj, i, j, inv_max, scale, &pl, &ph);
+              else
+                rank_pair(o, sj, si, lj, li, j, i, inv_max, scale, &pl, &ph);
+              t = 2.0 * pl;
+              valid = true;
+            }
+          }
+          const unsigned vm = __ballot_sync(full, valid);
+          for (int k = 0; k < 32; ++k) {
+            const double tk = __shfl_sync(full, t, k);
+            if ((vm >> k) & 1u) sum -= tk;
+          }
+        }
+      }
+    }
+    const bool rescale = o.norm && sum > 0.0;
+    const double nf = rescale ? log2(1.0 + sum) / sum : 1.0;
+    // per-document f32 sums in the reference's order
+    for (int r = lane; r < cnt; r += 32) {
+      const int d = ord[r];
+      const double sd = s[d];
+      const float ld = lab[d];
+      float lam = 0.0f, hes = 0.0f;
+      if (sd != kMinScore) {
+        const int n_in = min(r, I);
+        for (int i = 0; i < n_in; ++i) {  // pairs (i, r): this document is the inner one
+          const int e = ord[i];
+          const double se = s[e];
+          const float le = lab[e];
+          if (se == kMinScore || le == ld) continue;
+          double pl, ph;
+          if (le > ld) {
+            rank_pair(o, se, sd, le, ld, i, r, inv_max, scale, &pl, &ph);
+            lam -= (float)pl;
+          } else {
+            rank_pair(o, sd, se, ld, le, r, i, inv_max, scale, &pl, &ph);
+            lam += (float)pl;
+          }
+          hes += (float)ph;
+        }
+        if (r < I) {
+          for (int j = r + 1; j < cnt; ++j) {  // pairs (r, j): this document is the outer one
+            const int e = ord[j];
+            const double se = s[e];
+            const float le = lab[e];
+            if (se == kMinScore || le == ld) continue;
+            double pl, ph;
+            if (ld > le) {
+              rank_pair(o, sd, se, ld, le, r, j, inv_max, scale, &pl, &ph);
+              lam += (float)pl;
+            } else {
+              rank_pair(o, se, sd, le, ld, j, r, inv_max, scale, &pl, &ph);
+              lam -= (float)pl;
+            }
+            hes += (float)ph;
+          }
+        }
+      }
+      if (rescale) {
+        lam = (float)((double)lam * nf);
+        hes = (float)((double)hes * nf);
+      }
+      gh[b + d] = make_float2(lam, hes);
+      mg = max(mg, __float_as_uint(fabsf(lam)));
+      mh = max(mh, __float_as_uint(fabsf(hes)));
+      const uint32_t k = f32_key(hes);
+      kmin = min(kmin, k);
+      kmax = max(kmax, k);
+    }
+    __syncwarp();
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    mg = max(mg, __shfl_xor_sync(full, mg, off));
+    mh = max(mh, __shfl_xor_sync(full, mh, off));
+    kmin = min(kmin, __shfl_xor_sync(full, kmin, off));
+    kmax = max(kmax, __shfl_xor_sync(full, kmax, off));
+  }
+  if (lane == 0) {
     atomicMax(&o.ghp->max_abs_g_bits, mg);
     atomicMax(&o.ghp->max_abs_h_bits, mh);
     atomicMin(&o.ghp->min_h_key, kmin);
@@ -377,7 +564,13 @@ void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof,
   const int grid = num_sms_obj() * 8;
   const int slot = prof ? prof->begin(st, KC_GRAD) : -1;
   k_gh_reset<<<1, 1, 0, st>>>(o.ghp, o.stopped);
-  k_grad_pass1<<<grid, kObjThreads, 0, st>>>(o);
+  if (o.objective == LGBM_B200_OBJECTIVE_LAMBDARANK) {
+    const int64_t warps_needed = o.num_queries > 0 ? o.num_queries : 1;
+    const int64_t blocks = (warps_needed + kObjThreads / 32 - 1) / (kObjThreads / 32);
+    k_lambdarank<<<(int)std::min<int64_t>(blocks, (int64_t)grid * 4), kObjThreads, 0, st>>>(o);
+  } else {
+    k_grad_pass1<<<grid, kObjThreads, 0, st>>>(o);
+  }
   if (comm) {
     comm->max_u32(comm->ctx, &o.ghp->max_abs_g_bits, 2, st);
     comm->min_u32(comm->ctx, &o.ghp->min_h_key, 1, st);

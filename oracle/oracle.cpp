@@ -1123,7 +1123,8 @@ int32_t oracle_lambdarank_gradients(const double* score, const float* label, int
   auto sig = [&](double s) {
     if (s <= min_in) return table[0];
     if (s >= max_in) return table[kBins - 1];
-    return table[(size_t)((s - min_in) * idx_factor)];
+    const size_t i = (size_t)((s - min_in) * idx_factor);
+    return table[std::min<size_t>(i, (size_t)kBins - 1)];
   };
   const double kMinScore = -std::numeric_limits<double>::infinity();
 #pragma omp parallel for schedule(dynamic, 16) num_threads(nthreads) if (nthreads > 1 && nq >= 64)
