@@ -1,13 +1,19 @@
 """Benchmark: boosting iterations/s of the B200 histogram tree learner.
 
-Workload: 10,500,000 rows x 28 dense features from the
-configs[0] generator (seeded synthetic: no public dataset is named), max_bin=255,
+Default workload C1: 10,500,000 rows x 28 dense features from
+the configs[0] generator (seeded synthetic: no public dataset is named), max_bin=255,
 num_leaves=255, min_data_in_leaf=100, objective=binary, learning_rate=0.1.
 Default gradients: use_quantized_grad with 4 quantization bins (`--grad f32` for the
 f32-gradient variant). One step = one boosting iteration (gradients, quantization,
-one 255-leaf tree, shrinkage, score update) over all rows.
+one tree, shrinkage, score update) over all rows.
+
+`--workload c3`: 2,000,000 rows, 90 numeric features with 10 % NaN and 10 categorical
+features, L2 regression, 63 leaves. `--workload c4`: lambdarank over 20,000 queries
+(about 473k rows) x 700 sparse features, 255 leaves. Both are seeded synthetic
+stand-ins with the configurations' shapes (lightgbm_rs_b200/synthetic.py).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload c1|c3|c4] [--grad quantized|f32]
 
 Prints ONE JSON line on rank 0. `--impl reference` times the reference CPU learner
 (the C++ restatement in oracle/, the reference's Rust crates cannot be built here)
@@ -28,11 +34,19 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-N_ROWS = 10_500_000
-N_FEAT = 28
-NUM_LEAVES = 255
-MIN_DATA_IN_LEAF = 100
 LEARNING_RATE = 0.1
+
+# name -> rows, features, leaves, min_data_in_leaf, objective, description
+WORKLOADS = {
+    "c1": dict(rows=10_500_000, features=28, leaves=255, min_data=100, objective="binary",
+               desc="C1 binary {rows}x28 num_leaves=255 min_data_in_leaf=100 max_bin=255"),
+    "c3": dict(rows=2_000_000, features=100, leaves=63, min_data=20, objective="regression",
+               desc="C3 l2 {rows}x100 (90 numeric, 10% NaN; 10 categorical, 16-240 "
+                    "categories, Zipf 1.2) num_leaves=63 max_bin=255"),
+    "c4": dict(rows=473_000, features=700, leaves=255, min_data=20, objective="lambdarank",
+               desc="C4 lambdarank {rows} rows / {queries} queries x700 (80% zeros) "
+                    "num_leaves=255 max_bin=255"),
+}
 
 
 def parse():
@@ -42,9 +56,14 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--grad", default="quantized", choices=["quantized", "f32"])
-    ap.add_argument("--rows", type=int, default=N_ROWS)
+    ap.add_argument("--workload", default="c1", choices=sorted(WORKLOADS))
+    ap.add_argument("--rows", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    if args.rows is None:
+        args.rows = w["rows"]
+    return args
 
 
 def load_peaks():
@@ -56,11 +75,22 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def make_data(rows, seed=0):
-    """Seeded synthetic C1 data, binned with the reference BinMapper (host).
+class Data:
+    """A binned workload: feature-major bins, mappers, labels, query sizes (ranking)."""
+
+    def __init__(self, bins, mappers, y, group=None):
+        self.bins, self.mappers, self.y, self.group = bins, mappers, y, group
+        self.rows = bins.shape[1]
+        self.features = bins.shape[0]
+        self.qb = None if group is None else \
+            np.concatenate([[0], np.cumsum(group)]).astype(np.int32)
+
+
+def make_data(workload, rows, seed=0):
+    """Seeded synthetic data of the workload, binned with the reference BinMapper (host).
 
     The binned result is cached under the system temp directory so repeated runs on
-    one machine skip generation (the cache is keyed by rows and seed)."""
+    one machine skip generation (the cache is keyed by workload, rows and seed)."""
     import concurrent.futures as cf
     import pickle
     import tempfile
@@ -68,34 +98,47 @@ def make_data(rows, seed=0):
     import lightgbm_rs_b200 as lgb
     from lightgbm_rs_b200 import synthetic
 
-    cache = os.path.join(tempfile.gettempdir(), f"lgbm_b200_c1_{rows}_{seed}.pkl")
+    cache = os.path.join(tempfile.gettempdir(), f"lgbm_b200_{workload}_{rows}_{seed}.pkl")
     if os.path.exists(cache):
         with open(cache, "rb") as f:
             return pickle.load(f)
-    X, y = synthetic.binary_c0(num_data=rows, num_features=N_FEAT, seed=seed)
-    mappers = [None] * N_FEAT
-    bins = np.empty((N_FEAT, rows), dtype=np.uint8)
+    w = WORKLOADS[workload]
+    group, cats = None, []
+    if workload == "c1":
+        X, y = synthetic.binary_c0(num_data=rows, num_features=w["features"], seed=seed)
+    elif workload == "c3":
+        X, y, cats = synthetic.mixed_c3(num_data=rows, seed=seed)
+    else:
+        X, y, group = synthetic.rank_c4(num_queries=max(1, round(rows / 23.65)),
+                                        num_features=w["features"], seed=seed)
+    F = X.shape[1]
+    mappers = [None] * F
+    bins = np.empty((F, X.shape[0]), dtype=np.uint8)
 
     def one(j):
-        m, b = lgb.bin_column(X[:, j], max_bin=255, min_data_in_leaf=MIN_DATA_IN_LEAF)
+        m, b = lgb.bin_column(X[:, j], max_bin=255, min_data_in_leaf=w["min_data"],
+                              categorical=j in cats)
+        assert m["num_bin"] <= 256, f"feature {j}: {m['num_bin']} bins do not fit u8"
         mappers[j] = m
         bins[j] = b.astype(np.uint8)
 
     with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4)) as ex:
-        list(ex.map(one, range(N_FEAT)))
+        list(ex.map(one, range(F)))
     del X
+    data = Data(bins, mappers, y, group)
     try:
         with open(cache + ".tmp", "wb") as f:
-            pickle.dump((bins, mappers, y), f, protocol=4)
+            pickle.dump(data, f, protocol=4)
         os.replace(cache + ".tmp", cache)
     except OSError:
         pass
-    return bins, mappers, y
+    return data
 
 
-def params(grad):
-    p = {"objective": "binary", "num_leaves": NUM_LEAVES, "min_data_in_leaf": MIN_DATA_IN_LEAF,
-         "learning_rate": LEARNING_RATE, "max_bin": 255}
+def params(workload, grad):
+    w = WORKLOADS[workload]
+    p = {"objective": w["objective"], "num_leaves": w["leaves"],
+         "min_data_in_leaf": w["min_data"], "learning_rate": LEARNING_RATE, "max_bin": 255}
     if grad == "quantized":
         p.update(use_quantized_grad=True, num_grad_quant_bins=4)
     return p
@@ -158,7 +201,7 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def kernel_bytes(counts, rows, grad):
+def kernel_bytes(counts, rows, grad, features):
     """Algorithmic bytes per iteration of the tree kernels, from the device counters.
 
     Partition: per parent row 1 B (split-feature bin) + 4 B (index write) + 4 B (index read,
@@ -167,39 +210,60 @@ def kernel_bytes(counts, rows, grad):
     partition kernel builds the child itself, so those built rows are charged to it, minus
     the split-feature byte and the index it has already read."""
     s_gh = 2 if grad == "quantized" else 8
+    F = features
     rp, rb = counts["rows_parted"], counts["rows_built"]
     part = rp * 5 + max(rp - rows, 0) * 4
-    root_build = rows * (N_FEAT + s_gh)
+    root_build = rows * (F + s_gh)
     child_rows = max(rb - rows, 0)
     if counts["fused"]:
-        part += child_rows * (N_FEAT - 1 + s_gh)
+        part += child_rows * (F - 1 + s_gh)
         build = root_build
     else:
-        build = root_build + child_rows * (N_FEAT + s_gh + 4)
-    return {"partition": part, "build": build, "bin_bytes": rb * N_FEAT + rp}
+        build = root_build + child_rows * (F + s_gh + 4)
+    return {"partition": part, "build": build, "bin_bytes": rb * F + rp}
 
 
-def cpu_baseline(bins, mappers, y, grad, seconds_budget=25.0):
+def oracle_step(workload, data, score, grad, nt):
+    """One boosting iteration of the reference CPU learner (oracle/) on `score` in place."""
+    import oracle
+
+    w = WORKLOADS[workload]
+    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type",
+                                "bin_type")} for m in data.mappers]
+    if w["objective"] == "binary":
+        g, h = oracle.binary_gradients(score, data.y, 1.0, nt)
+    elif w["objective"] == "lambdarank":
+        g, h = oracle.lambdarank_gradients(score, data.y, data.qb, 1.0, True, 30, None, nt)
+    else:
+        g, h = oracle.l2_gradients(score, data.y, nt)
+    if grad == "quantized":
+        g, h, _, _ = oracle.quantize(g, h, 4)
+    tree, part, _ = oracle.grow_tree(data.bins, metas, g, h, w["leaves"], -1, nt,
+                                     min_data_in_leaf=w["min_data"])
+    oracle.tree_shrinkage(tree, LEARNING_RATE)
+    oracle.add_prediction_to_score(tree, part, score)
+
+
+def oracle_init_score(workload, data):
+    import oracle
+
+    obj = WORKLOADS[workload]["objective"]
+    init = 0.0 if obj == "lambdarank" else oracle.boost_from_score(obj, data.y)
+    return np.full(data.rows, init, dtype=np.float64)
+
+
+def cpu_baseline(workload, data, grad, seconds_budget=25.0):
     """The reference CPU learner (oracle/) on the host: boosting iterations on the full
     workload until ~seconds_budget is used (at least one)."""
     import oracle
 
     oracle.build()
-    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
-             for m in mappers]
     nt = os.cpu_count() or 1
-    q = grad == "quantized"
-    score = np.full(len(y), oracle.boost_from_score("binary", y), dtype=np.float64)
+    score = oracle_init_score(workload, data)
     t0 = time.perf_counter()
     iters = 0
     while True:
-        g, h = oracle.binary_gradients(score, y, 1.0, nt)
-        if q:
-            g, h, _, _ = oracle.quantize(g, h, 4)
-        tree, part, _ = oracle.grow_tree(bins, metas, g, h, NUM_LEAVES, -1, nt,
-                                         min_data_in_leaf=MIN_DATA_IN_LEAF)
-        oracle.tree_shrinkage(tree, LEARNING_RATE)
-        oracle.add_prediction_to_score(tree, part, score)
+        oracle_step(workload, data, score, grad, nt)
         iters += 1
         el = time.perf_counter() - t0
         if el >= seconds_budget or iters >= 50:
@@ -207,46 +271,39 @@ def cpu_baseline(bins, mappers, y, grad, seconds_budget=25.0):
     return iters / el, nt, iters, el
 
 
+def workload_desc(args, data):
+    w = WORKLOADS[args.workload]
+    q = 0 if data.qb is None else len(data.qb) - 1
+    return w["desc"].format(rows=data.rows, queries=q) + f" grad={args.grad}"
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    bins, mappers, y = make_data(args.rows)
+    data = make_data(args.workload, args.rows)
     import oracle
 
     oracle.build()
-    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
-             for m in mappers]
     nt = os.cpu_count() or 1
-    q = args.grad == "quantized"
-    score = np.full(len(y), oracle.boost_from_score("binary", y), dtype=np.float64)
-
-    def step():
-        g, h = oracle.binary_gradients(score, y, 1.0, nt)
-        if q:
-            g, h, _, _ = oracle.quantize(g, h, 4)
-        tree, part, _ = oracle.grow_tree(bins, metas, g, h, NUM_LEAVES, -1, nt,
-                                         min_data_in_leaf=MIN_DATA_IN_LEAF)
-        oracle.tree_shrinkage(tree, LEARNING_RATE)
-        oracle.add_prediction_to_score(tree, part, score)
-
+    score = oracle_init_score(args.workload, data)
     for _ in range(args.warmup):
-        step()
+        oracle_step(args.workload, data, score, args.grad, nt)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        oracle_step(args.workload, data, score, args.grad, nt)
     el = time.perf_counter() - t0
     v = args.steps / el
+    w = WORKLOADS[args.workload]
     out = {
         "metric": "boosting_iters_per_sec", "value": v, "unit": "iters/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * el / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": f"C1 binary {args.rows}x{N_FEAT} num_leaves={NUM_LEAVES} "
-                               f"grad={args.grad}", "rows": args.rows,
-                   "num_leaves": NUM_LEAVES, "max_bin": 255},
+        "config": {"workload": workload_desc(args, data), "rows": data.rows,
+                   "num_leaves": w["leaves"], "max_bin": 255},
         "cpu_baseline": {"value": v, "unit": "iters/s", "cores": nt, "kind": "port",
-                         "sample": f"{args.steps} full boosting iterations on all {args.rows} "
+                         "sample": f"{args.steps} full boosting iterations on all {data.rows} "
                                    f"rows, {nt} threads (C++ restatement; reference Rust "
                                    f"crates unbuildable here)"},
         "e2e": {"value": v, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -273,17 +330,25 @@ def run_ours(args):
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
     if rank == 0:
         libbuild.build()
-        make_data(args.rows)  # generates and caches for the other ranks
+        make_data(args.workload, args.rows)  # generates and caches for the other ranks
     if dist:
         dist.barrier()
     assert lgb._lib.device_count() > 0, "no CUDA device"
-    bins, mappers, y = make_data(args.rows)
-    p = params(args.grad)
+    data = make_data(args.workload, args.rows)
+    w = WORKLOADS[args.workload]
+    p = params(args.workload, args.grad)
     p["device"] = local
-    b0, b1 = D.shard_range(args.rows, world, rank)
+    # shards: contiguous rows, whole queries for a ranking objective
+    if data.qb is not None:
+        q0, q1 = D.shard_range(len(data.qb) - 1, world, rank)
+        b0, b1 = int(data.qb[q0]), int(data.qb[q1])
+        group = data.group[q0:q1]
+    else:
+        b0, b1 = D.shard_range(data.rows, world, rank)
+        group = None
     local_rows = b1 - b0
-    shard_bins = bins[:, b0:b1] if world > 1 else bins
-    shard_y = y[b0:b1]
+    shard_bins = data.bins[:, b0:b1] if world > 1 else data.bins
+    shard_y = data.y[b0:b1]
     comm = D.from_torch(local) if dist else None
 
     def max_over_ranks(x):
@@ -296,7 +361,8 @@ def run_ours(args):
         return float(t.item())
 
     # ---- device-resident run: inputs already in HBM when the timed region starts ----
-    ds = lgb.Dataset(bins=shard_bins, mappers=mappers, label=shard_y, params=p)
+    ds = lgb.Dataset(bins=shard_bins, mappers=data.mappers, label=shard_y, params=p,
+                     group=group)
     booster = lgb.Booster(p, ds, comm=comm)
     booster.update(args.warmup)
     if dist:
@@ -312,13 +378,13 @@ def run_ours(args):
 
     # ---- per-kernel timing of one more iteration (CUDA events on the library stream) ----
     kms, counts = booster.profile_iteration()
-    kb = kernel_bytes(counts, local_rows, args.grad)
+    kb = kernel_bytes(counts, local_rows, args.grad, data.features)
     peak, peak_kind = load_peaks()
     per_kernel = {}
     for cls, label in (("partition", "k_partition_q4 (partition + child histogram)"
                         if counts["fused"] else "k_partition (row partition)"),
                        ("build", "k_build_q4 (root histogram)" if counts["fused"]
-                        else "k_build (histogram build)")):
+                        else "k_build / k_build_q4 (histogram build)")):
         ms = kms[cls]
         ach = kb[cls] / (ms / 1000.0) / 1e9 if ms > 0 else 0.0
         per_kernel[cls] = {"kernel": label, "ms_per_iter": ms, "bytes_per_iter": kb[cls],
@@ -331,21 +397,23 @@ def run_ours(args):
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
-    ds2 = lgb.Dataset(bins=shard_bins, mappers=mappers, label=shard_y, params=p)
+    ds2 = lgb.Dataset(bins=shard_bins, mappers=data.mappers, label=shard_y, params=p,
+                      group=group)
     b2 = lgb.train(p, ds2, num_boost_round=args.steps, comm=comm)
     trees = b2.trees()
     scores = b2.train_scores()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
-    h2d = np.ascontiguousarray(shard_bins).nbytes + shard_y.nbytes
+    h2d = np.ascontiguousarray(shard_bins).nbytes + shard_y.nbytes + \
+        (0 if group is None else (len(group) + 1) * 4)
     d2h = scores.nbytes + sum(sum(np.asarray(v).nbytes for k, v in t.items()
                                   if isinstance(v, np.ndarray)) for t in trees)
     del b2, ds2
 
     cpu = None
     if not args.no_cpu_baseline and world == 1:
-        v, cores, iters, el = cpu_baseline(bins, mappers, y, args.grad)
+        v, cores, iters, el = cpu_baseline(args.workload, data, args.grad)
         cpu = {"value": v, "unit": "iters/s", "cores": cores, "kind": "port",
-               "sample": f"{iters} full boosting iterations on all {args.rows} rows "
+               "sample": f"{iters} full boosting iterations on all {data.rows} rows "
                          f"({el:.1f} s), {cores} threads"}
 
     par = "single GPU" if world == 1 else (
@@ -364,12 +432,11 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "int64+f64" if args.grad == "quantized" else "f32+f64",
         "data": "synthetic",
-        "config": {"workload": f"C1 binary {args.rows}x{N_FEAT} num_leaves={NUM_LEAVES} "
-                               f"min_data_in_leaf={MIN_DATA_IN_LEAF} max_bin=255 "
-                               f"grad={args.grad}",
-                   "rows": args.rows, "rows_per_gpu": local_rows, "features": N_FEAT,
-                   "num_leaves": NUM_LEAVES, "grad": args.grad, "parallelism": par,
-                   "l2": f"inputs larger than L2 (bin matrix {args.rows * 32 / 1e6:.0f} MB "
+        "config": {"workload": workload_desc(args, data),
+                   "rows": data.rows, "rows_per_gpu": local_rows, "features": data.features,
+                   "num_leaves": w["leaves"], "grad": args.grad, "parallelism": par,
+                   "l2": f"inputs larger than L2 (bin matrix "
+                         f"{data.rows * ((data.features + 15) // 16 * 16) / 1e6:.0f} MB "
                          f"> 126 MB)"},
         "roofline": {"bound": "hbm", "kernel": per_kernel[dom]["kernel"],
                      "achieved": per_kernel[dom]["achieved"], "peak": peak, "unit": "GB/s",
