@@ -384,6 +384,43 @@ int lgbm_b200_booster_create_distributed(lgbm_b200_dataset* ds, const float* lab
                                          const lgbm_b200_train_config* cfg,
                                          lgbm_b200_comm* comm, lgbm_b200_booster** out);
 
+/* ---- Batch prediction from raw feature values (Tree::predict / GetLeaf,
+ * lgbm-model/src/tree.rs:193-300; GbdtModel predict, lgbm-model/src/predict.rs) ---- */
+
+/* A tree ensemble: every tree's internal nodes and leaves concatenated, in tree order
+ * (borrowed for the create call). Child indices are tree-local: >= 0 an internal node
+ * (always greater than its parent's index, as LightGBM numbers nodes), < 0 the leaf ~c.
+ * A categorical node's threshold is its index into cat_boundaries over ALL trees;
+ * cat_threshold holds the bitsets of real category values (LightGBM model text). */
+typedef struct lgbm_b200_model {
+  int32_t num_trees;
+  int32_t num_features;          /* row width: max_feature_idx + 1 */
+  const int32_t* node_offset;    /* [num_trees + 1] */
+  const int32_t* leaf_offset;    /* [num_trees + 1] */
+  const int32_t* split_feature;  /* [nodes] */
+  const double* threshold;       /* [nodes] */
+  const int8_t* decision_type;   /* [nodes] bit0 categorical, bit1 default left, bits 2-3 missing type */
+  const int32_t* left_child;     /* [nodes] */
+  const int32_t* right_child;    /* [nodes] */
+  const double* leaf_value;      /* [leaves] */
+  int32_t num_cat;
+  int32_t transform;             /* 0 identity, 1 sigmoid (binary objective) */
+  const int32_t* cat_boundaries; /* [num_cat + 1] */
+  const uint32_t* cat_threshold; /* [cat_boundaries[num_cat]] */
+  double sigmoid;
+} lgbm_b200_model;
+
+typedef struct lgbm_b200_predictor lgbm_b200_predictor;
+
+/* Uploads the ensemble to `device` after checking every index in it. */
+int lgbm_b200_predictor_create(int32_t device, const lgbm_b200_model* model,
+                               lgbm_b200_predictor** out);
+int lgbm_b200_predictor_destroy(lgbm_b200_predictor* p);
+/* rows: host row-major f64 [num_rows][num_features]; out: host f64 [num_rows], the sum
+ * of the trees' leaf values in tree order, then the model's transform unless raw_score. */
+int lgbm_b200_predict(lgbm_b200_predictor* p, const double* rows, int64_t num_rows,
+                      int32_t raw_score, double* out);
+
 #ifdef __cplusplus
 }
 #endif

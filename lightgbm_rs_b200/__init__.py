@@ -12,11 +12,12 @@ import ctypes
 import numpy as np
 
 from . import _lib as C
+from . import model_text as MT
 from ._lib import LightGBMError
 from . import distributed  # noqa: E402
 
-__all__ = ["Dataset", "Booster", "train", "bin_column", "LightGBMError", "Learner",
-           "distributed", "categorical_bitsets"]
+__all__ = ["Dataset", "Booster", "Predictor", "train", "bin_column", "LightGBMError",
+           "Learner", "distributed", "categorical_bitsets", "model_text"]
 
 # Reference config defaults (crates/lgbm-core/src/config/mod.rs:430-587).
 _DEFAULTS = {
@@ -247,19 +248,76 @@ class Learner:
             pass
 
 
-class Booster:
-    """Trained model (lightgbm_rs.Booster subset: predict, trees, scores)."""
+class Predictor:
+    """A tree ensemble on the device for batch prediction from raw feature values
+    (lgbm_b200_predictor_*)."""
 
-    def __init__(self, params, train_set, comm=None):
-        """comm: a distributed.Communicator for data-parallel training; train_set then
-        holds this rank's shard of the rows (in global row order, shards in rank order)."""
+    def __init__(self, model, device=0):
+        self.model = model
+        f = MT.flatten(model)
+        self._flat = f  # the create call borrows these arrays
+        m = C.ModelC()
+        m.num_trees, m.num_features = f["num_trees"], f["num_features"]
+        for k in ("node_offset", "leaf_offset", "split_feature", "threshold", "decision_type",
+                  "left_child", "right_child", "leaf_value", "cat_boundaries",
+                  "cat_threshold"):
+            setattr(m, k, f[k].ctypes.data if len(f[k]) else None)
+        m.num_cat, m.transform, m.sigmoid = f["num_cat"], f["transform"], f["sigmoid"]
+        h = ctypes.c_void_p()
+        C.check(C.lib().lgbm_b200_predictor_create(int(device), ctypes.byref(m),
+                                                   ctypes.byref(h)))
+        self._handle = h
+
+    def predict(self, data, raw_score=False):
+        X = np.ascontiguousarray(data, dtype=np.float64)
+        if X.ndim == 1:
+            X = X.reshape(1, -1)
+        nf = self.model.max_feature_idx + 1
+        if X.ndim != 2 or X.shape[1] != nf:
+            raise LightGBMError(C.LENGTH_MISMATCH,
+                                f"data has {X.shape[-1]} columns, the model {nf} features")
+        out = np.empty(X.shape[0], dtype=np.float64)
+        C.check(C.lib().lgbm_b200_predict(self._handle, C.ptr(X), X.shape[0],
+                                          int(bool(raw_score)), C.ptr(out)))
+        return out
+
+    def __del__(self):
+        try:
+            C.lib().lgbm_b200_predictor_destroy(self._handle)
+        except Exception:
+            pass
+
+
+class Booster:
+    """lightgbm_rs.Booster for this path: training on the device, model text, predict."""
+
+    def __init__(self, params=None, train_set=None, model_file=None, model_str=None,
+                 comm=None):
+        """Train from `train_set`, or load LightGBM model text (`model_file` / `model_str`)
+        for prediction. comm: a distributed.Communicator for data-parallel training;
+        train_set then holds this rank's shard of the rows (in global row order, shards in
+        rank order)."""
         self.params = _resolve(params)
         self.train_set = train_set
+        self._model = None
+        self._predictor = None
+        self._handle = None
+        if model_file is not None or model_str is not None:
+            if model_str is None:
+                with open(model_file) as fh:
+                    model_str = fh.read()
+            self._model = MT.parse(model_str)
+            self.objective = self._model.objective_name
+            self.params["sigmoid"] = self._model.sigmoid
+            return
+        if train_set is None:
+            raise LightGBMError(C.INVALID_ARGUMENT, "Booster needs train_set or a model")
         p = self.params
         obj = str(p["objective"]).lower()
         if obj not in _OBJECTIVES:
             raise LightGBMError(C.CAPABILITY_UNAVAILABLE, f"objective {obj!r} not on the path")
-        self.objective = obj
+        self.objective = {C.OBJECTIVE_BINARY: "binary", C.OBJECTIVE_L2: "regression",
+                          C.OBJECTIVE_LAMBDARANK: "lambdarank"}[_OBJECTIVES[obj]]
         if train_set.label is None:
             raise LightGBMError(C.INVALID_ARGUMENT, "Dataset has no label")
         cfg = C.TrainConfig(_learner_config(p), _OBJECTIVES[obj], int(bool(p["use_quantized_grad"])),
@@ -303,18 +361,44 @@ class Booster:
         self._trees = None
 
     def update(self, num_iterations=1):
+        self._require_training()
         done = C._i32(0)
         C.check(C.lib().lgbm_b200_booster_train(self._handle, int(num_iterations),
                                                 ctypes.byref(done)))
         self._trees = None
+        self._model = None
+        self._predictor = None
         return done.value
 
+    def _require_training(self):
+        if self._handle is None:
+            raise LightGBMError(C.INVALID_ARGUMENT, "a booster loaded from model text "
+                                "does not train")
+
+    def model(self):
+        """The ensemble as a model_text.Model (trained trees, or the loaded model)."""
+        if self._model is None:
+            self._model = MT.from_booster(self)
+        return self._model
+
+    def model_to_string(self):
+        """LightGBM v4 model text (GBDT::SaveModelToString)."""
+        return MT.dump(self.model())
+
+    def save_model(self, filename):
+        with open(filename, "w") as fh:
+            fh.write(self.model_to_string())
+        return self
+
     def num_trees(self):
+        if self._handle is None:
+            return len(self._model.trees)
         n = C._i32(0)
         C.check(C.lib().lgbm_b200_booster_num_trees(self._handle, ctypes.byref(n)))
         return n.value
 
     def init_score(self):
+        self._require_training()
         v = C._f64(0.0)
         C.check(C.lib().lgbm_b200_booster_init_score(self._handle, ctypes.byref(v)))
         return v.value
@@ -360,72 +444,18 @@ class Booster:
                 {"launches": int(cnt[0]), "builds": int(cnt[1]), "rows_built": int(cnt[2]),
                  "splits": int(cnt[3]), "rows_parted": int(cnt[4]), "fused": bool(cnt[5])})
 
-    def _predict_bins(self, bins_cols):
-        """Raw score from binned features (feature-major [F, N])."""
-        n = bins_cols.shape[1]
-        out = np.full(n, self.init_score(), dtype=np.float64)
-        mappers = self.train_set.mappers
-        for t in self.trees():
-            if t["num_leaves"] <= 1:
-                continue
-            node = np.zeros(n, dtype=np.int64)
-            active = np.ones(n, dtype=bool)
-            leaf = np.zeros(n, dtype=np.int64)
-            while active.any():
-                nd = node[active]
-                f = t["split_feature"][nd]
-                b = bins_cols[f, np.nonzero(active)[0]].astype(np.int64)
-                thr = t["threshold_bin"][nd].astype(np.int64)
-                dl = (t["decision_type"][nd] & 2) != 0
-                nb = np.array([mappers[ff]["num_bin"] for ff in f], dtype=np.int64)
-                mt = np.array([mappers[ff].get("missing_type", 0) for ff in f], dtype=np.int64)
-                na = (mt == 2) & (nb > 2) & (b == nb - 1)
-                right = np.where(na, ~dl, b > thr)
-                cat = (t["decision_type"][nd] & 1) != 0
-                if cat.any():
-                    # categorical node: the bins in the node's set go left
-                    words = t["cat_bins"][nd, np.minimum(b >> 5, 7)].astype(np.int64)
-                    right = np.where(cat, ((words >> (b & 31)) & 1) == 0, right)
-                nxt = np.where(right, t["right_child"][nd], t["left_child"][nd])
-                idx = np.nonzero(active)[0]
-                done = nxt < 0
-                leaf[idx[done]] = ~nxt[done]
-                node[idx] = np.where(done, 0, nxt)
-                active[idx[done]] = False
-            out += t["leaf_value"][leaf]
-        return out
-
     def predict(self, data, raw_score=False):
-        X = np.asarray(data, dtype=np.float64)
-        cols = []
-        for j, m in enumerate(self.train_set.mappers):
-            v = X[:, j].copy()
-            nanm = np.isnan(v)
-            if m.get("bin_type", 0) == 1:
-                # categorical value_to_bin: the category's bin; NaN, negative, unseen -> 0
-                lut = {int(c): b for b, c in enumerate(m["bin_to_category"]) if c >= 0}
-                iv = np.where(nanm, -1, np.trunc(np.where(nanm, 0, v))).astype(np.int64)
-                cols.append(np.array([lut.get(int(c), 0) if c >= 0 else 0 for c in iv],
-                                     dtype=np.int64))
-                continue
-            up = m["upper"]
-            if m.get("missing_type", 0) == 2:
-                b = np.searchsorted(up[:-1][: m["num_bin"] - 1], v, side="left")
-                b = np.minimum(b, m["num_bin"] - 2)
-                b[nanm] = m["num_bin"] - 1
-            else:
-                v[nanm] = 0.0
-                b = np.searchsorted(up[: m["num_bin"]], v, side="left")
-                b = np.minimum(b, m["num_bin"] - 1)
-            cols.append(b)
-        raw = self._predict_bins(np.stack(cols))
-        if raw_score or self.objective != "binary":
-            return raw
-        return 1.0 / (1.0 + np.exp(-float(self.params["sigmoid"]) * raw))
+        """Predictions for raw feature rows [n, num_features] on the device: the trees'
+        leaf values summed in tree order (the boost-from-average score is in the first
+        tree), then the sigmoid for a binary model unless raw_score."""
+        if self._predictor is None:
+            self._predictor = Predictor(self.model(), int(self.params.get("device", 0)))
+        return self._predictor.predict(data, raw_score=raw_score)
 
     def __del__(self):
         try:
-            C.lib().lgbm_b200_booster_destroy(self._handle)
+            if self._handle is not None:
+                C.lib().lgbm_b200_booster_destroy(self._handle)
         except Exception:
             pass
 

@@ -98,6 +98,14 @@ class BinMapperC(ctypes.Structure):
                 ("min_val", _f64), ("max_val", _f64), ("sparse_rate", _f64)]
 
 
+class ModelC(ctypes.Structure):
+    _fields_ = [("num_trees", _i32), ("num_features", _i32), ("node_offset", _P),
+                ("leaf_offset", _P), ("split_feature", _P), ("threshold", _P),
+                ("decision_type", _P), ("left_child", _P), ("right_child", _P),
+                ("leaf_value", _P), ("num_cat", _i32), ("transform", _i32),
+                ("cat_boundaries", _P), ("cat_threshold", _P), ("sigmoid", _f64)]
+
+
 _SIGS = {
     "lgbm_b200_last_error": ([], ctypes.c_char_p),
     "lgbm_b200_abi_version": ([], _i32),
@@ -133,6 +141,9 @@ _SIGS = {
     "lgbm_b200_comm_create": ([_i32, _i32, _i32, _P, _P], ctypes.c_int),
     "lgbm_b200_comm_destroy": ([_P], ctypes.c_int),
     "lgbm_b200_booster_create_distributed": ([_P, _P, _P, _P, _P], ctypes.c_int),
+    "lgbm_b200_predictor_create": ([_i32, _P, _P], ctypes.c_int),
+    "lgbm_b200_predictor_destroy": ([_P], ctypes.c_int),
+    "lgbm_b200_predict": ([_P, _P, _i64, _i32, _P], ctypes.c_int),
 }
 
 _lib = None

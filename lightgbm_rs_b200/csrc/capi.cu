@@ -1745,3 +1745,154 @@ int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
 }
 
 }  // extern "C"
+
+struct lgbm_b200_predictor {
+  int device = 0;
+  PredModelDev m{};
+  DevBuf<int32_t> offsets;  // node_offset | leaf_offset | cat_boundaries
+  DevBuf<PredNode> nodes;
+  DevBuf<double> leaf_value;
+  DevBuf<uint32_t> cat_threshold;
+  DevBuf<double> rows;
+  DevBuf<double> out;
+  cudaStream_t stream = nullptr;
+  ~lgbm_b200_predictor() {
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+extern "C" {
+
+int lgbm_b200_predictor_create(int32_t device, const lgbm_b200_model* m,
+                               lgbm_b200_predictor** out) {
+  if (!m || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "predictor_create: null argument");
+  *out = nullptr;
+  const int32_t T = m->num_trees, F = m->num_features;
+  if (T < 0 || F < 1 || !m->node_offset || !m->leaf_offset)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "predictor_create: %d trees, %d features", T, F);
+  if (m->transform != 0 && m->transform != 1)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "transform %d", m->transform);
+  if (m->node_offset[0] != 0 || m->leaf_offset[0] != 0)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "node and leaf offsets must start at 0");
+  const int32_t NC = m->num_cat;
+  if (NC < 0 || (NC > 0 && (!m->cat_boundaries || !m->cat_threshold)))
+    return fail(LGBM_B200_INVALID_ARGUMENT, "num_cat %d", NC);
+  if (NC > 0 && m->cat_boundaries[0] != 0)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "cat_boundaries must start at 0");
+  for (int32_t c = 0; c < NC; ++c)
+    if (m->cat_boundaries[c + 1] < m->cat_boundaries[c])
+      return fail(LGBM_B200_INVALID_ARGUMENT, "cat_boundaries must be non-decreasing");
+  // every index the kernel follows is checked here
+  std::vector<PredNode> nodes;
+  for (int32_t t = 0; t < T; ++t) {
+    const int32_t nb = m->node_offset[t], ne = m->node_offset[t + 1];
+    const int32_t lb = m->leaf_offset[t], le = m->leaf_offset[t + 1];
+    const int32_t nn = ne - nb, nl = le - lb;
+    if (nn < 0 || nl < 1 || nl != nn + 1)
+      return fail(LGBM_B200_INVALID_ARGUMENT, "tree %d: %d internal nodes, %d leaves", t, nn, nl);
+    for (int32_t i = 0; i < nn; ++i) {
+      PredNode p{};
+      const int32_t k = nb + i;
+      p.threshold = m->threshold[k];
+      p.left = m->left_child[k];
+      p.right = m->right_child[k];
+      p.feature = m->split_feature[k];
+      p.dt = (int32_t)(uint8_t)m->decision_type[k];
+      p.cat = 0;
+      if (p.feature < 0 || p.feature >= F)
+        return fail(LGBM_B200_INVALID_ARGUMENT, "tree %d node %d: feature %d of %d", t, i,
+                    p.feature, F);
+      for (int32_t ch : {p.left, p.right}) {
+        if (ch >= 0 ? (ch <= i || ch >= nn) : (~ch >= nl))
+          return fail(LGBM_B200_INVALID_ARGUMENT, "tree %d node %d: child %d out of range", t,
+                      i, ch);
+      }
+      if (p.dt & 1) {
+        const double c = p.threshold;
+        if (!(c >= 0.0 && c < (double)NC && c == std::floor(c)))
+          return fail(LGBM_B200_INVALID_ARGUMENT,
+                      "tree %d node %d: categorical index %g of %d", t, i, c, NC);
+        p.cat = (int32_t)c;
+      }
+      nodes.push_back(p);
+    }
+  }
+  if (!have_device()) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "no CUDA device");
+  DeviceGuard g(device);
+  auto p = std::make_unique<lgbm_b200_predictor>();
+  p->device = device;
+  CUDA_TRY(cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking));
+  const size_t noff = (size_t)2 * (T + 1) + (size_t)NC + 1;
+  CUDA_TRY(p->offsets.alloc(noff));
+  std::vector<int32_t> offs;
+  offs.insert(offs.end(), m->node_offset, m->node_offset + T + 1);
+  offs.insert(offs.end(), m->leaf_offset, m->leaf_offset + T + 1);
+  if (NC > 0)
+    offs.insert(offs.end(), m->cat_boundaries, m->cat_boundaries + NC + 1);
+  else
+    offs.push_back(0);
+  CUDA_TRY(cudaMemcpy(p->offsets.p, offs.data(), offs.size() * 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(p->nodes.alloc(std::max<size_t>(nodes.size(), 1)));
+  if (!nodes.empty())
+    CUDA_TRY(cudaMemcpy(p->nodes.p, nodes.data(), nodes.size() * sizeof(PredNode),
+                        cudaMemcpyHostToDevice));
+  const int32_t L = m->leaf_offset[T];
+  CUDA_TRY(p->leaf_value.alloc(std::max<int32_t>(L, 1)));
+  if (L > 0)
+    CUDA_TRY(cudaMemcpy(p->leaf_value.p, m->leaf_value, (size_t)L * 8, cudaMemcpyHostToDevice));
+  const int32_t W = NC > 0 ? m->cat_boundaries[NC] : 0;
+  CUDA_TRY(p->cat_threshold.alloc(std::max<int32_t>(W, 1)));
+  if (W > 0)
+    CUDA_TRY(cudaMemcpy(p->cat_threshold.p, m->cat_threshold, (size_t)W * 4,
+                        cudaMemcpyHostToDevice));
+  PredModelDev& d = p->m;
+  d.num_trees = T;
+  d.num_features = F;
+  d.transform = m->transform;
+  d.sigmoid = m->sigmoid;
+  d.node_offset = p->offsets.p;
+  d.leaf_offset = p->offsets.p + (T + 1);
+  d.cat_boundaries = p->offsets.p + 2 * (T + 1);
+  d.nodes = p->nodes.p;
+  d.leaf_value = p->leaf_value.p;
+  d.cat_threshold = p->cat_threshold.p;
+  *out = p.release();
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_predictor_destroy(lgbm_b200_predictor* p) {
+  if (!p) return LGBM_B200_OK;
+  DeviceGuard g(p->device);
+  delete p;
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_predict(lgbm_b200_predictor* p, const double* rows, int64_t num_rows,
+                      int32_t raw_score, double* out) {
+  if (!p || (num_rows > 0 && (!rows || !out)) || num_rows < 0)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "predict: null argument or negative row count");
+  if (num_rows == 0) return LGBM_B200_OK;
+  DeviceGuard g(p->device);
+  const int64_t F = p->m.num_features;
+  // rows move in chunks of at most 256 MB
+  const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(num_rows, (256ll << 20) / (8 * F)));
+  if ((int64_t)p->rows.n < chunk * F) {
+    p->rows.release();
+    p->out.release();
+    CUDA_TRY(p->rows.alloc((size_t)(chunk * F)));
+    CUDA_TRY(p->out.alloc((size_t)chunk));
+  }
+  for (int64_t r0 = 0; r0 < num_rows; r0 += chunk) {
+    const int64_t n = std::min(chunk, num_rows - r0);
+    CUDA_TRY(cudaMemcpyAsync(p->rows.p, rows + r0 * F, (size_t)(n * F) * 8,
+                             cudaMemcpyHostToDevice, p->stream));
+    launch_predict(p->m, p->rows.p, n, raw_score, p->out.p, p->stream);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaMemcpyAsync(out + r0, p->out.p, (size_t)n * 8, cudaMemcpyDeviceToHost,
+                             p->stream));
+  }
+  CUDA_TRY(cudaStreamSynchronize(p->stream));
+  return LGBM_B200_OK;
+}
+
+}  // extern "C"

@@ -179,6 +179,32 @@ struct FinishDev {
 void launch_finish_iteration(const GrowDev& d, const FinishDev& f, cudaStream_t st,
                              LaunchProfiler* prof = nullptr);
 
+// Batch prediction (predict.cu). One internal node of a flattened ensemble.
+struct PredNode {
+  double threshold;  // numerical threshold
+  int32_t left;      // tree-local: >= 0 node, < 0 ~leaf
+  int32_t right;
+  int32_t feature;
+  int32_t cat;       // categorical: index into cat_boundaries over all trees
+  int32_t dt;        // decision_type
+  int32_t _pad;
+};
+struct PredModelDev {
+  int32_t num_trees;
+  int32_t num_features;
+  int32_t transform;  // 0 identity, 1 sigmoid
+  int32_t _pad;
+  double sigmoid;
+  const int32_t* node_offset;  // [num_trees + 1]
+  const int32_t* leaf_offset;  // [num_trees + 1]
+  const PredNode* nodes;
+  const double* leaf_value;
+  const int32_t* cat_boundaries;
+  const uint32_t* cat_threshold;
+};
+void launch_predict(const PredModelDev& m, const double* rows, int64_t n, int32_t raw,
+                    double* out, cudaStream_t st);
+
 // Standalone per-op launches (the Backend-trait entry points).
 void launch_construct_histogram_f32(const uint8_t* bins_rm, int32_t stride, int64_t n,
                                     const float2* gh, int32_t num_bin, double scale_g,

@@ -152,6 +152,8 @@ def lib():
             _P, _P, ctypes.c_int64, _P, ctypes.c_int32, ctypes.c_double, ctypes.c_int32,
             ctypes.c_int32, _P, ctypes.c_int32, _P, _P, ctypes.c_int32]
         L.oracle_lambdarank_gradients.restype = ctypes.c_int32
+        L.oracle_predict_raw.argtypes = [ctypes.c_int32, ctypes.c_int32] + [_P] * 11 + [
+            ctypes.c_int64, _P]
         L.oracle_binary_boost_from_score.argtypes = [_P, ctypes.c_int64, ctypes.c_double]
         L.oracle_binary_boost_from_score.restype = ctypes.c_double
         L.oracle_l2_boost_from_score.argtypes = [_P, ctypes.c_int64]
@@ -424,3 +426,19 @@ def categorical_bitsets(tree, bin_to_category_of):
         words.extend(blk)
         bounds.append(bounds[-1] + n)
     return bounds, words
+
+
+def predict_raw(flat, rows):
+    """Raw scores of a flattened ensemble (the dict lightgbm_rs_b200.model_text.flatten
+    returns) over row-major f64 rows: the reference's tree walk, in tree order."""
+    rows = np.ascontiguousarray(rows, dtype=np.float64)
+    n = rows.shape[0]
+    out = np.empty(n, dtype=np.float64)
+    cb = flat["cat_boundaries"] if len(flat["cat_boundaries"]) else np.zeros(1, np.int32)
+    ct = flat["cat_threshold"] if len(flat["cat_threshold"]) else np.zeros(1, np.uint32)
+    lib().oracle_predict_raw(
+        flat["num_trees"], flat["num_features"], _ptr(flat["node_offset"]),
+        _ptr(flat["leaf_offset"]), _ptr(flat["split_feature"]), _ptr(flat["threshold"]),
+        _ptr(flat["decision_type"]), _ptr(flat["left_child"]), _ptr(flat["right_child"]),
+        _ptr(flat["leaf_value"]), _ptr(cb), _ptr(ct), _ptr(rows), n, _ptr(out))
+    return out

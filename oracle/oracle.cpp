@@ -1194,6 +1194,60 @@ int32_t oracle_lambdarank_gradients(const double* score, const float* label, int
   return 0;
 }
 
+// GbdtModel raw prediction (lgbm-model/src/predict.rs) over a flattened ensemble:
+// Tree::get_leaf with numerical_decision / categorical_decision
+// (lgbm-model/src/tree.rs:173-300), leaf values summed in tree order. Child indices are
+// tree-local (< 0: leaf ~c); a categorical node's threshold indexes cat_boundaries over
+// all trees.
+void oracle_predict_raw(int32_t num_trees, int32_t num_features, const int32_t* node_offset,
+                        const int32_t* leaf_offset, const int32_t* split_feature,
+                        const double* threshold, const int8_t* decision_type,
+                        const int32_t* left_child, const int32_t* right_child,
+                        const double* leaf_value, const int32_t* cat_boundaries,
+                        const uint32_t* cat_threshold, const double* rows, int64_t n,
+                        double* out) {
+  for (int64_t r = 0; r < n; ++r) {
+    const double* x = rows + r * num_features;
+    double acc = 0.0;
+    for (int32_t t = 0; t < num_trees; ++t) {
+      const int32_t nb = node_offset[t];
+      int32_t node = node_offset[t + 1] > nb ? 0 : -1;
+      while (node >= 0) {
+        const int32_t k = nb + node;
+        double fval = x[split_feature[k]];
+        const int8_t dt = decision_type[k];
+        if (dt & 1) {
+          if (std::isnan(fval)) {
+            node = right_child[k];
+            continue;
+          }
+          const int32_t iv = (int32_t)std::max(-2147483648.0, std::min(2147483647.0, fval));
+          if (iv < 0) {
+            node = right_child[k];
+            continue;
+          }
+          const int32_t c = (int32_t)threshold[k];
+          const int32_t lo = cat_boundaries[c], nw = cat_boundaries[c + 1] - lo;
+          const int32_t w = iv / 32;
+          const bool in = w < nw && ((cat_threshold[lo + w] >> (iv % 32)) & 1u);
+          node = in ? left_child[k] : right_child[k];
+          continue;
+        }
+        const int mt = (dt >> 2) & 3;
+        if (std::isnan(fval) && mt != 2) fval = 0.0;
+        if ((mt == 1 && fval >= -kZeroThreshold && fval <= kZeroThreshold) ||
+            (mt == 2 && std::isnan(fval))) {
+          node = (dt & 2) ? left_child[k] : right_child[k];
+          continue;
+        }
+        node = fval <= threshold[k] ? left_child[k] : right_child[k];
+      }
+      acc += leaf_value[leaf_offset[t] + ~node];
+    }
+    out[r] = acc;
+  }
+}
+
 // Binary::boost_from_score (binary.rs:178-194)
 double oracle_binary_boost_from_score(const float* label, int64_t n, double sigmoid) {
   if (n == 0) return 0.0;

@@ -322,3 +322,32 @@ def rank_case():
     regen = rng.randint(0, 4, size=30).astype(np.float32)
     assert np.array_equal(regen, labels), "rank corpus regeneration drifted"
     return X, labels, qb, gh["GRAD"], gh["HESS"], final
+
+
+def bits_matrix(name):
+    """`# rows=<n> cols=<m>` (or width=) header + rows of f64 bit patterns."""
+    lines = read_text(name).splitlines()
+    rows = [[int(t) for t in l.split()] for l in lines[1:] if l.strip() and not l.startswith("#")]
+    return np.array(rows, dtype=np.uint64).view(np.float64)
+
+
+def early_stop_cells(name):
+    """`CELL freq=.. margin=.. rows=.. width=..` followed by one f64 bit pattern per row."""
+    cells, cur = [], None
+    for l in read_text(name).splitlines():
+        if l.startswith("CELL"):
+            f = dict(t.split("=") for t in l.split()[1:])
+            cur = {k: int(v) for k, v in f.items()}
+            cur["values"] = []
+            cells.append(cur)
+        elif l.strip() and not l.startswith("#") and cur is not None:
+            cur["values"].append(int(l.split()[0]))
+    for c in cells:
+        c["values"] = np.array(c["values"], dtype=np.uint64).view(np.float64)
+    return cells
+
+
+MODEL_TEXTS = ["rank_lambdarank_byq0_es0_model.txt", "binary_spine_model.txt",
+               "cat_onehot.txt", "cat_manyvsmany.txt", "predict_numeric_model.txt",
+               "predict_categorical_model.txt", "na_missing_model.txt",
+               "regression_3tree_model.txt"]

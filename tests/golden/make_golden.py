@@ -15,7 +15,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
-# (path inside the reference project, compress?)
+# (path inside the reference project, compress?[, name under tests/golden/])
 FILES = [
     ("crates/oracle-harness/tests/fixtures/kernels/histogram.txt", True),
     ("crates/oracle-harness/tests/fixtures/kernels/split.txt", False),
@@ -44,14 +44,34 @@ FILES = [
     ("crates/oracle-harness/tests/fixtures/rank/lambdarank_gh_iter1.txt", False),
     ("crates/oracle-harness/tests/fixtures/rank/lambdarank_scores.txt", False),
     ("crates/oracle-harness/tests/fixtures/rank/rank_lambdarank_byq0_es0_model.txt", False),
+    ("crates/oracle-harness/tests/fixtures/boosting/binary_spine_pred.txt", False),
+    ("crates/oracle-harness/tests/fixtures/predict_modes/numeric/model.txt", False,
+     "predict_numeric_model.txt"),
+    ("crates/oracle-harness/tests/fixtures/predict_modes/numeric/X.txt", False,
+     "predict_numeric_X.txt"),
+    ("crates/oracle-harness/tests/fixtures/predict_modes/numeric/early_stop.txt", False,
+     "predict_numeric_early_stop.txt"),
+    ("crates/oracle-harness/tests/fixtures/predict_modes/categorical/model.txt", False,
+     "predict_categorical_model.txt"),
+    ("crates/oracle-harness/tests/fixtures/predict_modes/categorical/X.txt", False,
+     "predict_categorical_X.txt"),
+    ("crates/oracle-harness/tests/fixtures/predict_modes/categorical/contrib.txt", False,
+     "predict_categorical_contrib.txt"),
+    ("crates/oracle-harness/tests/fixtures/predict_modes/numeric/contrib.txt", False,
+     "predict_numeric_contrib.txt"),
+    ("crates/oracle-harness/tests/fixtures/na_missing/model_real.txt", False,
+     "na_missing_model.txt"),
+    ("crates/oracle-harness/tests/fixtures/json_dump/regression_3tree/model.txt", False,
+     "regression_3tree_model.txt"),
 ]
 
 
 def main() -> None:
     ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-    for rel, compress in FILES:
+    for entry in FILES:
+        rel, compress = entry[0], entry[1]
         src = os.path.join(ref, rel)
-        name = os.path.basename(rel)
+        name = entry[2] if len(entry) > 2 else os.path.basename(rel)
         if not os.path.exists(src):
             print(f"missing: {src}")
             continue
