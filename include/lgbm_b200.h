@@ -302,6 +302,25 @@ int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t
                              int64_t num_data, int32_t num_features,
                              const lgbm_b200_feature_meta* meta, lgbm_b200_dataset** out);
 int lgbm_b200_dataset_destroy(lgbm_b200_dataset* ds);
+
+/* The device dataset from raw feature values: BinMapper::value_to_bin
+ * (crates/lgbm-dataset/src/bin_mapper.rs:148-199) runs on the device with the mappers
+ * found on the host from each column's sample (lgbm_b200_bin_column /
+ * lgbm_b200_bin_column_categorical with bins_out = NULL). columns: feature-major host
+ * arrays of f32 (value_width 4) or f64 (8). upper_bounds[f] (numerical features) and
+ * bin_to_category[f] (categorical features) hold num_bin values each. Replaces the
+ * host binning loop of the reference's dataset construction
+ * (crates/lgbm/src/booster.rs:381-540). */
+int lgbm_b200_dataset_create_from_values(int32_t device, const void* const* columns,
+                                         int32_t value_width, int64_t num_data,
+                                         int32_t num_features,
+                                         const lgbm_b200_feature_meta* meta,
+                                         const double* const* upper_bounds,
+                                         const int32_t* const* bin_to_category,
+                                         lgbm_b200_dataset** out);
+/* Copies the device bin matrix back: row-major u8 [num_data][stride], stride =
+ * num_features rounded up to a multiple of 16. */
+int lgbm_b200_dataset_copy_bins(const lgbm_b200_dataset* ds, uint8_t* out);
 int lgbm_b200_dataset_num_data(const lgbm_b200_dataset* ds, int64_t* out);
 
 /* ------------------------------------------------------------ tree learner */

@@ -120,8 +120,10 @@ def bin_column(values, max_bin=255, min_data_in_bin=3, min_data_in_leaf=20, pre_
 class Dataset:
     """Binned training data resident on one GPU (lightgbm_rs.Dataset for this path).
 
-    data: 2-D array [num_data, num_features] of raw values (binned on the host with
-    the reference BinMapper), or pass `bins`/`mappers` to reuse an existing binning."""
+    data: 2-D array [num_data, num_features] of raw values: the bin mappers are found on
+    the host from each column's sample (the reference BinMapper), and the values are
+    binned on the device when the dataset is constructed. Or pass `bins` / `mappers` to
+    reuse an existing binning."""
 
     def __init__(self, data=None, label=None, params=None, bins=None, mappers=None,
                  categorical_feature=None, group=None):
@@ -136,26 +138,69 @@ class Dataset:
         self.set_group(group)
         cats = set(int(c) for c in (categorical_feature or []))
         self.label = None if label is None else np.ascontiguousarray(label, dtype=np.float32)
+        self._cats = cats
+        self._bins = None
+        self._values = None
         if bins is None:
             X = np.asarray(data)
             if X.ndim != 2:
                 raise LightGBMError(C.INVALID_ARGUMENT, "data must be 2-D")
-            p = self.params
-            cols, mappers = [], []
-            for j in range(X.shape[1]):
-                m, b = bin_column(X[:, j], p["max_bin"], p["min_data_in_bin"],
-                                  p["min_data_in_leaf"], p["feature_pre_filter"],
-                                  p["use_missing"], p["zero_as_missing"],
-                                  p["bin_construct_sample_cnt"], p["data_random_seed"],
-                                  categorical=j in cats)
-                mappers.append(m)
-                cols.append(b.astype(np.uint8 if m["num_bin"] <= 256 else np.uint32))
-            width = 1 if all(c.dtype == np.uint8 for c in cols) else 4
-            bins = np.stack([c.astype(np.uint8 if width == 1 else np.uint32) for c in cols])
-        self.bins = np.ascontiguousarray(bins)
-        self.mappers = mappers
-        self.num_features, self.num_data = self.bins.shape
+            dt = np.float32 if X.dtype == np.float32 else np.float64
+            # feature-major raw values, binned on the device by construct()
+            self._values = np.ascontiguousarray(X.T, dtype=dt)
+            self.num_features, self.num_data = self._values.shape
+            self.mappers = self._find_mappers()
+        else:
+            self._bins = np.ascontiguousarray(bins)
+            self.mappers = mappers
+            self.num_features, self.num_data = self._bins.shape
         self._handle = None
+
+    def _bin_kwargs(self):
+        p = self.params
+        return dict(max_bin=p["max_bin"], min_data_in_bin=p["min_data_in_bin"],
+                    min_data_in_leaf=p["min_data_in_leaf"], pre_filter=p["feature_pre_filter"],
+                    use_missing=p["use_missing"], zero_as_missing=p["zero_as_missing"],
+                    bin_construct_sample_cnt=p["bin_construct_sample_cnt"],
+                    data_random_seed=p["data_random_seed"])
+
+    def _find_mappers(self):
+        """BinMapper::find_bin_from_column of every column (its sample only)."""
+        import concurrent.futures as cf
+        import os
+
+        kw = self._bin_kwargs()
+
+        def one(j):
+            m, _ = bin_column(self._values[j], want_bins=False, categorical=j in self._cats,
+                              **kw)
+            return m
+
+        with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4)) as ex:
+            return list(ex.map(one, range(self.num_features)))
+
+    @property
+    def bins(self):
+        """Feature-major bins [num_features, num_data]. For a dataset built from raw
+        values these are computed on the host (value_to_bin per value) on first use."""
+        if self._bins is None:
+            kw = self._bin_kwargs()
+            cols = []
+            for j in range(self.num_features):
+                _, b = bin_column(self._values[j], categorical=j in self._cats, **kw)
+                cols.append(b)
+            wide = any(m["num_bin"] > 256 for m in self.mappers)
+            self._bins = np.ascontiguousarray(
+                np.stack(cols).astype(np.uint32 if wide else np.uint8))
+        return self._bins
+
+    def device_bins(self):
+        """The device's row-major bin matrix, read back as feature-major [F, N] u8."""
+        h = self.construct()
+        stride = (self.num_features + 15) // 16 * 16
+        out = np.empty((self.num_data, stride), dtype=np.uint8)
+        C.check(C.lib().lgbm_b200_dataset_copy_bins(h, C.ptr(out)))
+        return np.ascontiguousarray(out[:, : self.num_features].T)
 
     def set_group(self, group):
         """Query sizes (or None); stored as query boundaries (prefix sums)."""
@@ -176,13 +221,33 @@ class Dataset:
                 metas[f] = C.FeatureMeta(int(m["num_bin"]), int(m["default_bin"]),
                                          int(m["most_freq_bin"]), int(m.get("missing_type", 0)),
                                          int(m.get("bin_type", 0)))
-            cols = (ctypes.c_void_p * self.num_features)(
-                *[self.bins[f].ctypes.data for f in range(self.num_features)])
             h = ctypes.c_void_p()
-            C.check(C.lib().lgbm_b200_dataset_create(
-                int(self.params.get("device", 0)), cols, self.bins.dtype.itemsize,
-                self.num_data, self.num_features, ctypes.cast(metas, ctypes.c_void_p),
-                ctypes.byref(h)))
+            dev = int(self.params.get("device", 0))
+            if self._values is not None and self._bins is None:
+                V = self._values
+                cols = (ctypes.c_void_p * self.num_features)(
+                    *[V[f].ctypes.data for f in range(self.num_features)])
+                keep = []
+                ups = (ctypes.c_void_p * self.num_features)()
+                b2c = (ctypes.c_void_p * self.num_features)()
+                for f, m in enumerate(self.mappers):
+                    if m.get("bin_type", 0) == 1:
+                        a = np.ascontiguousarray(m["bin_to_category"], dtype=np.int32)
+                        b2c[f] = a.ctypes.data
+                    else:
+                        a = np.ascontiguousarray(m["upper"], dtype=np.float64)
+                        ups[f] = a.ctypes.data
+                    keep.append(a)
+                C.check(C.lib().lgbm_b200_dataset_create_from_values(
+                    dev, cols, V.dtype.itemsize, self.num_data, self.num_features,
+                    ctypes.cast(metas, ctypes.c_void_p), ups, b2c, ctypes.byref(h)))
+            else:
+                B = self.bins
+                cols = (ctypes.c_void_p * self.num_features)(
+                    *[B[f].ctypes.data for f in range(self.num_features)])
+                C.check(C.lib().lgbm_b200_dataset_create(
+                    dev, cols, B.dtype.itemsize, self.num_data, self.num_features,
+                    ctypes.cast(metas, ctypes.c_void_p), ctypes.byref(h)))
             self._handle = h
         return self._handle
 

@@ -141,6 +141,9 @@ _SIGS = {
     "lgbm_b200_comm_create": ([_i32, _i32, _i32, _P, _P], ctypes.c_int),
     "lgbm_b200_comm_destroy": ([_P], ctypes.c_int),
     "lgbm_b200_booster_create_distributed": ([_P, _P, _P, _P, _P], ctypes.c_int),
+    "lgbm_b200_dataset_create_from_values": ([_i32, _P, _i32, _i64, _i32, _P, _P, _P, _P],
+                                             ctypes.c_int),
+    "lgbm_b200_dataset_copy_bins": ([_P, _P], ctypes.c_int),
     "lgbm_b200_predictor_create": ([_i32, _P, _P], ctypes.c_int),
     "lgbm_b200_predictor_destroy": ([_P], ctypes.c_int),
     "lgbm_b200_predict": ([_P, _P, _i64, _i32, _P], ctypes.c_int),

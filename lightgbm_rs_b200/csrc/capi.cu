@@ -1057,9 +1057,17 @@ int lgbm_b200_subtract_histograms(const double* parent, const double* child, int
   return LGBM_B200_OK;
 }
 
-int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t bin_width,
-                             int64_t num_data, int32_t num_features,
-                             const lgbm_b200_feature_meta* meta, lgbm_b200_dataset** out) {
+}  // extern "C"
+
+namespace {
+
+// Builds the device dataset: feature-major host columns go up in row chunks and
+// k_bin_rows writes the row-major u8 matrix (pre-binned columns are range-checked on
+// the device; raw values are binned with the given mappers).
+int dataset_build(int32_t device, const void* const* columns, int kind, int64_t num_data,
+                  int32_t num_features, const lgbm_b200_feature_meta* meta,
+                  const double* const* upper_bounds, const int32_t* const* bin_to_category,
+                  lgbm_b200_dataset** out) {
   if (!out || !meta || (num_features > 0 && !columns))
     return fail(LGBM_B200_INVALID_ARGUMENT, "dataset_create: null argument");
   *out = nullptr;
@@ -1068,9 +1076,9 @@ int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t
   if (num_data > (int64_t)INT32_MAX - 1)
     return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "num_data %lld exceeds 2^31-1",
                 (long long)num_data);
-  if (bin_width != 1 && bin_width != 2 && bin_width != 4)
-    return fail(LGBM_B200_INVALID_ARGUMENT, "bin_width must be 1, 2 or 4");
+  const bool values = kind == kBinRowsF32 || kind == kBinRowsF64;
   for (int f = 0; f < num_features; ++f) {
+    if (!columns[f]) return fail(LGBM_B200_INVALID_ARGUMENT, "feature %d: null column", f);
     if (meta[f].num_bin <= 0 || meta[f].num_bin > kMaxBins)
       return fail(LGBM_B200_CAPABILITY_UNAVAILABLE,
                   "feature %d: num_bin %d outside 1..256 (u8 bin matrix)", f, meta[f].num_bin);
@@ -1079,6 +1087,10 @@ int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t
     if (meta[f].bin_type != 0 && meta[f].bin_type != 1)
       return fail(LGBM_B200_INVALID_ARGUMENT, "feature %d: bin_type %d is not 0 or 1", f,
                   meta[f].bin_type);
+    if (values && meta[f].bin_type == 0 && (!upper_bounds || !upper_bounds[f]))
+      return fail(LGBM_B200_INVALID_ARGUMENT, "feature %d: no bin upper bounds", f);
+    if (values && meta[f].bin_type == 1 && (!bin_to_category || !bin_to_category[f]))
+      return fail(LGBM_B200_INVALID_ARGUMENT, "feature %d: no bin_to_category", f);
   }
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
@@ -1094,6 +1106,10 @@ int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t
   ds->num_features = num_features;
   ds->stride = ((num_features + 15) / 16) * 16;
   int32_t bin_off = 0;
+  std::vector<DevBinFeature> bf(num_features);
+  std::vector<double> upper;
+  std::vector<int32_t> cat_keys;
+  std::vector<uint8_t> cat_bins;
   for (int f = 0; f < num_features; ++f) {
     DevFeature d = make_feature(meta[f].num_bin, meta[f].default_bin, meta[f].most_freq_bin,
                                 meta[f].missing_type);
@@ -1102,38 +1118,122 @@ int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t
     d.slot_off = 2 * bin_off;
     bin_off += meta[f].num_bin;
     ds->feats.push_back(d);
+    DevBinFeature& b = bf[f];
+    b.num_bin = meta[f].num_bin;
+    b.missing_type = meta[f].missing_type;
+    b.bin_type = meta[f].bin_type;
+    b.n_cat = 0;
+    if (values && b.bin_type == 0) {
+      b.off = (int64_t)upper.size();
+      upper.insert(upper.end(), upper_bounds[f], upper_bounds[f] + b.num_bin);
+    } else if (values) {
+      // ascending categories of bins 1.. (bin 0 is the dummy bin of NaN / negatives)
+      std::vector<std::pair<int32_t, uint8_t>> kv;
+      for (int32_t k = 0; k < b.num_bin; ++k)
+        if (bin_to_category[f][k] >= 0) kv.emplace_back(bin_to_category[f][k], (uint8_t)k);
+      std::sort(kv.begin(), kv.end());
+      b.off = (int64_t)cat_keys.size();
+      b.n_cat = (int32_t)kv.size();
+      for (auto& e : kv) {
+        cat_keys.push_back(e.first);
+        cat_bins.push_back(e.second);
+      }
+    } else {
+      b.off = 0;
+    }
   }
   ds->total_bins = bin_off;
-  // bin-range gate + transpose to row-major u8, in row chunks
-  const int64_t chunk = 1 << 20;
-  std::vector<uint8_t> host((size_t)std::min(chunk, num_data) * ds->stride);
   CUDA_TRY(ds->bins.alloc((size_t)num_data * ds->stride));
+  cudaStream_t st = nullptr;
+  CUDA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  struct StreamGuard {
+    cudaStream_t s;
+    ~StreamGuard() { cudaStreamDestroy(s); }
+  } sg{st};
+  DevBuf<DevBinFeature> d_bf;
+  DevBuf<double> d_upper;
+  DevBuf<int32_t> d_keys;
+  DevBuf<uint8_t> d_cbins;
+  DevBuf<unsigned long long> d_bad;
+  CUDA_TRY(d_bf.alloc(num_features));
+  CUDA_TRY(cudaMemcpy(d_bf.p, bf.data(), num_features * sizeof(DevBinFeature),
+                      cudaMemcpyHostToDevice));
+  CUDA_TRY(d_upper.alloc(std::max<size_t>(upper.size(), 1)));
+  if (!upper.empty())
+    CUDA_TRY(cudaMemcpy(d_upper.p, upper.data(), upper.size() * 8, cudaMemcpyHostToDevice));
+  CUDA_TRY(d_keys.alloc(std::max<size_t>(cat_keys.size(), 1)));
+  CUDA_TRY(d_cbins.alloc(std::max<size_t>(cat_bins.size(), 1)));
+  if (!cat_keys.empty()) {
+    CUDA_TRY(cudaMemcpy(d_keys.p, cat_keys.data(), cat_keys.size() * 4, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(d_cbins.p, cat_bins.data(), cat_bins.size(), cudaMemcpyHostToDevice));
+  }
+  CUDA_TRY(d_bad.alloc(1));
+  CUDA_TRY(cudaMemset(d_bad.p, 0xff, 8));
+  BinRowsDev br{d_bf.p, num_features, ds->stride, d_upper.p, d_keys.p, d_cbins.p, d_bad.p};
+  const int elem = kind == kBinRowsF32 ? 4 : kind;
+  const int64_t chunk = std::max<int64_t>(
+      1, std::min<int64_t>(num_data, (256ll << 20) / ((int64_t)num_features * elem)));
+  DevBuf<uint8_t> staging;
+  CUDA_TRY(staging.alloc((size_t)chunk * num_features * elem));
   for (int64_t r0 = 0; r0 < num_data; r0 += chunk) {
-    const int64_t r1 = std::min(num_data, r0 + chunk);
-    std::fill(host.begin(), host.end(), 0);
-    for (int f = 0; f < num_features; ++f) {
-      const uint32_t nb = (uint32_t)meta[f].num_bin;
-      for (int64_t r = r0; r < r1; ++r) {
-        uint32_t b;
-        if (bin_width == 1)
-          b = ((const uint8_t*)columns[f])[r];
-        else if (bin_width == 2)
-          b = ((const uint16_t*)columns[f])[r];
-        else
-          b = ((const uint32_t*)columns[f])[r];
-        if (b >= nb)
-          return fail(LGBM_B200_BIN_OUT_OF_RANGE,
-                      "feature %d row %lld: bin %u >= num_bin %u", f, (long long)r, b, nb);
-        host[(size_t)(r - r0) * ds->stride + f] = (uint8_t)b;
-      }
-    }
-    CUDA_TRY(cudaMemcpy(ds->bins.p + (size_t)r0 * ds->stride, host.data(),
-                        (size_t)(r1 - r0) * ds->stride, cudaMemcpyHostToDevice));
+    const int64_t n = std::min(chunk, num_data - r0);
+    for (int f = 0; f < num_features; ++f)
+      CUDA_TRY(cudaMemcpyAsync(staging.p + (size_t)f * chunk * elem,
+                               (const uint8_t*)columns[f] + (size_t)r0 * elem, (size_t)n * elem,
+                               cudaMemcpyHostToDevice, st));
+    launch_bin_rows(br, kind, staging.p, chunk, n, r0, ds->bins.p + (size_t)r0 * ds->stride, st);
+    CUDA_TRY(cudaGetLastError());
+  }
+  CUDA_TRY(cudaStreamSynchronize(st));
+  unsigned long long bad = 0;
+  CUDA_TRY(cudaMemcpy(&bad, d_bad.p, 8, cudaMemcpyDeviceToHost));
+  if (bad != ~0ull) {
+    const int64_t row = (int64_t)(bad / (unsigned long long)num_features);
+    const int f = (int)(bad % (unsigned long long)num_features);
+    uint32_t b = kind == kBinRowsU8    ? ((const uint8_t*)columns[f])[row]
+                 : kind == kBinRowsU16 ? ((const uint16_t*)columns[f])[row]
+                                       : ((const uint32_t*)columns[f])[row];
+    return fail(LGBM_B200_BIN_OUT_OF_RANGE, "feature %d row %lld: bin %u >= num_bin %d", f,
+                (long long)row, b, meta[f].num_bin);
   }
   CUDA_TRY(ds->d_feats.alloc(num_features));
   CUDA_TRY(cudaMemcpy(ds->d_feats.p, ds->feats.data(), num_features * sizeof(DevFeature),
                       cudaMemcpyHostToDevice));
   *out = ds.release();
+  return LGBM_B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lgbm_b200_dataset_create(int32_t device, const void* const* columns, int32_t bin_width,
+                             int64_t num_data, int32_t num_features,
+                             const lgbm_b200_feature_meta* meta, lgbm_b200_dataset** out) {
+  if (bin_width != 1 && bin_width != 2 && bin_width != 4)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "bin_width must be 1, 2 or 4");
+  return dataset_build(device, columns, bin_width, num_data, num_features, meta, nullptr,
+                       nullptr, out);
+}
+
+int lgbm_b200_dataset_create_from_values(int32_t device, const void* const* columns,
+                                         int32_t value_width, int64_t num_data,
+                                         int32_t num_features,
+                                         const lgbm_b200_feature_meta* meta,
+                                         const double* const* upper_bounds,
+                                         const int32_t* const* bin_to_category,
+                                         lgbm_b200_dataset** out) {
+  if (value_width != 4 && value_width != 8)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "value_width must be 4 (f32) or 8 (f64)");
+  return dataset_build(device, columns, value_width == 4 ? kBinRowsF32 : kBinRowsF64,
+                       num_data, num_features, meta, upper_bounds, bin_to_category, out);
+}
+
+int lgbm_b200_dataset_copy_bins(const lgbm_b200_dataset* ds, uint8_t* out) {
+  if (!ds || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "dataset_copy_bins: null argument");
+  DeviceGuard g(ds->device);
+  CUDA_TRY(cudaMemcpy(out, ds->bins.p, (size_t)ds->num_data * ds->stride,
+                      cudaMemcpyDeviceToHost));
   return LGBM_B200_OK;
 }
 

@@ -179,6 +179,28 @@ struct FinishDev {
 void launch_finish_iteration(const GrowDev& d, const FinishDev& f, cudaStream_t st,
                              LaunchProfiler* prof = nullptr);
 
+// Row-major bin matrix from feature-major columns (bin_rows.cu).
+struct DevBinFeature {
+  int32_t num_bin;
+  int32_t missing_type;
+  int32_t bin_type;  // 0 numerical, 1 categorical
+  int32_t n_cat;     // categorical: categories in cat_keys
+  int64_t off;       // first bound in `upper` (numerical) or key in `cat_keys` (categorical)
+};
+struct BinRowsDev {
+  const DevBinFeature* feats;
+  int32_t num_features;
+  int32_t stride;                   // bytes per row (a multiple of 16)
+  const double* upper;              // numerical bin upper bounds, concatenated
+  const int32_t* cat_keys;          // categorical: ascending categories, concatenated
+  const uint8_t* cat_bins;          // their bins
+  unsigned long long* first_bad;    // pre-binned input: smallest row * F + feature out of range
+};
+enum BinRowsKind { kBinRowsU8 = 1, kBinRowsU16 = 2, kBinRowsU32 = 4, kBinRowsF32 = 5,
+                   kBinRowsF64 = 8 };
+void launch_bin_rows(const BinRowsDev& d, int kind, const void* cols, int64_t col_stride,
+                     int64_t n, int64_t row0, uint8_t* out, cudaStream_t st);
+
 // Batch prediction (predict.cu). One internal node of a flattened ensemble.
 struct PredNode {
   double threshold;  // numerical threshold
