@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--workload", default="c1", choices=sorted(WORKLOADS))
     ap.add_argument("--rows", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--measure", default="boosting", choices=["boosting", "binning"],
+                    help="binning: time Dataset construction from raw C1 values (device "
+                         "value_to_bin) against host value_to_bin on all cores")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     if args.rows is None:
@@ -465,10 +468,62 @@ def run_ours(args):
         print(json.dumps(out), flush=True)
 
 
+def run_binning(args):
+    """Device binning of the C1 raw matrix (f32, feature-major upload + value_to_bin into
+    the row-major u8 matrix) against the host value_to_bin of the same mappers on all
+    cores. Bin boundaries come from each column's 200k-row sample on the host in both."""
+    import concurrent.futures as cf
+
+    import lightgbm_rs_b200 as lgb
+    from lightgbm_rs_b200 import build as libbuild
+    from lightgbm_rs_b200 import synthetic
+
+    libbuild.build()
+    X, y = synthetic.binary_c0(num_data=args.rows, num_features=28, seed=0)
+    p = {"max_bin": 255, "min_data_in_leaf": 100}
+    t0 = time.perf_counter()
+    ds = lgb.Dataset(X, y, p)  # mappers from the samples (host)
+    t_map = time.perf_counter() - t0
+    dev_s = []
+    for _ in range(max(args.steps, 1)):
+        ds._handle = None
+        t0 = time.perf_counter()
+        ds.construct()
+        dev_s.append(time.perf_counter() - t0)
+        lgb._lib.lib().lgbm_b200_dataset_destroy(ds._handle)
+        ds._handle = None
+    ds.construct()
+    dev_bins = ds.device_bins()
+    nt = os.cpu_count() or 1
+    kw = ds._bin_kwargs()
+    t0 = time.perf_counter()
+
+    def one(j):
+        return lgb.bin_column(ds._values[j], **kw)[1]
+
+    with cf.ThreadPoolExecutor(max_workers=nt) as ex:
+        host = list(ex.map(one, range(ds.num_features)))
+    t_host = time.perf_counter() - t0
+    same = all(np.array_equal(dev_bins[j], host[j]) for j in range(ds.num_features))
+    vals = args.rows * 28
+    dev = min(dev_s)
+    out = {"metric": "binning_values_per_sec", "value": vals / dev, "unit": "values/s",
+           "impl": "ours", "data": "synthetic", "dtype": "f32",
+           "config": {"workload": f"C1 raw values {args.rows}x28 f32, max_bin=255"},
+           "device_s": dev, "host_value_to_bin_s": t_host, "host_threads": nt,
+           "host_note": "host time includes each column's find_bin on its sample",
+           "mapper_s": t_map, "bins_identical": bool(same),
+           "h2d_bytes": vals * 4}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse()
     if args.warmup < 3:
         args.warmup = 3
+    if args.measure == "binning":
+        run_binning(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
