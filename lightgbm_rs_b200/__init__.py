@@ -509,6 +509,18 @@ class Booster:
                 {"launches": int(cnt[0]), "builds": int(cnt[1]), "rows_built": int(cnt[2]),
                  "splits": int(cnt[3]), "rows_parted": int(cnt[4]), "fused": bool(cnt[5])})
 
+    def profile_launches(self):
+        """(kernel class name, device ms) of every span timed by the last
+        profile_iteration, in launch order."""
+        n = C._i32(0)
+        C.check(C.lib().lgbm_b200_booster_profile_launches(self._handle, 0, None, None,
+                                                           ctypes.byref(n)))
+        cls = np.zeros(n.value, dtype=np.int32)
+        ms = np.zeros(n.value, dtype=np.float32)
+        C.check(C.lib().lgbm_b200_booster_profile_launches(self._handle, n.value, C.ptr(cls),
+                                                           C.ptr(ms), ctypes.byref(n)))
+        return [(self.KERNEL_CLASSES[c], float(m)) for c, m in zip(cls, ms)]
+
     def predict(self, data, raw_score=False):
         """Predictions for raw feature rows [n, num_features] on the device: the trees'
         leaf values summed in tree order (the boost-from-average score is in the first

@@ -574,6 +574,7 @@ struct lgbm_b200_booster {
   cudaGraphExec_t graph_exec = nullptr;
   cudaGraph_t graph = nullptr;
   float last_ms = 0.f;
+  std::vector<std::pair<int32_t, float>> last_profile;  // (kernel class, ms) per launch
   lgbm_b200_comm* comm = nullptr;  // data-parallel job (null: one device)
   const DeviceComm* dcomm() const { return comm ? &comm->dev : nullptr; }
 
@@ -1793,6 +1794,19 @@ int lgbm_b200_booster_phase_ms(const lgbm_b200_booster* b, double* out3) {
   return LGBM_B200_OK;
 }
 
+int lgbm_b200_booster_profile_launches(const lgbm_b200_booster* b, int32_t cap,
+                                       int32_t* class_out, float* ms_out, int32_t* n_out) {
+  if (!b || !n_out || (cap > 0 && (!class_out || !ms_out)))
+    return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
+  const int32_t n = (int32_t)b->last_profile.size();
+  *n_out = n;
+  for (int32_t i = 0; i < std::min(n, cap); ++i) {
+    class_out[i] = b->last_profile[i].first;
+    ms_out[i] = b->last_profile[i].second;
+  }
+  return LGBM_B200_OK;
+}
+
 int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
                                         int64_t* counts_out) {
   if (!b || !ms_out || !counts_out) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
@@ -1824,10 +1838,12 @@ int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
   }
   for (int k = 0; k < KC_COUNT; ++k) ms_out[k] = 0.0;
   int64_t launches = 0;
+  b->last_profile.clear();
   for (int i = 0; i < prof.n; ++i) {
     float ms = 0.f;
     cudaEventElapsedTime(&ms, prof.ev[i][0], prof.ev[i][1]);
     ms_out[cls[i]] += ms;
+    b->last_profile.emplace_back(cls[i], ms);
     launches += (cls[i] == KC_GRAD) ? 4 : (cls[i] == KC_FINISH ? 2 : 1);
   }
   for (auto& e : evs) cudaEventDestroy(e);

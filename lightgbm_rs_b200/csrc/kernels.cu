@@ -1488,27 +1488,44 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
   // one histogram cell per thread (2*num_bin <= 512 cells)
   const bool mine = tid < 2 * nb;
   const size_t cell = 2 * (size_t)ft.bin_off + tid;
-  // the accumulated child (its left or right rows, all devices summed); read it and
-  // clear it for the next partition
-  long long bv = 0;
+  // Every global read of this feature's cells is issued here, before any store or branch
+  // on loaded data, so their round trips overlap: the accumulated child (its left or
+  // right rows, all devices summed; per-tile partials are integers, summed in any order),
+  // the parent's integer cells and the larger child's parent slot.
+  const int32_t S = P.S, Lg = P.Lg;
+  long long bv = 0, pv = 0;
+  double parent = 0.0;
   if (mine) {
-    if (P.priv_tiles > 0) {
-      for (int t = 0; t < P.priv_tiles; ++t) bv += __ldcg(&d.partials[(size_t)t * d.raw_len + cell]);
+    const int nt = P.priv_tiles;
+    if (nt > 0) {
+      const long long* pp = d.partials + cell;
+      const size_t rl = (size_t)d.raw_len;
+      long long a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+      int t = 0;
+      for (; t + 4 <= nt; t += 4) {
+        a0 += __ldcg(pp + (size_t)t * rl);
+        a1 += __ldcg(pp + (size_t)(t + 1) * rl);
+        a2 += __ldcg(pp + (size_t)(t + 2) * rl);
+        a3 += __ldcg(pp + (size_t)(t + 3) * rl);
+      }
+      for (; t < nt; ++t) a0 += __ldcg(pp + (size_t)t * rl);
+      bv = (a0 + a1) + (a2 + a3);
     } else {
-      bv = d.raw[cell];
-      d.raw[cell] = 0;
+      bv = __ldcg(d.raw + cell);
     }
+    if (P.live && P.applied) pv = __ldcg(d.rawpool + (size_t)P.leaf * d.raw_len + cell);
+    if (P.live && Lg >= 0) parent = d.pool[(size_t)P.lslot * d.slot_len + ft.slot_off + tid];
   }
+  const bool used_f =
+      !P.live || !P.use_sub || d.splittable[(size_t)P.mask_leaf * d.F + f] != 0;
+  // clear the accumulator for the next partition
+  if (mine && P.priv_tiles == 0) d.raw[cell] = 0;
   if (P.live) {
-    const int32_t S = P.S, Lg = P.Lg;
-    const bool used = !P.use_sub || d.splittable[(size_t)P.mask_leaf * d.F + f] != 0;
+    const bool used = used_f;
     if (used) {
       const DevGhParams& p = *d.ghp;
       const DevLeafSplits lss = P.lsS;
       const bool buildable = leaf_buildable(lss);
-      double* pl = d.pool + (size_t)P.lslot * d.slot_len + ft.slot_off;
-      double parent = 0.0;
-      if (mine && Lg >= 0) parent = pl[tid];
       double v = 0.0;
       if (mine) {
         // Integer histograms of both children: the accumulated side as is, the other as
@@ -1516,7 +1533,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
         long long sv = bv;
         if (P.applied) {
           long long* pr = d.rawpool + (size_t)P.leaf * d.raw_len + cell;
-          const long long ov = *pr - bv;
+          const long long ov = pv - bv;
           const bool bl = P.c.build_left != 0;
           const long long lv = bl ? bv : ov;
           const long long rv = bl ? ov : bv;
@@ -1615,7 +1632,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
         d.pool[(size_t)P.sslot * d.slot_len + ft.slot_off + tid] = sv;
         if (Lg >= 0) {
           const double lv = parent - sv;
-          pl[tid] = lv;
+          d.pool[(size_t)P.lslot * d.slot_len + ft.slot_off + tid] = lv;
           sm.hist[1][tid] = lv;
         }
       }
