@@ -2032,6 +2032,13 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
   // the first tile ticket is taken before anything else is read: its round trip overlaps
   // the reads below (a ticket taken when there is nothing to do is harmless)
   if (tid == 0) s_tile = (int32_t)atomicAdd(&d.ctrl->part_ticket, 1u);
+  // the dataset's feature table does not depend on the split: read it first
+  if (build)
+    for (int fl = tid; fl < d.F; fl += kFpThreads) {
+      const DevFeature g = d.feat[fl];
+      s_nb[fl] = g.num_bin;
+      s_boff[fl] = g.bin_off;
+    }
   GrowCtrl* c = d.ctrl;
   if (c->done || !c->pending) return;
   const int32_t leaf = c->split_leaf;
@@ -2051,6 +2058,13 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
   const bool is_cat = (ft.flags & kFeatCategorical) != 0;
   const int nf = d.F;
   const int cap = nf << SHIFT;
+  // the children keep the features their parent could split (learner.rs:2003-2020); the
+  // mask is read with the leaf's range
+  if (build && tid < 128) {
+    const uint8_t* ps = d.splittable + (size_t)leaf * d.F;
+    const uint32_t m = __ballot_sync(0xffffffffu, tid < nf && ps[tid] != 0);
+    if ((tid & 31) == 0) s_mask[tid >> 5] = m;
+  }
   // few tiles: every CTA takes exactly one tile and stores its own partial histogram
   // (plain stores, summed by the next control step) instead of adding it atomically
   const bool priv = build && ntiles <= d.private_tiles;
@@ -2074,17 +2088,6 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
     for (int i = tid; i < (cap + 3) / 4; i += kFpThreads) {
       h4[i] = z;
       c4[i] = z;
-    }
-    // the children keep the features their parent could split (learner.rs:2003-2020)
-    const uint8_t* ps = d.splittable + (size_t)leaf * d.F;
-    for (int fl = tid; fl < nf; fl += kFpThreads) {
-      const DevFeature g = d.feat[fl];
-      s_nb[fl] = g.num_bin;
-      s_boff[fl] = g.bin_off;
-    }
-    if (tid < 128) {
-      const uint32_t m = __ballot_sync(0xffffffffu, tid < nf && ps[tid] != 0);
-      if ((tid & 31) == 0) s_mask[tid >> 5] = m;
     }
   }
   __syncthreads();
