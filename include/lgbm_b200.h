@@ -372,6 +372,11 @@ int lgbm_b200_booster_phase_ms(const lgbm_b200_booster* b, double* out3);
  * builds the child histogram}. The iteration counts as a normal boosting iteration. */
 int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
                                         int64_t* counts_out);
+/* The launches timed by the last lgbm_b200_booster_profile_iteration, in launch order:
+ * kernel class (the ms_out order of that call) and device ms of each timed span; *n_out
+ * receives the count, at most cap entries are written. */
+int lgbm_b200_booster_profile_launches(const lgbm_b200_booster* b, int32_t cap,
+                                       int32_t* class_out, float* ms_out, int32_t* n_out);
 
 /* ---------------------------------------------------- data-parallel training */
 
