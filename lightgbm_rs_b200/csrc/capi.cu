@@ -1672,7 +1672,9 @@ int lgbm_b200_booster_create_distributed(lgbm_b200_dataset* ds, const float* lab
 
 int lgbm_b200_booster_destroy(lgbm_b200_booster* b) {
   if (b) {
-    DeviceGuard g(b->ds->device);
+    // the dataset may already be gone (a garbage collector frees handles in any order):
+    // only the booster's own state is touched here
+    DeviceGuard g(b->learner ? b->learner->device : 0);
     b->destroy_graph();
     if (b->learner && b->learner->stream) cudaStreamDestroy(b->learner->stream);
     delete b;
