@@ -105,8 +105,8 @@ struct DevGhParams {
   double inv_hess_scale;
   uint32_t max_abs_g_bits;  // running max |g| (f32 bits, non-negative floats order as ints)
   uint32_t max_abs_h_bits;
-  uint32_t min_h_key;       // ordered-int keys for the constant-hessian check
-  uint32_t max_h_key;
+  uint32_t min_h_key_inv;   // ordered-int keys for the constant-hessian check: the minimum
+  uint32_t max_h_key;       // is kept complemented, so all four reduce with one max
   long long root_g;         // root sums in accumulator units
   long long root_h;
   long long lut_g[256];     // QLUT: per-level accumulator value, index q + 128

@@ -2,6 +2,7 @@
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
+#include <cstddef>
 
 #include "kernels.cuh"
 
@@ -10,6 +11,8 @@ namespace lgbm_b200 {
 namespace {
 
 constexpr int kObjThreads = 256;
+static_assert(offsetof(DevGhParams, max_h_key) == offsetof(DevGhParams, max_abs_g_bits) + 12,
+              "the four gradient maxima are reduced over devices as one array");
 
 __device__ __forceinline__ uint32_t f32_key(float x) {
   x = x + 0.0f;  // -0.0 -> +0.0: the reference compares hessians with ==
@@ -42,7 +45,7 @@ __global__ void k_gh_reset(DevGhParams* p, const int32_t* stopped) {
   if (stopped && *stopped) return;
   p->max_abs_g_bits = 0u;
   p->max_abs_h_bits = 0u;
-  p->min_h_key = 0xffffffffu;
+  p->min_h_key_inv = 0u;
   p->max_h_key = 0u;
   p->root_g = 0;
   p->root_h = 0;
@@ -71,7 +74,7 @@ __global__ void __launch_bounds__(kObjThreads) k_grad_pass1(ObjDev o) {
   if ((threadIdx.x & 31) == 0) {
     atomicMax(&o.ghp->max_abs_g_bits, mg);
     atomicMax(&o.ghp->max_abs_h_bits, mh);
-    atomicMin(&o.ghp->min_h_key, kmin);
+    atomicMax(&o.ghp->min_h_key_inv, ~kmin);
     atomicMax(&o.ghp->max_h_key, kmax);
   }
 }
@@ -257,7 +260,7 @@ __global__ void __launch_bounds__(kObjThreads) k_lambdarank(ObjDev o) {
   if (lane == 0) {
     atomicMax(&o.ghp->max_abs_g_bits, mg);
     atomicMax(&o.ghp->max_abs_h_bits, mh);
-    atomicMin(&o.ghp->min_h_key, kmin);
+    atomicMax(&o.ghp->min_h_key_inv, ~kmin);
     atomicMax(&o.ghp->max_h_key, kmax);
   }
 }
@@ -320,7 +323,7 @@ __global__ void k_gh_scales(ObjDev o) {
     return;
   }
   const int bins = o.num_quant_bins;
-  const bool is_const = p->min_h_key == p->max_h_key;
+  const bool is_const = ~p->min_h_key_inv == p->max_h_key;
   const double half_bins = (double)(bins / 2);
   const double gs = max_g / half_bins;
   const double hs = is_const ? max_h : max_h / (double)bins;
@@ -572,9 +575,8 @@ void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof,
     k_grad_pass1<<<grid, kObjThreads, 0, st>>>(o);
   }
   if (comm) {
-    comm->max_u32(comm->ctx, &o.ghp->max_abs_g_bits, 2, st);
-    comm->min_u32(comm->ctx, &o.ghp->min_h_key, 1, st);
-    comm->max_u32(comm->ctx, &o.ghp->max_h_key, 1, st);
+    // max |g|, max |h|, ~min key, max key: one max over four words
+    comm->max_u32(comm->ctx, &o.ghp->max_abs_g_bits, 4, st);
   }
   k_gh_scales<<<1, 1, 0, st>>>(o);
   if (o.gh_mode == GH_FLOAT)
