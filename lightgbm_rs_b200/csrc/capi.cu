@@ -217,6 +217,7 @@ struct lgbm_b200_learner {
   DevBuf<unsigned long long> part_status;
   DevBuf<double> pool;
   DevBuf<long long> raw;
+  DevBuf<long long*> xtab;  // one-device exchange table: {raw}
   DevBuf<long long> rawpool;
   DevBuf<long long> partials;
   DevBuf<DevSplitInfo> scan_out;
@@ -386,6 +387,13 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.max_tiles = max_tiles;
   d.pool = pool.p;
   d.raw = raw.p;
+  // one device: the accumulator is its own one-rank exchange
+  CUDA_TRY(xtab.alloc(1));
+  CUDA_TRY(cudaMemcpy(xtab.p, &raw.p, sizeof(long long*), cudaMemcpyHostToDevice));
+  d.xranks = 1;
+  d.xrank = 0;
+  d.xpar = 0;
+  d.xbuf = xtab.p;
   d.rawpool = rawpool.p;
   d.partials = partials.p;
   d.private_tiles = kPrivateTiles;
@@ -585,7 +593,15 @@ struct lgbm_b200_booster {
     graph_exec = nullptr;
     graph = nullptr;
   }
-  ~lgbm_b200_booster() { destroy_graph(); }
+  // peer-memory exchange of the accumulated child (data-parallel, one node)
+  DevBuf<unsigned long long> xmem;  // [2][raw_len + 2] accumulators | flags | count
+  DevBuf<void*> xptrs;              // per-rank accumulator and flag pointers
+  std::vector<void*> xpeer;         // the other ranks' regions, opened by IPC handle
+  ~lgbm_b200_booster() {
+    destroy_graph();
+    for (void* p : xpeer)
+      if (p) cudaIpcCloseMemHandle(p);
+  }
 };
 
 int lgbm_b200_booster::ensure_capacity(int32_t need) {
@@ -1473,6 +1489,119 @@ int rank_tables(const lgbm_b200_train_config& cfg, const float* labels, int64_t 
   return LGBM_B200_OK;
 }
 
+// The accumulated child crosses between the ranks over peer memory instead of an NCCL
+// all-reduce when every rank can map every other rank's exchange region (CUDA IPC
+// handles, swapped over the NCCL communicator). All ranks agree on the outcome, so either
+// all exchange over peer memory or all keep NCCL. LGBM_B200_PEER_EXCHANGE=0 keeps NCCL;
+// LGBM_B200_PEER_WAIT_MS sets the wait limit (default 2000 ms).
+int setup_peer_exchange(lgbm_b200_booster* b, lgbm_b200_comm* comm) {
+  const int R = comm->nranks;
+  const char* env = std::getenv("LGBM_B200_PEER_EXCHANGE");
+  const bool want = R >= 2 && R <= kMaxXRanks && !(env && std::strcmp(env, "0") == 0);
+  GrowDev& d = b->learner->d;
+  if (!want) return LGBM_B200_OK;
+  cudaStream_t st = b->learner->stream;
+  const size_t xs = (size_t)d.raw_len + 2;
+  const size_t words = 2 * xs + kMaxXRanks + 1;
+  CUDA_TRY(b->xmem.alloc(words));
+  CUDA_TRY(cudaMemset(b->xmem.p, 0, words * 8));
+  // every rank's IPC handle, in rank order (the all-gather moves 8-byte words)
+  constexpr int kH = (int)sizeof(cudaIpcMemHandle_t);
+  static_assert(kH % 8 == 0, "IPC handles move as 8-byte words");
+  cudaIpcMemHandle_t mine;
+  int ok = cudaIpcGetMemHandle(&mine, b->xmem.p) == cudaSuccess ? 1 : 0;
+  cudaGetLastError();
+  DevBuf<long long> hbuf;
+  CUDA_TRY(hbuf.alloc((size_t)(R + 1) * kH / 8));
+  CUDA_TRY(cudaMemset(hbuf.p, 0, (size_t)(R + 1) * kH));
+  if (ok) CUDA_TRY(cudaMemcpy(hbuf.p + (size_t)R * kH / 8, &mine, kH, cudaMemcpyHostToDevice));
+  ncclResult_t r = nccl().AllGather(hbuf.p + (size_t)R * kH / 8, hbuf.p, kH / 8, ncclInt64,
+                                    comm->comm, st);
+  if (r != ncclSuccess)
+    return fail(LGBM_B200_RUNTIME, "NCCL all-gather failed: %s", nccl().GetErrorString(r));
+  std::vector<cudaIpcMemHandle_t> handles(R);
+  CUDA_TRY(cudaStreamSynchronize(st));
+  CUDA_TRY(cudaMemcpy(handles.data(), hbuf.p, (size_t)R * kH, cudaMemcpyDeviceToHost));
+  std::vector<unsigned long long*> base(R, nullptr);
+  base[comm->rank] = b->xmem.p;
+  for (int q = 0; q < R && ok; ++q) {
+    if (q == comm->rank) continue;
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, handles[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = 0;
+      break;
+    }
+    b->xpeer.push_back(p);
+    base[q] = static_cast<unsigned long long*>(p);
+  }
+  // agree: peer memory only if every rank mapped every region
+  DevBuf<int32_t> okbuf;
+  CUDA_TRY(okbuf.alloc(1));
+  CUDA_TRY(cudaMemcpy(okbuf.p, &ok, 4, cudaMemcpyHostToDevice));
+  r = nccl().AllReduce(okbuf.p, okbuf.p, 1, ncclInt32, ncclMin, comm->comm, st);
+  if (r != ncclSuccess)
+    return fail(LGBM_B200_RUNTIME, "NCCL all-reduce failed: %s", nccl().GetErrorString(r));
+  int all_ok = 0;
+  CUDA_TRY(cudaStreamSynchronize(st));
+  CUDA_TRY(cudaMemcpy(&all_ok, okbuf.p, 4, cudaMemcpyDeviceToHost));
+  if (!all_ok) {
+    for (void* p : b->xpeer) cudaIpcCloseMemHandle(p);
+    b->xpeer.clear();
+    b->xmem.release();
+    return LGBM_B200_OK;
+  }
+  long long wait_ms = 2000;
+  if (const char* w = std::getenv("LGBM_B200_PEER_WAIT_MS")) wait_ms = std::max(1ll, atoll(w));
+  std::vector<void*> ptrs(2 * (size_t)R);
+  for (int q = 0; q < R; ++q) {
+    ptrs[q] = base[q];
+    ptrs[R + q] = base[q] + 2 * xs;
+  }
+  CUDA_TRY(b->xptrs.alloc(ptrs.size()));
+  CUDA_TRY(cudaMemcpy(b->xptrs.p, ptrs.data(), ptrs.size() * sizeof(void*),
+                      cudaMemcpyHostToDevice));
+  d.xranks = R;
+  d.xrank = comm->rank;
+  d.xpar = 0;
+  d.xlocal = reinterpret_cast<long long*>(b->xmem.p);
+  d.xbuf = reinterpret_cast<long long* const*>(b->xptrs.p);
+  d.peer_xflags = reinterpret_cast<unsigned long long* const*>(b->xptrs.p + R);
+  d.xflags = b->xmem.p + 2 * xs;
+  d.xseq = b->xmem.p + 2 * xs + kMaxXRanks;
+  d.xwait_ns = wait_ms * 1000000ll;
+  return LGBM_B200_OK;
+}
+
+// Failure-detection hook for tests (LGBM_B200_PEER_EXCHANGE=silent-peer on a one-device
+// booster): the booster acts as rank 0 of two whose second rank never publishes, because
+// the signal kernel writes that rank's flags into scratch memory. Its first wait runs out
+// after LGBM_B200_PEER_WAIT_MS, training ends with the spin-timeout error bit, and no GPU
+// fault or hang is involved.
+int setup_silent_peer(lgbm_b200_booster* b) {
+  GrowDev& d = b->learner->d;
+  const size_t xs = (size_t)d.raw_len + 2;
+  const size_t words = 2 * xs + 2 * kMaxXRanks + 1;
+  CUDA_TRY(b->xmem.alloc(words));
+  CUDA_TRY(cudaMemset(b->xmem.p, 0, words * 8));
+  long long wait_ms = 2000;
+  if (const char* w = std::getenv("LGBM_B200_PEER_WAIT_MS")) wait_ms = std::max(1ll, atoll(w));
+  void* ptrs[4] = {b->xmem.p, b->xmem.p, b->xmem.p + 2 * xs,
+                   b->xmem.p + 2 * xs + kMaxXRanks + 1};  // rank 1's flags: scratch
+  CUDA_TRY(b->xptrs.alloc(4));
+  CUDA_TRY(cudaMemcpy(b->xptrs.p, ptrs, sizeof(ptrs), cudaMemcpyHostToDevice));
+  d.xranks = 2;
+  d.xrank = 0;
+  d.xpar = 0;
+  d.xlocal = reinterpret_cast<long long*>(b->xmem.p);
+  d.xbuf = reinterpret_cast<long long* const*>(b->xptrs.p);
+  d.peer_xflags = reinterpret_cast<unsigned long long* const*>(b->xptrs.p + 2);
+  d.xflags = b->xmem.p + 2 * xs;
+  d.xseq = b->xmem.p + 2 * xs + kMaxXRanks;
+  d.xwait_ns = wait_ms * 1000000ll;
+  return LGBM_B200_OK;
+}
+
 int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
                         const lgbm_b200_train_config* cfg, lgbm_b200_comm* comm,
                         lgbm_b200_booster** out) {
@@ -1553,7 +1682,17 @@ int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
                    b->ghp.p, b->state.p);
   b->learner->d.n_global = NG;
   // the accumulated child has to be summed over devices in one buffer, between kernels
-  if (comm) b->learner->d.private_tiles = 0;
+  if (comm) {
+    b->learner->d.private_tiles = 0;
+    rc = setup_peer_exchange(b.get(), comm);
+    if (rc) return rc;
+  } else if (const char* px = std::getenv("LGBM_B200_PEER_EXCHANGE")) {
+    if (std::strcmp(px, "silent-peer") == 0) {
+      b->learner->d.private_tiles = 0;
+      rc = setup_silent_peer(b.get());
+      if (rc) return rc;
+    }
+  }
   b->comm = comm;
   ObjDev& o = b->obj;
   o.N = N;
@@ -1853,6 +1992,7 @@ int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
   CUDA_TRY(cudaMemcpy(&c, b->learner->ctrl.p, sizeof(GrowCtrl), cudaMemcpyDeviceToHost));
   if (c.error)
     return fail(LGBM_B200_RUNTIME, "tree grower reported device error bits 0x%x", c.error);
+  if (b->learner->d.xranks > 1) launches += b->learner->L;  // one k_xsignal per producer
   counts_out[0] = launches;
   counts_out[1] = c.num_builds;
   counts_out[2] = c.rows_built;

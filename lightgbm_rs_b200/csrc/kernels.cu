@@ -83,6 +83,75 @@ __device__ __forceinline__ void build_account(const GrowDev& d, int phase, const
   }
 }
 
+// ------------------------------------------------------------------------------------
+// Exchange of the accumulated child over peer memory (GrowDev::xranks > 1).
+// ------------------------------------------------------------------------------------
+
+__device__ __forceinline__ long long ld_relaxed_sys(const long long* p) {
+  long long v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Cell `idx` of the accumulated child: the sum over the ranks' buffers of parity xpar
+// (integers: exact in any order); on one device, the launch's accumulator.
+__device__ __forceinline__ long long raw_sum(const GrowDev& d, size_t idx) {
+  if (d.xranks <= 1) return __ldcg(d.raw + idx);
+  const size_t off = (size_t)d.xpar * ((size_t)d.raw_len + 2) + idx;
+  long long s = 0;
+  for (int r = 0; r < d.xranks; ++r) s += ld_relaxed_sys(d.xbuf[r] + off);
+  return s;
+}
+
+// Waits (thread 0 of a consumer CTA) until every rank has published this rank's current
+// exchange count; false after wait_ns without it, or at once when a wait has already run
+// out (the caller records kErrSpinTimeout).
+__device__ __noinline__ bool x_wait_flags(const uint32_t* error, int xranks,
+                                          const unsigned long long* xflags,
+                                          const unsigned long long* xseq, long long wait_ns) {
+  if (*reinterpret_cast<const volatile uint32_t*>(error) & kErrSpinTimeout) return false;
+  const unsigned long long seq = *reinterpret_cast<const volatile unsigned long long*>(xseq);
+  const unsigned long long t0 = global_ns();
+  for (int r = 0; r < xranks; ++r) {
+    while (ld_acquire_sys(xflags + r) < seq) {
+      if (global_ns() - t0 > (unsigned long long)wait_ns) return false;
+      __nanosleep(64);
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool x_wait(const GrowDev& d) {
+  if (d.xranks <= 1) return true;
+  return x_wait_flags(&d.ctrl->error, d.xranks, d.xflags, d.xseq, d.xwait_ns);
+}
+
+// After a producer kernel: publish the next exchange count into every rank's flags
+// (system-scope release after the producer's completed writes). One warp.
+__global__ void k_xsignal(GrowDev d) {
+  const int lane = threadIdx.x;
+  const unsigned long long seq = *d.xseq + 1;
+  __syncwarp();
+  __threadfence_system();
+  if (lane < d.xranks) {
+    unsigned long long* f = d.peer_xflags[lane] + d.xrank;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(seq) : "memory");
+  }
+  if (lane == 0) *d.xseq = seq;
+}
+
 // Decoding of the raw integer accumulators into f64 histogram cells. For the
 // quantized modes the result equals the reference's f64 fold exactly: every
 // dequantized level is an integer multiple of the ulp of the smallest nonzero
@@ -796,6 +865,10 @@ __global__ void k_tree_init(GrowDev d) {
   const size_t nsp = (size_t)d.L * d.F;
   for (size_t i = gtid; i < nsp; i += gsz) d.splittable[i] = 1;
   for (int i = gtid; i < d.max_tiles; i += gsz) d.part_status[i] = 0ull;
+  // both peer-exchange accumulators start the tree empty (every rank has finished the
+  // previous tree: the gradient step's reductions came in between)
+  if (d.xranks > 1)
+    for (size_t i = gtid; i < 2 * ((size_t)d.raw_len + 2); i += gsz) d.xlocal[i] = 0;
   if (gtid == 0) {
     const uint32_t epoch = c->epoch;
     const uint32_t err = c->error;
@@ -891,7 +964,7 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
     const double old_value = d.t_leaf_value[leaf];
     const int32_t depth = d.t_leaf_depth[leaf];
     const int32_t mt = d.feat[f].missing_type;
-    const long long lcg_raw = d.raw[d.raw_len];
+    const long long lcg_raw = raw_sum(d, (size_t)d.raw_len);
     slot_left = d.slot_of_leaf[leaf];
     const int32_t parent_right = parent >= 0 ? d.t_right[parent] : 0;
     const int32_t lc = c.part_left_total;
@@ -1120,6 +1193,7 @@ __device__ void prep_commit(const GrowDev& d, const Prep& P) {
 // The control step alone: applies the tree's last split.
 __global__ void k_prepare(GrowDev d, int s) {
   if (threadIdx.x != 0) return;
+  if (!x_wait(d)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
   Prep P;
   prep_compute(d, s, P);
   if (d.has_cat)
@@ -1511,7 +1585,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
       for (; t < nt; ++t) a0 += __ldcg(pp + (size_t)t * rl);
       bv = (a0 + a1) + (a2 + a3);
     } else {
-      bv = __ldcg(d.raw + cell);
+      bv = raw_sum(d, cell);
     }
     if (P.live && P.applied) pv = __ldcg(d.rawpool + (size_t)P.leaf * d.raw_len + cell);
     if (P.live && Lg >= 0) parent = d.pool[(size_t)P.lslot * d.slot_len + ft.slot_off + tid];
@@ -1703,6 +1777,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   const int warp = tid >> 5;
   const int nparts = min(d.F, (int)gridDim.x);
   if (tid == 0) {
+    if (!x_wait(d)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
     prep_compute(d, s, cs.prep);
   } else if (warp == 1) {
     const Cand o = other_leaves_best(d);
@@ -1761,6 +1836,8 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
           for (int k = 0; k < kCatWords; ++k) d.split_cat[k] = cs.pick.split_cat[k];
       }
     }
+    c.error |= *reinterpret_cast<volatile uint32_t*>(&d.ctrl->error);  // other CTAs' bits
+    if (c.error & kErrSpinTimeout) c.done = 1;  // a rank stopped answering: end the tree
     *d.ctrl = c;
   }
 }
@@ -2415,49 +2492,75 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
   }
   const dim3 bgrid(build_blocks, d.num_groups);
   const int part_blocks = sms * 4;
-  auto build = [&](int phase) {
+  // Producer k of the tree (the root build, then split k-1's partition / build) adds into
+  // its accumulator; its consumer (the next control step, or the final k_prepare) reads
+  // the sum. Over peer memory (xranks > 1) the two alternate by k % 2 (GrowDev::xlocal).
+  const bool px = d.xranks > 1;
+  const size_t xs = (size_t)d.raw_len + 2;
+  auto producer = [&](int k) {
+    GrowDev x = d;
+    if (px) x.raw = d.xlocal + (size_t)(k & 1) * xs;
+    return x;
+  };
+  auto consumer = [&](int k) {
+    GrowDev x = d;
+    if (px) {
+      x.xpar = k & 1;
+      x.raw = d.xlocal + (size_t)((k + 1) & 1) * xs;  // cleared for producer k + 1
+    }
+    return x;
+  };
+  auto build = [&](const GrowDev& x, int phase) {
     PROF_BEGIN(KC_BUILD);
-    if (d.gh_mode == GH_QPACK)
-      q4_kernel(d.q4_shift, d.q4_nch)<<<bgrid, kQ4Threads, build_smem, st>>>(d, phase);
-    else if (d.gh_mode == GH_QLUT)
-      k_build<GH_QLUT><<<bgrid, kBuildThreads, build_smem, st>>>(d, phase);
+    if (x.gh_mode == GH_QPACK)
+      q4_kernel(x.q4_shift, x.q4_nch)<<<bgrid, kQ4Threads, build_smem, st>>>(x, phase);
+    else if (x.gh_mode == GH_QLUT)
+      k_build<GH_QLUT><<<bgrid, kBuildThreads, build_smem, st>>>(x, phase);
     else
-      k_build<GH_FLOAT><<<bgrid, kBuildThreads, build_smem, st>>>(d, phase);
+      k_build<GH_FLOAT><<<bgrid, kBuildThreads, build_smem, st>>>(x, phase);
     PROF_END();
   };
-  auto exchange_raw = [&]() {
-    if (comm) comm->sum_i64(comm->ctx, d.raw, (int64_t)d.raw_len + 1, st);
+  auto exchange = [&](const GrowDev& x) {
+    if (px)
+      k_xsignal<<<1, 32, 0, st>>>(x);
+    else if (comm)
+      comm->sum_i64(comm->ctx, x.raw, (int64_t)x.raw_len + 1, st);
   };
-  build(0);
-  exchange_raw();
+  {
+    const GrowDev x = producer(0);
+    build(x, 0);
+    exchange(x);
+  }
   for (int s = 0; s < d.L - 1; ++s) {
     {
+      const GrowDev x = consumer(s);
       PROF_BEGIN(KC_FIXSCAN);
-      if (d.has_cat)
-        k_fixscan<true><<<d.F, kScanThreads, 0, st>>>(d, s);
+      if (x.has_cat)
+        k_fixscan<true><<<x.F, kScanThreads, 0, st>>>(x, s);
       else
-        k_fixscan<false><<<d.F, kScanThreads, 0, st>>>(d, s);
+        k_fixscan<false><<<x.F, kScanThreads, 0, st>>>(x, s);
       PROF_END();
     }
     const int phase = s < d.L - 2 ? 1 : 2;
-    if (d.fused) {
+    const GrowDev x = producer(s + 1);
+    if (x.fused) {
       PROF_BEGIN(KC_PARTITION);
-      part_q4_kernel(d.q4_shift, d.q4_nch)<<<sms, kFpThreads, fused_partition_smem(), st>>>(
-          d, phase == 1 ? 1 : 0);
+      part_q4_kernel(x.q4_shift, x.q4_nch)<<<sms, kFpThreads, fused_partition_smem(), st>>>(
+          x, phase == 1 ? 1 : 0);
       PROF_END();
     } else {
       {
         PROF_BEGIN(KC_PARTITION);
-        k_partition<<<part_blocks, kPartThreads, 0, st>>>(d);
+        k_partition<<<part_blocks, kPartThreads, 0, st>>>(x);
         PROF_END();
       }
-      build(phase);
+      build(x, phase);
     }
-    exchange_raw();
+    exchange(x);
   }
   {
     PROF_BEGIN(KC_PREPARE);
-    k_prepare<<<1, 32, 0, st>>>(d, d.L - 1);
+    k_prepare<<<1, 32, 0, st>>>(consumer(d.L - 1), d.L - 1);
     PROF_END();
   }
 }

@@ -28,6 +28,9 @@ constexpr int kQ4MaxCells = 7168;
 // Rows per tile of the row-partition kernel (one look-back status word per tile).
 constexpr int kPartitionTileRows = 2048;
 
+// Most ranks of the peer-memory exchange (one node).
+constexpr int kMaxXRanks = 8;
+
 // Everything the per-split kernels touch, passed by value.
 struct GrowDev {
   GrowCtrl* ctrl;
@@ -87,6 +90,22 @@ struct GrowDev {
   uint32_t* split_cat;     // [kCatWords] left bins of the pending split (categorical)
   int32_t has_cat;         // some feature is categorical: the control step's CAT variant
   uint8_t* scan_ok;        // [2] leaf scanned flags
+  // Data-parallel exchange of the accumulated child over peer memory (xranks > 1). Every
+  // rank holds two accumulators [2][raw_len + 2]; producer k of a tree (the root build,
+  // then split k-1's partition or build) adds into its own buffer k % 2 and publishes a
+  // sequence number into every rank's flags; its consumer waits for all ranks' numbers,
+  // sums buffer xpar over the ranks and clears its own other buffer (`raw` in a consumer
+  // launch). With xranks <= 1 `raw` is the one accumulator of every launch.
+  int32_t xranks;
+  int32_t xrank;
+  int32_t xpar;
+  int32_t _xpad;
+  long long* xlocal;                          // this rank's two accumulators
+  long long* const* xbuf;                     // [xranks] each rank's accumulators (device)
+  unsigned long long* xflags;                 // this rank's flags, one per rank
+  unsigned long long* const* peer_xflags;     // [xranks] each rank's flags (device)
+  unsigned long long* xseq;                   // exchanges this rank has published
+  long long xwait_ns;                         // wait limit, then the spin-timeout error
   // gradients
   int32_t gh_mode;
   int32_t q4_shift;  // quantized build: log2 bin stride
