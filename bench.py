@@ -420,8 +420,8 @@ def run_ours(args):
                          f"({el:.1f} s), {cores} threads"}
 
     par = "single GPU" if world == 1 else (
-        f"data-parallel, {world} GPUs: rows sharded, one NCCL all-reduce of the integer "
-        f"child histogram per split")
+        f"data-parallel, {world} GPUs: rows sharded, the integer child histogram of every "
+        f"split exchanged over peer memory (NCCL when the peers cannot be mapped)")
     out = {
         "metric": "boosting_iters_per_sec",
         "value": value,
