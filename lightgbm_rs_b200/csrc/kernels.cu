@@ -107,8 +107,9 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 // Cell `idx` of the accumulated child: the sum over the ranks' buffers of parity xpar
 // (integers: exact in any order); on one device, the launch's accumulator.
+template <bool PEER>
 __device__ __forceinline__ long long raw_sum(const GrowDev& d, size_t idx) {
-  if (d.xranks <= 1) return __ldcg(d.raw + idx);
+  if (!PEER) return __ldcg(d.raw + idx);
   const size_t off = (size_t)d.xpar * ((size_t)d.raw_len + 2) + idx;
   long long s = 0;
   for (int r = 0; r < d.xranks; ++r) s += ld_relaxed_sys(d.xbuf[r] + off);
@@ -133,8 +134,9 @@ __device__ __noinline__ bool x_wait_flags(const uint32_t* error, int xranks,
   return true;
 }
 
+template <bool PEER>
 __device__ __forceinline__ bool x_wait(const GrowDev& d) {
-  if (d.xranks <= 1) return true;
+  if (!PEER) return true;
   return x_wait_flags(&d.ctrl->error, d.xranks, d.xflags, d.xseq, d.xwait_ns);
 }
 
@@ -934,6 +936,7 @@ struct Prep {
   int32_t priv_tiles;  // > 0: the accumulated child is this many per-tile partials
 };
 
+template <bool PEER>
 __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   GrowCtrl c = *d.ctrl;
   P.applied = 0;
@@ -964,7 +967,7 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
     const double old_value = d.t_leaf_value[leaf];
     const int32_t depth = d.t_leaf_depth[leaf];
     const int32_t mt = d.feat[f].missing_type;
-    const long long lcg_raw = raw_sum(d, (size_t)d.raw_len);
+    const long long lcg_raw = raw_sum<PEER>(d, (size_t)d.raw_len);
     slot_left = d.slot_of_leaf[leaf];
     const int32_t parent_right = parent >= 0 ? d.t_right[parent] : 0;
     const int32_t lc = c.part_left_total;
@@ -1193,9 +1196,13 @@ __device__ void prep_commit(const GrowDev& d, const Prep& P) {
 // The control step alone: applies the tree's last split.
 __global__ void k_prepare(GrowDev d, int s) {
   if (threadIdx.x != 0) return;
-  if (!x_wait(d)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
   Prep P;
-  prep_compute(d, s, P);
+  if (d.xranks > 1) {
+    if (!x_wait<true>(d)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
+    prep_compute<true>(d, s, P);
+  } else {
+    prep_compute<false>(d, s, P);
+  }
   if (d.has_cat)
     prep_commit<true>(d, P);
   else
@@ -1554,7 +1561,7 @@ struct FixScanSmem {
 // histogram cells (accumulated by the partition, or derived from the parent), FixHistogram,
 // compaction, the larger child by subtraction, and the REVERSE/FORWARD scans of both
 // children.
-template <bool CAT>
+template <bool CAT, bool PEER>
 __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanSmem& sm) {
   const int tid = threadIdx.x;
   const DevFeature ft = d.feat[f];
@@ -1585,7 +1592,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
       for (; t < nt; ++t) a0 += __ldcg(pp + (size_t)t * rl);
       bv = (a0 + a1) + (a2 + a3);
     } else {
-      bv = raw_sum(d, cell);
+      bv = raw_sum<PEER>(d, cell);
     }
     if (P.live && P.applied) pv = __ldcg(d.rawpool + (size_t)P.leaf * d.raw_len + cell);
     if (P.live && Lg >= 0) parent = d.pool[(size_t)P.lslot * d.slot_len + ft.slot_off + tid];
@@ -1771,21 +1778,21 @@ struct CtlSmem {
 // One control step by the CTAs [0, min(F, gridDim.x)), each taking features
 // blockIdx.x, blockIdx.x + gridDim.x, ...: apply the pending split, scan the two leaves,
 // and -- in the CTA that finishes last -- pick the next split and write the control block.
-template <bool CAT>
+template <bool CAT, bool PEER>
 __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& cs) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int nparts = min(d.F, (int)gridDim.x);
   if (tid == 0) {
-    if (!x_wait(d)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
-    prep_compute(d, s, cs.prep);
+    if (!x_wait<PEER>(d)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
+    prep_compute<PEER>(d, s, cs.prep);
   } else if (warp == 1) {
     const Cand o = other_leaves_best(d);
     if ((tid & 31) == 0) cs.other = o;
   }
   __syncthreads();
   for (int f = blockIdx.x; f < d.F; f += gridDim.x) {
-    fixscan_feature<CAT>(d, cs.prep, f, sm);
+    fixscan_feature<CAT, PEER>(d, cs.prep, f, sm);
     __syncthreads();
   }
   // last CTA: the pick (warp 0) and the control step's writes (warp 1) run side by side;
@@ -1842,11 +1849,11 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   }
 }
 
-template <bool CAT>
+template <bool CAT, bool PEER>
 __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
   __shared__ FixScanSmem sm;
   __shared__ CtlSmem cs;
-  control_step<CAT>(d, s, sm, cs);
+  control_step<CAT, PEER>(d, s, sm, cs);
 }
 
 // ------------------------------------------------------------------------------------
@@ -2535,10 +2542,12 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
     {
       const GrowDev x = consumer(s);
       PROF_BEGIN(KC_FIXSCAN);
+      // variants: categorical features, and the peer exchange (off on one device)
       if (x.has_cat)
-        k_fixscan<true><<<x.F, kScanThreads, 0, st>>>(x, s);
+        (px ? k_fixscan<true, true> : k_fixscan<true, false>)<<<x.F, kScanThreads, 0, st>>>(x, s);
       else
-        k_fixscan<false><<<x.F, kScanThreads, 0, st>>>(x, s);
+        (px ? k_fixscan<false, true> : k_fixscan<false, false>)<<<x.F, kScanThreads, 0, st>>>(
+            x, s);
       PROF_END();
     }
     const int phase = s < d.L - 2 ? 1 : 2;
