@@ -308,6 +308,12 @@ int lgbm_b200_learner::configure_groups(int mode) {
   build_blocks = sms * per_sm;
   const int64_t need = (ds->num_data + (1 << 18) - 1) >> 18;
   if (build_blocks < need) build_blocks = (int)need;
+  // the fused partition's cell layout (feature << shift) + bin, for f32 gradients
+  int shift = 4;
+  for (int f = 0; f < F; ++f)
+    while ((1 << shift) < ds->feats[f].num_bin) ++shift;
+  q4_shift = shift;
+  q4_nch = (F + 15) / 16;
   return LGBM_B200_OK;
 }
 
@@ -419,7 +425,7 @@ void lgbm_b200_learner::bind(const void* gh_ptr, const DevGhParams* ghp_ptr,
   d.stopped = stopped;
   d.gh_mode = gh_mode;
   d.q4_shift = q4_shift;
-  d.fused = fused_partition_supported(gh_mode, (int)groups.size(), q4_shift, q4_nch) ? 1 : 0;
+  d.fused = fused_partition_supported(gh_mode, ds->num_features, q4_shift, q4_nch) ? 1 : 0;
 
   d.q4_nch = q4_nch;
   d.groups = d_groups.p;

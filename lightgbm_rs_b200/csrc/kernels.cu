@@ -2100,9 +2100,34 @@ struct PartSmem {
   uint32_t cat[kCatWords];  // left bins of a categorical split
 };
 
+// f32 gradients in the fused partition: the 64-bit fixed-point values of the build
+// (GhValue<GH_FLOAT>) added with two native 64-bit shared atomics per (row, feature) into
+// g64 / h64, cell = (feature << SHIFT) + bin. The sums are exact integers, so the child
+// histogram is the one the separate build kernel would produce.
+template <int SHIFT, int NCH, bool MASKED>
+__device__ __forceinline__ void f32_row_regs(const uint4 (&w)[NCH], long long a, long long b,
+                                             unsigned long long* g64, const uint32_t* mask,
+                                             uint32_t tail) {
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch) {
+    const uint32_t words[4] = {w[ch].x, w[ch].y, w[ch].z, w[ch].w};
+    const uint32_t m16 = MASKED ? ((mask[ch >> 1] >> ((ch & 1) * 16)) & 0xffffu) : tail;
+    const bool test = MASKED || ch == NCH - 1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (test && !((m16 >> j) & 1u)) continue;
+      const uint32_t bin = (words[j >> 2] >> (8 * (j & 3))) & 0xffu;
+      unsigned long long* cell = g64 + ((16 * ch + j) << SHIFT) + bin;
+      atomicAdd(cell, (unsigned long long)a);
+      atomicAdd(cell + kQ4MaxCells, (unsigned long long)b);
+    }
+  }
+}
+
 // One fused partition by the whole grid (every thread of every CTA calls it); `sm` holds
-// the accumulators: hot | c3 | cold_g | cold_q, kQ4MaxCells words each.
-template <int SHIFT, int NCH>
+// the accumulators. Quantized (F32 false): hot | c3 | cold_g | cold_q, kQ4MaxCells u32
+// words each. f32 gradients: g64 | h64, kQ4MaxCells u64 words each (the same bytes).
+template <int SHIFT, int NCH, bool F32>
 __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, PartSmem& ps_) {
   static_assert(NCH <= kFpMaxChunks, "row chunks held in registers");
   int32_t* s_warp = ps_.warp;
@@ -2165,18 +2190,31 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
   uint32_t* c3 = sm + kQ4MaxCells;
   int32_t* cold_g = reinterpret_cast<int32_t*>(sm + 2 * kQ4MaxCells);
   int32_t* cold_q = reinterpret_cast<int32_t*>(sm + 3 * kQ4MaxCells);
+  unsigned long long* g64 = reinterpret_cast<unsigned long long*>(sm);
   if (build) {
-    uint4* h4 = reinterpret_cast<uint4*>(hot);
-    uint4* c4 = reinterpret_cast<uint4*>(c3);
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-    for (int i = tid; i < (cap + 3) / 4; i += kFpThreads) {
-      h4[i] = z;
-      c4[i] = z;
+    if (F32) {
+      uint4* a4 = reinterpret_cast<uint4*>(g64);
+      uint4* b4 = reinterpret_cast<uint4*>(g64 + kQ4MaxCells);
+      for (int i = tid; i < (cap + 1) / 2; i += kFpThreads) {
+        a4[i] = z;
+        b4[i] = z;
+      }
+    } else {
+      uint4* h4 = reinterpret_cast<uint4*>(hot);
+      uint4* c4 = reinterpret_cast<uint4*>(c3);
+      for (int i = tid; i < (cap + 3) / 4; i += kFpThreads) {
+        h4[i] = z;
+        c4[i] = z;
+      }
     }
   }
   __syncthreads();
   Q4Mask qm = q4_mask<NCH>(s_mask, nf);
   const uint16_t* gq = reinterpret_cast<const uint16_t*>(d.gh);
+  const float2* gf = reinterpret_cast<const float2*>(d.gh);
+  const double scale_g = F32 ? d.ghp->scale_g : 0.0;
+  const double scale_h = F32 ? d.ghp->scale_h : 0.0;
   const int fch = f >> 4, fw = (f >> 2) & 3, fsh = (f & 3) * 8;
   const size_t stride = (size_t)d.stride;
   bool folded = false;
@@ -2189,6 +2227,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
     uint32_t rows[kFpItems];
     uint4 w[kFpItems][NCH];
     uint16_t q[kFpItems];
+    float2 fv[kFpItems];
     uint32_t leftmask = 0, validmask = 0;
 #pragma unroll
     for (int j = 0; j < kFpItems; ++j) {
@@ -2205,11 +2244,15 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
         const uint4* rp = reinterpret_cast<const uint4*>(d.bins + (size_t)rows[j] * stride);
 #pragma unroll
         for (int ch = 0; ch < NCH; ++ch) w[j][ch] = rp[ch];
-        q[j] = build ? gq[rows[j]] : (uint16_t)0;
+        if (F32)
+          fv[j] = build ? gf[rows[j]] : make_float2(0.0f, 0.0f);
+        else
+          q[j] = build ? gq[rows[j]] : (uint16_t)0;
       } else {
 #pragma unroll
         for (int ch = 0; ch < NCH; ++ch) w[j][ch] = make_uint4(0u, 0u, 0u, 0u);
         q[j] = 0;
+        fv[j] = make_float2(0.0f, 0.0f);
       }
     }
 #pragma unroll
@@ -2255,11 +2298,20 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
         if (!((validmask >> j) & 1u)) continue;
         const bool is_left = (leftmask >> j) & 1u;
         if (is_left != build_left) continue;
-        const int qg = (int)(int8_t)(q[j] & 0xff), qh = (int)(int8_t)(q[j] >> 8);
-        if (qm.full)
-          q4_row_regs<SHIFT, NCH, false>(w[j], qg + (qh << 16), qh == 3, hot, qm.w, qm.tail);
-        else
-          q4_row_regs<SHIFT, NCH, true>(w[j], qg + (qh << 16), qh == 3, hot, qm.w, qm.tail);
+        if (F32) {
+          const long long a = __double2ll_rn((double)fv[j].x * scale_g);
+          const long long b = __double2ll_rn((double)fv[j].y * scale_h);
+          if (qm.full)
+            f32_row_regs<SHIFT, NCH, false>(w[j], a, b, g64, qm.w, qm.tail);
+          else
+            f32_row_regs<SHIFT, NCH, true>(w[j], a, b, g64, qm.w, qm.tail);
+        } else {
+          const int qg = (int)(int8_t)(q[j] & 0xff), qh = (int)(int8_t)(q[j] >> 8);
+          if (qm.full)
+            q4_row_regs<SHIFT, NCH, false>(w[j], qg + (qh << 16), qh == 3, hot, qm.w, qm.tail);
+          else
+            q4_row_regs<SHIFT, NCH, true>(w[j], qg + (qh << 16), qh == 3, hot, qm.w, qm.tail);
+        }
       }
     }
     __syncthreads();
@@ -2294,8 +2346,9 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
     __syncthreads();
     tile = s_tile;
     if (tile >= ntiles) break;
-    // fold the 16-bit packed fields before the next tile could overflow them
-    if (build && acc_rows + kPartTile > kQ4Chunk) {
+    // fold the 16-bit packed fields before the next tile could overflow them (the 64-bit
+    // f32 cells need no fold)
+    if (!F32 && build && acc_rows + kPartTile > kQ4Chunk) {
       for (int s2 = tid; s2 < cap; s2 += kFpThreads) {
         const int32_t v = (int32_t)hot[s2];
         const int32_t lo = (int32_t)(int16_t)(v & 0xffff);
@@ -2324,12 +2377,18 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
       const int fl = s2 >> SHIFT;
       const int bin = s2 & ((1 << SHIFT) - 1);
       if (fl >= nf || bin >= s_nb[fl]) continue;
-      const int32_t v = (int32_t)hot[s2];
-      const int32_t lo = (int32_t)(int16_t)(v & 0xffff);
-      const long long g = (folded ? (long long)cold_g[s2] : 0ll) + lo;
-      const long long qsum = (folded ? (long long)cold_q[s2] : 0ll) + ((v - lo) >> 16);
-      const long long n3 = (long long)c3[s2];
-      const long long h = (qsum - 3 * n3) | (n3 << 32);
+      long long g, h;
+      if (F32) {
+        g = (long long)g64[s2];
+        h = (long long)g64[kQ4MaxCells + s2];
+      } else {
+        const int32_t v = (int32_t)hot[s2];
+        const int32_t lo = (int32_t)(int16_t)(v & 0xffff);
+        g = (folded ? (long long)cold_g[s2] : 0ll) + lo;
+        const long long qsum = (folded ? (long long)cold_q[s2] : 0ll) + ((v - lo) >> 16);
+        const long long n3 = (long long)c3[s2];
+        h = (qsum - 3 * n3) | (n3 << 32);
+      }
       const size_t gb = (size_t)(s_boff[fl] + bin);
       if (priv) {
         *reinterpret_cast<longlong2*>(&part[2 * gb]) = make_longlong2(g, h);
@@ -2352,17 +2411,17 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
 }
 
 
-template <int SHIFT, int NCH>
+template <int SHIFT, int NCH, bool F32>
 __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int build) {
   extern __shared__ uint32_t sm[];
   __shared__ PartSmem ps;
-  partition_q4_phase<SHIFT, NCH>(d, build, sm, ps);
+  partition_q4_phase<SHIFT, NCH, F32>(d, build, sm, ps);
 }
 
 using PartQ4Kernel = void (*)(GrowDev, int);
-__host__ PartQ4Kernel part_q4_kernel(int shift, int nch) {
+__host__ PartQ4Kernel part_q4_kernel(int shift, int nch, bool f32 = false) {
 #define PQ4_CASE(S, N) \
-  if (shift == S && nch == N) return k_partition_q4<S, N>;
+  if (shift == S && nch == N) return f32 ? k_partition_q4<S, N, true> : k_partition_q4<S, N, false>;
   PQ4_CASE(4, 1) PQ4_CASE(4, 2) PQ4_CASE(5, 1) PQ4_CASE(5, 2) PQ4_CASE(6, 1) PQ4_CASE(6, 2)
   PQ4_CASE(7, 1) PQ4_CASE(7, 2) PQ4_CASE(8, 1) PQ4_CASE(8, 2)
 #undef PQ4_CASE
@@ -2476,9 +2535,12 @@ void LaunchProfiler::end(cudaStream_t st, int slot) {
     if (prof) prof->end(st, _slot); \
   } while (0)
 
-bool fused_partition_supported(int gh_mode, int num_groups, int shift, int nch) {
-  return gh_mode == GH_QPACK && num_groups == 1 && nch <= kFpMaxChunks &&
-         part_q4_kernel(shift, nch) != nullptr;
+// The partition accumulates the child itself for packed quantized gradients and for f32
+// gradients, when every feature fits one shared-memory layout (feature << shift) + bin.
+bool fused_partition_supported(int gh_mode, int num_features, int shift, int nch) {
+  return (gh_mode == GH_QPACK || gh_mode == GH_FLOAT) && num_features <= 128 &&
+         (num_features << shift) <= kQ4MaxCells && nch <= kFpMaxChunks &&
+         part_q4_kernel(shift, nch, gh_mode == GH_FLOAT) != nullptr;
 }
 
 size_t fused_partition_smem() { return (size_t)4 * sizeof(uint32_t) * kQ4MaxCells; }
@@ -2554,7 +2616,8 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
     const GrowDev x = producer(s + 1);
     if (x.fused) {
       PROF_BEGIN(KC_PARTITION);
-      part_q4_kernel(x.q4_shift, x.q4_nch)<<<sms, kFpThreads, fused_partition_smem(), st>>>(
+      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<sms, kFpThreads,
+                                                                fused_partition_smem(), st>>>(
           x, phase == 1 ? 1 : 0);
       PROF_END();
     } else {
@@ -2589,9 +2652,11 @@ void set_build_smem_limit(size_t bytes) {
       }
   for (int sh = 4; sh <= 8; ++sh)
     for (int n = 1; n <= kFpMaxChunks; ++n)
-      if (part_q4_kernel(sh, n))
-        cudaFuncSetAttribute(part_q4_kernel(sh, n), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)fused_partition_smem());
+      for (bool f32 : {false, true})
+        if (part_q4_kernel(sh, n, f32))
+          cudaFuncSetAttribute(part_q4_kernel(sh, n, f32),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)fused_partition_smem());
   cudaFuncSetAttribute(k_build<GH_QLUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)bytes);
   cudaFuncSetAttribute(k_build<GH_FLOAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,

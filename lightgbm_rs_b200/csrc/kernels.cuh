@@ -139,7 +139,7 @@ struct DeviceComm {
 // Host-side launch helpers (kernels.cu).
 void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStream_t st,
                  LaunchProfiler* prof = nullptr, const DeviceComm* comm = nullptr);
-bool fused_partition_supported(int gh_mode, int num_groups, int shift, int nch);
+bool fused_partition_supported(int gh_mode, int num_features, int shift, int nch);
 int build_smem_bytes_per_bin(int gh_mode);
 
 // Objective / score kernels (objective.cu).
