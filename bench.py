@@ -449,7 +449,9 @@ def run_ours(args):
                      "other_kernels": {k: v for k, v in per_kernel.items() if k != dom},
                      "rows_parted_per_iter": counts["rows_parted"],
                      "rows_built_per_iter": counts["rows_built"],
-                     "builds_per_iter": counts["builds"], "splits_per_iter": counts["splits"]},
+                     "builds_per_iter": counts["builds"], "splits_per_iter": counts["splits"],
+                     "lookahead_runs_per_iter": counts.get("lookahead_runs", 0),
+                     "lookahead_hits_per_iter": counts.get("lookahead_hits", 0)},
         "kernel_ms_per_iter": kms,
         "cpu_baseline": cpu,
         "e2e": {"value": args.steps / e2e_s, "unit": "iters/s",

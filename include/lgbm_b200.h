@@ -367,9 +367,11 @@ int lgbm_b200_booster_phase_ms(const lgbm_b200_booster* b, double* out3);
 /* Run ONE more boosting iteration outside the CUDA graph with CUDA events around
  * every kernel launch. ms_out[7] receives the summed device time per kernel class
  * {prepare, histogram build, fix+scan, partition, tree init, gradients, finish};
- * counts_out[6] = {kernel launches, histogram builds, rows streamed by the builds,
+ * counts_out[8] = {kernel launches, histogram builds, rows streamed by the builds,
  * splits, parent rows streamed by the partitions, 1 if the partition kernel also
- * builds the child histogram}. The iteration counts as a normal boosting iteration. */
+ * builds the child histogram, look-ahead partitions run, look-ahead partitions whose
+ * leaf was the next split}. Builds and rows count the partitions whose result the tree
+ * used. The iteration counts as a normal boosting iteration. */
 int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
                                         int64_t* counts_out);
 /* The launches timed by the last lgbm_b200_booster_profile_iteration, in launch order:

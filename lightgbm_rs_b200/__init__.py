@@ -502,12 +502,13 @@ class Booster:
         """One extra iteration with per-kernel-class device timing (CUDA events on the
         library's stream). Returns (ms by class, counts dict)."""
         ms = np.zeros(7, dtype=np.float64)
-        cnt = np.zeros(6, dtype=np.int64)
+        cnt = np.zeros(8, dtype=np.int64)
         C.check(C.lib().lgbm_b200_booster_profile_iteration(self._handle, C.ptr(ms), C.ptr(cnt)))
         self._trees = None
         return (dict(zip(self.KERNEL_CLASSES, ms.tolist())),
                 {"launches": int(cnt[0]), "builds": int(cnt[1]), "rows_built": int(cnt[2]),
-                 "splits": int(cnt[3]), "rows_parted": int(cnt[4]), "fused": bool(cnt[5])})
+                 "splits": int(cnt[3]), "rows_parted": int(cnt[4]), "fused": bool(cnt[5]),
+                 "lookahead_runs": int(cnt[6]), "lookahead_hits": int(cnt[7])})
 
     def profile_launches(self):
         """(kernel class name, device ms) of every span timed by the last

@@ -223,6 +223,13 @@ struct lgbm_b200_learner {
   DevBuf<DevSplitInfo> scan_out;
   DevBuf<uint32_t> cat_words;  // scan_cat [2F][8] | best_cat [L][8] | t_cat [L][8] | split_cat [8]
   DevBuf<uint8_t> scan_ok;
+  // look-ahead partitions: two slots and the second stream they run on
+  DevBuf<LookAhead> la;
+  DevBuf<long long> la_raw;
+  DevBuf<long long> la_partials;
+  DevBuf<unsigned long long> la_status;
+  LookAheadStreams las{};
+  bool la_enabled = true;  // LGBM_B200_LOOKAHEAD=0 turns the look-ahead off
   // gradients owned by a standalone learner (the booster owns its own)
   DevBuf<uint8_t> gh;
   DevBuf<DevGhParams> ghp;
@@ -231,6 +238,12 @@ struct lgbm_b200_learner {
   int configure_groups(int mode);
   int init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_config& c);
   void bind(const void* gh_ptr, const DevGhParams* ghp_ptr, const int32_t* stopped);
+  ~lgbm_b200_learner() {
+    if (las.st) cudaStreamDestroy(las.st);
+    if (las.fork) cudaEventDestroy(las.fork);
+    for (cudaEvent_t e : las.done)
+      if (e) cudaEventDestroy(e);
+  }
 };
 
 int lgbm_b200_learner::configure_groups(int mode) {
@@ -354,6 +367,20 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   CUDA_TRY(cudaMemset(cat_words.p, 0,
                       sizeof(uint32_t) * kCatWords * (2 * ds->num_features + 2 * L + 1)));
   CUDA_TRY(scan_ok.alloc(2));
+  CUDA_TRY(la.alloc(2));
+  CUDA_TRY(cudaMemset(la.p, 0, 2 * sizeof(LookAhead)));
+  CUDA_TRY(la_raw.alloc(2 * ((size_t)slot_len + 2)));
+  CUDA_TRY(la_partials.alloc((size_t)2 * kPrivateTiles * slot_len));
+  CUDA_TRY(la_status.alloc(max_tiles));
+  CUDA_TRY(cudaStreamCreateWithFlags(&las.st, cudaStreamNonBlocking));
+  CUDA_TRY(cudaEventCreateWithFlags(&las.fork, cudaEventDisableTiming));
+  CUDA_TRY(cudaEventCreateWithFlags(&las.done[0], cudaEventDisableTiming));
+  CUDA_TRY(cudaEventCreateWithFlags(&las.done[1], cudaEventDisableTiming));
+  {
+    const int sms = sm_count(device);
+    las.blocks = std::max(sms / 2, sms - std::min(ds->num_features, sms));
+  }
+  if (const char* e = std::getenv("LGBM_B200_LOOKAHEAD")) la_enabled = std::strcmp(e, "0") != 0;
   d = GrowDev{};
   d.ctrl = ctrl.p;
   d.feat = ds->d_feats.p;
@@ -415,6 +442,10 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   for (const DevFeature& f : ds->feats)
     if (f.flags & kFeatCategorical) d.has_cat = 1;
   d.scan_ok = scan_ok.p;
+  d.la = la.p;
+  d.la_raw = la_raw.p;
+  d.la_partials = la_partials.p;
+  d.la_status = la_status.p;
   return LGBM_B200_OK;
 }
 
@@ -426,6 +457,7 @@ void lgbm_b200_learner::bind(const void* gh_ptr, const DevGhParams* ghp_ptr,
   d.gh_mode = gh_mode;
   d.q4_shift = q4_shift;
   d.fused = fused_partition_supported(gh_mode, ds->num_features, q4_shift, q4_nch) ? 1 : 0;
+  d.lookahead = d.fused && la_enabled ? 1 : 0;
 
   d.q4_nch = q4_nch;
   d.groups = d_groups.p;
@@ -752,7 +784,7 @@ extern "C" {
 
 const char* lgbm_b200_last_error(void) { return g_last_error.c_str(); }
 
-int32_t lgbm_b200_abi_version(void) { return 102; }
+int32_t lgbm_b200_abi_version(void) { return 103; }
 
 int lgbm_b200_device_count(int32_t* out) {
   int n = 0;
@@ -1351,7 +1383,7 @@ int lgbm_b200_learner_grow_tree(lgbm_b200_learner* l, int32_t gh_kind, const voi
   o.ghp = l->ghp.p;
   o.num_quant_bins = hp.num_quant_bins;
   launch_learner_gradients(o, gh_kind, l->stream);
-  launch_tree(l->d, l->build_blocks, l->build_smem, l->stream);
+  launch_tree(l->d, l->build_blocks, l->build_smem, l->stream, nullptr, nullptr, &l->las);
   CUDA_TRY(cudaGetLastError());
   CUDA_TRY(cudaStreamSynchronize(l->stream));
   int rc = read_tree(l, tree_out);
@@ -1839,7 +1871,7 @@ int lgbm_b200_booster_train(lgbm_b200_booster* b, int32_t num_iterations, int32_
     CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     launch_gradients(b->obj, st, nullptr, b->dcomm());
     launch_tree(b->learner->d, b->learner->build_blocks, b->learner->build_smem, st, nullptr,
-                b->dcomm());
+                b->dcomm(), &b->learner->las);
     launch_finish_iteration(b->learner->d, b->fin, st);
     cudaError_t e = cudaStreamEndCapture(st, &b->graph);
     if (e != cudaSuccess)
@@ -1963,7 +1995,7 @@ int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
   int rc = b->ensure_capacity(state[1] + 1);
   if (rc) return rc;
   cudaStream_t st = b->learner->stream;
-  const int cap = 4 * b->learner->L + 64;
+  const int cap = 5 * b->learner->L + 64;
   std::vector<cudaEvent_t> evs(2 * (size_t)cap);
   for (auto& e : evs) CUDA_TRY(cudaEventCreate(&e));
   std::vector<int> cls(cap);
@@ -1974,7 +2006,7 @@ int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
   prof.n = 0;
   launch_gradients(b->obj, st, &prof, b->dcomm());
   launch_tree(b->learner->d, b->learner->build_blocks, b->learner->build_smem, st, &prof,
-              b->dcomm());
+              b->dcomm(), &b->learner->las);
   launch_finish_iteration(b->learner->d, b->fin, st, &prof);
   cudaError_t le = cudaGetLastError();
   cudaError_t se = cudaStreamSynchronize(st);
@@ -2005,6 +2037,8 @@ int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
   counts_out[3] = c.num_splits;
   counts_out[4] = c.rows_parted;
   counts_out[5] = b->learner->d.fused;
+  counts_out[6] = c.la_runs;
+  counts_out[7] = c.la_hits;
   return LGBM_B200_OK;
 }
 

@@ -140,7 +140,11 @@ struct GrowCtrl {
   long long rows_built;    // rows streamed by those builds
   long long rows_parted;   // parent rows streamed by the partitions
   int32_t num_cat;         // categorical nodes in the tree so far
-  int32_t _pad3;
+  int32_t pend_la;         // 0: the pending split's rows were partitioned by the main
+                           // partition; 1 + k: by the look-ahead partition of slot k
+  long long la_rows;       // parent rows streamed by look-ahead partitions (used or not)
+  int32_t la_runs;         // look-ahead partitions run in this tree
+  int32_t la_hits;         // ... whose leaf was the next split
   DevSplitInfo split;
 };
 

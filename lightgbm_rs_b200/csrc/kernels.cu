@@ -871,6 +871,12 @@ __global__ void k_tree_init(GrowDev d) {
   // previous tree: the gradient step's reductions came in between)
   if (d.xranks > 1)
     for (size_t i = gtid; i < 2 * ((size_t)d.raw_len + 2); i += gsz) d.xlocal[i] = 0;
+  // look-ahead slots: empty accumulators, no recorded leaf, no stale status words
+  if (d.lookahead) {
+    for (size_t i = gtid; i < 2 * ((size_t)d.raw_len + 2); i += gsz) d.la_raw[i] = 0;
+    for (int i = gtid; i < d.max_tiles; i += gsz) d.la_status[i] = 0ull;
+    if (gtid < 2) d.la[gtid] = LookAhead{};
+  }
   if (gtid == 0) {
     const uint32_t epoch = c->epoch;
     const uint32_t err = c->error;
@@ -934,6 +940,8 @@ struct Prep {
   int32_t S, Lg, sslot, lslot, use_sub, mask_leaf, smaller_is_left;
   DevLeafSplits lsS, lsLg;
   int32_t priv_tiles;  // > 0: the accumulated child is this many per-tile partials
+  int32_t acc_slot;    // >= 0: the pending split was partitioned by this look-ahead slot
+  int32_t la_clear;    // >= 0: the look-ahead slot this step clears (look-ahead on)
 };
 
 template <bool PEER>
@@ -950,6 +958,35 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   P.mask_leaf = -1;
   P.smaller_is_left = 1;
   P.priv_tiles = 0;
+  P.acc_slot = -1;
+  P.la_clear = -1;
+  // Look-ahead slot s % 2 was filled by the look-ahead kernel of step s - 2, which has
+  // finished: count it, and consume it when step s - 1 picked its leaf.
+  const LookAhead* lar = nullptr;
+  if (d.lookahead) {
+    P.la_clear = s & 1;
+    if (s >= 2) {
+      const LookAhead& r = d.la[s & 1];
+      if (r.active && r.ran) {
+        c.la_runs += 1;
+        c.la_rows += r.rows;
+      }
+      if (r.failed) {
+        c.error |= kErrSpinTimeout;
+        c.done = 1;
+      }
+      if (c.pending && c.pend_la == 1 + (s & 1)) {
+        lar = &r;
+        P.acc_slot = s & 1;
+        c.la_hits += 1;
+        c.rows_parted += r.rows;
+        if (r.build) {
+          c.rows_built += r.built;
+          c.num_builds += 1;
+        }
+      }
+    }
+  }
   int32_t left = c.left_leaf, right = c.right_leaf;
   int32_t cnt_left = 0, cnt_right = 0, depth_left = 0, slot_left = -1;
   bool known = false;
@@ -967,10 +1004,11 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
     const double old_value = d.t_leaf_value[leaf];
     const int32_t depth = d.t_leaf_depth[leaf];
     const int32_t mt = d.feat[f].missing_type;
-    const long long lcg_raw = raw_sum<PEER>(d, (size_t)d.raw_len);
+    // a look-ahead runs on one device only: its left rows are all the left rows
+    const long long lcg_raw = lar ? (long long)lar->left_total : raw_sum<PEER>(d, (size_t)d.raw_len);
     slot_left = d.slot_of_leaf[leaf];
     const int32_t parent_right = parent >= 0 ? d.t_right[parent] : 0;
-    const int32_t lc = c.part_left_total;
+    const int32_t lc = lar ? lar->left_total : c.part_left_total;
     const int32_t lcg = (int32_t)lcg_raw;
     P.applied = 1;
     P.leaf = leaf;
@@ -1029,6 +1067,7 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
     c.num_leaves = nr + 1;
     c.num_splits += 1;
     c.pending = 0;
+    c.pend_la = 0;
   }
   if (c.done || s >= d.L - 1) {
     c.do_find = 0;
@@ -1187,6 +1226,7 @@ __device__ void prep_commit(const GrowDev& d, const Prep& P) {
     d.best_feature[nr] = -1;
     d.raw[d.raw_len] = 0;
   }
+  if (P.la_clear >= 0) d.la_raw[(size_t)P.la_clear * (d.raw_len + 2) + d.raw_len] = 0;
   if (P.kill0 >= 0) d.best[P.kill0].gain = kNegInf;
   if (P.kill1 >= 0) d.best[P.kill1].gain = kNegInf;
   if (P.slot_leaf0 >= 0) d.slot_of_leaf[P.slot_leaf0] = P.slot_val0;
@@ -1243,11 +1283,57 @@ __device__ __forceinline__ void warp_argmax(Cand& c) {
   }
 }
 
-// Best split among the leaves a control step leaves alone: the arg_max inputs of
+__device__ __forceinline__ bool cand_lt(const Cand& a, const Cand& b) {  // a ranks first
+  return cand_better(a.g, a.f, a.i, b.g, b.f, b.i);
+}
+
+// The first two candidates in pick order. An empty place holds {-inf, -1, INT_MAX},
+// which every leaf's candidate outranks (its index is smaller).
+struct Cand2 {
+  Cand a, b;
+};
+
+__device__ __forceinline__ Cand cand_none() { return Cand{kNegInf, -1, 0x7fffffff}; }
+
+__device__ __forceinline__ void cand2_insert(Cand2& t, const Cand& x) {
+  if (cand_lt(x, t.a)) {
+    t.b = t.a;
+    t.a = x;
+  } else if (cand_lt(x, t.b)) {
+    t.b = x;
+  }
+}
+
+__device__ __forceinline__ Cand shfl_cand(const Cand& c, int o) {
+  Cand x;
+  x.g = __shfl_xor_sync(0xffffffffu, c.g, o);
+  x.f = __shfl_xor_sync(0xffffffffu, c.f, o);
+  x.i = __shfl_xor_sync(0xffffffffu, c.i, o);
+  return x;
+}
+
+__device__ __forceinline__ void warp_top2(Cand2& t) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const Cand xa = shfl_cand(t.a, o), xb = shfl_cand(t.b, o);
+    // merge of two ordered pairs (every lane ends with the same pair: a strict order)
+    Cand2 m;
+    if (cand_lt(xa, t.a)) {
+      m.a = xa;
+      m.b = cand_lt(t.a, xb) ? t.a : xb;
+    } else {
+      m.a = t.a;
+      m.b = cand_lt(xa, t.b) ? xa : t.b;
+    }
+    t = m;
+  }
+}
+
+// Best two splits among the leaves a control step leaves alone: the arg_max inputs of
 // learner.rs:4537-4551 other than the leaves being scanned (the two children of the
 // applied split, or the root), by one warp. Their best splits are final before the
-// step starts, so this runs concurrently with the control step itself.
-__device__ Cand other_leaves_best(const GrowDev& d) {
+// step starts, so this runs concurrently with the control step itself. The second is
+// the look-ahead's candidate when the first wins the pick.
+__device__ Cand2 other_leaves_best(const GrowDev& d) {
   const GrowCtrl* c = d.ctrl;
   const int lane = threadIdx.x & 31;
   int32_t ex0 = 0, ex1 = -1;
@@ -1255,14 +1341,13 @@ __device__ Cand other_leaves_best(const GrowDev& d) {
     ex0 = c->split_leaf;
     ex1 = c->num_leaves;
   }
-  Cand lc{kNegInf, -1, 0x7fffffff};
+  Cand2 t{cand_none(), cand_none()};
   for (int i = lane; i < d.L; i += 32) {
     if (i == ex0 || i == ex1) continue;
-    const Cand x{__ldcg(&d.best[i].gain), __ldcg(&d.best_feature[i]), i};
-    if (lc.i == 0x7fffffff || cand_better(x.g, x.f, x.i, lc.g, lc.f, lc.i)) lc = x;
+    cand2_insert(t, Cand{__ldcg(&d.best[i].gain), __ldcg(&d.best_feature[i]), i});
   }
-  warp_argmax(lc);
-  return lc;
+  warp_top2(t);
+  return t;
 }
 
 // Outcome of the pick at the end of a control step.
@@ -1274,17 +1359,21 @@ struct PickOut {
   DevSplitInfo split;  // the split to apply next
   uint32_t si_cat[2][kCatWords];  // left bins of si[] when their feature is categorical
   uint32_t split_cat[kCatWords];  // left bins of `split`
+  // the runner-up of the pick (the look-ahead's leaf), valid when la_leaf >= 0
+  int32_t la_leaf, la_feature, la_build_left;
+  DevSplitInfo la_split;
+  uint32_t la_cat[kCatWords];
 };
 
 // Cross-feature argmax of both scanned leaves (learner.rs:3314-3321) and the arg_max
 // over all leaves (learner.rs:4537-4551, first max under split_gt, learner.rs:1503-1505
 // stop rule), by one warp: the feature candidates are reduced with shuffles only.
 template <bool CAT>
-__device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand& other, PickOut& o) {
+__device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand2& other, PickOut& o) {
   const int lane = threadIdx.x & 31;
   const bool find = P.live != 0;
   const int32_t S = P.S, Lg = P.Lg;
-  Cand best = other;
+  Cand2 top = other;
   if (find) {
     const bool ok0 = __ldcg(&d.scan_ok[0]) != 0;
     const bool ok1 = Lg >= 0 && __ldcg(&d.scan_ok[1]) != 0;
@@ -1315,16 +1404,14 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand& other, Pi
           o.si_cat[1][k] =
               (Lg >= 0 && bf1 >= 0) ? d.scan_cat[((size_t)d.F + bf1) * kCatWords + k] : 0u;
     }
-    const Cand a{ok0 ? f0.g : kNegInf, ok0 ? f0.f : -1, S};
-    if (best.i == 0x7fffffff || cand_better(a.g, a.f, a.i, best.g, best.f, best.i)) best = a;
-    if (Lg >= 0) {
-      const Cand b{ok1 ? f1.g : kNegInf, ok1 ? f1.f : -1, Lg};
-      if (cand_better(b.g, b.f, b.i, best.g, best.f, best.i)) best = b;
-    }
+    cand2_insert(top, Cand{ok0 ? f0.g : kNegInf, ok0 ? f0.f : -1, S});
+    if (Lg >= 0) cand2_insert(top, Cand{ok1 ? f1.g : kNegInf, ok1 ? f1.f : -1, Lg});
   }
   __syncwarp();
   if (lane == 0) {
+    const Cand best = top.a;
     const int32_t bl = best.i;
+    o.la_leaf = -1;
     if (best.g <= 0.0 || bl == 0x7fffffff) {
       o.done = 1;
     } else {
@@ -1339,6 +1426,20 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand& other, Pi
           o.split_cat[k] = sel >= 0 ? o.si_cat[sel][k] : d.best_cat[(size_t)bl * kCatWords + k];
       // accumulate the side the scan expects to be smaller (any side is exact)
       o.build_left = sp.left_count <= sp.right_count ? 1 : 0;
+      // the runner-up: the next pick chooses it unless a child of this split outranks it
+      const Cand ru = top.b;
+      if (d.lookahead && ru.i != 0x7fffffff && ru.g > 0.0) {
+        const int32_t rl = ru.i;
+        const int rs = (find && rl == S) ? 0 : (find && rl == Lg) ? 1 : -1;
+        const DevSplitInfo rp = rs == 0 ? o.si[0] : rs == 1 ? o.si[1] : d.best[rl];
+        o.la_leaf = rl;
+        o.la_feature = ru.f;
+        o.la_split = rp;
+        o.la_build_left = rp.left_count <= rp.right_count ? 1 : 0;
+        if (CAT)
+          for (int k = 0; k < kCatWords; ++k)
+            o.la_cat[k] = rs >= 0 ? o.si_cat[rs][k] : d.best_cat[(size_t)rl * kCatWords + k];
+      }
     }
   }
 }
@@ -1578,8 +1679,10 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
   double parent = 0.0;
   if (mine) {
     const int nt = P.priv_tiles;
+    const int as = P.acc_slot;
     if (nt > 0) {
-      const long long* pp = d.partials + cell;
+      const long long* pp =
+          (as >= 0 ? d.la_partials + (size_t)as * d.private_tiles * d.raw_len : d.partials) + cell;
       const size_t rl = (size_t)d.raw_len;
       long long a0 = 0, a1 = 0, a2 = 0, a3 = 0;
       int t = 0;
@@ -1591,6 +1694,8 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
       }
       for (; t < nt; ++t) a0 += __ldcg(pp + (size_t)t * rl);
       bv = (a0 + a1) + (a2 + a3);
+    } else if (as >= 0) {
+      bv = __ldcg(d.la_raw + (size_t)as * (d.raw_len + 2) + cell);
     } else {
       bv = raw_sum<PEER>(d, cell);
     }
@@ -1599,8 +1704,10 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
   }
   const bool used_f =
       !P.live || !P.use_sub || d.splittable[(size_t)P.mask_leaf * d.F + f] != 0;
-  // clear the accumulator for the next partition
-  if (mine && P.priv_tiles == 0) d.raw[cell] = 0;
+  // clear the accumulator for the next partition (a look-ahead hit left it untouched),
+  // and this step's look-ahead slot for its next look-ahead kernel
+  if (mine && P.priv_tiles == 0 && P.acc_slot < 0) d.raw[cell] = 0;
+  if (mine && P.la_clear >= 0) d.la_raw[(size_t)P.la_clear * (d.raw_len + 2) + cell] = 0;
   if (P.live) {
     const bool used = used_f;
     if (used) {
@@ -1770,7 +1877,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
 // Shared memory of a control step besides the per-feature scratch.
 struct CtlSmem {
   Prep prep;
-  Cand other;
+  Cand2 other;
   PickOut pick;
   bool last;
 };
@@ -1787,7 +1894,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     if (!x_wait<PEER>(d)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
     prep_compute<PEER>(d, s, cs.prep);
   } else if (warp == 1) {
-    const Cand o = other_leaves_best(d);
+    const Cand2 o = other_leaves_best(d);
     if ((tid & 31) == 0) cs.other = o;
   }
   __syncthreads();
@@ -1841,10 +1948,33 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
         c.build_left = cs.pick.build_left;
         if (CAT)
           for (int k = 0; k < kCatWords; ++k) d.split_cat[k] = cs.pick.split_cat[k];
+        // the previous step's look-ahead partitioned this leaf already (it may still be
+        // running; the step that applies the split waits for it)
+        if (d.lookahead && s >= 1) {
+          const LookAhead& q = d.la[(s - 1) & 1];
+          if (q.active && q.leaf == cs.pick.leaf) c.pend_la = 1 + ((s - 1) & 1);
+        }
       }
     }
     c.error |= *reinterpret_cast<volatile uint32_t*>(&d.ctrl->error);  // other CTAs' bits
     if (c.error & kErrSpinTimeout) c.done = 1;  // a rank stopped answering: end the tree
+    // this step's look-ahead: the runner-up of the pick (its kernel runs next to the
+    // following control step; slot s % 2 was consumed and cleared above)
+    if (d.lookahead && s <= d.L - 3) {
+      LookAhead r{};
+      r.epoch = c.epoch;
+      if (!c.done && c.pending && cs.pick.la_leaf >= 0) {
+        r.active = 1;
+        r.leaf = cs.pick.la_leaf;
+        r.feature = cs.pick.la_feature;
+        r.build = s < d.L - 3 ? 1 : 0;  // the last look-ahead feeds no scan
+        r.build_left = cs.pick.la_build_left;
+        r.split = cs.pick.la_split;
+        if (CAT)
+          for (int k = 0; k < kCatWords; ++k) r.cat[k] = cs.pick.la_cat[k];
+      }
+      d.la[s & 1] = r;
+    }
     *d.ctrl = c;
   }
 }
@@ -2128,7 +2258,8 @@ __device__ __forceinline__ void f32_row_regs(const uint4 (&w)[NCH], long long a,
 // the accumulators. Quantized (F32 false): hot | c3 | cold_g | cold_q, kQ4MaxCells u32
 // words each. f32 gradients: g64 | h64, kQ4MaxCells u64 words each (the same bytes).
 template <int SHIFT, int NCH, bool F32>
-__device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, PartSmem& ps_) {
+__device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t* sm,
+                                   PartSmem& ps_) {
   static_assert(NCH <= kFpMaxChunks, "row chunks held in registers");
   int32_t* s_warp = ps_.warp;
   int32_t& s_tile = ps_.tile;
@@ -2138,9 +2269,13 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
   int32_t* s_boff = ps_.boff;
   uint32_t* s_mask = ps_.mask;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // la >= 0: the look-ahead partition of slot la (its leaf, split, counters, status
+  // words and accumulator); otherwise the pending split of the control block
+  LookAhead* const rec = la >= 0 ? d.la + la : nullptr;
+  uint32_t* const ticket = rec ? &rec->ticket : &d.ctrl->part_ticket;
   // the first tile ticket is taken before anything else is read: its round trip overlaps
   // the reads below (a ticket taken when there is nothing to do is harmless)
-  if (tid == 0) s_tile = (int32_t)atomicAdd(&d.ctrl->part_ticket, 1u);
+  if (tid == 0) s_tile = (int32_t)atomicAdd(ticket, 1u);
   // the dataset's feature table does not depend on the split: read it first
   if (build)
     for (int fl = tid; fl < d.F; fl += kFpThreads) {
@@ -2149,9 +2284,40 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
       s_boff[fl] = g.bin_off;
     }
   GrowCtrl* c = d.ctrl;
-  if (c->done || !c->pending) return;
-  const int32_t leaf = c->split_leaf;
-  const int32_t f = c->split_feature;
+  int32_t leaf, f;
+  uint32_t epoch, thr;
+  bool dl, build_left;
+  const uint32_t* cat_src;
+  unsigned long long* status;
+  long long* raw;
+  long long* partials;
+  if (rec) {
+    if (!rec->active) return;
+    leaf = rec->leaf;
+    f = rec->feature;
+    epoch = rec->epoch;
+    thr = rec->split.threshold;
+    dl = rec->split.default_left != 0;
+    build_left = rec->build_left != 0;
+    if (!rec->build) build = 0;
+    cat_src = rec->cat;
+    status = d.la_status;
+    raw = d.la_raw + (size_t)la * (d.raw_len + 2);
+    partials = d.la_partials + (size_t)la * d.private_tiles * d.raw_len;
+  } else {
+    // nothing to do after the tree, or when the look-ahead did this partition
+    if (c->done || !c->pending || c->pend_la) return;
+    leaf = c->split_leaf;
+    f = c->split_feature;
+    epoch = c->epoch;
+    thr = c->split.threshold;
+    dl = c->split.default_left != 0;
+    build_left = c->build_left != 0;
+    cat_src = d.split_cat;
+    status = d.part_status;
+    raw = d.raw;
+    partials = d.partials;
+  }
   const DevFeature ft = d.feat[f];
   const int32_t begin = d.leaf_begin[leaf];
   const int32_t count = d.leaf_count[leaf];
@@ -2160,10 +2326,6 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
   uint32_t* dp = src == 1 ? d.idx0 : d.idx1;
   const bool identity = src == 2;
   const int32_t ntiles = (count + kPartTile - 1) / kPartTile;
-  const uint32_t epoch = c->epoch;
-  const uint32_t thr = c->split.threshold;
-  const bool dl = c->split.default_left != 0;
-  const bool build_left = c->build_left != 0;
   const bool is_cat = (ft.flags & kFeatCategorical) != 0;
   const int nf = d.F;
   const int cap = nf << SHIFT;
@@ -2178,10 +2340,15 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
   // (plain stores, summed by the next control step) instead of adding it atomically
   const bool priv = build && ntiles <= d.private_tiles;
   if (blockIdx.x == 0 && tid == 0) {
-    c->rows_parted += count;
-    if (build) c->num_builds += 1;
+    if (rec) {
+      rec->ran = 1;
+      rec->rows = count;
+    } else {
+      c->rows_parted += count;
+      if (build) c->num_builds += 1;
+    }
   }
-  if (is_cat && tid < kCatWords) ps_.cat[tid] = d.split_cat[tid];
+  if (is_cat && tid < kCatWords) ps_.cat[tid] = cat_src[tid];
   __syncthreads();
   int32_t tile = s_tile;
   if (tile >= ntiles) return;
@@ -2285,7 +2452,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
     const int32_t excl = warp_off + incl - my_left;
     if (warp == 0) {
       int32_t ok = 1;
-      const int32_t prefix = tile_lookback(d.part_status, tile, epoch, tile_left, &ok);
+      const int32_t prefix = tile_lookback(status, tile, epoch, tile_left, &ok);
       if (lane == 0) {
         s_prefix = prefix;
         s_ok = ok;
@@ -2342,7 +2509,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
     cta_built += built;
     acc_rows += built;
     if (priv) break;
-    if (tid == 0) s_tile = (int32_t)atomicAdd(&c->part_ticket, 1u);
+    if (tid == 0) s_tile = (int32_t)atomicAdd(ticket, 1u);
     __syncthreads();
     tile = s_tile;
     if (tile >= ntiles) break;
@@ -2364,15 +2531,18 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
   }
   if (failed) {
     if (tid == 0) {
-      atomicOr(&c->error, kErrSpinTimeout);
-      c->done = 1;
+      if (rec) {
+        rec->failed = 1;  // reported by the control step that consumes the slot
+      } else {
+        atomicOr(&c->error, kErrSpinTimeout);
+        c->done = 1;
+      }
     }
     return;
   }
   if (build) {
     __syncthreads();
-    long long* raw = d.raw;
-    long long* part = d.partials + (size_t)my_tile * d.raw_len;
+    long long* part = partials + (size_t)my_tile * d.raw_len;
     for (int s2 = tid; s2 < cap; s2 += kFpThreads) {
       const int fl = s2 >> SHIFT;
       const int bin = s2 & ((1 << SHIFT) - 1);
@@ -2402,23 +2572,24 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, uint32_t* sm, Pa
     }
   }
   if (tid == 0) {
-    atomicAdd(&c->part_left_total, cta_left);
-    atomicAdd(reinterpret_cast<unsigned long long*>(&d.raw[d.raw_len]),
+    atomicAdd(rec ? &rec->left_total : &c->part_left_total, cta_left);
+    atomicAdd(reinterpret_cast<unsigned long long*>(&raw[d.raw_len]),
               (unsigned long long)(long long)cta_left);
-    if (build) atomicAdd(reinterpret_cast<unsigned long long*>(&c->rows_built),
-                         (unsigned long long)cta_built);
+    if (build)
+      atomicAdd(reinterpret_cast<unsigned long long*>(rec ? &rec->built : &c->rows_built),
+                (unsigned long long)cta_built);
   }
 }
 
 
 template <int SHIFT, int NCH, bool F32>
-__global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int build) {
+__global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int build, int la) {
   extern __shared__ uint32_t sm[];
   __shared__ PartSmem ps;
-  partition_q4_phase<SHIFT, NCH, F32>(d, build, sm, ps);
+  partition_q4_phase<SHIFT, NCH, F32>(d, build, la, sm, ps);
 }
 
-using PartQ4Kernel = void (*)(GrowDev, int);
+using PartQ4Kernel = void (*)(GrowDev, int, int);
 __host__ PartQ4Kernel part_q4_kernel(int shift, int nch, bool f32 = false) {
 #define PQ4_CASE(S, N) \
   if (shift == S && nch == N) return f32 ? k_partition_q4<S, N, true> : k_partition_q4<S, N, false>;
@@ -2551,9 +2722,15 @@ size_t fused_partition_smem() { return (size_t)4 * sizeof(uint32_t) * kQ4MaxCell
 // build kernel follows). With several devices the accumulated child (d.raw: raw_len
 // integer cells + the left-row count) is summed over them after every build, so every
 // device takes the same decisions.
-void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStream_t st,
-                 LaunchProfiler* prof, const DeviceComm* comm) {
+void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaStream_t st,
+                 LaunchProfiler* prof, const DeviceComm* comm, const LookAheadStreams* las) {
   const int sms = num_sms();
+  // Look-ahead partitions on the second stream (one device, fused partition): the kernel
+  // of step s starts after control step s and must end before control step s + 2, which
+  // consumes or clears its slot. The kernels see the flag only when they are launched.
+  const bool la_on = d_in.lookahead && las && d_in.fused && d_in.xranks <= 1 && !comm;
+  GrowDev d = d_in;
+  d.lookahead = la_on ? 1 : 0;
   {
     PROF_BEGIN(KC_INIT);
     k_tree_init<<<32, 256, 0, st>>>(d);
@@ -2601,6 +2778,7 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
     exchange(x);
   }
   for (int s = 0; s < d.L - 1; ++s) {
+    if (la_on && s >= 2) cudaStreamWaitEvent(st, las->done[s & 1], 0);
     {
       const GrowDev x = consumer(s);
       PROF_BEGIN(KC_FIXSCAN);
@@ -2614,11 +2792,21 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
     }
     const int phase = s < d.L - 2 ? 1 : 2;
     const GrowDev x = producer(s + 1);
+    if (la_on && s <= d.L - 3) {
+      cudaEventRecord(las->fork, st);
+      cudaStreamWaitEvent(las->st, las->fork, 0);
+      const int pslot = prof ? prof->begin(las->st, KC_PARTITION) : -1;
+      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<las->blocks, kFpThreads,
+                                                                fused_partition_smem(),
+                                                                las->st>>>(x, 1, s & 1);
+      if (prof) prof->end(las->st, pslot);
+      cudaEventRecord(las->done[s & 1], las->st);
+    }
     if (x.fused) {
       PROF_BEGIN(KC_PARTITION);
       part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<sms, kFpThreads,
                                                                 fused_partition_smem(), st>>>(
-          x, phase == 1 ? 1 : 0);
+          x, phase == 1 ? 1 : 0, -1);
       PROF_END();
     } else {
       {
@@ -2630,6 +2818,8 @@ void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStre
     }
     exchange(x);
   }
+  // the last split may come from the last look-ahead, which also joins the second stream
+  if (la_on && d.L >= 3) cudaStreamWaitEvent(st, las->done[(d.L - 1) & 1], 0);
   {
     PROF_BEGIN(KC_PREPARE);
     k_prepare<<<1, 32, 0, st>>>(consumer(d.L - 1), d.L - 1);

@@ -31,6 +31,28 @@ constexpr int kPartitionTileRows = 2048;
 // Most ranks of the peer-memory exchange (one node).
 constexpr int kMaxXRanks = 8;
 
+// One look-ahead partition: the leaf that ranks second at a control step's pick (the
+// runner-up) is partitioned, with its child histogram, while the next control step runs.
+// When the following pick chooses that leaf, its partition is already done. Written by
+// the control step that picks (its last CTA), read by the look-ahead kernel of that
+// step; the kernel adds the counters below.
+struct LookAhead {
+  int32_t active;      // a runner-up leaf with a positive gain was recorded
+  int32_t leaf;
+  int32_t feature;
+  int32_t build;       // accumulate the child histogram
+  int32_t build_left;  // ... of the left rows (else the right rows)
+  uint32_t epoch;      // status-word epoch of the partition
+  uint32_t ticket;     // tile tickets
+  int32_t left_total;  // left rows
+  int32_t failed;      // a look-back gave up (spin limit)
+  int32_t ran;         // the kernel partitioned the leaf
+  long long rows;      // parent rows streamed
+  long long built;     // rows accumulated into the child histogram
+  DevSplitInfo split;
+  uint32_t cat[kCatWords];  // left bins of a categorical split
+};
+
 // Everything the per-split kernels touch, passed by value.
 struct GrowDev {
   GrowCtrl* ctrl;
@@ -106,6 +128,15 @@ struct GrowDev {
   unsigned long long* const* peer_xflags;     // [xranks] each rank's flags (device)
   unsigned long long* xseq;                   // exchanges this rank has published
   long long xwait_ns;                         // wait limit, then the spin-timeout error
+  // Look-ahead partitions (one device, fused partition): two slots, control step s
+  // records slot s % 2 and its look-ahead kernel fills it; control step s + 2 consumes
+  // it (when step s + 1 picked the recorded leaf) and clears it.
+  int32_t lookahead;
+  int32_t _lapad;
+  LookAhead* la;                  // [2]
+  long long* la_raw;              // [2][raw_len + 2] accumulated child, left-row count
+  long long* la_partials;         // [2][private_tiles][raw_len]
+  unsigned long long* la_status;  // [max_tiles] look-back words of the look-ahead kernel
   // gradients
   int32_t gh_mode;
   int32_t q4_shift;  // quantized build: log2 bin stride
@@ -136,9 +167,18 @@ struct DeviceComm {
   void (*min_u32)(void* ctx, uint32_t* buf, int64_t n, cudaStream_t st);
 };
 
+// The second stream of the look-ahead partitions and its events (owned by the learner).
+struct LookAheadStreams {
+  cudaStream_t st;
+  cudaEvent_t fork;     // after control step s, on the main stream
+  cudaEvent_t done[2];  // after the look-ahead kernel of step s, slot s % 2
+  int blocks;           // CTAs of a look-ahead kernel (the control step keeps the rest)
+};
+
 // Host-side launch helpers (kernels.cu).
 void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStream_t st,
-                 LaunchProfiler* prof = nullptr, const DeviceComm* comm = nullptr);
+                 LaunchProfiler* prof = nullptr, const DeviceComm* comm = nullptr,
+                 const LookAheadStreams* las = nullptr);
 bool fused_partition_supported(int gh_mode, int num_features, int shift, int nch);
 int build_smem_bytes_per_bin(int gh_mode);
 
