@@ -35,7 +35,7 @@ namespace {
 
 // Splits of leaves with at most this many 2048-row tiles (this device's rows) hand the
 // accumulated child to the next control step as one partial histogram per tile.
-constexpr int kPrivateTiles = 16;
+constexpr int kPrivateTiles = kMaxPrivateTiles;
 
 thread_local std::string g_last_error;
 

@@ -21,6 +21,9 @@ namespace {
 constexpr int kBuildThreads = 512;
 constexpr int kMinRowsPerBlock = 1024;
 constexpr int kScanThreads = 1024;
+// The control step sums at most two halves of per-tile partials, one load per tile each.
+constexpr int kHalfTiles = kMaxPrivateTiles / 2;
+static_assert(kScanThreads == 1024, "the partial-sum halves are the CTA's two 512-thread halves");
 constexpr int kPartThreads = 256;
 constexpr int kPartItems = 8;
 constexpr int kPartTile = kPartThreads * kPartItems;
@@ -606,6 +609,18 @@ __device__ __forceinline__ double seq_sub(const double* v, int stride, int n, do
   return acc;
 }
 
+// Asynchronous prefetch of [p, p + bytes) into L2 (p and bytes multiples of 16).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void warp_best(double& gain, int32_t& k) {
   // max gain, ties to the smallest k (first in scan order)
   for (int o = 16; o > 0; o >>= 1) {
@@ -946,7 +961,9 @@ struct Prep {
 
 template <bool PEER>
 __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
-  GrowCtrl c = *d.ctrl;
+  // the control block is updated in place in P (shared memory in the control step)
+  GrowCtrl& c = P.c;
+  c = *d.ctrl;
   P.applied = 0;
   P.live = 0;
   P.kill0 = P.kill1 = -1;
@@ -1071,7 +1088,6 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   }
   if (c.done || s >= d.L - 1) {
     c.do_find = 0;
-    P.c = c;
     return;
   }
   if (!known) {
@@ -1105,7 +1121,6 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   }
   c.do_find = did;
   if (!did) {
-    P.c = c;
     return;
   }
   // ---- smaller child + pool slots (learner.rs:1882-1916) ----
@@ -1154,7 +1169,6 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
       c.error |= kErrNoParentHistogram;
       c.done = 1;
       c.do_find = 0;
-      P.c = c;
       return;
     }
   }
@@ -1163,7 +1177,6 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   c.smaller_slot = ss;
   c.larger_slot = lsl;
   c.use_subtract = use_sub;
-  P.c = c;
   P.live = 1;
   P.S = smaller;
   P.Lg = larger;
@@ -1334,17 +1347,35 @@ __device__ __forceinline__ void warp_top2(Cand2& t) {
 // step starts, so this runs concurrently with the control step itself. The second is
 // the look-ahead's candidate when the first wins the pick.
 __device__ Cand2 other_leaves_best(const GrowDev& d) {
+  constexpr int kPer = 8;  // leaves per lane: at most 256 leaves
   const GrowCtrl* c = d.ctrl;
   const int lane = threadIdx.x & 31;
+  // every read is issued before any is used: one round trip
+  double g[kPer];
+  int32_t bf[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = lane + 32 * k;
+    g[k] = kNegInf;
+    bf[k] = -1;
+    if (i < d.L) {
+      g[k] = __ldcg(&d.best[i].gain);
+      bf[k] = __ldcg(&d.best_feature[i]);
+    }
+  }
+  const int32_t pending = __ldcg(&c->pending);
+  const int32_t split_leaf = __ldcg(&c->split_leaf);
+  const int32_t num_leaves = __ldcg(&c->num_leaves);
   int32_t ex0 = 0, ex1 = -1;
-  if (c->pending) {
-    ex0 = c->split_leaf;
-    ex1 = c->num_leaves;
+  if (pending) {
+    ex0 = split_leaf;
+    ex1 = num_leaves;
   }
   Cand2 t{cand_none(), cand_none()};
-  for (int i = lane; i < d.L; i += 32) {
-    if (i == ex0 || i == ex1) continue;
-    cand2_insert(t, Cand{__ldcg(&d.best[i].gain), __ldcg(&d.best_feature[i]), i});
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = lane + 32 * k;
+    if (i < d.L && i != ex0 && i != ex1) cand2_insert(t, Cand{g[k], bf[k], i});
   }
   warp_top2(t);
   return t;
@@ -1368,19 +1399,43 @@ struct PickOut {
 // Cross-feature argmax of both scanned leaves (learner.rs:3314-3321) and the arg_max
 // over all leaves (learner.rs:4537-4551, first max under split_gt, learner.rs:1503-1505
 // stop rule), by one warp: the feature candidates are reduced with shuffles only.
-template <bool CAT>
-__device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand2& other, PickOut& o) {
+// Shared memory of a control step besides the per-feature scratch.
+struct CtlSmem {
+  Prep prep;
+  Cand2 other;                    // the best two leaves the step leaves alone
+  DevSplitInfo orec[2];           // ... their best splits (read at the kernel start)
+  uint32_t ocat[2][kCatWords];    // ... and their left bins
+  int32_t la_prev;                // the previous step's look-ahead leaf (-1: none)
+  int32_t oslot[2];               // the other leaves' best two: their histogram slots
+  DevFeature ft0;                 // the CTA's first feature
+  uint32_t err;                   // the control block's error bits, read by the last CTA
+  uint8_t ok[2];                  // the scanned leaves' scan flags
+  PickOut pick;
+  bool last;
+};
+
+// STAGED: `so` / `sc` are the scan results and bin sets in shared memory; otherwise the
+// global scan_out / scan_cat. `cs` holds the other leaves' best two and their splits.
+template <typename T, bool STAGED>
+__device__ __forceinline__ T pick_rd(const T* p) {
+  if (STAGED) return *p;
+  return __ldcg(p);
+}
+
+template <bool CAT, bool STAGED>
+__device__ void pick_warp(const GrowDev& d, const Prep& P, const CtlSmem& cs,
+                          const DevSplitInfo* so, const uint32_t* sc, PickOut& o) {
   const int lane = threadIdx.x & 31;
   const bool find = P.live != 0;
   const int32_t S = P.S, Lg = P.Lg;
-  Cand2 top = other;
+  Cand2 top = cs.other;
   if (find) {
-    const bool ok0 = __ldcg(&d.scan_ok[0]) != 0;
-    const bool ok1 = Lg >= 0 && __ldcg(&d.scan_ok[1]) != 0;
+    const bool ok0 = cs.ok[0] != 0;
+    const bool ok1 = Lg >= 0 && cs.ok[1] != 0;
     Cand f0{kNegInf, -1, -1}, f1{kNegInf, -1, -1};
     for (int f = lane; f < d.F; f += 32) {
-      const double g0 = __ldcg(&d.scan_out[f].gain);
-      const double g1 = Lg >= 0 ? __ldcg(&d.scan_out[d.F + f].gain) : kNegInf;
+      const double g0 = pick_rd<double, STAGED>(&so[f].gain);
+      const double g1 = Lg >= 0 ? pick_rd<double, STAGED>(&so[d.F + f].gain) : kNegInf;
       if (ok0) d.splittable[(size_t)S * d.F + f] = g0 > kNegInf ? 1 : 0;
       if (ok1) d.splittable[(size_t)Lg * d.F + f] = g1 > kNegInf ? 1 : 0;
       if (g0 > kNegInf && cand_better(g0, f, f, f0.g, f0.f, f0.i)) f0 = Cand{g0, f, f};
@@ -1391,18 +1446,17 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand2& other, P
     const int32_t bf0 = ok0 ? f0.f : -1;
     const int32_t bf1 = ok1 ? f1.f : -1;
     if (lane == 0) {
-      o.si[0] = bf0 >= 0 ? d.scan_out[bf0] : d_split_none();
+      o.si[0] = bf0 >= 0 ? so[bf0] : d_split_none();
       o.bf[0] = bf0;
       if (CAT)
         for (int k = 0; k < kCatWords; ++k)
-          o.si_cat[0][k] = bf0 >= 0 ? d.scan_cat[(size_t)bf0 * kCatWords + k] : 0u;
+          o.si_cat[0][k] = bf0 >= 0 ? sc[(size_t)bf0 * kCatWords + k] : 0u;
     } else if (lane == 1) {
-      o.si[1] = (Lg >= 0 && bf1 >= 0) ? d.scan_out[d.F + bf1] : d_split_none();
+      o.si[1] = (Lg >= 0 && bf1 >= 0) ? so[d.F + bf1] : d_split_none();
       o.bf[1] = bf1;
       if (CAT)
         for (int k = 0; k < kCatWords; ++k)
-          o.si_cat[1][k] =
-              (Lg >= 0 && bf1 >= 0) ? d.scan_cat[((size_t)d.F + bf1) * kCatWords + k] : 0u;
+          o.si_cat[1][k] = (Lg >= 0 && bf1 >= 0) ? sc[((size_t)d.F + bf1) * kCatWords + k] : 0u;
     }
     cand2_insert(top, Cand{ok0 ? f0.g : kNegInf, ok0 ? f0.f : -1, S});
     if (Lg >= 0) cand2_insert(top, Cand{ok1 ? f1.g : kNegInf, ok1 ? f1.f : -1, Lg});
@@ -1418,12 +1472,14 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand2& other, P
       o.done = 0;
       o.leaf = bl;
       o.feature = best.f;
+      // an old leaf that wins or runs up is one of the other leaves' best two
       const int sel = (find && bl == S) ? 0 : (find && bl == Lg) ? 1 : -1;
-      const DevSplitInfo sp = sel == 0 ? o.si[0] : sel == 1 ? o.si[1] : d.best[bl];
+      const int oi = bl == cs.other.a.i ? 0 : 1;
+      const DevSplitInfo sp = sel == 0 ? o.si[0] : sel == 1 ? o.si[1] : cs.orec[oi];
       o.split = sp;
       if (CAT)
         for (int k = 0; k < kCatWords; ++k)
-          o.split_cat[k] = sel >= 0 ? o.si_cat[sel][k] : d.best_cat[(size_t)bl * kCatWords + k];
+          o.split_cat[k] = sel >= 0 ? o.si_cat[sel][k] : cs.ocat[oi][k];
       // accumulate the side the scan expects to be smaller (any side is exact)
       o.build_left = sp.left_count <= sp.right_count ? 1 : 0;
       // the runner-up: the next pick chooses it unless a child of this split outranks it
@@ -1431,14 +1487,15 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const Cand2& other, P
       if (d.lookahead && ru.i != 0x7fffffff && ru.g > 0.0) {
         const int32_t rl = ru.i;
         const int rs = (find && rl == S) ? 0 : (find && rl == Lg) ? 1 : -1;
-        const DevSplitInfo rp = rs == 0 ? o.si[0] : rs == 1 ? o.si[1] : d.best[rl];
+        const int ri = rl == cs.other.a.i ? 0 : 1;
+        const DevSplitInfo rp = rs == 0 ? o.si[0] : rs == 1 ? o.si[1] : cs.orec[ri];
         o.la_leaf = rl;
         o.la_feature = ru.f;
         o.la_split = rp;
         o.la_build_left = rp.left_count <= rp.right_count ? 1 : 0;
         if (CAT)
           for (int k = 0; k < kCatWords; ++k)
-            o.la_cat[k] = rs >= 0 ? o.si_cat[rs][k] : d.best_cat[(size_t)rl * kCatWords + k];
+            o.la_cat[k] = rs >= 0 ? o.si_cat[rs][k] : cs.ocat[ri][k];
       }
     }
   }
@@ -1663,9 +1720,9 @@ struct FixScanSmem {
 // compaction, the larger child by subtraction, and the REVERSE/FORWARD scans of both
 // children.
 template <bool CAT, bool PEER>
-__device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanSmem& sm) {
+__device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const DevFeature& ft,
+                                FixScanSmem& sm) {
   const int tid = threadIdx.x;
-  const DevFeature ft = d.feat[f];
   const int nb = ft.num_bin;
   // one histogram cell per thread (2*num_bin <= 512 cells)
   const bool mine = tid < 2 * nb;
@@ -1677,33 +1734,40 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
   const int32_t S = P.S, Lg = P.Lg;
   long long bv = 0, pv = 0;
   double parent = 0.0;
+  const int nt = P.priv_tiles;
+  const int as = P.acc_slot;
   if (mine) {
-    const int nt = P.priv_tiles;
-    const int as = P.acc_slot;
-    if (nt > 0) {
-      const long long* pp =
-          (as >= 0 ? d.la_partials + (size_t)as * d.private_tiles * d.raw_len : d.partials) + cell;
-      const size_t rl = (size_t)d.raw_len;
-      long long a0 = 0, a1 = 0, a2 = 0, a3 = 0;
-      int t = 0;
-      for (; t + 4 <= nt; t += 4) {
-        a0 += __ldcg(pp + (size_t)t * rl);
-        a1 += __ldcg(pp + (size_t)(t + 1) * rl);
-        a2 += __ldcg(pp + (size_t)(t + 2) * rl);
-        a3 += __ldcg(pp + (size_t)(t + 3) * rl);
-      }
-      for (; t < nt; ++t) a0 += __ldcg(pp + (size_t)t * rl);
-      bv = (a0 + a1) + (a2 + a3);
-    } else if (as >= 0) {
-      bv = __ldcg(d.la_raw + (size_t)as * (d.raw_len + 2) + cell);
-    } else {
-      bv = raw_sum<PEER>(d, cell);
-    }
+    if (nt == 0) bv = as >= 0 ? __ldcg(d.la_raw + (size_t)as * (d.raw_len + 2) + cell)
+                              : raw_sum<PEER>(d, cell);
     if (P.live && P.applied) pv = __ldcg(d.rawpool + (size_t)P.leaf * d.raw_len + cell);
     if (P.live && Lg >= 0) parent = d.pool[(size_t)P.lslot * d.slot_len + ft.slot_off + tid];
   }
   const bool used_f =
       !P.live || !P.use_sub || d.splittable[(size_t)P.mask_leaf * d.F + f] != 0;
+  // Per-tile partials: the two halves of the CTA load tiles [0, 8) and [8, 16) of their
+  // cell, all in one round trip (integers: any order of summation).
+  long long tsum = 0;
+  if (nt > 0) {
+    const int half = tid >> 9, c2 = tid & 511;
+    const size_t rl = (size_t)d.raw_len;
+    const long long* pp =
+        (as >= 0 ? d.la_partials + (size_t)as * d.private_tiles * rl : d.partials) +
+        2 * (size_t)ft.bin_off + c2 + (size_t)(half * kHalfTiles) * rl;
+    const int nh = c2 < 2 * nb ? min(nt - half * kHalfTiles, kHalfTiles) : 0;
+    long long a[kHalfTiles];
+#pragma unroll
+    for (int j = 0; j < kHalfTiles; ++j) a[j] = j < nh ? __ldcg(pp + (size_t)j * rl) : 0ll;
+#pragma unroll
+    for (int j = 1; j < kHalfTiles; ++j) a[0] += a[j];
+    tsum = a[0];
+  }
+  if (nt > kHalfTiles) {  // uniform: the upper half hands its sums to the lower half
+    long long* xs = reinterpret_cast<long long*>(sm.hist[1]);
+    if (tid >= 512) xs[tid - 512] = tsum;
+    __syncthreads();
+    if (tid < 512) tsum += xs[tid];
+  }
+  if (mine && nt > 0) bv = tsum;
   // clear the accumulator for the next partition (a look-ahead hit left it untouched),
   // and this step's look-ahead slot for its next look-ahead kernel
   if (mine && P.priv_tiles == 0 && P.acc_slot < 0) d.raw[cell] = 0;
@@ -1874,13 +1938,12 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, FixScanS
   }
 }
 
-// Shared memory of a control step besides the per-feature scratch.
-struct CtlSmem {
-  Prep prep;
-  Cand2 other;
-  PickOut pick;
-  bool last;
-};
+
+// The last CTA copies every feature's scan result of both leaves (and their bin sets)
+// into the per-feature scratch in one round trip when they fit there.
+constexpr int kStageFeatures =
+    (int)(sizeof(FixScanSmem) / (2 * (sizeof(DevSplitInfo) + kCatWords * sizeof(uint32_t))));
+static_assert(sizeof(DevSplitInfo) % 8 == 0, "scan results are copied as 8-byte words");
 
 // One control step by the CTAs [0, min(F, gridDim.x)), each taking features
 // blockIdx.x, blockIdx.x + gridDim.x, ...: apply the pending split, scan the two leaves,
@@ -1894,32 +1957,101 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     if (!x_wait<PEER>(d)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
     prep_compute<PEER>(d, s, cs.prep);
   } else if (warp == 1) {
+    // the best two of the leaves this step leaves alone (final before the step starts;
+    // the last CTA reads their splits with its other inputs)
     const Cand2 o = other_leaves_best(d);
     if ((tid & 31) == 0) cs.other = o;
+  } else if (tid == 64) {
+    if (blockIdx.x < (unsigned)d.F) cs.ft0 = d.feat[blockIdx.x];
   }
   __syncthreads();
   for (int f = blockIdx.x; f < d.F; f += gridDim.x) {
-    fixscan_feature<CAT, PEER>(d, cs.prep, f, sm);
+    // the CTA's first feature was read while the pending split was applied
+    const DevFeature ft = f == (int)blockIdx.x ? cs.ft0 : d.feat[f];
+    fixscan_feature<CAT, PEER>(d, cs.prep, f, ft, sm);
     __syncthreads();
   }
-  // last CTA: the pick (warp 0) and the control step's writes (warp 1) run side by side;
-  // then one thread writes the scanned leaves' best splits and the control block
-  __threadfence();
+  // Arrival: the barrier orders every thread's writes before thread 0's release, and the
+  // CTA that arrives last acquires all of them (acq_rel add) before its barrier.
   __syncthreads();
   if (tid == 0) {
-    const uint32_t t = atomicAdd(&d.ctrl->scan_counter, 1u);
+    const uint32_t t = atom_add_acq_rel_gpu(&d.ctrl->scan_counter, 1u);
     cs.last = (t == (uint32_t)nparts - 1);
   }
   __syncthreads();
   if (!cs.last) return;
-  __threadfence();
   const Prep& P = cs.prep;
-  if (warp == 0) {
-    if (!P.c.done) pick_warp<CAT>(d, P, cs.other, cs.pick);
-  } else if (warp == 1 && (tid & 31) == 0) {
-    prep_commit<CAT>(d, P);
+  // One round trip for everything the pick reads that other CTAs wrote: the scan results
+  // (into the per-feature scratch, when they fit), the scan flags and the error bits.
+  const bool staged = d.F <= kStageFeatures;
+  DevSplitInfo* so = reinterpret_cast<DevSplitInfo*>(&sm);
+  uint32_t* sc = reinterpret_cast<uint32_t*>(so + 2 * kStageFeatures);
+  if (staged) {
+    const int nw = d.F * (int)(2 * sizeof(DevSplitInfo) / 8);
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(d.scan_out);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(so);
+    for (int i = tid; i < nw; i += kScanThreads) dst[i] = __ldcg(src + i);
+    if (CAT)
+      for (int i = tid; i < 2 * d.F * kCatWords; i += kScanThreads) sc[i] = __ldcg(d.scan_cat + i);
+  }
+  if (tid == kScanThreads - 32) {
+    cs.ok[0] = __ldcg(&d.scan_ok[0]);
+    cs.ok[1] = __ldcg(&d.scan_ok[1]);
+    cs.err = *reinterpret_cast<volatile uint32_t*>(&d.ctrl->error);  // other CTAs' bits
+  } else if (warp == 2) {
+    // the other leaves' best two: their splits, bin sets and histogram slots; and the
+    // previous step's look-ahead leaf
+    const int lane = tid & 31;
+    if (lane < 2) {
+      const int32_t i = lane == 0 ? cs.other.a.i : cs.other.b.i;
+      if (i != 0x7fffffff) {
+        cs.orec[lane] = d.best[i];
+        if (CAT)
+          for (int k = 0; k < kCatWords; ++k)
+            cs.ocat[lane][k] = d.best_cat[(size_t)i * kCatWords + k];
+      }
+    } else if (lane == 4 || lane == 5) {
+      const int32_t i = lane == 4 ? cs.other.a.i : cs.other.b.i;
+      cs.oslot[lane - 4] = i != 0x7fffffff ? d.slot_of_leaf[i] : -1;
+    } else if (lane == 2) {
+      int32_t lp = -1;
+      if (d.lookahead && s >= 1) {
+        const LookAhead& q = d.la[(s - 1) & 1];
+        if (q.active) lp = q.leaf;
+      }
+      cs.la_prev = lp;
+    }
+  }
+  if (warp == 1 && (tid & 31) == 0) prep_commit<CAT>(d, P);
+  __syncthreads();
+  if (warp == 0 && !P.c.done) {
+    if (staged)
+      pick_warp<CAT, true>(d, P, cs, so, sc, cs.pick);
+    else
+      pick_warp<CAT, false>(d, P, cs, d.scan_out, d.scan_cat, cs.pick);
   }
   __syncthreads();
+  // The next step reads the chosen leaf's integer and f64 histogram rows, which the
+  // partitions' streaming has usually pushed out of L2 since the leaf was scanned: bring
+  // them back now, one bulk prefetch per 16 KB.
+  if (warp == 1 && !P.c.done && !cs.pick.done) {
+    const int32_t b = cs.pick.leaf;
+    const int32_t slot = (P.live && b == P.S)    ? P.sslot
+                         : (P.live && b == P.Lg) ? P.lslot
+                         : cs.oslot[b == cs.other.a.i ? 0 : 1];
+    const uint32_t bytes = (uint32_t)d.raw_len * 8u;
+    const int lane = tid & 31;
+    constexpr uint32_t kChunk = 16384;
+    const uint32_t nck = (bytes + kChunk - 1) / kChunk;
+    for (uint32_t k = lane; k < 2 * nck; k += 32) {
+      const bool pool_row = k >= nck;
+      if (pool_row && slot < 0) continue;
+      const uint32_t off = (pool_row ? k - nck : k) * kChunk;
+      const char* base = pool_row ? reinterpret_cast<const char*>(d.pool + (size_t)slot * d.slot_len)
+                                  : reinterpret_cast<const char*>(d.rawpool + (size_t)b * d.raw_len);
+      prefetch_l2_bulk(base + off, min(kChunk, bytes - off));
+    }
+  }
   if (tid == 0) {
     GrowCtrl c = P.c;
     c.scan_counter = 0;
@@ -1950,13 +2082,11 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
           for (int k = 0; k < kCatWords; ++k) d.split_cat[k] = cs.pick.split_cat[k];
         // the previous step's look-ahead partitioned this leaf already (it may still be
         // running; the step that applies the split waits for it)
-        if (d.lookahead && s >= 1) {
-          const LookAhead& q = d.la[(s - 1) & 1];
-          if (q.active && q.leaf == cs.pick.leaf) c.pend_la = 1 + ((s - 1) & 1);
-        }
+        if (d.lookahead && s >= 1 && cs.la_prev == cs.pick.leaf)
+          c.pend_la = 1 + ((s - 1) & 1);
       }
     }
-    c.error |= *reinterpret_cast<volatile uint32_t*>(&d.ctrl->error);  // other CTAs' bits
+    c.error |= cs.err;
     if (c.error & kErrSpinTimeout) c.done = 1;  // a rank stopped answering: end the tree
     // this step's look-ahead: the runner-up of the pick (its kernel runs next to the
     // following control step; slot s % 2 was consumed and cleared above)
@@ -2792,16 +2922,10 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
     }
     const int phase = s < d.L - 2 ? 1 : 2;
     const GrowDev x = producer(s + 1);
-    if (la_on && s <= d.L - 3) {
-      cudaEventRecord(las->fork, st);
-      cudaStreamWaitEvent(las->st, las->fork, 0);
-      const int pslot = prof ? prof->begin(las->st, KC_PARTITION) : -1;
-      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<las->blocks, kFpThreads,
-                                                                fused_partition_smem(),
-                                                                las->st>>>(x, 1, s & 1);
-      if (prof) prof->end(las->st, pslot);
-      cudaEventRecord(las->done[s & 1], las->st);
-    }
+    const bool la_step = la_on && s <= d.L - 3;
+    if (la_step) cudaEventRecord(las->fork, st);
+    // the main partition is launched before the look-ahead, so that its CTAs (which
+    // mostly find the split already partitioned) are placed first
     if (x.fused) {
       PROF_BEGIN(KC_PARTITION);
       part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<sms, kFpThreads,
@@ -2815,6 +2939,15 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
         PROF_END();
       }
       build(x, phase);
+    }
+    if (la_step) {
+      cudaStreamWaitEvent(las->st, las->fork, 0);
+      const int pslot = prof ? prof->begin(las->st, KC_PARTITION) : -1;
+      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<las->blocks, kFpThreads,
+                                                                fused_partition_smem(),
+                                                                las->st>>>(x, 1, s & 1);
+      if (prof) prof->end(las->st, pslot);
+      cudaEventRecord(las->done[s & 1], las->st);
     }
     exchange(x);
   }

@@ -28,6 +28,9 @@ constexpr int kQ4MaxCells = 7168;
 // Rows per tile of the row-partition kernel (one look-back status word per tile).
 constexpr int kPartitionTileRows = 2048;
 
+// Splits of up to this many partition tiles store per-tile partial histograms.
+constexpr int kMaxPrivateTiles = 16;
+
 // Most ranks of the peer-memory exchange (one node).
 constexpr int kMaxXRanks = 8;
 
