@@ -18,6 +18,7 @@
 
 #include "binning.h"
 #include "common.cuh"
+#include "host_copy.h"
 #include "kernels.cuh"
 #include "lgbm_b200.h"
 
@@ -1230,12 +1231,13 @@ int dataset_build(int32_t device, const void* const* columns, int kind, int64_t 
       1, std::min<int64_t>(num_data, (256ll << 20) / ((int64_t)num_features * elem)));
   DevBuf<uint8_t> staging;
   CUDA_TRY(staging.alloc((size_t)chunk * num_features * elem));
+  std::vector<const void*> srcs(num_features);
   for (int64_t r0 = 0; r0 < num_data; r0 += chunk) {
     const int64_t n = std::min(chunk, num_data - r0);
     for (int f = 0; f < num_features; ++f)
-      CUDA_TRY(cudaMemcpyAsync(staging.p + (size_t)f * chunk * elem,
-                               (const uint8_t*)columns[f] + (size_t)r0 * elem, (size_t)n * elem,
-                               cudaMemcpyHostToDevice, st));
+      srcs[f] = (const uint8_t*)columns[f] + (size_t)r0 * elem;
+    CUDA_TRY(staged_h2d(staging.p, srcs.data(), num_features, (size_t)n * elem,
+                        (size_t)chunk * elem, st));
     launch_bin_rows(br, kind, staging.p, chunk, n, r0, ds->bins.p + (size_t)r0 * ds->stride, st);
     CUDA_TRY(cudaGetLastError());
   }
@@ -1680,7 +1682,10 @@ int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
   CUDA_TRY(b->state.alloc(2));
   CUDA_TRY(cudaMemset(b->ghp.p, 0, sizeof(DevGhParams)));
   CUDA_TRY(cudaMemset(b->state.p, 0, 8));
-  CUDA_TRY(cudaMemcpy(b->label.p, labels, N * 4, cudaMemcpyHostToDevice));
+  {
+    const void* src = labels;
+    CUDA_TRY(staged_h2d(b->label.p, &src, 1, (size_t)N * 4, 0, b->learner->stream));
+  }
   // the labels of every row of the job: this device's, or all ranks' in row order
   std::vector<float> gathered;
   const float* all = labels;
@@ -1699,8 +1704,10 @@ int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
   if (cfg->boost_from_average && !rank) {
     const double eps = (double)1e-15f;
     if (cfg->objective == LGBM_B200_OBJECTIVE_BINARY) {
-      double suml = 0.0;
-      for (int64_t i = 0; i < NG; ++i) suml += all[i] > 0.0f ? 1.0 : 0.0;
+      // the sum of 0/1 indicators is an exact integer: counted, in any order
+      int64_t npos = 0;
+      for (int64_t i = 0; i < NG; ++i) npos += all[i] > 0.0f ? 1 : 0;
+      const double suml = (double)npos;
       double pavg = suml / (double)NG;  // binary.rs:178-194
       pavg = std::min(pavg, 1.0 - eps);
       pavg = std::max(pavg, eps);
@@ -1712,10 +1719,10 @@ int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
     }
   }
   b->init_score = init;
-  {
-    std::vector<double> sc(N, std::fabs(init) > (double)1e-15f ? init : 0.0);
-    CUDA_TRY(cudaMemcpy(b->score.p, sc.data(), N * 8, cudaMemcpyHostToDevice));
-  }
+  // every row starts at the init score (on the learner's stream, ahead of any training)
+  launch_fill_f64(b->score.p, N, std::fabs(init) > (double)1e-15f ? init : 0.0,
+                  b->learner->stream);
+  CUDA_TRY(cudaGetLastError());
   b->learner->bind(mode == GH_FLOAT ? (const void*)b->gh.p : (const void*)(b->gh.p + 8 * N),
                    b->ghp.p, b->state.p);
   b->learner->d.n_global = NG;
@@ -1949,7 +1956,9 @@ int lgbm_b200_booster_init_score(const lgbm_b200_booster* b, double* out) {
 
 int lgbm_b200_booster_get_scores(lgbm_b200_booster* b, double* out) {
   if (!b || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
-  CUDA_TRY(cudaMemcpy(out, b->score.p, b->ds->num_data * 8, cudaMemcpyDeviceToHost));
+  DeviceGuard g(b->learner->device);
+  // after everything queued on the booster's stream (training, the initial score fill)
+  CUDA_TRY(staged_d2h(out, b->score.p, (size_t)b->ds->num_data * 8, b->learner->stream));
   return LGBM_B200_OK;
 }
 

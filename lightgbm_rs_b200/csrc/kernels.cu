@@ -1436,8 +1436,6 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const CtlSmem& cs,
     for (int f = lane; f < d.F; f += 32) {
       const double g0 = pick_rd<double, STAGED>(&so[f].gain);
       const double g1 = Lg >= 0 ? pick_rd<double, STAGED>(&so[d.F + f].gain) : kNegInf;
-      if (ok0) d.splittable[(size_t)S * d.F + f] = g0 > kNegInf ? 1 : 0;
-      if (ok1) d.splittable[(size_t)Lg * d.F + f] = g1 > kNegInf ? 1 : 0;
       if (g0 > kNegInf && cand_better(g0, f, f, f0.g, f0.f, f0.i)) f0 = Cand{g0, f, f};
       if (g1 > kNegInf && cand_better(g1, f, f, f1.g, f1.f, f1.i)) f1 = Cand{g1, f, f};
     }
@@ -1925,11 +1923,16 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
             }
           }
           d.scan_out[sl_i * d.F + f] = si;
+          // the scanned leaf's children may split this feature only if it has a split
+          // (learner.rs:2003-2020)
+          if (scannable) d.splittable[(size_t)leaf2 * d.F + f] = si.gain > kNegInf ? 1 : 0;
         }
       }
     } else if (tid == 0) {
       d.scan_out[f] = d_split_none();
       d.scan_out[d.F + f] = d_split_none();
+      if (leaf_buildable(P.lsS)) d.splittable[(size_t)S * d.F + f] = 0;
+      if (Lg >= 0 && leaf_buildable(P.lsLg)) d.splittable[(size_t)Lg * d.F + f] = 0;
       if (f == 0) {
         d.scan_ok[0] = leaf_buildable(P.lsS) ? 1 : 0;
         d.scan_ok[1] = Lg >= 0 && leaf_buildable(P.lsLg) ? 1 : 0;

@@ -214,6 +214,7 @@ struct ObjDev {
 constexpr int64_t kRankSigmoidBins = 1 << 20;  // LambdarankNDCG::_sigmoid_bins
 void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof = nullptr,
                       const DeviceComm* comm = nullptr);
+void launch_fill_f64(double* p, int64_t n, double v, cudaStream_t st);
 
 // Per-iteration tree finish: shrinkage + score update + tree record.
 struct FinishDev {

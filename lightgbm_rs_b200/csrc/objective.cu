@@ -41,6 +41,12 @@ __device__ __forceinline__ int as_i8(double x) {
   return (int)x;
 }
 
+__global__ void k_fill_f64(double* p, int64_t n, double v) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
 __global__ void k_gh_reset(DevGhParams* p, const int32_t* stopped) {
   if (stopped && *stopped) return;
   p->max_abs_g_bits = 0u;
@@ -559,6 +565,12 @@ int num_sms_obj() {
 }
 
 }  // namespace
+
+void launch_fill_f64(double* p, int64_t n, double v, cudaStream_t st) {
+  if (n <= 0) return;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms_obj() * 8);
+  k_fill_f64<<<blocks, 256, 0, st>>>(p, n, v);
+}
 
 // With several devices: the scales come from the maxima over all devices' rows, and the
 // root sums are summed over devices (integers, so exact in any order).
