@@ -1444,13 +1444,19 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const CtlSmem& cs,
     const int32_t bf0 = ok0 ? f0.f : -1;
     const int32_t bf1 = ok1 ? f1.f : -1;
     if (lane == 0) {
-      o.si[0] = bf0 >= 0 ? so[bf0] : d_split_none();
+      if (bf0 >= 0)
+        o.si[0] = so[bf0];
+      else
+        o.si[0] = d_split_none();
       o.bf[0] = bf0;
       if (CAT)
         for (int k = 0; k < kCatWords; ++k)
           o.si_cat[0][k] = bf0 >= 0 ? sc[(size_t)bf0 * kCatWords + k] : 0u;
     } else if (lane == 1) {
-      o.si[1] = (Lg >= 0 && bf1 >= 0) ? so[d.F + bf1] : d_split_none();
+      if (Lg >= 0 && bf1 >= 0)
+        o.si[1] = so[d.F + bf1];
+      else
+        o.si[1] = d_split_none();
       o.bf[1] = bf1;
       if (CAT)
         for (int k = 0; k < kCatWords; ++k)
@@ -1473,24 +1479,25 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const CtlSmem& cs,
       // an old leaf that wins or runs up is one of the other leaves' best two
       const int sel = (find && bl == S) ? 0 : (find && bl == Lg) ? 1 : -1;
       const int oi = bl == cs.other.a.i ? 0 : 1;
-      const DevSplitInfo sp = sel == 0 ? o.si[0] : sel == 1 ? o.si[1] : cs.orec[oi];
-      o.split = sp;
+      // selected by address: no 72-byte temporaries
+      const DevSplitInfo* sp = sel == 0 ? &o.si[0] : sel == 1 ? &o.si[1] : &cs.orec[oi];
+      o.split = *sp;
       if (CAT)
         for (int k = 0; k < kCatWords; ++k)
           o.split_cat[k] = sel >= 0 ? o.si_cat[sel][k] : cs.ocat[oi][k];
       // accumulate the side the scan expects to be smaller (any side is exact)
-      o.build_left = sp.left_count <= sp.right_count ? 1 : 0;
+      o.build_left = sp->left_count <= sp->right_count ? 1 : 0;
       // the runner-up: the next pick chooses it unless a child of this split outranks it
       const Cand ru = top.b;
       if (d.lookahead && ru.i != 0x7fffffff && ru.g > 0.0) {
         const int32_t rl = ru.i;
         const int rs = (find && rl == S) ? 0 : (find && rl == Lg) ? 1 : -1;
         const int ri = rl == cs.other.a.i ? 0 : 1;
-        const DevSplitInfo rp = rs == 0 ? o.si[0] : rs == 1 ? o.si[1] : cs.orec[ri];
+        const DevSplitInfo* rp = rs == 0 ? &o.si[0] : rs == 1 ? &o.si[1] : &cs.orec[ri];
         o.la_leaf = rl;
         o.la_feature = ru.f;
-        o.la_split = rp;
-        o.la_build_left = rp.left_count <= rp.right_count ? 1 : 0;
+        o.la_split = *rp;
+        o.la_build_left = rp->left_count <= rp->right_count ? 1 : 0;
         if (CAT)
           for (int k = 0; k < kCatWords; ++k)
             o.la_cat[k] = rs >= 0 ? o.si_cat[rs][k] : cs.ocat[ri][k];
@@ -2911,7 +2918,7 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
     exchange(x);
   }
   for (int s = 0; s < d.L - 1; ++s) {
-    if (la_on && s >= 2) cudaStreamWaitEvent(st, las->done[s & 1], 0);
+    if (la_on && !prof && s >= 2) cudaStreamWaitEvent(st, las->done[s & 1], 0);
     {
       const GrowDev x = consumer(s);
       PROF_BEGIN(KC_FIXSCAN);
@@ -2926,7 +2933,9 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
     const int phase = s < d.L - 2 ? 1 : 2;
     const GrowDev x = producer(s + 1);
     const bool la_step = la_on && s <= d.L - 3;
-    if (la_step) cudaEventRecord(las->fork, st);
+    // A profiled sequence runs the look-ahead on the main stream, right after the control
+    // step: each launch's event span is then its own run, not its wait for free SMs.
+    if (la_step && !prof) cudaEventRecord(las->fork, st);
     // the main partition is launched before the look-ahead, so that its CTAs (which
     // mostly find the split already partitioned) are placed first
     if (x.fused) {
@@ -2944,18 +2953,19 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       build(x, phase);
     }
     if (la_step) {
-      cudaStreamWaitEvent(las->st, las->fork, 0);
-      const int pslot = prof ? prof->begin(las->st, KC_PARTITION) : -1;
+      const cudaStream_t lst = prof ? st : las->st;
+      if (!prof) cudaStreamWaitEvent(lst, las->fork, 0);
+      const int pslot = prof ? prof->begin(lst, KC_PARTITION) : -1;
       part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<las->blocks, kFpThreads,
                                                                 fused_partition_smem(),
-                                                                las->st>>>(x, 1, s & 1);
-      if (prof) prof->end(las->st, pslot);
-      cudaEventRecord(las->done[s & 1], las->st);
+                                                                lst>>>(x, 1, s & 1);
+      if (prof) prof->end(lst, pslot);
+      if (!prof) cudaEventRecord(las->done[s & 1], lst);
     }
     exchange(x);
   }
   // the last split may come from the last look-ahead, which also joins the second stream
-  if (la_on && d.L >= 3) cudaStreamWaitEvent(st, las->done[(d.L - 1) & 1], 0);
+  if (la_on && !prof && d.L >= 3) cudaStreamWaitEvent(st, las->done[(d.L - 1) & 1], 0);
   {
     PROF_BEGIN(KC_PREPARE);
     k_prepare<<<1, 32, 0, st>>>(consumer(d.L - 1), d.L - 1);
