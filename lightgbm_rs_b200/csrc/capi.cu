@@ -7,6 +7,7 @@
 #include <cstring>
 #include <cstdlib>
 #include <limits>
+#include <map>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -63,17 +64,75 @@ int fail(int code, const char* fmt, ...) {
                   __FILE__, __LINE__);                                                     \
   } while (0)
 
-// RAII device buffer.
+// Large device blocks are kept after release and handed out again for the same size on
+// the same device: a booster built after another was destroyed (the same data, the same
+// sizes) maps no new memory. A cudaMalloc of hundreds of MB after a cudaFree cost tens
+// of milliseconds. Releasing a kept block waits for the device, as cudaFree does.
+struct BlockCache {
+  std::mutex mu;
+  std::multimap<std::pair<int, size_t>, void*> blocks;
+  size_t bytes = 0;
+};
+
+BlockCache& block_cache() {
+  static BlockCache* c = new BlockCache;  // never destroyed: no teardown-order hazards
+  return *c;
+}
+
+constexpr size_t kCacheMinBytes = 1ull << 20;
+constexpr size_t kCacheMaxBytes = 16ull << 30;
+
+cudaError_t dev_malloc(void** p, size_t bytes, bool cacheable) {
+  if (cacheable && bytes >= kCacheMinBytes) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    BlockCache& c = block_cache();
+    std::lock_guard<std::mutex> lk(c.mu);
+    auto it = c.blocks.find({dev, bytes});
+    if (it != c.blocks.end()) {
+      *p = it->second;
+      c.bytes -= bytes;
+      c.blocks.erase(it);
+      return cudaSuccess;
+    }
+  }
+  return cudaMalloc(p, bytes);
+}
+
+void dev_free(void* p, size_t bytes, bool cacheable) {
+  if (cacheable && bytes >= kCacheMinBytes) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) == cudaSuccess && a.type == cudaMemoryTypeDevice) {
+      int prev = -1;
+      cudaGetDevice(&prev);
+      if (prev != a.device) cudaSetDevice(a.device);
+      const bool idle = cudaDeviceSynchronize() == cudaSuccess;
+      if (prev >= 0 && prev != a.device) cudaSetDevice(prev);
+      BlockCache& c = block_cache();
+      std::lock_guard<std::mutex> lk(c.mu);
+      if (idle && c.bytes + bytes <= kCacheMaxBytes) {
+        c.blocks.insert({{a.device, bytes}, p});
+        c.bytes += bytes;
+        return;
+      }
+    }
+    cudaGetLastError();
+  }
+  cudaFree(p);
+}
+
+// RAII device buffer (large blocks through the cache above unless `nocache`).
 template <typename T>
 struct DevBuf {
   T* p = nullptr;
   size_t n = 0;
+  bool nocache = false;  // memory shared with other processes (CUDA IPC)
   DevBuf() = default;
   DevBuf(const DevBuf&) = delete;
   DevBuf& operator=(const DevBuf&) = delete;
   ~DevBuf() { release(); }
   void release() {
-    if (p) cudaFree(p);
+    if (p) dev_free(p, n * sizeof(T), !nocache);
     p = nullptr;
     n = 0;
   }
@@ -81,7 +140,7 @@ struct DevBuf {
     release();
     n = count;
     if (count == 0) return cudaSuccess;
-    return cudaMalloc((void**)&p, count * sizeof(T));
+    return dev_malloc((void**)&p, count * sizeof(T), !nocache);
   }
 };
 
@@ -368,15 +427,14 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   CUDA_TRY(cudaMemset(cat_words.p, 0,
                       sizeof(uint32_t) * kCatWords * (2 * ds->num_features + 2 * L + 1)));
   CUDA_TRY(scan_ok.alloc(2));
-  CUDA_TRY(la.alloc(2));
-  CUDA_TRY(cudaMemset(la.p, 0, 2 * sizeof(LookAhead)));
-  CUDA_TRY(la_raw.alloc(2 * ((size_t)slot_len + 2)));
-  CUDA_TRY(la_partials.alloc((size_t)2 * kPrivateTiles * slot_len));
+  CUDA_TRY(la.alloc(kLaSlots));
+  CUDA_TRY(cudaMemset(la.p, 0, kLaSlots * sizeof(LookAhead)));
+  CUDA_TRY(la_raw.alloc(kLaSlots * ((size_t)slot_len + 2)));
+  CUDA_TRY(la_partials.alloc((size_t)kLaSlots * kPrivateTiles * slot_len));
   CUDA_TRY(la_status.alloc(max_tiles));
   CUDA_TRY(cudaStreamCreateWithFlags(&las.st, cudaStreamNonBlocking));
   CUDA_TRY(cudaEventCreateWithFlags(&las.fork, cudaEventDisableTiming));
-  CUDA_TRY(cudaEventCreateWithFlags(&las.done[0], cudaEventDisableTiming));
-  CUDA_TRY(cudaEventCreateWithFlags(&las.done[1], cudaEventDisableTiming));
+  for (cudaEvent_t& e : las.done) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   {
     const int sms = sm_count(device);
     las.blocks = std::max(sms / 2, sms - std::min(ds->num_features, sms));
@@ -1542,7 +1600,13 @@ int setup_peer_exchange(lgbm_b200_booster* b, lgbm_b200_comm* comm) {
   if (!want) return LGBM_B200_OK;
   cudaStream_t st = b->learner->stream;
   const size_t xs = (size_t)d.raw_len + 2;
-  const size_t words = 2 * xs + kMaxXRanks + 1;
+  // one region per rank, opened by the others: the two exchange accumulators, their
+  // flags and count, then the look-ahead slots, their flags and count
+  const size_t off_la = 2 * xs + kMaxXRanks + 1;
+  const size_t off_laflags = off_la + kLaSlots * xs;
+  const size_t off_laseq = off_laflags + kMaxXRanks;
+  const size_t words = off_laseq + 1;
+  b->xmem.nocache = true;
   CUDA_TRY(b->xmem.alloc(words));
   CUDA_TRY(cudaMemset(b->xmem.p, 0, words * 8));
   // every rank's IPC handle, in rank order (the all-gather moves 8-byte words)
@@ -1593,10 +1657,12 @@ int setup_peer_exchange(lgbm_b200_booster* b, lgbm_b200_comm* comm) {
   }
   long long wait_ms = 2000;
   if (const char* w = std::getenv("LGBM_B200_PEER_WAIT_MS")) wait_ms = std::max(1ll, atoll(w));
-  std::vector<void*> ptrs(2 * (size_t)R);
+  std::vector<void*> ptrs(4 * (size_t)R);
   for (int q = 0; q < R; ++q) {
     ptrs[q] = base[q];
     ptrs[R + q] = base[q] + 2 * xs;
+    ptrs[2 * R + q] = base[q] + off_la;
+    ptrs[3 * R + q] = base[q] + off_laflags;
   }
   CUDA_TRY(b->xptrs.alloc(ptrs.size()));
   CUDA_TRY(cudaMemcpy(b->xptrs.p, ptrs.data(), ptrs.size() * sizeof(void*),

@@ -143,6 +143,7 @@ struct GrowCtrl {
   int32_t pend_la;         // 0: the pending split's rows were partitioned by the main
                            // partition; 1 + k: by the look-ahead partition of slot k
   long long la_rows;       // parent rows streamed by look-ahead partitions (used or not)
+  unsigned long long la_base;  // look-ahead signals published before this tree
   int32_t la_runs;         // look-ahead partitions run in this tree
   int32_t la_hits;         // ... whose leaf was the next split
   DevSplitInfo split;

@@ -122,11 +122,10 @@ __device__ __forceinline__ long long raw_sum(const GrowDev& d, size_t idx) {
 // Waits (thread 0 of a consumer CTA) until every rank has published this rank's current
 // exchange count; false after wait_ns without it, or at once when a wait has already run
 // out (the caller records kErrSpinTimeout).
-__device__ __noinline__ bool x_wait_flags(const uint32_t* error, int xranks,
-                                          const unsigned long long* xflags,
-                                          const unsigned long long* xseq, long long wait_ns) {
+__device__ __noinline__ bool x_wait_target(const uint32_t* error, int xranks,
+                                           const unsigned long long* xflags,
+                                           unsigned long long seq, long long wait_ns) {
   if (*reinterpret_cast<const volatile uint32_t*>(error) & kErrSpinTimeout) return false;
-  const unsigned long long seq = *reinterpret_cast<const volatile unsigned long long*>(xseq);
   const unsigned long long t0 = global_ns();
   for (int r = 0; r < xranks; ++r) {
     while (ld_acquire_sys(xflags + r) < seq) {
@@ -140,7 +139,31 @@ __device__ __noinline__ bool x_wait_flags(const uint32_t* error, int xranks,
 template <bool PEER>
 __device__ __forceinline__ bool x_wait(const GrowDev& d) {
   if (!PEER) return true;
-  return x_wait_flags(&d.ctrl->error, d.xranks, d.xflags, d.xseq, d.xwait_ns);
+  return x_wait_target(&d.ctrl->error, d.xranks, d.xflags,
+                       *reinterpret_cast<const volatile unsigned long long*>(d.xseq),
+                       d.xwait_ns);
+}
+
+// Cell idx of look-ahead slot `slot`: this device's, or the sum over the ranks.
+template <bool PEER>
+__device__ __forceinline__ long long la_sum(const GrowDev& d, int slot, size_t idx) {
+  const size_t off = (size_t)slot * ((size_t)d.raw_len + 2) + idx;
+  if (!PEER) return __ldcg(d.la_raw + off);
+  long long v = 0;
+  for (int r = 0; r < d.xranks; ++r) v += ld_relaxed_sys(d.la_xbuf[r] + off);
+  return v;
+}
+
+// With several devices, a pending split partitioned by the look-ahead of step s - 2 (the
+// (s - 1)-th look-ahead signal of the tree) is read from every rank's slot: wait for all
+// ranks' signals. False after the wait limit.
+template <bool PEER>
+__device__ __forceinline__ bool la_wait(const GrowDev& d, int s) {
+  if (!PEER || !d.lookahead) return true;
+  const GrowCtrl* c = d.ctrl;
+  if (!(c->pending && c->pend_la)) return true;
+  const unsigned long long want = c->la_base + (unsigned long long)(s - 1);
+  return x_wait_target(&c->error, d.xranks, d.la_flags, want, d.xwait_ns);
 }
 
 // After a producer kernel: publish the next exchange count into every rank's flags
@@ -155,6 +178,19 @@ __global__ void k_xsignal(GrowDev d) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(seq) : "memory");
   }
   if (lane == 0) *d.xseq = seq;
+}
+
+// After a look-ahead kernel: the same publication for the look-ahead slots.
+__global__ void k_lasignal(GrowDev d) {
+  const int lane = threadIdx.x;
+  const unsigned long long seq = *d.la_seq + 1;
+  __syncwarp();
+  __threadfence_system();
+  if (lane < d.xranks) {
+    unsigned long long* f = d.peer_la_flags[lane] + d.xrank;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(seq) : "memory");
+  }
+  if (lane == 0) *d.la_seq = seq;
 }
 
 // Decoding of the raw integer accumulators into f64 histogram cells. For the
@@ -888,9 +924,9 @@ __global__ void k_tree_init(GrowDev d) {
     for (size_t i = gtid; i < 2 * ((size_t)d.raw_len + 2); i += gsz) d.xlocal[i] = 0;
   // look-ahead slots: empty accumulators, no recorded leaf, no stale status words
   if (d.lookahead) {
-    for (size_t i = gtid; i < 2 * ((size_t)d.raw_len + 2); i += gsz) d.la_raw[i] = 0;
+    for (size_t i = gtid; i < kLaSlots * ((size_t)d.raw_len + 2); i += gsz) d.la_raw[i] = 0;
     for (int i = gtid; i < d.max_tiles; i += gsz) d.la_status[i] = 0ull;
-    if (gtid < 2) d.la[gtid] = LookAhead{};
+    if (gtid < kLaSlots) d.la[gtid] = LookAhead{};
   }
   if (gtid == 0) {
     const uint32_t epoch = c->epoch;
@@ -899,6 +935,8 @@ __global__ void k_tree_init(GrowDev d) {
     *c = z;
     c->epoch = epoch;
     c->error = err;
+    // the tree's look-ahead signals count from here (every earlier one has been sent)
+    c->la_base = (d.lookahead && d.xranks > 1) ? *d.la_seq : 0ull;
     c->num_leaves = 1;
     c->left_leaf = 0;
     c->right_leaf = -1;
@@ -977,13 +1015,15 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   P.priv_tiles = 0;
   P.acc_slot = -1;
   P.la_clear = -1;
-  // Look-ahead slot s % 2 was filled by the look-ahead kernel of step s - 2, which has
-  // finished: count it, and consume it when step s - 1 picked its leaf.
+  // Look-aheads of this tree that have finished (this step waited for the one of step
+  // s - 2): the one of step s - 3 is counted and its slot cleared here (every rank has
+  // consumed it by now); the one of step s - 2 is consumed when step s - 1 picked its leaf
+  // (the final step also counts it: no later step will).
   const LookAhead* lar = nullptr;
   if (d.lookahead) {
-    P.la_clear = s & 1;
-    if (s >= 2) {
-      const LookAhead& r = d.la[s & 1];
+    constexpr int M = kLaSlots - 1;
+    P.la_clear = (s + 1) & M;
+    auto count_la = [&](const LookAhead& r) {
       if (r.active && r.ran) {
         c.la_runs += 1;
         c.la_rows += r.rows;
@@ -992,15 +1032,18 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
         c.error |= kErrSpinTimeout;
         c.done = 1;
       }
-      if (c.pending && c.pend_la == 1 + (s & 1)) {
-        lar = &r;
-        P.acc_slot = s & 1;
-        c.la_hits += 1;
-        c.rows_parted += r.rows;
-        if (r.build) {
-          c.rows_built += r.built;
-          c.num_builds += 1;
-        }
+    };
+    if (s >= 3) count_la(d.la[(s + 1) & M]);
+    if (s >= 2 && s == d.L - 1) count_la(d.la[(s + 2) & M]);
+    if (s >= 2 && c.pending && c.pend_la == 1 + ((s + 2) & M)) {
+      const LookAhead& r = d.la[(s + 2) & M];
+      lar = &r;
+      P.acc_slot = (s + 2) & M;
+      c.la_hits += 1;
+      c.rows_parted += r.rows;
+      if (r.build) {
+        c.rows_built += r.built;
+        c.num_builds += 1;
       }
     }
   }
@@ -1021,8 +1064,10 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
     const double old_value = d.t_leaf_value[leaf];
     const int32_t depth = d.t_leaf_depth[leaf];
     const int32_t mt = d.feat[f].missing_type;
-    // a look-ahead runs on one device only: its left rows are all the left rows
-    const long long lcg_raw = lar ? (long long)lar->left_total : raw_sum<PEER>(d, (size_t)d.raw_len);
+    // the look-ahead's left rows: this device's, summed over the devices with several
+    const long long lcg_raw = lar ? (PEER ? la_sum<PEER>(d, P.acc_slot, (size_t)d.raw_len)
+                                          : (long long)lar->left_total)
+                                  : raw_sum<PEER>(d, (size_t)d.raw_len);
     slot_left = d.slot_of_leaf[leaf];
     const int32_t parent_right = parent >= 0 ? d.t_right[parent] : 0;
     const int32_t lc = lar ? lar->left_total : c.part_left_total;
@@ -1251,7 +1296,7 @@ __global__ void k_prepare(GrowDev d, int s) {
   if (threadIdx.x != 0) return;
   Prep P;
   if (d.xranks > 1) {
-    if (!x_wait<true>(d)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
+    if (!x_wait<true>(d) || !la_wait<true>(d, s)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
     prep_compute<true>(d, s, P);
   } else {
     prep_compute<false>(d, s, P);
@@ -1742,8 +1787,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
   const int nt = P.priv_tiles;
   const int as = P.acc_slot;
   if (mine) {
-    if (nt == 0) bv = as >= 0 ? __ldcg(d.la_raw + (size_t)as * (d.raw_len + 2) + cell)
-                              : raw_sum<PEER>(d, cell);
+    if (nt == 0) bv = as >= 0 ? la_sum<PEER>(d, as, cell) : raw_sum<PEER>(d, cell);
     if (P.live && P.applied) pv = __ldcg(d.rawpool + (size_t)P.leaf * d.raw_len + cell);
     if (P.live && Lg >= 0) parent = d.pool[(size_t)P.lslot * d.slot_len + ft.slot_off + tid];
   }
@@ -1773,9 +1817,10 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
     if (tid < 512) tsum += xs[tid];
   }
   if (mine && nt > 0) bv = tsum;
-  // clear the accumulator for the next partition (a look-ahead hit left it untouched),
-  // and this step's look-ahead slot for its next look-ahead kernel
-  if (mine && P.priv_tiles == 0 && P.acc_slot < 0) d.raw[cell] = 0;
+  // clear the accumulator for the next partition (on one device a look-ahead hit left it
+  // untouched; with several, `raw` is the other exchange buffer, read by every rank at the
+  // previous step), and this step's look-ahead slot for its next look-ahead kernel
+  if (mine && P.priv_tiles == 0 && (PEER || P.acc_slot < 0)) d.raw[cell] = 0;
   if (mine && P.la_clear >= 0) d.la_raw[(size_t)P.la_clear * (d.raw_len + 2) + cell] = 0;
   if (P.live) {
     const bool used = used_f;
@@ -1964,7 +2009,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   const int warp = tid >> 5;
   const int nparts = min(d.F, (int)gridDim.x);
   if (tid == 0) {
-    if (!x_wait<PEER>(d)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
+    if (!x_wait<PEER>(d) || !la_wait<PEER>(d, s)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
     prep_compute<PEER>(d, s, cs.prep);
   } else if (warp == 1) {
     // the best two of the leaves this step leaves alone (final before the step starts;
@@ -2026,7 +2071,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     } else if (lane == 2) {
       int32_t lp = -1;
       if (d.lookahead && s >= 1) {
-        const LookAhead& q = d.la[(s - 1) & 1];
+        const LookAhead& q = d.la[(s - 1) & (kLaSlots - 1)];
         if (q.active) lp = q.leaf;
       }
       cs.la_prev = lp;
@@ -2093,7 +2138,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
         // the previous step's look-ahead partitioned this leaf already (it may still be
         // running; the step that applies the split waits for it)
         if (d.lookahead && s >= 1 && cs.la_prev == cs.pick.leaf)
-          c.pend_la = 1 + ((s - 1) & 1);
+          c.pend_la = 1 + ((s - 1) & (kLaSlots - 1));
       }
     }
     c.error |= cs.err;
@@ -2113,7 +2158,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
         if (CAT)
           for (int k = 0; k < kCatWords; ++k) r.cat[k] = cs.pick.la_cat[k];
       }
-      d.la[s & 1] = r;
+      d.la[s & (kLaSlots - 1)] = r;
     }
     *d.ctrl = c;
   }
@@ -2868,7 +2913,8 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
   // Look-ahead partitions on the second stream (one device, fused partition): the kernel
   // of step s starts after control step s and must end before control step s + 2, which
   // consumes or clears its slot. The kernels see the flag only when they are launched.
-  const bool la_on = d_in.lookahead && las && d_in.fused && d_in.xranks <= 1 && !comm;
+  const bool la_on = d_in.lookahead && las && d_in.fused &&
+                     (d_in.xranks > 1 ? d_in.la_xbuf != nullptr : !comm);
   GrowDev d = d_in;
   d.lookahead = la_on ? 1 : 0;
   {
@@ -2918,7 +2964,7 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
     exchange(x);
   }
   for (int s = 0; s < d.L - 1; ++s) {
-    if (la_on && !prof && s >= 2) cudaStreamWaitEvent(st, las->done[s & 1], 0);
+    if (la_on && !prof && s >= 2) cudaStreamWaitEvent(st, las->done[(s - 2) & (kLaSlots - 1)], 0);
     {
       const GrowDev x = consumer(s);
       PROF_BEGIN(KC_FIXSCAN);
@@ -2958,14 +3004,16 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       const int pslot = prof ? prof->begin(lst, KC_PARTITION) : -1;
       part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<las->blocks, kFpThreads,
                                                                 fused_partition_smem(),
-                                                                lst>>>(x, 1, s & 1);
+                                                                lst>>>(x, 1, s & (kLaSlots - 1));
       if (prof) prof->end(lst, pslot);
-      if (!prof) cudaEventRecord(las->done[s & 1], lst);
+      if (px) k_lasignal<<<1, 32, 0, lst>>>(x);  // every rank may read the slot now
+      if (!prof) cudaEventRecord(las->done[s & (kLaSlots - 1)], lst);
     }
     exchange(x);
   }
   // the last split may come from the last look-ahead, which also joins the second stream
-  if (la_on && !prof && d.L >= 3) cudaStreamWaitEvent(st, las->done[(d.L - 1) & 1], 0);
+  if (la_on && !prof && d.L >= 3)
+    cudaStreamWaitEvent(st, las->done[(d.L - 3) & (kLaSlots - 1)], 0);
   {
     PROF_BEGIN(KC_PREPARE);
     k_prepare<<<1, 32, 0, st>>>(consumer(d.L - 1), d.L - 1);

@@ -28,6 +28,10 @@ constexpr int kQ4MaxCells = 7168;
 // Rows per tile of the row-partition kernel (one look-back status word per tile).
 constexpr int kPartitionTileRows = 2048;
 
+// Look-ahead slots: the kernel of step s uses slot s % kLaSlots. Step s + 2 may consume
+// it and step s + 3 clears it; with several devices every rank has read it by then.
+constexpr int kLaSlots = 4;
+
 // Splits of up to this many partition tiles store per-tile partial histograms.
 constexpr int kMaxPrivateTiles = 16;
 
@@ -131,15 +135,21 @@ struct GrowDev {
   unsigned long long* const* peer_xflags;     // [xranks] each rank's flags (device)
   unsigned long long* xseq;                   // exchanges this rank has published
   long long xwait_ns;                         // wait limit, then the spin-timeout error
-  // Look-ahead partitions (one device, fused partition): two slots, control step s
-  // records slot s % 2 and its look-ahead kernel fills it; control step s + 2 consumes
-  // it (when step s + 1 picked the recorded leaf) and clears it.
+  // Look-ahead partitions (fused partition): control step s records slot s % kLaSlots and
+  // its look-ahead kernel fills it; control step s + 2 consumes it (when step s + 1 picked
+  // the recorded leaf) and step s + 3 clears it. With the peer exchange (xranks > 1) the
+  // accumulators are exchanged like the main one: each look-ahead kernel is followed by a
+  // signal (la_seq) into every rank's la_flags, and the consumer sums all ranks' slot.
   int32_t lookahead;
   int32_t _lapad;
-  LookAhead* la;                  // [2]
-  long long* la_raw;              // [2][raw_len + 2] accumulated child, left-row count
-  long long* la_partials;         // [2][private_tiles][raw_len]
+  LookAhead* la;                  // [kLaSlots]
+  long long* la_raw;              // [kLaSlots][raw_len + 2] accumulated child, left-row count
+  long long* la_partials;         // [kLaSlots][private_tiles][raw_len]
   unsigned long long* la_status;  // [max_tiles] look-back words of the look-ahead kernel
+  long long* const* la_xbuf;                // [xranks] each rank's la_raw (device)
+  unsigned long long* la_flags;             // this rank's look-ahead flags, one per rank
+  unsigned long long* const* peer_la_flags; // [xranks] each rank's la_flags (device)
+  unsigned long long* la_seq;               // look-ahead signals this rank has published
   // gradients
   int32_t gh_mode;
   int32_t q4_shift;  // quantized build: log2 bin stride
@@ -174,7 +184,7 @@ struct DeviceComm {
 struct LookAheadStreams {
   cudaStream_t st;
   cudaEvent_t fork;     // after control step s, on the main stream
-  cudaEvent_t done[2];  // after the look-ahead kernel of step s, slot s % 2
+  cudaEvent_t done[kLaSlots];  // after the look-ahead kernel of step s, slot s % kLaSlots
   int blocks;           // CTAs of a look-ahead kernel (the control step keeps the rest)
 };
 
