@@ -1676,6 +1676,13 @@ int setup_peer_exchange(lgbm_b200_booster* b, lgbm_b200_comm* comm) {
   d.xflags = b->xmem.p + 2 * xs;
   d.xseq = b->xmem.p + 2 * xs + kMaxXRanks;
   d.xwait_ns = wait_ms * 1000000ll;
+  if (d.lookahead) {  // the look-ahead slots live in the exchanged region
+    d.la_raw = reinterpret_cast<long long*>(b->xmem.p + off_la);
+    d.la_xbuf = reinterpret_cast<long long* const*>(b->xptrs.p + 2 * R);
+    d.peer_la_flags = reinterpret_cast<unsigned long long* const*>(b->xptrs.p + 3 * R);
+    d.la_flags = b->xmem.p + off_laflags;
+    d.la_seq = b->xmem.p + off_laseq;
+  }
   return LGBM_B200_OK;
 }
 

@@ -2,7 +2,9 @@
 
 Quantized gradients: trees and scores of every rank must be bit-identical to training
 on all rows on one GPU. f32 gradients: same tree structure, scores within 1e-9.
-Needs at least 2 GPUs; never runs two ranks on one GPU.
+With 255 leaves most splits come from look-ahead partitions, whose child histograms are
+exchanged over peer memory like the main ones; the last iteration is profiled and must
+show them used. Needs at least 2 GPUs; never runs two ranks on one GPU.
 """
 
 import multiprocessing as mp
@@ -27,7 +29,7 @@ def _data():
     return lgb.Dataset(X, y, dict(PARAMS))  # host binning only, deterministic
 
 
-def _worker(rank, world, uid, quantized, q):
+def _worker(rank, world, uid, quantized, leaves, q):
     try:
         os.environ["NCCL_NVLS_ENABLE"] = "0"
         import sys
@@ -37,20 +39,22 @@ def _worker(rank, world, uid, quantized, q):
 
         full = _data()
         b, e = D.shard_range(full.num_data, world, rank)
-        p = dict(PARAMS, device=rank, use_quantized_grad=quantized, num_grad_quant_bins=4)
+        p = dict(PARAMS, device=rank, use_quantized_grad=quantized, num_grad_quant_bins=4,
+                 num_leaves=leaves)
         shard = lgb.Dataset(bins=full.bins[:, b:e], mappers=full.mappers,
                             label=full.label[b:e], params=p)
         comm = D.Communicator(rank, world, rank, uid)
-        booster = lgb.train(p, shard, num_boost_round=ITERS, comm=comm)
-        q.put((rank, booster.trees(), booster.train_scores()))
+        booster = lgb.train(p, shard, num_boost_round=ITERS - 1, comm=comm)
+        _, counts = booster.profile_iteration()  # the last iteration, with counters
+        q.put((rank, booster.trees(), booster.train_scores(), counts))
         del booster
         comm.close()
     except Exception as ex:
         q.put((rank, "error", repr(ex)))
 
 
-@pytest.mark.parametrize("quantized", [True, False])
-def test_two_gpus_match_one(quantized):
+@pytest.mark.parametrize("quantized,leaves", [(True, 31), (False, 31), (True, 255)])
+def test_two_gpus_match_one(quantized, leaves):
     import lightgbm_rs_b200 as lgb
     from lightgbm_rs_b200 import distributed as D
 
@@ -59,7 +63,8 @@ def test_two_gpus_match_one(quantized):
     uid = D.unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, uid, quantized, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, uid, quantized, leaves, q))
+             for r in range(2)]
     for p in procs:
         p.start()
     out = {}
@@ -74,8 +79,12 @@ def test_two_gpus_match_one(quantized):
                 p.kill()
     for r in range(2):
         assert out[r][1] != "error", out[r]
+    if leaves == 255:
+        for r in range(2):
+            c = out[r][3]
+            assert c["lookahead_runs"] > 0 and c["lookahead_hits"] > 0, (r, c)
     full = _data()
-    p = dict(PARAMS, use_quantized_grad=quantized, num_grad_quant_bins=4)
+    p = dict(PARAMS, use_quantized_grad=quantized, num_grad_quant_bins=4, num_leaves=leaves)
     ref = lgb.train(p, full, num_boost_round=ITERS)
     want_trees, want_scores = ref.trees(), ref.train_scores()
     scores = np.concatenate([out[0][2], out[1][2]])
