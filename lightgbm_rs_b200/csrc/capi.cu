@@ -264,7 +264,7 @@ struct lgbm_b200_learner {
   DevBuf<DevFeatureGroup> d_groups;
   DevBuf<GrowCtrl> ctrl;
   DevBuf<int32_t> leaf_i32;  // leaf_begin, leaf_count, leaf_buf, slot_of_leaf, best_feature,
-                             // leaf_count_g
+                             // leaf_count_g, leaf_is_right
   DevBuf<DevLeafSplits> ls;
   DevBuf<DevSplitInfo> best;
   DevBuf<uint8_t> splittable;
@@ -405,7 +405,7 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   CUDA_TRY(ctrl.alloc(1));
   CUDA_TRY(cudaMemset(ctrl.p, 0, sizeof(GrowCtrl)));
-  CUDA_TRY(leaf_i32.alloc((size_t)6 * L));
+  CUDA_TRY(leaf_i32.alloc((size_t)7 * L));
   CUDA_TRY(ls.alloc(L));
   CUDA_TRY(best.alloc(L));
   CUDA_TRY(splittable.alloc((size_t)L * ds->num_features));
@@ -457,6 +457,7 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.slot_of_leaf = leaf_i32.p + 3 * L;
   d.best_feature = leaf_i32.p + 4 * L;
   d.leaf_count_g = leaf_i32.p + 5 * L;
+  d.leaf_is_right = leaf_i32.p + 6 * L;
   d.ls = ls.p;
   d.best = best.p;
   d.splittable = splittable.p;

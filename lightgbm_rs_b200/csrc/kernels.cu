@@ -914,6 +914,7 @@ __global__ void k_tree_init(GrowDev d) {
     d.t_internal_count[l] = 0;
     d.t_leaf_depth[l] = 0;
     d.t_leaf_parent[l] = 0;
+    d.leaf_is_right[l] = 0;
   }
   const size_t nsp = (size_t)d.L * d.F;
   for (size_t i = gtid; i < nsp; i += gsz) d.splittable[i] = 1;
@@ -1069,7 +1070,9 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
                                           : (long long)lar->left_total)
                                   : raw_sum<PEER>(d, (size_t)d.raw_len);
     slot_left = d.slot_of_leaf[leaf];
-    const int32_t parent_right = parent >= 0 ? d.t_right[parent] : 0;
+    // read with the leaf's other fields (the parent's child pointer would be a
+    // dependent round trip)
+    const int32_t is_right = d.leaf_is_right[leaf];
     const int32_t lc = lar ? lar->left_total : c.part_left_total;
     const int32_t lcg = (int32_t)lcg_raw;
     P.applied = 1;
@@ -1077,7 +1080,7 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
     P.nr = nr;
     P.node = nr - 1;
     P.parent = parent;
-    P.parent_is_right = parent >= 0 && parent_right == ~leaf;
+    P.parent_is_right = parent >= 0 && is_right != 0;
     P.lc = lc;
     P.rc = cnt - lc;
     P.lcg = lcg;
@@ -1276,6 +1279,8 @@ __device__ void prep_commit(const GrowDev& d, const Prep& P) {
     d.t_leaf_depth[leaf] = P.depth + 1;
     d.t_leaf_parent[leaf] = node;
     d.t_leaf_parent[nr] = node;
+    d.leaf_is_right[leaf] = 0;  // the split leaf keeps its id as the left child
+    d.leaf_is_right[nr] = 1;
     d.ls[leaf] = P.lsL;
     d.ls[nr] = P.lsR;
     d.best[leaf] = d_split_none();

@@ -79,6 +79,7 @@ struct GrowDev {
   int32_t* leaf_begin;
   int32_t* leaf_count;    // rows of the leaf on this device
   int32_t* leaf_count_g;  // rows of the leaf on all devices
+  int32_t* leaf_is_right;  // the leaf is its parent node's right child
   int32_t* leaf_buf;  // 0/1 = index buffer, 2 = identity (root)
   int32_t* slot_of_leaf;
   DevLeafSplits* ls;
