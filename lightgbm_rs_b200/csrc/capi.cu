@@ -685,6 +685,17 @@ struct lgbm_b200_booster {
   const DeviceComm* dcomm() const { return comm ? &comm->dev : nullptr; }
 
   int ensure_capacity(int32_t need);
+  // Host copy of the first snap_n recorded trees, made by the first get_tree after
+  // training (one copy per record field instead of a dozen per tree); training drops it.
+  int32_t snap_n = -1;
+  std::vector<int32_t> snap_i32;  // num_leaves[n] | left | right | split_feature | leaf_count |
+                                  // internal_count, [n][L] each
+  std::vector<uint32_t> snap_thr;
+  std::vector<float> snap_gain;
+  std::vector<int8_t> snap_dec;
+  std::vector<double> snap_f64;   // leaf_value | leaf_weight | internal_value
+  std::vector<uint32_t> snap_cat;
+  int snapshot(int32_t n);
   void destroy_graph() {
     if (graph_exec) cudaGraphExecDestroy(graph_exec);
     if (graph) cudaGraphDestroy(graph);
@@ -702,8 +713,38 @@ struct lgbm_b200_booster {
   }
 };
 
+int lgbm_b200_booster::snapshot(int32_t n) {
+  const size_t L = learner->L, N = (size_t)n;
+  snap_i32.resize(N + 5 * N * L);
+  snap_thr.resize(N * L);
+  snap_gain.resize(N * L);
+  snap_dec.resize(N * L);
+  snap_f64.resize(3 * N * L);
+  snap_cat.resize(N * L * kCatWords);
+  if (n > 0) {
+    CUDA_TRY(cudaMemcpy(snap_i32.data(), fin.rec_num_leaves, N * 4, cudaMemcpyDeviceToHost));
+    const int32_t* i32src[5] = {fin.rec_left, fin.rec_right, fin.rec_split_feature,
+                                fin.rec_leaf_count, fin.rec_internal_count};
+    for (int a = 0; a < 5; ++a)
+      CUDA_TRY(cudaMemcpy(snap_i32.data() + N + a * N * L, i32src[a], N * L * 4,
+                          cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(snap_thr.data(), fin.rec_threshold, N * L * 4, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(snap_gain.data(), fin.rec_split_gain, N * L * 4, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(snap_dec.data(), fin.rec_decision, N * L, cudaMemcpyDeviceToHost));
+    const double* f64src[3] = {fin.rec_leaf_value, fin.rec_leaf_weight, fin.rec_internal_value};
+    for (int a = 0; a < 3; ++a)
+      CUDA_TRY(cudaMemcpy(snap_f64.data() + a * N * L, f64src[a], N * L * 8,
+                          cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(snap_cat.data(), fin.rec_cat, N * L * kCatWords * 4,
+                        cudaMemcpyDeviceToHost));
+  }
+  snap_n = n;
+  return LGBM_B200_OK;
+}
+
 int lgbm_b200_booster::ensure_capacity(int32_t need) {
   if (need <= capacity) return LGBM_B200_OK;
+  snap_n = -1;
   int32_t cap = std::max(need, capacity * 2);
   const int L = learner->L;
   // grow while keeping already recorded trees
@@ -1942,6 +1983,7 @@ int lgbm_b200_booster_destroy(lgbm_b200_booster* b) {
 
 int lgbm_b200_booster_train(lgbm_b200_booster* b, int32_t num_iterations, int32_t* done_out) {
   if (!b || num_iterations < 0) return fail(LGBM_B200_INVALID_ARGUMENT, "booster_train: args");
+  b->snap_n = -1;
   DeviceGuard g(b->ds->device);
   int32_t state[2];
   CUDA_TRY(cudaMemcpy(state, b->state.p, 8, cudaMemcpyDeviceToHost));
@@ -1996,29 +2038,32 @@ int lgbm_b200_booster_get_tree(lgbm_b200_booster* b, int32_t index, lgbm_b200_tr
   int rc = lgbm_b200_booster_num_trees(b, &n);
   if (rc) return rc;
   if (index < 0 || index >= n) return fail(LGBM_B200_INVALID_ARGUMENT, "tree %d of %d", index, n);
-  const size_t L = b->learner->L, cap = b->capacity, it = index;
-  int32_t nl;
-  CUDA_TRY(cudaMemcpy(&nl, b->fin.rec_num_leaves + it, 4, cudaMemcpyDeviceToHost));
+  DeviceGuard g(b->learner->device);
+  if (b->snap_n != n) {
+    rc = b->snapshot(n);
+    if (rc) return rc;
+  }
+  const size_t L = b->learner->L, N = (size_t)n, it = index;
+  const int32_t nl = b->snap_i32[it];
   if (out->max_leaves < nl) return fail(LGBM_B200_LENGTH_MISMATCH, "tree_out too small");
   out->num_leaves = nl;
-  auto cp = [&](void* dst, const void* src, size_t bytes) -> cudaError_t {
-    if (!dst || bytes == 0) return cudaSuccess;
-    return cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost);
+  auto cp = [&](void* dst, const void* src, size_t bytes) {
+    if (dst && bytes) std::memcpy(dst, src, bytes);
   };
   const size_t ni = nl > 1 ? nl - 1 : 0;
-  CUDA_TRY(cp(out->left_child, b->fin.rec_left + it * L, ni * 4));
-  CUDA_TRY(cp(out->right_child, b->fin.rec_right + it * L, ni * 4));
-  CUDA_TRY(cp(out->split_feature, b->fin.rec_split_feature + it * L, ni * 4));
-  CUDA_TRY(cp(out->internal_count, b->fin.rec_internal_count + it * L, ni * 4));
-  CUDA_TRY(cp(out->threshold_bin, b->fin.rec_threshold + it * L, ni * 4));
-  CUDA_TRY(cp(out->split_gain, b->fin.rec_split_gain + it * L, ni * 4));
-  CUDA_TRY(cp(out->decision_type, b->fin.rec_decision + it * L, ni));
-  CUDA_TRY(cp(out->internal_value, b->fin.rec_internal_value + it * L, ni * 8));
-  CUDA_TRY(cp(out->leaf_value, b->fin.rec_leaf_value + it * L, nl * 8));
-  CUDA_TRY(cp(out->leaf_weight, b->fin.rec_leaf_weight + it * L, nl * 8));
-  CUDA_TRY(cp(out->leaf_count, b->fin.rec_leaf_count + it * L, nl * 4));
-  CUDA_TRY(cp(out->cat_bins, b->fin.rec_cat + it * L * kCatWords, ni * kCatWords * 4));
-  (void)cap;
+  const int32_t* i32 = b->snap_i32.data() + N;
+  cp(out->left_child, i32 + it * L, ni * 4);
+  cp(out->right_child, i32 + N * L + it * L, ni * 4);
+  cp(out->split_feature, i32 + 2 * N * L + it * L, ni * 4);
+  cp(out->leaf_count, i32 + 3 * N * L + it * L, (size_t)nl * 4);
+  cp(out->internal_count, i32 + 4 * N * L + it * L, ni * 4);
+  cp(out->threshold_bin, b->snap_thr.data() + it * L, ni * 4);
+  cp(out->split_gain, b->snap_gain.data() + it * L, ni * 4);
+  cp(out->decision_type, b->snap_dec.data() + it * L, ni);
+  cp(out->leaf_value, b->snap_f64.data() + it * L, (size_t)nl * 8);
+  cp(out->leaf_weight, b->snap_f64.data() + N * L + it * L, (size_t)nl * 8);
+  cp(out->internal_value, b->snap_f64.data() + 2 * N * L + it * L, ni * 8);
+  cp(out->cat_bins, b->snap_cat.data() + it * L * kCatWords, ni * kCatWords * 4);
   return LGBM_B200_OK;
 }
 
@@ -2072,6 +2117,7 @@ int lgbm_b200_booster_profile_launches(const lgbm_b200_booster* b, int32_t cap,
 int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
                                         int64_t* counts_out) {
   if (!b || !ms_out || !counts_out) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
+  b->snap_n = -1;
   DeviceGuard g(b->ds->device);
   int32_t state[2];
   CUDA_TRY(cudaMemcpy(state, b->state.p, 8, cudaMemcpyDeviceToHost));
