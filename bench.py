@@ -7,20 +7,31 @@ Default gradients: use_quantized_grad with 4 quantization bins (`--grad f32` for
 f32-gradient variant). One step = one boosting iteration (gradients, quantization,
 one tree, shrinkage, score update) over all rows.
 
+`--workload c2`: 400,000 rows x 2,000 features ~ U(-1,1), max_bin=63, 127 leaves.
 `--workload c3`: 2,000,000 rows, 90 numeric features with 10 % NaN and 10 categorical
 features, L2 regression, 63 leaves. `--workload c4`: lambdarank over 20,000 queries
-(about 473k rows) x 700 sparse features, 255 leaves. Both are seeded synthetic
-stand-ins with the configurations' shapes (lightgbm_rs_b200/synthetic.py).
+(about 473k rows) x 700 sparse features, 255 leaves. All are seeded synthetic stand-ins
+with the configurations' shapes (lightgbm_rs_b200/synthetic.py).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload c1|c3|c4] [--grad quantized|f32]
+                  [--workload c1|c2|c3|c4] [--grad quantized|f32]
 
-Prints ONE JSON line on rank 0. `--impl reference` times the reference CPU learner
-(the C++ restatement in oracle/, the reference's Rust crates cannot be built here)
-on the host cores.
+Prints ONE JSON line on rank 0. Besides the timed steps, the default line carries:
+  parity    the first trees and the scores after them, grown on the device and by the
+            CPU oracle from the same binned data, compared bit for bit (N = 1);
+  digest    SHA-256 of every tree the timed booster grew (equal for every N);
+  f32       the same workload with f32 gradients;
+  full      a full-length run (C1: all 500 iterations) with its tree digest;
+  roofline  per-kernel device spans of the pipelined step (%globaltimer stamps in a
+            graph of the same launch sequence) against the algorithmic bytes.
+`--impl reference` times the reference CPU learner (the C++ restatement in oracle/, the
+reference's Rust crates cannot be built here) on the host cores; that process bins its
+data with the oracle's own BinMapper restatement and never loads the product library.
 """
 
 import argparse
+import hashlib
+import importlib.util
 import json
 import os
 import statistics
@@ -35,18 +46,32 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 LEARNING_RATE = 0.1
+PARITY_TREES = 3
 
-# name -> rows, features, leaves, min_data_in_leaf, objective, description
+# name -> rows, features, leaves, min_data_in_leaf, max_bin, objective, full-length
+# iterations, description
 WORKLOADS = {
-    "c1": dict(rows=10_500_000, features=28, leaves=255, min_data=100, objective="binary",
+    "c1": dict(rows=10_500_000, features=28, leaves=255, min_data=100, max_bin=255,
+               objective="binary", iterations=500,
                desc="C1 binary {rows}x28 num_leaves=255 min_data_in_leaf=100 max_bin=255"),
-    "c3": dict(rows=2_000_000, features=100, leaves=63, min_data=20, objective="regression",
+    "c2": dict(rows=400_000, features=2000, leaves=127, min_data=20, max_bin=63,
+               objective="binary", iterations=200,
+               desc="C2 binary {rows}x2000 U(-1,1) num_leaves=127 max_bin=63"),
+    "c3": dict(rows=2_000_000, features=100, leaves=63, min_data=20, max_bin=255,
+               objective="regression", iterations=300,
                desc="C3 l2 {rows}x100 (90 numeric, 10% NaN; 10 categorical, 16-240 "
                     "categories, Zipf 1.2) num_leaves=63 max_bin=255"),
-    "c4": dict(rows=473_000, features=700, leaves=255, min_data=20, objective="lambdarank",
+    "c4": dict(rows=473_000, features=700, leaves=255, min_data=20, max_bin=255,
+               objective="lambdarank", iterations=300,
                desc="C4 lambdarank {rows} rows / {queries} queries x700 (80% zeros) "
                     "num_leaves=255 max_bin=255"),
 }
+
+# DRAM bytes per algorithmic byte of each tree kernel, from the small-case ncu captures
+# summarised in profiles/ (dram__bytes_read.sum + dram__bytes_write.sum of the captured
+# launches over the algorithmic bytes of the same launches). The bench scales them to
+# its own launches to fill roofline.traffic.
+TRAFFIC_PER_ALGO_BYTE = {}
 
 
 def parse():
@@ -59,6 +84,8 @@ def parse():
     ap.add_argument("--workload", default="c1", choices=sorted(WORKLOADS))
     ap.add_argument("--rows", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the f32 and full-length runs and the parity check")
     ap.add_argument("--measure", default="boosting", choices=["boosting", "binning"],
                     help="binning: time Dataset construction from raw C1 values (device "
                          "value_to_bin) against host value_to_bin on all cores")
@@ -78,6 +105,16 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
+def load_synthetic():
+    """lightgbm_rs_b200/synthetic.py loaded by path, so that importing the generators
+    does not import (or load the library of) the product package."""
+    path = os.path.join(ROOT, "lightgbm_rs_b200", "synthetic.py")
+    spec = importlib.util.spec_from_file_location("lgbm_b200_synthetic_gen", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 class Data:
     """A binned workload: feature-major bins, mappers, labels, query sizes (ranking)."""
 
@@ -89,26 +126,39 @@ class Data:
             np.concatenate([[0], np.cumsum(group)]).astype(np.int32)
 
 
-def make_data(workload, rows, seed=0):
-    """Seeded synthetic data of the workload, binned with the reference BinMapper (host).
+def make_data(workload, rows, seed=0, binner="product"):
+    """Seeded synthetic data of the workload, binned on the host with the reference
+    BinMapper: the product's (`binner="product"`, lightgbm_rs_b200.bin_column) or the
+    oracle's restatement (`binner="oracle"`, used by the CPU reference arm so that its
+    process never loads the product library).
 
     The binned result is cached under the system temp directory so repeated runs on
-    one machine skip generation (the cache is keyed by workload, rows and seed)."""
+    one machine skip generation (keyed by workload, rows, seed and binner)."""
     import concurrent.futures as cf
     import pickle
     import tempfile
 
-    import lightgbm_rs_b200 as lgb
-    from lightgbm_rs_b200 import synthetic
-
-    cache = os.path.join(tempfile.gettempdir(), f"lgbm_b200_{workload}_{rows}_{seed}.pkl")
+    cache = os.path.join(tempfile.gettempdir(),
+                         f"lgbm_b200_{workload}_{rows}_{seed}_{binner}.pkl")
     if os.path.exists(cache):
         with open(cache, "rb") as f:
             return pickle.load(f)
+    if binner == "oracle":
+        import oracle
+
+        oracle.build()
+        bin_column = oracle.bin_column
+    else:
+        import lightgbm_rs_b200 as lgb
+
+        bin_column = lgb.bin_column
+    synthetic = load_synthetic()
     w = WORKLOADS[workload]
     group, cats = None, []
     if workload == "c1":
         X, y = synthetic.binary_c0(num_data=rows, num_features=w["features"], seed=seed)
+    elif workload == "c2":
+        X, y = synthetic.wide_c2(num_data=rows, num_features=w["features"], seed=seed)
     elif workload == "c3":
         X, y, cats = synthetic.mixed_c3(num_data=rows, seed=seed)
     else:
@@ -119,8 +169,8 @@ def make_data(workload, rows, seed=0):
     bins = np.empty((F, X.shape[0]), dtype=np.uint8)
 
     def one(j):
-        m, b = lgb.bin_column(X[:, j], max_bin=255, min_data_in_leaf=w["min_data"],
-                              categorical=j in cats)
+        m, b = bin_column(X[:, j], max_bin=w["max_bin"], min_data_in_leaf=w["min_data"],
+                          categorical=j in cats)
         assert m["num_bin"] <= 256, f"feature {j}: {m['num_bin']} bins do not fit u8"
         mappers[j] = m
         bins[j] = b.astype(np.uint8)
@@ -141,9 +191,11 @@ def make_data(workload, rows, seed=0):
 def params(workload, grad):
     w = WORKLOADS[workload]
     p = {"objective": w["objective"], "num_leaves": w["leaves"],
-         "min_data_in_leaf": w["min_data"], "learning_rate": LEARNING_RATE, "max_bin": 255}
+         "min_data_in_leaf": w["min_data"], "learning_rate": LEARNING_RATE,
+         "max_bin": w["max_bin"], "feature_pre_filter": False}
     if grad == "quantized":
-        p.update(use_quantized_grad=True, num_grad_quant_bins=4)
+        # stochastic_rounding=false: the deterministic rounding of the bit-exact gate
+        p.update(use_quantized_grad=True, num_grad_quant_bins=4, stochastic_rounding=False)
     return p
 
 
@@ -163,10 +215,11 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            time.sleep(0.15)  # the first sample lands inside the timed region
         except Exception:
             self.proc = None
         return self
@@ -211,23 +264,58 @@ def kernel_bytes(counts, rows, grad, features):
     none for the root's identity order). Build: per built row F B of bins + its gradient
     pair (2 B quantized, 8 B f32) + 4 B index (none at the root). In the fused mode the
     partition kernel builds the child itself, so those built rows are charged to it, minus
-    the split-feature byte and the index it has already read."""
+    the split-feature byte and the index it has already read. Control step (fixscan): per
+    split, the accumulated child, the parent's integer histogram and the written child
+    histograms: about 5 x 8 B per histogram cell, cells = 2 x bins (L2-resident)."""
     s_gh = 2 if grad == "quantized" else 8
     F = features
     rp, rb = counts["rows_parted"], counts["rows_built"]
     part = rp * 5 + max(rp - rows, 0) * 4
     root_build = rows * (F + s_gh)
     child_rows = max(rb - rows, 0)
+    child_hist = 0
     if counts["fused"]:
-        part += child_rows * (F - 1 + s_gh)
+        child_hist = child_rows * (F - 1 + s_gh)
+        part += child_hist
         build = root_build
     else:
         build = root_build + child_rows * (F + s_gh + 4)
-    return {"partition": part, "build": build, "bin_bytes": rb * F + rp}
+    return {"partition": part, "build": build, "child_hist_fused": child_hist,
+            "bin_bytes": rb * F + rp}
+
+
+TREE_EXACT = ["split_feature", "threshold_bin", "decision_type", "left_child", "right_child",
+              "leaf_count", "internal_count"]
+TREE_BITS = ["leaf_value", "leaf_weight", "internal_value", "split_gain"]
+
+
+def tree_digest(trees):
+    """SHA-256 over every tree's structure and the bits of its values."""
+    h = hashlib.sha256()
+    for t in trees:
+        h.update(np.int32(t["num_leaves"]).tobytes())
+        for k in TREE_EXACT + TREE_BITS:
+            h.update(np.ascontiguousarray(t[k]).tobytes())
+    return h.hexdigest()
+
+
+def trees_equal(got, want):
+    """First difference between a device tree and an oracle tree, or None."""
+    if got["num_leaves"] != want["num_leaves"]:
+        return f"num_leaves {got['num_leaves']} != {want['num_leaves']}"
+    for k in TREE_EXACT:
+        if np.asarray(got[k]).tolist() != np.asarray(want[k]).tolist():
+            return k
+    for k in TREE_BITS:
+        a = np.asarray(got[k])
+        if a.tobytes() != np.asarray(want[k]).astype(a.dtype).tobytes():
+            return k
+    return None
 
 
 def oracle_step(workload, data, score, grad, nt):
-    """One boosting iteration of the reference CPU learner (oracle/) on `score` in place."""
+    """One boosting iteration of the reference CPU learner (oracle/) on `score` in place.
+    Returns the tree (after shrinkage) and the f32 gradients it was grown from."""
     import oracle
 
     w = WORKLOADS[workload]
@@ -239,12 +327,14 @@ def oracle_step(workload, data, score, grad, nt):
         g, h = oracle.lambdarank_gradients(score, data.y, data.qb, 1.0, True, 30, None, nt)
     else:
         g, h = oracle.l2_gradients(score, data.y, nt)
+    g32, h32 = g, h
     if grad == "quantized":
         g, h, _, _ = oracle.quantize(g, h, 4)
     tree, part, _ = oracle.grow_tree(data.bins, metas, g, h, w["leaves"], -1, nt,
                                      min_data_in_leaf=w["min_data"])
     oracle.tree_shrinkage(tree, LEARNING_RATE)
     oracle.add_prediction_to_score(tree, part, score)
+    return tree, (g32, h32)
 
 
 def oracle_init_score(workload, data):
@@ -255,23 +345,32 @@ def oracle_init_score(workload, data):
     return np.full(data.rows, init, dtype=np.float64)
 
 
-def cpu_baseline(workload, data, grad, seconds_budget=25.0):
-    """The reference CPU learner (oracle/) on the host: boosting iterations on the full
-    workload until ~seconds_budget is used (at least one)."""
+def cpu_run(workload, data, grad, seconds_budget=25.0, keep=PARITY_TREES):
+    """The reference CPU learner (oracle/) on all host threads: boosting iterations on the
+    full workload until ~seconds_budget of training time is used (at least `keep` + 1).
+    Returns the rate, the thread count, the iterations, the seconds, and the first `keep`
+    trees with the scores after them and the first iteration's f32 gradients."""
     import oracle
 
     oracle.build()
     nt = os.cpu_count() or 1
     score = oracle_init_score(workload, data)
-    t0 = time.perf_counter()
-    iters = 0
+    el, iters, trees, score_k, grad0 = 0.0, 0, [], None, None
     while True:
-        oracle_step(workload, data, score, grad, nt)
+        t0 = time.perf_counter()
+        tree, gh = oracle_step(workload, data, score, grad, nt)
+        el += time.perf_counter() - t0
         iters += 1
-        el = time.perf_counter() - t0
-        if el >= seconds_budget or iters >= 50:
+        if iters == 1:
+            grad0 = gh
+        if iters <= keep:
+            trees.append(tree)
+        if iters == keep:
+            score_k = score.copy()
+        if iters > keep and (el >= seconds_budget or iters >= 50):
             break
-    return iters / el, nt, iters, el
+    return {"rate": iters / el, "threads": nt, "iters": iters, "seconds": el,
+            "trees": trees, "score_k": score_k, "grad0": grad0}
 
 
 def workload_desc(args, data):
@@ -281,10 +380,13 @@ def workload_desc(args, data):
 
 
 def run_reference(args):
+    """The reference arm: the oracle port of the reference's CPU learner, timed on all
+    host cores. Its data is binned by the oracle's BinMapper; the product library is
+    never imported or loaded in this process."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    data = make_data(args.workload, args.rows)
+    data = make_data(args.workload, args.rows, binner="oracle")
     import oracle
 
     oracle.build()
@@ -298,18 +400,22 @@ def run_reference(args):
     el = time.perf_counter() - t0
     v = args.steps / el
     w = WORKLOADS[args.workload]
+    loaded = sorted({ln.split()[-1] for ln in open("/proc/self/maps")
+                     if ln.rstrip().endswith(".so") and ROOT in ln})
     out = {
         "metric": "boosting_iters_per_sec", "value": v, "unit": "iters/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * el / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": {"workload": workload_desc(args, data), "rows": data.rows,
-                   "num_leaves": w["leaves"], "max_bin": 255},
+                   "num_leaves": w["leaves"], "max_bin": w["max_bin"]},
         "cpu_baseline": {"value": v, "unit": "iters/s", "cores": nt, "kind": "port",
                          "sample": f"{args.steps} full boosting iterations on all {data.rows} "
-                                   f"rows, {nt} threads (C++ restatement; reference Rust "
-                                   f"crates unbuildable here)"},
+                                   f"rows after {args.warmup} warm-up iterations, {nt} threads "
+                                   f"(C++ restatement; reference Rust crates unbuildable "
+                                   f"here); data binned by the oracle's BinMapper"},
         "e2e": {"value": v, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "repo_libraries_loaded": loaded,
     }
     print(json.dumps(out), flush=True)
 
@@ -329,7 +435,7 @@ def run_ours(args):
         import torch.distributed as dist
 
         # host plumbing only (barriers, the NCCL id, max over ranks); the data path's
-        # all-reduces run inside the library on its own NCCL communicator
+        # exchanges run inside the library
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
     if rank == 0:
         libbuild.build()
@@ -350,8 +456,8 @@ def run_ours(args):
         b0, b1 = D.shard_range(data.rows, world, rank)
         group = None
     local_rows = b1 - b0
-    shard_bins = data.bins[:, b0:b1] if world > 1 else data.bins
-    shard_y = data.y[b0:b1]
+    shard_bins = np.ascontiguousarray(data.bins[:, b0:b1]) if world > 1 else data.bins
+    shard_y = np.ascontiguousarray(data.y[b0:b1])
     comm = D.from_torch(local) if dist else None
 
     def max_over_ranks(x):
@@ -363,42 +469,32 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- device-resident run: inputs already in HBM when the timed region starts ----
-    ds = lgb.Dataset(bins=shard_bins, mappers=data.mappers, label=shard_y, params=p,
-                     group=group)
-    booster = lgb.Booster(p, ds, comm=comm)
-    booster.update(args.warmup)
-    if dist:
-        dist.barrier()
-    with ClockSampler(local) as clk:
-        done = booster.update(args.steps)
-        dev_ms = booster.last_train_ms()
-    if dist:
-        dist.barrier()
-    assert done == args.steps, f"training stopped early ({done} of {args.steps})"
-    dev_ms = max_over_ranks(dev_ms)
-    value = args.steps / (dev_ms / 1000.0)
+    def barrier():
+        if dist:
+            dist.barrier()
 
-    # ---- per-kernel timing of one more iteration (CUDA events on the library stream) ----
-    kms, counts = booster.profile_iteration()
-    kb = kernel_bytes(counts, local_rows, args.grad, data.features)
-    peak, peak_kind = load_peaks()
-    per_kernel = {}
-    for cls, label in (("partition", "k_partition_q4 (partition + child histogram)"
-                        if counts["fused"] else "k_partition (row partition)"),
-                       ("build", "k_build_q4 (root histogram)" if counts["fused"]
-                        else "k_build / k_build_q4 (histogram build)")):
-        ms = kms[cls]
-        ach = kb[cls] / (ms / 1000.0) / 1e9 if ms > 0 else 0.0
-        per_kernel[cls] = {"kernel": label, "ms_per_iter": ms, "bytes_per_iter": kb[cls],
-                           "achieved": ach, "frac": ach / peak if peak else None}
-    dom = max(per_kernel, key=lambda k: per_kernel[k]["ms_per_iter"])
-    launches_per_step = counts["launches"]
-    del booster
+    def resident_booster(pp, warmup, steps):
+        ds_ = lgb.Dataset(bins=shard_bins, mappers=data.mappers, label=shard_y, params=pp,
+                          group=group)
+        b_ = lgb.Booster(pp, ds_, comm=comm)
+        b_.update(warmup)
+        barrier()
+        done_ = b_.update(steps)
+        ms_ = max_over_ranks(b_.last_train_ms())
+        assert done_ == steps, f"training stopped early ({done_} of {steps})"
+        return ds_, b_, ms_
 
-    # ---- end to end through the public API from host buffers ----
-    if dist:
-        dist.barrier()
+    # ---- context and modules loaded, then every cached device block released: the
+    # end-to-end leg below starts from a cold buffer cache, as a fresh lgb.train does ----
+    tiny = lgb.Dataset(bins=np.zeros((data.features, 256), dtype=np.uint8),
+                       mappers=data.mappers, label=(np.arange(256) % 2).astype(np.float32),
+                       params=p, group=None if group is None else [256])
+    lgb.train(p, tiny, num_boost_round=1)  # this device alone
+    del tiny
+    lgb._lib.lib().lgbm_b200_release_cached_memory(-1, None)
+    barrier()
+
+    # ---- end to end through the public API from host buffers (cold buffer cache) ----
     t0 = time.perf_counter()
     ds2 = lgb.Dataset(bins=shard_bins, mappers=data.mappers, label=shard_y, params=p,
                       group=group)
@@ -406,18 +502,117 @@ def run_ours(args):
     trees = b2.trees()
     scores = b2.train_scores()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
-    h2d = np.ascontiguousarray(shard_bins).nbytes + shard_y.nbytes + \
-        (0 if group is None else (len(group) + 1) * 4)
+    h2d = shard_bins.nbytes + shard_y.nbytes + (0 if group is None else (len(group) + 1) * 4)
     d2h = scores.nbytes + sum(sum(np.asarray(v).nbytes for k, v in t.items()
                                   if isinstance(v, np.ndarray)) for t in trees)
-    del b2, ds2
+    del b2, ds2, trees, scores
 
+    # ---- device-resident run: inputs already in HBM when the timed region starts ----
+    ds = lgb.Dataset(bins=shard_bins, mappers=data.mappers, label=shard_y, params=p,
+                     group=group)
+    booster = lgb.Booster(p, ds, comm=comm)
+    booster.update(args.warmup)
+    barrier()
+    with ClockSampler(local) as clk:
+        done = booster.update(args.steps)
+        dev_ms = booster.last_train_ms()
+    barrier()
+    assert done == args.steps, f"training stopped early ({done} of {args.steps})"
+    dev_ms = max_over_ranks(dev_ms)
+    value = args.steps / (dev_ms / 1000.0)
+    digest = tree_digest(booster.trees())
+
+    # ---- per-kernel device spans of the pipelined step (same launch sequence, kernels
+    # stamping %globaltimer at entry and exit), and the kernels' own work counters ----
+    spans, pc = booster.profile_pipeline(5)
+    kb = kernel_bytes(pc, local_rows, args.grad, data.features)
+    peak, peak_kind = load_peaks()
+    part_ms = spans["partition"] + pc["lookahead"]
+
+    def entry(label, ms, nbytes, traffic_key=None):
+        ach = nbytes / (ms / 1000.0) / 1e9 if ms > 0 else 0.0
+        e = {"kernel": label, "ms_per_iter": ms, "bytes_per_iter": nbytes, "achieved": ach,
+             "frac": ach / peak if peak else None}
+        if traffic_key in TRAFFIC_PER_ALGO_BYTE:
+            e["traffic_per_iter"] = nbytes * TRAFFIC_PER_ALGO_BYTE[traffic_key]
+        return e
+
+    fused = pc["fused"]
+    cells = 2 * sum(int(m["num_bin"]) for m in data.mappers)
+    fix_bytes = pc["splits"] * cells * 8 * 5
+    kern = {
+        "partition": entry("k_partition_q4 (row partition + fused child histogram; main and "
+                           "look-ahead launches)" if fused else "k_partition (row partition)",
+                           part_ms, kb["partition"], "partition"),
+        "build": entry("k_build_q4 (root histogram)" if fused else
+                       "k_build / k_build_q4 (histogram build)", spans["build"], kb["build"],
+                       "build"),
+        "fixscan": entry("k_fixscan (control step: decode, FixHistogram, subtraction, "
+                         "threshold scans, pick; L2-resident)", spans["fixscan"], fix_bytes),
+    }
+    dom = max(kern, key=lambda k: kern[k]["ms_per_iter"])
+    hist = {"root": kern["build"],
+            "child_fused": {"bytes_per_iter": kb["child_hist_fused"],
+                            "share_of_partition_bytes":
+                                kb["child_hist_fused"] / kb["partition"] if kb["partition"]
+                                else 0.0}}
+    launches_per_step = pc["stamped_launches"] + 10  # + gradient, init, prepare, finish
+    del booster
+
+    # ---- the first trees vs the CPU oracle on the same binned data (one device) ----
+    extras = {}
     cpu = None
-    if not args.no_cpu_baseline and world == 1:
-        v, cores, iters, el = cpu_baseline(args.workload, data, args.grad)
-        cpu = {"value": v, "unit": "iters/s", "cores": cores, "kind": "port",
-               "sample": f"{iters} full boosting iterations on all {data.rows} rows "
-                         f"({el:.1f} s), {cores} threads"}
+    cpu_res = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu_res = cpu_run(args.workload, data, args.grad)
+        cpu = {"value": cpu_res["rate"], "unit": "iters/s", "cores": cpu_res["threads"],
+               "kind": "port",
+               "sample": f"{cpu_res['iters']} full boosting iterations on all {data.rows} rows "
+                         f"({cpu_res['seconds']:.1f} s of training), {cpu_res['threads']} "
+                         f"threads"}
+    if cpu_res is not None and not args.no_extras:
+        bp = lgb.Booster(p, ds, comm=comm)
+        bp.update(1)
+        g0, h0 = bp.last_gradients()
+        bp.update(PARITY_TREES - 1)
+        got = bp.trees()
+        s_dev = bp.train_scores()
+        diffs = [trees_equal(a, b) for a, b in zip(got, cpu_res["trees"])]
+        gw, hw = cpu_res["grad0"]
+        extras["parity"] = {
+            "trees": PARITY_TREES, "rows": data.rows,
+            "bit_exact": all(d is None for d in diffs) and
+            s_dev.tobytes() == cpu_res["score_k"].tobytes(),
+            "tree_mismatch": [d for d in diffs],
+            "scores_bit_exact": s_dev.tobytes() == cpu_res["score_k"].tobytes(),
+            "grad_f32_mismatches_iter0": int(np.sum(g0.view(np.uint32) !=
+                                                    gw.astype(np.float32).view(np.uint32)) +
+                                             np.sum(h0.view(np.uint32) !=
+                                                    hw.astype(np.float32).view(np.uint32))),
+            "checked_against": "oracle/ (CPU restatement pinned to the reference's goldens), "
+                               "same binned data, both from the initial score"}
+        del bp
+
+    # ---- the same workload with f32 gradients, and a full-length run ----
+    if not args.no_extras and args.grad == "quantized":
+        pf = params(args.workload, "f32")
+        pf["device"] = local
+        ds_f, bf, ms_f = resident_booster(pf, args.warmup, args.steps)
+        extras["f32"] = {"value": args.steps / (ms_f / 1000.0), "unit": "iters/s",
+                         "steps": args.steps, "warmup": args.warmup,
+                         "ms_per_step": ms_f / args.steps}
+        del bf, ds_f
+    if not args.no_extras:
+        n_full = w["iterations"]
+        bfull = lgb.Booster(p, ds, comm=comm)
+        barrier()
+        done_full = bfull.update(n_full)
+        ms_full = max_over_ranks(bfull.last_train_ms())
+        extras["full"] = {"iterations": done_full, "value": done_full / (ms_full / 1000.0),
+                          "unit": "iters/s", "ms": ms_full,
+                          "digest": tree_digest(bfull.trees())}
+        del bfull
+    del ds
 
     par = "single GPU" if world == 1 else (
         f"data-parallel, {world} GPUs: rows sharded, the integer child histogram of every "
@@ -437,30 +632,44 @@ def run_ours(args):
         "data": "synthetic",
         "config": {"workload": workload_desc(args, data),
                    "rows": data.rows, "rows_per_gpu": local_rows, "features": data.features,
-                   "num_leaves": w["leaves"], "grad": args.grad, "parallelism": par,
+                   "num_leaves": w["leaves"], "max_bin": w["max_bin"], "grad": args.grad,
+                   "parallelism": par,
                    "l2": f"inputs larger than L2 (bin matrix "
                          f"{data.rows * ((data.features + 15) // 16 * 16) / 1e6:.0f} MB "
-                         f"> 126 MB)"},
-        "roofline": {"bound": "hbm", "kernel": per_kernel[dom]["kernel"],
-                     "achieved": per_kernel[dom]["achieved"], "peak": peak, "unit": "GB/s",
-                     "frac": per_kernel[dom]["frac"], "peak_kind": peak_kind, "traffic": None,
-                     "algorithmic_bytes_per_iter": per_kernel[dom]["bytes_per_iter"],
-                     "ms_per_iter": per_kernel[dom]["ms_per_iter"],
-                     "other_kernels": {k: v for k, v in per_kernel.items() if k != dom},
-                     "rows_parted_per_iter": counts["rows_parted"],
-                     "rows_built_per_iter": counts["rows_built"],
-                     "builds_per_iter": counts["builds"], "splits_per_iter": counts["splits"],
-                     "lookahead_runs_per_iter": counts.get("lookahead_runs", 0),
-                     "lookahead_hits_per_iter": counts.get("lookahead_hits", 0)},
-        "kernel_ms_per_iter": kms,
+                         f"> 126 MB)" if data.rows * data.features > 126e6 else
+                         "bin matrix smaller than L2; no flush between iterations"},
+        "roofline": {"bound": "hbm", "kernel": kern[dom]["kernel"],
+                     "achieved": kern[dom]["achieved"], "peak": peak, "unit": "GB/s",
+                     "frac": kern[dom]["frac"], "peak_kind": peak_kind,
+                     "traffic": (kern[dom].get("traffic_per_iter") / (
+                         pc["splits"] + 1) if kern[dom].get("traffic_per_iter") else None),
+                     "traffic_note": "DRAM bytes per launch (per split step), scaled from the "
+                                     "small-case ncu capture in profiles/",
+                     "algorithmic_bytes_per_iter": kern[dom]["bytes_per_iter"],
+                     "ms_per_iter": kern[dom]["ms_per_iter"],
+                     "timing": "device spans (%globaltimer, first CTA entry to last CTA exit) "
+                               "of each launch in a CUDA graph of the training pipeline, "
+                               "look-ahead stream included; mean of 5 iterations",
+                     "pipeline_ms_per_iter": pc["ms_per_iter"],
+                     "kernels": kern,
+                     "histogram": hist,
+                     "rows_parted_per_iter": pc["rows_parted"],
+                     "rows_built_per_iter": pc["rows_built"],
+                     "splits_per_iter": pc["splits"],
+                     "lookahead_runs_per_iter": pc["lookahead_runs"],
+                     "lookahead_hits_per_iter": pc["lookahead_hits"]},
+        "kernel_span_ms_per_iter": spans,
         "cpu_baseline": cpu,
         "e2e": {"value": args.steps / e2e_s, "unit": "iters/s",
                 "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps,
                 "note": "lgb.train from host bins+labels: upload, K iterations, model+scores "
-                        "readback (binning excluded on both arms)"},
-        "gpu_launches": launches_per_step * args.steps,
+                        "readback (binning excluded on both arms); run first, with the "
+                        "library's device-buffer cache emptied (cold)"},
+        "digest": digest,
+        "gpu_launches": int(round(launches_per_step * args.steps)),
         "clocks": clk.summary(),
     }
+    out.update(extras)
     if comm is not None:
         comm.close()
     if dist:
@@ -478,11 +687,11 @@ def run_binning(args):
 
     import lightgbm_rs_b200 as lgb
     from lightgbm_rs_b200 import build as libbuild
-    from lightgbm_rs_b200 import synthetic
 
+    synthetic = load_synthetic()
     libbuild.build()
     X, y = synthetic.binary_c0(num_data=args.rows, num_features=28, seed=0)
-    p = {"max_bin": 255, "min_data_in_leaf": 100}
+    p = {"max_bin": 255, "min_data_in_leaf": 100, "feature_pre_filter": False}
     t0 = time.perf_counter()
     ds = lgb.Dataset(X, y, p)  # mappers from the samples (host)
     t_map = time.perf_counter() - t0

@@ -205,6 +205,13 @@ int32_t lgbm_b200_abi_version(void);
 /* Number of CUDA devices visible (0 when none; never an error). */
 int lgbm_b200_device_count(int32_t* out);
 
+/* Frees the device blocks (1 MB and larger) that destroyed datasets and
+ * boosters left in this library's per-process cache, on `device` (-1: every
+ * device), and reports the bytes freed (may be NULL). No counterpart in the
+ * reference, whose CubeCL runtime keeps its own memory pool. The cache is
+ * also trimmed on its own before a cudaMalloc is reported as failed. */
+int lgbm_b200_release_cached_memory(int32_t device, int64_t* released_bytes);
+
 /* ------------------------------------------------------------------ binning */
 
 /* BinMapper::find_bin_from_column + value_to_bin
@@ -256,6 +263,21 @@ int lgbm_b200_data_partition(const uint32_t* bins, int64_t n, uint32_t num_bin, 
                              uint32_t max_bin, uint32_t threshold, uint32_t most_freq_bin,
                              uint32_t* order_out, int64_t* split_point_out);
 
+/* The kernel-level partition with the whole missing-value routing fan-out:
+ * partition_leaf_stable / partition_on_device (crates/lgbm-compute/src/kernels/
+ * data_partition.rs:487-520, routing RouteFlags::derive + route_to_left :325-406,
+ * :64-138). Arguments as lgbm_b200_data_partition plus default_bin, missing_type
+ * (0 None, 1 Zero, 2 NaN) and default_left. missing_type 1 routes the zero bin
+ * (min_bin + default_bin - [most_freq_bin == 0]) and 2 the NA bin (max_bin) by
+ * default_left, unless the most frequent bin is that bin; min_bin == max_bin is the
+ * degenerate one-bin feature. Host buffers; result [left ascending | right
+ * ascending]. */
+int lgbm_b200_data_partition_missing(const uint32_t* bins, int64_t n, uint32_t num_bin,
+                                     uint32_t min_bin, uint32_t max_bin, uint32_t threshold,
+                                     uint32_t most_freq_bin, uint32_t default_bin,
+                                     int32_t missing_type, int32_t default_left,
+                                     uint32_t* order_out, int64_t* split_point_out);
+
 /* Allocation-free variant of lgbm_b200_data_partition. No counterpart in the
  * reference: it exists for callers that cannot call cudaMalloc when they
  * partition rows. Examples are a host engine whose device memory belongs to its
@@ -281,7 +303,14 @@ int lgbm_b200_data_partition(const uint32_t* bins, int64_t n, uint32_t num_bin, 
  * on the GPU (different streams, or different host threads) race and return
  * wrong results: serialise them. The first call on each device looks the
  * array up with cudaGetSymbolAddress (with that device current); make that
- * first call before any stream capture. */
+ * first call before any stream capture. A failed lookup returns
+ * LGBM_B200_RUNTIME and is tried again by the next call.
+ *
+ * The partition's look-back waits are bounded. If one runs out (a tile whose
+ * predecessor never published, e.g. under heavy preemption), `order_out` is
+ * left incomplete and *split_point_out is set to the sentinel -1 on the
+ * stream: check it before using the order. The allocating entry point
+ * returns LGBM_B200_RUNTIME in the same case. */
 #define LGBM_B200_NOALLOC_MAX_ROWS 67108864 /* 2^26 rows */
 int lgbm_b200_data_partition_noalloc(const uint8_t* bins, int64_t n, uint32_t num_bin,
                                      uint32_t min_bin, uint32_t max_bin, uint32_t threshold,
@@ -374,6 +403,19 @@ int lgbm_b200_booster_phase_ms(const lgbm_b200_booster* b, double* out3);
  * used. The iteration counts as a normal boosting iteration. */
 int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
                                         int64_t* counts_out);
+/* Run `iterations` more boosting iterations through a CUDA graph of the same launch
+ * sequence as lgbm_b200_booster_train (look-ahead stream included), whose tree kernels
+ * stamp their device-time spans (%globaltimer at each CTA's entry and exit): a span is
+ * first entry to last exit of one launch, as it ran in the pipeline. span_ms_out[7]
+ * receives the mean per iteration of the summed spans per kernel class (same order as
+ * profile_iteration; partition = the main-stream partitions). iter_ms_out[2] = {mean
+ * device ms per iteration, mean summed spans of the look-ahead partitions, which run
+ * beside the control steps}. counts_out[8] receives the same counters as
+ * profile_iteration, summed over the iterations (counts_out[0]: stamped tree-kernel
+ * launches). No counterpart in the reference (a profiling aid). */
+int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
+                                       double* span_ms_out, double* iter_ms_out,
+                                       int64_t* counts_out);
 /* The launches timed by the last lgbm_b200_booster_profile_iteration, in launch order:
  * kernel class (the ms_out order of that call) and device ms of each timed span; *n_out
  * receives the count, at most cap entries are written. */

@@ -510,6 +510,24 @@ class Booster:
                  "splits": int(cnt[3]), "rows_parted": int(cnt[4]), "fused": bool(cnt[5]),
                  "lookahead_runs": int(cnt[6]), "lookahead_hits": int(cnt[7])})
 
+    def profile_pipeline(self, iterations=5):
+        """`iterations` more iterations through a graph of the training pipeline whose
+        tree kernels stamp their device-time spans. Returns (mean summed span ms per
+        iteration by kernel class, {"ms_per_iter": mean iteration ms, "lookahead": mean
+        summed look-ahead partition spans, and the tree counters per iteration})."""
+        span = np.zeros(7, dtype=np.float64)
+        it = np.zeros(2, dtype=np.float64)
+        cnt = np.zeros(8, dtype=np.int64)
+        C.check(C.lib().lgbm_b200_booster_profile_pipeline(self._handle, int(iterations),
+                                                           C.ptr(span), C.ptr(it), C.ptr(cnt)))
+        self._trees = None
+        n = float(iterations)
+        return (dict(zip(self.KERNEL_CLASSES, span.tolist())),
+                {"ms_per_iter": float(it[0]), "lookahead": float(it[1]),
+                 "stamped_launches": cnt[0] / n, "builds": cnt[1] / n, "rows_built": cnt[2] / n,
+                 "splits": cnt[3] / n, "rows_parted": cnt[4] / n, "fused": bool(cnt[5]),
+                 "lookahead_runs": cnt[6] / n, "lookahead_hits": cnt[7] / n})
+
     def profile_launches(self):
         """(kernel class name, device ms) of every span timed by the last
         profile_iteration, in launch order."""

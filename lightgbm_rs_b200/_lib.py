@@ -110,6 +110,7 @@ _SIGS = {
     "lgbm_b200_last_error": ([], ctypes.c_char_p),
     "lgbm_b200_abi_version": ([], _i32),
     "lgbm_b200_device_count": ([_P], ctypes.c_int),
+    "lgbm_b200_release_cached_memory": ([_i32, _P], ctypes.c_int),
     "lgbm_b200_bin_column": ([_P, _i64, _P, _P, _P, _i32, _P], ctypes.c_int),
     "lgbm_b200_bin_column_categorical": ([_P, _i64, _P, _P, _P, _i32, _P], ctypes.c_int),
     "lgbm_b200_construct_histograms": ([_P, _P, _P, _i64, _u32, _P], ctypes.c_int),
@@ -118,6 +119,8 @@ _SIGS = {
     "lgbm_b200_find_best_splits_batched": ([_P, _i64, _P, _i32, _P, _f64, _f64, _i32, _P],
                                            ctypes.c_int),
     "lgbm_b200_data_partition": ([_P, _i64, _u32, _u32, _u32, _u32, _u32, _P, _P], ctypes.c_int),
+    "lgbm_b200_data_partition_missing": ([_P, _i64, _u32, _u32, _u32, _u32, _u32, _u32, _i32,
+                                          _i32, _P, _P], ctypes.c_int),
     "lgbm_b200_data_partition_noalloc": ([_P, _i64, _u32, _u32, _u32, _u32, _u32, _P, _P, _P],
                                          ctypes.c_int),
     "lgbm_b200_subtract_histograms": ([_P, _P, _i64, _P], ctypes.c_int),
@@ -137,6 +140,7 @@ _SIGS = {
     "lgbm_b200_booster_get_gradients": ([_P, _P, _P], ctypes.c_int),
     "lgbm_b200_booster_phase_ms": ([_P, _P], ctypes.c_int),
     "lgbm_b200_booster_profile_iteration": ([_P, _P, _P], ctypes.c_int),
+    "lgbm_b200_booster_profile_pipeline": ([_P, _i32, _P, _P, _P], ctypes.c_int),
     "lgbm_b200_booster_profile_launches": ([_P, _i32, _P, _P, _P], ctypes.c_int),
     "lgbm_b200_comm_unique_id": ([_P], ctypes.c_int),
     "lgbm_b200_comm_create": ([_i32, _i32, _i32, _P, _P], ctypes.c_int),

@@ -82,10 +82,32 @@ BlockCache& block_cache() {
 constexpr size_t kCacheMinBytes = 1ull << 20;
 constexpr size_t kCacheMaxBytes = 16ull << 30;
 
+// Frees every kept block of `device` (-1: of every device); returns the bytes freed.
+size_t release_cached_blocks(int device) {
+  BlockCache& c = block_cache();
+  std::lock_guard<std::mutex> lk(c.mu);
+  size_t freed = 0;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  for (auto it = c.blocks.begin(); it != c.blocks.end();) {
+    if (device >= 0 && it->first.first != device) {
+      ++it;
+      continue;
+    }
+    if (it->first.first != prev) cudaSetDevice(it->first.first);
+    cudaFree(it->second);
+    freed += it->first.second;
+    c.bytes -= it->first.second;
+    it = c.blocks.erase(it);
+  }
+  if (prev >= 0) cudaSetDevice(prev);
+  return freed;
+}
+
 cudaError_t dev_malloc(void** p, size_t bytes, bool cacheable) {
+  int dev = 0;
+  cudaGetDevice(&dev);
   if (cacheable && bytes >= kCacheMinBytes) {
-    int dev = 0;
-    cudaGetDevice(&dev);
     BlockCache& c = block_cache();
     std::lock_guard<std::mutex> lk(c.mu);
     auto it = c.blocks.find({dev, bytes});
@@ -96,7 +118,13 @@ cudaError_t dev_malloc(void** p, size_t bytes, bool cacheable) {
       return cudaSuccess;
     }
   }
-  return cudaMalloc(p, bytes);
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e == cudaErrorMemoryAllocation && release_cached_blocks(dev) > 0) {
+    // idle kept blocks of other sizes stood in the way: give them back and retry once
+    cudaGetLastError();
+    e = cudaMalloc(p, bytes);
+  }
+  return e;
 }
 
 void dev_free(void* p, size_t bytes, bool cacheable) {
@@ -681,12 +709,16 @@ struct lgbm_b200_booster {
   cudaGraph_t graph = nullptr;
   float last_ms = 0.f;
   std::vector<std::pair<int32_t, float>> last_profile;  // (kernel class, ms) per launch
+  DevBuf<unsigned long long> spans;  // [2][span_slots(L)] start | end (profile_pipeline)
   lgbm_b200_comm* comm = nullptr;  // data-parallel job (null: one device)
   const DeviceComm* dcomm() const { return comm ? &comm->dev : nullptr; }
 
   int ensure_capacity(int32_t need);
   // Host copy of the first snap_n recorded trees, made by the first get_tree after
   // training (one copy per record field instead of a dozen per tree); training drops it.
+  // snap_mu guards the snapshot: ctypes callers release the GIL, so two threads may read
+  // trees of one booster at once.
+  std::mutex snap_mu;
   int32_t snap_n = -1;
   std::vector<int32_t> snap_i32;  // num_leaves[n] | left | right | split_feature | leaf_count |
                                   // internal_count, [n][L] each
@@ -817,6 +849,7 @@ int lgbm_b200_booster::ensure_capacity(int32_t need) {
 // counters (left total, tile ticket) and the routing descriptor -- lives in the fixed
 // array below instead of a cudaMalloc'd buffer. Layout, in 8-byte words:
 //   word 0        int32 left total | uint32 tile ticket
+//   word 1        uint32 error bits (kErrSpinTimeout: a tile's look-back wait ran out)
 //   words 8..     DevFeature routing descriptor
 //   words 32..    status words, one per tile, at most LGBM_B200_NOALLOC_MAX_ROWS / 2048
 // Every call on a device shares this one array: calls that overlap on the GPU race.
@@ -836,10 +869,12 @@ static_assert(sizeof(DevFeature) <= 8 * (kNoAllocHeaderWords - kNoAllocFeatureWo
 static __device__ __align__(256) unsigned long long
     g_noalloc_partition_scratch[kNoAllocHeaderWords + kNoAllocMaxTiles];
 
-// Per-device result of the one-time symbol lookup.
+// Per-device result of the symbol lookup. Only a successful lookup is kept: a failed one
+// (a transient error, or a first call made during stream capture) is tried again by the
+// next call.
 struct NoAllocDevice {
-  std::once_flag once;
-  cudaError_t err = cudaSuccess;
+  std::mutex mu;
+  bool done = false;
   unsigned long long* scratch = nullptr;
   int sms = 0;
 };
@@ -856,14 +891,21 @@ __global__ void k_noalloc_partition_setup(unsigned long long* scratch, int64_t t
     status[i] = 0ull;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     scratch[0] = 0ull;
+    scratch[1] = 0ull;
     *reinterpret_cast<DevFeature*>(scratch + kNoAllocFeatureWord) = f;
   }
 }
 
 // The partition kernel writes right-going rows from the back of the range; this puts
 // them in ascending order, as the host entry point does, and publishes the split point.
+// When a tile's look-back wait ran out, some rows were never written: the split point is
+// the sentinel -1 and `order` is left as it is.
 __global__ void k_noalloc_partition_finish(const unsigned long long* scratch, uint32_t* order,
                                            int64_t n, int64_t* split_point) {
+  if (*reinterpret_cast<const volatile uint32_t*>(scratch + 1) != 0u) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) *split_point = -1;
+    return;
+  }
   const int64_t left = (int64_t)*reinterpret_cast<const int32_t*>(scratch);
   const int64_t half = (n - left) / 2;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < half;
@@ -885,7 +927,13 @@ extern "C" {
 
 const char* lgbm_b200_last_error(void) { return g_last_error.c_str(); }
 
-int32_t lgbm_b200_abi_version(void) { return 103; }
+int32_t lgbm_b200_abi_version(void) { return 104; }
+
+int lgbm_b200_release_cached_memory(int32_t device, int64_t* released_bytes) {
+  const size_t freed = release_cached_blocks(device < 0 ? -1 : device);
+  if (released_bytes) *released_bytes = (int64_t)freed;
+  return LGBM_B200_OK;
+}
 
 int lgbm_b200_device_count(int32_t* out) {
   int n = 0;
@@ -1083,9 +1131,35 @@ int lgbm_b200_find_best_splits_batched(const double* buf, int64_t buf_len,
   return scan_batch(buf, buf_len, f, cfg, sum_gradient, sum_hessian, num_data, out);
 }
 
+static int data_partition_impl(const uint32_t* bins, int64_t n, uint32_t num_bin,
+                               uint32_t min_bin, uint32_t max_bin, uint32_t threshold,
+                               uint32_t most_freq_bin, const int32_t* missing,
+                               uint32_t* order_out, int64_t* split_point_out);
+
 int lgbm_b200_data_partition(const uint32_t* bins, int64_t n, uint32_t num_bin, uint32_t min_bin,
                              uint32_t max_bin, uint32_t threshold, uint32_t most_freq_bin,
                              uint32_t* order_out, int64_t* split_point_out) {
+  return data_partition_impl(bins, n, num_bin, min_bin, max_bin, threshold, most_freq_bin,
+                             nullptr, order_out, split_point_out);
+}
+
+int lgbm_b200_data_partition_missing(const uint32_t* bins, int64_t n, uint32_t num_bin,
+                                     uint32_t min_bin, uint32_t max_bin, uint32_t threshold,
+                                     uint32_t most_freq_bin, uint32_t default_bin,
+                                     int32_t missing_type, int32_t default_left,
+                                     uint32_t* order_out, int64_t* split_point_out) {
+  if (missing_type < 0 || missing_type > 2)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "data_partition_missing: missing_type %d",
+                missing_type);
+  const int32_t m[3] = {(int32_t)default_bin, missing_type, default_left ? 1 : 0};
+  return data_partition_impl(bins, n, num_bin, min_bin, max_bin, threshold, most_freq_bin, m,
+                             order_out, split_point_out);
+}
+
+static int data_partition_impl(const uint32_t* bins, int64_t n, uint32_t num_bin,
+                               uint32_t min_bin, uint32_t max_bin, uint32_t threshold,
+                               uint32_t most_freq_bin, const int32_t* missing,
+                               uint32_t* order_out, int64_t* split_point_out) {
   if (!order_out || !split_point_out || (n > 0 && !bins) || n < 0)
     return fail(LGBM_B200_INVALID_ARGUMENT, "data_partition: null argument");
   if (num_bin == 0) return fail(LGBM_B200_RUNTIME, "data_partition: num_bin must be > 0");
@@ -1107,26 +1181,39 @@ int lgbm_b200_data_partition(const uint32_t* bins, int64_t n, uint32_t num_bin, 
   DevFeature f = make_feature((int32_t)num_bin, 0, (int32_t)most_freq_bin, 0);
   f.route_min = (int32_t)min_bin;
   f.route_max = (int32_t)max_bin;
+  int32_t default_left = 0;
+  if (missing) {  // the kernel router's missing-value fan-out
+    f.default_bin = missing[0];
+    f.missing_type = missing[1];
+    f.flags = kFeatMissingRoute;
+    default_left = missing[2];
+  }
   const int64_t tiles = (n + 2047) / 2048;
   DevBuf<uint8_t> d_rm;
   DevBuf<uint32_t> d_dst;
   DevBuf<unsigned long long> d_status;
-  DevBuf<int32_t> d_cnt;  // [0] left total, [1] ticket
+  DevBuf<int32_t> d_cnt;  // [0] left total, [1] ticket, [2] error bits
   DevBuf<DevFeature> d_f;
   CUDA_TRY(d_rm.alloc(rm.size()));
   CUDA_TRY(d_dst.alloc(n));
   CUDA_TRY(d_status.alloc(tiles));
-  CUDA_TRY(d_cnt.alloc(2));
+  CUDA_TRY(d_cnt.alloc(3));
   CUDA_TRY(d_f.alloc(1));
   CUDA_TRY(cudaMemcpy(d_rm.p, rm.data(), rm.size(), cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMemcpy(d_f.p, &f, sizeof(f), cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMemset(d_status.p, 0, tiles * 8));
-  CUDA_TRY(cudaMemset(d_cnt.p, 0, 8));
-  launch_partition_rows(d_rm.p, 16, 0, d_f.p, threshold, 0, n, d_dst.p, d_status.p, d_cnt.p,
-                        reinterpret_cast<uint32_t*>(d_cnt.p + 1), 0);
+  CUDA_TRY(cudaMemset(d_cnt.p, 0, 12));
+  launch_partition_rows(d_rm.p, 16, 0, d_f.p, threshold, default_left, n, d_dst.p, d_status.p,
+                        d_cnt.p,
+                        reinterpret_cast<uint32_t*>(d_cnt.p + 1),
+                        reinterpret_cast<uint32_t*>(d_cnt.p + 2), 0);
   CUDA_TRY(cudaGetLastError());
-  int32_t cnt[2];
-  CUDA_TRY(cudaMemcpy(cnt, d_cnt.p, 8, cudaMemcpyDeviceToHost));
+  int32_t cnt[3];
+  CUDA_TRY(cudaMemcpy(cnt, d_cnt.p, 12, cudaMemcpyDeviceToHost));
+  if (cnt[2] != 0)
+    return fail(LGBM_B200_RUNTIME,
+                "data_partition: the look-back wait ran out (error bits 0x%x); no result",
+                (unsigned)cnt[2]);
   CUDA_TRY(cudaMemcpy(order_out, d_dst.p, n * 4, cudaMemcpyDeviceToHost));
   // the device writes the right rows from the back; the reference returns them ascending
   std::reverse(order_out + cnt[0], order_out + n);
@@ -1159,19 +1246,31 @@ int lgbm_b200_data_partition_noalloc(const uint8_t* bins, int64_t n, uint32_t nu
     return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "data_partition_noalloc: device %d >= %d",
                 dev, kNoAllocMaxDevices);
   NoAllocDevice& nd = g_noalloc_devices[dev];
-  std::call_once(nd.once, [&nd, dev] {
-    nd.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&nd.scratch),
-                                  g_noalloc_partition_scratch);
-    if (nd.err == cudaSuccess)
-      nd.err = cudaDeviceGetAttribute(&nd.sms, cudaDevAttrMultiProcessorCount, dev);
-  });
-  if (nd.err != cudaSuccess || !nd.scratch)
-    return fail(LGBM_B200_RUNTIME,
-                "data_partition_noalloc: scratch set-up on device %d failed: %s", dev,
-                cudaGetErrorString(nd.err));
+  unsigned long long* scratch = nullptr;
+  int sms = 1;
+  {
+    std::lock_guard<std::mutex> lock(nd.mu);
+    if (!nd.done) {
+      unsigned long long* p = nullptr;
+      int count = 0;
+      cudaError_t err = cudaGetSymbolAddress(reinterpret_cast<void**>(&p),
+                                             g_noalloc_partition_scratch);
+      if (err == cudaSuccess)
+        err = cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+      if (err != cudaSuccess || !p) {
+        cudaGetLastError();  // not sticky: the next call tries again
+        return fail(LGBM_B200_RUNTIME,
+                    "data_partition_noalloc: scratch set-up on device %d failed: %s", dev,
+                    cudaGetErrorString(err));
+      }
+      nd.scratch = p;
+      nd.sms = count;
+      nd.done = true;
+    }
+    scratch = nd.scratch;
+    sms = std::max(1, nd.sms);
+  }
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  unsigned long long* scratch = nd.scratch;
-  const int sms = std::max(1, nd.sms);
   DevFeature f = make_feature((int32_t)num_bin, 0, (int32_t)most_freq_bin, 0);
   f.route_min = (int32_t)min_bin;
   f.route_max = (int32_t)max_bin;
@@ -1184,7 +1283,8 @@ int lgbm_b200_data_partition_noalloc(const uint8_t* bins, int64_t n, uint32_t nu
     launch_partition_rows(bins, 1, 0,
                           reinterpret_cast<const DevFeature*>(scratch + kNoAllocFeatureWord),
                           threshold, 0, n, order_out, scratch + kNoAllocHeaderWords, counters,
-                          reinterpret_cast<uint32_t*>(counters + 1), st);
+                          reinterpret_cast<uint32_t*>(counters + 1),
+                          reinterpret_cast<uint32_t*>(scratch + 1), st);
     CUDA_TRY(cudaGetLastError());
   }
   const int finish_blocks =
@@ -1983,7 +2083,10 @@ int lgbm_b200_booster_destroy(lgbm_b200_booster* b) {
 
 int lgbm_b200_booster_train(lgbm_b200_booster* b, int32_t num_iterations, int32_t* done_out) {
   if (!b || num_iterations < 0) return fail(LGBM_B200_INVALID_ARGUMENT, "booster_train: args");
-  b->snap_n = -1;
+  {
+    std::lock_guard<std::mutex> lock(b->snap_mu);
+    b->snap_n = -1;
+  }
   DeviceGuard g(b->ds->device);
   int32_t state[2];
   CUDA_TRY(cudaMemcpy(state, b->state.p, 8, cudaMemcpyDeviceToHost));
@@ -2039,6 +2142,7 @@ int lgbm_b200_booster_get_tree(lgbm_b200_booster* b, int32_t index, lgbm_b200_tr
   if (rc) return rc;
   if (index < 0 || index >= n) return fail(LGBM_B200_INVALID_ARGUMENT, "tree %d of %d", index, n);
   DeviceGuard g(b->learner->device);
+  std::lock_guard<std::mutex> lock(b->snap_mu);
   if (b->snap_n != n) {
     rc = b->snapshot(n);
     if (rc) return rc;
@@ -2114,10 +2218,115 @@ int lgbm_b200_booster_profile_launches(const lgbm_b200_booster* b, int32_t cap,
   return LGBM_B200_OK;
 }
 
+int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
+                                       double* span_ms_out, double* iter_ms_out,
+                                       int64_t* counts_out) {
+  if (!b || !span_ms_out || !iter_ms_out || !counts_out || iterations <= 0)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "profile_pipeline: arguments");
+  {
+    std::lock_guard<std::mutex> lock(b->snap_mu);
+    b->snap_n = -1;
+  }
+  DeviceGuard g(b->ds->device);
+  int32_t state[2];
+  CUDA_TRY(cudaMemcpy(state, b->state.p, 8, cudaMemcpyDeviceToHost));
+  int rc = b->ensure_capacity(state[1] + iterations);
+  if (rc) return rc;
+  const int L = b->learner->L;
+  const int slots = span_slots(L);
+  if (!b->spans.p) CUDA_TRY(b->spans.alloc(2 * (size_t)slots));
+  // a graph of the same launch sequence whose tree kernels stamp their spans
+  cudaStream_t st = b->learner->stream;
+  GrowDev d = b->learner->d;
+  d.span_start = b->spans.p;
+  d.span_end = b->spans.p + slots;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  launch_gradients(b->obj, st, nullptr, b->dcomm());
+  launch_tree(d, b->learner->build_blocks, b->learner->build_smem, st, nullptr, b->dcomm(),
+              &b->learner->las);
+  launch_finish_iteration(d, b->fin, st);
+  cudaError_t e = cudaStreamEndCapture(st, &graph);
+  if (e != cudaSuccess)
+    return fail(LGBM_B200_RUNTIME, "profile_pipeline: graph capture failed: %s",
+                cudaGetErrorString(e));
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess)
+    return fail(LGBM_B200_RUNTIME, "profile_pipeline: instantiate failed: %s",
+                cudaGetErrorString(e));
+  std::vector<unsigned long long> h(2 * (size_t)slots);
+  double cls[KC_COUNT] = {0};
+  double total_ms = 0.0;
+  for (int k = 0; k < 8; ++k) counts_out[k] = 0;
+  iter_ms_out[1] = 0.0;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  for (int it = 0; it < iterations && e == cudaSuccess; ++it) {
+    e = cudaMemsetAsync(b->spans.p, 0xff, slots * 8, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(b->spans.p + slots, 0, slots * 8, st);
+    if (e == cudaSuccess) e = cudaEventRecord(e0, st);
+    if (e == cudaSuccess) e = cudaGraphLaunch(exec, st);
+    if (e == cudaSuccess) e = cudaEventRecord(e1, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(h.data(), b->spans.p, h.size() * 8, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) break;
+    GrowCtrl gc;
+    e = cudaMemcpy(&gc, b->learner->ctrl.p, sizeof(GrowCtrl), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) break;
+    counts_out[1] += gc.num_builds;
+    counts_out[2] += gc.rows_built;
+    counts_out[3] += gc.num_splits;
+    counts_out[4] += gc.rows_parted;
+    counts_out[5] = b->learner->d.fused;
+    counts_out[6] += gc.la_runs;
+    counts_out[7] += gc.la_hits;
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    total_ms += ms;
+    for (int k = 0; k < slots; ++k) {
+      const unsigned long long t0 = h[k], t1 = h[slots + k];
+      if (t0 == ~0ull || t1 < t0) continue;  // not launched, or returned before its stamp
+      counts_out[0] += 1;
+      int c = KC_BUILD;
+      if (k != kSpanRootBuild) {
+        const int kind = (k - 1) % 4;
+        c = kind == SPAN_FIXSCAN ? KC_FIXSCAN
+                                 : (kind == SPAN_BUILD ? KC_BUILD : KC_PARTITION);
+        if (kind == SPAN_LOOKAHEAD) c = KC_COUNT;  // reported apart (runs beside the control step)
+      }
+      const double span = (double)(t1 - t0) * 1e-6;
+      if (c == KC_COUNT)
+        iter_ms_out[1] += span;
+      else
+        cls[c] += span;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaGraphExecDestroy(exec);
+  if (e != cudaSuccess)
+    return fail(LGBM_B200_RUNTIME, "profile_pipeline: %s", cudaGetErrorString(e));
+  for (int k = 0; k < KC_COUNT; ++k) span_ms_out[k] = cls[k] / iterations;
+  iter_ms_out[0] = total_ms / iterations;
+  iter_ms_out[1] /= iterations;
+  GrowCtrl c;
+  CUDA_TRY(cudaMemcpy(&c, b->learner->ctrl.p, sizeof(GrowCtrl), cudaMemcpyDeviceToHost));
+  if (c.error)
+    return fail(LGBM_B200_RUNTIME, "tree grower reported device error bits 0x%x", c.error);
+  return LGBM_B200_OK;
+}
+
 int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
                                         int64_t* counts_out) {
   if (!b || !ms_out || !counts_out) return fail(LGBM_B200_INVALID_ARGUMENT, "null argument");
-  b->snap_n = -1;
+  {
+    std::lock_guard<std::mutex> lock(b->snap_mu);
+    b->snap_n = -1;
+  }
   DeviceGuard g(b->ds->device);
   int32_t state[2];
   CUDA_TRY(cudaMemcpy(state, b->state.p, 8, cudaMemcpyDeviceToHost));

@@ -248,6 +248,38 @@ __device__ __forceinline__ bool d_cat_go_right(const uint32_t* cat, int32_t bin)
   return !((cat[bin >> 5] >> (bin & 31)) & 1u);
 }
 
+// DevFeature::flags bit 5: route with the kernel partition's whole missing-value fan-out
+// (d_route_left_missing) instead of the learner's rule (d_go_right).
+constexpr int32_t kFeatMissingRoute = 32;
+
+// The kernel-level router of partition_leaf_stable (RouteFlags::derive + route_left_host,
+// lgbm-compute/src/kernels/data_partition.rs:325-406): true = left. missing_type 1 sends
+// the zero bin (route_min + default_bin - [mfb == 0]) and 2 the NA bin (route_max) the
+// default_left way unless the most frequent bin is that bin; then out-of-range bins take
+// the missing direction instead of the most frequent bin's. route_min == route_max is
+// the degenerate one-bin case.
+__device__ __forceinline__ bool d_route_left_missing(const DevFeature& f, uint32_t threshold,
+                                                    bool default_left, int32_t bin) {
+  const int32_t lo = f.route_min, hi = f.route_max, mfb = f.most_freq_bin;
+  const bool zm = f.missing_type == 1, nm = f.missing_type == 2;
+  const bool mfb_zero = zm && f.default_bin == mfb;
+  const bool mfb_na = nm && hi == mfb + lo && mfb > 0;
+  const int32_t shift = mfb == 0 ? 1 : 0;
+  const int32_t th = (int32_t)threshold + lo - shift;
+  const bool miss_left = (zm || nm) && default_left;
+  const bool mfb_left = mfb <= (int32_t)threshold;
+  const bool oor_missing = (nm && mfb_na) || (zm && mfb_zero);
+  const bool oor_left = oor_missing ? miss_left : mfb_left;
+  if (zm && !mfb_zero && bin == lo + f.default_bin - shift) return miss_left;
+  if (lo == hi) {
+    if (bin != hi) return oor_left;
+    return (nm && !mfb_na) ? miss_left : hi <= th;
+  }
+  if (nm && !mfb_na && bin == hi) return miss_left;
+  if (bin < lo || bin > hi) return oor_left;
+  return bin <= th;
+}
+
 __device__ __forceinline__ bool d_go_right(const DevFeature& f, uint32_t threshold,
                                            bool default_left, int32_t bin) {
   int32_t th = (int32_t)threshold + f.route_min;

@@ -108,6 +108,18 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
+// Entry/exit stamps of a launch into GrowDev's span arrays (thread 0 of every CTA);
+// nothing when the spans are off.
+struct SpanStamp {
+  const GrowDev& d;
+  __device__ __forceinline__ explicit SpanStamp(const GrowDev& g) : d(g) {
+    if (d.span_start && threadIdx.x == 0) atomicMin(d.span_start + d.span_slot, global_ns());
+  }
+  __device__ __forceinline__ ~SpanStamp() {
+    if (d.span_end && threadIdx.x == 0) atomicMax(d.span_end + d.span_slot, global_ns());
+  }
+};
+
 // Cell `idx` of the accumulated child: the sum over the ranks' buffers of parity xpar
 // (integers: exact in any order); on one device, the launch's accumulator.
 template <bool PEER>
@@ -303,6 +315,7 @@ __device__ __forceinline__ void build_block(const uint8_t* __restrict__ bins, in
 
 template <int MODE>
 __global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d, int phase) {
+  const SpanStamp span(d);
   extern __shared__ unsigned long long acc[];
   __shared__ int32_t s_binoff[128];
   __shared__ uint8_t s_used[128];
@@ -443,6 +456,7 @@ __device__ __forceinline__ Q4Mask q4_mask(const uint32_t* s_mask, int nf) {
 
 template <int SHIFT, int NCH>
 __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase) {
+  const SpanStamp span(d);
   extern __shared__ uint32_t sm[];
   __shared__ uint32_t s_mask[4];
   const BuildTarget t = build_target(d, phase);
@@ -2171,6 +2185,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
 
 template <bool CAT, bool PEER>
 __global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
+  const SpanStamp span(d);
   __shared__ FixScanSmem sm;
   __shared__ CtlSmem cs;
   control_step<CAT, PEER>(d, s, sm, cs);
@@ -2213,7 +2228,10 @@ struct PartitionTile {
         rows[j] = row;
         const int32_t bin = bins[(size_t)row * stride + feature];
         validmask |= 1u << j;
-        const bool gr = cat ? d_cat_go_right(cat, bin) : d_go_right(ft, threshold, default_left, bin);
+        const bool gr = cat ? d_cat_go_right(cat, bin)
+                            : ((ft.flags & kFeatMissingRoute)
+                                   ? !d_route_left_missing(ft, threshold, default_left, bin)
+                                   : d_go_right(ft, threshold, default_left, bin));
         if (!gr) leftmask |= 1u << j;
       }
     }
@@ -2309,6 +2327,7 @@ struct PartitionTile {
 };
 
 __global__ void __launch_bounds__(kPartThreads) k_partition(GrowDev d) {
+  const SpanStamp span(d);
   __shared__ int32_t s_tile;
   GrowCtrl* c = d.ctrl;
   if (c->done || !c->pending) return;
@@ -2774,6 +2793,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
 
 template <int SHIFT, int NCH, bool F32>
 __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int build, int la) {
+  const SpanStamp span(d);
   extern __shared__ uint32_t sm[];
   __shared__ PartSmem ps;
   partition_q4_phase<SHIFT, NCH, F32>(d, build, la, sm, ps);
@@ -2830,7 +2850,7 @@ __global__ void __launch_bounds__(512) k_scan_standalone(const double* hist,
 __global__ void __launch_bounds__(kPartThreads) k_partition_standalone(
     const uint8_t* bins, int32_t stride, int32_t feature, const DevFeature* feat,
     uint32_t threshold, int32_t default_left, int32_t count, uint32_t* dst,
-    unsigned long long* status, int32_t* left_total, uint32_t* ticket) {
+    unsigned long long* status, int32_t* left_total, uint32_t* ticket, uint32_t* error) {
   __shared__ int32_t s_tile;
   const DevFeature ft = *feat;
   const int32_t ntiles = (count + kPartTile - 1) / kPartTile;
@@ -2841,8 +2861,11 @@ __global__ void __launch_bounds__(kPartThreads) k_partition_standalone(
     __syncthreads();
     if (tile >= ntiles) break;
     if (!PartitionTile::run(bins, stride, ft, feature, threshold, default_left != 0, nullptr,
-                            true, dst, 0, count, tile, 1u, status, left_total))
+                            true, dst, 0, count, tile, 1u, status, left_total)) {
+      // the look-back gave up: this tile's rows were not written, so the result is void
+      if (threadIdx.x == 0) atomicOr(error, kErrSpinTimeout);
       break;
+    }
   }
 }
 
@@ -2964,14 +2987,16 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       comm->sum_i64(comm->ctx, x.raw, (int64_t)x.raw_len + 1, st);
   };
   {
-    const GrowDev x = producer(0);
+    GrowDev x = producer(0);
+    x.span_slot = kSpanRootBuild;
     build(x, 0);
     exchange(x);
   }
   for (int s = 0; s < d.L - 1; ++s) {
     if (la_on && !prof && s >= 2) cudaStreamWaitEvent(st, las->done[(s - 2) & (kLaSlots - 1)], 0);
     {
-      const GrowDev x = consumer(s);
+      GrowDev x = consumer(s);
+      x.span_slot = span_slot_of(s, SPAN_FIXSCAN);
       PROF_BEGIN(KC_FIXSCAN);
       // variants: categorical features, and the peer exchange (off on one device)
       if (x.has_cat)
@@ -2982,7 +3007,8 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       PROF_END();
     }
     const int phase = s < d.L - 2 ? 1 : 2;
-    const GrowDev x = producer(s + 1);
+    GrowDev x = producer(s + 1);
+    x.span_slot = span_slot_of(s, SPAN_PARTITION);
     const bool la_step = la_on && s <= d.L - 3;
     // A profiled sequence runs the look-ahead on the main stream, right after the control
     // step: each launch's event span is then its own run, not its wait for free SMs.
@@ -3001,15 +3027,19 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
         k_partition<<<part_blocks, kPartThreads, 0, st>>>(x);
         PROF_END();
       }
-      build(x, phase);
+      GrowDev xb = x;
+      xb.span_slot = span_slot_of(s, SPAN_BUILD);
+      build(xb, phase);
     }
     if (la_step) {
       const cudaStream_t lst = prof ? st : las->st;
       if (!prof) cudaStreamWaitEvent(lst, las->fork, 0);
       const int pslot = prof ? prof->begin(lst, KC_PARTITION) : -1;
+      GrowDev xl = x;
+      xl.span_slot = span_slot_of(s, SPAN_LOOKAHEAD);
       part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<las->blocks, kFpThreads,
                                                                 fused_partition_smem(),
-                                                                lst>>>(x, 1, s & (kLaSlots - 1));
+                                                                lst>>>(xl, 1, s & (kLaSlots - 1));
       if (prof) prof->end(lst, pslot);
       if (px) k_lasignal<<<1, 32, 0, lst>>>(x);  // every rank may read the slot now
       if (!prof) cudaEventRecord(las->done[s & (kLaSlots - 1)], lst);
@@ -3071,13 +3101,14 @@ void launch_scan_features(const double* hist, const DevFeature* feats, int32_t n
 void launch_partition_rows(const uint8_t* bins_rm, int32_t stride, int32_t feature,
                            const DevFeature* feat, uint32_t threshold, int32_t default_left,
                            int64_t count, uint32_t* dst, unsigned long long* status,
-                           int32_t* left_total, uint32_t* ticket, cudaStream_t st) {
+                           int32_t* left_total, uint32_t* ticket, uint32_t* error,
+                           cudaStream_t st) {
   const int32_t ntiles = (int32_t)((count + kPartTile - 1) / kPartTile);
   int blocks = std::min(ntiles, num_sms() * 4);
   if (blocks < 1) blocks = 1;
   k_partition_standalone<<<blocks, kPartThreads, 0, st>>>(
       bins_rm, stride, feature, feat, threshold, default_left, (int32_t)count, dst, status,
-      left_total, ticket);
+      left_total, ticket, error);
 }
 
 void launch_gather_partition(const GrowDev& d, uint32_t* out, cudaStream_t st) {

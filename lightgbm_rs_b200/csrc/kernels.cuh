@@ -157,7 +157,21 @@ struct GrowDev {
   int32_t q4_nch;    // quantized build: 16-feature chunks per group
   const void* gh;  // float2[N] (GH_FLOAT) or uint16 int8 pairs (quantized)
   const DevGhParams* ghp;
+  // Device-time spans of the tree's launches as the pipeline runs them (null: off). Each
+  // CTA's thread 0 lowers span_start[span_slot] to its entry time and raises
+  // span_end[span_slot] to its exit time (%globaltimer, ns). Slots: kSpanRootBuild, then
+  // span_slot_of(s, kind) for split step s.
+  unsigned long long* span_start;
+  unsigned long long* span_end;
+  int32_t span_slot;
+  int32_t _spanpad;
 };
+
+// Span slots of one tree: the root build, then four per split step.
+enum SpanKind { SPAN_FIXSCAN = 0, SPAN_PARTITION = 1, SPAN_LOOKAHEAD = 2, SPAN_BUILD = 3 };
+constexpr int kSpanRootBuild = 0;
+__host__ __device__ inline int span_slot_of(int s, int kind) { return 1 + 4 * s + kind; }
+inline int span_slots(int L) { return 1 + 4 * (L > 1 ? L - 1 : 1); }
 
 // Optional per-kernel timing of a launch sequence: events recorded around each kernel.
 enum KernelClass { KC_PREPARE = 0, KC_BUILD = 1, KC_FIXSCAN = 2, KC_PARTITION = 3, KC_INIT = 4,
@@ -311,7 +325,8 @@ void launch_scan_features(const double* hist, const DevFeature* feats, int32_t n
 void launch_partition_rows(const uint8_t* bins_rm, int32_t stride, int32_t feature,
                            const DevFeature* feat, uint32_t threshold, int32_t default_left,
                            int64_t count, uint32_t* dst, unsigned long long* status,
-                           int32_t* left_total, uint32_t* ticket, cudaStream_t st);
+                           int32_t* left_total, uint32_t* ticket, uint32_t* error,
+                           cudaStream_t st);
 void launch_subtract(const double* parent, const double* child, double* out, int64_t len,
                      cudaStream_t st);
 

@@ -2,8 +2,10 @@
 
 LightGBM's data-parallel tree learner (tree_learner=data): every rank holds a contiguous
 shard of the rows; after each histogram build the ranks sum the integer child histogram
-and its left-row count over NCCL (inside the library, one all-reduce per split), so all
-ranks grow identical trees. The reference maps tree_learner=data back to serial
+and its left-row count inside the library -- over peer memory (CUDA IPC mappings of
+every rank's accumulators, plain loads, bounded waits) when all ranks can map each
+other, else with one NCCL all-reduce per split -- so all ranks grow identical trees.
+The gradient step's scale maxima and root sums are NCCL reductions. The reference maps tree_learner=data back to serial
 (crates/lgbm-core/src/config/set.rs:592-600); this module has no counterpart there.
 
 The NCCL id is made on rank 0 and handed to the other ranks out of band; with

@@ -79,6 +79,14 @@ class LearnerConfig(ctypes.Structure):
 _P = ctypes.c_void_p
 
 
+class OracleBinMapper(ctypes.Structure):
+    _fields_ = [("num_bin", ctypes.c_int32), ("missing_type", ctypes.c_int32),
+                ("default_bin", ctypes.c_int32), ("most_freq_bin", ctypes.c_int32),
+                ("is_trivial", ctypes.c_int32), ("is_categorical", ctypes.c_int32),
+                ("min_val", ctypes.c_double), ("max_val", ctypes.c_double),
+                ("sparse_rate", ctypes.c_double)]
+
+
 class Tree(ctypes.Structure):
     _fields_ = [
         ("num_leaves", ctypes.c_int32),
@@ -141,6 +149,9 @@ def lib():
                                        ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
                                        ctypes.c_int32, ctypes.c_int32]
         L.oracle_partition.restype = ctypes.c_int64
+        L.oracle_partition_missing.argtypes = [_P, _P, ctypes.c_int64] + [ctypes.c_uint32] * 5 + [
+            ctypes.c_int32, ctypes.c_int32]
+        L.oracle_partition_missing.restype = ctypes.c_int64
         L.oracle_grow_tree.argtypes = [
             _P, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _P, _P, _P,
             ctypes.POINTER(LearnerConfig), ctypes.c_int32, ctypes.POINTER(Tree), _P, _P, _P, _P]
@@ -162,6 +173,9 @@ def lib():
         L.oracle_tree_shrinkage.argtypes = [_P, ctypes.c_int32, _P, ctypes.c_double]
         L.oracle_add_prediction_to_score.argtypes = [_P, ctypes.c_int32, _P, _P, _P, _P]
         L.oracle_max_threads.restype = ctypes.c_int32
+        L.oracle_bin_column.argtypes = [_P, ctypes.c_int64] + [ctypes.c_int32] * 9 + [
+            ctypes.POINTER(OracleBinMapper), _P, _P, ctypes.c_int32, _P]
+        L.oracle_bin_column.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -179,6 +193,39 @@ def gain_config(min_data_in_leaf=20, min_sum_hessian_in_leaf=1e-3, max_delta_ste
                       float(min_gain_to_split), float(path_smooth), float(parent_output),
                       int(min_data_per_group), int(max_cat_threshold), int(max_cat_to_onehot),
                       0, float(cat_l2), float(cat_smooth))
+
+
+def bin_column(values, max_bin=255, min_data_in_bin=3, min_data_in_leaf=20, pre_filter=False,
+               use_missing=True, zero_as_missing=False, bin_construct_sample_cnt=200000,
+               data_random_seed=1, want_bins=True, categorical=False):
+    """The reference's BinMapper::find_bin_from_column + value_to_bin
+    (crates/lgbm-dataset/src/bin_mapper.rs:642-675, 148-199), restated in bin_mapper.cpp.
+    Returns (mapper dict, bins u32 or None) with the keys the learner needs."""
+    col = np.ascontiguousarray(values, dtype=np.float64)
+    cap = max(int(max_bin) + 2, 4)
+    if categorical:
+        cap = max(cap, min(len(col), 1 << 20) + 2)
+    upper = np.zeros(cap, dtype=np.float64)
+    b2c = np.zeros(cap, dtype=np.int32)
+    bins = np.empty(len(col), dtype=np.uint32) if want_bins else None
+    m = OracleBinMapper()
+    rc = lib().oracle_bin_column(_ptr(col), len(col), int(max_bin), int(min_data_in_bin),
+                                 int(min_data_in_leaf), int(bool(pre_filter)),
+                                 int(bool(use_missing)), int(bool(zero_as_missing)),
+                                 int(bin_construct_sample_cnt), int(data_random_seed),
+                                 int(bool(categorical)), ctypes.byref(m), _ptr(upper), _ptr(b2c),
+                                 cap, _ptr(bins))
+    if rc != 0:
+        raise RuntimeError("oracle_bin_column: bin capacity too small")
+    mapper = {"num_bin": m.num_bin, "missing_type": m.missing_type,
+              "default_bin": m.default_bin, "most_freq_bin": m.most_freq_bin,
+              "is_trivial": bool(m.is_trivial), "min_val": m.min_val, "max_val": m.max_val,
+              "sparse_rate": m.sparse_rate, "bin_type": 1 if categorical else 0}
+    if categorical:
+        mapper["bin_to_category"] = b2c[: m.num_bin].copy()
+    else:
+        mapper["upper"] = upper[: m.num_bin].copy()
+    return mapper, bins
 
 
 def construct_histogram(bins, g, h, num_bin):
@@ -228,6 +275,18 @@ def partition(bins_of_rows, rows, num_bin, min_bin, max_bin, threshold, most_fre
     r = np.array(rows, dtype=np.uint32)
     left = lib().oracle_partition(_ptr(b), _ptr(r), len(r), num_bin, min_bin, max_bin, threshold,
                                   most_freq_bin, int(na_as_missing), int(default_left))
+    return r, int(left)
+
+
+def partition_missing(bins_of_rows, rows, min_bin, max_bin, threshold, most_freq_bin,
+                      default_bin, missing_type, default_left):
+    """The kernel partition with the missing-value routing fan-out
+    (partition_leaf_stable, lgbm-compute/src/kernels/data_partition.rs:487)."""
+    b = np.ascontiguousarray(bins_of_rows, dtype=np.uint32)
+    r = np.array(rows, dtype=np.uint32)
+    left = lib().oracle_partition_missing(_ptr(b), _ptr(r), len(r), min_bin, max_bin,
+                                          threshold, most_freq_bin, default_bin,
+                                          int(missing_type), int(default_left))
     return r, int(left)
 
 

@@ -1037,6 +1037,54 @@ int64_t oracle_partition(const uint32_t* bins_of_rows, uint32_t* rows, int64_t c
   return (int64_t)L.size();
 }
 
+// The kernel-level partition with the whole missing-value fan-out: RouteFlags::derive
+// and route_left_host (lgbm-compute/src/kernels/data_partition.rs:325-406), driven by
+// partition_leaf_stable (:487-520). missing_type 1 routes the zero bin
+// (min_bin + default_bin - [mfb == 0]) and 2 the NA bin (max_bin) by default_left,
+// unless the most frequent bin coincides with it, in which case out-of-range rows
+// follow default_left instead; min_bin == max_bin is the degenerate one-bin feature.
+int64_t oracle_partition_missing(const uint32_t* bins_of_rows, uint32_t* rows, int64_t count,
+                                 uint32_t min_bin, uint32_t max_bin, uint32_t threshold,
+                                 uint32_t most_freq_bin, uint32_t default_bin,
+                                 int32_t missing_type, int32_t default_left) {
+  const bool zero_missing = missing_type == 1, na_missing = missing_type == 2;
+  const bool mfb_zero = zero_missing && default_bin == most_freq_bin;
+  const bool mfb_na = na_missing && max_bin == most_freq_bin + min_bin && most_freq_bin > 0;
+  const int32_t lo = (int32_t)min_bin, hi = (int32_t)max_bin;
+  const int32_t shift = most_freq_bin == 0 ? 1 : 0;
+  const int32_t th = (int32_t)threshold + lo - shift;
+  const int32_t zero_bin = lo + (int32_t)default_bin - shift;
+  // 0 = left, 1 = right
+  const int mfb_side = most_freq_bin <= threshold ? 0 : 1;
+  const int missing_side = ((zero_missing || na_missing) && default_left) ? 0 : 1;
+  const bool oor_is_missing = (na_missing && mfb_na) || (zero_missing && mfb_zero);
+  const bool zero_sentinel = zero_missing && !mfb_zero;
+  const bool na_sentinel = na_missing && !mfb_na;
+  std::vector<uint32_t> L, R;
+  for (int64_t i = 0; i < count; ++i) {
+    const int32_t b = (int32_t)bins_of_rows[i];
+    int side;
+    if (zero_sentinel && b == zero_bin) {
+      side = missing_side;
+    } else if (lo == hi) {
+      if (b != hi)
+        side = oor_is_missing ? missing_side : mfb_side;
+      else
+        side = na_sentinel ? missing_side : (hi <= th ? 0 : 1);
+    } else if (na_sentinel && b == hi) {
+      side = missing_side;
+    } else if (b < lo || b > hi) {
+      side = oor_is_missing ? missing_side : mfb_side;
+    } else {
+      side = b > th ? 1 : 0;
+    }
+    (side ? R : L).push_back(rows[i]);
+  }
+  std::copy(L.begin(), L.end(), rows);
+  std::copy(R.begin(), R.end(), rows + L.size());
+  return (int64_t)L.size();
+}
+
 // SerialTreeLearner::train (spine path). Returns the number of splits made, or
 // a negative code. `cols` are feature-major bin columns of `bin_bytes` width.
 int32_t oracle_grow_tree(const void* const* cols, int32_t bin_bytes, int64_t num_data,

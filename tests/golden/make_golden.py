@@ -67,7 +67,9 @@ FILES = [
 
 
 def main() -> None:
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LGBM_REF_ROOT")
+    if not ref:
+        sys.exit("usage: make_golden.py <reference checkout> (or set LGBM_REF_ROOT)")
     for entry in FILES:
         rel, compress = entry[0], entry[1]
         src = os.path.join(ref, rel)

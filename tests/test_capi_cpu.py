@@ -29,7 +29,7 @@ def test_library_exports_every_header_symbol(capi):
     assert len(names) >= 20
     missing = [n for n in names if not hasattr(L, n)]
     assert not missing, missing
-    assert L.lgbm_b200_abi_version() == 103
+    assert L.lgbm_b200_abi_version() == 104
 
 
 def test_device_count_never_errors(capi):

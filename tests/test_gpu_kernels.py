@@ -161,6 +161,57 @@ def test_partition_golden_exact(capi):
     assert n >= 4
 
 
+def test_partition_golden_missing_fanout_exact(capi):
+    """Every partition.txt case, the six with missing_type != 0 included (missing zero /
+    NA with both default directions, the most frequent bin at the zero or NA bin),
+    through the device router, as crates/oracle-harness/tests/partition_parity.rs:112-190
+    replays them."""
+    L = capi.lib()
+    missing = 0
+    for c in G.partition_cases():
+        order = np.empty(len(c["bins"]), dtype=np.uint32)
+        sp = ctypes.c_int64(0)
+        capi.check(L.lgbm_b200_data_partition_missing(
+            capi.ptr(c["bins"]), len(c["bins"]), c["num_bin"], c["min_bin"], c["max_bin"],
+            c["threshold"], c["most_freq_bin"], c["default_bin"], c["missing_type"],
+            c["default_left"], capi.ptr(order), ctypes.byref(sp)))
+        assert order.tolist() == c["order"].tolist(), c["name"]
+        assert sp.value == c["split"], c["name"]
+        missing += c["missing_type"] != 0
+    assert missing == 6
+
+
+@pytest.mark.parametrize("missing_type", [1, 2])
+def test_partition_missing_random_matches_oracle(capi, missing_type):
+    """Multi-tile partitions with every missing-route flag combination against the
+    oracle's restatement of the same router."""
+    import oracle
+
+    L = capi.lib()
+    rng = np.random.default_rng(40 + missing_type)
+    n = 300_001
+    for trial in range(24):
+        num_bin = int(rng.integers(3, 40))
+        min_bin = int(rng.integers(0, 3))
+        max_bin = int(rng.integers(min_bin, num_bin)) if trial % 6 else min_bin
+        mfb = int(rng.integers(0, num_bin))
+        default_bin = mfb if trial % 4 == 0 else int(rng.integers(0, num_bin))
+        if missing_type == 2 and trial % 5 == 0 and max_bin > min_bin:
+            mfb = max_bin - min_bin  # the most frequent bin is the NA bin
+        thr = int(rng.integers(0, num_bin))
+        dl = int(trial % 2)
+        bins = rng.integers(0, num_bin, n).astype(np.uint32)
+        order = np.empty(n, dtype=np.uint32)
+        sp = ctypes.c_int64(0)
+        capi.check(L.lgbm_b200_data_partition_missing(
+            capi.ptr(bins), n, num_bin, min_bin, max_bin, thr, mfb, default_bin, missing_type,
+            dl, capi.ptr(order), ctypes.byref(sp)))
+        want, left = oracle.partition_missing(bins, np.arange(n, dtype=np.uint32), min_bin,
+                                              max_bin, thr, mfb, default_bin, missing_type, dl)
+        assert sp.value == left, trial
+        assert np.array_equal(order, want), trial
+
+
 def test_partition_large_random_matches_oracle(capi):
     """Multi-tile decoupled look-back path: 3M rows, every tile boundary case."""
     import oracle

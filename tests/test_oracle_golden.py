@@ -231,3 +231,95 @@ def test_lambdarank_training_real_lightgbm(oracle_lib):
             assert t[k].tolist() == m[k].tolist(), (i, k)
         assert [G.g17(x) for x in t["leaf_value"]] == [G.g17(x) for x in m["leaf_value"]], i
     assert out["scores"].view(np.uint64).tolist() == final.view(np.uint64).tolist()
+
+
+def test_oracle_numeric_binning_golden_bit_exact(oracle_lib):
+    """The oracle's own BinMapper restatement (oracle/bin_mapper.cpp) replays the
+    reference's 45 numeric binning goldens (crates/lgbm-dataset/tests/golden/)."""
+    cases = G.binning_cases()
+    assert len(cases) == 45
+    for c in cases:
+        m, bins = oracle_lib.bin_column(c["values"], max_bin=c["max_bin"],
+                                        min_data_in_bin=c["min_data_in_bin"],
+                                        min_data_in_leaf=c["min_split_data"],
+                                        pre_filter=c["pre_filter"], use_missing=c["use_missing"],
+                                        zero_as_missing=c["zero_as_missing"],
+                                        bin_construct_sample_cnt=c["sample_cnt"],
+                                        data_random_seed=c["seed"])
+        gold = c["golden"]
+        for k in ("num_bin", "missing_type", "default_bin", "most_freq_bin", "is_trivial"):
+            assert m[k] == gold[k], (c["name"], k)
+        gn, wn = np.isnan(m["upper"]), np.isnan(gold["upper"])
+        assert gn.tolist() == wn.tolist(), c["name"]
+        assert m["upper"].view(np.uint64)[~gn].tolist() == \
+            gold["upper"].view(np.uint64)[~wn].tolist(), c["name"]
+        assert bins.tolist() == c["assign"].tolist(), c["name"]
+
+
+def test_oracle_categorical_binning_golden(oracle_lib):
+    """categorical_folding.txt through the oracle's BinMapper restatement."""
+    cases = G.categorical_binning_cases()
+    assert len(cases) == 6
+    for c in cases:
+        m, bins = oracle_lib.bin_column(c["values"], max_bin=c["max_bin"],
+                                        min_data_in_bin=c["min_data_in_bin"],
+                                        min_data_in_leaf=c["min_split_data"],
+                                        pre_filter=c["pre_filter"], use_missing=c["use_missing"],
+                                        zero_as_missing=c["zero_as_missing"],
+                                        bin_construct_sample_cnt=max(len(c["values"]), 1),
+                                        categorical=True)
+        gm = c["mapper"]
+        for k in ("num_bin", "missing_type", "default_bin", "most_freq_bin"):
+            assert m[k] == gm[k], (c["name"], k)
+        assert m["is_trivial"] == bool(gm["is_trivial"]), c["name"]
+        assert m["bin_to_category"].tolist() == c["b2c"], c["name"]
+        assert bins.tolist() == c["assign"].tolist(), c["name"]
+
+
+@pytest.mark.parametrize("kind", ["normal", "skewed_nan", "categorical", "sparse"])
+def test_oracle_binning_equals_product_binning(oracle_lib, kind):
+    """The product's host binning and the oracle's restatement agree on sampled
+    columns larger than the sample (200k of 400k rows), including NaN, zero-heavy and
+    categorical columns like those of the bench workloads."""
+    import lightgbm_rs_b200 as lgb
+
+    r = np.random.default_rng(hash(kind) % 2**32)
+    n = 400_000
+    cat = False
+    if kind == "normal":
+        x = r.normal(size=n)
+    elif kind == "skewed_nan":
+        x = np.exp(r.normal(size=n))
+        x[r.random(n) < 0.1] = np.nan
+    elif kind == "categorical":
+        x = np.minimum(r.zipf(1.2, n), 900).astype(np.float64)
+        cat = True
+    else:
+        x = np.where(r.random(n) < 0.8, 0.0, r.exponential(size=n))
+    for max_bin, min_leaf in ((255, 20), (63, 100)):
+        kw = dict(max_bin=max_bin, min_data_in_leaf=min_leaf, categorical=cat)
+        mo, bo = oracle_lib.bin_column(x, **kw)
+        mp, bp = lgb.bin_column(x, **kw)
+        for k in ("num_bin", "missing_type", "default_bin", "most_freq_bin", "is_trivial"):
+            assert mo[k] == mp[k], (kind, k)
+        key = "bin_to_category" if cat else "upper"
+        assert np.array_equal(mo[key], mp[key], equal_nan=not cat), kind
+        assert np.array_equal(bo, bp), kind
+
+
+def test_partition_golden_missing_fanout(oracle_lib):
+    """Every partition.txt case, the six missing_type != 0 ones included, through the
+    oracle's restatement of the kernel router with its whole missing-value fan-out
+    (crates/oracle-harness/tests/partition_parity.rs:112-190 replays them the same way)."""
+    cases = G.partition_cases()
+    missing = 0
+    for c in cases:
+        rows = np.arange(len(c["bins"]), dtype=np.uint32)
+        order, left = oracle_lib.partition_missing(c["bins"], rows, c["min_bin"], c["max_bin"],
+                                                   c["threshold"], c["most_freq_bin"],
+                                                   c["default_bin"], c["missing_type"],
+                                                   c["default_left"])
+        assert order.tolist() == c["order"].tolist(), c["name"]
+        assert left == c["split"], c["name"]
+        missing += c["missing_type"] != 0
+    assert missing == 6

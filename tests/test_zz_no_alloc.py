@@ -87,6 +87,36 @@ def test_noalloc_repeated_identical_calls(capi):
         assert np.array_equal(got[0], want[0])
 
 
+def test_noalloc_keeps_device_memory_unchanged(capi):
+    """After a warm-up call (which loads the module and looks the scratch array up), a
+    batch of calls leaves the device's free memory exactly as it was: nothing is
+    allocated and kept."""
+    import torch
+
+    L = capi.lib()
+    r = np.random.default_rng(31)
+    n = 2_000_000
+    d_bins = torch.from_numpy(r.integers(0, 256, n).astype(np.uint8)).cuda()
+    d_order = torch.empty(n, dtype=torch.int32, device="cuda")
+    d_sp = torch.empty(1, dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call():
+        capi.check(L.lgbm_b200_data_partition_noalloc(d_bins.data_ptr(), n, 256, 0, 255, 77,
+                                                      3, d_order.data_ptr(),
+                                                      d_sp.data_ptr(), stream))
+
+    call()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(8):
+        call()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert 0 <= int(d_sp.item()) <= n
+
+
 def test_noalloc_empty_and_limit(capi):
     import torch
 
