@@ -86,9 +86,12 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the f32 and full-length runs and the parity check")
-    ap.add_argument("--measure", default="boosting", choices=["boosting", "binning"],
+    ap.add_argument("--measure", default="boosting", choices=["boosting", "binning", "profile"],
                     help="binning: time Dataset construction from raw C1 values (device "
-                         "value_to_bin) against host value_to_bin on all cores")
+                         "value_to_bin) against host value_to_bin on all cores; profile: "
+                         "W warm-up iterations, then one iteration with every kernel launched "
+                         "on its own (the case the committed ncu captures are taken on), "
+                         "printing its algorithmic bytes per kernel class")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     if args.rows is None:
@@ -728,12 +731,44 @@ def run_binning(args):
     print(json.dumps(out), flush=True)
 
 
+def run_profile_case(args):
+    """The capture case of the committed ncu summaries: W warm-up iterations through the
+    training graph, then one iteration whose kernels run one at a time
+    (Booster.profile_iteration), with the algorithmic bytes of that iteration's launches.
+    Skip 761 x W tree-kernel launches (C1: 1 root build + 254 control steps + 254 main
+    and 252 look-ahead partitions per iteration) to capture the profiled iteration."""
+    import lightgbm_rs_b200 as lgb
+    from lightgbm_rs_b200 import build as libbuild
+
+    libbuild.build()
+    data = make_data(args.workload, args.rows)
+    p = params(args.workload, args.grad)
+    ds = lgb.Dataset(bins=data.bins, mappers=data.mappers, label=data.y, params=p,
+                     group=data.group)
+    b = lgb.Booster(p, ds)
+    b.update(args.warmup)
+    kms, counts = b.profile_iteration()
+    kb = kernel_bytes(counts, data.rows, args.grad, data.features)
+    launches = b.profile_launches()
+    per = {}
+    for cls, ms in launches:
+        e = per.setdefault(cls, {"launches": 0, "ms": 0.0})
+        e["launches"] += 1
+        e["ms"] += ms
+    print(json.dumps({"measure": "profile", "workload": workload_desc(args, data),
+                      "warmup": args.warmup, "counts": counts, "algorithmic_bytes": kb,
+                      "event_ms_by_class": kms, "launches_by_class": per}), flush=True)
+
+
 def main():
     args = parse()
     if args.warmup < 3:
         args.warmup = 3
     if args.measure == "binning":
         run_binning(args)
+        return
+    if args.measure == "profile":
+        run_profile_case(args)
         return
     if args.impl == "reference":
         run_reference(args)

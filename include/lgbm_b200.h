@@ -165,6 +165,14 @@ typedef struct lgbm_b200_train_config {
   int32_t lambdarank_norm;
   int32_t num_label_gain;
   const double* label_gain;
+  /* use_quantized_grad only: stochastic rounding (the reference's default,
+   * crates/lgbm-core/src/config/mod.rs:485): rounding offsets from the reference's
+   * seeded xorshift64 (crates/lgbm-treelearner/src/gradient_discretizer.rs:252-262),
+   * seed ((iteration << 20) ^ 0x51702010) per iteration (crates/lgbm-boosting/src/
+   * gbdt.rs:950), drawn over the rows of the whole job in row order (a data-parallel
+   * job: rank 0's rows first). 0: deterministic rounding (offset 0.5). */
+  int32_t stochastic_rounding;
+  int32_t _reserved0;
 } lgbm_b200_train_config;
 
 /* BinMapper::find_bin_from_column parameters (crates/lgbm-dataset/src/bin_mapper.rs:642-675). */

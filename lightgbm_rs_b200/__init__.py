@@ -38,10 +38,10 @@ _DEFAULTS = {
     "data_random_seed": 1,
     "use_missing": True,
     "zero_as_missing": False,
-    "feature_pre_filter": False,
+    "feature_pre_filter": True,
     "use_quantized_grad": False,
     "num_grad_quant_bins": 4,
-    "stochastic_rounding": False,
+    "stochastic_rounding": True,
     "min_data_per_group": 100,
     "max_cat_threshold": 32,
     "max_cat_to_onehot": 4,
@@ -76,10 +76,21 @@ def _resolve(params):
     for k, v in (params or {}).items():
         k = _ALIASES.get(k, k)
         p[k] = v
-    if p.get("stochastic_rounding"):
-        raise LightGBMError(C.CAPABILITY_UNAVAILABLE,
-                            "stochastic_rounding=true is not on the device path")
     return p
+
+
+def _excluded(m):
+    """A trivial feature's mapper as a one-bin feature that never splits. The reference
+    leaves trivial features out of the dataset (lgbm-dataset/src/dataset.rs:106-126:
+    used features are the non-trivial ones); a one-bin feature has no threshold, so the
+    trees are the same while feature indices stay those of the input columns."""
+    out = dict(m)
+    out.update(num_bin=1, default_bin=0, most_freq_bin=0, missing_type=0, is_trivial=True)
+    if m.get("bin_type", 0) == 1:
+        out["bin_to_category"] = np.array([-1], dtype=np.int32)
+    else:
+        out["upper"] = np.array([np.inf], dtype=np.float64)
+    return out
 
 
 def bin_column(values, max_bin=255, min_data_in_bin=3, min_data_in_leaf=20, pre_filter=False,
@@ -174,7 +185,7 @@ class Dataset:
         def one(j):
             m, _ = bin_column(self._values[j], want_bins=False, categorical=j in self._cats,
                               **kw)
-            return m
+            return _excluded(m) if m["is_trivial"] else m
 
         with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4)) as ex:
             return list(ex.map(one, range(self.num_features)))
@@ -187,6 +198,9 @@ class Dataset:
             kw = self._bin_kwargs()
             cols = []
             for j in range(self.num_features):
+                if self.mappers[j]["num_bin"] == 1:  # constant or left out: one bin
+                    cols.append(np.zeros(self.num_data, dtype=np.uint32))
+                    continue
                 _, b = bin_column(self._values[j], categorical=j in self._cats, **kw)
                 cols.append(b)
             wide = any(m["num_bin"] > 256 for m in self.mappers)
@@ -388,6 +402,7 @@ class Booster:
         cfg = C.TrainConfig(_learner_config(p), _OBJECTIVES[obj], int(bool(p["use_quantized_grad"])),
                             int(p["num_grad_quant_bins"]), int(bool(p["boost_from_average"])),
                             float(p["sigmoid"]), float(p["learning_rate"]))
+        cfg.stochastic_rounding = int(bool(p["stochastic_rounding"]))
         self._rank_arrays = None
         if obj == "lambdarank":
             qb = train_set.query_boundaries

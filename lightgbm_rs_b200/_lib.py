@@ -83,7 +83,8 @@ class TrainConfig(ctypes.Structure):
                 ("num_grad_quant_bins", _i32), ("boost_from_average", _i32), ("sigmoid", _f64),
                 ("learning_rate", _f64), ("query_boundaries", _P), ("num_queries", _i32),
                 ("lambdarank_truncation_level", _i32), ("lambdarank_norm", _i32),
-                ("num_label_gain", _i32), ("label_gain", _P)]
+                ("num_label_gain", _i32), ("label_gain", _P), ("stochastic_rounding", _i32),
+                ("_reserved0", _i32)]
 
 
 class BinConfig(ctypes.Structure):

@@ -702,6 +702,7 @@ struct lgbm_b200_booster {
   DevBuf<int32_t> rank_qb;
   DevBuf<double> rank_f64;  // sigmoid table | discounts | label gains | inverse max DCGs
   DevBuf<int32_t> rank_order;
+  DevBuf<unsigned long long> xs_pow;  // stochastic rounding: xorshift jump matrices
   double init_score = 0.0;
   ObjDev obj{};
   FinishDev fin{};
@@ -1613,7 +1614,7 @@ namespace {
 // All ranks' labels in global row order (shards in rank order), gathered once so that
 // the init score is computed exactly as on one device.
 int gather_labels(lgbm_b200_comm* comm, const float* labels, int64_t n_local, cudaStream_t st,
-                  std::vector<float>* all) {
+                  std::vector<float>* all, int64_t* row_offset) {
   const int R = comm->nranks;
   DevBuf<long long> cnt;
   CUDA_TRY(cnt.alloc((size_t)R + 1));
@@ -1630,6 +1631,8 @@ int gather_labels(lgbm_b200_comm* comm, const float* labels, int64_t n_local, cu
     mx = std::max(mx, c);
     total += c;
   }
+  *row_offset = 0;
+  for (int k = 0; k < comm->rank && k < R; ++k) *row_offset += counts[k];
   DevBuf<float> send, recv;
   CUDA_TRY(send.alloc((size_t)std::max(mx, 1ll)));
   CUDA_TRY(recv.alloc((size_t)std::max(mx, 1ll) * R));
@@ -1905,8 +1908,9 @@ int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
   std::vector<float> gathered;
   const float* all = labels;
   int64_t NG = N;
+  int64_t row_offset = 0;
   if (comm) {
-    rc = gather_labels(comm, labels, N, b->learner->stream, &gathered);
+    rc = gather_labels(comm, labels, N, b->learner->stream, &gathered, &row_offset);
     if (rc) return rc;
     all = gathered.data();
     NG = (int64_t)gathered.size();
@@ -1966,6 +1970,16 @@ int booster_create_impl(lgbm_b200_dataset* ds, const float* labels,
   o.ghp = b->ghp.p;
   o.num_quant_bins = cfg->num_grad_quant_bins;
   o.stopped = b->state.p;
+  o.iter_counter = b->state.p + 1;
+  o.row_offset = row_offset;
+  if (cfg->use_quantized_grad && cfg->stochastic_rounding) {
+    std::vector<unsigned long long> pow(64 * 64);
+    xorshift_pow_table(pow.data());
+    CUDA_TRY(b->xs_pow.alloc(pow.size()));
+    CUDA_TRY(cudaMemcpy(b->xs_pow.p, pow.data(), pow.size() * 8, cudaMemcpyHostToDevice));
+    o.stochastic = 1;
+    o.xs_pow = b->xs_pow.p;
+  }
   if (rank) {
     const size_t nq = rt.inv_max.size();
     CUDA_TRY(b->rank_qb.alloc(nq + 1));

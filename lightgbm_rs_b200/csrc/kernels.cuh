@@ -235,7 +235,17 @@ struct ObjDev {
   const double* label_gain;   // gain of each integer label
   const double* inv_max_dcg;  // [num_queries] 1 / max DCG at the truncation level
   int32_t* order;             // [N] each query's rows by descending score
+  // Stochastic rounding of the quantized gradients (stochastic_rounding=true): the
+  // reference's xorshift64 stream over the rows of the whole job in row order, seeded per
+  // iteration from *iter_counter. xs_pow[64 j + k] is column k of T^(2^j), T the 64x64
+  // bit matrix of one xorshift step, for jumping to a row's place in the stream.
+  int32_t stochastic;
+  int32_t _sr_pad;
+  const int32_t* iter_counter;
+  int64_t row_offset;  // global index of this device's first row
+  const unsigned long long* xs_pow;
 };
+void xorshift_pow_table(unsigned long long* out /* [64 * 64] */);
 constexpr int64_t kRankSigmoidBins = 1 << 20;  // LambdarankNDCG::_sigmoid_bins
 void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof = nullptr,
                       const DeviceComm* comm = nullptr);

@@ -434,6 +434,109 @@ __global__ void __launch_bounds__(kObjThreads) k_quantize(ObjDev o) {
   }
 }
 
+// ------------------------------------------------------------------------------------
+// GradientDiscretizer::quantize_pair with stochastic rounding
+// (lgbm-treelearner/src/gradient_discretizer.rs:167-191, 252-262; seed per iteration
+// gbdt.rs:950). The offsets are one xorshift64 stream over every row of the job in row
+// order, a gradient draw then a hessian draw per row. The stream is linear over GF(2),
+// so a warp jumps to its segment's place with bit-matrix products (one per set bit of
+// 2 x the segment's first global row), then hands each lane the state 64 draws further
+// on; each lane then runs the sequential stream over its 32 consecutive rows. Rows are
+// staged through shared memory so that global loads and stores stay coalesced.
+// ------------------------------------------------------------------------------------
+constexpr int kSrLaneRows = 32;
+constexpr int kSrWarpRows = 32 * kSrLaneRows;
+constexpr int kSrThreads = 128;
+constexpr int kSrLanePow = 6;  // 2 draws x kSrLaneRows rows = 2^6 steps per lane
+static_assert(2 * kSrLaneRows == (1 << kSrLanePow), "lane stride is a power of two");
+
+__device__ __forceinline__ unsigned long long xs_step_warp(const unsigned long long* cols,
+                                                           unsigned long long s, int lane) {
+  // y = M s over GF(2): lane l folds columns 2l and 2l+1, then the warp XOR-reduces
+  const unsigned long long c0 = cols[2 * lane], c1 = cols[2 * lane + 1];
+  unsigned long long y = (((s >> (2 * lane)) & 1ull) ? c0 : 0ull) ^
+                         (((s >> (2 * lane + 1)) & 1ull) ? c1 : 0ull);
+  for (int o = 16; o > 0; o >>= 1) y ^= __shfl_xor_sync(0xffffffffu, y, o);
+  return y;
+}
+
+__device__ __forceinline__ double xs_next_u01(unsigned long long& x) {
+  x ^= x << 13;
+  x ^= x >> 7;
+  x ^= x << 17;
+  return (double)(x >> 11) / 9007199254740992.0;  // 2^53
+}
+
+__global__ void __launch_bounds__(kSrThreads) k_quantize_sr(ObjDev o) {
+  if (o.stopped && *o.stopped) return;
+  constexpr int kWarps = kSrThreads / 32;
+  constexpr int kPad = kSrWarpRows + kSrWarpRows / 32;
+  __shared__ float s_g[kWarps][kPad];
+  __shared__ float s_h[kWarps][kPad];
+  const DevGhParams& p = *o.ghp;
+  const float2* gh = reinterpret_cast<const float2*>(o.gh);
+  uint16_t* q = reinterpret_cast<uint16_t*>(reinterpret_cast<float2*>(o.gh) + o.N);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t warps_total = (int64_t)gridDim.x * kWarps;
+  const int64_t gw = (int64_t)blockIdx.x * kWarps + w;
+  const unsigned long long seed =
+      ((unsigned long long)(uint32_t)*o.iter_counter << 20) ^ 0x51702010ull;
+  const unsigned long long s0 = seed ^ 0x9E3779B97F4A7C15ull;
+  const double igs = p.inv_grad_scale, ihs = p.inv_hess_scale;
+  const bool cst = p.is_const_hess != 0;
+  const bool pack = p.mode == GH_QPACK;
+  long long sa = 0, sb = 0;
+  for (int64_t seg = gw * kSrWarpRows; seg < o.N; seg += warps_total * kSrWarpRows) {
+    const int nrows = (int)min((int64_t)kSrWarpRows, o.N - seg);
+    for (int k = lane; k < nrows; k += 32) {
+      const float2 v = gh[seg + k];
+      s_g[w][k + (k >> 5)] = v.x;
+      s_h[w][k + (k >> 5)] = v.y;
+    }
+    __syncwarp();
+    unsigned long long st = s0;
+    unsigned long long e = 2ull * (unsigned long long)(o.row_offset + seg);
+    for (int j = 0; e != 0ull; ++j, e >>= 1)
+      if (e & 1ull) st = xs_step_warp(o.xs_pow + 64 * j, st, lane);
+    unsigned long long mine = st;
+    for (int l = 1; l < 32; ++l) {
+      st = xs_step_warp(o.xs_pow + 64 * kSrLanePow, st, lane);
+      if (lane == l) mine = st;
+    }
+    for (int k = 0; k < kSrLaneRows; ++k) {
+      const int r = lane * kSrLaneRows + k;
+      const double bg = xs_next_u01(mine);
+      const double bh = xs_next_u01(mine);
+      if (r >= nrows) continue;
+      const int pr = r + (r >> 5);
+      const float gv32 = s_g[w][pr], hv32 = s_h[w][pr];
+      const double gv = (double)gv32 * igs;
+      const int qg = as_i8(gv32 >= 0.0f ? gv + bg : gv - bg);
+      const int qh = cst ? 1 : as_i8((double)hv32 * ihs + bh);
+      s_g[w][pr] = __uint_as_float((uint32_t)((qg & 0xff) | ((qh & 0xff) << 8)));
+      if (pack) {
+        sa += qg;
+        sb += qh == 3 ? (1ll << 32) : (long long)qh;
+      } else {
+        sa += p.lut_g[qg + 128];
+        sb += p.lut_h[qh + 128];
+      }
+    }
+    __syncwarp();
+    for (int k = lane; k < nrows; k += 32)
+      q[seg + k] = (uint16_t)__float_as_uint(s_g[w][k + (k >> 5)]);
+    __syncwarp();
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    sa += __shfl_xor_sync(0xffffffffu, sa, off);
+    sb += __shfl_xor_sync(0xffffffffu, sb, off);
+  }
+  if (lane == 0) {
+    atomicAdd((unsigned long long*)&o.ghp->root_g, (unsigned long long)sa);
+    atomicAdd((unsigned long long*)&o.ghp->root_h, (unsigned long long)sb);
+  }
+}
+
 __global__ void __launch_bounds__(kObjThreads) k_root_sums_float(ObjDev o) {
   if (o.stopped && *o.stopped) return;
   const DevGhParams& p = *o.ghp;
@@ -591,12 +694,39 @@ void launch_gradients(const ObjDev& o, cudaStream_t st, LaunchProfiler* prof,
     comm->max_u32(comm->ctx, &o.ghp->max_abs_g_bits, 4, st);
   }
   k_gh_scales<<<1, 1, 0, st>>>(o);
-  if (o.gh_mode == GH_FLOAT)
+  if (o.gh_mode == GH_FLOAT) {
     k_root_sums_float<<<grid, kObjThreads, 0, st>>>(o);
-  else
+  } else if (o.stochastic) {
+    const int64_t segs = (o.N + kSrWarpRows - 1) / kSrWarpRows;
+    const int64_t blocks = (segs + kSrThreads / 32 - 1) / (kSrThreads / 32);
+    k_quantize_sr<<<(int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)grid * 2)),
+                    kSrThreads, 0, st>>>(o);
+  } else {
     k_quantize<<<grid, kObjThreads, 0, st>>>(o);
+  }
   if (comm) comm->sum_i64(comm->ctx, &o.ghp->root_g, 2, st);
   if (prof) prof->end(st, slot);
+}
+
+// Columns of T^(2^j), j = 0..63, for T the bit matrix of one xorshift64 step (the
+// reference's next_u01 shifts 13, 7, 17): out[64 j + k] = T^(2^j) e_k.
+void xorshift_pow_table(unsigned long long* out) {
+  auto step = [](unsigned long long x) {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    return x;
+  };
+  for (int k = 0; k < 64; ++k) out[k] = step(1ull << k);
+  for (int j = 1; j < 64; ++j) {
+    const unsigned long long* m = out + 64 * (j - 1);
+    for (int k = 0; k < 64; ++k) {
+      unsigned long long x = m[k], y = 0ull;  // M (M e_k)
+      for (int b = 0; b < 64; ++b)
+        if ((x >> b) & 1ull) y ^= m[b];
+      out[64 * j + k] = y;
+    }
+  }
 }
 
 void launch_learner_gradients(const ObjDev& o, int32_t kind, cudaStream_t st) {

@@ -170,6 +170,8 @@ def lib():
         L.oracle_l2_boost_from_score.argtypes = [_P, ctypes.c_int64]
         L.oracle_l2_boost_from_score.restype = ctypes.c_double
         L.oracle_quantize.argtypes = [_P, _P, ctypes.c_int64, ctypes.c_int32, _P, _P]
+        L.oracle_quantize_ex.argtypes = [_P, _P, ctypes.c_int64, ctypes.c_int32, _P, _P,
+                                         ctypes.c_int32, ctypes.c_uint64]
         L.oracle_tree_shrinkage.argtypes = [_P, ctypes.c_int32, _P, ctypes.c_double]
         L.oracle_add_prediction_to_score.argtypes = [_P, ctypes.c_int32, _P, _P, _P, _P]
         L.oracle_max_threads.restype = ctypes.c_int32
@@ -381,14 +383,21 @@ def boost_from_score(objective, label, sigmoid=1.0):
     return lib().oracle_l2_boost_from_score(_ptr(label), len(label))
 
 
-def quantize(g, h, num_grad_quant_bins):
-    """Returns (dequantized g, dequantized h, int8 pairs [N,2] (qg, qh), scales)."""
+def stochastic_seed(iteration, class_id=0):
+    """The per-(iteration, class) seed of stochastic rounding (lgbm-boosting/src/gbdt.rs:950)."""
+    return ((int(iteration) << 20) ^ int(class_id) ^ 0x51702010) & 0xFFFFFFFFFFFFFFFF
+
+
+def quantize(g, h, num_grad_quant_bins, stochastic=False, seed=0):
+    """Returns (dequantized g, dequantized h, int8 pairs [N,2] (qg, qh), scales).
+    stochastic: stochastic rounding from the reference's seeded xorshift64
+    (gradient_discretizer.rs:252-262) with `seed` (see stochastic_seed)."""
     g = np.array(g, dtype=np.float32)
     h = np.array(h, dtype=np.float32)
     q = np.empty((len(g), 2), dtype=np.int8)
     scales = np.empty(3, dtype=np.float64)
-    lib().oracle_quantize(_ptr(g), _ptr(h), len(g), int(num_grad_quant_bins), _ptr(q),
-                          _ptr(scales))
+    lib().oracle_quantize_ex(_ptr(g), _ptr(h), len(g), int(num_grad_quant_bins), _ptr(q),
+                             _ptr(scales), int(bool(stochastic)), ctypes.c_uint64(seed))
     return g, h, q, scales
 
 
@@ -412,7 +421,8 @@ def max_threads():
 
 def train(bins_cols, metas, labels, objective="binary", num_iterations=10, learning_rate=0.1,
           num_leaves=31, max_depth=-1, use_quantized_grad=False, num_grad_quant_bins=4,
-          boost_from_average=True, sigmoid=1.0, nthreads=1, record=False,
+          stochastic_rounding=False, boost_from_average=True, sigmoid=1.0, nthreads=1,
+          record=False,
           query_boundaries=None, lambdarank_norm=True, lambdarank_truncation_level=30,
           label_gain=None, **gain_kw):
     """Gbdt::train_one_iter loop (lgbm-boosting/src/gbdt.rs:691-1300), non-bagging GBDT.
@@ -443,7 +453,8 @@ def train(bins_cols, metas, labels, objective="binary", num_iterations=10, learn
         if record:
             iter_gh.append((g.copy(), h.copy()))
         if use_quantized_grad:
-            g, h, _, _ = quantize(g, h, num_grad_quant_bins)
+            g, h, _, _ = quantize(g, h, num_grad_quant_bins, stochastic_rounding,
+                                  stochastic_seed(it))
         tree, part, _ = grow_tree(bins_cols, metas, g, h, num_leaves, max_depth, nthreads,
                                   **gain_kw)
         if tree["num_leaves"] > 1:

@@ -1321,9 +1321,34 @@ double oracle_l2_boost_from_score(const float* label, int64_t n) {
 // (lgbm-treelearner/src/gradient_discretizer.rs:126-191), deterministic rounding.
 // Writes the int8 pair (qg, qh) per row when q_out != NULL and the dequantized f32
 // values back into g/h. scales_out = {grad_scale, hess_scale, is_constant_hessian}.
+// GradientDiscretizer with stochastic rounding (gradient_discretizer.rs:83-90,167-191,
+// 252-262): a seeded xorshift64, one draw for the gradient then one for the hessian of
+// every row in row order, each draw the top 53 bits over 2^53.
+struct Xorshift64 {
+  uint64_t s;
+  double next_u01() {
+    s ^= s << 13;
+    s ^= s >> 7;
+    s ^= s << 17;
+    return (double)(s >> 11) / (double)(1ull << 53);
+  }
+};
+
+void oracle_quantize_ex(float* g, float* h, int64_t n, int32_t num_grad_quant_bins,
+                        int8_t* q_out, double* scales_out, int32_t stochastic, uint64_t seed);
+
 void oracle_quantize(float* g, float* h, int64_t n, int32_t num_grad_quant_bins,
                      int8_t* q_out, double* scales_out) {
+  oracle_quantize_ex(g, h, n, num_grad_quant_bins, q_out, scales_out, 0, 0);
+}
+
+// stochastic != 0: the rounding offsets come from the xorshift stream seeded with
+// seed ^ 0x9E3779B97F4A7C15 (new_stochastic); the caller passes the per-iteration seed
+// of gbdt.rs:950, ((iter << 20) ^ class ^ 0x51702010).
+void oracle_quantize_ex(float* g, float* h, int64_t n, int32_t num_grad_quant_bins,
+                        int8_t* q_out, double* scales_out, int32_t stochastic, uint64_t seed) {
   if (n == 0) return;
+  Xorshift64 rng{seed ^ 0x9E3779B97F4A7C15ull};
   bool is_const = true;
   for (int64_t i = 0; i < n; ++i)
     if (!(h[i] == h[0])) {
@@ -1340,9 +1365,14 @@ void oracle_quantize(float* g, float* h, int64_t n, int32_t num_grad_quant_bins,
   const double hs = is_const ? max_h : max_h / (double)num_grad_quant_bins;
   const double igs = 1.0 / gs, ihs = 1.0 / hs;
   for (int64_t i = 0; i < n; ++i) {
+    double bg = 0.5, bh = 0.5;
+    if (stochastic) {
+      bg = rng.next_u01();
+      bh = rng.next_u01();
+    }
     const double gv = (double)g[i] * igs;
-    const int8_t qg = (int8_t)(int32_t)(g[i] >= 0.0f ? gv + 0.5 : gv - 0.5);
-    const int8_t qh = is_const ? (int8_t)1 : (int8_t)(int32_t)((double)h[i] * ihs + 0.5);
+    const int8_t qg = (int8_t)(int32_t)(g[i] >= 0.0f ? gv + bg : gv - bg);
+    const int8_t qh = is_const ? (int8_t)1 : (int8_t)(int32_t)((double)h[i] * ihs + bh);
     if (q_out) {
       q_out[2 * i] = qg;
       q_out[2 * i + 1] = qh;

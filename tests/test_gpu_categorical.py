@@ -124,6 +124,7 @@ def test_categorical_booster_bit_exact_and_predict():
     booster = lgb.train(params, ds, num_boost_round=6)
     ref = oracle.train(ds.bins, metas, y, objective="binary", num_iterations=6,
                        learning_rate=0.1, num_leaves=31, use_quantized_grad=True,
+                       stochastic_rounding=True,
                        num_grad_quant_bins=4, min_data_in_leaf=20, min_data_per_group=50,
                        cat_smooth=5.0)
     for i, (a, b) in enumerate(zip(booster.trees(), ref["trees"])):

@@ -112,6 +112,7 @@ def test_booster_quantized_bit_exact_vs_oracle(data):
     booster = lgb.train(params, ds, num_boost_round=10)
     ref = oracle.train(ds.bins, metas, y, objective="binary", num_iterations=10,
                        learning_rate=0.1, num_leaves=31, use_quantized_grad=True,
+                       stochastic_rounding=True,
                        num_grad_quant_bins=4, min_data_in_leaf=20)
     trees = booster.trees()
     assert len(trees) == len(ref["trees"])
@@ -119,6 +120,59 @@ def test_booster_quantized_bit_exact_vs_oracle(data):
         _assert_trees_bit_equal(a, b, f"tree {i}")
     s = booster.train_scores()
     assert s.view(np.uint64).tolist() == ref["scores"].view(np.uint64).tolist()
+
+
+@pytest.mark.parametrize("stochastic", [False, True])
+def test_booster_quantized_rounding_modes(data, stochastic):
+    """Deterministic rounding (the reference's bit-exact gate) and stochastic rounding
+    (its default: the seeded xorshift64 stream of gradient_discretizer.rs:252-262, seed
+    per iteration gbdt.rs:950), 5 iterations of 63 leaves, bit-exact vs the oracle."""
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    X, y, ds, metas = data
+    params = {"objective": "binary", "num_leaves": 63, "min_data_in_leaf": 20,
+              "learning_rate": 0.1, "use_quantized_grad": True, "num_grad_quant_bins": 4,
+              "stochastic_rounding": stochastic}
+    booster = lgb.train(params, ds, num_boost_round=5)
+    ref = oracle.train(ds.bins, metas, y, objective="binary", num_iterations=5,
+                       learning_rate=0.1, num_leaves=63, use_quantized_grad=True,
+                       stochastic_rounding=stochastic, num_grad_quant_bins=4,
+                       min_data_in_leaf=20)
+    for i, (a, b) in enumerate(zip(booster.trees(), ref["trees"])):
+        _assert_trees_bit_equal(a, b, f"tree {i}")
+    assert booster.train_scores().tobytes() == ref["scores"].tobytes()
+
+
+def test_booster_stochastic_rounding_many_segments():
+    """2.1M rows: the device jumps each 1024-row segment to its place in the xorshift
+    stream (up to 2^22 steps); trees and scores bit-exact vs the oracle's sequential
+    stream, L2 objective (constant hessian: the hessian draw is still consumed)."""
+    import lightgbm_rs_b200 as lgb
+    import oracle
+
+    rng = np.random.default_rng(17)
+    n, F = 2_100_000, 6
+    bins = rng.integers(0, 64, (F, n)).astype(np.uint8)
+    y = (bins[0].astype(np.float32) * 0.05 - bins[1] * 0.02 +
+         rng.normal(0, 0.5, n).astype(np.float32)).astype(np.float32)
+    mappers = [{"num_bin": 64, "default_bin": 0, "most_freq_bin": 0, "missing_type": 0,
+                "bin_type": 0, "upper": np.arange(64, dtype=np.float64) + 0.5,
+                "is_trivial": False} for _ in range(F)]
+    params = {"objective": "regression", "num_leaves": 15, "min_data_in_leaf": 20,
+              "learning_rate": 0.1, "use_quantized_grad": True, "num_grad_quant_bins": 4,
+              "stochastic_rounding": True}
+    ds = lgb.Dataset(bins=bins, mappers=mappers, label=y, params=params)
+    booster = lgb.train(params, ds, num_boost_round=3)
+    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
+             for m in mappers]
+    ref = oracle.train(bins, metas, y, objective="regression", num_iterations=3,
+                       learning_rate=0.1, num_leaves=15, use_quantized_grad=True,
+                       stochastic_rounding=True, num_grad_quant_bins=4, min_data_in_leaf=20,
+                       nthreads=oracle.max_threads())
+    for i, (a, b) in enumerate(zip(booster.trees(), ref["trees"])):
+        _assert_trees_bit_equal(a, b, f"tree {i}")
+    assert booster.train_scores().tobytes() == ref["scores"].tobytes()
 
 
 def test_booster_float_predictions_close(data):
@@ -149,7 +203,8 @@ def test_booster_l2_quantized_constant_hessian(data):
               "use_quantized_grad": True, "num_grad_quant_bins": 4}
     booster = lgb.train(params, ds2, num_boost_round=5)
     ref = oracle.train(ds.bins, metas, yr, objective="l2", num_iterations=5, learning_rate=0.1,
-                       num_leaves=15, use_quantized_grad=True, num_grad_quant_bins=4,
+                       num_leaves=15, use_quantized_grad=True,
+                       stochastic_rounding=True, num_grad_quant_bins=4,
                        min_data_in_leaf=20)
     for i, (a, b) in enumerate(zip(booster.trees(), ref["trees"])):
         _assert_trees_bit_equal(a, b, f"l2 tree {i}")
@@ -246,8 +301,44 @@ def test_missing_values_booster_bit_exact():
     booster = lgb.train(params, ds, num_boost_round=6)
     ref = oracle.train(ds.bins, metas, y, objective="binary", num_iterations=6,
                        learning_rate=0.1, num_leaves=31, use_quantized_grad=True,
+                       stochastic_rounding=True,
                        num_grad_quant_bins=4, min_data_in_leaf=20)
     for i, (a, b) in enumerate(zip(booster.trees(), ref["trees"])):
         _assert_trees_bit_equal(a, b, f"missing tree {i}")
     s = booster.train_scores()
     assert s.view(np.uint64).tolist() == ref["scores"].view(np.uint64).tolist()
+
+
+def test_trivial_features_left_out():
+    """feature_pre_filter (the reference default, true): a constant column and a column
+    with too few non-zero rows for any split of min_data_in_leaf rows on both sides are
+    trivial, so the reference leaves them out of the dataset
+    (lgbm-dataset/src/dataset.rs:106-126). Here they become one-bin features that never
+    split; trees and scores stay bit-exact vs the oracle."""
+    import lightgbm_rs_b200 as lgb
+    import oracle
+    from lightgbm_rs_b200 import synthetic
+
+    X, y = synthetic.binary_c0(num_data=40_000, num_features=6, seed=9)
+    X = np.concatenate([X, np.full((len(y), 1), 3.0, np.float32),
+                        np.zeros((len(y), 1), np.float32)], axis=1)
+    X[:10, -1] = np.arange(1, 11)  # 10 non-zero rows: no split leaves 20 on both sides
+    params = {"objective": "binary", "num_leaves": 31, "min_data_in_leaf": 20,
+              "use_quantized_grad": True, "num_grad_quant_bins": 4}
+    ds = lgb.Dataset(X, y, params)
+    assert [m["num_bin"] for m in ds.mappers[-2:]] == [1, 1]
+    assert all(m["is_trivial"] for m in ds.mappers[-2:])
+    assert not any(m["is_trivial"] for m in ds.mappers[:-2])
+    booster = lgb.train(params, ds, num_boost_round=3)
+    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
+             for m in ds.mappers]
+    ref = oracle.train(ds.bins, metas, y, objective="binary", num_iterations=3,
+                       learning_rate=0.1, num_leaves=31, use_quantized_grad=True,
+                       stochastic_rounding=True, num_grad_quant_bins=4, min_data_in_leaf=20)
+    for i, (a, b) in enumerate(zip(booster.trees(), ref["trees"])):
+        _assert_trees_bit_equal(a, b, f"tree {i}")
+        assert not set(a["split_feature"].tolist()) & {6, 7}
+    assert booster.train_scores().tobytes() == ref["scores"].tobytes()
+    # without the pre-filter only the constant column is trivial
+    ds2 = lgb.Dataset(X, y, dict(params, feature_pre_filter=False))
+    assert [m["num_bin"] > 1 for m in ds2.mappers[-2:]] == [False, True]

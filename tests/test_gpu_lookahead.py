@@ -76,6 +76,7 @@ def test_lookahead_quantized_bit_exact(data, num_leaves):
     assert c_on["builds"] == c_off["builds"] and c_on["rows_built"] == c_off["rows_built"]
     ref = oracle.train(ds.bins, metas, y, objective="binary", num_iterations=5,
                        learning_rate=0.1, num_leaves=num_leaves, use_quantized_grad=True,
+                       stochastic_rounding=True,
                        num_grad_quant_bins=4, min_data_in_leaf=50, nthreads=8)
     a, b = on.trees(), off.trees()
     assert len(a) == len(b) == len(ref["trees"]) == 5

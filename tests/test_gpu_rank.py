@@ -120,6 +120,7 @@ def test_lambdarank_quantized_booster_bit_exact_vs_oracle():
     b = lgb.train(p, ds, num_boost_round=8)
     ref = oracle.train(ds.bins, metas, y, objective="lambdarank", num_iterations=8,
                        learning_rate=0.1, num_leaves=63, use_quantized_grad=True,
+                       stochastic_rounding=True,
                        num_grad_quant_bins=4, query_boundaries=qb, min_data_in_leaf=20)
     assert len(b.trees()) == len(ref["trees"])
     for i, (a, r) in enumerate(zip(b.trees(), ref["trees"])):

@@ -323,3 +323,59 @@ def test_partition_golden_missing_fanout(oracle_lib):
         assert left == c["split"], c["name"]
         missing += c["missing_type"] != 0
     assert missing == 6
+
+
+def _xorshift_offsets(seed, count):
+    """Pure-Python restatement of the reference's next_u01 stream
+    (lgbm-treelearner/src/gradient_discretizer.rs:252-262), seeded as new_stochastic
+    (:78-83) does: state = seed ^ 0x9E3779B97F4A7C15."""
+    m = (1 << 64) - 1
+    x = (seed ^ 0x9E3779B97F4A7C15) & m
+    out = []
+    for _ in range(count):
+        x ^= (x << 13) & m
+        x ^= x >> 7
+        x ^= (x << 17) & m
+        out.append((x >> 11) / float(1 << 53))
+    return out
+
+
+def test_oracle_stochastic_rounding_matches_python_restatement(oracle_lib):
+    """Each row draws the gradient offset then the hessian offset; q = trunc(v * inv +-
+    offset) (gradient_discretizer.rs:167-191). The C++ oracle against a Python loop."""
+    rng = np.random.default_rng(3)
+    n = 3000
+    g = rng.normal(size=n).astype(np.float32)
+    h = rng.uniform(0.01, 0.25, n).astype(np.float32)
+    seed = oracle_lib.stochastic_seed(5)
+    assert seed == (5 << 20) ^ 0x51702010
+    _, _, q, scales = oracle_lib.quantize(g, h, 4, stochastic=True, seed=seed)
+    off = _xorshift_offsets(seed, 2 * n)
+    igs, ihs = 1.0 / scales[0], 1.0 / scales[1]
+    want_g = [int(np.trunc(float(g[i]) * igs + (off[2 * i] if g[i] >= 0 else -off[2 * i])))
+              for i in range(n)]
+    want_h = [int(np.trunc(float(h[i]) * ihs + off[2 * i + 1])) for i in range(n)]
+    assert q[:, 0].tolist() == want_g
+    assert q[:, 1].tolist() == want_h
+
+
+def test_oracle_stochastic_rounding_properties(oracle_lib):
+    """The reference's own property tests (gradient_discretizer.rs:337-374): reproducible
+    per seed, different for another seed, and unbiased where deterministic rounding is
+    biased to the grid point."""
+    grad = ((np.arange(200) - 100.0) * 0.013).astype(np.float32)
+    hess = np.ones(200, dtype=np.float32)
+    a = oracle_lib.quantize(grad, hess, 16, stochastic=True, seed=42)[2]
+    b = oracle_lib.quantize(grad, hess, 16, stochastic=True, seed=42)[2]
+    c = oracle_lib.quantize(grad, hess, 16, stochastic=True, seed=43)[2]
+    assert np.array_equal(a, b) and not np.array_equal(a, c)
+    n = 20_002
+    grad = np.full(n, 0.3, dtype=np.float32)
+    grad[0], grad[1] = 1.0, -1.0
+    hess = np.ones(n, dtype=np.float32)
+    _, _, qd, sd = oracle_lib.quantize(grad, hess, 4)
+    _, _, qs, ss = oracle_lib.quantize(grad, hess, 4, stochastic=True, seed=7)
+    det_mean = qd[2:, 0].astype(np.int64).sum() * sd[0] / (n - 2)
+    sto_mean = qs[2:, 0].astype(np.int64).sum() * ss[0] / (n - 2)
+    assert abs(det_mean - 0.5) < 1e-9
+    assert abs(sto_mean - 0.3) < 0.01
