@@ -71,7 +71,11 @@ WORKLOADS = {
 # summarised in profiles/ (dram__bytes_read.sum + dram__bytes_write.sum of the captured
 # launches over the algorithmic bytes of the same launches). The bench scales them to
 # its own launches to fill roofline.traffic.
-TRAFFIC_PER_ALGO_BYTE = {}
+TRAFFIC_PER_ALGO_BYTE = {
+    "partition": 5.37,  # warm capture: 4,076 MB DRAM for 759 MB algorithmic
+    "build": 1.20,      # cold capture: 179.8 MB DRAM for 150 MB algorithmic
+    "fixscan": 0.56,    # warm capture: 80.8 MB DRAM for 145 MB algorithmic (L2-resident)
+}
 
 
 def parse():
@@ -86,12 +90,15 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the f32 and full-length runs and the parity check")
-    ap.add_argument("--measure", default="boosting", choices=["boosting", "binning", "profile"],
+    ap.add_argument("--measure", default="boosting",
+                    choices=["boosting", "binning", "profile", "atomics"],
                     help="binning: time Dataset construction from raw C1 values (device "
                          "value_to_bin) against host value_to_bin on all cores; profile: "
                          "W warm-up iterations, then one iteration with every kernel launched "
                          "on its own (the case the committed ncu captures are taken on), "
-                         "printing its algorithmic bytes per kernel class")
+                         "printing its algorithmic bytes per kernel class; atomics: the root "
+                         "histogram build's shared-memory atomic rate on bin patterns that "
+                         "set the bank conflicts (conflict-free, random, one address)")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     if args.rows is None:
@@ -551,7 +558,8 @@ def run_ours(args):
                        "k_build / k_build_q4 (histogram build)", spans["build"], kb["build"],
                        "build"),
         "fixscan": entry("k_fixscan (control step: decode, FixHistogram, subtraction, "
-                         "threshold scans, pick; L2-resident)", spans["fixscan"], fix_bytes),
+                         "threshold scans, pick; L2-resident)", spans["fixscan"], fix_bytes,
+                         "fixscan"),
     }
     dom = max(kern, key=lambda k: kern[k]["ms_per_iter"])
     hist = {"root": kern["build"],
@@ -605,6 +613,13 @@ def run_ours(args):
                          "steps": args.steps, "warmup": args.warmup,
                          "ms_per_step": ms_f / args.steps}
         del bf, ds_f
+        ps = dict(p, stochastic_rounding=True)
+        ds_s, bs, ms_s = resident_booster(ps, args.warmup, args.steps)
+        extras["stochastic_rounding"] = {"value": args.steps / (ms_s / 1000.0),
+                                         "unit": "iters/s", "steps": args.steps,
+                                         "ms_per_step": ms_s / args.steps,
+                                         "digest": tree_digest(bs.trees())}
+        del bs, ds_s
     if not args.no_extras:
         n_full = w["iterations"]
         bfull = lgb.Booster(p, ds, comm=comm)
@@ -644,10 +659,12 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "kernel": kern[dom]["kernel"],
                      "achieved": kern[dom]["achieved"], "peak": peak, "unit": "GB/s",
                      "frac": kern[dom]["frac"], "peak_kind": peak_kind,
-                     "traffic": (kern[dom].get("traffic_per_iter") / (
-                         pc["splits"] + 1) if kern[dom].get("traffic_per_iter") else None),
-                     "traffic_note": "DRAM bytes per launch (per split step), scaled from the "
-                                     "small-case ncu capture in profiles/",
+                     "traffic": kern[dom].get("traffic_per_iter"),
+                     "traffic_note": "DRAM bytes per iteration of the kernel's launches, like "
+                                     "achieved (bytes per iteration / span ms per iteration): "
+                                     "its algorithmic bytes times the DRAM/algorithmic ratio "
+                                     "of the 5M-row ncu captures in profiles/"
+                                     "tree_kernels_dram_traffic_c1_5M.md",
                      "algorithmic_bytes_per_iter": kern[dom]["bytes_per_iter"],
                      "ms_per_iter": kern[dom]["ms_per_iter"],
                      "timing": "device spans (%globaltimer, first CTA entry to last CTA exit) "
@@ -760,6 +777,62 @@ def run_profile_case(args):
                       "event_ms_by_class": kms, "launches_by_class": per}), flush=True)
 
 
+def run_atomics(args):
+    """Shared-memory atomic ceiling of the root build k_build_q4, measured with the kernel
+    itself. The build adds one packed 32-bit atomic per (row, feature) into cell
+    (feature << 8) + bin; a warp's lanes take consecutive rows, so the bin pattern decides
+    the bank conflicts of each warp-wide atomic:
+      lanes   bin = row % 32: every lane its own bank (conflict-free, distinct cells)
+      random  uniform bins over 256 (the C1 matrix's quantile bins are close to this)
+      c1      the C1 matrix itself
+      same    every row bin 0: all lanes on one cell
+    One binary boosting iteration from the initial score (constant hessian, so exactly F
+    atomics per row); the root build's device span comes from the pipeline stamps."""
+    import lightgbm_rs_b200 as lgb
+    from lightgbm_rs_b200 import build as libbuild
+
+    libbuild.build()
+    n, F = args.rows, 28
+    rng = np.random.default_rng(0)
+    y = (rng.random(n) < 0.5).astype(np.float32)
+    mappers = [{"num_bin": 256, "default_bin": 0, "most_freq_bin": 0, "missing_type": 0,
+                "bin_type": 0, "upper": np.arange(256, dtype=np.float64) + 0.5,
+                "is_trivial": False} for _ in range(F)]
+    rows = np.arange(n, dtype=np.int64)
+    patterns = {
+        "lanes": lambda f: ((rows + 7 * f) % 32).astype(np.uint8),
+        "random": lambda f: rng.integers(0, 256, n).astype(np.uint8),
+        "same": lambda f: np.zeros(n, dtype=np.uint8),
+    }
+    out = {"measure": "atomics", "rows": n, "features": F, "patterns": {}}
+    p = {"objective": "binary", "num_leaves": 2, "min_data_in_leaf": 100,
+         "learning_rate": 0.1, "use_quantized_grad": True, "num_grad_quant_bins": 4,
+         "stochastic_rounding": False}
+    sources = list(patterns.items())
+    if n == WORKLOADS["c1"]["rows"]:
+        c1 = make_data("c1", n)
+        sources.append(("c1", lambda f: c1.bins[f]))
+        y_c1 = c1.y
+    for name, gen in sources:
+        bins = np.ascontiguousarray(np.stack([gen(f) for f in range(F)]))
+        lab = y_c1 if name == "c1" else y
+        maps = c1.mappers if name == "c1" else mappers
+        ds = lgb.Dataset(bins=bins, mappers=maps, label=lab, params=p)
+        b = lgb.Booster(p, ds)
+        b.update(1)
+        ms = []
+        for _ in range(max(3, args.steps)):
+            spans, _ = b.profile_pipeline(1)
+            ms.append(spans["build"])
+        t = min(ms)
+        out["patterns"][name] = {"build_ms": t, "atomics_per_s": n * F / (t / 1e3),
+                                 "atomics_per_sm_clock_at_1965mhz":
+                                     n * F / (t / 1e3) / (148 * 1.965e9),
+                                 "bytes_per_s": n * (F + 2) / (t / 1e3)}
+        del b, ds
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse()
     if args.warmup < 3:
@@ -769,6 +842,9 @@ def main():
         return
     if args.measure == "profile":
         run_profile_case(args)
+        return
+    if args.measure == "atomics":
+        run_atomics(args)
         return
     if args.impl == "reference":
         run_reference(args)

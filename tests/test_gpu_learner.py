@@ -339,6 +339,36 @@ def test_trivial_features_left_out():
         _assert_trees_bit_equal(a, b, f"tree {i}")
         assert not set(a["split_feature"].tolist()) & {6, 7}
     assert booster.train_scores().tobytes() == ref["scores"].tobytes()
-    # without the pre-filter only the constant column is trivial
+    # without the pre-filter neither is trivial: the constant column keeps the zero bin
+    # and its value's bin, as the reference's BinMapper does
     ds2 = lgb.Dataset(X, y, dict(params, feature_pre_filter=False))
-    assert [m["num_bin"] > 1 for m in ds2.mappers[-2:]] == [False, True]
+    assert [m["num_bin"] for m in ds2.mappers[-2:]] == [2, 5]
+    assert not any(m["is_trivial"] for m in ds2.mappers)
+
+
+def test_wide_c2_shape_bit_exact():
+    """The C2 shape at test size: 1,200 features ~ U(-1,1), max_bin 63, 127 leaves
+    (several feature groups, the non-fused partition + build, one control-step CTA per
+    feature), 3 boosting iterations bit-exact vs the oracle."""
+    import lightgbm_rs_b200 as lgb
+    import oracle
+    from lightgbm_rs_b200 import synthetic
+
+    X, y = synthetic.wide_c2(num_data=24_000, num_features=1200, seed=4)
+    params = {"objective": "binary", "num_leaves": 127, "min_data_in_leaf": 20,
+              "max_bin": 63, "learning_rate": 0.1, "use_quantized_grad": True,
+              "num_grad_quant_bins": 4}
+    ds = lgb.Dataset(X, y, params)
+    assert max(m["num_bin"] for m in ds.mappers) <= 64
+    booster = lgb.train(params, ds, num_boost_round=3)
+    metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type")}
+             for m in ds.mappers]
+    ref = oracle.train(ds.bins, metas, y, objective="binary", num_iterations=3,
+                       learning_rate=0.1, num_leaves=127, use_quantized_grad=True,
+                       stochastic_rounding=True, num_grad_quant_bins=4, min_data_in_leaf=20,
+                       nthreads=oracle.max_threads())
+    trees = booster.trees()
+    assert len(trees) == 3
+    for i, (a, b) in enumerate(zip(trees, ref["trees"])):
+        _assert_trees_bit_equal(a, b, f"tree {i}")
+    assert booster.train_scores().tobytes() == ref["scores"].tobytes()
