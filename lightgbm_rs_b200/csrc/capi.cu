@@ -472,6 +472,9 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.ctrl = ctrl.p;
   d.feat = ds->d_feats.p;
   d.F = ds->num_features;
+  d.sliced = 0;  // every feature on this device (a data-parallel job may slice them)
+  d.slice_begin = 0;
+  d.slice_end = d.F;
   d.bins = ds->bins.p;
   d.stride = ds->stride;
   d.L = L;
@@ -1750,7 +1753,11 @@ int setup_peer_exchange(lgbm_b200_booster* b, lgbm_b200_comm* comm) {
   const size_t off_la = 2 * xs + kMaxXRanks + 1;
   const size_t off_laflags = off_la + kLaSlots * xs;
   const size_t off_laseq = off_laflags + kMaxXRanks;
-  const size_t words = off_laseq + 1;
+  // then the sliced pick's records [2][kMaxXRanks], their flags and count
+  const size_t off_pick = (off_laseq + 1 + 1) / 2 * 2;  // 16-byte aligned records
+  const size_t off_pickflags = off_pick + 2 * kMaxXRanks * (size_t)kXPickWords;
+  const size_t off_pickseq = off_pickflags + kMaxXRanks;
+  const size_t words = off_pickseq + 1;
   b->xmem.nocache = true;
   CUDA_TRY(b->xmem.alloc(words));
   CUDA_TRY(cudaMemset(b->xmem.p, 0, words * 8));
@@ -1802,12 +1809,14 @@ int setup_peer_exchange(lgbm_b200_booster* b, lgbm_b200_comm* comm) {
   }
   long long wait_ms = 2000;
   if (const char* w = std::getenv("LGBM_B200_PEER_WAIT_MS")) wait_ms = std::max(1ll, atoll(w));
-  std::vector<void*> ptrs(4 * (size_t)R);
+  std::vector<void*> ptrs(6 * (size_t)R);
   for (int q = 0; q < R; ++q) {
     ptrs[q] = base[q];
     ptrs[R + q] = base[q] + 2 * xs;
     ptrs[2 * R + q] = base[q] + off_la;
     ptrs[3 * R + q] = base[q] + off_laflags;
+    ptrs[4 * R + q] = base[q] + off_pick;
+    ptrs[5 * R + q] = base[q] + off_pickflags;
   }
   CUDA_TRY(b->xptrs.alloc(ptrs.size()));
   CUDA_TRY(cudaMemcpy(b->xptrs.p, ptrs.data(), ptrs.size() * sizeof(void*),
@@ -1827,6 +1836,20 @@ int setup_peer_exchange(lgbm_b200_booster* b, lgbm_b200_comm* comm) {
     d.peer_la_flags = reinterpret_cast<unsigned long long* const*>(b->xptrs.p + 3 * R);
     d.la_flags = b->xmem.p + off_laflags;
     d.la_seq = b->xmem.p + off_laseq;
+  }
+  // Feature slices (the data-parallel learner's split of the scan work): rank q decodes
+  // and scans features [q F / R, (q + 1) F / R), when every rank gets at least two
+  // (LGBM_B200_FEATURE_SLICES=0 keeps every feature on every rank).
+  const char* fs = std::getenv("LGBM_B200_FEATURE_SLICES");
+  if (d.F >= 2 * R && !(fs && std::strcmp(fs, "0") == 0)) {
+    d.sliced = 1;
+    d.slice_begin = (int32_t)((int64_t)d.F * comm->rank / R);
+    d.slice_end = (int32_t)((int64_t)d.F * (comm->rank + 1) / R);
+    d.pick_local = b->xmem.p + off_pick;
+    d.peer_pick = reinterpret_cast<unsigned long long* const*>(b->xptrs.p + 4 * R);
+    d.pick_flags = b->xmem.p + off_pickflags;
+    d.peer_pick_flags = reinterpret_cast<unsigned long long* const*>(b->xptrs.p + 5 * R);
+    d.pick_seq = b->xmem.p + off_pickseq;
   }
   return LGBM_B200_OK;
 }

@@ -96,12 +96,6 @@ __device__ __forceinline__ long long ld_relaxed_sys(const long long* p) {
   return v;
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -120,31 +114,57 @@ struct SpanStamp {
   }
 };
 
+// Sum over the ranks of word `off` of each rank's buffer (integers: exact in any order).
+// The ranks' buffer pointers are read first and every rank's load is issued before any
+// is added, so one round trip over the peer links covers all ranks.
+__device__ __forceinline__ long long peer_sum(long long* const* bufs, int ranks, size_t off) {
+  const long long* p[kMaxXRanks];
+#pragma unroll
+  for (int r = 0; r < kMaxXRanks; ++r) p[r] = r < ranks ? bufs[r] : nullptr;
+  long long v[kMaxXRanks];
+#pragma unroll
+  for (int r = 0; r < kMaxXRanks; ++r) v[r] = r < ranks ? ld_relaxed_sys(p[r] + off) : 0ll;
+  long long s = 0;
+#pragma unroll
+  for (int r = 0; r < kMaxXRanks; ++r) s += v[r];
+  return s;
+}
+
 // Cell `idx` of the accumulated child: the sum over the ranks' buffers of parity xpar
 // (integers: exact in any order); on one device, the launch's accumulator.
 template <bool PEER>
 __device__ __forceinline__ long long raw_sum(const GrowDev& d, size_t idx) {
   if (!PEER) return __ldcg(d.raw + idx);
   const size_t off = (size_t)d.xpar * ((size_t)d.raw_len + 2) + idx;
-  long long s = 0;
-  for (int r = 0; r < d.xranks; ++r) s += ld_relaxed_sys(d.xbuf[r] + off);
-  return s;
+  return peer_sum(d.xbuf, d.xranks, off);
 }
 
 // Waits (thread 0 of a consumer CTA) until every rank has published this rank's current
 // exchange count; false after wait_ns without it, or at once when a wait has already run
-// out (the caller records kErrSpinTimeout).
+// out (the caller records kErrSpinTimeout). Each poll reads every rank's flag in one round
+// trip (relaxed loads issued together); once all have reached `seq`, one system-scope
+// acquire fence orders the caller's later reads of the ranks' buffers after the ranks'
+// release stores of those flags.
 __device__ __noinline__ bool x_wait_target(const uint32_t* error, int xranks,
                                            const unsigned long long* xflags,
                                            unsigned long long seq, long long wait_ns) {
   if (*reinterpret_cast<const volatile uint32_t*>(error) & kErrSpinTimeout) return false;
   const unsigned long long t0 = global_ns();
-  for (int r = 0; r < xranks; ++r) {
-    while (ld_acquire_sys(xflags + r) < seq) {
-      if (global_ns() - t0 > (unsigned long long)wait_ns) return false;
-      __nanosleep(64);
-    }
+  while (true) {
+    unsigned long long v[kMaxXRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxXRanks; ++r)
+      v[r] = r < xranks ? (unsigned long long)ld_relaxed_sys(
+                              reinterpret_cast<const long long*>(xflags + r))
+                        : seq;
+    bool ready = true;
+#pragma unroll
+    for (int r = 0; r < kMaxXRanks; ++r) ready = ready && v[r] >= seq;
+    if (ready) break;
+    if (global_ns() - t0 > (unsigned long long)wait_ns) return false;
+    __nanosleep(64);
   }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
   return true;
 }
 
@@ -161,9 +181,7 @@ template <bool PEER>
 __device__ __forceinline__ long long la_sum(const GrowDev& d, int slot, size_t idx) {
   const size_t off = (size_t)slot * ((size_t)d.raw_len + 2) + idx;
   if (!PEER) return __ldcg(d.la_raw + off);
-  long long v = 0;
-  for (int r = 0; r < d.xranks; ++r) v += ld_relaxed_sys(d.la_xbuf[r] + off);
-  return v;
+  return peer_sum(d.la_xbuf, d.xranks, off);
 }
 
 // With several devices, a pending split partitioned by the look-ahead of step s - 2 (the
@@ -351,7 +369,9 @@ __global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d, int phase) {
     const bool sub = t.mask_leaf >= 0;
     const uint8_t* ps = d.splittable + (size_t)(sub ? t.mask_leaf : 0) * d.F;
     for (int fl = threadIdx.x; fl < nf; fl += blockDim.x)
-      s_used[fl] = sub ? ps[grp.f_begin + fl] : (uint8_t)1;
+      // feature slices: other ranks own most features and this rank's flags of them are
+      // stale, so every feature is accumulated for the ranks that scan it
+      s_used[fl] = (sub && !d.sliced) ? ps[grp.f_begin + fl] : (uint8_t)1;
   }
   for (int fl = threadIdx.x; fl < nf; fl += blockDim.x)
     s_binoff[fl] = d.feat[grp.f_begin + fl].bin_off - grp.bin_base;
@@ -506,7 +526,8 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase
   const uint8_t* ps = d.splittable + (size_t)(sub ? t.mask_leaf : 0) * d.F + grp.f_begin;
   if (threadIdx.x < 128) {
     const int fl = threadIdx.x;
-    const uint32_t m = __ballot_sync(0xffffffffu, fl < nf && (!sub || ps[fl] != 0));
+    const uint32_t m =
+        __ballot_sync(0xffffffffu, fl < nf && (!sub || d.sliced || ps[fl] != 0));
     if ((fl & 31) == 0) s_mask[fl >> 5] = m;
   }
   __syncthreads();
@@ -1450,6 +1471,7 @@ struct PickOut {
   DevSplitInfo si[2];  // best split of the smaller / larger scanned leaf
   int32_t bf[2];       // its feature (-1: none)
   int32_t done;        // no leaf has a positive gain: the tree is finished
+  int32_t xerr;        // a sliced pick's wait for the other ranks ran out
   int32_t leaf, feature, build_left;
   DevSplitInfo split;  // the split to apply next
   uint32_t si_cat[2][kCatWords];  // left bins of si[] when their feature is categorical
@@ -1486,6 +1508,109 @@ __device__ __forceinline__ T pick_rd(const T* p) {
   return __ldcg(p);
 }
 
+// The sliced pick's exchange, by the last CTA's warp 0 on every rank. f0 / f1 are this
+// rank's best feature of the smaller / larger scanned leaf over its slice (in split_gt
+// order, ties to the lower feature); on return they are the best over all ranks, and
+// o.si / o.bf / o.si_cat hold those features' splits. Lane q writes this rank's record
+// into rank q's pick area (slot [seq parity][this rank]) and releases rank q's flag for
+// this rank; lane 0 then waits (bounded) for every rank's flag, and lane q reads rank q's
+// record from the local area. A fast rank cannot overwrite a slot that a slow rank still
+// reads: it would first have to pass the next step's wait, which needs the slow rank's
+// next record.
+template <bool CAT, bool STAGED>
+__device__ void sliced_pick_exchange(const GrowDev& d, int32_t Lg, const DevSplitInfo* so,
+                                     const uint32_t* sc, PickOut& o, Cand& f0, Cand& f1) {
+  const int lane = threadIdx.x & 31;
+  const unsigned long long target = *reinterpret_cast<const volatile unsigned long long*>(d.pick_seq) + 1;
+  const size_t par = (size_t)(target & 1ull);
+  // this rank's record, assembled in o by lanes 0 and 1
+  if (lane < 2) {
+    const Cand& c = lane == 0 ? f0 : f1;
+    const bool have = c.f >= 0 && (lane == 0 || Lg >= 0);
+    o.si[lane] = have ? so[(size_t)lane * d.F + c.f] : d_split_none();
+    o.bf[lane] = have ? c.f : -1;
+    if (CAT)
+      for (int k = 0; k < kCatWords; ++k)
+        o.si_cat[lane][k] = have ? sc[((size_t)lane * d.F + c.f) * kCatWords + k] : 0u;
+  }
+  __syncwarp();
+  if (lane < d.xranks) {
+    XPick rec;
+    rec.si[0] = o.si[0];
+    rec.si[1] = o.si[1];
+    rec.bf[0] = o.bf[0];
+    rec.bf[1] = o.bf[1];
+    for (int k = 0; k < kCatWords; ++k) {
+      rec.cat[0][k] = CAT ? o.si_cat[0][k] : 0u;
+      rec.cat[1][k] = CAT ? o.si_cat[1][k] : 0u;
+    }
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(&rec);
+    unsigned long long* dst =
+        d.peer_pick[lane] + (par * kMaxXRanks + (size_t)d.xrank) * kXPickWords;
+    for (int k = 0; k < (int)(sizeof(XPick) / 8); ++k) dst[k] = src[k];
+    __threadfence_system();
+    unsigned long long* flag = d.peer_pick_flags[lane] + d.xrank;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(target) : "memory");
+  }
+  int ok = 1;
+  if (lane == 0)
+    ok = x_wait_target(&d.ctrl->error, d.xranks, d.pick_flags, target, d.xwait_ns) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  Cand r0{kNegInf, -1, -1}, r1{kNegInf, -1, -1};
+  if (ok && lane < d.xranks) {
+    const long long* rec = reinterpret_cast<const long long*>(
+        d.pick_local + (par * kMaxXRanks + (size_t)lane) * kXPickWords);
+    const long long w0 = ld_relaxed_sys(rec + (offsetof(XPick, si) + offsetof(DevSplitInfo, gain)) / 8);
+    const long long w1 = ld_relaxed_sys(rec + (offsetof(XPick, si) + sizeof(DevSplitInfo) + offsetof(DevSplitInfo, gain)) / 8);
+    const long long wf = ld_relaxed_sys(rec + offsetof(XPick, bf) / 8);
+    const int32_t q0 = (int32_t)(wf & 0xffffffffll), q1 = (int32_t)(wf >> 32);
+    if (q0 >= 0) r0 = Cand{__longlong_as_double(w0), q0, q0};
+    if (q1 >= 0) r1 = Cand{__longlong_as_double(w1), q1, q1};
+  }
+  warp_argmax(r0);
+  warp_argmax(r1);
+  f0 = r0;
+  f1 = r1;
+  // the owners' records of the winners: lane c copies leaf c's split
+  if (ok && lane < 2) {
+    const Cand& c = lane == 0 ? r0 : r1;
+    if (c.f >= 0) {
+      int owner = 0;
+      for (int q = 0; q < d.xranks; ++q) {
+        const long long wf = ld_relaxed_sys(reinterpret_cast<const long long*>(
+            d.pick_local + (par * kMaxXRanks + (size_t)q) * kXPickWords) +
+            offsetof(XPick, bf) / 8);
+        const int32_t qf = lane == 0 ? (int32_t)(wf & 0xffffffffll) : (int32_t)(wf >> 32);
+        if (qf == c.f) owner = q;
+      }
+      const long long* rec = reinterpret_cast<const long long*>(
+          d.pick_local + (par * kMaxXRanks + (size_t)owner) * kXPickWords);
+      long long* dst = reinterpret_cast<long long*>(&o.si[lane]);
+      const size_t si0 = offsetof(XPick, si) / 8 + (size_t)lane * (sizeof(DevSplitInfo) / 8);
+      for (int k = 0; k < (int)(sizeof(DevSplitInfo) / 8); ++k) dst[k] = ld_relaxed_sys(rec + si0 + k);
+      o.bf[lane] = c.f;
+      if (CAT) {
+        const uint32_t* cr = reinterpret_cast<const uint32_t*>(rec + offsetof(XPick, cat) / 8);
+        for (int k = 0; k < kCatWords; ++k)
+          o.si_cat[lane][k] = (uint32_t)(ld_relaxed_sys(reinterpret_cast<const long long*>(
+                                             cr + (size_t)lane * kCatWords + (k & ~1))) >>
+                                         (32 * (k & 1)));
+      }
+    } else {
+      o.si[lane] = d_split_none();
+      o.bf[lane] = -1;
+      if (CAT)
+        for (int k = 0; k < kCatWords; ++k) o.si_cat[lane][k] = 0u;
+    }
+  }
+  if (lane == 0) {
+    if (!ok) o.xerr = 1;
+    *reinterpret_cast<volatile unsigned long long*>(d.pick_seq) = target;
+  }
+  __syncwarp();
+}
+
 template <bool CAT, bool STAGED>
 __device__ void pick_warp(const GrowDev& d, const Prep& P, const CtlSmem& cs,
                           const DevSplitInfo* so, const uint32_t* sc, PickOut& o) {
@@ -1493,11 +1618,12 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const CtlSmem& cs,
   const bool find = P.live != 0;
   const int32_t S = P.S, Lg = P.Lg;
   Cand2 top = cs.other;
+  if (lane == 0) o.xerr = 0;
   if (find) {
     const bool ok0 = cs.ok[0] != 0;
     const bool ok1 = Lg >= 0 && cs.ok[1] != 0;
     Cand f0{kNegInf, -1, -1}, f1{kNegInf, -1, -1};
-    for (int f = lane; f < d.F; f += 32) {
+    for (int f = d.slice_begin + lane; f < d.slice_end; f += 32) {
       const double g0 = pick_rd<double, STAGED>(&so[f].gain);
       const double g1 = Lg >= 0 ? pick_rd<double, STAGED>(&so[d.F + f].gain) : kNegInf;
       if (g0 > kNegInf && cand_better(g0, f, f, f0.g, f0.f, f0.i)) f0 = Cand{g0, f, f};
@@ -1505,9 +1631,23 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const CtlSmem& cs,
     }
     warp_argmax(f0);
     warp_argmax(f1);
+    if (d.sliced) sliced_pick_exchange<CAT, STAGED>(d, Lg, so, sc, o, f0, f1);
     const int32_t bf0 = ok0 ? f0.f : -1;
     const int32_t bf1 = ok1 ? f1.f : -1;
-    if (lane == 0) {
+    if (d.sliced) {
+      // the exchange left every rank's best of both leaves in o: apply the scan flags
+      if (lane == 0 && bf0 < 0) {
+        o.si[0] = d_split_none();
+        o.bf[0] = -1;
+        if (CAT)
+          for (int k = 0; k < kCatWords; ++k) o.si_cat[0][k] = 0u;
+      } else if (lane == 1 && bf1 < 0) {
+        o.si[1] = d_split_none();
+        o.bf[1] = -1;
+        if (CAT)
+          for (int k = 0; k < kCatWords; ++k) o.si_cat[1][k] = 0u;
+      }
+    } else if (lane == 0) {
       if (bf0 >= 0)
         o.si[0] = so[bf0];
       else
@@ -1981,7 +2121,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
         if (leaf2 >= 0) {
           const DevLeafSplits ls = sl_i == 0 ? P.lsS : P.lsLg;
           const bool scannable = leaf_buildable(ls);
-          if (f == 0) d.scan_ok[sl_i] = scannable ? 1 : 0;
+          if (f == d.slice_begin) d.scan_ok[sl_i] = scannable ? 1 : 0;
           DevSplitInfo si = d_split_none();
           if (scannable) {
             if (is_cat) {
@@ -2004,7 +2144,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
       d.scan_out[d.F + f] = d_split_none();
       if (leaf_buildable(P.lsS)) d.splittable[(size_t)S * d.F + f] = 0;
       if (Lg >= 0 && leaf_buildable(P.lsLg)) d.splittable[(size_t)Lg * d.F + f] = 0;
-      if (f == 0) {
+      if (f == d.slice_begin) {
         d.scan_ok[0] = leaf_buildable(P.lsS) ? 1 : 0;
         d.scan_ok[1] = Lg >= 0 && leaf_buildable(P.lsLg) ? 1 : 0;
       }
@@ -2026,7 +2166,8 @@ template <bool CAT, bool PEER>
 __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& cs) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
-  const int nparts = min(d.F, (int)gridDim.x);
+  const int fb = d.slice_begin, fe = d.slice_end;  // this rank's features
+  const int nparts = min(fe - fb, (int)gridDim.x);
   if (tid == 0) {
     if (!x_wait<PEER>(d) || !la_wait<PEER>(d, s)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
     prep_compute<PEER>(d, s, cs.prep);
@@ -2036,12 +2177,12 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     const Cand2 o = other_leaves_best(d);
     if ((tid & 31) == 0) cs.other = o;
   } else if (tid == 64) {
-    if (blockIdx.x < (unsigned)d.F) cs.ft0 = d.feat[blockIdx.x];
+    if (fb + (int)blockIdx.x < fe) cs.ft0 = d.feat[fb + blockIdx.x];
   }
   __syncthreads();
-  for (int f = blockIdx.x; f < d.F; f += gridDim.x) {
+  for (int f = fb + blockIdx.x; f < fe; f += gridDim.x) {
     // the CTA's first feature was read while the pending split was applied
-    const DevFeature ft = f == (int)blockIdx.x ? cs.ft0 : d.feat[f];
+    const DevFeature ft = f == fb + (int)blockIdx.x ? cs.ft0 : d.feat[f];
     fixscan_feature<CAT, PEER>(d, cs.prep, f, ft, sm);
     __syncthreads();
   }
@@ -2161,6 +2302,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
       }
     }
     c.error |= cs.err;
+    if (!P.c.done && cs.pick.xerr) c.error |= kErrSpinTimeout;
     if (c.error & kErrSpinTimeout) c.done = 1;  // a rank stopped answering: end the tree
     // this step's look-ahead: the runner-up of the pick (its kernel runs next to the
     // following control step; slot s % 2 was consumed and cleared above)
@@ -2482,6 +2624,17 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
   // words and accumulator); otherwise the pending split of the control block
   LookAhead* const rec = la >= 0 ? d.la + la : nullptr;
   uint32_t* const ticket = rec ? &rec->ticket : &d.ctrl->part_ticket;
+  if (!rec) {
+    // The main partition has nothing to do after the tree, or when the look-ahead did this
+    // partition (most splits): one read of the control block decides, before any other
+    // request, so that such a launch costs a single round trip.
+    if (tid == 0) {
+      const GrowCtrl* c0 = d.ctrl;
+      s_ok = (c0->done || !c0->pending || c0->pend_la) ? 0 : 1;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+  }
   // the first tile ticket is taken before anything else is read: its round trip overlaps
   // the reads below (a ticket taken when there is nothing to do is harmless)
   if (tid == 0) s_tile = (int32_t)atomicAdd(ticket, 1u);
@@ -2542,7 +2695,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
   // mask is read with the leaf's range
   if (build && tid < 128) {
     const uint8_t* ps = d.splittable + (size_t)leaf * d.F;
-    const uint32_t m = __ballot_sync(0xffffffffu, tid < nf && ps[tid] != 0);
+    const uint32_t m = __ballot_sync(0xffffffffu, tid < nf && (d.sliced || ps[tid] != 0));
     if ((tid & 31) == 0) s_mask[tid >> 5] = m;
   }
   // few tiles: every CTA takes exactly one tile and stores its own partial histogram
@@ -2999,10 +3152,11 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       x.span_slot = span_slot_of(s, SPAN_FIXSCAN);
       PROF_BEGIN(KC_FIXSCAN);
       // variants: categorical features, and the peer exchange (off on one device)
+      const int grid = x.slice_end - x.slice_begin;  // this rank's features
       if (x.has_cat)
-        (px ? k_fixscan<true, true> : k_fixscan<true, false>)<<<x.F, kScanThreads, 0, st>>>(x, s);
+        (px ? k_fixscan<true, true> : k_fixscan<true, false>)<<<grid, kScanThreads, 0, st>>>(x, s);
       else
-        (px ? k_fixscan<false, true> : k_fixscan<false, false>)<<<x.F, kScanThreads, 0, st>>>(
+        (px ? k_fixscan<false, true> : k_fixscan<false, false>)<<<grid, kScanThreads, 0, st>>>(
             x, s);
       PROF_END();
     }

@@ -164,8 +164,29 @@ struct GrowDev {
   unsigned long long* span_start;
   unsigned long long* span_end;
   int32_t span_slot;
-  int32_t _spanpad;
+  // Feature slices of a data-parallel job over peer memory (sliced = 1): this rank's
+  // control step decodes and scans features [slice_begin, slice_end) only, then the ranks
+  // exchange their slices' best split of each scanned leaf (XPick records, pushed into
+  // every rank's pick area, a flag per rank) and every rank reduces them in split_gt order
+  // to the same pick. Otherwise the slice is every feature.
+  int32_t sliced;
+  int32_t slice_begin;
+  int32_t slice_end;
+  unsigned long long* pick_local;               // [2][kMaxXRanks][kXPickWords] records
+  unsigned long long* const* peer_pick;         // [xranks] each rank's pick area (device)
+  unsigned long long* pick_flags;               // this rank's pick flags, one per rank
+  unsigned long long* const* peer_pick_flags;   // [xranks] each rank's pick flags (device)
+  unsigned long long* pick_seq;                 // picks this rank has published
 };
+
+// One rank's contribution to a sliced pick: its slice's best split of each scanned leaf
+// (feature -1: none) and their categorical left bins.
+struct XPick {
+  DevSplitInfo si[2];
+  int32_t bf[2];
+  uint32_t cat[2][kCatWords];
+};
+constexpr int kXPickWords = (int)((sizeof(XPick) + 15) / 16 * 2);
 
 // Span slots of one tree: the root build, then four per split step.
 enum SpanKind { SPAN_FIXSCAN = 0, SPAN_PARTITION = 1, SPAN_LOOKAHEAD = 2, SPAN_BUILD = 3 };

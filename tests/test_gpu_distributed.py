@@ -21,26 +21,31 @@ ROWS = 50_001
 ITERS = 5
 
 
-def _data():
+def _data(wide=False):
     import lightgbm_rs_b200 as lgb
     from lightgbm_rs_b200 import synthetic
 
+    if wide:  # the C2 shape: many 63-bin features, every rank scans its own slice
+        X, y = synthetic.wide_c2(num_data=ROWS, num_features=600, seed=7)
+        return lgb.Dataset(X, y, dict(PARAMS, max_bin=63))
     X, y = synthetic.binary_c0(num_data=ROWS, seed=7)
     return lgb.Dataset(X, y, dict(PARAMS))  # host binning only, deterministic
 
 
-def _worker(rank, world, uid, quantized, leaves, q):
+def _worker(rank, world, uid, quantized, leaves, q, wide=False, slices=True):
     try:
         os.environ["NCCL_NVLS_ENABLE"] = "0"
+        if not slices:
+            os.environ["LGBM_B200_FEATURE_SLICES"] = "0"
         import sys
         sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         import lightgbm_rs_b200 as lgb
         from lightgbm_rs_b200 import distributed as D
 
-        full = _data()
+        full = _data(wide)
         b, e = D.shard_range(full.num_data, world, rank)
         p = dict(PARAMS, device=rank, use_quantized_grad=quantized, num_grad_quant_bins=4,
-                 num_leaves=leaves)
+                 num_leaves=leaves, max_bin=63 if wide else 255)
         shard = lgb.Dataset(bins=full.bins[:, b:e], mappers=full.mappers,
                             label=full.label[b:e], params=p)
         comm = D.Communicator(rank, world, rank, uid)
@@ -53,8 +58,12 @@ def _worker(rank, world, uid, quantized, leaves, q):
         q.put((rank, "error", repr(ex)))
 
 
-@pytest.mark.parametrize("quantized,leaves", [(True, 31), (False, 31), (True, 255)])
-def test_two_gpus_match_one(quantized, leaves):
+@pytest.mark.parametrize("quantized,leaves,wide,slices", [
+    (True, 31, False, True), (False, 31, False, True), (True, 255, False, True),
+    (True, 63, True, True), (True, 255, False, False)])
+def test_two_gpus_match_one(quantized, leaves, wide, slices):
+    """Feature slices on (each rank scans half the features, the slices' best splits are
+    exchanged before the pick) and off (every rank scans every feature)."""
     import lightgbm_rs_b200 as lgb
     from lightgbm_rs_b200 import distributed as D
 
@@ -63,7 +72,7 @@ def test_two_gpus_match_one(quantized, leaves):
     uid = D.unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, uid, quantized, leaves, q))
+    procs = [ctx.Process(target=_worker, args=(r, 2, uid, quantized, leaves, q, wide, slices))
              for r in range(2)]
     for p in procs:
         p.start()
@@ -83,8 +92,9 @@ def test_two_gpus_match_one(quantized, leaves):
         for r in range(2):
             c = out[r][3]
             assert c["lookahead_runs"] > 0 and c["lookahead_hits"] > 0, (r, c)
-    full = _data()
-    p = dict(PARAMS, use_quantized_grad=quantized, num_grad_quant_bins=4, num_leaves=leaves)
+    full = _data(wide)
+    p = dict(PARAMS, use_quantized_grad=quantized, num_grad_quant_bins=4, num_leaves=leaves,
+             max_bin=63 if wide else 255)
     ref = lgb.train(p, full, num_boost_round=ITERS)
     want_trees, want_scores = ref.trees(), ref.train_scores()
     scores = np.concatenate([out[0][2], out[1][2]])
