@@ -530,8 +530,16 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.t_cat = d.best_cat + (size_t)kCatWords * L;
   d.split_cat = d.t_cat + (size_t)kCatWords * L;
   d.has_cat = 0;
-  for (const DevFeature& f : ds->feats)
+  int32_t max_bins = 0;
+  for (const DevFeature& f : ds->feats) {
     if (f.flags & kFeatCategorical) d.has_cat = 1;
+    max_bins = std::max(max_bins, f.num_bin);
+  }
+  // Narrow features (wide data such as max_bin 63): one 256-thread control-step CTA per
+  // feature, four resident per SM, instead of 1024 threads of which most would idle
+  // (LGBM_B200_NARROW_SCAN=0 keeps the 1024-thread CTAs).
+  const char* ns = std::getenv("LGBM_B200_NARROW_SCAN");
+  d.narrow_scan = (!d.has_cat && max_bins <= 64 && !(ns && ns[0] == '0')) ? 1 : 0;
   d.scan_ok = scan_ok.p;
   d.la = la.p;
   d.la_raw = la_raw.p;

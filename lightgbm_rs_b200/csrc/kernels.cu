@@ -635,9 +635,10 @@ struct ScanLeaf {
   int32_t num_data;
 };
 
-// Named barrier over one 256-thread group (ids 1..15; id 0 is __syncthreads).
+// Named barrier over one G-thread group (ids 1..15; id 0 is __syncthreads).
+template <int G = 256>
 __device__ __forceinline__ void group_sync(int id) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(256) : "memory");
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(G) : "memory");
 }
 
 // p[k] <- init + p[0] + ... + p[k] in place, strictly left to right: the reference's
@@ -719,14 +720,15 @@ struct ScanScratch {
 };
 
 // One direction of find_best_split_cpu_native (lgbm-compute/src/kernels/split.rs:8970-9329)
-// for one feature, by one 256-thread group (thread k owns candidate step k). The two
+// for one feature, by one G-thread group (thread k owns candidate step k). The two
 // dependent f64 chains (running gradient and hessian sums, the hessian seeded with
 // kEpsilon) run sequentially in the reference's order on threads 0 and 32; counts,
 // the sticky stop, gains and the first-max selection run across the group.
+template <int G>
 __device__ void scan_direction(const double* hist, const DevFeature& f, const DevGainConfig& cfg,
                                const ScanLeaf& leaf, bool forward, ScanScratch& s, int bar_id,
                                ScanCand* out) {
-  const int gt = threadIdx.x & (kScanGroup - 1);
+  const int gt = threadIdx.x & (G - 1);
   const int lane = gt & 31, wg = gt >> 5;
   const double eps = k_eps();
   const int nb = f.num_bin;
@@ -762,7 +764,7 @@ __device__ void scan_direction(const double* hist, const DevFeature& f, const De
   }
   int32_t cv = act_t ? d_round_int(ah * cnt_factor) : 0;
   int32_t pre = (na_pre && gt < nb - offset) ? d_round_int(hist[2 * gt + 1] * cnt_factor) : 0;
-  group_sync(bar_id);
+  group_sync<G>(bar_id);
   // 2. sequential chains
   if ((gt == 0 || gt == 32) && count > 0) {
     const bool isg = gt == 0;
@@ -781,16 +783,16 @@ __device__ void scan_direction(const double* hist, const DevFeature& f, const De
   for (int o = 16; o > 0; o >>= 1) pre += __shfl_xor_sync(0xffffffffu, pre, o);
   if (lane == 31) s.wsum[wg] = incl;
   if (lane == 0) s.wpre[wg] = pre;
-  group_sync(bar_id);
+  group_sync<G>(bar_id);
   int32_t c_init = 0, woff = 0;
   if (na_pre) {
     int32_t tot = 0;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) tot += s.wpre[w];
+    for (int w = 0; w < G / 32; ++w) tot += s.wpre[w];
     c_init = leaf.num_data - tot;
   }
 #pragma unroll
-  for (int w = 0; w < 8; ++w)
+  for (int w = 0; w < G / 32; ++w)
     if (w < wg) woff += s.wsum[w];
   const int32_t c_own = c_init + woff + incl;
   const int32_t c_oth = leaf.num_data - c_own;
@@ -807,10 +809,10 @@ __device__ void scan_direction(const double* hist, const DevFeature& f, const De
   int32_t kst = (act && !cont && brk) ? k : 0x7fffffff;
   for (int o = 16; o > 0; o >>= 1) kst = min(kst, __shfl_xor_sync(0xffffffffu, kst, o));
   if (lane == 0) s.wmin[wg] = kst;
-  group_sync(bar_id);
+  group_sync<G>(bar_id);
   int32_t kstar = 0x7fffffff;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) kstar = min(kstar, s.wmin[w]);
+  for (int w = 0; w < G / 32; ++w) kstar = min(kstar, s.wmin[w]);
   // 5. candidate gain of step k
   double best_gain = kNegInf;
   int32_t best_k = -1;
@@ -838,12 +840,12 @@ __device__ void scan_direction(const double* hist, const DevFeature& f, const De
     s.wk[wg] = best_k;
     s.whas[wg] = has;
   }
-  group_sync(bar_id);
+  group_sync<G>(bar_id);
   if (gt == 0) {
     double bg = kNegInf;
     int32_t bk = -1, hs = 0;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
+    for (int w = 0; w < G / 32; ++w) {
       hs |= s.whas[w];
       const double g = s.wgain[w];
       const int32_t kk = s.wk[w];
@@ -1928,9 +1930,10 @@ struct FixScanSmem {
 // histogram cells (accumulated by the partition, or derived from the parent), FixHistogram,
 // compaction, the larger child by subtraction, and the REVERSE/FORWARD scans of both
 // children.
-template <bool CAT, bool PEER>
+template <bool CAT, bool PEER, int CT>
 __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const DevFeature& ft,
                                 FixScanSmem& sm) {
+  static_assert(CT == 1024 || (CT == 256 && !CAT), "control-step CTA sizes");
   const int tid = threadIdx.x;
   const int nb = ft.num_bin;
   // one histogram cell per thread (2*num_bin <= 512 cells)
@@ -1956,7 +1959,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
   // cell, all in one round trip (integers: any order of summation).
   long long tsum = 0;
   if (nt > 0) {
-    const int half = tid >> 9, c2 = tid & 511;
+    const int half = tid / (CT / 2), c2 = tid % (CT / 2);
     const size_t rl = (size_t)d.raw_len;
     const long long* pp =
         (as >= 0 ? d.la_partials + (size_t)as * d.private_tiles * rl : d.partials) +
@@ -1971,9 +1974,9 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
   }
   if (nt > kHalfTiles) {  // uniform: the upper half hands its sums to the lower half
     long long* xs = reinterpret_cast<long long*>(sm.hist[1]);
-    if (tid >= 512) xs[tid - 512] = tsum;
+    if (tid >= CT / 2) xs[tid - CT / 2] = tsum;
     __syncthreads();
-    if (tid < 512) tsum += xs[tid];
+    if (tid < CT / 2) tsum += xs[tid];
   }
   if (mine && nt > 0) bv = tsum;
   // clear the accumulator for the next partition (on one device a look-ahead hit left it
@@ -2098,7 +2101,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
         }
       }
       __syncthreads();
-      const int grp = tid >> 8;  // (leaf, direction) group
+      const int grp = tid / (CT / 4);  // (leaf, direction) group
       const int sel = grp >> 1;
       const bool fwd = (grp & 1) != 0;
       const int32_t leaf = sel == 0 ? S : Lg;
@@ -2108,8 +2111,8 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
         if (leaf_buildable(ls)) {
           ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
           if (!is_cat)
-            scan_direction(sm.hist[sel], ft, d.gain, sl, fwd, sm.scan[grp], 1 + grp,
-                           &sm.cand[grp]);
+            scan_direction<CT / 4>(sm.hist[sel], ft, d.gain, sl, fwd, sm.scan[grp], 1 + grp,
+                                   &sm.cand[grp]);
           else if (!fwd)  // bin_type dispatch (learner.rs:3099-3149)
             cat_scan(sm.hist[sel], ft, d.gain, sl, sm.scan[grp], 1 + grp, &sm.cat[sel]);
         }
@@ -2162,7 +2165,7 @@ static_assert(sizeof(DevSplitInfo) % 8 == 0, "scan results are copied as 8-byte 
 // One control step by the CTAs [0, min(F, gridDim.x)), each taking features
 // blockIdx.x, blockIdx.x + gridDim.x, ...: apply the pending split, scan the two leaves,
 // and -- in the CTA that finishes last -- pick the next split and write the control block.
-template <bool CAT, bool PEER>
+template <bool CAT, bool PEER, int CT>
 __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& cs) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -2183,7 +2186,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   for (int f = fb + blockIdx.x; f < fe; f += gridDim.x) {
     // the CTA's first feature was read while the pending split was applied
     const DevFeature ft = f == fb + (int)blockIdx.x ? cs.ft0 : d.feat[f];
-    fixscan_feature<CAT, PEER>(d, cs.prep, f, ft, sm);
+    fixscan_feature<CAT, PEER, CT>(d, cs.prep, f, ft, sm);
     __syncthreads();
   }
   // Arrival: the barrier orders every thread's writes before thread 0's release, and the
@@ -2205,11 +2208,11 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     const int nw = d.F * (int)(2 * sizeof(DevSplitInfo) / 8);
     const unsigned long long* src = reinterpret_cast<const unsigned long long*>(d.scan_out);
     unsigned long long* dst = reinterpret_cast<unsigned long long*>(so);
-    for (int i = tid; i < nw; i += kScanThreads) dst[i] = __ldcg(src + i);
+    for (int i = tid; i < nw; i += CT) dst[i] = __ldcg(src + i);
     if (CAT)
-      for (int i = tid; i < 2 * d.F * kCatWords; i += kScanThreads) sc[i] = __ldcg(d.scan_cat + i);
+      for (int i = tid; i < 2 * d.F * kCatWords; i += CT) sc[i] = __ldcg(d.scan_cat + i);
   }
-  if (tid == kScanThreads - 32) {
+  if (tid == CT - 32) {
     cs.ok[0] = __ldcg(&d.scan_ok[0]);
     cs.ok[1] = __ldcg(&d.scan_ok[1]);
     cs.err = *reinterpret_cast<volatile uint32_t*>(&d.ctrl->error);  // other CTAs' bits
@@ -2325,12 +2328,12 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   }
 }
 
-template <bool CAT, bool PEER>
-__global__ void __launch_bounds__(kScanThreads) k_fixscan(GrowDev d, int s) {
+template <bool CAT, bool PEER, int CT>
+__global__ void __launch_bounds__(CT, CT == 1024 ? 1 : 4) k_fixscan(GrowDev d, int s) {
   const SpanStamp span(d);
   __shared__ FixScanSmem sm;
   __shared__ CtlSmem cs;
-  control_step<CAT, PEER>(d, s, sm, cs);
+  control_step<CAT, PEER, CT>(d, s, sm, cs);
 }
 
 // ------------------------------------------------------------------------------------
@@ -2995,7 +2998,7 @@ __global__ void __launch_bounds__(512) k_scan_standalone(const double* hist,
   __syncthreads();
   const int grp = threadIdx.x >> 8;
   ScanLeaf sl{ls.sum_g, ls.sum_h, ls.weight, ls.num_data};
-  scan_direction(s_hist, ft, cfg, sl, grp == 1, s_scan[grp], 1 + grp, &s_cand[grp]);
+  scan_direction<256>(s_hist, ft, cfg, sl, grp == 1, s_scan[grp], 1 + grp, &s_cand[grp]);
   __syncthreads();
   if (threadIdx.x == 0) out[blockIdx.x] = finalize_split(cfg, sl, s_cand[0], s_cand[1]);
 }
@@ -3154,9 +3157,13 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       // variants: categorical features, and the peer exchange (off on one device)
       const int grid = x.slice_end - x.slice_begin;  // this rank's features
       if (x.has_cat)
-        (px ? k_fixscan<true, true> : k_fixscan<true, false>)<<<grid, kScanThreads, 0, st>>>(x, s);
+        (px ? k_fixscan<true, true, 1024> : k_fixscan<true, false, 1024>)<<<grid, 1024, 0, st>>>(
+            x, s);
+      else if (x.narrow_scan)  // every feature has at most 64 bins: 256-thread CTAs
+        (px ? k_fixscan<false, true, 256> : k_fixscan<false, false, 256>)<<<grid, 256, 0, st>>>(
+            x, s);
       else
-        (px ? k_fixscan<false, true> : k_fixscan<false, false>)<<<grid, kScanThreads, 0, st>>>(
+        (px ? k_fixscan<false, true, 1024> : k_fixscan<false, false, 1024>)<<<grid, 1024, 0, st>>>(
             x, s);
       PROF_END();
     }

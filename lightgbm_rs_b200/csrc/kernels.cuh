@@ -119,6 +119,7 @@ struct GrowDev {
   uint32_t* t_cat;         // [L][kCatWords] left bins of each categorical tree node
   uint32_t* split_cat;     // [kCatWords] left bins of the pending split (categorical)
   int32_t has_cat;         // some feature is categorical: the control step's CAT variant
+  int32_t narrow_scan;     // numeric features of at most 64 bins: 256-thread control CTAs
   uint8_t* scan_ok;        // [2] leaf scanned flags
   // Data-parallel exchange of the accumulated child over peer memory (xranks > 1). Every
   // rank holds two accumulators [2][raw_len + 2]; producer k of a tree (the root build,
