@@ -370,6 +370,11 @@ int lgbm_b200_learner::configure_groups(int mode) {
     CUDA_TRY(cudaGetLastError());
     const int sms = sm_count(device);
     build_blocks = sms * 2;
+    // Several feature groups (wide data): about two waves of CTAs over all groups. A build
+    // CTA holds most of an SM's shared memory, so CTAs of a small child that find no rows
+    // would otherwise take SMs wave after wave.
+    const int ng = (int)groups.size();
+    if (ng > 1) build_blocks = std::max(1, (2 * sms + ng - 1) / ng);
     // per-CTA row ranges stay below 65536 rows (level-3 counters and cold sums)
     const int64_t need = (ds->num_data + 65535 - 1) / 65535;
     if (build_blocks < need) build_blocks = (int)need;
@@ -407,6 +412,8 @@ int lgbm_b200_learner::configure_groups(int mode) {
   per_sm = std::min(per_sm, 4);
   const int sms = sm_count(device);
   build_blocks = sms * per_sm;
+  if (groups.size() > 1)  // about two waves over all groups (see the quantized build)
+    build_blocks = std::max(1, (2 * sms * per_sm + (int)groups.size() - 1) / (int)groups.size());
   const int64_t need = (ds->num_data + (1 << 18) - 1) >> 18;
   if (build_blocks < need) build_blocks = (int)need;
   // the fused partition's cell layout (feature << shift) + bin, for f32 gradients
