@@ -1,9 +1,9 @@
 // Device construction of the row-major u8 bin matrix from feature-major columns: either
 // bins already computed (range-checked here), or raw feature values binned here with
 // the host-found bin mappers (BinMapper::value_to_bin, lgbm-dataset/src/bin_mapper.rs:
-// 148-199). One thread handles one row and 16 consecutive features: 16 coalesced column
-// reads (consecutive threads hold consecutive rows) and one 16-byte store of the row's
-// bins.
+// 148-199). One thread handles one row and 16 consecutive features (32 in a 4-bit
+// matrix): coalesced column reads (consecutive threads hold consecutive rows) and one
+// 16-byte store of the row's bins.
 #include <cmath>
 #include <type_traits>
 
@@ -80,12 +80,22 @@ __global__ void __launch_bounds__(kBinRowThreads) k_bin_rows(BinRowsDev d, const
   if (r >= n) return;
   const int g = blockIdx.y;
   uint32_t w[4] = {0u, 0u, 0u, 0u};
-  for (int j = 0; j < 16; ++j) {
-    const int f = g * 16 + j;
-    if (f >= d.num_features) break;
-    const uint32_t b = to_bin<T>(d, f, cols[(int64_t)f * col_stride + r], row0 + r,
-                                 d.first_bad);
-    w[j >> 2] |= (b & 0xffu) << (8 * (j & 3));
+  if (d.packed4) {  // 32 features per 16-byte chunk, two 4-bit bins per byte
+    for (int j = 0; j < 32; ++j) {
+      const int f = g * 32 + j;
+      if (f >= d.num_features) break;
+      const uint32_t b = to_bin<T>(d, f, cols[(int64_t)f * col_stride + r], row0 + r,
+                                   d.first_bad);
+      w[j >> 3] |= (b & 0xfu) << (4 * (j & 7));
+    }
+  } else {
+    for (int j = 0; j < 16; ++j) {
+      const int f = g * 16 + j;
+      if (f >= d.num_features) break;
+      const uint32_t b = to_bin<T>(d, f, cols[(int64_t)f * col_stride + r], row0 + r,
+                                   d.first_bad);
+      w[j >> 2] |= (b & 0xffu) << (8 * (j & 3));
+    }
   }
   *reinterpret_cast<uint4*>(out + r * d.stride + g * 16) = make_uint4(w[0], w[1], w[2], w[3]);
 }

@@ -26,7 +26,7 @@
 namespace lgbm_b200 {
 void set_build_smem_limit(size_t bytes);
 int q4_max_cells();
-bool q4_supported(int shift, int nch);
+bool q4_supported(int shift, int nch, bool pack4);
 void launch_learner_gradients(const ObjDev& o, int32_t kind, cudaStream_t st);
 void launch_gather_partition(const GrowDev& d, uint32_t* out, cudaStream_t st);
 }  // namespace lgbm_b200
@@ -264,7 +264,8 @@ struct lgbm_b200_dataset {
   int device = 0;
   int64_t num_data = 0;
   int32_t num_features = 0;
-  int32_t stride = 0;
+  int32_t stride = 0;   // bytes per row of the bin matrix
+  int32_t packed4 = 0;  // two 4-bit bins per byte
   int32_t total_bins = 0;
   std::vector<DevFeature> feats;
   DevBuf<uint8_t> bins;
@@ -348,14 +349,16 @@ int lgbm_b200_learner::configure_groups(int mode) {
     for (int f = 0; f < F; ++f)
       while ((1 << shift) < ds->feats[f].num_bin) ++shift;
     const int max_nf = std::min(128, kQ4MaxCells >> shift);
-    const int per_group = F <= max_nf ? F : (max_nf / 16) * 16;
+    // groups start on a 16-byte boundary of the row: 16 features, or 32 in a 4-bit matrix
+    const int align = ds->packed4 ? 32 : 16;
+    const int per_group = F <= max_nf ? F : (max_nf / align) * align;
     for (int f0 = 0; f0 < F; f0 += per_group) {
       const int f1 = std::min(F, f0 + per_group);
       groups.push_back(DevFeatureGroup{f0, f1, ds->feats[f0].bin_off, (f1 - f0) << shift, shift,
                                        0});
     }
     const int nch = (per_group + 15) / 16;
-    if (!q4_supported(shift, nch))
+    if (!q4_supported(shift, nch, ds->packed4 != 0))
       return fail(LGBM_B200_CAPABILITY_UNAVAILABLE,
                   "quantized build: no kernel for bin stride 2^%d with %d feature chunks", shift,
                   nch);
@@ -381,8 +384,9 @@ int lgbm_b200_learner::configure_groups(int mode) {
     return LGBM_B200_OK;
   }
   DevFeatureGroup cur{0, 0, 0, 0, 0, 0};
-  for (int b0 = 0; b0 < F; b0 += 16) {
-    const int b1 = std::min(F, b0 + 16);
+  const int blk = ds->packed4 ? 32 : 16;  // a group starts on a 16-byte boundary of the row
+  for (int b0 = 0; b0 < F; b0 += blk) {
+    const int b1 = std::min(F, b0 + blk);
     int nb = 0;
     for (int f = b0; f < b1; ++f) nb += ds->feats[f].num_bin;
     const bool fits = (size_t)(cur.num_bins + nb) * bpb <= budget && (b1 - cur.f_begin) <= 128;
@@ -479,6 +483,7 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.ctrl = ctrl.p;
   d.feat = ds->d_feats.p;
   d.F = ds->num_features;
+  d.packed4 = ds->packed4;
   d.sliced = 0;  // every feature on this device (a data-parallel job may slice them)
   d.slice_begin = 0;
   d.slice_end = d.F;
@@ -562,7 +567,8 @@ void lgbm_b200_learner::bind(const void* gh_ptr, const DevGhParams* ghp_ptr,
   d.stopped = stopped;
   d.gh_mode = gh_mode;
   d.q4_shift = q4_shift;
-  d.fused = fused_partition_supported(gh_mode, ds->num_features, q4_shift, q4_nch) ? 1 : 0;
+  d.fused = fused_partition_supported(gh_mode, ds->num_features, q4_shift, q4_nch,
+                                      ds->packed4 != 0) ? 1 : 0;
   d.lookahead = d.fused && la_enabled ? 1 : 0;
 
   d.q4_nch = q4_nch;
@@ -1379,7 +1385,13 @@ int dataset_build(int32_t device, const void* const* columns, int kind, int64_t 
   ds->device = device;
   ds->num_data = num_data;
   ds->num_features = num_features;
-  ds->stride = ((num_features + 15) / 16) * 16;
+  // 4-bit rows when every feature has at most 16 bins (max_bin <= 15 and the like): two
+  // bins per byte, row stride rounded up to 16 bytes (LGBM_B200_PACK4=0: one byte per bin)
+  int32_t max_bins = 0;
+  for (int f = 0; f < num_features; ++f) max_bins = std::max(max_bins, meta[f].num_bin);
+  const char* p4 = std::getenv("LGBM_B200_PACK4");
+  ds->packed4 = (max_bins <= 16 && !(p4 && p4[0] == '0')) ? 1 : 0;
+  ds->stride = ds->packed4 ? ((num_features + 31) / 32) * 16 : ((num_features + 15) / 16) * 16;
   int32_t bin_off = 0;
   std::vector<DevBinFeature> bf(num_features);
   std::vector<double> upper;
@@ -1444,7 +1456,8 @@ int dataset_build(int32_t device, const void* const* columns, int kind, int64_t 
   }
   CUDA_TRY(d_bad.alloc(1));
   CUDA_TRY(cudaMemset(d_bad.p, 0xff, 8));
-  BinRowsDev br{d_bf.p, num_features, ds->stride, d_upper.p, d_keys.p, d_cbins.p, d_bad.p};
+  BinRowsDev br{d_bf.p,    num_features, ds->packed4, ds->stride,
+                d_upper.p, d_keys.p,     d_cbins.p,   d_bad.p};
   const int elem = kind == kBinRowsF32 ? 4 : kind;
   const int64_t chunk = std::max<int64_t>(
       1, std::min<int64_t>(num_data, (256ll << 20) / ((int64_t)num_features * elem)));
@@ -1508,8 +1521,21 @@ int lgbm_b200_dataset_create_from_values(int32_t device, const void* const* colu
 int lgbm_b200_dataset_copy_bins(const lgbm_b200_dataset* ds, uint8_t* out) {
   if (!ds || !out) return fail(LGBM_B200_INVALID_ARGUMENT, "dataset_copy_bins: null argument");
   DeviceGuard g(ds->device);
-  CUDA_TRY(cudaMemcpy(out, ds->bins.p, (size_t)ds->num_data * ds->stride,
-                      cudaMemcpyDeviceToHost));
+  if (!ds->packed4) {
+    CUDA_TRY(cudaMemcpy(out, ds->bins.p, (size_t)ds->num_data * ds->stride,
+                        cudaMemcpyDeviceToHost));
+    return LGBM_B200_OK;
+  }
+  // a 4-bit matrix: read back packed, handed out one byte per bin
+  const int32_t F = ds->num_features, wide = ((F + 15) / 16) * 16;
+  std::vector<uint8_t> packed((size_t)ds->num_data * ds->stride);
+  CUDA_TRY(cudaMemcpy(packed.data(), ds->bins.p, packed.size(), cudaMemcpyDeviceToHost));
+  for (int64_t r = 0; r < ds->num_data; ++r) {
+    const uint8_t* src = packed.data() + (size_t)r * ds->stride;
+    uint8_t* dst = out + (size_t)r * wide;
+    for (int32_t f = 0; f < wide; ++f)
+      dst[f] = f < F ? (uint8_t)((src[f >> 1] >> ((f & 1) * 4)) & 15) : 0;
+  }
   return LGBM_B200_OK;
 }
 

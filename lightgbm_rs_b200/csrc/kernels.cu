@@ -297,8 +297,43 @@ __device__ __forceinline__ void unpack_qpack(unsigned long long v, long long* g,
   *hlc3 = hl | (c3 << 32);
 }
 
+// 32 4-bit bins (one 16-byte chunk of a packed row: feature 2k in the low nibble of byte
+// k, 2k + 1 in the high nibble) -> the same bins one per byte (two 16-byte chunks).
+__device__ __forceinline__ void unpack4(const uint4 p, uint4& a, uint4& b) {
+  const uint32_t in[4] = {p.x, p.y, p.z, p.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t lo = in[k] & 0x0f0f0f0fu, hi = (in[k] >> 4) & 0x0f0f0f0fu;
+    o[2 * k] = __byte_perm(lo, hi, 0x5140);
+    o[2 * k + 1] = __byte_perm(lo, hi, 0x7362);
+  }
+  a = make_uint4(o[0], o[1], o[2], o[3]);
+  b = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// The first NCH 16-feature chunks of a row as one byte per bin: loaded as they are, or
+// (PACK4) from half as many packed chunks.
+template <int NCH, bool PACK4>
+__device__ __forceinline__ void load_row(const uint8_t* __restrict__ row, uint4 (&w)[NCH]) {
+  const uint4* rp = reinterpret_cast<const uint4*>(row);
+  if (!PACK4) {
+#pragma unroll
+    for (int ch = 0; ch < NCH; ++ch) w[ch] = rp[ch];
+  } else {
+#pragma unroll
+    for (int pc = 0; pc < (NCH + 1) / 2; ++pc) {
+      uint4 a, b;
+      unpack4(rp[pc], a, b);
+      w[2 * pc] = a;
+      if (2 * pc + 1 < NCH) w[2 * pc + 1] = b;
+    }
+  }
+}
+
 template <int MODE>
 __device__ __forceinline__ void build_block(const uint8_t* __restrict__ bins, int32_t stride,
+                                            bool packed4,
                                             const uint32_t* __restrict__ idx, int32_t begin,
                                             int32_t r0, int32_t r1, bool identity,
                                             const void* __restrict__ gh, const DevGhParams& p,
@@ -313,9 +348,16 @@ __device__ __forceinline__ void build_block(const uint8_t* __restrict__ bins, in
     const uint32_t row = identity ? (uint32_t)(begin + k) : idx[begin + k];
     GhValue<MODE> v;
     v.load(gh, row, p, s_lut_g, s_lut_h);
-    const uint8_t* rp = bins + (size_t)row * stride + grp.f_begin;
+    const uint8_t* rp = bins + (size_t)row * stride + (packed4 ? grp.f_begin / 2 : grp.f_begin);
     for (int c = 0; c < nchunks; ++c) {
-      const uint4 w = *reinterpret_cast<const uint4*>(rp + 16 * c);
+      uint4 w;
+      if (packed4) {  // 16 features = half of a packed 16-byte chunk
+        uint4 a, b;
+        unpack4(*reinterpret_cast<const uint4*>(rp + 16 * (c >> 1)), a, b);
+        w = (c & 1) ? b : a;
+      } else {
+        w = *reinterpret_cast<const uint4*>(rp + 16 * c);
+      }
       const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -381,7 +423,8 @@ __global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d, int phase) {
   __syncthreads();
   const DevGhParams& p = *d.ghp;
   const uint32_t* idx = buf == 1 ? d.idx1 : d.idx0;
-  build_block<MODE>(d.bins, d.stride, idx, begin, r0, r1, buf == 2, d.gh, p, grp, s_binoff,
+  build_block<MODE>(d.bins, d.stride, d.packed4 != 0, idx, begin, r0, r1, buf == 2, d.gh, p, grp,
+                    s_binoff,
                     s_used, s_lut, s_lut + 256, acc);
   __syncthreads();
   long long* raw = d.raw + 2 * (size_t)grp.bin_base;
@@ -438,12 +481,11 @@ __device__ __forceinline__ void q4_row_regs(const uint4 (&w)[NCH], int32_t pv, b
   }
 }
 
-template <int SHIFT, int NCH, bool MASKED>
-__device__ __forceinline__ void q4_row(const uint4* __restrict__ rp, int32_t pv, bool is3,
+template <int SHIFT, int NCH, bool MASKED, bool PACK4>
+__device__ __forceinline__ void q4_row(const uint8_t* __restrict__ rp, int32_t pv, bool is3,
                                        uint32_t* hot, const uint32_t* mask, uint32_t tail) {
   uint4 w[NCH];
-#pragma unroll
-  for (int ch = 0; ch < NCH; ++ch) w[ch] = rp[ch];
+  load_row<NCH, PACK4>(rp, w);
   q4_row_regs<SHIFT, NCH, MASKED>(w, pv, is3, hot, mask, tail);
 }
 
@@ -474,7 +516,7 @@ __device__ __forceinline__ Q4Mask q4_mask(const uint32_t* s_mask, int nf) {
   return m;
 }
 
-template <int SHIFT, int NCH>
+template <int SHIFT, int NCH, bool PACK4 = false>
 __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase) {
   const SpanStamp span(d);
   extern __shared__ uint32_t sm[];
@@ -538,7 +580,7 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase
   const uint32_t* idx = buf == 1 ? d.idx1 : d.idx0;
   const uint16_t* gq = reinterpret_cast<const uint16_t*>(d.gh);
   const bool identity = buf == 2;
-  const uint8_t* bins = d.bins + grp.f_begin;
+  const uint8_t* bins = d.bins + (PACK4 ? grp.f_begin / 2 : grp.f_begin);
   const size_t stride = (size_t)d.stride;
   for (int32_t cs = r0; cs < r1; cs += kQ4Chunk) {
     const int32_t ce = min(r1, cs + kQ4Chunk);
@@ -549,16 +591,18 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase
       const uint32_t row1 = two ? (identity ? (uint32_t)(begin + k2) : idx[begin + k2]) : row0;
       const uint16_t q0 = gq[row0];
       const uint16_t q1 = gq[row1];
-      const uint4* rp0 = reinterpret_cast<const uint4*>(bins + (size_t)row0 * stride);
-      const uint4* rp1 = reinterpret_cast<const uint4*>(bins + (size_t)row1 * stride);
+      const uint8_t* rp0 = bins + (size_t)row0 * stride;
+      const uint8_t* rp1 = bins + (size_t)row1 * stride;
       const int qg0 = (int)(int8_t)(q0 & 0xff), qh0 = (int)(int8_t)(q0 >> 8);
       const int qg1 = (int)(int8_t)(q1 & 0xff), qh1 = (int)(int8_t)(q1 >> 8);
       if (full) {
-        q4_row<SHIFT, NCH, false>(rp0, qg0 + (qh0 << 16), qh0 == 3, hot, mask, tail);
-        if (two) q4_row<SHIFT, NCH, false>(rp1, qg1 + (qh1 << 16), qh1 == 3, hot, mask, tail);
+        q4_row<SHIFT, NCH, false, PACK4>(rp0, qg0 + (qh0 << 16), qh0 == 3, hot, mask, tail);
+        if (two)
+          q4_row<SHIFT, NCH, false, PACK4>(rp1, qg1 + (qh1 << 16), qh1 == 3, hot, mask, tail);
       } else {
-        q4_row<SHIFT, NCH, true>(rp0, qg0 + (qh0 << 16), qh0 == 3, hot, mask, tail);
-        if (two) q4_row<SHIFT, NCH, true>(rp1, qg1 + (qh1 << 16), qh1 == 3, hot, mask, tail);
+        q4_row<SHIFT, NCH, true, PACK4>(rp0, qg0 + (qh0 << 16), qh0 == 3, hot, mask, tail);
+        if (two)
+          q4_row<SHIFT, NCH, true, PACK4>(rp1, qg1 + (qh1 << 16), qh1 == 3, hot, mask, tail);
       }
     }
     if (ce < r1) {
@@ -598,7 +642,15 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase
 
 // (SHIFT, NCH) instantiations with (16 * (NCH - 1) + 1) << SHIFT <= kQ4MaxCells.
 using Q4Kernel = void (*)(GrowDev, int);
-__host__ Q4Kernel q4_kernel(int shift, int nch) {
+__host__ Q4Kernel q4_kernel(int shift, int nch, bool pack4 = false) {
+  if (pack4) {  // 4-bit rows: every feature has at most 16 bins (shift 4)
+#define Q4P_CASE(N) \
+  if (shift == 4 && nch == N) return k_build_q4<4, N, true>;
+    Q4P_CASE(1) Q4P_CASE(2) Q4P_CASE(3) Q4P_CASE(4) Q4P_CASE(5) Q4P_CASE(6) Q4P_CASE(7)
+    Q4P_CASE(8)
+#undef Q4P_CASE
+    return nullptr;
+  }
 #define Q4_CASE(S, N) \
   if (shift == S && nch == N) return k_build_q4<S, N>;
   Q4_CASE(4, 1) Q4_CASE(4, 2) Q4_CASE(4, 3) Q4_CASE(4, 4)
@@ -2350,7 +2402,7 @@ __device__ __forceinline__ unsigned long long pack_status(uint32_t epoch, uint32
 
 struct PartitionTile {
   // returns false on look-back timeout
-  __device__ static bool run(const uint8_t* __restrict__ bins, int32_t stride,
+  __device__ static bool run(const uint8_t* __restrict__ bins, int32_t stride, bool packed4,
                              const DevFeature& ft, int32_t feature, uint32_t threshold,
                              bool default_left, const uint32_t* __restrict__ src,
                              bool identity, uint32_t* __restrict__ dst, int32_t begin,
@@ -2371,7 +2423,7 @@ struct PartitionTile {
       if (p < count) {
         const uint32_t row = identity ? (uint32_t)(begin + p) : src[begin + p];
         rows[j] = row;
-        const int32_t bin = bins[(size_t)row * stride + feature];
+        const int32_t bin = (int32_t)row_bin(bins + (size_t)row * stride, feature, packed4);
         validmask |= 1u << j;
         const bool gr = cat ? d_cat_go_right(cat, bin)
                             : ((ft.flags & kFeatMissingRoute)
@@ -2495,7 +2547,8 @@ __global__ void __launch_bounds__(kPartThreads) k_partition(GrowDev d) {
     const int32_t tile = s_tile;
     __syncthreads();
     if (tile >= ntiles) break;
-    const bool ok = PartitionTile::run(d.bins, d.stride, ft, f, thr, dl, sp, src == 2, dp, begin,
+    const bool ok = PartitionTile::run(d.bins, d.stride, d.packed4 != 0, ft, f, thr, dl, sp,
+                                       src == 2, dp, begin,
                                        count, tile, epoch, d.part_status, &c->part_left_total,
                                        (ft.flags & kFeatCategorical) ? d.split_cat : nullptr);
     if (!ok) {
@@ -2611,7 +2664,7 @@ __device__ __forceinline__ void f32_row_regs(const uint4 (&w)[NCH], long long a,
 // One fused partition by the whole grid (every thread of every CTA calls it); `sm` holds
 // the accumulators. Quantized (F32 false): hot | c3 | cold_g | cold_q, kQ4MaxCells u32
 // words each. f32 gradients: g64 | h64, kQ4MaxCells u64 words each (the same bytes).
-template <int SHIFT, int NCH, bool F32>
+template <int SHIFT, int NCH, bool F32, bool PACK4>
 __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t* sm,
                                    PartSmem& ps_) {
   static_assert(NCH <= kFpMaxChunks, "row chunks held in registers");
@@ -2773,9 +2826,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
 #pragma unroll
     for (int j = 0; j < kFpItems; ++j) {
       if ((validmask >> j) & 1u) {
-        const uint4* rp = reinterpret_cast<const uint4*>(d.bins + (size_t)rows[j] * stride);
-#pragma unroll
-        for (int ch = 0; ch < NCH; ++ch) w[j][ch] = rp[ch];
+        load_row<NCH, PACK4>(d.bins + (size_t)rows[j] * stride, w[j]);
         if (F32)
           fv[j] = build ? gf[rows[j]] : make_float2(0.0f, 0.0f);
         else
@@ -2947,16 +2998,21 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
 }
 
 
-template <int SHIFT, int NCH, bool F32>
+template <int SHIFT, int NCH, bool F32, bool PACK4 = false>
 __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int build, int la) {
   const SpanStamp span(d);
   extern __shared__ uint32_t sm[];
   __shared__ PartSmem ps;
-  partition_q4_phase<SHIFT, NCH, F32>(d, build, la, sm, ps);
+  partition_q4_phase<SHIFT, NCH, F32, PACK4>(d, build, la, sm, ps);
 }
 
 using PartQ4Kernel = void (*)(GrowDev, int, int);
-__host__ PartQ4Kernel part_q4_kernel(int shift, int nch, bool f32 = false) {
+__host__ PartQ4Kernel part_q4_kernel(int shift, int nch, bool f32 = false, bool pack4 = false) {
+  if (pack4) {  // 4-bit rows (shift 4)
+    if (shift == 4 && nch == 1) return f32 ? k_partition_q4<4, 1, true, true> : k_partition_q4<4, 1, false, true>;
+    if (shift == 4 && nch == 2) return f32 ? k_partition_q4<4, 2, true, true> : k_partition_q4<4, 2, false, true>;
+    return nullptr;
+  }
 #define PQ4_CASE(S, N) \
   if (shift == S && nch == N) return f32 ? k_partition_q4<S, N, true> : k_partition_q4<S, N, false>;
   PQ4_CASE(4, 1) PQ4_CASE(4, 2) PQ4_CASE(5, 1) PQ4_CASE(5, 2) PQ4_CASE(6, 1) PQ4_CASE(6, 2)
@@ -3016,7 +3072,7 @@ __global__ void __launch_bounds__(kPartThreads) k_partition_standalone(
     const int32_t tile = s_tile;
     __syncthreads();
     if (tile >= ntiles) break;
-    if (!PartitionTile::run(bins, stride, ft, feature, threshold, default_left != 0, nullptr,
+    if (!PartitionTile::run(bins, stride, false, ft, feature, threshold, default_left != 0, nullptr,
                             true, dst, 0, count, tile, 1u, status, left_total)) {
       // the look-back gave up: this tile's rows were not written, so the result is void
       if (threadIdx.x == 0) atomicOr(error, kErrSpinTimeout);
@@ -3077,10 +3133,10 @@ void LaunchProfiler::end(cudaStream_t st, int slot) {
 
 // The partition accumulates the child itself for packed quantized gradients and for f32
 // gradients, when every feature fits one shared-memory layout (feature << shift) + bin.
-bool fused_partition_supported(int gh_mode, int num_features, int shift, int nch) {
+bool fused_partition_supported(int gh_mode, int num_features, int shift, int nch, bool pack4) {
   return (gh_mode == GH_QPACK || gh_mode == GH_FLOAT) && num_features <= 128 &&
          (num_features << shift) <= kQ4MaxCells && nch <= kFpMaxChunks &&
-         part_q4_kernel(shift, nch, gh_mode == GH_FLOAT) != nullptr;
+         part_q4_kernel(shift, nch, gh_mode == GH_FLOAT, pack4) != nullptr;
 }
 
 size_t fused_partition_smem() { return (size_t)4 * sizeof(uint32_t) * kQ4MaxCells; }
@@ -3129,7 +3185,8 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
   auto build = [&](const GrowDev& x, int phase) {
     PROF_BEGIN(KC_BUILD);
     if (x.gh_mode == GH_QPACK)
-      q4_kernel(x.q4_shift, x.q4_nch)<<<bgrid, kQ4Threads, build_smem, st>>>(x, phase);
+      q4_kernel(x.q4_shift, x.q4_nch, x.packed4 != 0)<<<bgrid, kQ4Threads, build_smem, st>>>(
+          x, phase);
     else if (x.gh_mode == GH_QLUT)
       k_build<GH_QLUT><<<bgrid, kBuildThreads, build_smem, st>>>(x, phase);
     else
@@ -3178,7 +3235,7 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
     // mostly find the split already partitioned) are placed first
     if (x.fused) {
       PROF_BEGIN(KC_PARTITION);
-      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<sms, kFpThreads,
+      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT, x.packed4 != 0)<<<sms, kFpThreads,
                                                                 fused_partition_smem(), st>>>(
           x, phase == 1 ? 1 : 0, -1);
       PROF_END();
@@ -3198,7 +3255,7 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       const int pslot = prof ? prof->begin(lst, KC_PARTITION) : -1;
       GrowDev xl = x;
       xl.span_slot = span_slot_of(s, SPAN_LOOKAHEAD);
-      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT)<<<las->blocks, kFpThreads,
+      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT, x.packed4 != 0)<<<las->blocks, kFpThreads,
                                                                 fused_partition_smem(),
                                                                 lst>>>(xl, 1, s & (kLaSlots - 1));
       if (prof) prof->end(lst, pslot);
@@ -3219,24 +3276,26 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
 
 int q4_max_cells() { return kQ4MaxCells; }
 
-bool q4_supported(int shift, int nch) { return q4_kernel(shift, nch) != nullptr; }
+bool q4_supported(int shift, int nch, bool pack4) { return q4_kernel(shift, nch, pack4) != nullptr; }
 
 void set_build_smem_limit(size_t bytes) {
   for (int sh = 4; sh <= 8; ++sh)
     for (int n = 1; n <= 8; ++n)
-      if (q4_kernel(sh, n)) {
-        cudaFuncSetAttribute(q4_kernel(sh, n), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(4 * sizeof(uint32_t) * kQ4MaxCells));
-        cudaFuncSetAttribute(q4_kernel(sh, n), cudaFuncAttributePreferredSharedMemoryCarveout,
-                             100);
-      }
+      for (bool p4 : {false, true})
+        if (q4_kernel(sh, n, p4)) {
+          cudaFuncSetAttribute(q4_kernel(sh, n, p4), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)(4 * sizeof(uint32_t) * kQ4MaxCells));
+          cudaFuncSetAttribute(q4_kernel(sh, n, p4),
+                               cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        }
   for (int sh = 4; sh <= 8; ++sh)
     for (int n = 1; n <= kFpMaxChunks; ++n)
       for (bool f32 : {false, true})
-        if (part_q4_kernel(sh, n, f32))
-          cudaFuncSetAttribute(part_q4_kernel(sh, n, f32),
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)fused_partition_smem());
+        for (bool p4 : {false, true})
+          if (part_q4_kernel(sh, n, f32, p4))
+            cudaFuncSetAttribute(part_q4_kernel(sh, n, f32, p4),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)fused_partition_smem());
   cudaFuncSetAttribute(k_build<GH_QLUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)bytes);
   cudaFuncSetAttribute(k_build<GH_FLOAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -118,6 +118,7 @@ struct GrowDev {
   uint32_t* best_cat;      // [L][kCatWords] left bins of each leaf's best split
   uint32_t* t_cat;         // [L][kCatWords] left bins of each categorical tree node
   uint32_t* split_cat;     // [kCatWords] left bins of the pending split (categorical)
+  int32_t packed4;         // the bin matrix holds two 4-bit bins per byte (row_bin)
   int32_t has_cat;         // some feature is categorical: the control step's CAT variant
   int32_t narrow_scan;     // numeric features of at most 64 bins: 256-thread control CTAs
   uint8_t* scan_ok;        // [2] leaf scanned flags
@@ -229,7 +230,7 @@ struct LookAheadStreams {
 void launch_tree(const GrowDev& d, int build_blocks, size_t build_smem, cudaStream_t st,
                  LaunchProfiler* prof = nullptr, const DeviceComm* comm = nullptr,
                  const LookAheadStreams* las = nullptr);
-bool fused_partition_supported(int gh_mode, int num_features, int shift, int nch);
+bool fused_partition_supported(int gh_mode, int num_features, int shift, int nch, bool pack4);
 int build_smem_bytes_per_bin(int gh_mode);
 
 // Objective / score kernels (objective.cu).
@@ -307,9 +308,17 @@ struct DevBinFeature {
   int32_t n_cat;     // categorical: categories in cat_keys
   int64_t off;       // first bound in `upper` (numerical) or key in `cat_keys` (categorical)
 };
+// Bin of feature f in one row of the bin matrix: one byte per bin, or (packed4, every
+// feature with at most 16 bins) two 4-bit bins per byte, feature 2k in the low nibble of
+// byte k and 2k + 1 in the high nibble.
+__device__ __forceinline__ uint32_t row_bin(const uint8_t* row, int f, bool packed4) {
+  return packed4 ? ((uint32_t)row[f >> 1] >> ((f & 1) << 2)) & 15u : (uint32_t)row[f];
+}
+
 struct BinRowsDev {
   const DevBinFeature* feats;
   int32_t num_features;
+  int32_t packed4;                  // write two 4-bit bins per byte
   int32_t stride;                   // bytes per row (a multiple of 16)
   const double* upper;              // numerical bin upper bounds, concatenated
   const int32_t* cat_keys;          // categorical: ascending categories, concatenated

@@ -648,8 +648,9 @@ __global__ void __launch_bounds__(256) k_score_update(GrowDev d, double* score,
     while (node >= 0) {
       const int f = s_feat[node];
       const int8_t dec = s_dec[node];
-      const bool right = (dec & 1) ? d_cat_go_right(s_cat[node], rp[f])
-                                   : d_go_right(d.feat[f], s_thr[node], (dec & 2) != 0, rp[f]);
+      const int32_t bin = (int32_t)row_bin(rp, f, d.packed4 != 0);
+      const bool right = (dec & 1) ? d_cat_go_right(s_cat[node], bin)
+                                   : d_go_right(d.feat[f], s_thr[node], (dec & 2) != 0, bin);
       node = right ? s_right[node] : s_left[node];
     }
     score[r] += s_val[~node];
