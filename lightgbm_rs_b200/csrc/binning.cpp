@@ -9,6 +9,8 @@
 #include <cmath>
 #include <cstdint>
 #include <limits>
+#include <memory>
+#include <mutex>
 #include <set>
 #include <vector>
 
@@ -60,6 +62,24 @@ struct Random {
 inline double next_up(double a) { return std::nextafter(a, std::numeric_limits<double>::infinity()); }
 inline double upper_bound_of(double a) { return next_up(a); }                // bin_mapper.rs:22-25
 inline bool check_equal_ordered(double a, double b) { return b <= next_up(a); }  // :27-30
+
+// Every column of a dataset draws the same sample (same row count, sample size and seed:
+// create_sample_indices, bin_mapper.rs:92-95), so the indices of the last (n, k, seed) are
+// kept and shared by the columns instead of being drawn again for each one.
+std::shared_ptr<const std::vector<int32_t>> sample_indices(int32_t n, int32_t k, int32_t seed) {
+  static std::mutex mu;
+  static int32_t key_n = -1, key_k = -1, key_seed = 0;
+  static std::shared_ptr<const std::vector<int32_t>> cached;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cached || key_n != n || key_k != k || key_seed != seed) {
+    Random rnd(seed);
+    cached = std::make_shared<const std::vector<int32_t>>(rnd.sample(n, k));
+    key_n = n;
+    key_k = k;
+    key_seed = seed;
+  }
+  return cached;
+}
 
 // greedy_find_bin (bin_mapper.rs:711-790)
 std::vector<double> greedy_find_bin(const double* dv, const int32_t* cnt, int32_t nd,
@@ -447,8 +467,8 @@ BinMapperHost find_bin_from_column(const double* column, int64_t n, int32_t max_
                                    bool categorical) {
   const int32_t total = (int32_t)n;
   const int32_t k = total < bin_construct_sample_cnt ? total : bin_construct_sample_cnt;
-  Random rnd(data_random_seed);
-  std::vector<int32_t> idx = rnd.sample(total, k);
+  const std::shared_ptr<const std::vector<int32_t>> ip = sample_indices(total, k, data_random_seed);
+  const std::vector<int32_t>& idx = *ip;
   std::vector<double> sampled(idx.size());
   for (size_t i = 0; i < idx.size(); ++i) sampled[i] = column[idx[i]];
   const int64_t total_sample_cnt = (int64_t)sampled.size();
