@@ -240,6 +240,19 @@ int lgbm_b200_bin_column_categorical(const double* column, int64_t n,
                                      lgbm_b200_bin_mapper* mapper_out, int32_t* bin_to_category,
                                      int32_t cap, uint32_t* bins_out);
 
+/* BinMapper::find_bin_from_column of many numerical columns at once, on the device
+ * (crates/lgbm-dataset/src/bin_mapper.rs:642-675 with find_bin_numeric :201-415): every
+ * column's sample (the same rows for every column: create_sample_indices, :92-95) is
+ * gathered on the host, then sorted and binned on the device; the mappers and bounds
+ * equal lgbm_b200_bin_column's. columns: feature-major host arrays of n f32
+ * (value_width 4) or f64 (8) values. mappers_out[f] and upper_bounds[f * upper_cap ...]
+ * (num_bin values; upper_cap >= max_bin + 2) receive the results. Categorical columns
+ * go through lgbm_b200_bin_column_categorical. */
+int lgbm_b200_find_bins(int32_t device, const void* const* columns, int32_t value_width,
+                        int64_t n, int32_t num_features, const lgbm_b200_bin_config* cfg,
+                        lgbm_b200_bin_mapper* mappers_out, double* upper_bounds,
+                        int32_t upper_cap);
+
 /* ------------------------------------------------------ per-op Backend mirror */
 
 /* Backend::construct_histograms (crates/lgbm-compute/src/lib.rs:1119-1126):

@@ -16,7 +16,7 @@ from . import model_text as MT
 from ._lib import LightGBMError
 from . import distributed  # noqa: E402
 
-__all__ = ["Dataset", "Booster", "Predictor", "train", "bin_column", "LightGBMError",
+__all__ = ["Dataset", "Booster", "Predictor", "train", "bin_column", "find_bins", "LightGBMError",
            "Learner", "distributed", "categorical_bitsets", "model_text"]
 
 # Reference config defaults (crates/lgbm-core/src/config/mod.rs:430-587).
@@ -128,6 +128,40 @@ def bin_column(values, max_bin=255, min_data_in_bin=3, min_data_in_leaf=20, pre_
     return mapper, bins
 
 
+def find_bins(columns, max_bin=255, min_data_in_bin=3, min_data_in_leaf=20, pre_filter=False,
+              use_missing=True, zero_as_missing=False, bin_construct_sample_cnt=200000,
+              data_random_seed=1, device=0):
+    """BinMapper::find_bin_from_column of numerical columns on the device: the mappers
+    bin_column would return (bin_mapper.rs:642-675), for every row of `columns`
+    (feature-major [F, n], f32 or f64). Needs a CUDA device."""
+    if isinstance(columns, np.ndarray) and columns.ndim == 2:
+        columns = list(columns)
+    dt = np.float32 if all(np.asarray(c).dtype == np.float32 for c in columns) else np.float64
+    cols = [np.ascontiguousarray(c, dtype=dt) for c in columns]
+    F = len(cols)
+    n = len(cols[0]) if F else 0
+    if any(len(c) != n for c in cols):
+        raise LightGBMError(C.INVALID_ARGUMENT, "columns differ in length")
+    cfg = C.BinConfig(int(max_bin), int(min_data_in_bin), int(min_data_in_leaf),
+                      int(bool(pre_filter)), int(bool(use_missing)), int(bool(zero_as_missing)),
+                      int(bin_construct_sample_cnt), int(data_random_seed))
+    cap = int(max_bin) + 2
+    ptrs = (ctypes.c_void_p * max(F, 1))(*[c.ctypes.data for c in cols])
+    ms = (C.BinMapperC * max(F, 1))()
+    upper = np.zeros((max(F, 1), cap), dtype=np.float64)
+    C.check(C.lib().lgbm_b200_find_bins(int(device), ptrs, np.dtype(dt).itemsize, n, F,
+                                        ctypes.byref(cfg), ms, C.ptr(upper), cap))
+    out = []
+    for f in range(F):
+        m = ms[f]
+        out.append({"num_bin": m.num_bin, "missing_type": m.missing_type,
+                    "default_bin": m.default_bin, "most_freq_bin": m.most_freq_bin,
+                    "is_trivial": bool(m.is_trivial), "min_val": m.min_val,
+                    "max_val": m.max_val, "sparse_rate": m.sparse_rate, "bin_type": 0,
+                    "upper": upper[f, : m.num_bin].copy()})
+    return out
+
+
 class Dataset:
     """Binned training data resident on one GPU (lightgbm_rs.Dataset for this path).
 
@@ -176,15 +210,26 @@ class Dataset:
                     data_random_seed=p["data_random_seed"])
 
     def _find_mappers(self):
-        """BinMapper::find_bin_from_column of every column (its sample only)."""
+        """BinMapper::find_bin_from_column of every column (its sample only): numerical
+        columns on the device when one is present (find_bins), categorical ones on the
+        host."""
         import concurrent.futures as cf
         import os
 
         kw = self._bin_kwargs()
+        maps = [None] * self.num_features
+        numeric = [j for j in range(self.num_features) if j not in self._cats]
+        if numeric and self.params.get("device_binning", True) and C.device_count() > 0:
+            found = find_bins([self._values[j] for j in numeric],
+                              device=int(self.params.get("device", 0)), **kw)
+            for j, m in zip(numeric, found):
+                maps[j] = m
 
         def one(j):
-            m, _ = bin_column(self._values[j], want_bins=False, categorical=j in self._cats,
-                              **kw)
+            m = maps[j]
+            if m is None:
+                m, _ = bin_column(self._values[j], want_bins=False,
+                                  categorical=j in self._cats, **kw)
             return _excluded(m) if m["is_trivial"] else m
 
         with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4)) as ex:

@@ -114,6 +114,7 @@ _SIGS = {
     "lgbm_b200_release_cached_memory": ([_i32, _P], ctypes.c_int),
     "lgbm_b200_bin_column": ([_P, _i64, _P, _P, _P, _i32, _P], ctypes.c_int),
     "lgbm_b200_bin_column_categorical": ([_P, _i64, _P, _P, _P, _i32, _P], ctypes.c_int),
+    "lgbm_b200_find_bins": ([_i32, _P, _i32, _i64, _i32, _P, _P, _P, _i32], ctypes.c_int),
     "lgbm_b200_construct_histograms": ([_P, _P, _P, _i64, _u32, _P], ctypes.c_int),
     "lgbm_b200_find_best_split": ([_P, _P, _u32, _i32, _u32, _u32, _i32, _i32, _i32, _f64, _f64,
                                    _i32, _P], ctypes.c_int),

@@ -240,7 +240,8 @@ namespace {
 void distinct_with_zero(std::vector<double>& values, int32_t zero_cnt, std::vector<double>* dv,
                         std::vector<int32_t>* counts) {
   const size_t ns = values.size();
-  std::sort(values.begin(), values.end());
+  // stable, as the reference's sort_by (bin_mapper.rs:250): -0.0 and 0.0 keep input order
+  std::stable_sort(values.begin(), values.end());
   if (ns == 0 || (values[0] > 0.0 && zero_cnt > 0)) {
     dv->push_back(0.0);
     counts->push_back(zero_cnt);
@@ -457,6 +458,11 @@ BinMapperHost find_bin_categorical(std::vector<double> values, int32_t max_bin,
   }
   m.is_trivial = trivial;
   return m;
+}
+
+std::shared_ptr<const std::vector<int32_t>> shared_sample_indices(int32_t n, int32_t k,
+                                                                  int32_t seed) {
+  return sample_indices(n, k, seed);
 }
 
 // find_bin_from_column (bin_mapper.rs:642-675)

@@ -2,6 +2,7 @@
 
 #include <cstdint>
 #include <map>
+#include <memory>
 #include <vector>
 
 namespace lgbm_b200 {
@@ -30,6 +31,11 @@ BinMapperHost find_bin_categorical(std::vector<double> values, int32_t max_bin,
                                    int32_t min_data_in_bin, int32_t min_split_data,
                                    bool pre_filter, bool use_missing, bool zero_as_missing,
                                    int64_t total_sample_cnt);
+
+// The bin-construction sample of a column of n rows (create_sample_indices,
+// bin_mapper.rs:92-95): ascending row indices, shared by every column of that size.
+std::shared_ptr<const std::vector<int32_t>> shared_sample_indices(int32_t n, int32_t k,
+                                                                  int32_t seed);
 
 BinMapperHost find_bin_from_column(const double* column, int64_t n, int32_t max_bin,
                                    int32_t min_data_in_bin, int32_t min_data_in_leaf,

@@ -998,6 +998,133 @@ int lgbm_b200_bin_column(const double* column, int64_t n, const lgbm_b200_bin_co
   return LGBM_B200_OK;
 }
 
+int lgbm_b200_find_bins(int32_t device, const void* const* columns, int32_t value_width,
+                        int64_t n, int32_t num_features, const lgbm_b200_bin_config* cfg,
+                        lgbm_b200_bin_mapper* mappers_out, double* upper_bounds,
+                        int32_t upper_cap) {
+  if (!columns || !cfg || !mappers_out || !upper_bounds || num_features < 0 || n <= 0)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "find_bins: argument");
+  if (value_width != 4 && value_width != 8)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "find_bins: value_width %d is not 4 or 8",
+                value_width);
+  if (n > (int64_t)INT32_MAX) return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "n > 2^31 - 1");
+  if (cfg->max_bin < 2 || cfg->max_bin > 4096)
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "find_bins: max_bin %d outside 2..4096",
+                cfg->max_bin);
+  if (upper_cap < cfg->max_bin + 2)
+    return fail(LGBM_B200_LENGTH_MISMATCH, "find_bins: upper_cap %d < max_bin + 2", upper_cap);
+  for (int f = 0; f < num_features; ++f)
+    if (!columns[f]) return fail(LGBM_B200_INVALID_ARGUMENT, "find_bins: column %d is null", f);
+  if (num_features == 0) return LGBM_B200_OK;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    cudaGetLastError();
+    return fail(LGBM_B200_CAPABILITY_UNAVAILABLE, "no CUDA device");
+  }
+  if (device < 0 || device >= ndev)
+    return fail(LGBM_B200_INVALID_ARGUMENT, "device %d not present", device);
+  DeviceGuard guard(device);
+  // the sample every column shares (create_sample_indices, bin_mapper.rs:92-95)
+  const int32_t total = (int32_t)n;
+  const int32_t ks = total < cfg->bin_construct_sample_cnt ? total : cfg->bin_construct_sample_cnt;
+  const std::shared_ptr<const std::vector<int32_t>> ip =
+      shared_sample_indices(total, ks, cfg->data_random_seed);
+  const std::vector<int32_t>& idx = *ip;
+  const int64_t k = (int64_t)idx.size();
+  if (k == 0) return fail(LGBM_B200_RUNTIME, "find_bins: empty sample");
+  // scaled_filter_cnt (bin_mapper.rs:684-689)
+  const int32_t filter_cnt = (int32_t)(((int64_t)cfg->min_data_in_leaf * k) / (int64_t)total);
+  const int32_t mb = cfg->max_bin, cap = upper_cap;
+  // features per batch: about 2 GB of device scratch
+  const size_t per_feature = (size_t)k * 45 + (size_t)(4 * mb + 16 + 2 * cap) * 8;
+  const int32_t batch =
+      (int32_t)std::max<size_t>(1, std::min<size_t>(num_features, (2ull << 30) / per_feature));
+  DevBuf<double> vals_a, vals_b, dv, edges, side, upper, meta_f;
+  DevBuf<unsigned long long> keys_a, keys_b;
+  DevBuf<int32_t> which, na, cnt, cib, meta;
+  DevBuf<uint8_t> big;
+  const size_t B = (size_t)batch, K = (size_t)k;
+  CUDA_TRY(vals_a.alloc(B * K));
+  CUDA_TRY(vals_b.alloc(B * K));
+  CUDA_TRY(keys_a.alloc(B * K));
+  CUDA_TRY(keys_b.alloc(B * K));
+  CUDA_TRY(dv.alloc(B * (K + 2)));
+  CUDA_TRY(cnt.alloc(B * (K + 2)));
+  CUDA_TRY(big.alloc(B * (K + 2)));
+  CUDA_TRY(edges.alloc(B * 2 * mb));
+  CUDA_TRY(side.alloc(B * (mb + 1)));
+  CUDA_TRY(cib.alloc(B * cap));
+  CUDA_TRY(upper.alloc(B * cap));
+  CUDA_TRY(meta.alloc(B * 6));
+  CUDA_TRY(meta_f.alloc(B * 3));
+  CUDA_TRY(which.alloc(B));
+  CUDA_TRY(na.alloc(B));
+  std::vector<double> host_vals(B * K);
+  std::vector<int32_t> h_meta(B * 6);
+  std::vector<double> h_metaf(B * 3);
+  for (int32_t f0 = 0; f0 < num_features; f0 += batch) {
+    const int32_t nb = std::min(batch, num_features - f0);
+    // gather the sampled rows of each column (ascending indices: a forward sweep)
+    for (int32_t j = 0; j < nb; ++j) {
+      double* dst = host_vals.data() + (size_t)j * K;
+      if (value_width == 4) {
+        const float* col = static_cast<const float*>(columns[f0 + j]);
+        for (int64_t i = 0; i < k; ++i) dst[i] = (double)col[idx[i]];
+      } else {
+        const double* col = static_cast<const double*>(columns[f0 + j]);
+        for (int64_t i = 0; i < k; ++i) dst[i] = col[idx[i]];
+      }
+    }
+    CUDA_TRY(cudaMemcpy(vals_a.p, host_vals.data(), (size_t)nb * K * 8, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemset(na.p, 0, (size_t)nb * 4));
+    FindBinsDev d{};
+    d.vals_a = vals_a.p;
+    d.vals_b = vals_b.p;
+    d.keys_a = keys_a.p;
+    d.keys_b = keys_b.p;
+    d.which = which.p;
+    d.na_cnt = na.p;
+    d.k = k;
+    d.nf = nb;
+    d.max_bin = mb;
+    d.min_data_in_bin = cfg->min_data_in_bin;
+    d.filter_cnt = filter_cnt;
+    d.pre_filter = cfg->pre_filter ? 1 : 0;
+    d.use_missing = cfg->use_missing ? 1 : 0;
+    d.zero_as_missing = cfg->zero_as_missing ? 1 : 0;
+    d.cap = cap;
+    d.dv = dv.p;
+    d.cnt = cnt.p;
+    d.big = big.p;
+    d.edges = edges.p;
+    d.side = side.p;
+    d.cnt_in_bin = cib.p;
+    d.upper = upper.p;
+    d.meta = meta.p;
+    d.meta_f = meta_f.p;
+    launch_find_bins(d, 0);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(h_meta.data(), meta.p, (size_t)nb * 6 * 4, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(h_metaf.data(), meta_f.p, (size_t)nb * 3 * 8, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(upper_bounds + (size_t)f0 * cap, upper.p, (size_t)nb * cap * 8,
+                        cudaMemcpyDeviceToHost));
+    for (int32_t j = 0; j < nb; ++j) {
+      lgbm_b200_bin_mapper& m = mappers_out[f0 + j];
+      m.num_bin = h_meta[j * 6 + 0];
+      m.missing_type = h_meta[j * 6 + 1];
+      m.default_bin = h_meta[j * 6 + 2];
+      m.most_freq_bin = h_meta[j * 6 + 3];
+      m.is_trivial = h_meta[j * 6 + 4];
+      m._reserved = 0;  // numerical
+      m.min_val = h_metaf[j * 3 + 0];
+      m.max_val = h_metaf[j * 3 + 1];
+      m.sparse_rate = h_metaf[j * 3 + 2];
+    }
+  }
+  return LGBM_B200_OK;
+}
+
 int lgbm_b200_bin_column_categorical(const double* column, int64_t n,
                                      const lgbm_b200_bin_config* cfg,
                                      lgbm_b200_bin_mapper* mapper_out, int32_t* bin_to_category,

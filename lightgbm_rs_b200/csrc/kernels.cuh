@@ -327,6 +327,36 @@ struct BinRowsDev {
 };
 enum BinRowsKind { kBinRowsU8 = 1, kBinRowsU16 = 2, kBinRowsU32 = 4, kBinRowsF32 = 5,
                    kBinRowsF64 = 8 };
+
+// Bin finding of a batch of numerical features on the device (find_bin.cu): the sampled
+// values in, each feature's mapper fields and bin upper bounds out.
+struct FindBinsDev {
+  double* vals_a;                 // [nf][k] sampled values (sorted in place, or into b)
+  double* vals_b;                 // [nf][k]
+  unsigned long long* keys_a;     // [nf][k]
+  unsigned long long* keys_b;     // [nf][k]
+  int32_t* which;                 // [nf]
+  int32_t* na_cnt;                // [nf] (zeroed by the caller)
+  int64_t k;
+  int32_t nf;
+  int32_t max_bin;
+  int32_t min_data_in_bin;
+  int32_t filter_cnt;
+  int32_t pre_filter;
+  int32_t use_missing;
+  int32_t zero_as_missing;
+  int32_t cap;                    // >= max_bin + 2
+  double* dv;                     // [nf][k + 2]
+  int32_t* cnt;                   // [nf][k + 2]
+  uint8_t* big;                   // [nf][k + 2]
+  double* edges;                  // [nf][2][max_bin]
+  double* side;                   // [nf][max_bin + 1]
+  int32_t* cnt_in_bin;            // [nf][cap]
+  double* upper;                  // [nf][cap]
+  int32_t* meta;                  // [nf][6]
+  double* meta_f;                 // [nf][3]
+};
+void launch_find_bins(const FindBinsDev& d, cudaStream_t st);
 void launch_bin_rows(const BinRowsDev& d, int kind, const void* cols, int64_t col_stride,
                      int64_t n, int64_t row0, uint8_t* out, cudaStream_t st);
 
