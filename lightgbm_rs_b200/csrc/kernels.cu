@@ -2235,6 +2235,21 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     if (fb + (int)blockIdx.x < fe) cs.ft0 = d.feat[fb + blockIdx.x];
   }
   __syncthreads();
+  if (PEER && d.sliced) {
+    // With feature slices the owners of all features sum every rank's buffers, so this
+    // rank clears every cell of its next accumulator and of the look-ahead slot it
+    // releases (fixscan_feature clears only its slice's): the CTAs share the cells. Both
+    // were last read at the previous step, which every rank has finished.
+    const Prep& P = cs.prep;
+    const int64_t rl = d.raw_len;
+    const int64_t per = (rl + gridDim.x - 1) / gridDim.x;
+    const int64_t lo = per * blockIdx.x, hi = min(rl, lo + per);
+    long long* la = P.la_clear >= 0 ? d.la_raw + (size_t)P.la_clear * (rl + 2) : nullptr;
+    for (int64_t i = lo + tid; i < hi; i += CT) {
+      d.raw[i] = 0;
+      if (la) la[i] = 0;
+    }
+  }
   for (int f = fb + blockIdx.x; f < fe; f += gridDim.x) {
     // the CTA's first feature was read while the pending split was applied
     const DevFeature ft = f == fb + (int)blockIdx.x ? cs.ft0 : d.feat[f];
