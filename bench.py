@@ -535,6 +535,7 @@ def run_ours(args):
     # ---- per-kernel device spans of the pipelined step (same launch sequence, kernels
     # stamping %globaltimer at entry and exit), and the kernels' own work counters ----
     spans, pc = booster.profile_pipeline(5)
+    chain = booster.profile_chain()  # the last of those iterations, step by step
     kb = kernel_bytes(pc, local_rows, args.grad, data.features)
     peak, peak_kind = load_peaks()
     part_ms = spans["partition"] + pc["lookahead"]
@@ -677,7 +678,8 @@ def run_ours(args):
                      "rows_built_per_iter": pc["rows_built"],
                      "splits_per_iter": pc["splits"],
                      "lookahead_runs_per_iter": pc["lookahead_runs"],
-                     "lookahead_hits_per_iter": pc["lookahead_hits"]},
+                     "lookahead_hits_per_iter": pc["lookahead_hits"],
+                     "chain": chain},
         "kernel_span_ms_per_iter": spans,
         "cpu_baseline": cpu,
         "e2e": {"value": args.steps / e2e_s, "unit": "iters/s",

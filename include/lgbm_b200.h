@@ -437,6 +437,19 @@ int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
 int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
                                        double* span_ms_out, double* iter_ms_out,
                                        int64_t* counts_out);
+/* The raw spans of the last iteration lgbm_b200_booster_profile_pipeline ran: per slot
+ * (0: the root build; 1 + 4*s + kind for split step s, kind 0 control step, 1 main-stream
+ * partition, 2 look-ahead partition, 3 separate build) the earliest CTA entry and latest
+ * CTA exit in %globaltimer ns; a slot not launched holds start = UINT64_MAX. phase_out
+ * (optional, cap * 8 entries): for split step s, eight control-step phase marks at
+ * phase_out[8*s] (latest CTA time, 0 when not reached): pending split applied, feature
+ * cells loaded, FixHistogram and child stores done, scans done, every feature of the CTA
+ * done, pick inputs staged, pick made, control block written. *n_out receives the slot
+ * count; at most cap entries of each span array are written. No counterpart in the
+ * reference (a profiling aid). */
+int lgbm_b200_booster_profile_spans(const lgbm_b200_booster* b, int32_t cap,
+                                    uint64_t* start_out, uint64_t* end_out, uint64_t* phase_out,
+                                    int32_t* n_out);
 /* The launches timed by the last lgbm_b200_booster_profile_iteration, in launch order:
  * kernel class (the ms_out order of that call) and device ms of each timed span; *n_out
  * receives the count, at most cap entries are written. */

@@ -194,6 +194,9 @@ class Dataset:
             # feature-major raw values, binned on the device by construct()
             self._values = np.ascontiguousarray(X.T, dtype=dt)
             self.num_features, self.num_data = self._values.shape
+            # the binning settings the mappers were found with; the host view `bins`
+            # applies the same ones whatever train() later merges into params
+            self._bin_kw = self._bin_kwargs()
             self.mappers = self._find_mappers()
         else:
             self._bins = np.ascontiguousarray(bins)
@@ -216,7 +219,7 @@ class Dataset:
         import concurrent.futures as cf
         import os
 
-        kw = self._bin_kwargs()
+        kw = self._bin_kw
         maps = [None] * self.num_features
         numeric = [j for j in range(self.num_features) if j not in self._cats]
         if numeric and self.params.get("device_binning", True) and C.device_count() > 0:
@@ -240,7 +243,7 @@ class Dataset:
         """Feature-major bins [num_features, num_data]. For a dataset built from raw
         values these are computed on the host (value_to_bin per value) on first use."""
         if self._bins is None:
-            kw = self._bin_kwargs()
+            kw = self._bin_kw
             cols = []
             for j in range(self.num_features):
                 if self.mappers[j]["num_bin"] == 1:  # constant or left out: one bin
@@ -588,6 +591,79 @@ class Booster:
                  "splits": cnt[3] / n, "rows_parted": cnt[4] / n, "fused": bool(cnt[5]),
                  "lookahead_runs": cnt[6] / n, "lookahead_hits": cnt[7] / n})
 
+    # control-step phase marks (CtlPhase), each the latest CTA's time at that point
+    CONTROL_PHASES = ("prep", "loaded", "fixed", "scanned", "features", "staged", "picked",
+                      "written")
+
+    def profile_chain(self):
+        """What held the split chain in the last iteration profile_pipeline ran, from the
+        raw spans. Control step s + 1 starts after control step s, the main-stream
+        partition s and the look-ahead partition s - 1 have ended (graph edges). Over the
+        steps, the time from one control step's start to the next one's is split into the
+        control step's own span, the main partition's run past it, the look-ahead's run
+        past both, and the gap from the last of them to the next control step's first CTA
+        (launch and scheduling). ms summed over the steps of the tree; "lookahead_limited"
+        counts the steps whose look-ahead ended last. "control_phases": the control step's
+        span split at its phase marks (time to each mark from the previous one, summed)."""
+        n = C._i32(0)
+        C.check(C.lib().lgbm_b200_booster_profile_spans(self._handle, 0, None, None, None,
+                                                        ctypes.byref(n)))
+        st = np.zeros(n.value, dtype=np.uint64)
+        en = np.zeros(n.value, dtype=np.uint64)
+        ph = np.zeros((n.value, len(self.CONTROL_PHASES)), dtype=np.uint64)
+        C.check(C.lib().lgbm_b200_booster_profile_spans(self._handle, n.value, C.ptr(st),
+                                                        C.ptr(en), C.ptr(ph), ctypes.byref(n)))
+        none = np.iinfo(np.uint64).max
+
+        def span(k):
+            if k < 0 or k >= len(st) or st[k] == none or en[k] < st[k]:
+                return None
+            return int(st[k]), int(en[k])
+
+        out = {"control_step": 0.0, "main_partition_past": 0.0, "lookahead_past": 0.0,
+               "launch_gap": 0.0, "steps": 0, "lookahead_limited": 0, "main_limited": 0,
+               "before_first_step": 0.0, "tree": 0.0, "control_phases": {}}
+        steps = (len(st) - 1) // 4
+        first = span(1)
+        root = span(0)
+        if first and root:
+            out["before_first_step"] = (first[0] - root[0]) * 1e-6
+        for s in range(steps - 1):
+            ctl, nxt = span(1 + 4 * s), span(1 + 4 * (s + 1))
+            if ctl is None or nxt is None:
+                break
+            main = span(1 + 4 * s + 1)
+            la = span(1 + 4 * (s - 1) + 2) if s >= 1 else None
+            t = ctl[1]
+            out["control_step"] += (ctl[1] - ctl[0]) * 1e-6
+            if main and main[1] > t:
+                out["main_partition_past"] += (main[1] - t) * 1e-6
+                t = main[1]
+                lim = "main"
+            else:
+                lim = "control"
+            if la and la[1] > t:
+                out["lookahead_past"] += (la[1] - t) * 1e-6
+                t = la[1]
+                lim = "lookahead"
+            out["launch_gap"] += max(nxt[0] - t, 0) * 1e-6
+            out["lookahead_limited"] += lim == "lookahead"
+            out["main_limited"] += lim == "main"
+            out["steps"] += 1
+            # inside the control step: entry, the phase marks in order, exit
+            marks = [ctl[0]] + [int(v) for v in ph[s]] + [ctl[1]]
+            prev = marks[0]
+            for name, t_m in zip(self.CONTROL_PHASES + ("exit",), marks[1:]):
+                if t_m == 0:  # not reached (a scan-free step, or a CTA with no feature)
+                    continue
+                out["control_phases"][name] = out["control_phases"].get(name, 0.0) + \
+                    max(t_m - prev, 0) * 1e-6
+                prev = max(prev, t_m)
+        ends = [e[1] for e in map(span, range(len(st))) if e is not None]
+        if first and ends:
+            out["tree"] = (max(ends) - (root[0] if root else first[0])) * 1e-6
+        return out
+
     def profile_launches(self):
         """(kernel class name, device ms) of every span timed by the last
         profile_iteration, in launch order."""
@@ -624,8 +700,9 @@ def train(params, train_set, num_boost_round=100, comm=None):
               "num_round", "num_rounds", "num_boost_round", "n_estimators"):
         if k in p:
             num_boost_round = int(p.pop(k))
-    if isinstance(train_set, Dataset) and train_set.params != _resolve(p):
-        train_set.params.update(_resolve(p))
+    if isinstance(train_set, Dataset):
+        # the parameters given here reach the dataset; its own binning stays as found
+        train_set.params.update({_ALIASES.get(k, k): v for k, v in p.items()})
     b = Booster(p, train_set, comm=comm)
     b.update(int(num_boost_round))
     return b

@@ -144,6 +144,7 @@ _SIGS = {
     "lgbm_b200_booster_profile_iteration": ([_P, _P, _P], ctypes.c_int),
     "lgbm_b200_booster_profile_pipeline": ([_P, _i32, _P, _P, _P], ctypes.c_int),
     "lgbm_b200_booster_profile_launches": ([_P, _i32, _P, _P, _P], ctypes.c_int),
+    "lgbm_b200_booster_profile_spans": ([_P, _i32, _P, _P, _P, _P], ctypes.c_int),
     "lgbm_b200_comm_unique_id": ([_P], ctypes.c_int),
     "lgbm_b200_comm_create": ([_i32, _i32, _i32, _P, _P], ctypes.c_int),
     "lgbm_b200_comm_destroy": ([_P], ctypes.c_int),

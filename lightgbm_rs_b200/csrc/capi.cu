@@ -735,6 +735,9 @@ struct lgbm_b200_booster {
   float last_ms = 0.f;
   std::vector<std::pair<int32_t, float>> last_profile;  // (kernel class, ms) per launch
   DevBuf<unsigned long long> spans;  // [2][span_slots(L)] start | end (profile_pipeline)
+  std::vector<unsigned long long> span_last;  // the last profiled iteration's spans (host)
+  DevBuf<unsigned long long> phases;          // [L][kCtlPhases] control-step phase marks
+  std::vector<unsigned long long> phase_last;  // the last profiled iteration's marks (host)
   lgbm_b200_comm* comm = nullptr;  // data-parallel job (null: one device)
   const DeviceComm* dcomm() const { return comm ? &comm->dev : nullptr; }
 
@@ -2440,11 +2443,14 @@ int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
   const int L = b->learner->L;
   const int slots = span_slots(L);
   if (!b->spans.p) CUDA_TRY(b->spans.alloc(2 * (size_t)slots));
+  const size_t nph = (size_t)L * kCtlPhases;
+  if (!b->phases.p) CUDA_TRY(b->phases.alloc(nph));
   // a graph of the same launch sequence whose tree kernels stamp their spans
   cudaStream_t st = b->learner->stream;
   GrowDev d = b->learner->d;
   d.span_start = b->spans.p;
   d.span_end = b->spans.p + slots;
+  d.ctl_phase = b->phases.p;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
@@ -2461,7 +2467,7 @@ int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
   if (e != cudaSuccess)
     return fail(LGBM_B200_RUNTIME, "profile_pipeline: instantiate failed: %s",
                 cudaGetErrorString(e));
-  std::vector<unsigned long long> h(2 * (size_t)slots);
+  std::vector<unsigned long long> h(2 * (size_t)slots), hp(nph);
   double cls[KC_COUNT] = {0};
   double total_ms = 0.0;
   for (int k = 0; k < 8; ++k) counts_out[k] = 0;
@@ -2472,12 +2478,15 @@ int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
   for (int it = 0; it < iterations && e == cudaSuccess; ++it) {
     e = cudaMemsetAsync(b->spans.p, 0xff, slots * 8, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(b->spans.p + slots, 0, slots * 8, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(b->phases.p, 0, nph * 8, st);
     if (e == cudaSuccess) e = cudaEventRecord(e0, st);
     if (e == cudaSuccess) e = cudaGraphLaunch(exec, st);
     if (e == cudaSuccess) e = cudaEventRecord(e1, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e == cudaSuccess)
       e = cudaMemcpy(h.data(), b->spans.p, h.size() * 8, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(hp.data(), b->phases.p, nph * 8, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) break;
     GrowCtrl gc;
     e = cudaMemcpy(&gc, b->learner->ctrl.p, sizeof(GrowCtrl), cudaMemcpyDeviceToHost);
@@ -2518,10 +2527,29 @@ int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
   for (int k = 0; k < KC_COUNT; ++k) span_ms_out[k] = cls[k] / iterations;
   iter_ms_out[0] = total_ms / iterations;
   iter_ms_out[1] /= iterations;
+  b->span_last = h;
+  b->phase_last = hp;
   GrowCtrl c;
   CUDA_TRY(cudaMemcpy(&c, b->learner->ctrl.p, sizeof(GrowCtrl), cudaMemcpyDeviceToHost));
   if (c.error)
     return fail(LGBM_B200_RUNTIME, "tree grower reported device error bits 0x%x", c.error);
+  return LGBM_B200_OK;
+}
+
+int lgbm_b200_booster_profile_spans(const lgbm_b200_booster* b, int32_t cap,
+                                    uint64_t* start_out, uint64_t* end_out, uint64_t* phase_out,
+                                    int32_t* n_out) {
+  if (!b || !n_out || cap < 0 || (cap > 0 && (!start_out || !end_out)))
+    return fail(LGBM_B200_INVALID_ARGUMENT, "profile_spans: arguments");
+  const int32_t slots = (int32_t)(b->span_last.size() / 2);
+  *n_out = slots;
+  for (int32_t k = 0; k < slots && k < cap; ++k) {
+    start_out[k] = b->span_last[k];
+    end_out[k] = b->span_last[(size_t)slots + k];
+  }
+  if (phase_out)  // step s of slot 1 + 4 s: kCtlPhases marks at phase_out[s * kCtlPhases]
+    for (size_t k = 0; k < b->phase_last.size() && k < (size_t)cap * kCtlPhases; ++k)
+      phase_out[k] = b->phase_last[k];
   return LGBM_B200_OK;
 }
 

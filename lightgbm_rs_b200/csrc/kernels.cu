@@ -114,6 +114,11 @@ struct SpanStamp {
   }
 };
 
+// Phase mark p of control step s (thread 0 of the calling CTA; nothing when off).
+__device__ __forceinline__ void ctl_mark(const GrowDev& d, int s, int p) {
+  if (d.ctl_phase && threadIdx.x == 0) atomicMax(d.ctl_phase + (size_t)s * kCtlPhases + p, global_ns());
+}
+
 // Sum over the ranks of word `off` of each rank's buffer (integers: exact in any order).
 // The ranks' buffer pointers are read first and every rank's load is issued before any
 // is added, so one round trip over the peer links covers all ranks.
@@ -1984,7 +1989,7 @@ struct FixScanSmem {
 // children.
 template <bool CAT, bool PEER, int CT>
 __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const DevFeature& ft,
-                                FixScanSmem& sm) {
+                                FixScanSmem& sm, int s) {
   static_assert(CT == 1024 || (CT == 256 && !CAT), "control-step CTA sizes");
   const int tid = threadIdx.x;
   const int nb = ft.num_bin;
@@ -2063,6 +2068,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
         sm.hist[0][tid] = v;
       }
       __syncthreads();
+      ctl_mark(d, s, CP_LOADED);
       // FixHistogram (fix_histogram.rs:50-81): the most-frequent-bin cell becomes the leaf
       // sum minus the other cells, subtracted in ascending order. With quantized
       // gradients every cell is an exact multiple of one unit u. When every partial
@@ -2153,6 +2159,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
         }
       }
       __syncthreads();
+      ctl_mark(d, s, CP_FIXED);
       const int grp = tid / (CT / 4);  // (leaf, direction) group
       const int sel = grp >> 1;
       const bool fwd = (grp & 1) != 0;
@@ -2170,6 +2177,7 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
         }
       }
       __syncthreads();
+      ctl_mark(d, s, CP_SCANNED);
       if (tid == 0 || tid == 32) {
         const int sl_i = tid == 0 ? 0 : 1;
         const int32_t leaf2 = sl_i == 0 ? S : Lg;
@@ -2235,6 +2243,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     if (fb + (int)blockIdx.x < fe) cs.ft0 = d.feat[fb + blockIdx.x];
   }
   __syncthreads();
+  ctl_mark(d, s, CP_PREP);
   if (PEER && d.sliced) {
     // With feature slices the owners of all features sum every rank's buffers, so this
     // rank clears every cell of its next accumulator and of the look-ahead slot it
@@ -2253,9 +2262,10 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   for (int f = fb + blockIdx.x; f < fe; f += gridDim.x) {
     // the CTA's first feature was read while the pending split was applied
     const DevFeature ft = f == fb + (int)blockIdx.x ? cs.ft0 : d.feat[f];
-    fixscan_feature<CAT, PEER, CT>(d, cs.prep, f, ft, sm);
+    fixscan_feature<CAT, PEER, CT>(d, cs.prep, f, ft, sm, s);
     __syncthreads();
   }
+  ctl_mark(d, s, CP_FEATURES);
   // Arrival: the barrier orders every thread's writes before thread 0's release, and the
   // CTA that arrives last acquires all of them (acq_rel add) before its barrier.
   __syncthreads();
@@ -2309,6 +2319,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   }
   if (warp == 1 && (tid & 31) == 0) prep_commit<CAT>(d, P);
   __syncthreads();
+  ctl_mark(d, s, CP_STAGED);
   if (warp == 0 && !P.c.done) {
     if (staged)
       pick_warp<CAT, true>(d, P, cs, so, sc, cs.pick);
@@ -2316,6 +2327,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
       pick_warp<CAT, false>(d, P, cs, d.scan_out, d.scan_cat, cs.pick);
   }
   __syncthreads();
+  ctl_mark(d, s, CP_PICKED);
   // The next step reads the chosen leaf's integer and f64 histogram rows, which the
   // partitions' streaming has usually pushed out of L2 since the leaf was scanned: bring
   // them back now, one bulk prefetch per 16 KB.
@@ -2393,6 +2405,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     }
     *d.ctrl = c;
   }
+  ctl_mark(d, s, CP_WRITTEN);
 }
 
 template <bool CAT, bool PEER, int CT>

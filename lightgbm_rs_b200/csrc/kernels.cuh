@@ -166,6 +166,9 @@ struct GrowDev {
   unsigned long long* span_start;
   unsigned long long* span_end;
   int32_t span_slot;
+  // Control-step phases (null: off): ctl_phase[s * kCtlPhases + p] is raised to the
+  // latest CTA's %globaltimer at phase p of split step s (CtlPhase).
+  unsigned long long* ctl_phase;
   // Feature slices of a data-parallel job over peer memory (sliced = 1): this rank's
   // control step decodes and scans features [slice_begin, slice_end) only, then the ranks
   // exchange their slices' best split of each scanned leaf (XPick records, pushed into
@@ -195,6 +198,16 @@ enum SpanKind { SPAN_FIXSCAN = 0, SPAN_PARTITION = 1, SPAN_LOOKAHEAD = 2, SPAN_B
 constexpr int kSpanRootBuild = 0;
 __host__ __device__ inline int span_slot_of(int s, int kind) { return 1 + 4 * s + kind; }
 inline int span_slots(int L) { return 1 + 4 * (L > 1 ? L - 1 : 1); }
+
+// Phase marks of one control step: the pending split applied (every CTA), the feature's
+// cells loaded and decoded, FixHistogram / compaction / child stores done, the scans done,
+// every feature of the CTA done; then, in the last CTA only, the pick's inputs staged, the
+// pick made, and the control block written.
+enum CtlPhase {
+  CP_PREP = 0, CP_LOADED = 1, CP_FIXED = 2, CP_SCANNED = 3, CP_FEATURES = 4, CP_STAGED = 5,
+  CP_PICKED = 6, CP_WRITTEN = 7
+};
+constexpr int kCtlPhases = 8;
 
 // Optional per-kernel timing of a launch sequence: events recorded around each kernel.
 enum KernelClass { KC_PREPARE = 0, KC_BUILD = 1, KC_FIXSCAN = 2, KC_PARTITION = 3, KC_INIT = 4,

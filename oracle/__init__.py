@@ -306,6 +306,14 @@ def grow_tree(bins_cols, metas, g, h, num_leaves, max_depth=-1, nthreads=1, **ga
     """Grow one tree. bins_cols: 2-D array [num_features, num_data] (u8/u16/u32)."""
     bins_cols = np.ascontiguousarray(bins_cols)
     F, N = bins_cols.shape
+    if F != len(metas):
+        raise ValueError(f"{F} bin columns but {len(metas)} feature metas")
+    if N:
+        top = bins_cols.max(axis=1)
+        for f in range(F):  # a bin past num_bin would index past the feature's histogram
+            if int(top[f]) >= max(int(metas[f]["num_bin"]), 1):
+                raise ValueError(f"feature {f}: bin {int(top[f])} >= num_bin "
+                                 f"{int(metas[f]['num_bin'])}")
     width = bins_cols.dtype.itemsize
     col_ptrs = (ctypes.c_void_p * F)(*[bins_cols[f].ctypes.data for f in range(F)])
     g = np.ascontiguousarray(g, dtype=np.float32)
