@@ -600,11 +600,15 @@ class Booster:
         raw spans. Control step s + 1 starts after control step s, the main-stream
         partition s and the look-ahead partition s - 1 have ended (graph edges). Over the
         steps, the time from one control step's start to the next one's is split into the
-        control step's own span, the main partition's run past it, the look-ahead's run
-        past both, and the gap from the last of them to the next control step's first CTA
-        (launch and scheduling). ms summed over the steps of the tree; "lookahead_limited"
-        counts the steps whose look-ahead ended last. "control_phases": the control step's
-        span split at its phase marks (time to each mark from the previous one, summed)."""
+        control step's own span, the main partition's run past it, the separate build's
+        run past that (no fused partition), the look-ahead's run past all of them, and the
+        gap from the last of them to the next control step's first CTA (launch and
+        scheduling). ms summed over the steps of the tree; "lookahead_limited" counts the
+        steps whose look-ahead ended last. "control_phases": the control step's span split
+        at its phase marks (time to each mark from the previous one, summed). "main_noop" /
+        "main_run": the main partitions shorter / longer than 8 us (it found its leaf
+        partitioned by the look-ahead, or ran), with their mean delay after the control
+        step and mean span in us."""
         n = C._i32(0)
         C.check(C.lib().lgbm_b200_booster_profile_spans(self._handle, 0, None, None, None,
                                                         ctypes.byref(n)))
@@ -620,9 +624,12 @@ class Booster:
                 return None
             return int(st[k]), int(en[k])
 
-        out = {"control_step": 0.0, "main_partition_past": 0.0, "lookahead_past": 0.0,
+        out = {"control_step": 0.0, "main_partition_past": 0.0, "build_past": 0.0,
+               "lookahead_past": 0.0,
                "launch_gap": 0.0, "steps": 0, "lookahead_limited": 0, "main_limited": 0,
-               "before_first_step": 0.0, "tree": 0.0, "control_phases": {}}
+               "before_first_step": 0.0, "tree": 0.0, "control_phases": {},
+               "main_noop": {"n": 0, "launch_after_control_us": 0.0, "span_us": 0.0},
+               "main_run": {"n": 0, "launch_after_control_us": 0.0, "span_us": 0.0}}
         steps = (len(st) - 1) // 4
         first = span(1)
         root = span(0)
@@ -633,15 +640,19 @@ class Booster:
             if ctl is None or nxt is None:
                 break
             main = span(1 + 4 * s + 1)
+            build = span(1 + 4 * s + 3)  # the separate build (no fused partition)
             la = span(1 + 4 * (s - 1) + 2) if s >= 1 else None
             t = ctl[1]
             out["control_step"] += (ctl[1] - ctl[0]) * 1e-6
+            lim = "control"
             if main and main[1] > t:
                 out["main_partition_past"] += (main[1] - t) * 1e-6
                 t = main[1]
                 lim = "main"
-            else:
-                lim = "control"
+            if build and build[1] > t:
+                out["build_past"] += (build[1] - t) * 1e-6
+                t = build[1]
+                lim = "build"
             if la and la[1] > t:
                 out["lookahead_past"] += (la[1] - t) * 1e-6
                 t = la[1]
@@ -650,6 +661,12 @@ class Booster:
             out["lookahead_limited"] += lim == "lookahead"
             out["main_limited"] += lim == "main"
             out["steps"] += 1
+            if main:  # a main partition that found its leaf done is short: a no-op
+                kind = "noop" if main[1] - main[0] < 8000 else "run"
+                m = out["main_" + kind]
+                m["n"] += 1
+                m["launch_after_control_us"] += (main[0] - ctl[1]) * 1e-3
+                m["span_us"] += (main[1] - main[0]) * 1e-3
             # inside the control step: entry, the phase marks in order, exit
             marks = [ctl[0]] + [int(v) for v in ph[s]] + [ctl[1]]
             prev = marks[0]
@@ -659,6 +676,11 @@ class Booster:
                 out["control_phases"][name] = out["control_phases"].get(name, 0.0) + \
                     max(t_m - prev, 0) * 1e-6
                 prev = max(prev, t_m)
+        for kind in ("main_noop", "main_run"):  # means per launch
+            m = out[kind]
+            if m["n"]:
+                m["launch_after_control_us"] /= m["n"]
+                m["span_us"] /= m["n"]
         ends = [e[1] for e in map(span, range(len(st))) if e is not None]
         if first and ends:
             out["tree"] = (max(ends) - (root[0] if root else first[0])) * 1e-6

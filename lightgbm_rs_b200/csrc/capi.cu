@@ -441,7 +441,14 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   slot_len = 2 * ds->total_bins;
   const int64_t N = ds->num_data;
   max_tiles = (int32_t)((N + 2047) / 2048) + 1;
-  CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  // The main stream at the highest priority and the look-ahead stream at the lowest: when
+  // both have CTAs waiting for an SM, the main-stream partition of the pick goes first
+  // (graphs keep each kernel's capture-stream priority: cudaGraphInstantiateFlagUseNodePriority).
+  int prio_lo = 0, prio_hi = 0;
+  CUDA_TRY(cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi));
+  if (const char* e = std::getenv("LGBM_B200_STREAM_PRIORITY"))
+    if (e[0] == '0') prio_lo = prio_hi = 0;
+  CUDA_TRY(cudaStreamCreateWithPriority(&stream, cudaStreamNonBlocking, prio_hi));
   CUDA_TRY(ctrl.alloc(1));
   CUDA_TRY(cudaMemset(ctrl.p, 0, sizeof(GrowCtrl)));
   CUDA_TRY(leaf_i32.alloc((size_t)7 * L));
@@ -471,12 +478,17 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   CUDA_TRY(la_raw.alloc(kLaSlots * ((size_t)slot_len + 2)));
   CUDA_TRY(la_partials.alloc((size_t)kLaSlots * kPrivateTiles * slot_len));
   CUDA_TRY(la_status.alloc(max_tiles));
-  CUDA_TRY(cudaStreamCreateWithFlags(&las.st, cudaStreamNonBlocking));
+  CUDA_TRY(cudaStreamCreateWithPriority(&las.st, cudaStreamNonBlocking, prio_lo));
   CUDA_TRY(cudaEventCreateWithFlags(&las.fork, cudaEventDisableTiming));
   for (cudaEvent_t& e : las.done) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   {
     const int sms = sm_count(device);
     las.blocks = std::max(sms / 2, sms - std::min(ds->num_features, sms));
+    las.main_blocks = sms;
+    // launch-shape overrides (tuning): look-ahead and main-partition CTAs
+    if (const char* e = std::getenv("LGBM_B200_LA_BLOCKS")) las.blocks = std::max(1, std::atoi(e));
+    if (const char* e = std::getenv("LGBM_B200_MAIN_BLOCKS"))
+      las.main_blocks = std::max(1, std::atoi(e));
   }
   if (const char* e = std::getenv("LGBM_B200_LOOKAHEAD")) la_enabled = std::strcmp(e, "0") != 0;
   d = GrowDev{};
@@ -2310,7 +2322,8 @@ int lgbm_b200_booster_train(lgbm_b200_booster* b, int32_t num_iterations, int32_
     cudaError_t e = cudaStreamEndCapture(st, &b->graph);
     if (e != cudaSuccess)
       return fail(LGBM_B200_RUNTIME, "graph capture failed: %s", cudaGetErrorString(e));
-    CUDA_TRY(cudaGraphInstantiate(&b->graph_exec, b->graph, 0));
+    CUDA_TRY(cudaGraphInstantiate(&b->graph_exec, b->graph,
+                                  cudaGraphInstantiateFlagUseNodePriority));
   }
   cudaEvent_t e0, e1;
   CUDA_TRY(cudaEventCreate(&e0));
@@ -2462,7 +2475,7 @@ int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
   if (e != cudaSuccess)
     return fail(LGBM_B200_RUNTIME, "profile_pipeline: graph capture failed: %s",
                 cudaGetErrorString(e));
-  e = cudaGraphInstantiate(&exec, graph, 0);
+  e = cudaGraphInstantiate(&exec, graph, cudaGraphInstantiateFlagUseNodePriority);
   cudaGraphDestroy(graph);
   if (e != cudaSuccess)
     return fail(LGBM_B200_RUNTIME, "profile_pipeline: instantiate failed: %s",

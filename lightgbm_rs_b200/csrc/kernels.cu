@@ -1557,7 +1557,60 @@ struct CtlSmem {
   uint8_t ok[2];                  // the scanned leaves' scan flags
   PickOut pick;
   bool last;
+  int32_t wide;                   // the features' argmax was taken by the whole CTA ...
+  Cand wbest[2];                  // ... into these (smaller / larger scanned leaf)
+  Cand wpart[32][2];              // per-warp partials of that argmax
 };
+
+// Slices wider than this take the features' argmax with every thread of the last CTA
+// (their gain loads issued together) instead of one warp.
+constexpr int kWidePick = 128;
+
+// Best feature of each scanned leaf over this rank's slice, by every thread of the CTA:
+// the gains of both leaves (scan_out[0..F), scan_out[F..2F)), strided over the threads and
+// loaded kUnroll at a time, reduced in split_gt order (higher gain, then lower feature: a
+// strict order, so any partition of the features gives the one-warp loop's result).
+template <int CT>
+__device__ void block_best_features(const GrowDev& d, int32_t Lg, CtlSmem& cs) {
+  constexpr int kUnroll = 4;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  Cand f0{kNegInf, -1, -1}, f1{kNegInf, -1, -1};
+  for (int base = d.slice_begin + tid; base < d.slice_end; base += CT * kUnroll) {
+    double g0[kUnroll], g1[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int f = base + u * CT;
+      g0[u] = f < d.slice_end ? __ldcg(&d.scan_out[f].gain) : kNegInf;
+      g1[u] = (f < d.slice_end && Lg >= 0) ? __ldcg(&d.scan_out[d.F + f].gain) : kNegInf;
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int f = base + u * CT;
+      if (g0[u] > kNegInf && cand_better(g0[u], f, f, f0.g, f0.f, f0.i)) f0 = Cand{g0[u], f, f};
+      if (g1[u] > kNegInf && cand_better(g1[u], f, f, f1.g, f1.f, f1.i)) f1 = Cand{g1[u], f, f};
+    }
+  }
+  warp_argmax(f0);
+  warp_argmax(f1);
+  if (lane == 0) {
+    cs.wpart[warp][0] = f0;
+    cs.wpart[warp][1] = f1;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    Cand a{kNegInf, -1, -1}, b{kNegInf, -1, -1};
+    if (lane < CT / 32) {
+      a = cs.wpart[lane][0];
+      b = cs.wpart[lane][1];
+    }
+    warp_argmax(a);
+    warp_argmax(b);
+    if (lane == 0) {
+      cs.wbest[0] = a;
+      cs.wbest[1] = b;
+    }
+  }
+}
 
 // STAGED: `so` / `sc` are the scan results and bin sets in shared memory; otherwise the
 // global scan_out / scan_cat. `cs` holds the other leaves' best two and their splits.
@@ -1670,30 +1723,43 @@ __device__ void sliced_pick_exchange(const GrowDev& d, int32_t Lg, const DevSpli
   __syncwarp();
 }
 
+// The pick's inputs besides the scan results (the step's shared state).
+struct PickIn {
+  Cand2 other;     // the best two leaves the step leaves alone
+  Cand wbest[2];   // the features' argmax of a wide slice (wide = 1)
+  int32_t live, S, Lg, ok0, ok1, wide;
+};
+
 template <bool CAT, bool STAGED>
-__device__ void pick_warp(const GrowDev& d, const Prep& P, const CtlSmem& cs,
+__device__ void pick_warp(const GrowDev& d, const PickIn& in, const CtlSmem& cs,
                           const DevSplitInfo* so, const uint32_t* sc, PickOut& o) {
   const int lane = threadIdx.x & 31;
-  const bool find = P.live != 0;
-  const int32_t S = P.S, Lg = P.Lg;
-  Cand2 top = cs.other;
+  const bool find = in.live != 0;
+  const int32_t S = in.S, Lg = in.Lg;
+  const bool xch = d.sliced != 0;
+  Cand2 top = in.other;
   if (lane == 0) o.xerr = 0;
   if (find) {
-    const bool ok0 = cs.ok[0] != 0;
-    const bool ok1 = Lg >= 0 && cs.ok[1] != 0;
+    const bool ok0 = in.ok0 != 0;
+    const bool ok1 = Lg >= 0 && in.ok1 != 0;
     Cand f0{kNegInf, -1, -1}, f1{kNegInf, -1, -1};
-    for (int f = d.slice_begin + lane; f < d.slice_end; f += 32) {
-      const double g0 = pick_rd<double, STAGED>(&so[f].gain);
-      const double g1 = Lg >= 0 ? pick_rd<double, STAGED>(&so[d.F + f].gain) : kNegInf;
-      if (g0 > kNegInf && cand_better(g0, f, f, f0.g, f0.f, f0.i)) f0 = Cand{g0, f, f};
-      if (g1 > kNegInf && cand_better(g1, f, f, f1.g, f1.f, f1.i)) f1 = Cand{g1, f, f};
+    if (in.wide) {  // taken by the whole CTA (block_best_features)
+      f0 = in.wbest[0];
+      f1 = in.wbest[1];
+    } else {
+      for (int f = d.slice_begin + lane; f < d.slice_end; f += 32) {
+        const double g0 = pick_rd<double, STAGED>(&so[f].gain);
+        const double g1 = Lg >= 0 ? pick_rd<double, STAGED>(&so[d.F + f].gain) : kNegInf;
+        if (g0 > kNegInf && cand_better(g0, f, f, f0.g, f0.f, f0.i)) f0 = Cand{g0, f, f};
+        if (g1 > kNegInf && cand_better(g1, f, f, f1.g, f1.f, f1.i)) f1 = Cand{g1, f, f};
+      }
+      warp_argmax(f0);
+      warp_argmax(f1);
     }
-    warp_argmax(f0);
-    warp_argmax(f1);
-    if (d.sliced) sliced_pick_exchange<CAT, STAGED>(d, Lg, so, sc, o, f0, f1);
+    if (xch) sliced_pick_exchange<CAT, STAGED>(d, Lg, so, sc, o, f0, f1);
     const int32_t bf0 = ok0 ? f0.f : -1;
     const int32_t bf1 = ok1 ? f1.f : -1;
-    if (d.sliced) {
+    if (xch) {
       // the exchange left every rank's best of both leaves in o: apply the scan flags
       if (lane == 0 && bf0 < 0) {
         o.si[0] = d_split_none();
@@ -1741,7 +1807,7 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const CtlSmem& cs,
       o.feature = best.f;
       // an old leaf that wins or runs up is one of the other leaves' best two
       const int sel = (find && bl == S) ? 0 : (find && bl == Lg) ? 1 : -1;
-      const int oi = bl == cs.other.a.i ? 0 : 1;
+      const int oi = bl == in.other.a.i ? 0 : 1;
       // selected by address: no 72-byte temporaries
       const DevSplitInfo* sp = sel == 0 ? &o.si[0] : sel == 1 ? &o.si[1] : &cs.orec[oi];
       o.split = *sp;
@@ -1755,7 +1821,7 @@ __device__ void pick_warp(const GrowDev& d, const Prep& P, const CtlSmem& cs,
       if (d.lookahead && ru.i != 0x7fffffff && ru.g > 0.0) {
         const int32_t rl = ru.i;
         const int rs = (find && rl == S) ? 0 : (find && rl == Lg) ? 1 : -1;
-        const int ri = rl == cs.other.a.i ? 0 : 1;
+        const int ri = rl == in.other.a.i ? 0 : 1;
         const DevSplitInfo* rp = rs == 0 ? &o.si[0] : rs == 1 ? &o.si[1] : &cs.orec[ri];
         o.la_leaf = rl;
         o.la_feature = ru.f;
@@ -1876,13 +1942,34 @@ __device__ void cat_scan(const double* hist, const DevFeature& ft, const DevGain
     s.pg[gt] = ctr;
     s.pc[gt] = keep ? 1 : 0;
     group_sync(bar_id);
-    int rank = 0;
+    // Place in the reference's stable sort by ctr (sort_by with partial_cmp, unordered as
+    // Equal; an insertion sort on up to 20 elements): a category moves left past every
+    // neighbour with a strictly greater ctr. A NaN ctr (0/0: cat_smooth 0 and a category
+    // without rows in this leaf) is ordered with nothing, so it keeps its place among the
+    // kept categories and the runs on either side of it are sorted apart. Rank = start of
+    // this category's run + the run's members that precede it.
+    const bool nan_me = isnan(ctr);
+    int pos = 0, lo = 0, less = 0;
+    bool past = false, stop = false;
     for (int u = 0; u < nscan; ++u) {
       if (!s.pc[u]) continue;
-      ++used;
       const double cu = s.pg[u];
-      if (cu < ctr || (cu == ctr && u < gt)) ++rank;
+      if (u == gt) {
+        pos = used;
+        past = true;
+      } else if (isnan(cu)) {
+        if (!past) {
+          lo = used + 1;  // a NaN before this category closes the run before it
+          less = 0;
+        } else {
+          stop = true;  // ... and one after it closes its run
+        }
+      } else if (!stop && (cu < ctr || (cu == ctr && u < gt))) {
+        ++less;
+      }
+      ++used;
     }
+    const int rank = nan_me ? pos : lo + less;
     group_sync(bar_id);
     if (keep) sorted[rank] = t;
     group_sync(bar_id);
@@ -2318,20 +2405,30 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     }
   }
   if (warp == 1 && (tid & 31) == 0) prep_commit<CAT>(d, P);
+  // wide slices: the features' argmax by the whole CTA (its gain loads issued together)
+  const bool wide = !staged && P.live && !P.c.done && (fe - fb) > kWidePick;
+  if (tid == 0) cs.wide = wide ? 1 : 0;
+  if (wide) block_best_features<CT>(d, P.Lg, cs);
   __syncthreads();
   ctl_mark(d, s, CP_STAGED);
   if (warp == 0 && !P.c.done) {
+    const PickIn in{cs.other, {cs.wbest[0], cs.wbest[1]}, P.live, P.S, P.Lg, cs.ok[0], cs.ok[1],
+                    cs.wide};
     if (staged)
-      pick_warp<CAT, true>(d, P, cs, so, sc, cs.pick);
+      pick_warp<CAT, true>(d, in, cs, so, sc, cs.pick);
     else
-      pick_warp<CAT, false>(d, P, cs, d.scan_out, d.scan_cat, cs.pick);
+      pick_warp<CAT, false>(d, in, cs, d.scan_out, d.scan_cat, cs.pick);
   }
   __syncthreads();
   ctl_mark(d, s, CP_PICKED);
   // The next step reads the chosen leaf's integer and f64 histogram rows, which the
   // partitions' streaming has usually pushed out of L2 since the leaf was scanned: bring
   // them back now, one bulk prefetch per 16 KB.
-  if (warp == 1 && !P.c.done && !cs.pick.done) {
+  // Rows above kPrefetchMax bytes (wide data) are left out: one SM's bulk prefetches of
+  // megabytes hold the kernel's end back longer than the next step's many CTAs take to
+  // read the rows themselves.
+  constexpr uint32_t kPrefetchMax = 512u << 10;
+  if (warp == 1 && !P.c.done && !cs.pick.done && (uint64_t)d.raw_len * 8u <= kPrefetchMax) {
     const int32_t b = cs.pick.leaf;
     const int32_t slot = (P.live && b == P.S)    ? P.sslot
                          : (P.live && b == P.Lg) ? P.lslot
@@ -3239,8 +3336,12 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       GrowDev x = consumer(s);
       x.span_slot = span_slot_of(s, SPAN_FIXSCAN);
       PROF_BEGIN(KC_FIXSCAN);
-      // variants: categorical features, and the peer exchange (off on one device)
-      const int grid = x.slice_end - x.slice_begin;  // this rank's features
+      // variants: categorical features, and the peer exchange (off on one device). One
+      // CTA per feature of this rank's slice, at most one resident wave of CTAs (each
+      // takes features blockIdx.x, blockIdx.x + grid, ...): a CTA applies the pending
+      // split once, however many features it scans.
+      const int slice = x.slice_end - x.slice_begin;
+      const int grid = std::min(slice, (x.narrow_scan && !x.has_cat ? 4 : 1) * sms);
       if (x.has_cat)
         (px ? k_fixscan<true, true, 1024> : k_fixscan<true, false, 1024>)<<<grid, 1024, 0, st>>>(
             x, s);
@@ -3263,7 +3364,9 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
     // mostly find the split already partitioned) are placed first
     if (x.fused) {
       PROF_BEGIN(KC_PARTITION);
-      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT, x.packed4 != 0)<<<sms, kFpThreads,
+      const int main_grid = la_on ? las->main_blocks : sms;
+      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT, x.packed4 != 0)<<<main_grid,
+                                                                kFpThreads,
                                                                 fused_partition_smem(), st>>>(
           x, phase == 1 ? 1 : 0, -1);
       PROF_END();

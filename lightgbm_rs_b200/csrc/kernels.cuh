@@ -237,6 +237,7 @@ struct LookAheadStreams {
   cudaEvent_t fork;     // after control step s, on the main stream
   cudaEvent_t done[kLaSlots];  // after the look-ahead kernel of step s, slot s % kLaSlots
   int blocks;           // CTAs of a look-ahead kernel (the control step keeps the rest)
+  int main_blocks;      // CTAs of the main-stream partition while look-aheads run
 };
 
 // Host-side launch helpers (kernels.cu).

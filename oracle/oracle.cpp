@@ -480,8 +480,18 @@ OSplitInfo find_best_categorical(const double* hist, const GainCfg& cfg, int32_t
     used = (int32_t)order.size();
     l2 += cfg.cat_l2;
     auto ctr = [&](int32_t t) { return hist[2 * t] / (hist[2 * t + 1] + cfg.cat_smooth); };
-    std::stable_sort(order.begin(), order.end(),
-                     [&](int32_t a, int32_t b) { return ctr(a) < ctr(b); });
+    // Stable ascending sort by ctr as the reference's sort_by(partial_cmp, unordered as
+    // Equal) runs it on up to 20 elements: an insertion sort that moves a category left
+    // while its ctr is strictly below its neighbour's. A NaN ctr (0/0: cat_smooth 0 and a
+    // category without rows in the leaf) is below nothing and nothing is below it, so it
+    // keeps its place and the categories on either side are sorted apart.
+    for (size_t i = 1; i < order.size(); ++i) {
+      const int32_t t = order[i];
+      const double c = ctr(t);
+      size_t j = i;
+      for (; j > 0 && c < ctr(order[j - 1]); --j) order[j] = order[j - 1];
+      order[j] = t;
+    }
     const int32_t max_num_cat = std::min(cfg.max_cat_threshold, (used + 1) / 2);
     for (int dir_i = 0; dir_i < 2; ++dir_i) {
       const int32_t dir = dir_i == 0 ? 1 : -1;

@@ -83,27 +83,31 @@ def _mixed_data(n=30_000, seed=5):
     return X, y, [4, 5, 6, 7]
 
 
-@pytest.mark.parametrize("quant_bins,max_cat_to_onehot", [(4, 4), (16, 4), (4, 16)])
-def test_categorical_tree_bit_exact_vs_oracle(quant_bins, max_cat_to_onehot):
+@pytest.mark.parametrize("quant_bins,max_cat_to_onehot,cat_smooth",
+                         [(4, 4, 5.0), (16, 4, 5.0), (4, 16, 5.0), (4, 4, 0.0)])
+def test_categorical_tree_bit_exact_vs_oracle(quant_bins, max_cat_to_onehot, cat_smooth):
+    """cat_smooth 0 keeps categories without rows in a leaf, whose ratio is 0/0 (NaN):
+    they keep their place in the sort and split it into runs sorted apart."""
     import lightgbm_rs_b200 as lgb
     import oracle
 
     X, y, cats = _mixed_data()
     params = {"max_bin": 255, "min_data_in_leaf": 20, "min_data_per_group": 50,
-              "cat_smooth": 5.0, "max_cat_to_onehot": max_cat_to_onehot}
+              "cat_smooth": cat_smooth, "max_cat_to_onehot": max_cat_to_onehot}
     ds = lgb.Dataset(X, y, params, categorical_feature=cats)
     assert [m["bin_type"] for m in ds.mappers] == [0, 0, 0, 0, 1, 1, 1, 1]
     metas = [{k: m[k] for k in ("num_bin", "default_bin", "most_freq_bin", "missing_type",
                                 "bin_type")} for m in ds.mappers]
     g, h = oracle.binary_gradients(np.zeros(len(y)), y)
     gq, hq, q, scales = oracle.quantize(g, h, quant_bins)
-    kw = dict(min_data_in_leaf=20, min_data_per_group=50, cat_smooth=5.0,
+    kw = dict(min_data_in_leaf=20, min_data_per_group=50, cat_smooth=cat_smooth,
               max_cat_to_onehot=max_cat_to_onehot)
     want, wpart, _ = oracle.grow_tree(ds.bins, metas, gq, hq, num_leaves=63, **kw)
     assert (want["decision_type"] & 1).sum() > 0, "the data should grow categorical nodes"
     learner = lgb.Learner(ds, {"num_leaves": 63, **kw})
     got, gpart = learner.grow(quantized=q, scales=[scales[0], scales[1], scales[2], quant_bins])
-    _assert_trees_bit_equal(got, want, f"cat q{quant_bins} onehot<={max_cat_to_onehot}")
+    _assert_trees_bit_equal(got, want,
+                            f"cat q{quant_bins} onehot<={max_cat_to_onehot} smooth {cat_smooth}")
     for l in range(got["num_leaves"]):
         a = np.sort(gpart["indices"][gpart["leaf_begin"][l]:][:gpart["leaf_count"][l]])
         b = np.sort(wpart["indices"][wpart["leaf_begin"][l]:][:wpart["leaf_count"][l]])
