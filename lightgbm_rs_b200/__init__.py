@@ -608,7 +608,8 @@ class Booster:
         at its phase marks (time to each mark from the previous one, summed). "main_noop" /
         "main_run": the main partitions shorter / longer than 8 us (it found its leaf
         partitioned by the look-ahead, or ran), with their mean delay after the control
-        step and mean span in us."""
+        step and mean span in us (and [step, span us] of each run); "lookahead_span_us":
+        the mean look-ahead span."""
         n = C._i32(0)
         C.check(C.lib().lgbm_b200_booster_profile_spans(self._handle, 0, None, None, None,
                                                         ctypes.byref(n)))
@@ -629,7 +630,9 @@ class Booster:
                "launch_gap": 0.0, "steps": 0, "lookahead_limited": 0, "main_limited": 0,
                "before_first_step": 0.0, "tree": 0.0, "control_phases": {},
                "main_noop": {"n": 0, "launch_after_control_us": 0.0, "span_us": 0.0},
-               "main_run": {"n": 0, "launch_after_control_us": 0.0, "span_us": 0.0}}
+               "main_run": {"n": 0, "launch_after_control_us": 0.0, "span_us": 0.0,
+                            "steps": []},
+               "lookahead_span_us": 0.0, "lookahead_n": 0}
         steps = (len(st) - 1) // 4
         first = span(1)
         root = span(0)
@@ -667,6 +670,12 @@ class Booster:
                 m["n"] += 1
                 m["launch_after_control_us"] += (main[0] - ctl[1]) * 1e-3
                 m["span_us"] += (main[1] - main[0]) * 1e-3
+                if kind == "run":
+                    m["steps"].append([s, round((main[1] - main[0]) * 1e-3, 1)])
+            own_la = span(1 + 4 * s + 2)
+            if own_la:
+                out["lookahead_span_us"] += (own_la[1] - own_la[0]) * 1e-3
+                out["lookahead_n"] += 1
             # inside the control step: entry, the phase marks in order, exit
             marks = [ctl[0]] + [int(v) for v in ph[s]] + [ctl[1]]
             prev = marks[0]
@@ -676,6 +685,8 @@ class Booster:
                 out["control_phases"][name] = out["control_phases"].get(name, 0.0) + \
                     max(t_m - prev, 0) * 1e-6
                 prev = max(prev, t_m)
+        if out["lookahead_n"]:
+            out["lookahead_span_us"] /= out["lookahead_n"]
         for kind in ("main_noop", "main_run"):  # means per launch
             m = out[kind]
             if m["n"]:

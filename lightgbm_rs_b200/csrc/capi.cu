@@ -351,7 +351,18 @@ int lgbm_b200_learner::configure_groups(int mode) {
     const int max_nf = std::min(128, kQ4MaxCells >> shift);
     // groups start on a 16-byte boundary of the row: 16 features, or 32 in a 4-bit matrix
     const int align = ds->packed4 ? 32 : 16;
-    const int per_group = F <= max_nf ? F : (max_nf / align) * align;
+    int per_group = F <= max_nf ? F : (max_nf / align) * align;
+    // Wide data: groups of 48 features rather than the widest the shared layout holds. A
+    // child's build splits its rows over the CTAs of each group and every CTA flushes its
+    // group's cells with global atomics, so narrower groups (more groups, fewer CTAs per
+    // group) flush fewer cells in total (C2, 2,000 features of 63 bins: builds 5.8 -> 4.4
+    // ms per tree with 112 -> 48 features per group; 16 gave 4.6).
+    constexpr int kWideGroup = 48;
+    if (F > max_nf && per_group > kWideGroup && kWideGroup % align == 0) per_group = kWideGroup;
+    if (const char* e = std::getenv("LGBM_B200_Q4_GROUP")) {  // tuning: features per group
+      const int g = (std::atoi(e) / align) * align;
+      if (g >= align && g < per_group) per_group = g;
+    }
     for (int f0 = 0; f0 < F; f0 += per_group) {
       const int f1 = std::min(F, f0 + per_group);
       groups.push_back(DevFeatureGroup{f0, f1, ds->feats[f0].bin_off, (f1 - f0) << shift, shift,
@@ -777,6 +788,7 @@ struct lgbm_b200_booster {
   // peer-memory exchange of the accumulated child (data-parallel, one node)
   DevBuf<unsigned long long> xmem;  // [2][raw_len + 2] accumulators | flags | count
   DevBuf<void*> xptrs;              // per-rank accumulator and flag pointers
+  DevBuf<uint32_t> arrive;          // producer launches' CTA arrival counters (two kinds)
   std::vector<void*> xpeer;         // the other ranks' regions, opened by IPC handle
   ~lgbm_b200_booster() {
     destroy_graph();
@@ -1992,6 +2004,14 @@ int setup_peer_exchange(lgbm_b200_booster* b, lgbm_b200_comm* comm) {
   }
   long long wait_ms = 2000;
   if (const char* w = std::getenv("LGBM_B200_PEER_WAIT_MS")) wait_ms = std::max(1ll, atoll(w));
+  // producers publish their own exchange (LGBM_B200_SELF_SIGNAL=0: a signal kernel after
+  // each producer instead)
+  const char* ss = std::getenv("LGBM_B200_SELF_SIGNAL");
+  if (!(ss && std::strcmp(ss, "0") == 0)) {
+    CUDA_TRY(b->arrive.alloc(2));
+    CUDA_TRY(cudaMemset(b->arrive.p, 0, 2 * sizeof(uint32_t)));
+    d.arrive = b->arrive.p;
+  }
   std::vector<void*> ptrs(6 * (size_t)R);
   for (int q = 0; q < R; ++q) {
     ptrs[q] = base[q];
@@ -2021,10 +2041,16 @@ int setup_peer_exchange(lgbm_b200_booster* b, lgbm_b200_comm* comm) {
     d.la_seq = b->xmem.p + off_laseq;
   }
   // Feature slices (the data-parallel learner's split of the scan work): rank q decodes
-  // and scans features [q F / R, (q + 1) F / R), when every rank gets at least two
-  // (LGBM_B200_FEATURE_SLICES=0 keeps every feature on every rank).
+  // and scans features [q F / R, (q + 1) F / R). They pay when each rank's slice is wide:
+  // the sliced pick costs one more cross-device round trip per split, which a narrow
+  // slice (C1: 14 of 28 features per rank) does not win back (2 B200s, C1: 67 it/s
+  // sliced, 86 unsliced; C2, 1,000 per rank: 73 sliced, 71 unsliced). By default a rank
+  // gets a slice when it holds at least kSliceMinFeatures features;
+  // LGBM_B200_FEATURE_SLICES=1 slices whenever every rank gets two, =0 never.
+  constexpr int kSliceMinFeatures = 128;
   const char* fs = std::getenv("LGBM_B200_FEATURE_SLICES");
-  if (d.F >= 2 * R && !(fs && std::strcmp(fs, "0") == 0)) {
+  const bool force = fs && std::strcmp(fs, "1") == 0, never = fs && std::strcmp(fs, "0") == 0;
+  if (d.F >= 2 * R && !never && (force || d.F >= kSliceMinFeatures * R)) {
     d.sliced = 1;
     d.slice_begin = (int32_t)((int64_t)d.F * comm->rank / R);
     d.slice_end = (int32_t)((int64_t)d.F * (comm->rank + 1) / R);

@@ -228,6 +228,36 @@ __global__ void k_lasignal(GrowDev d) {
   if (lane == 0) *d.la_seq = seq;
 }
 
+// End of a producer launch that publishes its own exchange (self_signal): what k_xsignal
+// or k_lasignal would do after the kernel, without a launch of its own. Every thread of
+// every CTA calls it after its last write. The CTAs arrive on an acq_rel counter (so the
+// last one to arrive has every CTA's writes ordered before it), and the last one resets
+// the counter for the next launch of its kind (stream-ordered after this one), fences at
+// system scope and releases the next sequence number into every rank's flag.
+__device__ __forceinline__ void producer_signal(const GrowDev& d) {
+  if (!d.self_signal) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  const int k = d.self_signal - 1;
+  uint32_t* cnt = d.arrive + k;
+  const uint32_t n = gridDim.x * gridDim.y * gridDim.z;
+  uint32_t t;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(t) : "l"(cnt), "r"(1u)
+               : "memory");
+  if (t != n - 1) return;
+  *cnt = 0u;
+  unsigned long long* seqp = k == 0 ? d.xseq : d.la_seq;
+  unsigned long long* const* flags = k == 0 ? d.peer_xflags : d.peer_la_flags;
+  const unsigned long long seq = *seqp + 1;
+  __threadfence_system();
+  for (int r = 0; r < d.xranks; ++r) {
+    unsigned long long* f = flags[r] + d.xrank;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(seq) : "memory");
+  }
+  *seqp = seq;
+}
+
 // Decoding of the raw integer accumulators into f64 histogram cells. For the
 // quantized modes the result equals the reference's f64 fold exactly: every
 // dequantized level is an integer multiple of the ulp of the smallest nonzero
@@ -379,8 +409,7 @@ __device__ __forceinline__ void build_block(const uint8_t* __restrict__ bins, in
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d, int phase) {
-  const SpanStamp span(d);
+__device__ __forceinline__ void build_body(const GrowDev& d, int phase) {
   extern __shared__ unsigned long long acc[];
   __shared__ int32_t s_binoff[128];
   __shared__ uint8_t s_used[128];
@@ -448,6 +477,13 @@ __global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d, int phase) {
       if (b) atomicAdd((unsigned long long*)&raw[2 * w + 1], b);
     }
   }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kBuildThreads) k_build(GrowDev d, int phase) {
+  const SpanStamp span(d);
+  build_body<MODE>(d, phase);
+  producer_signal(d);
 }
 
 // ------------------------------------------------------------------------------------
@@ -521,9 +557,8 @@ __device__ __forceinline__ Q4Mask q4_mask(const uint32_t* s_mask, int nf) {
   return m;
 }
 
-template <int SHIFT, int NCH, bool PACK4 = false>
-__global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase) {
-  const SpanStamp span(d);
+template <int SHIFT, int NCH, bool PACK4>
+__device__ __forceinline__ void build_q4_body(const GrowDev& d, int phase) {
   extern __shared__ uint32_t sm[];
   __shared__ uint32_t s_mask[4];
   const BuildTarget t = build_target(d, phase);
@@ -643,6 +678,13 @@ __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase
     if (h)
       atomicAdd(reinterpret_cast<unsigned long long*>(&raw[2 * gb + 1]), (unsigned long long)h);
   }
+}
+
+template <int SHIFT, int NCH, bool PACK4 = false>
+__global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase) {
+  const SpanStamp span(d);
+  build_q4_body<SHIFT, NCH, PACK4>(d, phase);
+  producer_signal(d);
 }
 
 // (SHIFT, NCH) instantiations with (16 * (NCH - 1) + 1) << SHIFT <= kQ4MaxCells.
@@ -1545,6 +1587,13 @@ struct PickOut {
 // over all leaves (learner.rs:4537-4551, first max under split_gt, learner.rs:1503-1505
 // stop rule), by one warp: the feature candidates are reduced with shuffles only.
 // Shared memory of a control step besides the per-feature scratch.
+// The pick's inputs besides the scan results (the step's shared state).
+struct PickIn {
+  Cand2 other;     // the best two leaves the step leaves alone
+  Cand wbest[2];   // the features' argmax of a wide slice (wide = 1)
+  int32_t live, S, Lg, ok0, ok1, wide;
+};
+
 struct CtlSmem {
   Prep prep;
   Cand2 other;                    // the best two leaves the step leaves alone
@@ -1722,13 +1771,6 @@ __device__ void sliced_pick_exchange(const GrowDev& d, int32_t Lg, const DevSpli
   }
   __syncwarp();
 }
-
-// The pick's inputs besides the scan results (the step's shared state).
-struct PickIn {
-  Cand2 other;     // the best two leaves the step leaves alone
-  Cand wbest[2];   // the features' argmax of a wide slice (wide = 1)
-  int32_t live, S, Lg, ok0, ok1, wide;
-};
 
 template <bool CAT, bool STAGED>
 __device__ void pick_warp(const GrowDev& d, const PickIn& in, const CtlSmem& cs,
@@ -3129,6 +3171,7 @@ __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int b
   extern __shared__ uint32_t sm[];
   __shared__ PartSmem ps;
   partition_q4_phase<SHIFT, NCH, F32, PACK4>(d, build, la, sm, ps);
+  producer_signal(d);
 }
 
 using PartQ4Kernel = void (*)(GrowDev, int, int);
@@ -3318,15 +3361,21 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       k_build<GH_FLOAT><<<bgrid, kBuildThreads, build_smem, st>>>(x, phase);
     PROF_END();
   };
+  // Over peer memory each producer launch publishes its own exchange at its end
+  // (producer_signal); without it a one-warp k_xsignal follows. With NCCL the sum
+  // follows the producer.
+  const bool self_sig = px && d.arrive != nullptr;
   auto exchange = [&](const GrowDev& x) {
-    if (px)
-      k_xsignal<<<1, 32, 0, st>>>(x);
-    else if (comm)
+    if (px) {
+      if (!self_sig) k_xsignal<<<1, 32, 0, st>>>(x);
+    } else if (comm) {
       comm->sum_i64(comm->ctx, x.raw, (int64_t)x.raw_len + 1, st);
+    }
   };
   {
     GrowDev x = producer(0);
     x.span_slot = kSpanRootBuild;
+    x.self_signal = self_sig ? 1 : 0;
     build(x, 0);
     exchange(x);
   }
@@ -3356,6 +3405,7 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
     const int phase = s < d.L - 2 ? 1 : 2;
     GrowDev x = producer(s + 1);
     x.span_slot = span_slot_of(s, SPAN_PARTITION);
+    x.self_signal = (self_sig && x.fused) ? 1 : 0;  // the fused partition is the producer
     const bool la_step = la_on && s <= d.L - 3;
     // A profiled sequence runs the look-ahead on the main stream, right after the control
     // step: each launch's event span is then its own run, not its wait for free SMs.
@@ -3378,6 +3428,7 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       }
       GrowDev xb = x;
       xb.span_slot = span_slot_of(s, SPAN_BUILD);
+      xb.self_signal = self_sig ? 1 : 0;  // the build after the partition is the producer
       build(xb, phase);
     }
     if (la_step) {
@@ -3386,11 +3437,12 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       const int pslot = prof ? prof->begin(lst, KC_PARTITION) : -1;
       GrowDev xl = x;
       xl.span_slot = span_slot_of(s, SPAN_LOOKAHEAD);
+      xl.self_signal = self_sig ? 2 : 0;
       part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT, x.packed4 != 0)<<<las->blocks, kFpThreads,
                                                                 fused_partition_smem(),
                                                                 lst>>>(xl, 1, s & (kLaSlots - 1));
       if (prof) prof->end(lst, pslot);
-      if (px) k_lasignal<<<1, 32, 0, lst>>>(x);  // every rank may read the slot now
+      if (px && !self_sig) k_lasignal<<<1, 32, 0, lst>>>(x);  // every rank may read the slot
       if (!prof) cudaEventRecord(las->done[s & (kLaSlots - 1)], lst);
     }
     exchange(x);

@@ -137,6 +137,12 @@ struct GrowDev {
   unsigned long long* xflags;                 // this rank's flags, one per rank
   unsigned long long* const* peer_xflags;     // [xranks] each rank's flags (device)
   unsigned long long* xseq;                   // exchanges this rank has published
+  // Producer launches over peer memory publish their own exchange at the end (set on the
+  // launch's copy): 1 the accumulator exchange (xflags / xseq), 2 the look-ahead slot
+  // (la_flags / la_seq); 0 none (one device, or a separate signal kernel). arrive: the
+  // two kinds' CTA arrival counters (zero between launches).
+  int32_t self_signal;
+  uint32_t* arrive;
   long long xwait_ns;                         // wait limit, then the spin-timeout error
   // Look-ahead partitions (fused partition): control step s records slot s % kLaSlots and
   // its look-ahead kernel fills it; control step s + 2 consumes it (when step s + 1 picked

@@ -35,8 +35,9 @@ def _data(wide=False):
 def _worker(rank, world, uid, quantized, leaves, q, wide=False, slices=True):
     try:
         os.environ["NCCL_NVLS_ENABLE"] = "0"
-        if not slices:
-            os.environ["LGBM_B200_FEATURE_SLICES"] = "0"
+        # on: every rank scans its own half of the features (forced for narrow data, where
+        # the default keeps every feature on every rank); off: every rank scans all
+        os.environ["LGBM_B200_FEATURE_SLICES"] = "1" if slices else "0"
         import sys
         sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         import lightgbm_rs_b200 as lgb
