@@ -2004,10 +2004,11 @@ int setup_peer_exchange(lgbm_b200_booster* b, lgbm_b200_comm* comm) {
   }
   long long wait_ms = 2000;
   if (const char* w = std::getenv("LGBM_B200_PEER_WAIT_MS")) wait_ms = std::max(1ll, atoll(w));
-  // producers publish their own exchange (LGBM_B200_SELF_SIGNAL=0: a signal kernel after
-  // each producer instead)
+  // LGBM_B200_SELF_SIGNAL=1: producers publish their own exchange instead of a signal
+  // kernel after each. Off by default: on 2 B200s (C1) the system-scope fence in the last
+  // CTA delayed each partition's end by about what the saved launch cost (83.4 vs 85.5 it/s).
   const char* ss = std::getenv("LGBM_B200_SELF_SIGNAL");
-  if (!(ss && std::strcmp(ss, "0") == 0)) {
+  if (ss && std::strcmp(ss, "1") == 0) {
     CUDA_TRY(b->arrive.alloc(2));
     CUDA_TRY(cudaMemset(b->arrive.p, 0, 2 * sizeof(uint32_t)));
     d.arrive = b->arrive.p;

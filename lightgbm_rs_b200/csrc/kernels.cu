@@ -1993,23 +1993,35 @@ __device__ void cat_scan(const double* hist, const DevFeature& ft, const DevGain
     const bool nan_me = isnan(ctr);
     int pos = 0, lo = 0, less = 0;
     bool past = false, stop = false;
-    for (int u = 0; u < nscan; ++u) {
-      if (!s.pc[u]) continue;
-      const double cu = s.pg[u];
-      if (u == gt) {
-        pos = used;
-        past = true;
-      } else if (isnan(cu)) {
-        if (!past) {
-          lo = used + 1;  // a NaN before this category closes the run before it
-          less = 0;
-        } else {
-          stop = true;  // ... and one after it closes its run
-        }
-      } else if (!stop && (cu < ctr || (cu == ctr && u < gt))) {
-        ++less;
+    // eight categories at a time, their shared-memory loads issued together
+    for (int u0 = 0; u0 < nscan; u0 += 8) {
+      int32_t kp[8];
+      double cv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {  // u < kMaxBins: in the arrays even past nscan
+        kp[j] = u0 + j < nscan ? s.pc[u0 + j] : 0;
+        cv[j] = s.pg[u0 + j];
       }
-      ++used;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (!kp[j]) continue;
+        const int u = u0 + j;
+        const double cu = cv[j];
+        if (u == gt) {
+          pos = used;
+          past = true;
+        } else if (isnan(cu)) {
+          if (!past) {
+            lo = used + 1;  // a NaN before this category closes the run before it
+            less = 0;
+          } else {
+            stop = true;  // ... and one after it closes its run
+          }
+        } else if (!stop && (cu < ctr || (cu == ctr && u < gt))) {
+          ++less;
+        }
+        ++used;
+      }
     }
     const int rank = nan_me ? pos : lo + less;
     group_sync(bar_id);
