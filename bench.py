@@ -538,6 +538,16 @@ def run_ours(args):
     # stamping %globaltimer at entry and exit), and the kernels' own work counters ----
     spans, pc = booster.profile_pipeline(5)
     chain = booster.profile_chain()  # the last of those iterations, step by step
+    # the part of the split chain that holds the tree longest, and inside the control step
+    # its longest phase
+    parts = {k: chain[k] for k in ("control_step", "main_partition_past", "build_past",
+                                   "lookahead_past", "launch_gap")}
+    top = max(parts, key=parts.get)
+    ph = chain.get("control_phases") or {}
+    chain["limiting_phase"] = {
+        "part": top, "ms_per_tree": parts[top],
+        "share_of_tree": parts[top] / chain["tree"] if chain["tree"] else None,
+        "control_step_phase": max(ph, key=ph.get) if ph else None}
     kb = kernel_bytes(pc, local_rows, args.grad, data.features)
     peak, peak_kind = load_peaks()
     part_ms = spans["partition"] + pc["lookahead"]
