@@ -7,6 +7,7 @@ Default gradients: use_quantized_grad with 4 quantization bins (`--grad f32` for
 f32-gradient variant). One step = one boosting iteration (gradients, quantization,
 one tree, shrinkage, score update) over all rows.
 
+`--workload c0`: configs[0] itself, 100,000 rows x 28, 31 leaves, 100 iterations.
 `--workload c2`: 400,000 rows x 2,000 features ~ U(-1,1), max_bin=63, 127 leaves.
 `--workload c3`: 2,000,000 rows, 90 numeric features with 10 % NaN and 10 categorical
 features, L2 regression, 63 leaves. `--workload c4`: lambdarank over 20,000 queries
@@ -14,7 +15,7 @@ features, L2 regression, 63 leaves. `--workload c4`: lambdarank over 20,000 quer
 with the configurations' shapes (lightgbm_rs_b200/synthetic.py).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload c1|c2|c3|c4] [--grad quantized|f32]
+                  [--workload c0|c1|c2|c3|c4] [--grad quantized|f32]
 
 Prints ONE JSON line on rank 0. Besides the timed steps, the default line carries:
   parity    the first trees and the scores after them, grown on the device and by the
@@ -51,6 +52,9 @@ PARITY_TREES = 3
 # name -> rows, features, leaves, min_data_in_leaf, max_bin, objective, full-length
 # iterations, description
 WORKLOADS = {
+    "c0": dict(rows=100_000, features=28, leaves=31, min_data=20, max_bin=255,
+               objective="binary", iterations=100,
+               desc="C0 binary {rows}x28 num_leaves=31 max_bin=255"),
     "c1": dict(rows=10_500_000, features=28, leaves=255, min_data=100, max_bin=255,
                objective="binary", iterations=500,
                desc="C1 binary {rows}x28 num_leaves=255 min_data_in_leaf=100 max_bin=255"),
@@ -165,7 +169,7 @@ def make_data(workload, rows, seed=0, binner="product"):
     synthetic = load_synthetic()
     w = WORKLOADS[workload]
     group, cats = None, []
-    if workload == "c1":
+    if workload in ("c0", "c1"):  # C1 is C0's generator at 10.5M rows
         X, y = synthetic.binary_c0(num_data=rows, num_features=w["features"], seed=seed)
     elif workload == "c2":
         X, y = synthetic.wide_c2(num_data=rows, num_features=w["features"], seed=seed)

@@ -780,11 +780,6 @@ __device__ __forceinline__ double seq_sub(const double* v, int stride, int n, do
   return acc;
 }
 
-// Prefetch of the line holding p into L2.
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-
 // Asynchronous prefetch of [p, p + bytes) into L2 (p and bytes multiples of 16).
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -2815,7 +2810,6 @@ __device__ __forceinline__ int32_t tile_lookback(unsigned long long* status, int
 struct PartSmem {
   int32_t warp[kFpThreads / 32];
   int32_t tile, prefix, ok;
-  int32_t next;  // the CTA's next tile, its ticket taken while the current one runs
   int32_t nb[128];
   int32_t boff[128];
   uint32_t mask[4];
@@ -2992,14 +2986,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
   int32_t cta_left = 0;
   long long cta_built = 0;
   bool failed = false;
-  // Rows of the CTA's next tile, read while the current tile runs (its ticket is taken at
-  // the top of the current one) and prefetched into L2 before the current tile's look-back
-  // wait, so a tile's row gather starts from L2 and no ticket round trip sits between
-  // tiles. A reserved tile is always held by a running CTA, so every look-back still ends.
-  uint32_t pre[kFpItems];
-  bool have_pre = false;
   while (true) {
-    if (tid == 0 && !priv) ps_.next = (int32_t)atomicAdd(ticket, 1u);
     const int32_t base = tile * kPartTile;
     uint32_t rows[kFpItems];
     uint4 w[kFpItems][NCH];
@@ -3011,7 +2998,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
       const int32_t p = base + tid * kFpItems + j;
       rows[j] = 0;
       if (p < count) {
-        rows[j] = have_pre ? pre[j] : identity ? (uint32_t)(begin + p) : sp[begin + p];
+        rows[j] = identity ? (uint32_t)(begin + p) : sp[begin + p];
         validmask |= 1u << j;
       }
     }
@@ -3050,16 +3037,6 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     }
     if (lane == 31) s_warp[warp] = incl;
     __syncthreads();
-    // the next tile's row indices: loads issued now, used after this tile's atomics
-    const int32_t next_tile = priv ? ntiles : ps_.next;
-    have_pre = next_tile < ntiles;
-    if (have_pre) {
-#pragma unroll
-      for (int j = 0; j < kFpItems; ++j) {
-        const int32_t p = next_tile * kPartTile + tid * kFpItems + j;
-        pre[j] = p < count ? (identity ? (uint32_t)(begin + p) : sp[begin + p]) : 0u;
-      }
-    }
     int32_t warp_off = 0, tile_left = 0;
 #pragma unroll 8
     for (int wi = 0; wi < kFpThreads / 32; ++wi) {
@@ -3099,15 +3076,6 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
         }
       }
     }
-    if (have_pre) {  // the next tile's bin rows and gradients into L2 during the look-back
-#pragma unroll
-      for (int j = 0; j < kFpItems; ++j) {
-        const int32_t p = next_tile * kPartTile + tid * kFpItems + j;
-        if (p >= count) continue;
-        prefetch_l2(d.bins + (size_t)pre[j] * stride);
-        if (build) prefetch_l2(F32 ? (const void*)(gf + pre[j]) : (const void*)(gq + pre[j]));
-      }
-    }
     __syncthreads();
     const int32_t prefix_left = s_prefix;
     if (s_ok == 0) {
@@ -3136,7 +3104,9 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     cta_built += built;
     acc_rows += built;
     if (priv) break;
-    tile = next_tile;
+    if (tid == 0) s_tile = (int32_t)atomicAdd(ticket, 1u);
+    __syncthreads();
+    tile = s_tile;
     if (tile >= ntiles) break;
     // fold the 16-bit packed fields before the next tile could overflow them (the 64-bit
     // f32 cells need no fold)
