@@ -804,6 +804,10 @@ def run_atomics(args):
       random  uniform bins over 256 (the C1 matrix's quantile bins are close to this)
       c1      the C1 matrix itself
       same    every row bin 0: all lanes on one cell
+      skewed  bin 0 for 90 % of rows, uniform otherwise (a heavily skewed feature)
+    Each pattern runs with one atomic per (row, feature) and with warp-aggregated atomics
+    (LGBM_B200_WARP_AGG=1: lanes with the same bin summed with __match_any_sync and
+    __reduce_add_sync, one atomic per group).
     The first boosting iteration of a fresh booster (binary, from the initial score: a
     constant hessian, so exactly F atomics per row); the root build's device span comes
     from the pipeline stamps, best of `--steps` boosters."""
@@ -822,6 +826,8 @@ def run_atomics(args):
         "lanes": lambda f: ((rows + 7 * f) % 32).astype(np.uint8),
         "random": lambda f: rng.integers(0, 256, n).astype(np.uint8),
         "same": lambda f: np.zeros(n, dtype=np.uint8),
+        "skewed": lambda f: np.where(rng.random(n) < 0.9, 0,
+                                     rng.integers(0, 256, n)).astype(np.uint8),
     }
     out = {"measure": "atomics", "rows": n, "features": F, "patterns": {}}
     p = {"objective": "binary", "num_leaves": 2, "min_data_in_leaf": 100,
@@ -837,18 +843,23 @@ def run_atomics(args):
         lab = y_c1 if name == "c1" else y
         maps = c1.mappers if name == "c1" else mappers
         ds = lgb.Dataset(bins=bins, mappers=maps, label=lab, params=p)
-        ms = []
-        for _ in range(max(3, args.steps)):
-            # the first iteration of a fresh booster: constant hessian, F atomics per row
-            b = lgb.Booster(p, ds)
-            spans, _ = b.profile_pipeline(1)
-            ms.append(spans["build"])
-            del b
-        t = min(ms)
-        out["patterns"][name] = {"build_ms": t, "atomics_per_s": n * F / (t / 1e3),
-                                 "atomics_per_sm_clock_at_1965mhz":
-                                     n * F / (t / 1e3) / (148 * 1.965e9),
-                                 "bytes_per_s": n * (F + 2) / (t / 1e3)}
+        for agg in ("0", "1"):
+            os.environ["LGBM_B200_WARP_AGG"] = agg
+            ms = []
+            digests = set()
+            for _ in range(max(3, args.steps)):
+                # the first iteration of a fresh booster: constant hessian, F atomics per row
+                b = lgb.Booster(p, ds)
+                spans, _ = b.profile_pipeline(1)
+                ms.append(spans["build"])
+                digests.add(tree_digest(b.trees()))
+                del b
+            t = min(ms)
+            out["patterns"][name + ("_warp_aggregated" if agg == "1" else "")] = {
+                "build_ms": t, "atomics_per_s": n * F / (t / 1e3),
+                "atomics_per_sm_clock_at_1965mhz": n * F / (t / 1e3) / (148 * 1.965e9),
+                "bytes_per_s": n * (F + 2) / (t / 1e3), "tree_digests": sorted(digests)}
+        os.environ.pop("LGBM_B200_WARP_AGG", None)
         del ds
     print(json.dumps(out), flush=True)
 

@@ -508,6 +508,7 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.F = ds->num_features;
   d.packed4 = ds->packed4;
   d.sliced = 0;  // every feature on this device (a data-parallel job may slice them)
+  if (const char* e = std::getenv("LGBM_B200_WARP_AGG")) d.warp_agg = std::strcmp(e, "1") == 0;
   d.slice_begin = 0;
   d.slice_end = d.F;
   d.bins = ds->bins.p;

@@ -503,7 +503,11 @@ constexpr int kQ4Chunk = 8191;  // |sum qg| <= 2*8191 and sum qh <= 4*8191 fit 1
 
 // MASKED: per-feature build mask on every chunk. Otherwise every feature of the group
 // is used and only the last chunk (features nf-16(NCH-1) .. 15 absent) is masked.
-template <int SHIFT, int NCH, bool MASKED>
+// AGG (measured, not the default): warp-aggregated atomics. The lanes that hold the same
+// bin of a feature are found with __match_any_sync, their packed words summed with
+// __reduce_add_sync over that group, and only the group's lowest lane adds the sum (and the
+// group's level-3 count). Sums of the same rows: the packed fields fold as before.
+template <int SHIFT, int NCH, bool MASKED, bool AGG = false>
 __device__ __forceinline__ void q4_row_regs(const uint4 (&w)[NCH], int32_t pv, bool is3,
                                             uint32_t* hot, const uint32_t* mask, uint32_t tail) {
 #pragma unroll
@@ -516,18 +520,29 @@ __device__ __forceinline__ void q4_row_regs(const uint4 (&w)[NCH], int32_t pv, b
       if (test && !((m16 >> j) & 1u)) continue;
       const uint32_t bin = (words[j >> 2] >> (8 * (j & 3))) & 0xffu;
       uint32_t* cell = hot + ((16 * ch + j) << SHIFT) + bin;
-      atomicAdd(reinterpret_cast<int*>(cell), pv);
-      if (is3) atomicAdd(cell + kQ4MaxCells, 1u);
+      if (AGG) {
+        const unsigned am = __activemask();
+        const unsigned grp = __match_any_sync(am, bin);
+        const int sum = __reduce_add_sync(grp, pv);
+        const unsigned n3 = (unsigned)__popc(__ballot_sync(am, is3) & grp);
+        if ((int)(threadIdx.x & 31) == __ffs(grp) - 1) {
+          atomicAdd(reinterpret_cast<int*>(cell), sum);
+          if (n3) atomicAdd(cell + kQ4MaxCells, n3);
+        }
+      } else {
+        atomicAdd(reinterpret_cast<int*>(cell), pv);
+        if (is3) atomicAdd(cell + kQ4MaxCells, 1u);
+      }
     }
   }
 }
 
-template <int SHIFT, int NCH, bool MASKED, bool PACK4>
+template <int SHIFT, int NCH, bool MASKED, bool PACK4, bool AGG = false>
 __device__ __forceinline__ void q4_row(const uint8_t* __restrict__ rp, int32_t pv, bool is3,
                                        uint32_t* hot, const uint32_t* mask, uint32_t tail) {
   uint4 w[NCH];
   load_row<NCH, PACK4>(rp, w);
-  q4_row_regs<SHIFT, NCH, MASKED>(w, pv, is3, hot, mask, tail);
+  q4_row_regs<SHIFT, NCH, MASKED, AGG>(w, pv, is3, hot, mask, tail);
 }
 
 // Build mask of one 128-feature group as four 32-bit words, and whether every feature of
@@ -557,7 +572,7 @@ __device__ __forceinline__ Q4Mask q4_mask(const uint32_t* s_mask, int nf) {
   return m;
 }
 
-template <int SHIFT, int NCH, bool PACK4>
+template <int SHIFT, int NCH, bool PACK4, bool AGG>
 __device__ __forceinline__ void build_q4_body(const GrowDev& d, int phase) {
   extern __shared__ uint32_t sm[];
   __shared__ uint32_t s_mask[4];
@@ -636,13 +651,15 @@ __device__ __forceinline__ void build_q4_body(const GrowDev& d, int phase) {
       const int qg0 = (int)(int8_t)(q0 & 0xff), qh0 = (int)(int8_t)(q0 >> 8);
       const int qg1 = (int)(int8_t)(q1 & 0xff), qh1 = (int)(int8_t)(q1 >> 8);
       if (full) {
-        q4_row<SHIFT, NCH, false, PACK4>(rp0, qg0 + (qh0 << 16), qh0 == 3, hot, mask, tail);
+        q4_row<SHIFT, NCH, false, PACK4, AGG>(rp0, qg0 + (qh0 << 16), qh0 == 3, hot, mask, tail);
         if (two)
-          q4_row<SHIFT, NCH, false, PACK4>(rp1, qg1 + (qh1 << 16), qh1 == 3, hot, mask, tail);
+          q4_row<SHIFT, NCH, false, PACK4, AGG>(rp1, qg1 + (qh1 << 16), qh1 == 3, hot, mask,
+                                                tail);
       } else {
-        q4_row<SHIFT, NCH, true, PACK4>(rp0, qg0 + (qh0 << 16), qh0 == 3, hot, mask, tail);
+        q4_row<SHIFT, NCH, true, PACK4, AGG>(rp0, qg0 + (qh0 << 16), qh0 == 3, hot, mask, tail);
         if (two)
-          q4_row<SHIFT, NCH, true, PACK4>(rp1, qg1 + (qh1 << 16), qh1 == 3, hot, mask, tail);
+          q4_row<SHIFT, NCH, true, PACK4, AGG>(rp1, qg1 + (qh1 << 16), qh1 == 3, hot, mask,
+                                               tail);
       }
     }
     if (ce < r1) {
@@ -680,16 +697,18 @@ __device__ __forceinline__ void build_q4_body(const GrowDev& d, int phase) {
   }
 }
 
-template <int SHIFT, int NCH, bool PACK4 = false>
+template <int SHIFT, int NCH, bool PACK4 = false, bool AGG = false>
 __global__ void __launch_bounds__(kQ4Threads, 2) k_build_q4(GrowDev d, int phase) {
   const SpanStamp span(d);
-  build_q4_body<SHIFT, NCH, PACK4>(d, phase);
+  build_q4_body<SHIFT, NCH, PACK4, AGG>(d, phase);
   producer_signal(d);
 }
 
 // (SHIFT, NCH) instantiations with (16 * (NCH - 1) + 1) << SHIFT <= kQ4MaxCells.
 using Q4Kernel = void (*)(GrowDev, int);
-__host__ Q4Kernel q4_kernel(int shift, int nch, bool pack4 = false) {
+__host__ Q4Kernel q4_kernel(int shift, int nch, bool pack4 = false, bool agg = false) {
+  // warp-aggregated atomics: one instantiation, the C1 layout (measured, not the default)
+  if (agg && !pack4 && shift == 8 && nch == 2) return k_build_q4<8, 2, false, true>;
   if (pack4) {  // 4-bit rows: every feature has at most 16 bins (shift 4)
 #define Q4P_CASE(N) \
   if (shift == 4 && nch == N) return k_build_q4<4, N, true>;
@@ -1376,60 +1395,78 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
 // Writes of the control step except the control block itself. CAT: the dataset has
 // categorical features, whose nodes also record their bin set.
 template <bool CAT>
-__device__ void prep_commit(const GrowDev& d, const Prep& P) {
+__device__ void prep_commit(const GrowDev& d, const Prep& P, int lane = -1) {
+  // lane >= 0: the lanes of one warp share the stores (section lane % 8); -1: all of them
+  auto mine = [&](int sec) { return lane < 0 || (lane & 7) == sec; };
   if (P.applied) {
     const int32_t leaf = P.leaf, nr = P.nr, node = P.node;
     const DevSplitInfo& b = P.c.split;
-    d.leaf_begin[nr] = P.beg + P.lc;
-    d.leaf_count[leaf] = P.lc;
-    d.leaf_count[nr] = P.rc;
-    d.leaf_count_g[leaf] = P.lcg;
-    d.leaf_count_g[nr] = P.rcg;
-    d.leaf_buf[leaf] = P.dst;
-    d.leaf_buf[nr] = P.dst;
-    // Tree::split (lgbm-model/src/tree.rs:614-690)
-    if (P.parent >= 0) {
-      if (P.parent_is_right)
-        d.t_right[P.parent] = node;
-      else
-        d.t_left[P.parent] = node;
+    if (mine(0)) {
+      d.leaf_begin[nr] = P.beg + P.lc;
+      d.leaf_count[leaf] = P.lc;
+      d.leaf_count[nr] = P.rc;
+      d.leaf_count_g[leaf] = P.lcg;
+      d.leaf_count_g[nr] = P.rcg;
+      d.leaf_buf[leaf] = P.dst;
+      d.leaf_buf[nr] = P.dst;
+      d.raw[d.raw_len] = 0;
     }
-    d.t_split_feature[node] = P.feature;
-    d.t_split_gain[node] = P.split_gain;
-    d.t_threshold[node] = P.cat_index >= 0 ? (uint32_t)P.cat_index : b.threshold;
-    if (CAT)
-      for (int k = 0; k < kCatWords; ++k)
-        d.t_cat[(size_t)node * kCatWords + k] = P.cat_index >= 0 ? d.split_cat[k] : 0u;
-    d.t_internal_value[node] = P.old_value;
-    d.t_internal_count[node] = P.lcg + P.rcg;
-    d.t_left[node] = ~leaf;
-    d.t_right[node] = ~nr;
-    d.t_decision[node] = P.dt;
-    d.t_leaf_value[leaf] = b.left_output;
-    d.t_leaf_weight[leaf] = b.left_sum_hessian;
-    d.t_leaf_count[leaf] = P.lcg;
-    d.t_leaf_value[nr] = b.right_output;
-    d.t_leaf_weight[nr] = b.right_sum_hessian;
-    d.t_leaf_count[nr] = P.rcg;
-    d.t_leaf_depth[nr] = P.depth + 1;
-    d.t_leaf_depth[leaf] = P.depth + 1;
-    d.t_leaf_parent[leaf] = node;
-    d.t_leaf_parent[nr] = node;
-    d.leaf_is_right[leaf] = 0;  // the split leaf keeps its id as the left child
-    d.leaf_is_right[nr] = 1;
-    d.ls[leaf] = P.lsL;
-    d.ls[nr] = P.lsR;
-    d.best[leaf] = d_split_none();
-    d.best_feature[leaf] = -1;
-    d.best[nr] = d_split_none();
-    d.best_feature[nr] = -1;
-    d.raw[d.raw_len] = 0;
+    // Tree::split (lgbm-model/src/tree.rs:614-690)
+    if (mine(1)) {
+      if (P.parent >= 0) {
+        if (P.parent_is_right)
+          d.t_right[P.parent] = node;
+        else
+          d.t_left[P.parent] = node;
+      }
+      d.t_split_feature[node] = P.feature;
+      d.t_split_gain[node] = P.split_gain;
+      d.t_threshold[node] = P.cat_index >= 0 ? (uint32_t)P.cat_index : b.threshold;
+      if (CAT)
+        for (int k = 0; k < kCatWords; ++k)
+          d.t_cat[(size_t)node * kCatWords + k] = P.cat_index >= 0 ? d.split_cat[k] : 0u;
+    }
+    if (mine(2)) {
+      d.t_internal_value[node] = P.old_value;
+      d.t_internal_count[node] = P.lcg + P.rcg;
+      d.t_left[node] = ~leaf;
+      d.t_right[node] = ~nr;
+      d.t_decision[node] = P.dt;
+    }
+    if (mine(3)) {
+      d.t_leaf_value[leaf] = b.left_output;
+      d.t_leaf_weight[leaf] = b.left_sum_hessian;
+      d.t_leaf_count[leaf] = P.lcg;
+      d.t_leaf_value[nr] = b.right_output;
+      d.t_leaf_weight[nr] = b.right_sum_hessian;
+      d.t_leaf_count[nr] = P.rcg;
+    }
+    if (mine(4)) {
+      d.t_leaf_depth[nr] = P.depth + 1;
+      d.t_leaf_depth[leaf] = P.depth + 1;
+      d.t_leaf_parent[leaf] = node;
+      d.t_leaf_parent[nr] = node;
+      d.leaf_is_right[leaf] = 0;  // the split leaf keeps its id as the left child
+      d.leaf_is_right[nr] = 1;
+    }
+    if (mine(5)) {
+      d.ls[leaf] = P.lsL;
+      d.ls[nr] = P.lsR;
+    }
+    if (mine(6)) {
+      d.best[leaf] = d_split_none();
+      d.best_feature[leaf] = -1;
+      d.best[nr] = d_split_none();
+      d.best_feature[nr] = -1;
+    }
   }
-  if (P.la_clear >= 0) d.la_raw[(size_t)P.la_clear * (d.raw_len + 2) + d.raw_len] = 0;
-  if (P.kill0 >= 0) d.best[P.kill0].gain = kNegInf;
-  if (P.kill1 >= 0) d.best[P.kill1].gain = kNegInf;
-  if (P.slot_leaf0 >= 0) d.slot_of_leaf[P.slot_leaf0] = P.slot_val0;
-  if (P.slot_leaf1 >= 0) d.slot_of_leaf[P.slot_leaf1] = P.slot_val1;
+  if (mine(7)) {
+    if (P.la_clear >= 0) d.la_raw[(size_t)P.la_clear * (d.raw_len + 2) + d.raw_len] = 0;
+    if (P.kill0 >= 0) d.best[P.kill0].gain = kNegInf;
+    if (P.kill1 >= 0) d.best[P.kill1].gain = kNegInf;
+    if (P.slot_leaf0 >= 0) d.slot_of_leaf[P.slot_leaf0] = P.slot_val0;
+    if (P.slot_leaf1 >= 0) d.slot_of_leaf[P.slot_leaf1] = P.slot_val1;
+  }
 }
 
 // The control step alone: applies the tree's last split.
@@ -1605,6 +1642,8 @@ struct CtlSmem {
   uint32_t err;                   // the control block's error bits, read by the last CTA
   uint8_t ok[2];                  // the scanned leaves' scan flags
   PickOut pick;
+  GrowCtrl cout;                  // the control block this step writes
+  LookAhead lout;                 // ... and its look-ahead record
   bool last;
   int32_t wide;                   // the features' argmax was taken by the whole CTA ...
   Cand wbest[2];                  // ... into these (smaller / larger scanned leaf)
@@ -1981,51 +2020,55 @@ __device__ void cat_scan(const double* hist, const DevFeature& ft, const DevGain
       keep = (double)d_round_int(hist[2 * t + 1] * cf) >= cfg.cat_smooth;
       ctr = hist[2 * t] / (hist[2 * t + 1] + cfg.cat_smooth);
     }
-    s.pg[gt] = ctr;
-    s.pc[gt] = keep ? 1 : 0;
+    // The reference's stable sort by ctr (sort_by with partial_cmp, unordered as Equal; an
+    // insertion sort on up to 20 elements): a category moves left past every neighbour with
+    // a strictly greater ctr. A NaN ctr (0/0: cat_smooth 0 and a category without rows in
+    // this leaf) is ordered with nothing, so it keeps its place among the kept categories
+    // and the runs on either side of it are sorted apart. As one total order: key (run,
+    // ctr, bin), where a category's run counts the NaNs kept before it and a NaN category
+    // opens the run after its own (ctr -inf, first in that run); the bin breaks ties in
+    // kept order. A bitonic sort of the 256 keys by the group, 36 compare-exchange stages.
+    const bool nan_me = keep && isnan(ctr);
+    const unsigned lt = (1u << lane) - 1u;
+    const unsigned kb = __ballot_sync(0xffffffffu, keep);
+    const unsigned nb = __ballot_sync(0xffffffffu, nan_me);
+    if (lane == 0) {
+      s.wsum[wg] = __popc(kb);
+      s.wpre[wg] = __popc(nb);
+    }
     group_sync(bar_id);
-    // Place in the reference's stable sort by ctr (sort_by with partial_cmp, unordered as
-    // Equal; an insertion sort on up to 20 elements): a category moves left past every
-    // neighbour with a strictly greater ctr. A NaN ctr (0/0: cat_smooth 0 and a category
-    // without rows in this leaf) is ordered with nothing, so it keeps its place among the
-    // kept categories and the runs on either side of it are sorted apart. Rank = start of
-    // this category's run + the run's members that precede it.
-    const bool nan_me = isnan(ctr);
-    int pos = 0, lo = 0, less = 0;
-    bool past = false, stop = false;
-    // eight categories at a time, their shared-memory loads issued together
-    for (int u0 = 0; u0 < nscan; u0 += 8) {
-      int32_t kp[8];
-      double cv[8];
+    int nan_before = __popc(nb & lt);
+    used = 0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {  // u < kMaxBins: in the arrays even past nscan
-        kp[j] = u0 + j < nscan ? s.pc[u0 + j] : 0;
-        cv[j] = s.pg[u0 + j];
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (!kp[j]) continue;
-        const int u = u0 + j;
-        const double cu = cv[j];
-        if (u == gt) {
-          pos = used;
-          past = true;
-        } else if (isnan(cu)) {
-          if (!past) {
-            lo = used + 1;  // a NaN before this category closes the run before it
-            less = 0;
-          } else {
-            stop = true;  // ... and one after it closes its run
+    for (int w = 0; w < kScanGroup / 32; ++w) {
+      used += s.wsum[w];
+      if (w < wg) nan_before += s.wpre[w];
+    }
+    const int run = nan_me ? nan_before + 1 : nan_before;
+    s.pg[gt] = nan_me ? kNegInf : ctr;
+    s.pc[gt] = keep ? (run << 9) | t : 0x7ffffe00 | gt;  // left out: last
+    group_sync(bar_id);
+    for (int k = 2; k <= kScanGroup; k <<= 1) {
+      for (int jj = k >> 1; jj > 0; jj >>= 1) {
+        const int o = gt ^ jj;
+        if (o > gt) {
+          const int32_t ka = s.pc[gt], kbb = s.pc[o];
+          const double ca = s.pg[gt], cb = s.pg[o];
+          const int ra = ka >> 9, rb = kbb >> 9;
+          // a after b: a higher run, or the same run and a higher ctr, or equal ctr and a
+          // later bin
+          const bool after = ra != rb ? ra > rb : (ca != cb ? ca > cb : (ka & 511) > (kbb & 511));
+          if (after == ((gt & k) == 0)) {
+            s.pc[gt] = kbb;
+            s.pc[o] = ka;
+            s.pg[gt] = cb;
+            s.pg[o] = ca;
           }
-        } else if (!stop && (cu < ctr || (cu == ctr && u < gt))) {
-          ++less;
         }
-        ++used;
+        group_sync(bar_id);
       }
     }
-    const int rank = nan_me ? pos : lo + less;
-    group_sync(bar_id);
-    if (keep) sorted[rank] = t;
+    if (gt < used) sorted[gt] = s.pc[gt] & 511;
     group_sync(bar_id);
     if (gt == 0 || gt == 32) {
       const int di = gt == 0 ? 0 : 1;
@@ -2362,6 +2405,8 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
 constexpr int kStageFeatures =
     (int)(sizeof(FixScanSmem) / (2 * (sizeof(DevSplitInfo) + kCatWords * sizeof(uint32_t))));
 static_assert(sizeof(DevSplitInfo) % 8 == 0, "scan results are copied as 8-byte words");
+static_assert(sizeof(GrowCtrl) % 8 == 0 && sizeof(LookAhead) % 8 == 0,
+              "the control block and look-ahead records are stored as 8-byte words");
 
 // One control step by the CTAs [0, min(F, gridDim.x)), each taking features
 // blockIdx.x, blockIdx.x + gridDim.x, ...: apply the pending split, scan the two leaves,
@@ -2458,7 +2503,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
       cs.la_prev = lp;
     }
   }
-  if (warp == 1 && (tid & 31) == 0) prep_commit<CAT>(d, P);
+  if (warp == 1 && (tid & 31) < 8) prep_commit<CAT>(d, P, tid & 31);
   // wide slices: the features' argmax by the whole CTA (its gain loads issued together)
   const bool wide = !staged && P.live && !P.c.done && (fe - fb) > kWidePick;
   if (tid == 0) cs.wide = wide ? 1 : 0;
@@ -2500,27 +2545,17 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
       prefetch_l2_bulk(base + off, min(kChunk, bytes - off));
     }
   }
-  if (tid == 0) {
-    GrowCtrl c = P.c;
-    c.scan_counter = 0;
-    if (!c.done) {
-      if (P.live) {
-        d.best[P.S] = cs.pick.si[0];
-        d.best_feature[P.S] = cs.pick.bf[0];
-        if (CAT)
-          for (int k = 0; k < kCatWords; ++k)
-            d.best_cat[(size_t)P.S * kCatWords + k] = cs.pick.si_cat[0][k];
-        if (P.Lg >= 0) {
-          d.best[P.Lg] = cs.pick.si[1];
-          d.best_feature[P.Lg] = cs.pick.bf[1];
-          if (CAT)
-            for (int k = 0; k < kCatWords; ++k)
-              d.best_cat[(size_t)P.Lg * kCatWords + k] = cs.pick.si_cat[1][k];
-        }
-      }
-      if (cs.pick.done) {
-        c.done = 1;
-      } else {
+  // The step's writes by warp 0: lane 0 composes the control block and the look-ahead
+  // record in shared memory, then the warp stores them, and the scanned leaves' best
+  // splits, as 8-byte words (a few coalesced stores instead of one thread's long run).
+  if (warp == 0) {
+    const int lane = tid & 31;
+    const bool lrec = d.lookahead && s <= d.L - 3;
+    if (lane == 0) {
+      GrowCtrl& c = cs.cout;
+      c = P.c;
+      c.scan_counter = 0;
+      if (!c.done && !cs.pick.done) {
         c.pending = 1;
         c.split_leaf = cs.pick.leaf;
         c.split_feature = cs.pick.feature;
@@ -2532,29 +2567,63 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
         // running; the step that applies the split waits for it)
         if (d.lookahead && s >= 1 && cs.la_prev == cs.pick.leaf)
           c.pend_la = 1 + ((s - 1) & (kLaSlots - 1));
+      } else if (!c.done) {
+        c.done = 1;
+      }
+      c.error |= cs.err;
+      if (!P.c.done && cs.pick.xerr) c.error |= kErrSpinTimeout;
+      if (c.error & kErrSpinTimeout) c.done = 1;  // a rank stopped answering: end the tree
+      // this step's look-ahead: the runner-up of the pick (its kernel runs next to the
+      // following control step; its slot was consumed and cleared above)
+      if (lrec) {
+        LookAhead& r = cs.lout;
+        r = LookAhead{};
+        r.epoch = c.epoch;
+        if (!c.done && c.pending && cs.pick.la_leaf >= 0) {
+          r.active = 1;
+          r.leaf = cs.pick.la_leaf;
+          r.feature = cs.pick.la_feature;
+          r.build = s < d.L - 3 ? 1 : 0;  // the last look-ahead feeds no scan
+          r.build_left = cs.pick.la_build_left;
+          r.split = cs.pick.la_split;
+          if (CAT)
+            for (int k = 0; k < kCatWords; ++k) r.cat[k] = cs.pick.la_cat[k];
+        }
       }
     }
-    c.error |= cs.err;
-    if (!P.c.done && cs.pick.xerr) c.error |= kErrSpinTimeout;
-    if (c.error & kErrSpinTimeout) c.done = 1;  // a rank stopped answering: end the tree
-    // this step's look-ahead: the runner-up of the pick (its kernel runs next to the
-    // following control step; slot s % 2 was consumed and cleared above)
-    if (d.lookahead && s <= d.L - 3) {
-      LookAhead r{};
-      r.epoch = c.epoch;
-      if (!c.done && c.pending && cs.pick.la_leaf >= 0) {
-        r.active = 1;
-        r.leaf = cs.pick.la_leaf;
-        r.feature = cs.pick.la_feature;
-        r.build = s < d.L - 3 ? 1 : 0;  // the last look-ahead feeds no scan
-        r.build_left = cs.pick.la_build_left;
-        r.split = cs.pick.la_split;
-        if (CAT)
-          for (int k = 0; k < kCatWords; ++k) r.cat[k] = cs.pick.la_cat[k];
+    __syncwarp();
+    // the scanned leaves' best splits (P.c.done: no scan this step)
+    if (!P.c.done && P.live) {
+      constexpr int kW = (int)(sizeof(DevSplitInfo) / 8);
+      for (int k = lane; k < 2 * kW; k += 32) {
+        const int which = k / kW;
+        const int32_t leaf = which == 0 ? P.S : P.Lg;
+        if (leaf < 0) continue;
+        reinterpret_cast<unsigned long long*>(d.best + leaf)[k % kW] =
+            reinterpret_cast<const unsigned long long*>(&cs.pick.si[which])[k % kW];
       }
-      d.la[s & (kLaSlots - 1)] = r;
+      if (lane < 2) {
+        const int32_t leaf = lane == 0 ? P.S : P.Lg;
+        if (leaf >= 0) d.best_feature[leaf] = cs.pick.bf[lane];
+      }
+      if (CAT)
+        for (int k = lane; k < 2 * kCatWords; k += 32) {
+          const int32_t leaf = k < kCatWords ? P.S : P.Lg;
+          if (leaf >= 0)
+            d.best_cat[(size_t)leaf * kCatWords + (k % kCatWords)] =
+                cs.pick.si_cat[k / kCatWords][k % kCatWords];
+        }
     }
-    *d.ctrl = c;
+    if (lrec) {
+      constexpr int kL = (int)(sizeof(LookAhead) / 8);
+      for (int k = lane; k < kL; k += 32)
+        reinterpret_cast<unsigned long long*>(d.la + (s & (kLaSlots - 1)))[k] =
+            reinterpret_cast<const unsigned long long*>(&cs.lout)[k];
+    }
+    constexpr int kC = (int)(sizeof(GrowCtrl) / 8);
+    for (int k = lane; k < kC; k += 32)
+      reinterpret_cast<unsigned long long*>(d.ctrl)[k] =
+          reinterpret_cast<const unsigned long long*>(&cs.cout)[k];
   }
   ctl_mark(d, s, CP_WRITTEN);
 }
@@ -3365,8 +3434,8 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
   auto build = [&](const GrowDev& x, int phase) {
     PROF_BEGIN(KC_BUILD);
     if (x.gh_mode == GH_QPACK)
-      q4_kernel(x.q4_shift, x.q4_nch, x.packed4 != 0)<<<bgrid, kQ4Threads, build_smem, st>>>(
-          x, phase);
+      q4_kernel(x.q4_shift, x.q4_nch, x.packed4 != 0, x.warp_agg != 0)<<<bgrid, kQ4Threads,
+                                                                      build_smem, st>>>(x, phase);
     else if (x.gh_mode == GH_QLUT)
       k_build<GH_QLUT><<<bgrid, kBuildThreads, build_smem, st>>>(x, phase);
     else
@@ -3477,11 +3546,12 @@ void set_build_smem_limit(size_t bytes) {
   for (int sh = 4; sh <= 8; ++sh)
     for (int n = 1; n <= 8; ++n)
       for (bool p4 : {false, true})
-        if (q4_kernel(sh, n, p4)) {
-          cudaFuncSetAttribute(q4_kernel(sh, n, p4), cudaFuncAttributeMaxDynamicSharedMemorySize,
+        for (bool agg : {false, true}) {
+          const Q4Kernel k = q4_kernel(sh, n, p4, agg);
+          if (!k) continue;
+          cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)(4 * sizeof(uint32_t) * kQ4MaxCells));
-          cudaFuncSetAttribute(q4_kernel(sh, n, p4),
-                               cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+          cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         }
   for (int sh = 4; sh <= 8; ++sh)
     for (int n = 1; n <= kFpMaxChunks; ++n)

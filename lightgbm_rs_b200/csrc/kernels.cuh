@@ -143,6 +143,8 @@ struct GrowDev {
   // two kinds' CTA arrival counters (zero between launches).
   int32_t self_signal;
   uint32_t* arrive;
+  // Histogram builds with warp-aggregated atomics (LGBM_B200_WARP_AGG=1; the C1 layout only).
+  int32_t warp_agg;
   long long xwait_ns;                         // wait limit, then the spin-timeout error
   // Look-ahead partitions (fused partition): control step s records slot s % kLaSlots and
   // its look-ahead kernel fills it; control step s + 2 consumes it (when step s + 1 picked

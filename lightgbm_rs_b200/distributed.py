@@ -5,8 +5,11 @@ shard of the rows; after each histogram build the ranks sum the integer child hi
 and its left-row count inside the library -- over peer memory (CUDA IPC mappings of
 every rank's accumulators, plain loads, bounded waits) when all ranks can map each
 other, else with one NCCL all-reduce per split -- so all ranks grow identical trees.
-The gradient step's scale maxima and root sums are NCCL reductions. The reference maps tree_learner=data back to serial
-(crates/lgbm-core/src/config/set.rs:592-600); this module has no counterpart there.
+With wide data (at least 128 features per rank) each rank decodes and scans only its slice
+of the features, and the slices' best splits are exchanged before every rank takes the
+same pick. The gradient step's scale maxima and root sums are NCCL reductions. The
+reference maps tree_learner=data back to serial (crates/lgbm-core/src/config/set.rs:
+592-600); this module has no counterpart there.
 
 The NCCL id is made on rank 0 and handed to the other ranks out of band; with
 torch.distributed already initialised (any backend, e.g. gloo), `from_torch` does that.

@@ -372,3 +372,32 @@ def test_wide_c2_shape_bit_exact():
     for i, (a, b) in enumerate(zip(trees, ref["trees"])):
         _assert_trees_bit_equal(a, b, f"tree {i}")
     assert booster.train_scores().tobytes() == ref["scores"].tobytes()
+
+
+def test_warp_aggregated_build_same_trees():
+    """The measured-only warp-aggregated histogram build (LGBM_B200_WARP_AGG=1, the
+    255-bin, 28-feature layout) grows the same trees and scores as the default build, on
+    data with a heavily skewed feature (most lanes of a warp share a bin)."""
+    import os
+
+    import lightgbm_rs_b200 as lgb
+    from lightgbm_rs_b200 import synthetic
+
+    X, y = synthetic.binary_c0(num_data=60_000, num_features=28, seed=11)
+    X[np.random.default_rng(2).random(len(y)) < 0.8, 3] = 0.0
+    ds = lgb.Dataset(X, y, {"max_bin": 255})
+    p = {"objective": "binary", "num_leaves": 63, "use_quantized_grad": True,
+         "num_grad_quant_bins": 4}
+    out = []
+    for agg in ("0", "1"):
+        os.environ["LGBM_B200_WARP_AGG"] = agg
+        try:
+            b = lgb.train(p, ds, num_boost_round=3)
+        finally:
+            os.environ.pop("LGBM_B200_WARP_AGG", None)
+        out.append((b.trees(), b.train_scores()))
+    for a, w in zip(out[0][0], out[1][0]):
+        for k in ("split_feature", "threshold_bin", "left_child", "right_child", "leaf_count"):
+            assert np.asarray(a[k]).tolist() == np.asarray(w[k]).tolist(), k
+        assert np.asarray(a["leaf_value"]).tobytes() == np.asarray(w["leaf_value"]).tobytes()
+    assert out[0][1].tobytes() == out[1][1].tobytes()
