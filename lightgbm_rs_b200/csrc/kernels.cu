@@ -1395,78 +1395,60 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
 // Writes of the control step except the control block itself. CAT: the dataset has
 // categorical features, whose nodes also record their bin set.
 template <bool CAT>
-__device__ void prep_commit(const GrowDev& d, const Prep& P, int lane = -1) {
-  // lane >= 0: the lanes of one warp share the stores (section lane % 8); -1: all of them
-  auto mine = [&](int sec) { return lane < 0 || (lane & 7) == sec; };
+__device__ void prep_commit(const GrowDev& d, const Prep& P) {
   if (P.applied) {
     const int32_t leaf = P.leaf, nr = P.nr, node = P.node;
     const DevSplitInfo& b = P.c.split;
-    if (mine(0)) {
-      d.leaf_begin[nr] = P.beg + P.lc;
-      d.leaf_count[leaf] = P.lc;
-      d.leaf_count[nr] = P.rc;
-      d.leaf_count_g[leaf] = P.lcg;
-      d.leaf_count_g[nr] = P.rcg;
-      d.leaf_buf[leaf] = P.dst;
-      d.leaf_buf[nr] = P.dst;
-      d.raw[d.raw_len] = 0;
-    }
+    d.leaf_begin[nr] = P.beg + P.lc;
+    d.leaf_count[leaf] = P.lc;
+    d.leaf_count[nr] = P.rc;
+    d.leaf_count_g[leaf] = P.lcg;
+    d.leaf_count_g[nr] = P.rcg;
+    d.leaf_buf[leaf] = P.dst;
+    d.leaf_buf[nr] = P.dst;
     // Tree::split (lgbm-model/src/tree.rs:614-690)
-    if (mine(1)) {
-      if (P.parent >= 0) {
-        if (P.parent_is_right)
-          d.t_right[P.parent] = node;
-        else
-          d.t_left[P.parent] = node;
-      }
-      d.t_split_feature[node] = P.feature;
-      d.t_split_gain[node] = P.split_gain;
-      d.t_threshold[node] = P.cat_index >= 0 ? (uint32_t)P.cat_index : b.threshold;
-      if (CAT)
-        for (int k = 0; k < kCatWords; ++k)
-          d.t_cat[(size_t)node * kCatWords + k] = P.cat_index >= 0 ? d.split_cat[k] : 0u;
+    if (P.parent >= 0) {
+      if (P.parent_is_right)
+        d.t_right[P.parent] = node;
+      else
+        d.t_left[P.parent] = node;
     }
-    if (mine(2)) {
-      d.t_internal_value[node] = P.old_value;
-      d.t_internal_count[node] = P.lcg + P.rcg;
-      d.t_left[node] = ~leaf;
-      d.t_right[node] = ~nr;
-      d.t_decision[node] = P.dt;
-    }
-    if (mine(3)) {
-      d.t_leaf_value[leaf] = b.left_output;
-      d.t_leaf_weight[leaf] = b.left_sum_hessian;
-      d.t_leaf_count[leaf] = P.lcg;
-      d.t_leaf_value[nr] = b.right_output;
-      d.t_leaf_weight[nr] = b.right_sum_hessian;
-      d.t_leaf_count[nr] = P.rcg;
-    }
-    if (mine(4)) {
-      d.t_leaf_depth[nr] = P.depth + 1;
-      d.t_leaf_depth[leaf] = P.depth + 1;
-      d.t_leaf_parent[leaf] = node;
-      d.t_leaf_parent[nr] = node;
-      d.leaf_is_right[leaf] = 0;  // the split leaf keeps its id as the left child
-      d.leaf_is_right[nr] = 1;
-    }
-    if (mine(5)) {
-      d.ls[leaf] = P.lsL;
-      d.ls[nr] = P.lsR;
-    }
-    if (mine(6)) {
-      d.best[leaf] = d_split_none();
-      d.best_feature[leaf] = -1;
-      d.best[nr] = d_split_none();
-      d.best_feature[nr] = -1;
-    }
+    d.t_split_feature[node] = P.feature;
+    d.t_split_gain[node] = P.split_gain;
+    d.t_threshold[node] = P.cat_index >= 0 ? (uint32_t)P.cat_index : b.threshold;
+    if (CAT)
+      for (int k = 0; k < kCatWords; ++k)
+        d.t_cat[(size_t)node * kCatWords + k] = P.cat_index >= 0 ? d.split_cat[k] : 0u;
+    d.t_internal_value[node] = P.old_value;
+    d.t_internal_count[node] = P.lcg + P.rcg;
+    d.t_left[node] = ~leaf;
+    d.t_right[node] = ~nr;
+    d.t_decision[node] = P.dt;
+    d.t_leaf_value[leaf] = b.left_output;
+    d.t_leaf_weight[leaf] = b.left_sum_hessian;
+    d.t_leaf_count[leaf] = P.lcg;
+    d.t_leaf_value[nr] = b.right_output;
+    d.t_leaf_weight[nr] = b.right_sum_hessian;
+    d.t_leaf_count[nr] = P.rcg;
+    d.t_leaf_depth[nr] = P.depth + 1;
+    d.t_leaf_depth[leaf] = P.depth + 1;
+    d.t_leaf_parent[leaf] = node;
+    d.t_leaf_parent[nr] = node;
+    d.leaf_is_right[leaf] = 0;  // the split leaf keeps its id as the left child
+    d.leaf_is_right[nr] = 1;
+    d.ls[leaf] = P.lsL;
+    d.ls[nr] = P.lsR;
+    d.best[leaf] = d_split_none();
+    d.best_feature[leaf] = -1;
+    d.best[nr] = d_split_none();
+    d.best_feature[nr] = -1;
+    d.raw[d.raw_len] = 0;
   }
-  if (mine(7)) {
-    if (P.la_clear >= 0) d.la_raw[(size_t)P.la_clear * (d.raw_len + 2) + d.raw_len] = 0;
-    if (P.kill0 >= 0) d.best[P.kill0].gain = kNegInf;
-    if (P.kill1 >= 0) d.best[P.kill1].gain = kNegInf;
-    if (P.slot_leaf0 >= 0) d.slot_of_leaf[P.slot_leaf0] = P.slot_val0;
-    if (P.slot_leaf1 >= 0) d.slot_of_leaf[P.slot_leaf1] = P.slot_val1;
-  }
+  if (P.la_clear >= 0) d.la_raw[(size_t)P.la_clear * (d.raw_len + 2) + d.raw_len] = 0;
+  if (P.kill0 >= 0) d.best[P.kill0].gain = kNegInf;
+  if (P.kill1 >= 0) d.best[P.kill1].gain = kNegInf;
+  if (P.slot_leaf0 >= 0) d.slot_of_leaf[P.slot_leaf0] = P.slot_val0;
+  if (P.slot_leaf1 >= 0) d.slot_of_leaf[P.slot_leaf1] = P.slot_val1;
 }
 
 // The control step alone: applies the tree's last split.
@@ -1642,8 +1624,6 @@ struct CtlSmem {
   uint32_t err;                   // the control block's error bits, read by the last CTA
   uint8_t ok[2];                  // the scanned leaves' scan flags
   PickOut pick;
-  GrowCtrl cout;                  // the control block this step writes
-  LookAhead lout;                 // ... and its look-ahead record
   bool last;
   int32_t wide;                   // the features' argmax was taken by the whole CTA ...
   Cand wbest[2];                  // ... into these (smaller / larger scanned leaf)
@@ -2405,8 +2385,6 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
 constexpr int kStageFeatures =
     (int)(sizeof(FixScanSmem) / (2 * (sizeof(DevSplitInfo) + kCatWords * sizeof(uint32_t))));
 static_assert(sizeof(DevSplitInfo) % 8 == 0, "scan results are copied as 8-byte words");
-static_assert(sizeof(GrowCtrl) % 8 == 0 && sizeof(LookAhead) % 8 == 0,
-              "the control block and look-ahead records are stored as 8-byte words");
 
 // One control step by the CTAs [0, min(F, gridDim.x)), each taking features
 // blockIdx.x, blockIdx.x + gridDim.x, ...: apply the pending split, scan the two leaves,
@@ -2503,7 +2481,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
       cs.la_prev = lp;
     }
   }
-  if (warp == 1 && (tid & 31) < 8) prep_commit<CAT>(d, P, tid & 31);
+  if (warp == 1 && (tid & 31) == 0) prep_commit<CAT>(d, P);
   // wide slices: the features' argmax by the whole CTA (its gain loads issued together)
   const bool wide = !staged && P.live && !P.c.done && (fe - fb) > kWidePick;
   if (tid == 0) cs.wide = wide ? 1 : 0;
@@ -2545,17 +2523,27 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
       prefetch_l2_bulk(base + off, min(kChunk, bytes - off));
     }
   }
-  // The step's writes by warp 0: lane 0 composes the control block and the look-ahead
-  // record in shared memory, then the warp stores them, and the scanned leaves' best
-  // splits, as 8-byte words (a few coalesced stores instead of one thread's long run).
-  if (warp == 0) {
-    const int lane = tid & 31;
-    const bool lrec = d.lookahead && s <= d.L - 3;
-    if (lane == 0) {
-      GrowCtrl& c = cs.cout;
-      c = P.c;
-      c.scan_counter = 0;
-      if (!c.done && !cs.pick.done) {
+  if (tid == 0) {
+    GrowCtrl c = P.c;
+    c.scan_counter = 0;
+    if (!c.done) {
+      if (P.live) {
+        d.best[P.S] = cs.pick.si[0];
+        d.best_feature[P.S] = cs.pick.bf[0];
+        if (CAT)
+          for (int k = 0; k < kCatWords; ++k)
+            d.best_cat[(size_t)P.S * kCatWords + k] = cs.pick.si_cat[0][k];
+        if (P.Lg >= 0) {
+          d.best[P.Lg] = cs.pick.si[1];
+          d.best_feature[P.Lg] = cs.pick.bf[1];
+          if (CAT)
+            for (int k = 0; k < kCatWords; ++k)
+              d.best_cat[(size_t)P.Lg * kCatWords + k] = cs.pick.si_cat[1][k];
+        }
+      }
+      if (cs.pick.done) {
+        c.done = 1;
+      } else {
         c.pending = 1;
         c.split_leaf = cs.pick.leaf;
         c.split_feature = cs.pick.feature;
@@ -2567,63 +2555,29 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
         // running; the step that applies the split waits for it)
         if (d.lookahead && s >= 1 && cs.la_prev == cs.pick.leaf)
           c.pend_la = 1 + ((s - 1) & (kLaSlots - 1));
-      } else if (!c.done) {
-        c.done = 1;
-      }
-      c.error |= cs.err;
-      if (!P.c.done && cs.pick.xerr) c.error |= kErrSpinTimeout;
-      if (c.error & kErrSpinTimeout) c.done = 1;  // a rank stopped answering: end the tree
-      // this step's look-ahead: the runner-up of the pick (its kernel runs next to the
-      // following control step; its slot was consumed and cleared above)
-      if (lrec) {
-        LookAhead& r = cs.lout;
-        r = LookAhead{};
-        r.epoch = c.epoch;
-        if (!c.done && c.pending && cs.pick.la_leaf >= 0) {
-          r.active = 1;
-          r.leaf = cs.pick.la_leaf;
-          r.feature = cs.pick.la_feature;
-          r.build = s < d.L - 3 ? 1 : 0;  // the last look-ahead feeds no scan
-          r.build_left = cs.pick.la_build_left;
-          r.split = cs.pick.la_split;
-          if (CAT)
-            for (int k = 0; k < kCatWords; ++k) r.cat[k] = cs.pick.la_cat[k];
-        }
       }
     }
-    __syncwarp();
-    // the scanned leaves' best splits (P.c.done: no scan this step)
-    if (!P.c.done && P.live) {
-      constexpr int kW = (int)(sizeof(DevSplitInfo) / 8);
-      for (int k = lane; k < 2 * kW; k += 32) {
-        const int which = k / kW;
-        const int32_t leaf = which == 0 ? P.S : P.Lg;
-        if (leaf < 0) continue;
-        reinterpret_cast<unsigned long long*>(d.best + leaf)[k % kW] =
-            reinterpret_cast<const unsigned long long*>(&cs.pick.si[which])[k % kW];
+    c.error |= cs.err;
+    if (!P.c.done && cs.pick.xerr) c.error |= kErrSpinTimeout;
+    if (c.error & kErrSpinTimeout) c.done = 1;  // a rank stopped answering: end the tree
+    // this step's look-ahead: the runner-up of the pick (its kernel runs next to the
+    // following control step; slot s % 2 was consumed and cleared above)
+    if (d.lookahead && s <= d.L - 3) {
+      LookAhead r{};
+      r.epoch = c.epoch;
+      if (!c.done && c.pending && cs.pick.la_leaf >= 0) {
+        r.active = 1;
+        r.leaf = cs.pick.la_leaf;
+        r.feature = cs.pick.la_feature;
+        r.build = s < d.L - 3 ? 1 : 0;  // the last look-ahead feeds no scan
+        r.build_left = cs.pick.la_build_left;
+        r.split = cs.pick.la_split;
+        if (CAT)
+          for (int k = 0; k < kCatWords; ++k) r.cat[k] = cs.pick.la_cat[k];
       }
-      if (lane < 2) {
-        const int32_t leaf = lane == 0 ? P.S : P.Lg;
-        if (leaf >= 0) d.best_feature[leaf] = cs.pick.bf[lane];
-      }
-      if (CAT)
-        for (int k = lane; k < 2 * kCatWords; k += 32) {
-          const int32_t leaf = k < kCatWords ? P.S : P.Lg;
-          if (leaf >= 0)
-            d.best_cat[(size_t)leaf * kCatWords + (k % kCatWords)] =
-                cs.pick.si_cat[k / kCatWords][k % kCatWords];
-        }
+      d.la[s & (kLaSlots - 1)] = r;
     }
-    if (lrec) {
-      constexpr int kL = (int)(sizeof(LookAhead) / 8);
-      for (int k = lane; k < kL; k += 32)
-        reinterpret_cast<unsigned long long*>(d.la + (s & (kLaSlots - 1)))[k] =
-            reinterpret_cast<const unsigned long long*>(&cs.lout)[k];
-    }
-    constexpr int kC = (int)(sizeof(GrowCtrl) / 8);
-    for (int k = lane; k < kC; k += 32)
-      reinterpret_cast<unsigned long long*>(d.ctrl)[k] =
-          reinterpret_cast<const unsigned long long*>(&cs.cout)[k];
+    *d.ctrl = c;
   }
   ctl_mark(d, s, CP_WRITTEN);
 }
