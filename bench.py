@@ -718,9 +718,10 @@ def run_ours(args):
 
 
 def run_binning(args):
-    """Device binning of the C1 raw matrix (f32, feature-major upload + value_to_bin into
-    the row-major u8 matrix) against the host value_to_bin of the same mappers on all
-    cores. Bin boundaries come from each column's 200k-row sample on the host in both."""
+    """Binning of the C1 raw matrix on the device against the host on all cores: bin
+    finding (find_bin_from_column on each column's 200k-row sample; find_bins against
+    bin_column), and value_to_bin into the row-major u8 matrix (f32 feature-major upload
+    + k_bin_rows, against the host's value_to_bin of the same mappers)."""
     import concurrent.futures as cf
 
     import lightgbm_rs_b200 as lgb
@@ -731,8 +732,24 @@ def run_binning(args):
     X, y = synthetic.binary_c0(num_data=args.rows, num_features=28, seed=0)
     p = {"max_bin": 255, "min_data_in_leaf": 100, "feature_pre_filter": False}
     t0 = time.perf_counter()
-    ds = lgb.Dataset(X, y, p)  # mappers from the samples (host)
+    ds = lgb.Dataset(X, y, p)  # mappers from the samples (device; first CUDA use: context)
     t_map = time.perf_counter() - t0
+    kw = ds._bin_kwargs()
+    cols = list(ds._values)
+    # bin finding (find_bin_from_column of every column's sample), device and host, warm
+    find_dev = []
+    for _ in range(max(args.steps, 1)):
+        t0 = time.perf_counter()
+        dev_maps = lgb.find_bins(cols, **kw)
+        find_dev.append(time.perf_counter() - t0)
+    nt = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=nt) as ex:
+        host_maps = list(ex.map(lambda c: lgb.bin_column(c, want_bins=False, **kw)[0], cols))
+    t_find_host = time.perf_counter() - t0
+    maps_same = all(a["num_bin"] == b["num_bin"] and a["default_bin"] == b["default_bin"]
+                    and np.asarray(a["upper"]).tobytes() == np.asarray(b["upper"]).tobytes()
+                    for a, b in zip(dev_maps, host_maps))
     dev_s = []
     for _ in range(max(args.steps, 1)):
         ds._handle = None
@@ -743,8 +760,6 @@ def run_binning(args):
         ds._handle = None
     ds.construct()
     dev_bins = ds.device_bins()
-    nt = os.cpu_count() or 1
-    kw = ds._bin_kwargs()
     t0 = time.perf_counter()
 
     def one(j):
@@ -761,7 +776,9 @@ def run_binning(args):
            "config": {"workload": f"C1 raw values {args.rows}x28 f32, max_bin=255"},
            "device_s": dev, "host_value_to_bin_s": t_host, "host_threads": nt,
            "host_note": "host time includes each column's find_bin on its sample",
-           "mapper_s": t_map, "bins_identical": bool(same),
+           "dataset_with_context_s": t_map, "bins_identical": bool(same),
+           "find_bins_device_s": min(find_dev), "find_bins_host_s": t_find_host,
+           "mappers_identical": bool(maps_same),
            "h2d_bytes": vals * 4}
     print(json.dumps(out), flush=True)
 

@@ -799,11 +799,6 @@ __device__ __forceinline__ double seq_sub(const double* v, int stride, int n, do
   return acc;
 }
 
-// Prefetch of the line holding p into L2 (a hint: nothing waits on it).
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-
 // Asynchronous prefetch of [p, p + bytes) into L2 (p and bytes multiples of 16).
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -1610,9 +1605,6 @@ struct PickOut {
 // Cross-feature argmax of both scanned leaves (learner.rs:3314-3321) and the arg_max
 // over all leaves (learner.rs:4537-4551, first max under split_gt, learner.rs:1503-1505
 // stop rule), by one warp: the feature candidates are reduced with shuffles only.
-// Feature descriptors a control-step CTA reads up front (its first kFtCache features).
-constexpr int kFtCache = 8;
-
 // Shared memory of a control step besides the per-feature scratch.
 // The pick's inputs besides the scan results (the step's shared state).
 struct PickIn {
@@ -1628,7 +1620,7 @@ struct CtlSmem {
   uint32_t ocat[2][kCatWords];    // ... and their left bins
   int32_t la_prev;                // the previous step's look-ahead leaf (-1: none)
   int32_t oslot[2];               // the other leaves' best two: their histogram slots
-  DevFeature ftl[kFtCache];       // the CTA's first features, read while the split applies
+  DevFeature ft0;                 // the CTA's first feature
   uint32_t err;                   // the control block's error bits, read by the last CTA
   uint8_t ok[2];                  // the scanned leaves' scan flags
   PickOut pick;
@@ -2161,7 +2153,7 @@ struct FixScanSmem {
 // children.
 template <bool CAT, bool PEER, int CT>
 __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const DevFeature& ft,
-                                FixScanSmem& sm, int s, const DevFeature* ftn) {
+                                FixScanSmem& sm, int s) {
   static_assert(CT == 1024 || (CT == 256 && !CAT), "control-step CTA sizes");
   const int tid = threadIdx.x;
   const int nb = ft.num_bin;
@@ -2241,36 +2233,6 @@ __device__ void fixscan_feature(const GrowDev& d, const Prep& P, int f, const De
       }
       __syncthreads();
       ctl_mark(d, s, CP_LOADED);
-      // A CTA with several features: bring the next feature's cells (accumulated side or
-      // its tile partials, the parent's integer cells, the larger child's parent slot)
-      // into L2 while this one is fixed and scanned (its descriptor was read up front).
-      if (ftn && tid < 128) {
-        const int na = 3 + max(P.priv_tiles - 1, 0);  // arrays of the next feature's cells
-        const size_t c0 = 2 * (size_t)ftn->bin_off;
-        const int lines = (2 * ftn->num_bin * 8 + 127) / 128;
-        for (int k = tid; k < na * lines; k += 128) {
-          const int a = k / lines, ln = k % lines;
-          const long long* base = nullptr;
-          if (a == 0) {
-            if (P.priv_tiles == 0 && !PEER)
-              base = P.acc_slot >= 0 ? d.la_raw + (size_t)P.acc_slot * (d.raw_len + 2) : d.raw;
-            else if (P.priv_tiles > 0)
-              base = P.acc_slot >= 0 ? d.la_partials + (size_t)P.acc_slot * d.private_tiles * d.raw_len
-                                     : d.partials;
-          } else if (a == 1) {
-            if (P.applied) base = d.rawpool + (size_t)P.leaf * d.raw_len;
-          } else if (a == 2) {
-            if (Lg >= 0) {
-              prefetch_l2(d.pool + (size_t)P.lslot * d.slot_len + ftn->slot_off + ln * 16);
-              continue;
-            }
-          } else {  // tile partials 1 .. priv_tiles - 1
-            base = (P.acc_slot >= 0 ? d.la_partials + (size_t)P.acc_slot * d.private_tiles * d.raw_len
-                                    : d.partials) + (size_t)(a - 2) * d.raw_len;
-          }
-          if (base) prefetch_l2(base + c0 + ln * 16);
-        }
-      }
       // FixHistogram (fix_histogram.rs:50-81): the most-frequent-bin cell becomes the leaf
       // sum minus the other cells, subtracted in ascending order. With quantized
       // gradients every cell is an exact multiple of one unit u. When every partial
@@ -2441,10 +2403,8 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     // the last CTA reads their splits with its other inputs)
     const Cand2 o = other_leaves_best(d);
     if ((tid & 31) == 0) cs.other = o;
-  } else if (tid >= 64 && tid < 64 + kFtCache) {
-    // the CTA's features (blockIdx.x, blockIdx.x + grid, ...), read while the split applies
-    const int f = fb + (int)blockIdx.x + (tid - 64) * (int)gridDim.x;
-    if (f < fe) cs.ftl[tid - 64] = d.feat[f];
+  } else if (tid == 64) {
+    if (fb + (int)blockIdx.x < fe) cs.ft0 = d.feat[fb + blockIdx.x];
   }
   __syncthreads();
   ctl_mark(d, s, CP_PREP);
@@ -2463,12 +2423,10 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
       if (la) la[i] = 0;
     }
   }
-  int it = 0;
-  for (int f = fb + blockIdx.x; f < fe; f += gridDim.x, ++it) {
-    // the CTA's first kFtCache features were read while the pending split was applied
-    const DevFeature ft = it < kFtCache ? cs.ftl[it] : d.feat[f];
-    const bool next = it + 1 < kFtCache && f + (int)gridDim.x < fe;
-    fixscan_feature<CAT, PEER, CT>(d, cs.prep, f, ft, sm, s, next ? &cs.ftl[it + 1] : nullptr);
+  for (int f = fb + blockIdx.x; f < fe; f += gridDim.x) {
+    // the CTA's first feature was read while the pending split was applied
+    const DevFeature ft = f == fb + (int)blockIdx.x ? cs.ft0 : d.feat[f];
+    fixscan_feature<CAT, PEER, CT>(d, cs.prep, f, ft, sm, s);
     __syncthreads();
   }
   ctl_mark(d, s, CP_FEATURES);
