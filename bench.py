@@ -514,10 +514,18 @@ def run_ours(args):
     t0 = time.perf_counter()
     ds2 = lgb.Dataset(bins=shard_bins, mappers=data.mappers, label=shard_y, params=p,
                       group=group)
-    b2 = lgb.train(p, ds2, num_boost_round=args.steps, comm=comm)
+    ds2.construct()  # the upload (lgb.train would do it first)
+    t1 = time.perf_counter()
+    b2 = lgb.Booster(p, ds2, comm=comm)  # device buffers, labels, the iteration's graph
+    t2 = time.perf_counter()
+    b2.update(args.steps)
+    t3 = time.perf_counter()
     trees = b2.trees()
     scores = b2.train_scores()
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    t4 = time.perf_counter()
+    e2e_s = max_over_ranks(t4 - t0)
+    e2e_parts = {"dataset_upload_s": t1 - t0, "booster_create_s": t2 - t1,
+                 "train_s": t3 - t2, "readback_s": t4 - t3}
     h2d = shard_bins.nbytes + shard_y.nbytes + (0 if group is None else (len(group) + 1) * 4)
     d2h = scores.nbytes + sum(sum(np.asarray(v).nbytes for k, v in t.items()
                                   if isinstance(v, np.ndarray)) for t in trees)
@@ -700,6 +708,7 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": args.steps / e2e_s, "unit": "iters/s",
                 "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps,
+                "parts_rank0": e2e_parts,
                 "note": "lgb.train from host bins+labels: upload, K iterations, model+scores "
                         "readback (binning excluded on both arms); run first, with the "
                         "library's device-buffer cache emptied (cold)"},

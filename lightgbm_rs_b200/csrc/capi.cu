@@ -9,7 +9,9 @@
 #include <limits>
 #include <map>
 #include <memory>
+#include <atomic>
 #include <mutex>
+#include <thread>
 #include <string>
 #include <vector>
 
@@ -1092,8 +1094,9 @@ int lgbm_b200_find_bins(int32_t device, const void* const* columns, int32_t valu
   std::vector<double> h_metaf(B * 3);
   for (int32_t f0 = 0; f0 < num_features; f0 += batch) {
     const int32_t nb = std::min(batch, num_features - f0);
-    // gather the sampled rows of each column (ascending indices: a forward sweep)
-    for (int32_t j = 0; j < nb; ++j) {
+    // gather the sampled rows of each column (ascending indices: a forward sweep of
+    // scattered reads), the columns split over the host's cores
+    auto gather = [&](int32_t j) {
       double* dst = host_vals.data() + (size_t)j * K;
       if (value_width == 4) {
         const float* col = static_cast<const float*>(columns[f0 + j]);
@@ -1102,6 +1105,18 @@ int lgbm_b200_find_bins(int32_t device, const void* const* columns, int32_t valu
         const double* col = static_cast<const double*>(columns[f0 + j]);
         for (int64_t i = 0; i < k; ++i) dst[i] = col[idx[i]];
       }
+    };
+    {
+      const int nt = (int)std::max(1u, std::min<unsigned>(std::thread::hardware_concurrency(),
+                                                         (unsigned)nb));
+      std::atomic<int32_t> next{0};
+      std::vector<std::thread> pool;
+      for (int t = 1; t < nt; ++t)
+        pool.emplace_back([&] {
+          for (int32_t j; (j = next.fetch_add(1)) < nb;) gather(j);
+        });
+      for (int32_t j; (j = next.fetch_add(1)) < nb;) gather(j);
+      for (std::thread& th : pool) th.join();
     }
     CUDA_TRY(cudaMemcpy(vals_a.p, host_vals.data(), (size_t)nb * K * 8, cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemset(na.p, 0, (size_t)nb * 4));
