@@ -173,6 +173,51 @@ __device__ __noinline__ bool x_wait_target(const uint32_t* error, int xranks,
   return true;
 }
 
+// The control step's two waits in one polling loop: every rank's accumulator flag at
+// `seq`, and, when the pending split was partitioned by a look-ahead, every rank's
+// look-ahead flag at `want` (both arrays' loads issued together: one round trip when
+// both are ready). One acquire fence after both.
+__device__ __noinline__ bool x_wait_both(const uint32_t* error, int xranks,
+                                         const unsigned long long* xflags,
+                                         unsigned long long seq,
+                                         const unsigned long long* laflags,
+                                         unsigned long long want, long long wait_ns) {
+  if (*reinterpret_cast<const volatile uint32_t*>(error) & kErrSpinTimeout) return false;
+  const unsigned long long t0 = global_ns();
+  while (true) {
+    unsigned long long v[kMaxXRanks], w[kMaxXRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxXRanks; ++r) {
+      v[r] = r < xranks ? (unsigned long long)ld_relaxed_sys(
+                              reinterpret_cast<const long long*>(xflags + r))
+                        : seq;
+      w[r] = (laflags && r < xranks) ? (unsigned long long)ld_relaxed_sys(
+                                           reinterpret_cast<const long long*>(laflags + r))
+                                     : want;
+    }
+    bool ready = true;
+#pragma unroll
+    for (int r = 0; r < kMaxXRanks; ++r) ready = ready && v[r] >= seq && w[r] >= want;
+    if (ready) break;
+    if (global_ns() - t0 > (unsigned long long)wait_ns) return false;
+    __nanosleep(64);
+  }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  return true;
+}
+
+// Both waits of the control step: x_wait, then la_wait, as one poll.
+template <bool PEER>
+__device__ __forceinline__ bool x_la_wait(const GrowDev& d, int s) {
+  if (!PEER) return true;
+  const GrowCtrl* c = d.ctrl;
+  const bool la = d.lookahead && c->pending && c->pend_la;
+  return x_wait_both(&c->error, d.xranks, d.xflags,
+                     *reinterpret_cast<const volatile unsigned long long*>(d.xseq),
+                     la ? d.la_flags : nullptr,
+                     la ? c->la_base + (unsigned long long)(s - 1) : 0ull, d.xwait_ns);
+}
+
 template <bool PEER>
 __device__ __forceinline__ bool x_wait(const GrowDev& d) {
   if (!PEER) return true;
@@ -2396,7 +2441,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   const int fb = d.slice_begin, fe = d.slice_end;  // this rank's features
   const int nparts = min(fe - fb, (int)gridDim.x);
   if (tid == 0) {
-    if (!x_wait<PEER>(d) || !la_wait<PEER>(d, s)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
+    if (!x_la_wait<PEER>(d, s)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
     prep_compute<PEER>(d, s, cs.prep);
   } else if (warp == 1) {
     // the best two of the leaves this step leaves alone (final before the step starts;
