@@ -222,7 +222,14 @@ class Dataset:
         kw = self._bin_kw
         maps = [None] * self.num_features
         numeric = [j for j in range(self.num_features) if j not in self._cats]
-        if numeric and self.params.get("device_binning", True) and C.device_count() > 0:
+        # device_binning: True / False, or "auto" (the default): on the device when there
+        # are at least 512 numerical columns. The device runs one thread per column, so its
+        # time barely grows with the columns, while the host's grows with columns / cores:
+        # for C1's 28 columns the device took 0.14 s against 0.095 s on 16 host threads.
+        dev_bin = self.params.get("device_binning", "auto")
+        if dev_bin == "auto":
+            dev_bin = len(numeric) >= 512
+        if numeric and dev_bin and C.device_count() > 0:
             found = find_bins([self._values[j] for j in numeric],
                               device=int(self.params.get("device", 0)), **kw)
             for j, m in zip(numeric, found):

@@ -124,6 +124,11 @@ __device__ __forceinline__ bool equal_ordered(double a, double b) { return b <= 
 
 // greedy_find_bin (bin_mapper.rs:749-835) over dv[0, nd): its bounds, appended at out[0..),
 // count returned. hi / lo: scratch of max_bin entries; big: scratch of nd flags.
+// The sequential per-feature loops read one lane's arrays kSeqBlock elements at a time: a
+// block's loads are issued together, so a loop waits on memory once per block, not once
+// per element (one thread walks ~200k elements per feature).
+constexpr int kSeqBlock = 16;
+
 __device__ int greedy_bins(const double* dv, const int32_t* cnt, int32_t nd, int32_t max_bin,
                            int64_t total_cnt, int32_t min_data_in_bin, double* hi, double* lo,
                            uint8_t* big, double* out) {
@@ -150,11 +155,19 @@ __device__ int greedy_bins(const double* dv, const int32_t* cnt, int32_t nd, int
   double mean = (double)total_cnt / (double)max_bin;
   int32_t bins_left = max_bin;
   int32_t samples_left = (int32_t)total_cnt;
-  for (int32_t i = 0; i < nd; ++i) {
-    big[i] = (double)cnt[i] >= mean ? 1 : 0;
-    if (big[i]) {
-      --bins_left;
-      samples_left -= cnt[i];
+  for (int32_t i0 = 0; i0 < nd; i0 += kSeqBlock) {
+    int32_t c[kSeqBlock];
+#pragma unroll
+    for (int j = 0; j < kSeqBlock; ++j) c[j] = i0 + j < nd ? cnt[i0 + j] : 0;
+#pragma unroll
+    for (int j = 0; j < kSeqBlock; ++j) {
+      if (i0 + j >= nd) break;
+      const bool bg = (double)c[j] >= mean;
+      big[i0 + j] = bg ? 1 : 0;
+      if (bg) {
+        --bins_left;
+        samples_left -= c[j];
+      }
     }
   }
   mean = (double)samples_left / (double)bins_left;
@@ -165,19 +178,38 @@ __device__ int greedy_bins(const double* dv, const int32_t* cnt, int32_t nd, int
   int32_t nb = 0;
   lo[0] = dv[0];
   int32_t run = 0;
-  for (int32_t i = 0; i + 1 < nd; ++i) {
-    if (!big[i]) samples_left -= cnt[i];
-    run += cnt[i];
-    // mean * 0.5f: the reference's float literal, exactly 0.5
-    if (big[i] || (double)run >= mean || (big[i + 1] && (double)run >= fmax(1.0, mean * 0.5))) {
-      hi[nb] = dv[i];
-      ++nb;
-      lo[nb] = dv[i + 1];
-      if (nb >= max_bin - 1) break;
-      run = 0;
-      if (!big[i]) {
-        --bins_left;
-        mean = (double)samples_left / (double)bins_left;
+  bool stop = false;
+  for (int32_t i0 = 0; i0 + 1 < nd && !stop; i0 += kSeqBlock) {
+    // elements i0 .. i0 + kSeqBlock: one past the block for big[i + 1] and dv[i + 1]
+    int32_t c[kSeqBlock];
+    uint8_t bg[kSeqBlock + 1];
+    double v[kSeqBlock + 1];
+#pragma unroll
+    for (int j = 0; j <= kSeqBlock; ++j) {
+      const bool in = i0 + j < nd;
+      if (j < kSeqBlock) c[j] = in ? cnt[i0 + j] : 0;
+      bg[j] = in ? big[i0 + j] : 0;
+      v[j] = in ? dv[i0 + j] : 0.0;
+    }
+#pragma unroll
+    for (int j = 0; j < kSeqBlock; ++j) {
+      if (i0 + j + 1 >= nd) break;
+      if (!bg[j]) samples_left -= c[j];
+      run += c[j];
+      // mean * 0.5f: the reference's float literal, exactly 0.5
+      if (bg[j] || (double)run >= mean || (bg[j + 1] && (double)run >= fmax(1.0, mean * 0.5))) {
+        hi[nb] = v[j];
+        ++nb;
+        lo[nb] = v[j + 1];
+        if (nb >= max_bin - 1) {
+          stop = true;
+          break;
+        }
+        run = 0;
+        if (!bg[j]) {
+          --bins_left;
+          mean = (double)samples_left / (double)bins_left;
+        }
       }
     }
   }
@@ -248,21 +280,34 @@ __global__ void k_find_bins(FindBinArgs a) {
     cnt[nd++] = zero_cnt;
   }
   if (ns > 0) {
-    dv[nd] = vals[0];
-    cnt[nd++] = 1;
-  }
-  for (int32_t i = 1; i < ns; ++i) {
-    if (!equal_ordered(vals[i - 1], vals[i])) {
-      if (vals[i - 1] < 0.0 && vals[i] > 0.0) {
-        dv[nd] = 0.0;
-        cnt[nd++] = zero_cnt;
+    // the open run (its last value and its count) stays in registers and is stored when
+    // the next distinct value starts; the sorted values are read a block at a time
+    double prev = vals[0], rv = vals[0];
+    int32_t rc = 1;
+    for (int32_t i0 = 1; i0 < ns; i0 += kSeqBlock) {
+      double x[kSeqBlock];
+#pragma unroll
+      for (int j = 0; j < kSeqBlock; ++j) x[j] = i0 + j < ns ? vals[i0 + j] : 0.0;
+#pragma unroll
+      for (int j = 0; j < kSeqBlock; ++j) {
+        if (i0 + j >= ns) break;
+        const double v = x[j];
+        if (!equal_ordered(prev, v)) {
+          dv[nd] = rv;
+          cnt[nd++] = rc;
+          if (prev < 0.0 && v > 0.0) {
+            dv[nd] = 0.0;
+            cnt[nd++] = zero_cnt;
+          }
+          rc = 0;
+        }
+        rv = v;
+        ++rc;
+        prev = v;
       }
-      dv[nd] = vals[i];
-      cnt[nd++] = 1;
-    } else {
-      dv[nd - 1] = vals[i];
-      cnt[nd - 1] += 1;
     }
+    dv[nd] = rv;
+    cnt[nd++] = rc;
   }
   if (ns > 0 && vals[ns - 1] < 0.0 && zero_cnt > 0) {
     dv[nd] = 0.0;
@@ -278,20 +323,36 @@ __global__ void k_find_bins(FindBinArgs a) {
   uint8_t* big = a.big + (size_t)f * (k + 2);
   double* side = a.side + (size_t)f * (a.max_bin + 1);
   int32_t neg = 0, zc = 0, pos = 0;
-  for (int32_t i = 0; i < nd; ++i) {
-    if (dv[i] <= -kZeroThr)
-      neg += cnt[i];
-    else if (dv[i] > kZeroThr)
-      pos += cnt[i];
-    else
-      zc += cnt[i];
-  }
-  int32_t first_nonneg = nd;
-  for (int32_t i = 0; i < nd; ++i)
-    if (dv[i] > -kZeroThr) {
-      first_nonneg = i;
-      break;
+  for (int32_t i0 = 0; i0 < nd; i0 += kSeqBlock) {
+    double x[kSeqBlock];
+    int32_t c[kSeqBlock];
+#pragma unroll
+    for (int j = 0; j < kSeqBlock; ++j) {
+      x[j] = i0 + j < nd ? dv[i0 + j] : 0.0;
+      c[j] = i0 + j < nd ? cnt[i0 + j] : 0;
     }
+#pragma unroll
+    for (int j = 0; j < kSeqBlock; ++j) {
+      if (x[j] <= -kZeroThr)
+        neg += c[j];
+      else if (x[j] > kZeroThr)
+        pos += c[j];
+      else
+        zc += c[j];
+    }
+  }
+  int32_t first_nonneg = nd;  // dv ascends: the first entry above -kZeroThr, by bisection
+  {
+    int32_t l = 0, r = nd;
+    while (l < r) {
+      const int32_t m = (l + r) / 2;
+      if (dv[m] > -kZeroThr)
+        r = m;
+      else
+        l = m + 1;
+    }
+    first_nonneg = l;
+  }
   int nu = 0;
   if (first_nonneg > 0 && mb > 1) {
     int32_t neg_bins = (int32_t)((double)neg / (double)((int32_t)tc - zc) * (double)(mb - 1));
@@ -300,11 +361,17 @@ __global__ void k_find_bins(FindBinArgs a) {
     if (nu > 0) up[nu - 1] = -kZeroThr;
   }
   int32_t first_pos = -1;
-  for (int32_t i = first_nonneg; i < nd; ++i)
-    if (dv[i] > kZeroThr) {
-      first_pos = i;
-      break;
+  {
+    int32_t l = first_nonneg, r = nd;  // the first entry above kZeroThr, by bisection
+    while (l < r) {
+      const int32_t m = (l + r) / 2;
+      if (dv[m] > kZeroThr)
+        r = m;
+      else
+        l = m + 1;
     }
+    if (l < nd) first_pos = l;
+  }
   const int32_t pos_bins = mb - 1 - nu;
   if (first_pos >= 0 && pos_bins > 0) {
     const int ns2 = greedy_bins(dv + first_pos, cnt + first_pos, nd - first_pos, pos_bins, pos,
@@ -321,11 +388,30 @@ __global__ void k_find_bins(FindBinArgs a) {
   int32_t* cib = a.cnt_in_bin + (size_t)f * a.cap;
   for (int b = 0; b < num_bin; ++b) cib[b] = 0;
   {
-    int32_t b = 0;
-    for (int32_t i = 0; i < nd; ++i) {
-      while (dv[i] > up[b] && b < num_bin - 1) ++b;
-      cib[b] += cnt[i];
+    // the current bin's count in a register, stored when the bin advances
+    int32_t b = 0, acc = 0;
+    double ub = up[0];
+    for (int32_t i0 = 0; i0 < nd; i0 += kSeqBlock) {
+      double x[kSeqBlock];
+      int32_t c[kSeqBlock];
+#pragma unroll
+      for (int j = 0; j < kSeqBlock; ++j) {
+        x[j] = i0 + j < nd ? dv[i0 + j] : 0.0;
+        c[j] = i0 + j < nd ? cnt[i0 + j] : 0;
+      }
+#pragma unroll
+      for (int j = 0; j < kSeqBlock; ++j) {
+        if (i0 + j >= nd) break;
+        if (x[j] > ub && b < num_bin - 1) {
+          cib[b] += acc;
+          acc = 0;
+          while (x[j] > up[b] && b < num_bin - 1) ++b;
+          ub = up[b];
+        }
+        acc += c[j];
+      }
     }
+    cib[b] += acc;
     if (missing == 2) cib[num_bin - 1] = na_cnt;
   }
   bool trivial = num_bin <= 1;

@@ -75,7 +75,7 @@ def test_dataset_uses_device_bins():
     from lightgbm_rs_b200 import synthetic
 
     X, y = synthetic.binary_c0(num_data=300_000, seed=5)
-    ds = lgb.Dataset(X, y, {"max_bin": 255})
+    ds = lgb.Dataset(X, y, {"max_bin": 255, "device_binning": True})  # ("auto": host at 28)
     host = lgb.Dataset(X, y, {"max_bin": 255, "device_binning": False})
     for a, b in zip(ds.mappers, host.mappers):
         _same(a, b, "dataset")
