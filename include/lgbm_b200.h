@@ -441,10 +441,13 @@ int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
  * (0: the root build; 1 + 4*s + kind for split step s, kind 0 control step, 1 main-stream
  * partition, 2 look-ahead partition, 3 separate build) the earliest CTA entry and latest
  * CTA exit in %globaltimer ns; a slot not launched holds start = UINT64_MAX. phase_out
- * (optional, cap * 8 entries): for split step s, eight control-step phase marks at
- * phase_out[8*s] (latest CTA time, 0 when not reached): pending split applied, feature
+ * (optional, cap * 20 entries): for split step s, twenty marks at phase_out[20*s] (latest
+ * CTA time, 0 when not reached). Eight control-step marks: pending split applied, feature
  * cells loaded, FixHistogram and child stores done, scans done, every feature of the CTA
- * done, pick inputs staged, pick made, control block written. *n_out receives the slot
+ * done, pick inputs staged, pick made, control block written. Then six marks of the
+ * step's look-ahead partition and six of its main partition, raised by the CTAs that hold
+ * a tile: entry, setup done, first tile's rows routed, its prefix known, last tile
+ * written, histogram flushed. *n_out receives the slot
  * count; at most cap entries of each span array are written. No counterpart in the
  * reference (a profiling aid). */
 int lgbm_b200_booster_profile_spans(const lgbm_b200_booster* b, int32_t cap,

@@ -601,6 +601,9 @@ class Booster:
     # control-step phase marks (CtlPhase), each the latest CTA's time at that point
     CONTROL_PHASES = ("prep", "loaded", "fixed", "scanned", "features", "staged", "picked",
                       "written")
+    # partition phase marks (PartPhase), each the latest tile-holding CTA's time at that point
+    PARTITION_PHASES = ("start", "ready", "loaded", "prefix", "tiles", "flushed")
+    STEP_MARKS = len(CONTROL_PHASES) + 2 * len(PARTITION_PHASES)
 
     def profile_chain(self):
         """What held the split chain in the last iteration profile_pipeline ran, from the
@@ -616,13 +619,16 @@ class Booster:
         "main_run": the main partitions shorter / longer than 8 us (it found its leaf
         partitioned by the look-ahead, or ran), with their mean delay after the control
         step and mean span in us (and [step, span us] of each run); "lookahead_span_us":
-        the mean look-ahead span."""
+        the mean look-ahead span. "lookahead_phases_us" / "main_run_phases_us": the mean
+        look-ahead span / main run split at the partition's marks (the latest tile-holding
+        CTA's entry, its setup, first tile routed, that tile's prefix, last tile written,
+        histogram flushed, then the launch's exit)."""
         n = C._i32(0)
         C.check(C.lib().lgbm_b200_booster_profile_spans(self._handle, 0, None, None, None,
                                                         ctypes.byref(n)))
         st = np.zeros(n.value, dtype=np.uint64)
         en = np.zeros(n.value, dtype=np.uint64)
-        ph = np.zeros((n.value, len(self.CONTROL_PHASES)), dtype=np.uint64)
+        ph = np.zeros((n.value, self.STEP_MARKS), dtype=np.uint64)
         C.check(C.lib().lgbm_b200_booster_profile_spans(self._handle, n.value, C.ptr(st),
                                                         C.ptr(en), C.ptr(ph), ctypes.byref(n)))
         none = np.iinfo(np.uint64).max
@@ -639,7 +645,20 @@ class Booster:
                "main_noop": {"n": 0, "launch_after_control_us": 0.0, "span_us": 0.0},
                "main_run": {"n": 0, "launch_after_control_us": 0.0, "span_us": 0.0,
                             "steps": []},
-               "lookahead_span_us": 0.0, "lookahead_n": 0}
+               "lookahead_span_us": 0.0, "lookahead_n": 0,
+               "lookahead_phases_us": {}, "main_run_phases_us": {}}
+        nc, npp = len(self.CONTROL_PHASES), len(self.PARTITION_PHASES)
+
+        def part_phases(sp_, marks_, acc):
+            # a partition launch's span split at its marks (the latest tile-holding CTA's
+            # entry, setup, first tile routed, its prefix, last tile, flush), then its exit
+            prev_ = sp_[0]
+            for name_, t_ in zip(self.PARTITION_PHASES + ("exit",),
+                                 [int(v) for v in marks_] + [sp_[1]]):
+                if t_ == 0:
+                    continue
+                acc[name_] = acc.get(name_, 0.0) + max(t_ - prev_, 0) * 1e-3
+                prev_ = max(prev_, t_)
         steps = (len(st) - 1) // 4
         first = span(1)
         root = span(0)
@@ -679,12 +698,14 @@ class Booster:
                 m["span_us"] += (main[1] - main[0]) * 1e-3
                 if kind == "run":
                     m["steps"].append([s, round((main[1] - main[0]) * 1e-3, 1)])
+                    part_phases(main, ph[s][nc + npp:nc + 2 * npp], out["main_run_phases_us"])
             own_la = span(1 + 4 * s + 2)
             if own_la:
                 out["lookahead_span_us"] += (own_la[1] - own_la[0]) * 1e-3
                 out["lookahead_n"] += 1
+                part_phases(own_la, ph[s][nc:nc + npp], out["lookahead_phases_us"])
             # inside the control step: entry, the phase marks in order, exit
-            marks = [ctl[0]] + [int(v) for v in ph[s]] + [ctl[1]]
+            marks = [ctl[0]] + [int(v) for v in ph[s][:nc]] + [ctl[1]]
             prev = marks[0]
             for name, t_m in zip(self.CONTROL_PHASES + ("exit",), marks[1:]):
                 if t_m == 0:  # not reached (a scan-free step, or a CTA with no feature)
@@ -694,6 +715,11 @@ class Booster:
                 prev = max(prev, t_m)
         if out["lookahead_n"]:
             out["lookahead_span_us"] /= out["lookahead_n"]
+            for k in out["lookahead_phases_us"]:
+                out["lookahead_phases_us"][k] /= out["lookahead_n"]
+        if out["main_run"]["n"]:
+            for k in out["main_run_phases_us"]:
+                out["main_run_phases_us"][k] /= out["main_run"]["n"]
         for kind in ("main_noop", "main_run"):  # means per launch
             m = out[kind]
             if m["n"]:

@@ -762,7 +762,7 @@ struct lgbm_b200_booster {
   std::vector<std::pair<int32_t, float>> last_profile;  // (kernel class, ms) per launch
   DevBuf<unsigned long long> spans;  // [2][span_slots(L)] start | end (profile_pipeline)
   std::vector<unsigned long long> span_last;  // the last profiled iteration's spans (host)
-  DevBuf<unsigned long long> phases;          // [L][kCtlPhases] control-step phase marks
+  DevBuf<unsigned long long> phases;          // [L][kStepMarks] phase marks of each split step
   std::vector<unsigned long long> phase_last;  // the last profiled iteration's marks (host)
   lgbm_b200_comm* comm = nullptr;  // data-parallel job (null: one device)
   const DeviceComm* dcomm() const { return comm ? &comm->dev : nullptr; }
@@ -2499,7 +2499,7 @@ int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
   const int L = b->learner->L;
   const int slots = span_slots(L);
   if (!b->spans.p) CUDA_TRY(b->spans.alloc(2 * (size_t)slots));
-  const size_t nph = (size_t)L * kCtlPhases;
+  const size_t nph = (size_t)L * kStepMarks;
   if (!b->phases.p) CUDA_TRY(b->phases.alloc(nph));
   // a graph of the same launch sequence whose tree kernels stamp their spans
   cudaStream_t st = b->learner->stream;
@@ -2603,8 +2603,8 @@ int lgbm_b200_booster_profile_spans(const lgbm_b200_booster* b, int32_t cap,
     start_out[k] = b->span_last[k];
     end_out[k] = b->span_last[(size_t)slots + k];
   }
-  if (phase_out)  // step s of slot 1 + 4 s: kCtlPhases marks at phase_out[s * kCtlPhases]
-    for (size_t k = 0; k < b->phase_last.size() && k < (size_t)cap * kCtlPhases; ++k)
+  if (phase_out)  // step s of slot 1 + 4 s: kStepMarks marks at phase_out[s * kStepMarks]
+    for (size_t k = 0; k < b->phase_last.size() && k < (size_t)cap * kStepMarks; ++k)
       phase_out[k] = b->phase_last[k];
   return LGBM_B200_OK;
 }

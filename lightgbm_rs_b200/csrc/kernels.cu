@@ -116,7 +116,17 @@ struct SpanStamp {
 
 // Phase mark p of control step s (thread 0 of the calling CTA; nothing when off).
 __device__ __forceinline__ void ctl_mark(const GrowDev& d, int s, int p) {
-  if (d.ctl_phase && threadIdx.x == 0) atomicMax(d.ctl_phase + (size_t)s * kCtlPhases + p, global_ns());
+  if (d.ctl_phase && threadIdx.x == 0) atomicMax(d.ctl_phase + (size_t)s * kStepMarks + p, global_ns());
+}
+
+// Phase mark p of a partition launch (thread 0; nothing when off). The launch's split step
+// is that of its span slot; `t` is the time to record.
+__device__ __forceinline__ void part_mark(const GrowDev& d, bool lookahead, int p,
+                                          unsigned long long t) {
+  if (d.ctl_phase && threadIdx.x == 0 && d.span_slot >= 1)
+    atomicMax(d.ctl_phase + (size_t)((d.span_slot - 1) >> 2) * kStepMarks + kCtlPhases +
+                  (lookahead ? 0 : kPartPhases) + p,
+              t);
 }
 
 // Sum over the ranks of word `off` of each rank's buffer (integers: exact in any order).
@@ -2927,6 +2937,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
   // words and accumulator); otherwise the pending split of the control block
   LookAhead* const rec = la >= 0 ? d.la + la : nullptr;
   uint32_t* const ticket = rec ? &rec->ticket : &d.ctrl->part_ticket;
+  const unsigned long long t_entry = d.ctl_phase ? global_ns() : 0ull;
   if (!rec) {
     // The main partition has nothing to do after the tree, or when the look-ahead did this
     // partition (most splits): one read of the control block decides, before any other
@@ -3018,6 +3029,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
   int32_t tile = s_tile;
   if (tile >= ntiles) return;
   const int32_t my_tile = tile;
+  part_mark(d, rec != nullptr, PP_START, t_entry);
   uint32_t* hot = sm;
   uint32_t* c3 = sm + kQ4MaxCells;
   int32_t* cold_g = reinterpret_cast<int32_t*>(sm + 2 * kQ4MaxCells);
@@ -3042,6 +3054,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     }
   }
   __syncthreads();
+  if (d.ctl_phase) part_mark(d, rec != nullptr, PP_READY, global_ns());
   Q4Mask qm = q4_mask<NCH>(s_mask, nf);
   const uint16_t* gq = reinterpret_cast<const uint16_t*>(d.gh);
   const float2* gf = reinterpret_cast<const float2*>(d.gh);
@@ -3105,6 +3118,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     }
     if (lane == 31) s_warp[warp] = incl;
     __syncthreads();
+    if (d.ctl_phase && tile == my_tile) part_mark(d, rec != nullptr, PP_LOADED, global_ns());
     int32_t warp_off = 0, tile_left = 0;
 #pragma unroll 8
     for (int wi = 0; wi < kFpThreads / 32; ++wi) {
@@ -3145,6 +3159,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
       }
     }
     __syncthreads();
+    if (d.ctl_phase && tile == my_tile) part_mark(d, rec != nullptr, PP_PREFIX, global_ns());
     const int32_t prefix_left = s_prefix;
     if (s_ok == 0) {
       failed = true;
@@ -3192,6 +3207,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
       __syncthreads();
     }
   }
+  if (d.ctl_phase) part_mark(d, rec != nullptr, PP_TILES, global_ns());
   if (failed) {
     if (tid == 0) {
       if (rec) {
@@ -3241,6 +3257,10 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     if (build)
       atomicAdd(reinterpret_cast<unsigned long long*>(rec ? &rec->built : &c->rows_built),
                 (unsigned long long)cta_built);
+  }
+  if (d.ctl_phase) {  // uniform over the CTA (a launch parameter)
+    __syncthreads();
+    part_mark(d, rec != nullptr, PP_FLUSHED, global_ns());
   }
 }
 

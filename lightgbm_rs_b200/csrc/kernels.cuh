@@ -174,8 +174,10 @@ struct GrowDev {
   unsigned long long* span_start;
   unsigned long long* span_end;
   int32_t span_slot;
-  // Control-step phases (null: off): ctl_phase[s * kCtlPhases + p] is raised to the
-  // latest CTA's %globaltimer at phase p of split step s (CtlPhase).
+  // Phase marks of split step s (null: off), kStepMarks words per step: word p is raised
+  // to the latest CTA's %globaltimer at control-step phase p (CtlPhase), word
+  // kCtlPhases + p at phase p of the step's look-ahead partition and word
+  // kCtlPhases + kPartPhases + p at phase p of its main partition (PartPhase).
   unsigned long long* ctl_phase;
   // Feature slices of a data-parallel job over peer memory (sliced = 1): this rank's
   // control step decodes and scans features [slice_begin, slice_end) only, then the ranks
@@ -216,6 +218,16 @@ enum CtlPhase {
   CP_PICKED = 6, CP_WRITTEN = 7
 };
 constexpr int kCtlPhases = 8;
+
+// Phase marks of a partition launch, raised by each CTA that holds a tile: its entry, its
+// setup done (leaf range, feature mask, cleared accumulators), its first tile's rows loaded
+// and routed, that tile's prefix known (look-back), its last tile written, its histogram
+// flushed.
+enum PartPhase {
+  PP_START = 0, PP_READY = 1, PP_LOADED = 2, PP_PREFIX = 3, PP_TILES = 4, PP_FLUSHED = 5
+};
+constexpr int kPartPhases = 6;
+constexpr int kStepMarks = kCtlPhases + 2 * kPartPhases;  // control, look-ahead, main
 
 // Optional per-kernel timing of a launch sequence: events recorded around each kernel.
 enum KernelClass { KC_PREPARE = 0, KC_BUILD = 1, KC_FIXSCAN = 2, KC_PARTITION = 3, KC_INIT = 4,
