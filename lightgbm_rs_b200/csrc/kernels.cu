@@ -1546,16 +1546,6 @@ struct Cand {
   int32_t f, i;
 };
 
-__device__ __forceinline__ void warp_argmax(Cand& c) {
-  for (int o = 16; o > 0; o >>= 1) {
-    Cand x;
-    x.g = __shfl_xor_sync(0xffffffffu, c.g, o);
-    x.f = __shfl_xor_sync(0xffffffffu, c.f, o);
-    x.i = __shfl_xor_sync(0xffffffffu, c.i, o);
-    if (cand_better(x.g, x.f, x.i, c.g, c.f, c.i)) c = x;
-  }
-}
-
 __device__ __forceinline__ bool cand_lt(const Cand& a, const Cand& b) {  // a ranks first
   return cand_better(a.g, a.f, a.i, b.g, b.f, b.i);
 }
@@ -1575,6 +1565,41 @@ __device__ __forceinline__ void cand2_insert(Cand2& t, const Cand& x) {
   } else if (cand_lt(x, t.b)) {
     t.b = x;
   }
+}
+
+// Orderable key of a gain (a larger gain has a larger key; -0.0 counts as +0.0). Gains
+// are never NaN; key 0 is no candidate.
+__device__ __forceinline__ unsigned long long gain_key(double g) {
+  const long long b = __double_as_longlong(g == 0.0 ? 0.0 : g);
+  return b >= 0 ? (unsigned long long)b ^ 0x8000000000000000ull : ~(unsigned long long)b;
+}
+
+__device__ __forceinline__ double key_gain(unsigned long long k) {
+  return __longlong_as_double((long long)((k >> 63) ? (k ^ 0x8000000000000000ull) : ~k));
+}
+
+// The warp's best feature under split_gt (the larger gain, then the lower feature), from
+// each lane's own best {g, f, f} (f = -1: none); every lane gets it. The same order as
+// cand_better over the lanes, from two warp max-reductions of the gain key's halves and a
+// min-reduction of the tied features.
+__device__ __forceinline__ Cand warp_best_feature(const Cand& c) {
+  const unsigned long long k = c.f >= 0 ? gain_key(c.g) : 0ull;
+  const unsigned hi = (unsigned)(k >> 32), lo = (unsigned)k;
+  const unsigned m1 = __reduce_max_sync(0xffffffffu, hi);
+  const unsigned m2 = __reduce_max_sync(0xffffffffu, hi == m1 ? lo : 0u);
+  const bool tie = k != 0ull && hi == m1 && lo == m2;
+  const unsigned fm = __reduce_min_sync(0xffffffffu, tie ? (unsigned)c.f : 0xffffffffu);
+  if (fm == 0xffffffffu) return Cand{kNegInf, -1, -1};
+  return Cand{key_gain(((unsigned long long)m1 << 32) | m2), (int32_t)fm, (int32_t)fm};
+}
+
+// DevSplitInfo as 8-byte words, and word w of d_split_none(): threshold 0 and
+// default_left 1 in word 0, gain -inf in word 2, zeros elsewhere.
+constexpr int kSplitWords = (int)(sizeof(DevSplitInfo) / 8);
+static_assert(offsetof(DevSplitInfo, default_left) == 4 && offsetof(DevSplitInfo, gain) == 16,
+              "d_split_none's words");
+__device__ __forceinline__ unsigned long long split_none_word(int w) {
+  return w == 0 ? (1ull << 32) : w == 2 ? (unsigned long long)__double_as_longlong(kNegInf) : 0ull;
 }
 
 __device__ __forceinline__ Cand shfl_cand(const Cand& c, int o) {
@@ -1713,8 +1738,8 @@ __device__ void block_best_features(const GrowDev& d, int32_t Lg, CtlSmem& cs) {
       if (g1[u] > kNegInf && cand_better(g1[u], f, f, f1.g, f1.f, f1.i)) f1 = Cand{g1[u], f, f};
     }
   }
-  warp_argmax(f0);
-  warp_argmax(f1);
+  f0 = warp_best_feature(f0);
+  f1 = warp_best_feature(f1);
   if (lane == 0) {
     cs.wpart[warp][0] = f0;
     cs.wpart[warp][1] = f1;
@@ -1726,8 +1751,8 @@ __device__ void block_best_features(const GrowDev& d, int32_t Lg, CtlSmem& cs) {
       a = cs.wpart[lane][0];
       b = cs.wpart[lane][1];
     }
-    warp_argmax(a);
-    warp_argmax(b);
+    a = warp_best_feature(a);
+    b = warp_best_feature(b);
     if (lane == 0) {
       cs.wbest[0] = a;
       cs.wbest[1] = b;
@@ -1803,8 +1828,8 @@ __device__ void sliced_pick_exchange(const GrowDev& d, int32_t Lg, const DevSpli
     if (q0 >= 0) r0 = Cand{__longlong_as_double(w0), q0, q0};
     if (q1 >= 0) r1 = Cand{__longlong_as_double(w1), q1, q1};
   }
-  warp_argmax(r0);
-  warp_argmax(r1);
+  r0 = warp_best_feature(r0);
+  r1 = warp_best_feature(r1);
   f0 = r0;
   f1 = r1;
   // the owners' records of the winners: lane c copies leaf c's split
@@ -1869,8 +1894,8 @@ __device__ void pick_warp(const GrowDev& d, const PickIn& in, const CtlSmem& cs,
         if (g0 > kNegInf && cand_better(g0, f, f, f0.g, f0.f, f0.i)) f0 = Cand{g0, f, f};
         if (g1 > kNegInf && cand_better(g1, f, f, f1.g, f1.f, f1.i)) f1 = Cand{g1, f, f};
       }
-      warp_argmax(f0);
-      warp_argmax(f1);
+      f0 = warp_best_feature(f0);
+      f1 = warp_best_feature(f1);
     }
     if (xch) sliced_pick_exchange<CAT, STAGED>(d, Lg, so, sc, o, f0, f1);
     const int32_t bf0 = ok0 ? f0.f : -1;
@@ -1888,65 +1913,67 @@ __device__ void pick_warp(const GrowDev& d, const PickIn& in, const CtlSmem& cs,
         if (CAT)
           for (int k = 0; k < kCatWords; ++k) o.si_cat[1][k] = 0u;
       }
-    } else if (lane == 0) {
-      if (bf0 >= 0)
-        o.si[0] = so[bf0];
-      else
-        o.si[0] = d_split_none();
-      o.bf[0] = bf0;
-      if (CAT)
-        for (int k = 0; k < kCatWords; ++k)
-          o.si_cat[0][k] = bf0 >= 0 ? sc[(size_t)bf0 * kCatWords + k] : 0u;
-    } else if (lane == 1) {
-      if (Lg >= 0 && bf1 >= 0)
-        o.si[1] = so[d.F + bf1];
-      else
-        o.si[1] = d_split_none();
-      o.bf[1] = bf1;
-      if (CAT)
-        for (int k = 0; k < kCatWords; ++k)
-          o.si_cat[1][k] = (Lg >= 0 && bf1 >= 0) ? sc[((size_t)d.F + bf1) * kCatWords + k] : 0u;
+    } else {
+      // each scanned leaf's best split, one 8-byte word per lane: lanes 0-8 the smaller
+      // leaf's, lanes 16-24 the larger leaf's (and their bin sets)
+      const int side = lane >> 4, w = lane & 15;
+      const int32_t bf = side ? bf1 : bf0;
+      const size_t row = (size_t)(side ? d.F : 0) + (size_t)(bf >= 0 ? bf : 0);
+      if (w < kSplitWords)
+        reinterpret_cast<unsigned long long*>(&o.si[side])[w] =
+            bf >= 0 ? pick_rd<unsigned long long, STAGED>(
+                          reinterpret_cast<const unsigned long long*>(so + row) + w)
+                    : split_none_word(w);
+      if (w == 0) o.bf[side] = bf;
+      if (CAT && w < kCatWords)
+        o.si_cat[side][w] = bf >= 0 ? pick_rd<uint32_t, STAGED>(sc + row * kCatWords + w) : 0u;
     }
     cand2_insert(top, Cand{ok0 ? f0.g : kNegInf, ok0 ? f0.f : -1, S});
     if (Lg >= 0) cand2_insert(top, Cand{ok1 ? f1.g : kNegInf, ok1 ? f1.f : -1, Lg});
   }
   __syncwarp();
+  // the pick and its runner-up, the same in every lane; their splits are copied one word
+  // per lane (lanes 0-8 the pick's, lanes 16-24 the runner-up's)
+  const Cand best = top.a;
+  const int32_t bl = best.i;
+  const bool done = best.g <= 0.0 || bl == 0x7fffffff;
   if (lane == 0) {
-    const Cand best = top.a;
-    const int32_t bl = best.i;
     o.la_leaf = -1;
-    if (best.g <= 0.0 || bl == 0x7fffffff) {
-      o.done = 1;
-    } else {
-      o.done = 0;
-      o.leaf = bl;
-      o.feature = best.f;
-      // an old leaf that wins or runs up is one of the other leaves' best two
-      const int sel = (find && bl == S) ? 0 : (find && bl == Lg) ? 1 : -1;
-      const int oi = bl == in.other.a.i ? 0 : 1;
-      // selected by address: no 72-byte temporaries
-      const DevSplitInfo* sp = sel == 0 ? &o.si[0] : sel == 1 ? &o.si[1] : &cs.orec[oi];
-      o.split = *sp;
-      if (CAT)
-        for (int k = 0; k < kCatWords; ++k)
-          o.split_cat[k] = sel >= 0 ? o.si_cat[sel][k] : cs.ocat[oi][k];
-      // accumulate the side the scan expects to be smaller (any side is exact)
-      o.build_left = sp->left_count <= sp->right_count ? 1 : 0;
-      // the runner-up: the next pick chooses it unless a child of this split outranks it
-      const Cand ru = top.b;
-      if (d.lookahead && ru.i != 0x7fffffff && ru.g > 0.0) {
-        const int32_t rl = ru.i;
-        const int rs = (find && rl == S) ? 0 : (find && rl == Lg) ? 1 : -1;
-        const int ri = rl == in.other.a.i ? 0 : 1;
-        const DevSplitInfo* rp = rs == 0 ? &o.si[0] : rs == 1 ? &o.si[1] : &cs.orec[ri];
-        o.la_leaf = rl;
-        o.la_feature = ru.f;
-        o.la_split = *rp;
-        o.la_build_left = rp->left_count <= rp->right_count ? 1 : 0;
-        if (CAT)
-          for (int k = 0; k < kCatWords; ++k)
-            o.la_cat[k] = rs >= 0 ? o.si_cat[rs][k] : cs.ocat[ri][k];
-      }
+    o.done = done ? 1 : 0;
+  }
+  if (done) return;
+  // an old leaf that wins or runs up is one of the other leaves' best two
+  const int sel = (find && bl == S) ? 0 : (find && bl == Lg) ? 1 : -1;
+  const int oi = bl == in.other.a.i ? 0 : 1;
+  const DevSplitInfo* sp = sel == 0 ? &o.si[0] : sel == 1 ? &o.si[1] : &cs.orec[oi];
+  // the runner-up: the next pick chooses it unless a child of this split outranks it
+  const Cand ru = top.b;
+  const bool la = d.lookahead && ru.i != 0x7fffffff && ru.g > 0.0;
+  const int32_t rl = ru.i;
+  const int rs = (find && rl == S) ? 0 : (find && rl == Lg) ? 1 : -1;
+  const int ri = rl == in.other.a.i ? 0 : 1;
+  const DevSplitInfo* rp = rs == 0 ? &o.si[0] : rs == 1 ? &o.si[1] : &cs.orec[ri];
+  const int side = lane >> 4, w = lane & 15;
+  if (side == 0 || la) {
+    if (w < kSplitWords)
+      reinterpret_cast<unsigned long long*>(side ? &o.la_split : &o.split)[w] =
+          reinterpret_cast<const unsigned long long*>(side ? rp : sp)[w];
+    if (CAT && w < kCatWords) {
+      if (side == 0)
+        o.split_cat[w] = sel >= 0 ? o.si_cat[sel][w] : cs.ocat[oi][w];
+      else
+        o.la_cat[w] = rs >= 0 ? o.si_cat[rs][w] : cs.ocat[ri][w];
+    }
+  }
+  if (lane == 0) {
+    o.leaf = bl;
+    o.feature = best.f;
+    // accumulate the side the scan expects to be smaller (any side is exact)
+    o.build_left = sp->left_count <= sp->right_count ? 1 : 0;
+    if (la) {
+      o.la_leaf = rl;
+      o.la_feature = ru.f;
+      o.la_build_left = rp->left_count <= rp->right_count ? 1 : 0;
     }
   }
 }
