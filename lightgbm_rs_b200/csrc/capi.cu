@@ -511,6 +511,8 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.packed4 = ds->packed4;
   d.sliced = 0;  // every feature on this device (a data-parallel job may slice them)
   if (const char* e = std::getenv("LGBM_B200_WARP_AGG")) d.warp_agg = std::strcmp(e, "1") == 0;
+  d.warm_pick = 1;
+  if (const char* e = std::getenv("LGBM_B200_WARM_PICK")) d.warm_pick = std::strcmp(e, "0") != 0;
   d.slice_begin = 0;
   d.slice_end = d.F;
   d.bins = ds->bins.p;

@@ -1686,6 +1686,41 @@ struct PickOut {
 // over all leaves (learner.rs:4537-4551, first max under split_gt, learner.rs:1503-1505
 // stop rule), by one warp: the feature candidates are reduced with shuffles only.
 // Shared memory of a control step besides the per-feature scratch.
+// The launch parameters the pick reads, copied into shared memory at the start of the
+// control step: the pick is not inlined, and a reference to the launch's GrowDev would copy
+// all of it to every thread's stack.
+struct PickEnv {
+  const DevSplitInfo* scan_out;
+  const uint32_t* scan_cat;
+  GrowCtrl* ctrl;
+  unsigned long long* pick_local;
+  unsigned long long* const* peer_pick;
+  unsigned long long* pick_flags;
+  unsigned long long* const* peer_pick_flags;
+  unsigned long long* pick_seq;
+  long long xwait_ns;
+  int32_t F, slice_begin, slice_end, sliced, lookahead, xrank, xranks;
+};
+
+__device__ __forceinline__ void pick_env_set(PickEnv& e, const GrowDev& d) {
+  e.scan_out = d.scan_out;
+  e.scan_cat = d.scan_cat;
+  e.ctrl = d.ctrl;
+  e.pick_local = d.pick_local;
+  e.peer_pick = d.peer_pick;
+  e.pick_flags = d.pick_flags;
+  e.peer_pick_flags = d.peer_pick_flags;
+  e.pick_seq = d.pick_seq;
+  e.xwait_ns = d.xwait_ns;
+  e.F = d.F;
+  e.slice_begin = d.slice_begin;
+  e.slice_end = d.slice_end;
+  e.sliced = d.sliced;
+  e.lookahead = d.lookahead;
+  e.xrank = d.xrank;
+  e.xranks = d.xranks;
+}
+
 // The pick's inputs besides the scan results (the step's shared state).
 struct PickIn {
   Cand2 other;     // the best two leaves the step leaves alone
@@ -1704,6 +1739,9 @@ struct CtlSmem {
   uint32_t err;                   // the control block's error bits, read by the last CTA
   uint8_t ok[2];                  // the scanned leaves' scan flags
   PickOut pick;
+  PickOut pick_dry[3];            // the placeholder runs' outputs (warm_pick)
+  PickIn pin[4];                  // the pick's inputs: the real one, the placeholders'
+  PickEnv env[3];                 // the launch parameters the pick reads, per placeholder warp
   bool last;
   int32_t wide;                   // the features' argmax was taken by the whole CTA ...
   Cand wbest[2];                  // ... into these (smaller / larger scanned leaf)
@@ -1778,7 +1816,7 @@ __device__ __forceinline__ T pick_rd(const T* p) {
 // reads: it would first have to pass the next step's wait, which needs the slow rank's
 // next record.
 template <bool CAT, bool STAGED>
-__device__ void sliced_pick_exchange(const GrowDev& d, int32_t Lg, const DevSplitInfo* so,
+__device__ void sliced_pick_exchange(const PickEnv& d, int32_t Lg, const DevSplitInfo* so,
                                      const uint32_t* sc, PickOut& o, Cand& f0, Cand& f1) {
   const int lane = threadIdx.x & 31;
   const unsigned long long target = *reinterpret_cast<const volatile unsigned long long*>(d.pick_seq) + 1;
@@ -1871,23 +1909,35 @@ __device__ void sliced_pick_exchange(const GrowDev& d, int32_t Lg, const DevSpli
   __syncwarp();
 }
 
+// Parts of the pick: the features' argmax of both scanned leaves; their split records and
+// the candidates' order; the chosen leaf and runner-up with their records. A real pick
+// runs all three; a placeholder run may run any of them alone (on placeholder values).
+constexpr int kPickFeatures = 1, kPickRecords = 2, kPickLeaf = 4, kPickAll = 7;
+
+// dry: a placeholder run (no exchange; the output goes to a scratch record).
 template <bool CAT, bool STAGED>
-__device__ void pick_warp(const GrowDev& d, const PickIn& in, const CtlSmem& cs,
-                          const DevSplitInfo* so, const uint32_t* sc, PickOut& o) {
+__device__ __forceinline__ void pick_warp(const PickEnv& d, const PickIn& in, const CtlSmem& cs,
+                                          const DevSplitInfo* so, const uint32_t* sc,
+                                          PickOut& o, bool dry, int parts) {
   const int lane = threadIdx.x & 31;
   const bool find = in.live != 0;
   const int32_t S = in.S, Lg = in.Lg;
-  const bool xch = d.sliced != 0;
+  const bool xch = !dry && d.sliced != 0;
   Cand2 top = in.other;
   if (lane == 0) o.xerr = 0;
   if (find) {
     const bool ok0 = in.ok0 != 0;
     const bool ok1 = Lg >= 0 && in.ok1 != 0;
-    Cand f0{kNegInf, -1, -1}, f1{kNegInf, -1, -1};
-    if (in.wide) {  // taken by the whole CTA (block_best_features)
+    // a placeholder run of the later parts alone starts from the slice's first feature
+    const Cand ph = d.slice_end > d.slice_begin ? Cand{1.0, d.slice_begin, d.slice_begin}
+                                                : Cand{kNegInf, -1, -1};
+    Cand f0 = ph, f1 = ph;
+    if (!(parts & kPickFeatures)) {
+    } else if (in.wide) {  // taken by the whole CTA (block_best_features)
       f0 = in.wbest[0];
       f1 = in.wbest[1];
     } else {
+      f0 = f1 = Cand{kNegInf, -1, -1};
       for (int f = d.slice_begin + lane; f < d.slice_end; f += 32) {
         const double g0 = pick_rd<double, STAGED>(&so[f].gain);
         const double g1 = Lg >= 0 ? pick_rd<double, STAGED>(&so[d.F + f].gain) : kNegInf;
@@ -1897,6 +1947,7 @@ __device__ void pick_warp(const GrowDev& d, const PickIn& in, const CtlSmem& cs,
       f0 = warp_best_feature(f0);
       f1 = warp_best_feature(f1);
     }
+    if (parts & kPickRecords) {
     if (xch) sliced_pick_exchange<CAT, STAGED>(d, Lg, so, sc, o, f0, f1);
     const int32_t bf0 = ok0 ? f0.f : -1;
     const int32_t bf1 = ok1 ? f1.f : -1;
@@ -1930,8 +1981,10 @@ __device__ void pick_warp(const GrowDev& d, const PickIn& in, const CtlSmem& cs,
     }
     cand2_insert(top, Cand{ok0 ? f0.g : kNegInf, ok0 ? f0.f : -1, S});
     if (Lg >= 0) cand2_insert(top, Cand{ok1 ? f1.g : kNegInf, ok1 ? f1.f : -1, Lg});
+    }
   }
   __syncwarp();
+  if (!(parts & kPickLeaf)) return;
   // the pick and its runner-up, the same in every lane; their splits are copied one word
   // per lane (lanes 0-8 the pick's, lanes 16-24 the runner-up's)
   const Cand best = top.a;
@@ -1976,6 +2029,18 @@ __device__ void pick_warp(const GrowDev& d, const PickIn& in, const CtlSmem& cs,
       o.la_build_left = rp->left_count <= rp->right_count ? 1 : 0;
     }
   }
+}
+
+// The pick from staged (shared-memory) or global scan results. Not inlined: its one copy
+// of the code is the one the placeholder runs bring into the SM's instruction cache.
+template <bool CAT>
+__device__ __noinline__ void pick_call(const PickEnv& d, const PickIn& in, const CtlSmem& cs,
+                                       bool staged, const DevSplitInfo* so, const uint32_t* sc,
+                                       PickOut& o, bool dry, int parts) {
+  if (staged)
+    pick_warp<CAT, true>(d, in, cs, so, sc, o, dry, parts);
+  else
+    pick_warp<CAT, false>(d, in, cs, d.scan_out, d.scan_cat, o, dry, parts);
 }
 
 // ------------------------------------------------------------------------------------
@@ -2487,6 +2552,38 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     if ((tid & 31) == 0) cs.other = o;
   } else if (tid == 64) {
     if (fb + (int)blockIdx.x < fe) cs.ft0 = d.feat[fb + blockIdx.x];
+  } else {
+    // Placeholder warps k = 0, 1, 2 (warps 4, 8, 12 with 1024 threads, on warp 0's
+    // scheduler partition; warps 4, 5, 6 with 256): each copies the pick's launch
+    // parameters, and with warm_pick runs part k of the pick on placeholder inputs (two
+    // old leaves with positive gains, both scanned leaves live) into its own scratch
+    // record. A run takes the real pick's path through that part of the code, so that the
+    // code is in the SM's instruction cache when the last CTA runs the pick; it reads only
+    // shared memory or in-range scan results. The three parts run side by side, each
+    // shorter than the prep above.
+    const int k = CT == 1024 ? (warp - 4) >> 2 : warp - 4;
+    const bool ph_warp = warp >= 4 && k < 3 && (CT != 1024 || (warp & 3) == 0);
+    if (ph_warp) {
+      const bool st = d.F <= kStageFeatures;
+      if ((tid & 31) == 0) {
+        pick_env_set(cs.env[k], d);
+        PickIn& in = cs.pin[1 + k];
+        in.other.a = Cand{1e300, 0, 0x7ffffffe};
+        in.other.b = Cand{1e299, 0, 0x7ffffffd};
+        in.wbest[0] = in.wbest[1] = Cand{kNegInf, -1, -1};
+        in.live = 1;
+        in.S = 0x7ffffffc;
+        in.Lg = 0x7ffffffb;
+        in.ok0 = in.ok1 = 1;
+        in.wide = !st && (fe - fb) > kWidePick ? 1 : 0;
+      }
+      __syncwarp();
+      if (d.warm_pick) {
+        const DevSplitInfo* so = reinterpret_cast<const DevSplitInfo*>(&sm);
+        const uint32_t* sc = reinterpret_cast<const uint32_t*>(so + 2 * kStageFeatures);
+        pick_call<CAT>(cs.env[k], cs.pin[1 + k], cs, st, so, sc, cs.pick_dry[k], true, 1 << k);
+      }
+    }
   }
   __syncthreads();
   ctl_mark(d, s, CP_PREP);
@@ -2571,12 +2668,11 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   __syncthreads();
   ctl_mark(d, s, CP_STAGED);
   if (warp == 0 && !P.c.done) {
-    const PickIn in{cs.other, {cs.wbest[0], cs.wbest[1]}, P.live, P.S, P.Lg, cs.ok[0], cs.ok[1],
-                    cs.wide};
-    if (staged)
-      pick_warp<CAT, true>(d, in, cs, so, sc, cs.pick);
-    else
-      pick_warp<CAT, false>(d, in, cs, d.scan_out, d.scan_cat, cs.pick);
+    if ((tid & 31) == 0)
+      cs.pin[0] = PickIn{cs.other, {cs.wbest[0], cs.wbest[1]}, P.live, P.S, P.Lg, cs.ok[0],
+                         cs.ok[1], cs.wide};
+    __syncwarp();
+    pick_call<CAT>(cs.env[0], cs.pin[0], cs, staged, so, sc, cs.pick, false, kPickAll);
   }
   __syncthreads();
   ctl_mark(d, s, CP_PICKED);

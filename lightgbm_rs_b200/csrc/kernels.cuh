@@ -145,6 +145,10 @@ struct GrowDev {
   uint32_t* arrive;
   // Histogram builds with warp-aggregated atomics (LGBM_B200_WARP_AGG=1; the C1 layout only).
   int32_t warp_agg;
+  // Placeholder warps of every control-step CTA run the pick's code on placeholder inputs
+  // into scratch records while the prep runs, so that the code is in the SM's instruction
+  // cache when the last CTA runs the pick for real.
+  int32_t warm_pick;
   long long xwait_ns;                         // wait limit, then the spin-timeout error
   // Look-ahead partitions (fused partition): control step s records slot s % kLaSlots and
   // its look-ahead kernel fills it; control step s + 2 consumes it (when step s + 1 picked
