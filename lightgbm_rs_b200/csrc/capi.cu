@@ -498,10 +498,20 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
     const int sms = sm_count(device);
     las.blocks = std::max(sms / 2, sms - std::min(ds->num_features, sms));
     las.main_blocks = sms;
+    // Past the first splits the main partition almost always finds its leaf done by the
+    // look-ahead. A smaller grid then costs less (fewer CTAs to place and retire) and leaves
+    // the SMs to the look-ahead launched next to it; the few leaves it does partition there
+    // are small.
+    las.main_late_blocks = std::max(1, sms * 7 / 16);
+    las.main_early_steps = 16;
     // launch-shape overrides (tuning): look-ahead and main-partition CTAs
     if (const char* e = std::getenv("LGBM_B200_LA_BLOCKS")) las.blocks = std::max(1, std::atoi(e));
     if (const char* e = std::getenv("LGBM_B200_MAIN_BLOCKS"))
       las.main_blocks = std::max(1, std::atoi(e));
+    if (const char* e = std::getenv("LGBM_B200_MAIN_LATE_BLOCKS"))
+      las.main_late_blocks = std::max(1, std::atoi(e));
+    if (const char* e = std::getenv("LGBM_B200_MAIN_EARLY_STEPS"))
+      las.main_early_steps = std::max(0, std::atoi(e));
   }
   if (const char* e = std::getenv("LGBM_B200_LOOKAHEAD")) la_enabled = std::strcmp(e, "0") != 0;
   d = GrowDev{};

@@ -3637,7 +3637,8 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
     // mostly find the split already partitioned) are placed first
     if (x.fused) {
       PROF_BEGIN(KC_PARTITION);
-      const int main_grid = la_on ? las->main_blocks : sms;
+      const int main_grid =
+          la_on ? (s < las->main_early_steps ? las->main_blocks : las->main_late_blocks) : sms;
       part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT, x.packed4 != 0)<<<main_grid,
                                                                 kFpThreads,
                                                                 fused_partition_smem(), st>>>(
