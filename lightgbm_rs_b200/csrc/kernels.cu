@@ -2735,6 +2735,13 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
           c.pend_la = 1 + ((s - 1) & (kLaSlots - 1));
       }
     }
+    // The previous step's look-ahead is of no use when this pick took another leaf (or
+    // ended the tree): its kernel, which may still be partitioning a big leaf beside this
+    // step, stops taking tiles and leaves the SMs to the main partition. Its slot is never
+    // read; it is cleared as every unused slot is.
+    if (d.la_cancel && d.lookahead && s >= 1 && cs.la_prev >= 0 &&
+        !(!c.done && c.pend_la == 1 + ((s - 1) & (kLaSlots - 1))))
+      d.la[(s - 1) & (kLaSlots - 1)].cancel = 1;
     c.error |= cs.err;
     if (!P.c.done && cs.pick.xerr) c.error |= kErrSpinTimeout;
     if (c.error & kErrSpinTimeout) c.done = 1;  // a rank stopped answering: end the tree
@@ -3190,8 +3197,12 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
   int32_t cta_left = 0;
   long long cta_built = 0;
   bool failed = false;
+  bool cancelled = false;
   while (true) {
     const int32_t base = tile * kPartTile;
+    // a look-ahead's cancel flag, read as the tile starts and used before the next ticket
+    int32_t cancel_seen = 0;
+    if (rec && tid == 0) cancel_seen = *reinterpret_cast<volatile int32_t*>(&rec->cancel);
     uint32_t rows[kFpItems];
     uint4 w[kFpItems][NCH];
     uint16_t q[kFpItems];
@@ -3310,9 +3321,15 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     cta_built += built;
     acc_rows += built;
     if (priv) break;
-    if (tid == 0) s_tile = (int32_t)atomicAdd(ticket, 1u);
+    // A cancelled look-ahead takes no further ticket, so no tile is left untaken behind
+    // a ticket that a later tile's look-back would wait on.
+    if (tid == 0) s_tile = cancel_seen ? -1 : (int32_t)atomicAdd(ticket, 1u);
     __syncthreads();
     tile = s_tile;
+    if (tile < 0) {
+      cancelled = true;
+      break;
+    }
     if (tile >= ntiles) break;
     // fold the 16-bit packed fields before the next tile could overflow them (the 64-bit
     // f32 cells need no fold)
@@ -3342,6 +3359,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     }
     return;
   }
+  if (cancelled) return;  // its slot is never read
   if (build) {
     __syncthreads();
     long long* part = partials + (size_t)my_tile * d.raw_len;

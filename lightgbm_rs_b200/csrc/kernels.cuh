@@ -54,6 +54,7 @@ struct LookAhead {
   int32_t left_total;  // left rows
   int32_t failed;      // a look-back gave up (spin limit)
   int32_t ran;         // the kernel partitioned the leaf
+  int32_t cancel;      // the next pick took another leaf: the kernel takes no more tiles
   long long rows;      // parent rows streamed
   long long built;     // rows accumulated into the child histogram
   DevSplitInfo split;
@@ -149,6 +150,8 @@ struct GrowDev {
   // into scratch records while the prep runs, so that the code is in the SM's instruction
   // cache when the last CTA runs the pick for real.
   int32_t warm_pick;
+  // A look-ahead whose leaf the next pick did not take is cancelled (LookAhead.cancel).
+  int32_t la_cancel;
   long long xwait_ns;                         // wait limit, then the spin-timeout error
   // Look-ahead partitions (fused partition): control step s records slot s % kLaSlots and
   // its look-ahead kernel fills it; control step s + 2 consumes it (when step s + 1 picked
