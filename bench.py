@@ -278,24 +278,33 @@ def kernel_bytes(counts, rows, grad, features):
     none for the root's identity order). Build: per built row F B of bins + its gradient
     pair (2 B quantized, 8 B f32) + 4 B index (none at the root). In the fused mode the
     partition kernel builds the child itself, so those built rows are charged to it, minus
-    the split-feature byte and the index it has already read. Control step (fixscan): per
+    the split-feature byte and the index it has already read. On one device the control
+    step runs the main partition of the splits the look-ahead missed (rows_parted_ctl /
+    rows_built_ctl, the root's among them): those bytes are charged to the control step
+    ("partition_ctl"), the rest to the partition launches. Control step (fixscan): per
     split, the accumulated child, the parent's integer histogram and the written child
     histograms: about 5 x 8 B per histogram cell, cells = 2 x bins (L2-resident)."""
     s_gh = 2 if grad == "quantized" else 8
     F = features
     rp, rb = counts["rows_parted"], counts["rows_built"]
-    part = rp * 5 + max(rp - rows, 0) * 4
+    rpc, rbc = counts.get("rows_parted_ctl", 0), counts.get("rows_built_ctl", 0)
+    root_in_ctl = rpc >= rows  # the root's partition ran inside a control step
+
+    def part_bytes(rp_, child_rows_, has_root):
+        b = rp_ * 5 + max(rp_ - (rows if has_root else 0), 0) * 4
+        ch = child_rows_ * (F - 1 + s_gh) if counts["fused"] else 0
+        return b + ch, ch
+
     root_build = rows * (F + s_gh)
     child_rows = max(rb - rows, 0)
-    child_hist = 0
+    part, ch_a = part_bytes(rp - rpc, child_rows - rbc, not root_in_ctl)
+    part_ctl, ch_b = part_bytes(rpc, rbc, root_in_ctl)
     if counts["fused"]:
-        child_hist = child_rows * (F - 1 + s_gh)
-        part += child_hist
         build = root_build
     else:
         build = root_build + child_rows * (F + s_gh + 4)
-    return {"partition": part, "build": build, "child_hist_fused": child_hist,
-            "bin_bytes": rb * F + rp}
+    return {"partition": part, "partition_ctl": part_ctl, "build": build,
+            "child_hist_fused": ch_a + ch_b, "bin_bytes": rb * F + rp}
 
 
 TREE_EXACT = ["split_feature", "threshold_bin", "decision_type", "left_child", "right_child",
@@ -573,19 +582,29 @@ def run_ours(args):
         return e
 
     fused = pc["fused"]
+    in_ctl = pc.get("rows_parted_ctl", 0) > 0  # main partitions inside the control steps
     cells = 2 * sum(int(m["num_bin"]) for m in data.mappers)
     fix_bytes = pc["splits"] * cells * 8 * 5
     kern = {
-        "partition": entry("k_partition_q4 (row partition + fused child histogram; main and "
-                           "look-ahead launches)" if fused else "k_partition (row partition)",
+        "partition": entry(("k_partition_q4 (row partition + fused child histogram; the "
+                            "look-ahead launches and the last split's main partition)")
+                           if in_ctl else
+                           ("k_partition_q4 (row partition + fused child histogram; main and "
+                            "look-ahead launches)") if fused else "k_partition (row partition)",
                            part_ms, kb["partition"], "partition"),
         "build": entry("k_build_q4 (root histogram)" if fused else
                        "k_build / k_build_q4 (histogram build)", spans["build"], kb["build"],
                        "build"),
-        "fixscan": entry("k_fixscan (control step: decode, FixHistogram, subtraction, "
-                         "threshold scans, pick; L2-resident)", spans["fixscan"], fix_bytes,
-                         "fixscan"),
+        "fixscan": entry(("k_fixscan_part (control step: decode, FixHistogram, subtraction, "
+                          "threshold scans, pick; L2-resident; and the main partition of the "
+                          "splits the look-ahead missed, with its child histogram)") if in_ctl
+                         else ("k_fixscan (control step: decode, FixHistogram, subtraction, "
+                               "threshold scans, pick; L2-resident)"),
+                         spans["fixscan"], fix_bytes + kb["partition_ctl"]),
     }
+    kern["fixscan"]["traffic_per_iter"] = (fix_bytes * TRAFFIC_PER_ALGO_BYTE["fixscan"] +
+                                           kb["partition_ctl"] *
+                                           TRAFFIC_PER_ALGO_BYTE["partition"])
     dom = max(kern, key=lambda k: kern[k]["ms_per_iter"])
     hist = {"root": kern["build"],
             "child_fused": {"bytes_per_iter": kb["child_hist_fused"],

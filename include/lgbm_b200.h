@@ -431,9 +431,12 @@ int lgbm_b200_booster_profile_iteration(lgbm_b200_booster* b, double* ms_out,
  * receives the mean per iteration of the summed spans per kernel class (same order as
  * profile_iteration; partition = the main-stream partitions). iter_ms_out[2] = {mean
  * device ms per iteration, mean summed spans of the look-ahead partitions, which run
- * beside the control steps}. counts_out[8] receives the same counters as
+ * beside the control steps}. counts_out[10] receives the same eight counters as
  * profile_iteration, summed over the iterations (counts_out[0]: stamped tree-kernel
- * launches). No counterpart in the reference (a profiling aid). */
+ * launches), then the parent rows of the main partitions that ran inside control steps
+ * (one device: a control step partitions the previous split's leaf itself when the
+ * look-ahead did not) and the rows their child builds accumulated. No counterpart in the
+ * reference (a profiling aid). */
 int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
                                        double* span_ms_out, double* iter_ms_out,
                                        int64_t* counts_out);

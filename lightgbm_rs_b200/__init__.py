@@ -584,10 +584,11 @@ class Booster:
         """`iterations` more iterations through a graph of the training pipeline whose
         tree kernels stamp their device-time spans. Returns (mean summed span ms per
         iteration by kernel class, {"ms_per_iter": mean iteration ms, "lookahead": mean
-        summed look-ahead partition spans, and the tree counters per iteration})."""
+        summed look-ahead partition spans, and the tree counters per iteration; rows_parted_ctl
+        / rows_built_ctl: the rows of the main partitions that ran inside control steps})."""
         span = np.zeros(7, dtype=np.float64)
         it = np.zeros(2, dtype=np.float64)
-        cnt = np.zeros(8, dtype=np.int64)
+        cnt = np.zeros(10, dtype=np.int64)
         C.check(C.lib().lgbm_b200_booster_profile_pipeline(self._handle, int(iterations),
                                                            C.ptr(span), C.ptr(it), C.ptr(cnt)))
         self._trees = None
@@ -596,7 +597,8 @@ class Booster:
                 {"ms_per_iter": float(it[0]), "lookahead": float(it[1]),
                  "stamped_launches": cnt[0] / n, "builds": cnt[1] / n, "rows_built": cnt[2] / n,
                  "splits": cnt[3] / n, "rows_parted": cnt[4] / n, "fused": bool(cnt[5]),
-                 "lookahead_runs": cnt[6] / n, "lookahead_hits": cnt[7] / n})
+                 "lookahead_runs": cnt[6] / n, "lookahead_hits": cnt[7] / n,
+                 "rows_parted_ctl": cnt[8] / n, "rows_built_ctl": cnt[9] / n})
 
     # control-step phase marks (CtlPhase), each the latest CTA's time at that point
     CONTROL_PHASES = ("prep", "loaded", "fixed", "scanned", "features", "staged", "picked",

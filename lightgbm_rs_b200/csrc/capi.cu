@@ -523,6 +523,8 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   if (const char* e = std::getenv("LGBM_B200_WARP_AGG")) d.warp_agg = std::strcmp(e, "1") == 0;
   d.warm_pick = 1;
   if (const char* e = std::getenv("LGBM_B200_WARM_PICK")) d.warm_pick = std::strcmp(e, "0") != 0;
+  d.fuse_main = 1;
+  if (const char* e = std::getenv("LGBM_B200_FUSE_MAIN")) d.fuse_main = std::strcmp(e, "0") != 0;
   d.la_cancel = 1;
   if (const char* e = std::getenv("LGBM_B200_LA_CANCEL")) d.la_cancel = std::strcmp(e, "0") != 0;
   d.slice_begin = 0;
@@ -2540,7 +2542,7 @@ int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
   std::vector<unsigned long long> h(2 * (size_t)slots), hp(nph);
   double cls[KC_COUNT] = {0};
   double total_ms = 0.0;
-  for (int k = 0; k < 8; ++k) counts_out[k] = 0;
+  for (int k = 0; k < 10; ++k) counts_out[k] = 0;
   iter_ms_out[1] = 0.0;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   cudaEventCreate(&e0);
@@ -2568,6 +2570,8 @@ int lgbm_b200_booster_profile_pipeline(lgbm_b200_booster* b, int32_t iterations,
     counts_out[5] = b->learner->d.fused;
     counts_out[6] += gc.la_runs;
     counts_out[7] += gc.la_hits;
+    counts_out[8] += gc.rows_parted_ctl;
+    counts_out[9] += gc.rows_built_ctl;
     float ms = 0.f;
     cudaEventElapsedTime(&ms, e0, e1);
     total_ms += ms;

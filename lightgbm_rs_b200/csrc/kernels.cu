@@ -1189,6 +1189,7 @@ __global__ void k_tree_init(GrowDev d) {
 
 struct Prep {
   GrowCtrl c;  // control block after this step
+  int32_t main_needed;  // the pending split still needs its main partition (no look-ahead)
   int32_t applied;
   int32_t leaf, nr, node, parent, parent_is_right;
   int32_t lc, rc, lcg, rcg, dst, beg, depth;
@@ -1213,6 +1214,7 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   // the control block is updated in place in P (shared memory in the control step)
   GrowCtrl& c = P.c;
   c = *d.ctrl;
+  P.main_needed = (!c.done && c.pending && !c.pend_la) ? 1 : 0;
   P.applied = 0;
   P.live = 0;
   P.kill0 = P.kill1 = -1;
@@ -1359,6 +1361,7 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   c.epoch += 1;
   c.part_ticket = 0;
   c.part_left_total = 0;
+  c.part_done = 0;
   c.scan_counter = 0;
   // ---- BeforeFindBestSplit (learner.rs:1808-1839) ----
   const int32_t min2 = d.gain.min_data_in_leaf * 2;
@@ -2536,12 +2539,17 @@ static_assert(sizeof(DevSplitInfo) % 8 == 0, "scan results are copied as 8-byte 
 // One control step by the CTAs [0, min(F, gridDim.x)), each taking features
 // blockIdx.x, blockIdx.x + gridDim.x, ...: apply the pending split, scan the two leaves,
 // and -- in the CTA that finishes last -- pick the next split and write the control block.
-template <bool CAT, bool PEER, int CT>
-__device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& cs) {
+// nctl: the control CTAs (the launch's first nctl CTAs). main_part: run by every control CTA
+// after the prep when the pending split still needs its main partition (the fused control
+// step partitions it itself, then redoes the prep; elsewhere a no-op, the partition having
+// run as its own launch).
+template <bool CAT, bool PEER, int CT, class MainPart>
+__device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& cs, int nctl,
+                             MainPart&& main_part) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int fb = d.slice_begin, fe = d.slice_end;  // this rank's features
-  const int nparts = min(fe - fb, (int)gridDim.x);
+  const int nparts = min(fe - fb, nctl);
   if (tid == 0) {
     if (!x_la_wait<PEER>(d, s)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
     prep_compute<PEER>(d, s, cs.prep);
@@ -2587,6 +2595,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
   }
   __syncthreads();
   ctl_mark(d, s, CP_PREP);
+  if (cs.prep.main_needed) main_part();
   if (PEER && d.sliced) {
     // With feature slices the owners of all features sum every rank's buffers, so this
     // rank clears every cell of its next accumulator and of the look-ahead slot it
@@ -2594,7 +2603,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
     // were last read at the previous step, which every rank has finished.
     const Prep& P = cs.prep;
     const int64_t rl = d.raw_len;
-    const int64_t per = (rl + gridDim.x - 1) / gridDim.x;
+    const int64_t per = (rl + nctl - 1) / nctl;
     const int64_t lo = per * blockIdx.x, hi = min(rl, lo + per);
     long long* la = P.la_clear >= 0 ? d.la_raw + (size_t)P.la_clear * (rl + 2) : nullptr;
     for (int64_t i = lo + tid; i < hi; i += CT) {
@@ -2602,7 +2611,7 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
       if (la) la[i] = 0;
     }
   }
-  for (int f = fb + blockIdx.x; f < fe; f += gridDim.x) {
+  for (int f = fb + blockIdx.x; f < fe; f += nctl) {
     // the CTA's first feature was read while the pending split was applied
     const DevFeature ft = f == fb + (int)blockIdx.x ? cs.ft0 : d.feat[f];
     fixscan_feature<CAT, PEER, CT>(d, cs.prep, f, ft, sm, s);
@@ -2772,7 +2781,7 @@ __global__ void __launch_bounds__(CT, CT == 1024 ? 1 : 4) k_fixscan(GrowDev d, i
   const SpanStamp span(d);
   __shared__ FixScanSmem sm;
   __shared__ CtlSmem cs;
-  control_step<CAT, PEER, CT>(d, s, sm, cs);
+  control_step<CAT, PEER, CT>(d, s, sm, cs, (int)gridDim.x, [] {});
 }
 
 // ------------------------------------------------------------------------------------
@@ -3018,6 +3027,7 @@ __device__ __forceinline__ int32_t tile_lookback(unsigned long long* status, int
 struct PartSmem {
   int32_t warp[kFpThreads / 32];
   int32_t tile, prefix, ok;
+  int32_t ntiles;  // tiles of the partitioned leaf (set once the leaf is known)
   int32_t nb[128];
   int32_t boff[128];
   uint32_t mask[4];
@@ -3051,9 +3061,11 @@ __device__ __forceinline__ void f32_row_regs(const uint4 (&w)[NCH], long long a,
 // One fused partition by the whole grid (every thread of every CTA calls it); `sm` holds
 // the accumulators. Quantized (F32 false): hot | c3 | cold_g | cold_q, kQ4MaxCells u32
 // words each. f32 gradients: g64 | h64, kQ4MaxCells u64 words each (the same bytes).
+// done_ctr (the fused control step's main partition): each CTA adds the tiles it finished
+// there, with release semantics, after its histogram is flushed.
 template <int SHIFT, int NCH, bool F32, bool PACK4>
 __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t* sm,
-                                   PartSmem& ps_) {
+                                   PartSmem& ps_, uint32_t* done_ctr = nullptr) {
   static_assert(NCH <= kFpMaxChunks, "row chunks held in registers");
   int32_t* s_warp = ps_.warp;
   int32_t& s_tile = ps_.tile;
@@ -3132,6 +3144,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
   uint32_t* dp = src == 1 ? d.idx0 : d.idx1;
   const bool identity = src == 2;
   const int32_t ntiles = (count + kPartTile - 1) / kPartTile;
+  if (tid == 0) ps_.ntiles = ntiles;
   const bool is_cat = (ft.flags & kFeatCategorical) != 0;
   const int nf = d.F;
   const int cap = nf << SHIFT;
@@ -3152,6 +3165,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     } else {
       c->rows_parted += count;
       if (build) c->num_builds += 1;
+      if (done_ctr) c->rows_parted_ctl += count;
     }
   }
   if (is_cat && tid < kCatWords) ps_.cat[tid] = cat_src[tid];
@@ -3198,6 +3212,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
   long long cta_built = 0;
   bool failed = false;
   bool cancelled = false;
+  uint32_t tiles_done = 0;
   while (true) {
     const int32_t base = tile * kPartTile;
     // a look-ahead's cancel flag, read as the tile starts and used before the next ticket
@@ -3320,6 +3335,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     cta_left += tile_left;
     cta_built += built;
     acc_rows += built;
+    ++tiles_done;
     if (priv) break;
     // A cancelled look-ahead takes no further ticket, so no tile is left untaken behind
     // a ticket that a later tile's look-back would wait on.
@@ -3398,10 +3414,18 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     if (build)
       atomicAdd(reinterpret_cast<unsigned long long*>(rec ? &rec->built : &c->rows_built),
                 (unsigned long long)cta_built);
+    if (build && done_ctr)
+      atomicAdd(reinterpret_cast<unsigned long long*>(&c->rows_built_ctl),
+                (unsigned long long)cta_built);
   }
   if (d.ctl_phase) {  // uniform over the CTA (a launch parameter)
     __syncthreads();
     part_mark(d, rec != nullptr, PP_FLUSHED, global_ns());
+  }
+  if (done_ctr) {
+    // the barrier orders every thread's flush before thread 0's release
+    __syncthreads();
+    if (tid == 0) atom_add_acq_rel_gpu(done_ctr, tiles_done);
   }
 }
 
@@ -3413,6 +3437,59 @@ __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int b
   __shared__ PartSmem ps;
   partition_q4_phase<SHIFT, NCH, F32, PACK4>(d, build, la, sm, ps);
   producer_signal(d);
+}
+
+// Bounded wait (thread 0) until `want` tiles of the main partition are done, or the tree was
+// ended (a look-back that gave up sets done). False when the wait ran out.
+__device__ __noinline__ bool wait_part_done(GrowCtrl* c, uint32_t want) {
+  // twice the look-back's limit: a partition CTA that gives up ends the tree first
+  for (long long spins = 0;; ++spins) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&c->part_done) : "memory");
+    if (v >= want) return true;
+    if (*reinterpret_cast<volatile int32_t*>(&c->done)) return true;
+    if (spins > 2 * kSpinLimit) return false;
+    __nanosleep(32);
+  }
+}
+
+// The control step of split step s with the main partition of the split picked at step
+// s - 1 folded in: when the previous look-ahead did not partition that leaf, the control
+// CTAs (the first nctl) and the helper CTAs after them partition it first (the main
+// partition's own code, tiles by ticket), the control CTAs wait for every tile, redo the
+// prep and go on. Otherwise the helpers return after one read of the control block, and
+// the split costs one launch instead of two (control step, then a main partition that
+// finds nothing to do). No CTA waits on a CTA that has not taken a tile: a control CTA
+// leaves the tile loop only once every ticket is drawn, by CTAs that are running.
+template <int SHIFT, int NCH, bool F32, bool PACK4>
+__global__ void __launch_bounds__(1024, 1)
+    k_fixscan_part(GrowDev d, int s, GrowDev dp, int nctl) {
+  static_assert(kFpThreads == 1024, "the fused control step runs the partition's CTA shape");
+  const SpanStamp span(d);
+  extern __shared__ uint32_t smp[];
+  __shared__ FixScanSmem sm;
+  __shared__ CtlSmem cs;
+  __shared__ PartSmem ps;
+  if ((int)blockIdx.x >= nctl) {
+    partition_q4_phase<SHIFT, NCH, F32, PACK4>(dp, 1, -1, smp, ps, &dp.ctrl->part_done);
+    return;
+  }
+  control_step<false, false, 1024>(d, s, sm, cs, nctl, [&] {
+    partition_q4_phase<SHIFT, NCH, F32, PACK4>(dp, 1, -1, smp, ps, &dp.ctrl->part_done);
+    if (threadIdx.x == 0) {
+      if (!wait_part_done(d.ctrl, (uint32_t)ps.ntiles)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
+      prep_compute<false>(d, s, cs.prep);  // with the partition's counts
+    }
+    __syncthreads();
+  });
+}
+
+using FixscanPartKernel = void (*)(GrowDev, int, GrowDev, int);
+__host__ FixscanPartKernel fixscan_part_kernel(int shift, int nch, bool f32, bool pack4) {
+  if (shift != 8 || pack4) return nullptr;
+  if (nch == 1) return f32 ? k_fixscan_part<8, 1, true, false> : k_fixscan_part<8, 1, false, false>;
+  if (nch == 2) return f32 ? k_fixscan_part<8, 2, true, false> : k_fixscan_part<8, 2, false, false>;
+  return nullptr;
 }
 
 using PartQ4Kernel = void (*)(GrowDev, int, int);
@@ -3620,9 +3697,27 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
     build(x, 0);
     exchange(x);
   }
+  // One launch per split on one device: the control step of split s >= 1 runs the main
+  // partition of split s - 1 itself when the look-ahead did not (k_fixscan_part). Wide
+  // (256-thread) and categorical control steps, peers and the event profiler keep the
+  // separate main partition.
+  const int ctl_slice = d.slice_end - d.slice_begin;
+  const int ctl_grid = std::min(ctl_slice, (d.narrow_scan && !d.has_cat ? 4 : 1) * sms);
+  const FixscanPartKernel fpk =
+      fixscan_part_kernel(d.q4_shift, d.q4_nch, d.gh_mode == GH_FLOAT, d.packed4 != 0);
+  const bool fuse_main = d.fused && la_on && d.fuse_main && !prof && !px && !comm &&
+                         !d.has_cat && !d.narrow_scan && fpk != nullptr &&
+                         ctl_grid >= d.private_tiles;
   for (int s = 0; s < d.L - 1; ++s) {
     if (la_on && !prof && s >= 2) cudaStreamWaitEvent(st, las->done[(s - 2) & (kLaSlots - 1)], 0);
-    {
+    if (fuse_main && s >= 1) {
+      GrowDev x = consumer(s);
+      x.span_slot = span_slot_of(s, SPAN_FIXSCAN);
+      GrowDev xp = producer(s);
+      xp.span_slot = span_slot_of(s - 1, SPAN_PARTITION);
+      const int mg = (s - 1) < las->main_early_steps ? las->main_blocks : las->main_late_blocks;
+      fpk<<<std::max(ctl_grid, mg), 1024, fused_partition_smem(), st>>>(x, s, xp, ctl_grid);
+    } else {
       GrowDev x = consumer(s);
       x.span_slot = span_slot_of(s, SPAN_FIXSCAN);
       PROF_BEGIN(KC_FIXSCAN);
@@ -3653,7 +3748,9 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
     if (la_step && !prof) cudaEventRecord(las->fork, st);
     // the main partition is launched before the look-ahead, so that its CTAs (which
     // mostly find the split already partitioned) are placed first
-    if (x.fused) {
+    if (x.fused && fuse_main && s < d.L - 2) {
+      // the next control step partitions this split's leaf when it must
+    } else if (x.fused) {
       PROF_BEGIN(KC_PARTITION);
       const int main_grid =
           la_on ? (s < las->main_early_steps ? las->main_blocks : las->main_late_blocks) : sms;
@@ -3722,6 +3819,11 @@ void set_build_smem_limit(size_t bytes) {
             cudaFuncSetAttribute(part_q4_kernel(sh, n, f32, p4),
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)fused_partition_smem());
+  for (int n = 1; n <= 2; ++n)
+    for (bool f32 : {false, true})
+      cudaFuncSetAttribute(fixscan_part_kernel(8, n, f32, false),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)fused_partition_smem());
   cudaFuncSetAttribute(k_build<GH_QLUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)bytes);
   cudaFuncSetAttribute(k_build<GH_FLOAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,

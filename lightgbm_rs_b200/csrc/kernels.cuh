@@ -150,6 +150,9 @@ struct GrowDev {
   // into scratch records while the prep runs, so that the code is in the SM's instruction
   // cache when the last CTA runs the pick for real.
   int32_t warm_pick;
+  // One device, fused partition: the control step runs the main partition of the previous
+  // split itself when the look-ahead did not (k_fixscan_part); else a launch of its own.
+  int32_t fuse_main;
   // A look-ahead whose leaf the next pick did not take is cancelled (LookAhead.cancel).
   int32_t la_cancel;
   long long xwait_ns;                         // wait limit, then the spin-timeout error
