@@ -505,7 +505,11 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
     las.main_late_blocks = std::max(1, sms * 7 / 16);
     las.main_early_steps = 16;
     // launch-shape overrides (tuning): look-ahead and main-partition CTAs
-    if (const char* e = std::getenv("LGBM_B200_LA_BLOCKS")) las.blocks = std::max(1, std::atoi(e));
+    // With the main partition inside the control step the look-ahead does better with every
+    // SM: its idle CTAs return at once, and the control step's CTAs are placed as they do.
+    las.blocks_fused = sms;
+    if (const char* e = std::getenv("LGBM_B200_LA_BLOCKS"))
+      las.blocks = las.blocks_fused = std::max(1, std::atoi(e));
     if (const char* e = std::getenv("LGBM_B200_MAIN_BLOCKS"))
       las.main_blocks = std::max(1, std::atoi(e));
     if (const char* e = std::getenv("LGBM_B200_MAIN_LATE_BLOCKS"))

@@ -3777,7 +3777,8 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       GrowDev xl = x;
       xl.span_slot = span_slot_of(s, SPAN_LOOKAHEAD);
       xl.self_signal = self_sig ? 2 : 0;
-      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT, x.packed4 != 0)<<<las->blocks, kFpThreads,
+      part_q4_kernel(x.q4_shift, x.q4_nch, x.gh_mode == GH_FLOAT, x.packed4 != 0)<<<
+          fuse_main ? las->blocks_fused : las->blocks, kFpThreads,
                                                                 fused_partition_smem(),
                                                                 lst>>>(xl, 1, s & (kLaSlots - 1));
       if (prof) prof->end(lst, pslot);

@@ -266,7 +266,8 @@ struct LookAheadStreams {
   cudaStream_t st;
   cudaEvent_t fork;     // after control step s, on the main stream
   cudaEvent_t done[kLaSlots];  // after the look-ahead kernel of step s, slot s % kLaSlots
-  int blocks;           // CTAs of a look-ahead kernel (the control step keeps the rest)
+  int blocks;           // CTAs of a look-ahead kernel (the control step keeps the rest) ...
+  int blocks_fused;     // ... when the control step runs the main partition (all SMs)
   int main_blocks;      // CTAs of the main-stream partition while look-aheads run ...
   int main_late_blocks; // ... and from split step main_early_steps on, where its leaf is
   int main_early_steps; //     almost always partitioned already by the look-ahead
