@@ -120,3 +120,45 @@ def test_lookahead_learner_grow_partition(data):
         a = np.sort(gpart["indices"][gpart["leaf_begin"][l]:][:gpart["leaf_count"][l]])
         b = np.sort(wpart["indices"][wpart["leaf_begin"][l]:][:wpart["leaf_count"][l]])
         assert np.array_equal(a, b), l
+
+
+def _train_env(ds, params, rounds, env):
+    import lightgbm_rs_b200 as lgb
+
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
+    try:
+        booster = lgb.train(params, ds, num_boost_round=rounds)
+        _, pc = booster.profile_pipeline(1)
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    return booster, pc
+
+
+@pytest.mark.parametrize("env", [
+    {"LGBM_B200_FUSE_MAIN": "0"},   # the main partition as its own launch
+    {"LGBM_B200_LA_CANCEL": "0"},   # missed look-aheads run to the end
+    {"LGBM_B200_WARM_PICK": "0"},   # no placeholder picks
+    {"LGBM_B200_LA_BLOCKS": "120", "LGBM_B200_MAIN_LATE_BLOCKS": "148"},
+])
+def test_split_step_variants_same_trees(data, env):
+    """The launch-shape variants of the split step (the main partition inside the next
+    control step or its own launch, cancelled or finished look-aheads, the pick's
+    instruction-cache warm-up, grid sizes) change when work runs, never its result: the
+    same trees and scores, bit for bit. The default run's main partitions ran inside the
+    control steps (their rows are counted there); with LGBM_B200_FUSE_MAIN=0 none did."""
+    X, y, ds, metas = data
+    params = {"objective": "binary", "num_leaves": 255, "min_data_in_leaf": 50,
+              "learning_rate": 0.1, "use_quantized_grad": True, "num_grad_quant_bins": 4}
+    base, pc_base = _train_env(ds, params, 3, {})
+    var, pc_var = _train_env(ds, params, 3, env)
+    assert pc_base["fused"] and pc_base["rows_parted_ctl"] > 0, pc_base
+    if env.get("LGBM_B200_FUSE_MAIN") == "0":
+        assert pc_var["rows_parted_ctl"] == 0, pc_var
+    for i, (a, b) in enumerate(zip(base.trees(), var.trees())):
+        _assert_trees_bit_equal(b, a, f"{env} tree {i}")
+    assert base.train_scores().tobytes() == var.train_scores().tobytes()
