@@ -316,6 +316,7 @@ struct lgbm_b200_learner {
   DevBuf<uint8_t> scan_ok;
   // look-ahead partitions: two slots and the second stream they run on
   DevBuf<LookAhead> la;
+  DevBuf<LookAhead> mainrec;  // [2] the fused control step's main-partition records
   DevBuf<long long> la_raw;
   DevBuf<long long> la_partials;
   DevBuf<unsigned long long> la_status;
@@ -487,6 +488,8 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
                       sizeof(uint32_t) * kCatWords * (2 * ds->num_features + 2 * L + 1)));
   CUDA_TRY(scan_ok.alloc(2));
   CUDA_TRY(la.alloc(kLaSlots));
+  CUDA_TRY(mainrec.alloc(2));
+  CUDA_TRY(cudaMemset(mainrec.p, 0, 2 * sizeof(LookAhead)));
   CUDA_TRY(cudaMemset(la.p, 0, kLaSlots * sizeof(LookAhead)));
   CUDA_TRY(la_raw.alloc(kLaSlots * ((size_t)slot_len + 2)));
   CUDA_TRY(la_partials.alloc((size_t)kLaSlots * kPrivateTiles * slot_len));
@@ -600,6 +603,7 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   d.narrow_scan = (!d.has_cat && max_bins <= 64 && !(ns && ns[0] == '0')) ? 1 : 0;
   d.scan_ok = scan_ok.p;
   d.la = la.p;
+  d.mainrec = mainrec.p;
   d.la_raw = la_raw.p;
   d.la_partials = la_partials.p;
   d.la_status = la_status.p;

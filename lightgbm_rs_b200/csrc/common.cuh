@@ -147,8 +147,6 @@ struct GrowCtrl {
   int32_t la_runs;         // look-ahead partitions run in this tree
   int32_t la_hits;         // ... whose leaf was the next split
   DevSplitInfo split;
-  uint32_t part_done;      // tiles of the main partition finished (fused control step)
-  uint32_t _pad_done;
   long long rows_parted_ctl;  // parent rows of main partitions run inside control steps
   long long rows_built_ctl;   // ... and the rows their fused child builds accumulated
 };

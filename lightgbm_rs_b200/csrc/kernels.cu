@@ -1361,7 +1361,6 @@ __device__ void prep_compute(const GrowDev& d, int s, Prep& P) {
   c.epoch += 1;
   c.part_ticket = 0;
   c.part_left_total = 0;
-  c.part_done = 0;
   c.scan_counter = 0;
   // ---- BeforeFindBestSplit (learner.rs:1808-1839) ----
   const int32_t min2 = d.gain.min_data_in_leaf * 2;
@@ -2771,6 +2770,23 @@ __device__ void control_step(const GrowDev& d, int s, FixScanSmem& sm, CtlSmem& 
       }
       d.la[s & (kLaSlots - 1)] = r;
     }
+    if (d.mainrec) {
+      // the next (fused) control step's main partition: the split it partitions when the
+      // look-ahead did not, with the epoch this control block carries and fresh counters
+      LookAhead m{};
+      m.active = (!c.done && c.pending && !c.pend_la) ? 1 : 0;
+      if (m.active) {
+        m.leaf = c.split_leaf;
+        m.feature = c.split_feature;
+        m.build = 1;
+        m.build_left = c.build_left;
+        m.epoch = c.epoch;
+        m.split = c.split;
+        if (CAT)
+          for (int k = 0; k < kCatWords; ++k) m.cat[k] = cs.pick.split_cat[k];
+      }
+      d.mainrec[(s + 1) & 1] = m;
+    }
     *d.ctrl = c;
   }
   ctl_mark(d, s, CP_WRITTEN);
@@ -3061,11 +3077,15 @@ __device__ __forceinline__ void f32_row_regs(const uint4 (&w)[NCH], long long a,
 // One fused partition by the whole grid (every thread of every CTA calls it); `sm` holds
 // the accumulators. Quantized (F32 false): hot | c3 | cold_g | cold_q, kQ4MaxCells u32
 // words each. f32 gradients: g64 | h64, kQ4MaxCells u64 words each (the same bytes).
-// done_ctr (the fused control step's main partition): each CTA adds the tiles it finished
-// there, with release semantics, after its histogram is flushed.
+// mrec (the fused control step's main partition): the split, its status-word epoch, the
+// tile tickets and the finished-tile counter come from this record, written by the control
+// step before, instead of the control block (which this kernel's own last CTA rewrites);
+// the outputs are the main partition's. Each CTA adds the tiles it finished to mrec->done,
+// with release semantics, after its histogram is flushed.
 template <int SHIFT, int NCH, bool F32, bool PACK4>
 __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t* sm,
-                                   PartSmem& ps_, uint32_t* done_ctr = nullptr) {
+                                   PartSmem& ps_, LookAhead* mrec = nullptr) {
+  uint32_t* const done_ctr = mrec ? &mrec->done : nullptr;
   static_assert(NCH <= kFpMaxChunks, "row chunks held in registers");
   int32_t* s_warp = ps_.warp;
   int32_t& s_tile = ps_.tile;
@@ -3078,7 +3098,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
   // la >= 0: the look-ahead partition of slot la (its leaf, split, counters, status
   // words and accumulator); otherwise the pending split of the control block
   LookAhead* const rec = la >= 0 ? d.la + la : nullptr;
-  uint32_t* const ticket = rec ? &rec->ticket : &d.ctrl->part_ticket;
+  uint32_t* const ticket = rec ? &rec->ticket : mrec ? &mrec->ticket : &d.ctrl->part_ticket;
   const unsigned long long t_entry = d.ctl_phase ? global_ns() : 0ull;
   if (!rec) {
     // The main partition has nothing to do after the tree, or when the look-ahead did this
@@ -3086,7 +3106,7 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     // request, so that such a launch costs a single round trip.
     if (tid == 0) {
       const GrowCtrl* c0 = d.ctrl;
-      s_ok = (c0->done || !c0->pending || c0->pend_la) ? 0 : 1;
+      s_ok = mrec ? (mrec->active ? 1 : 0) : (c0->done || !c0->pending || c0->pend_la) ? 0 : 1;
     }
     __syncthreads();
     if (!s_ok) return;
@@ -3122,6 +3142,17 @@ __device__ void partition_q4_phase(const GrowDev& d, int build, int la, uint32_t
     status = d.la_status;
     raw = d.la_raw + (size_t)la * (d.raw_len + 2);
     partials = d.la_partials + (size_t)la * d.private_tiles * d.raw_len;
+  } else if (mrec) {
+    leaf = mrec->leaf;
+    f = mrec->feature;
+    epoch = mrec->epoch;
+    thr = mrec->split.threshold;
+    dl = mrec->split.default_left != 0;
+    build_left = mrec->build_left != 0;
+    cat_src = mrec->cat;
+    status = d.part_status;
+    raw = d.raw;
+    partials = d.partials;
   } else {
     // nothing to do after the tree, or when the look-ahead did this partition
     if (c->done || !c->pending || c->pend_la) return;
@@ -3441,11 +3472,11 @@ __global__ void __launch_bounds__(kFpThreads, 1) k_partition_q4(GrowDev d, int b
 
 // Bounded wait (thread 0) until `want` tiles of the main partition are done, or the tree was
 // ended (a look-back that gave up sets done). False when the wait ran out.
-__device__ __noinline__ bool wait_part_done(GrowCtrl* c, uint32_t want) {
+__device__ __noinline__ bool wait_part_done(GrowCtrl* c, const uint32_t* done, uint32_t want) {
   // twice the look-back's limit: a partition CTA that gives up ends the tree first
   for (long long spins = 0;; ++spins) {
     uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&c->part_done) : "memory");
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(done) : "memory");
     if (v >= want) return true;
     if (*reinterpret_cast<volatile int32_t*>(&c->done)) return true;
     if (spins > 2 * kSpinLimit) return false;
@@ -3457,9 +3488,13 @@ __device__ __noinline__ bool wait_part_done(GrowCtrl* c, uint32_t want) {
 // s - 1 folded in: when the previous look-ahead did not partition that leaf, the control
 // CTAs (the first nctl) and the helper CTAs after them partition it first (the main
 // partition's own code, tiles by ticket), the control CTAs wait for every tile, redo the
-// prep and go on. Otherwise the helpers return after one read of the control block, and
-// the split costs one launch instead of two (control step, then a main partition that
-// finds nothing to do). No CTA waits on a CTA that has not taken a tile: a control CTA
+// prep and go on. Otherwise the helpers return after one read of their record, and the
+// split costs one launch instead of two (control step, then a main partition that finds
+// nothing to do). The partition's split, epoch, tickets and tile counter come from
+// mainrec[s & 1], which the previous control step wrote: a helper placed on an SM only
+// after this kernel's last CTA rewrote the control block still reads its own step's
+// record, finds every ticket drawn (or nothing to do) and returns; the next step's record
+// is the other one. No CTA waits on a CTA that has not taken a tile: a control CTA
 // leaves the tile loop only once every ticket is drawn, by CTAs that are running.
 template <int SHIFT, int NCH, bool F32, bool PACK4>
 __global__ void __launch_bounds__(1024, 1)
@@ -3470,14 +3505,16 @@ __global__ void __launch_bounds__(1024, 1)
   __shared__ FixScanSmem sm;
   __shared__ CtlSmem cs;
   __shared__ PartSmem ps;
+  LookAhead* const mrec = dp.mainrec + (s & 1);
   if ((int)blockIdx.x >= nctl) {
-    partition_q4_phase<SHIFT, NCH, F32, PACK4>(dp, 1, -1, smp, ps, &dp.ctrl->part_done);
+    partition_q4_phase<SHIFT, NCH, F32, PACK4>(dp, 1, -1, smp, ps, mrec);
     return;
   }
   control_step<false, false, 1024>(d, s, sm, cs, nctl, [&] {
-    partition_q4_phase<SHIFT, NCH, F32, PACK4>(dp, 1, -1, smp, ps, &dp.ctrl->part_done);
+    partition_q4_phase<SHIFT, NCH, F32, PACK4>(dp, 1, -1, smp, ps, mrec);
     if (threadIdx.x == 0) {
-      if (!wait_part_done(d.ctrl, (uint32_t)ps.ntiles)) atomicOr(&d.ctrl->error, kErrSpinTimeout);
+      if (!wait_part_done(d.ctrl, &mrec->done, (uint32_t)ps.ntiles))
+        atomicOr(&d.ctrl->error, kErrSpinTimeout);
       prep_compute<false>(d, s, cs.prep);  // with the partition's counts
     }
     __syncthreads();
@@ -3715,11 +3752,13 @@ void launch_tree(const GrowDev& d_in, int build_blocks, size_t build_smem, cudaS
       x.span_slot = span_slot_of(s, SPAN_FIXSCAN);
       GrowDev xp = producer(s);
       xp.span_slot = span_slot_of(s - 1, SPAN_PARTITION);
+      x.mainrec = xp.mainrec = d.mainrec;
       const int mg = (s - 1) < las->main_early_steps ? las->main_blocks : las->main_late_blocks;
       fpk<<<std::max(ctl_grid, mg), 1024, fused_partition_smem(), st>>>(x, s, xp, ctl_grid);
     } else {
       GrowDev x = consumer(s);
       x.span_slot = span_slot_of(s, SPAN_FIXSCAN);
+      x.mainrec = fuse_main ? d.mainrec : nullptr;  // the first step writes step 1's record
       PROF_BEGIN(KC_FIXSCAN);
       // variants: categorical features, and the peer exchange (off on one device). One
       // CTA per feature of this rank's slice, at most one resident wave of CTAs (each

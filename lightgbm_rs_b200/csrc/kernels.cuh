@@ -55,6 +55,8 @@ struct LookAhead {
   int32_t failed;      // a look-back gave up (spin limit)
   int32_t ran;         // the kernel partitioned the leaf
   int32_t cancel;      // the next pick took another leaf: the kernel takes no more tiles
+  uint32_t done;       // tiles finished (the fused control step's main partition record)
+  uint32_t _pad;
   long long rows;      // parent rows streamed
   long long built;     // rows accumulated into the child histogram
   DevSplitInfo split;
@@ -164,6 +166,9 @@ struct GrowDev {
   int32_t lookahead;
   int32_t _lapad;
   LookAhead* la;                  // [kLaSlots]
+  // [2] the split each fused control step partitions when the look-ahead did not, written
+  // by the control step before it (record (s & 1) for step s; null when not fused)
+  LookAhead* mainrec;
   long long* la_raw;              // [kLaSlots][raw_len + 2] accumulated child, left-row count
   long long* la_partials;         // [kLaSlots][private_tiles][raw_len]
   unsigned long long* la_status;  // [max_tiles] look-back words of the look-ahead kernel
