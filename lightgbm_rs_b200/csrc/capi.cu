@@ -530,8 +530,8 @@ int lgbm_b200_learner::init(lgbm_b200_dataset* dataset, const lgbm_b200_learner_
   if (const char* e = std::getenv("LGBM_B200_WARP_AGG")) d.warp_agg = std::strcmp(e, "1") == 0;
   d.warm_pick = 1;
   if (const char* e = std::getenv("LGBM_B200_WARM_PICK")) d.warm_pick = std::strcmp(e, "0") != 0;
-  d.fuse_main = 0;
-  if (const char* e = std::getenv("LGBM_B200_FUSE_MAIN")) d.fuse_main = std::strcmp(e, "1") == 0;
+  d.fuse_main = 1;
+  if (const char* e = std::getenv("LGBM_B200_FUSE_MAIN")) d.fuse_main = std::strcmp(e, "0") != 0;
   d.la_cancel = 1;
   if (const char* e = std::getenv("LGBM_B200_LA_CANCEL")) d.la_cancel = std::strcmp(e, "0") != 0;
   d.slice_begin = 0;
